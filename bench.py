@@ -1,0 +1,360 @@
+#!/usr/bin/env python
+"""Decode benchmark: Qwen3-1.7B-shaped Q4_0 batch-1 greedy decode.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl zero_b200|reference]
+
+A step is one decode step (forward through 28 layers + LM-head argmax) for
+one token; K steps are timed after a 16-token prompt prefill.  Prints one
+JSON line on rank 0.
+
+  value    tok/s of the K decode steps, device-timed with CUDA events around
+           the CUDA-graph replays (weights resident in HBM; the token chain
+           stays on the device).  Weights stream 1.12 GB per step, far above
+           the 126 MB L2, so no flush is needed between steps.
+  e2e      the same metric through the reference-facing C ABI per token
+           (zgpu_forward_single_token + zgpu_lm_head_argmax), host token in,
+           host token out, host wall clock.
+  roofline the dominant kernel class (Q4_0X4 GEMV, 2048 -> 6144 per launch,
+           over the 56 gate/up tensors of the model so every launch streams
+           from HBM): algorithmic bytes / CUDA-event duration vs the measured
+           HBM copy bandwidth.
+  cpu_baseline  the CPU oracle's AVX-512-order restatement of the reference
+           decode, all host cores, on a bounded sample (rank 0, N=1 only).
+
+With --gpus N > 1 (launched under torchrun) every rank decodes its own
+replica (weak scaling); times are the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tok/s, Qwen3-1.7B-shape Q4_0 b=1; GEMV HBM GB/s vs ~8 TB/s peak"
+PUBLISHED_TOK_S = 194.5      # README.md:29 of the reference (EPYC 9354P, AVX-512, CPU only)
+PROMPT_LEN = 16
+SEED = 0
+# dram bytes (read + write) of one 2048->6144 Q4_0X4 GEMV launch, from the ncu
+# capture summarised in profiles/gemv_q4x4_2048x6144.md (None until captured).
+NCU_TRAFFIC_PER_LAUNCH = None
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="zero_b200", choices=["zero_b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def physical_cores() -> int:
+    try:
+        out = subprocess.run(["lscpu", "-p=CORE,SOCKET"], capture_output=True, text=True).stdout
+        cores = {tuple(l.split(",")) for l in out.splitlines() if l and not l.startswith("#")}
+        if cores:
+            return len(cores)
+    except OSError:
+        pass
+    return os.cpu_count() or 1
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d.get("hbm_gbs", 6650.0), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(prefix="clocks", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [s.strip() for s in line.split(",")]
+                if len(parts) >= 9 and parts[1].isdigit():
+                    rows.append(parts)
+        except OSError:
+            pass
+        finally:
+            if self.path:
+                try:
+                    os.unlink(self.path)
+                except OSError:
+                    pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [int(r[1]) for r in rows]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": int(statistics.median(sm)), "sm_max_mhz": int(rows[0][2]),
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3] not in ("[N/A]", "")),
+                "reasons": sorted(reasons)}
+
+
+def physical_gpu_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local_rank < len(ids) and ids[local_rank].isdigit():
+            return int(ids[local_rank])
+    return local_rank
+
+
+def cpu_decode(cfg, weights, prompt, steps: int, threads: int):
+    """Time `steps` decode steps (forward + LM head) of the CPU oracle's AVX-512 path."""
+    import oracle as O
+
+    r = O.OracleRun(cfg, weights, PROMPT_LEN + steps + 2, order=O.ORDER_AVX512, threads=threads)
+    for i, t in enumerate(prompt):
+        r.forward(int(t), i)
+    rc, tok, _ = r.lm_head()
+    pos = len(prompt)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        r.forward(tok, pos)
+        rc, tok, _ = r.lm_head()
+        pos += 1
+    dt = time.perf_counter() - t0
+    r.close()
+    return steps / dt, dt
+
+
+def run_reference(args, rank):
+    """The reference arm: the reference's CPU decode path (restated, AVX-512 order)
+    on the host cores, same config and metric."""
+    if rank != 0:
+        return
+    from zero_b200 import synth
+
+    cfg = synth.QWEN3_1_7B
+    weights = synth.qwen3_weights(cfg, seed=SEED, x4=False)
+    prompt = synth.prompt_ids(cfg, PROMPT_LEN, seed=SEED)
+    cores = physical_cores()
+    cpu_decode(cfg, weights, prompt, max(1, min(args.warmup, 3)), cores)   # warm-up
+    tok_s, dt = cpu_decode(cfg, weights, prompt, args.steps, cores)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(tok_s, 3), "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000 * dt / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": round(tok_s / PUBLISHED_TOK_S, 4), "dtype": "f32",
+        "data": "synthetic (seeded random-init .smodel v2 weights)",
+        "config": {"workload": "qwen3-1.7b-shape q4_0 decode b=1 (BASELINE config 0)",
+                   "prompt": PROMPT_LEN, "decode_steps": args.steps, "layers": cfg.n_layers,
+                   "hidden": cfg.hidden, "ffn": cfg.ffn, "vocab": cfg.vocab_padded,
+                   "parallelism": "cpu threads"},
+        "cpu_baseline": {"value": round(tok_s, 3), "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} decode steps after a {PROMPT_LEN}-token prefill"},
+        "e2e": {"value": round(tok_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    import torch
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    import zero_b200 as zb
+    from zero_b200 import synth
+
+    cfg = synth.QWEN3_1_7B
+    weights = synth.qwen3_weights(cfg, seed=SEED)
+    prompt = synth.prompt_ids(cfg, PROMPT_LEN, seed=SEED)
+    ctx = zb.Context(device=local)
+    model = zb.Qwen3Model(ctx, cfg, weights)
+    max_tokens = 512
+    n_gen_timed = args.steps + 1
+    assert PROMPT_LEN + n_gen_timed - 1 <= max_tokens
+    kv = model.new_kv(max_tokens)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+
+    # warm-up: W decode steps (graphs captured on the first call)
+    model.generate_greedy(kv, prompt, args.warmup + 1)
+    barrier()
+    with ClockSampler(physical_gpu_index(local)) as clocks:
+        toks, _ = model.generate_greedy(kv, prompt, n_gen_timed)
+        barrier()
+    perf = model.perf()
+    dec_ms = float(perf["decode_ms"])
+    if world > 1:
+        t = torch.tensor([dec_ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        dec_ms = float(t.item())
+    tok_s = world * args.steps / (dec_ms / 1000.0)
+    # generate() replayed PROMPT_LEN prefill steps and K decode steps of the same graph
+    step_kernels = perf["kernel_launches"] // (PROMPT_LEN + args.steps)
+    gpu_launches = step_kernels * args.steps
+
+    # ------------------------------------------------ e2e through the C ABI
+    kv2 = model.new_kv(max_tokens)
+    for i, t in enumerate(prompt):
+        model.forward_single_token(kv2, int(t), i)
+    tok, _ = model.lm_head_argmax(want_logits=False)
+    barrier()
+    t0 = time.perf_counter()
+    pos = PROMPT_LEN
+    for _ in range(args.steps):
+        model.forward_single_token(kv2, tok, pos)
+        tok, _ = model.lm_head_argmax(want_logits=False)
+        pos += 1
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_tok_s = world * args.steps / e2e_s
+    kv2.close()
+
+    # -------------------------------------- roofline of the dominant kernel
+    # Q4_0X4 GEMV 2048 -> 6144 (ffn_gate / ffn_up of every layer: 56 distinct
+    # 7.08 MB tensors, 396 MB per sweep > L2), on a torch stream timed with
+    # CUDA events on that same stream.
+    keys = []
+    for i in range(cfg.n_layers):
+        keys.append(model._layers[i].ffn_gate)
+        keys.append(model._layers[i].ffn_up)
+    x = torch.randn(cfg.hidden, device="cuda", dtype=torch.float32)
+    y = torch.empty(cfg.ffn, device="cuda", dtype=torch.float32)
+    stream = torch.cuda.Stream()
+    sh = stream.cuda_stream
+    reps = 4
+    with torch.cuda.stream(stream):
+        for k in keys:   # warm-up sweep
+            ctx.linear_dispatch_device(x.data_ptr(), k, y.data_ptr(), cfg.hidden, cfg.ffn, zb.Q4_0, sh)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            for k in keys:
+                ctx.linear_dispatch_device(x.data_ptr(), k, y.data_ptr(), cfg.hidden, cfg.ffn, zb.Q4_0, sh)
+        e1.record(stream)
+    stream.synchronize()
+    gemv_ms = e0.elapsed_time(e1) / (reps * len(keys))
+    gemv_bytes = cfg.ffn * cfg.hidden * 18 // 32 + cfg.hidden * 4 + cfg.ffn * 4
+    gemv_gbs = gemv_bytes / (gemv_ms * 1e-3) / 1e9
+    peaks = measured_peaks()
+    step_bytes = cfg.weight_bytes_per_token()
+    step_gbs = step_bytes * (args.steps / (dec_ms / 1000.0)) / 1e9
+
+    # ------------------------------------------------------- CPU baseline
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cores = physical_cores()
+        probe_rate, _ = cpu_decode(cfg, weights, prompt, 1, cores)
+        n = int(max(2, min(64, 15.0 * probe_rate)))
+        rate, dt = cpu_decode(cfg, weights, prompt, n, cores)
+        cpu = {"value": round(rate, 3), "unit": "tok/s", "cores": cores, "kind": "port",
+               "sample": f"{n} decode steps (forward + LM head) after a {PROMPT_LEN}-token prefill, "
+                         f"same seeded weights, AVX-512-order restatement, {dt:.1f} s"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dec_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": round(tok_s / PUBLISHED_TOK_S, 3), "dtype": "f32",
+            "data": "synthetic (seeded random-init .smodel v2 weights, BASELINE config 0)",
+            "config": {"workload": "qwen3-1.7b-shape q4_0 decode b=1 (BASELINE config 0)",
+                       "prompt": PROMPT_LEN, "decode_steps": args.steps, "layers": cfg.n_layers,
+                       "hidden": cfg.hidden, "ffn": cfg.ffn, "vocab": cfg.vocab_padded,
+                       "weight_bytes_per_step": step_bytes,
+                       "l2": "inputs larger than L2 (1.12 GB of weights streamed per step)",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "tokens_first": [int(v) for v in toks[:4]]},
+            "roofline": {"bound": "hbm", "kernel": "gemv_x4 Q4_0 2048->6144",
+                         "achieved": round(gemv_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gemv_gbs / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
+                         "traffic": NCU_TRAFFIC_PER_LAUNCH, "algorithmic_bytes": gemv_bytes,
+                         "avg_launch_us": round(gemv_ms * 1000, 3),
+                         "step_hbm_gbs": round(step_gbs, 1),
+                         "step_frac": round(step_gbs / peaks["hbm_gbs"], 4)},
+            "e2e": {"value": round(e2e_tok_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 84,
+                    "d2h_bytes_per_step": 12},
+            "gpu_launches": int(gpu_launches),
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    kv.close()
+    model.close()
+    ctx.close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

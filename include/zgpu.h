@@ -1,0 +1,245 @@
+/*
+ * zgpu.h — C ABI of zero-b200, the B200 (sm_100a) decode hot path that drops
+ * in under silicatetech/zero's `zero-llm-inference` forward/matmul API.
+ *
+ * Conventions
+ *   - Plain C types only: pointers, sizes, integer status codes.  No CUDA or
+ *     torch types cross the ABI (streams are passed as `void*`, a
+ *     cudaStream_t; NULL means the context's own stream).
+ *   - Every entry point returns a zgpu_status.  Codes map 1:1 onto the Rust
+ *     error enums the reference returns (see each code's comment);
+ *     zgpu_last_error() gives a human-readable message for the last failure
+ *     on a context.  No C++ exception ever crosses the ABI.
+ *   - The caller owns every host buffer.  Weights are registered once, keyed
+ *     by the host address of the tensor payload, mirroring
+ *     kernel/src/weight_layout.rs:40 (register) / :133 (group_of); the
+ *     library keeps a device copy.  Contexts are not thread-safe (the
+ *     reference's decode API is single-caller, kv_cache.rs:60).
+ *   - There is no CPU fallback: every compute entry point runs CUDA kernels
+ *     built for sm_100a and fails with ZGPU_ERR_NO_DEVICE when no device is
+ *     usable.
+ */
+#ifndef ZGPU_H
+#define ZGPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ZGPU_ABI_VERSION 1u
+
+/* ggml / .smodel dtype ids (zero-gguf-parser lib.rs:95-126; .smodel v2 ids
+ * tools/silicatepack.py:75-83). */
+enum zgpu_dtype {
+  ZGPU_F32 = 0,
+  ZGPU_F16 = 1,
+  ZGPU_Q4_0 = 2,
+  ZGPU_Q8_0 = 8,
+  ZGPU_Q4_0X4 = 100,
+  ZGPU_Q8_0X4 = 101
+};
+
+typedef enum zgpu_status {
+  ZGPU_OK = 0,
+  ZGPU_ERR_INVALID_ARG = 1,
+  /* LinearDispatchError::UnsupportedQuant (ops.rs:461); the reference panics
+   * at ops.rs:520 and inference_avx512.rs:1178. */
+  ZGPU_ERR_UNSUPPORTED_QUANT = 2,
+  /* a weight key that was never registered (no counterpart: the reference
+   * reads host memory directly). */
+  ZGPU_ERR_UNREGISTERED_WEIGHT = 3,
+  /* KvCacheError (kv_cache.rs:68-83). */
+  ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE = 10,
+  ZGPU_ERR_KV_LAYER_OUT_OF_RANGE = 11,
+  ZGPU_ERR_KV_INVALID_SLICE_LENGTH = 12,
+  ZGPU_ERR_KV_TOKEN_COUNT_EXCEEDS_MAX = 13,
+  /* AttentionError::NumericalInstability (attention.rs:26-31). */
+  ZGPU_ERR_NUMERICAL_INSTABILITY = 20,
+  /* EmbedDispatchError (forward_pass.rs:276-286). */
+  ZGPU_ERR_EMBED_UNSUPPORTED_QUANT = 30,
+  ZGPU_ERR_EMBED_DIM_MISALIGNMENT = 31,
+  /* LmHeadError (lm_head.rs:31-38). */
+  ZGPU_ERR_LM_NON_FINITE_LOGITS = 40,
+  ZGPU_ERR_LM_ARGMAX_IN_PADDING = 41,
+  /* runtime */
+  ZGPU_ERR_NO_DEVICE = 90,
+  ZGPU_ERR_CUDA = 91,
+  ZGPU_ERR_OUT_OF_MEMORY = 92,
+  /* a device-side bounded wait gave up (no counterpart; the reference's SMP
+   * barrier times out after 1 s, smp.rs:311). */
+  ZGPU_ERR_DEVICE_TIMEOUT = 93
+} zgpu_status;
+
+typedef struct zgpu_ctx zgpu_ctx;
+typedef struct zgpu_kv zgpu_kv;
+typedef struct zgpu_model zgpu_model;
+
+typedef struct zgpu_opts {
+  uint32_t abi_version;  /* must be ZGPU_ABI_VERSION */
+  int32_t device;        /* CUDA device ordinal */
+  uint32_t flags;        /* ZGPU_FLAG_* */
+} zgpu_opts;
+
+/* Capture the decode step into a CUDA graph (default on). */
+#define ZGPU_FLAG_NO_GRAPH 0x1u
+/* Launch kernels with programmatic dependent launch (default on). */
+#define ZGPU_FLAG_NO_PDL 0x2u
+
+/* ---------------------------------------------------------------- context */
+zgpu_status zgpu_init(const zgpu_opts *opts, zgpu_ctx **out);
+void zgpu_destroy(zgpu_ctx *ctx);
+const char *zgpu_last_error(const zgpu_ctx *ctx);
+const char *zgpu_status_string(zgpu_status s);
+/* Number of streaming multiprocessors on the context's device. */
+zgpu_status zgpu_device_info(const zgpu_ctx *ctx, int32_t *sm_count, int32_t *cc_major,
+                             int32_t *cc_minor);
+zgpu_status zgpu_synchronize(zgpu_ctx *ctx);
+
+/* ------------------------------------------------------- weight registry */
+/* Upload one tensor and key it by `host_ptr` (weight_layout.rs:40 register,
+ * model_loader.rs:532-570).  dtype is ZGPU_Q4_0 / ZGPU_Q8_0 (plain row
+ * blocks), ZGPU_Q4_0X4 / ZGPU_Q8_0X4 (.smodel v2 4-row interleave) or
+ * ZGPU_F32.  rows/cols give the logical matrix (cols = in_dim). */
+zgpu_status zgpu_register_weights(zgpu_ctx *ctx, const void *host_ptr, size_t len,
+                                  uint32_t dtype, uint64_t rows, uint64_t cols);
+/* weight_layout.rs:133 group_of: 4 for an interleaved registration, 1
+ * otherwise (also for unregistered addresses). */
+uint32_t zgpu_group_of(const zgpu_ctx *ctx, const void *host_ptr);
+/* weight_layout.rs:58 clear. Frees every device copy. */
+zgpu_status zgpu_clear_weights(zgpu_ctx *ctx);
+
+/* ------------------------------------------------------------ matmul API */
+/* out[out_dim] = W[out_dim x in_dim] . x[in_dim] with host x/out buffers.
+ * Mirrors linear_dispatch (ops.rs:486-523) and linear_dispatch_avx512
+ * (inference_avx512.rs:1147-1185); `w_key` is the registered host address.
+ * quant is the ggml type of the tensor (Q4_0 or Q8_0); the stored layout
+ * (plain or X4) comes from the registry, as group_of decides at
+ * inference_avx512.rs:638. */
+zgpu_status zgpu_linear_dispatch(zgpu_ctx *ctx, const float *x, const void *w_key, float *out,
+                                 uint64_t in_dim, uint64_t out_dim, uint32_t quant);
+/* Same with device-resident x/out on `stream` (no host copies, async). */
+zgpu_status zgpu_linear_dispatch_device(zgpu_ctx *ctx, const float *d_x, const void *w_key,
+                                        float *d_out, uint64_t in_dim, uint64_t out_dim,
+                                        uint32_t quant, void *stream);
+/* Q8_0 activation quantiser: x[n] -> n/32 blocks of {fp16 d, i8 q[32]} with
+ * the packer's rule (tools/silicatepack.py:893-907).  No counterpart on the
+ * reference's decode path (it multiplies f32 activations). */
+zgpu_status zgpu_quantize_q8_0(zgpu_ctx *ctx, const float *x, void *blocks_out, uint64_t n);
+/* Q4_0 weight x Q8_0 activation GEMV (int8 dot products, per-block fp16
+ * scales): out = sum_b d_w*d_x*sum_j (n-8)*q.  Host buffers. */
+zgpu_status zgpu_linear_q8act(zgpu_ctx *ctx, const void *xq_blocks, const void *w_key, float *out,
+                              uint64_t in_dim, uint64_t out_dim);
+
+/* ------------------------------------------------------------- small ops */
+/* rmsnorm (ops.rs:29-52). */
+zgpu_status zgpu_rmsnorm(zgpu_ctx *ctx, const float *x, const float *w, float *out, uint64_t n,
+                         float eps);
+/* RopeContext::new (ops.rs:79-93) + rope_sincos_lut_avx512/rope_apply_avx512
+ * (trig.rs:148,192) on `n_heads` heads of `head_dim`, in place. */
+zgpu_status zgpu_rope(zgpu_ctx *ctx, float *qk, uint32_t n_heads, uint32_t head_dim,
+                      uint32_t pos, float freq_base);
+/* silu_mul_avx512 (activation.rs:115-148). */
+zgpu_status zgpu_silu_mul(zgpu_ctx *ctx, const float *gate, const float *up, float *out,
+                          uint64_t n);
+
+/* --------------------------------------------------------------- KV cache */
+/* KvCache::new (kv_cache.rs:100-126): layer-major [K block | V block], each
+ * block max_tokens x n_kv_heads x head_dim f32, in device memory. */
+zgpu_status zgpu_kv_create(zgpu_ctx *ctx, uint32_t max_tokens, uint32_t n_layers,
+                           uint32_t n_kv_heads, uint32_t head_dim, zgpu_kv **out);
+void zgpu_kv_destroy(zgpu_kv *kv);
+/* KvCache::store_kv (kv_cache.rs:139-183), host k/v of n_kv_heads*head_dim. */
+zgpu_status zgpu_kv_store(zgpu_kv *kv, uint32_t layer, uint32_t token, const float *k,
+                          const float *v, uint64_t len);
+/* get_k_slice / get_v_slice (kv_cache.rs:186-222) copied to host:
+ * token_count * n_kv_heads * head_dim floats each (either may be NULL). */
+zgpu_status zgpu_kv_read(zgpu_kv *kv, uint32_t layer, uint32_t token_count, float *k_out,
+                         float *v_out);
+
+/* ------------------------------------------------------------ Qwen3 model */
+/* One decoder layer's tensors, each a registered host key (LayerWeights,
+ * forward_pass.rs:226-239).  Matmul tensors are Q4_0 (plain) or Q4_0X4;
+ * norms are f32 host arrays (copied at model creation). */
+typedef struct zgpu_qwen3_layer {
+  const float *attn_norm;
+  const void *attn_q, *attn_k, *attn_v, *attn_o;
+  const float *q_norm, *k_norm;
+  const float *ffn_norm;
+  const void *ffn_gate, *ffn_up, *ffn_down;
+} zgpu_qwen3_layer;
+
+typedef struct zgpu_qwen3_desc {
+  uint32_t n_layers, hidden, ffn, n_q_heads, n_kv_heads, head_dim;
+  uint32_t vocab_padded, vocab_real;
+  float rms_eps, rope_theta;
+  uint32_t token_embd_quant;  /* ZGPU_Q8_0 or ZGPU_Q4_0, plain rows */
+  const void *token_embd;     /* registered key */
+  uint32_t output_quant;      /* ZGPU_Q8_0 or ZGPU_Q4_0 (stored X4 or plain) */
+  const void *output;         /* registered key */
+  const float *output_norm;
+  const zgpu_qwen3_layer *layers;
+} zgpu_qwen3_desc;
+
+zgpu_status zgpu_qwen3_create(zgpu_ctx *ctx, const zgpu_qwen3_desc *desc, zgpu_model **out);
+void zgpu_qwen3_destroy(zgpu_model *m);
+/* forward_single_token (forward_pass.rs:515-631) /
+ * forward_single_token_avx512 (inference_avx512.rs:1826-1987): token at
+ * position `pos` through all layers, updating `kv`; the final hidden state
+ * (pre-norm) is copied to hidden_out when non-NULL. */
+zgpu_status zgpu_forward_single_token(zgpu_model *m, zgpu_kv *kv, uint32_t token, uint32_t pos,
+                                      float *hidden_out);
+/* lm_head_argmax_dynamic (lm_head.rs:98-166) / lm_head_argmax_avx512
+ * (inference_avx512.rs:1200-1270) on the model's current hidden state:
+ * final RMSNorm, logits over vocab_padded rows, first-max argmax, then the
+ * non-finite / padding checks against vocab_real.  logits_out (nullable)
+ * receives vocab_padded floats. */
+zgpu_status zgpu_lm_head_argmax(zgpu_model *m, uint32_t vocab_real, uint32_t *token_out,
+                                float *logits_out);
+/* The reference's generation loop (inference.rs:1188-1320 prefill,
+ * :1836-1999 decode): forward every prompt token, take the LM-head argmax
+ * after the last one, then n_gen-1 greedy steps (forward + LM head).
+ * tokens_out receives n_gen ids.  The decode step runs as one CUDA graph
+ * replay with the token chained on the device.  logits_out (nullable)
+ * receives n_gen * vocab_padded floats. */
+zgpu_status zgpu_generate_greedy(zgpu_model *m, zgpu_kv *kv, const uint32_t *prompt,
+                                 uint32_t n_prompt, uint32_t n_gen, uint32_t *tokens_out,
+                                 float *logits_out);
+
+/* Per-kernel-class counters, mirroring Avx512PerfCounters
+ * (inference_avx512.rs:274-330): calls and device milliseconds of the last
+ * zgpu_generate_greedy decode phase. */
+typedef struct zgpu_perf {
+  uint64_t steps;
+  uint64_t kernel_launches;   /* of this library's kernels */
+  double decode_ms;           /* device time of the decode steps */
+  double prefill_ms;
+} zgpu_perf;
+zgpu_status zgpu_perf_snapshot(const zgpu_model *m, zgpu_perf *out);
+
+/* ------------------------------------------ synthetic .smodel generation */
+/* Deterministic seeded tensors for the BASELINE configs (counter-based
+ * SplitMix64, so any sub-range is reproducible).  Blocks are written in the
+ * plain row-major layout; zgpu_pack_x4 re-lays them out as the packer's
+ * writer does (tools/silicatepack.py:982-1022). */
+/* Q4_0: nibbles uniform 0..15, d = fp16(|N(0, sigma)| / 8). */
+void zgpu_synth_q4_0(uint64_t seed, uint64_t stream, uint64_t rows, uint64_t cols, float sigma,
+                     void *out);
+/* Q8_0: i8 uniform -127..127, d = fp16(scale). */
+void zgpu_synth_q8_0(uint64_t seed, uint64_t stream, uint64_t rows, uint64_t cols, float scale,
+                     void *out);
+/* f32 N(mean, sigma) values (sigma 0 gives a constant). */
+void zgpu_synth_f32(uint64_t seed, uint64_t stream, uint64_t n, float mean, float sigma,
+                    float *out);
+/* uniform token ids in [0, vocab). */
+void zgpu_synth_tokens(uint64_t seed, uint64_t stream, uint64_t n, uint32_t vocab, uint32_t *out);
+/* Plain -> X4 (quant ZGPU_Q4_0 or ZGPU_Q8_0); rows % 4 == 0, cols % 32 == 0. */
+zgpu_status zgpu_pack_x4(const void *plain, void *x4, uint64_t rows, uint64_t cols,
+                         uint32_t quant);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ZGPU_H */

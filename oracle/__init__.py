@@ -1,0 +1,337 @@
+"""CPU parity oracle for the zero-llm-inference decode hot path (ctypes wrapper).
+
+TEST INFRASTRUCTURE ONLY.  Only ``tests/``, ``__graft_entry__.smoke()`` and
+``bench.py``'s CPU-baseline / reference arm may import this module, and only
+as the checker or the timed CPU baseline.  The product package ``zero_b200``
+never imports it.  The C sources (``zoracle.c``) restate the reference's
+scalar crate order and its AVX-512 kernel order; see ``zoracle.h``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "liboracle.so"
+
+Q4_0, Q8_0 = 2, 8
+ORDER_SCALAR, ORDER_AVX512 = 0, 1
+
+_f32p = C.POINTER(C.c_float)
+_u8p = C.POINTER(C.c_uint8)
+_u32p = C.POINTER(C.c_uint32)
+
+
+def build() -> Path:
+    """Compile liboracle.so with the committed Makefile (gcc, no GPU)."""
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return LIB_PATH
+
+
+def _load() -> C.CDLL:
+    if not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < (HERE / "zoracle.c").stat().st_mtime:
+        build()
+    lib = C.CDLL(str(LIB_PATH))
+    sz = C.c_size_t
+    sig = {
+        "zo_fp16_to_f32": (C.c_float, [C.c_uint16]),
+        "zo_f64_to_fp16": (C.c_uint16, [C.c_double]),
+        "zo_dequant_q4_0_block": (None, [_u8p, _f32p]),
+        "zo_dequant_q8_0_block": (None, [_u8p, _f32p]),
+        "zo_quantize_q4_0_block": (None, [_f32p, _u8p]),
+        "zo_quantize_q8_0_block": (None, [_f32p, _u8p]),
+        "zo_quantize_row_q8_0": (None, [_f32p, _u8p, sz]),
+        "zo_linear_q4_0_q8act": (None, [_u8p, _u8p, _f32p, sz, sz]),
+        "zo_interleave_x4": (C.c_int, [_u8p, _u8p, sz, sz, C.c_int]),
+        "zo_rmsnorm": (None, [_f32p, _f32p, _f32p, sz, C.c_float]),
+        "zo_rope_ctx": (None, [C.c_float, sz, _f32p]),
+        "zo_rope": (None, [_f32p, _f32p, sz, sz]),
+        "zo_linear_q4_0": (None, [_f32p, _u8p, _f32p, sz, sz]),
+        "zo_linear_q8_0": (None, [_f32p, _u8p, _f32p, sz, sz]),
+        "zo_linear_dispatch": (C.c_int, [_f32p, _u8p, _f32p, sz, sz, C.c_int]),
+        "zo_softmax": (C.c_int, [_f32p, sz]),
+        "zo_linear_q4_0x4_avx512": (None, [_f32p, _u8p, _f32p, sz, sz, C.c_int, C.c_int]),
+        "zo_linear_q8_0x4_avx512": (None, [_f32p, _u8p, _f32p, sz, sz, C.c_int, C.c_int]),
+        "zo_linear_q4_0_avx512": (None, [_f32p, _u8p, _f32p, sz, sz, C.c_int, C.c_int]),
+        "zo_linear_q8_0_avx512": (None, [_f32p, _u8p, _f32p, sz, sz, C.c_int, C.c_int]),
+        "zo_dot_product_avx512": (C.c_float, [_f32p, _f32p, sz]),
+        "zo_weighted_add_avx512": (None, [C.c_float, _f32p, _f32p, sz]),
+        "zo_argmax_avx512": (sz, [_f32p, sz, _f32p]),
+        "zo_exp_avx512": (None, [_f32p, _f32p, sz]),
+        "zo_silu_mul_avx512": (None, [_f32p, _f32p, _f32p, sz]),
+        "zo_rope_sincos_lut_avx512": (None, [sz, _f32p, _f32p, _f32p, sz]),
+        "zo_rope_apply_avx512": (None, [_f32p, _f32p, _f32p, sz]),
+        "zo_have_avx512": (C.c_int, []),
+        "zo_run_create": (C.c_void_p, [C.c_void_p, C.c_uint32, C.c_int, C.c_int, C.c_int]),
+        "zo_run_destroy": (None, [C.c_void_p]),
+        "zo_run_forward": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, _f32p]),
+        "zo_run_lm_head": (C.c_int, [C.c_void_p, _u32p, _f32p]),
+        "zo_run_kv": (_f32p, [C.c_void_p]),
+        "zo_run_generate": (C.c_int, [C.c_void_p, _u32p, C.c_uint32, C.c_uint32, _u32p, _f32p, _f32p]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+LIB = _load()
+
+
+def _f(a: np.ndarray):
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_f32p)
+
+
+def _b(a: np.ndarray):
+    assert a.dtype == np.uint8 and a.flags.c_contiguous
+    return a.ctypes.data_as(_u8p)
+
+
+def _u(a: np.ndarray):
+    assert a.dtype == np.uint32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_u32p)
+
+
+# ---------------------------------------------------------------- codecs
+def fp16_to_f32(bits: int) -> float:
+    return LIB.zo_fp16_to_f32(bits)
+
+
+def f64_to_fp16(v: float) -> int:
+    return LIB.zo_f64_to_fp16(v)
+
+
+def quantize_q4_0_block(v) -> bytes:
+    x = np.ascontiguousarray(np.asarray(v, dtype=np.float32))
+    out = np.zeros(18, np.uint8)
+    LIB.zo_quantize_q4_0_block(_f(x), _b(out))
+    return out.tobytes()
+
+
+def quantize_q8_0_block(v) -> bytes:
+    x = np.ascontiguousarray(np.asarray(v, dtype=np.float32))
+    out = np.zeros(34, np.uint8)
+    LIB.zo_quantize_q8_0_block(_f(x), _b(out))
+    return out.tobytes()
+
+
+def quantize_row_q8_0(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.zeros(x.size // 32 * 34, np.uint8)
+    LIB.zo_quantize_row_q8_0(_f(x), _b(out), x.size)
+    return out
+
+
+def linear_q4_0_q8act(xq: np.ndarray, w: np.ndarray, in_dim: int, out_dim: int) -> np.ndarray:
+    out = np.zeros(out_dim, np.float32)
+    LIB.zo_linear_q4_0_q8act(_b(np.ascontiguousarray(xq, np.uint8)), _b(np.ascontiguousarray(w, np.uint8)),
+                             _f(out), in_dim, out_dim)
+    return out
+
+
+def dequant_q4_0_block(blk: bytes) -> np.ndarray:
+    b = np.frombuffer(blk, np.uint8).copy()
+    out = np.zeros(32, np.float32)
+    LIB.zo_dequant_q4_0_block(_b(b), _f(out))
+    return out
+
+
+def dequant_q8_0_block(blk: bytes) -> np.ndarray:
+    b = np.frombuffer(blk, np.uint8).copy()
+    out = np.zeros(32, np.float32)
+    LIB.zo_dequant_q8_0_block(_b(b), _f(out))
+    return out
+
+
+def interleave_x4(plain: np.ndarray, rows: int, cols: int, quant: int) -> np.ndarray:
+    plain = np.ascontiguousarray(plain, dtype=np.uint8)
+    out = np.zeros_like(plain)
+    rc = LIB.zo_interleave_x4(_b(plain), _b(out), rows, cols, quant)
+    if rc:
+        raise ValueError(f"interleave_x4 rejected rows={rows} cols={cols}")
+    return out
+
+
+# ------------------------------------------------------------ scalar ops
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.zeros_like(x)
+    LIB.zo_rmsnorm(_f(x), _f(w), _f(out), x.size, eps)
+    return out
+
+
+def rope_ctx(base: float, half: int) -> np.ndarray:
+    out = np.zeros(half, np.float32)
+    LIB.zo_rope_ctx(base, half, _f(out))
+    return out
+
+
+def rope(qk: np.ndarray, inv: np.ndarray, pos: int) -> np.ndarray:
+    qk = np.ascontiguousarray(qk, np.float32).copy()
+    inv = np.ascontiguousarray(inv, np.float32)
+    LIB.zo_rope(_f(qk), _f(inv), inv.size, pos)
+    return qk
+
+
+def linear(x: np.ndarray, w: np.ndarray, in_dim: int, out_dim: int, quant: int) -> np.ndarray:
+    """Scalar linear_dispatch (ops.rs:486) on plain blocks."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros(out_dim, np.float32)
+    rc = LIB.zo_linear_dispatch(_f(x), _b(np.ascontiguousarray(w, np.uint8)), _f(out), in_dim, out_dim, quant)
+    if rc:
+        raise ValueError(f"linear_dispatch: unsupported quant {quant}")
+    return out
+
+
+def linear_x4_avx512(x, w_x4, in_dim, out_dim, quant, threads=0, simd=1) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros(out_dim, np.float32)
+    fn = LIB.zo_linear_q4_0x4_avx512 if quant == Q4_0 else LIB.zo_linear_q8_0x4_avx512
+    fn(_f(x), _b(np.ascontiguousarray(w_x4, np.uint8)), _f(out), in_dim, out_dim, threads, simd)
+    return out
+
+
+def linear_plain_avx512(x, w, in_dim, out_dim, quant, threads=0) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros(out_dim, np.float32)
+    fn = LIB.zo_linear_q4_0_avx512 if quant == Q4_0 else LIB.zo_linear_q8_0_avx512
+    fn(_f(x), _b(np.ascontiguousarray(w, np.uint8)), _f(out), in_dim, out_dim, threads, 0)
+    return out
+
+
+def softmax(s: np.ndarray):
+    s = np.ascontiguousarray(s, np.float32).copy()
+    rc = LIB.zo_softmax(_f(s), s.size)
+    return rc, s
+
+
+def exp_avx512(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.zeros_like(x)
+    LIB.zo_exp_avx512(_f(x), _f(y), x.size)
+    return y
+
+
+def silu_mul_avx512(g: np.ndarray, u: np.ndarray) -> np.ndarray:
+    g = np.ascontiguousarray(g, np.float32)
+    u = np.ascontiguousarray(u, np.float32)
+    out = np.zeros_like(g)
+    LIB.zo_silu_mul_avx512(_f(g), _f(u), _f(out), g.size)
+    return out
+
+
+def rope_lut_avx512(pos: int, inv: np.ndarray):
+    inv = np.ascontiguousarray(inv, np.float32)
+    c = np.zeros_like(inv)
+    s = np.zeros_like(inv)
+    LIB.zo_rope_sincos_lut_avx512(pos, _f(inv), _f(c), _f(s), inv.size)
+    return c, s
+
+
+def rope_apply_avx512(qk: np.ndarray, c: np.ndarray, s: np.ndarray) -> np.ndarray:
+    qk = np.ascontiguousarray(qk, np.float32).copy()
+    LIB.zo_rope_apply_avx512(_f(qk), _f(np.ascontiguousarray(c, np.float32)),
+                             _f(np.ascontiguousarray(s, np.float32)), c.size)
+    return qk
+
+
+def argmax_avx512(v: np.ndarray):
+    v = np.ascontiguousarray(v, np.float32)
+    mx = C.c_float(0)
+    idx = LIB.zo_argmax_avx512(_f(v), v.size, C.byref(mx))
+    return idx, mx.value
+
+
+def have_avx512() -> bool:
+    return bool(LIB.zo_have_avx512())
+
+
+# ------------------------------------------------------------ model runs
+class _Layer(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "attn_norm", "attn_q", "attn_k", "attn_v", "attn_o", "q_norm", "k_norm",
+        "ffn_norm", "ffn_gate", "ffn_up", "ffn_down")]
+
+
+class _Model(C.Structure):
+    _fields_ = [
+        ("n_layers", C.c_uint32), ("hidden", C.c_uint32), ("ffn", C.c_uint32),
+        ("n_q_heads", C.c_uint32), ("n_kv_heads", C.c_uint32), ("head_dim", C.c_uint32),
+        ("vocab_padded", C.c_uint32), ("vocab_real", C.c_uint32),
+        ("rms_eps", C.c_float), ("rope_theta", C.c_float),
+        ("token_embd_quant", C.c_int), ("token_embd", C.c_void_p),
+        ("output_quant", C.c_int), ("output", C.c_void_p), ("output_norm", C.c_void_p),
+        ("layers", C.POINTER(_Layer)),
+    ]
+
+
+class OracleRun:
+    """A Qwen3-shaped decode run on the CPU oracle.
+
+    ``weights`` is the dict produced by ``zero_b200.synth.qwen3_weights``
+    (plain-layout blocks).  order: ORDER_SCALAR (crate, forward_pass.rs:515)
+    or ORDER_AVX512 (inference_avx512.rs:1826).
+    """
+
+    def __init__(self, cfg, weights, max_tokens: int, order: int = ORDER_AVX512,
+                 threads: int = 0, simd: int = 1):
+        self._keep = weights
+        L = cfg.n_layers
+        self._layers = (_Layer * L)()
+        for i in range(L):
+            lw = weights["layers"][i]
+            for name in _Layer._fields_:
+                setattr(self._layers[i], name[0], lw[name[0]].ctypes.data)
+        self._m = _Model(
+            cfg.n_layers, cfg.hidden, cfg.ffn, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim,
+            cfg.vocab_padded, cfg.vocab_real, cfg.rms_eps, cfg.rope_theta,
+            Q8_0 if cfg.embd_quant == "q8_0" else Q4_0, weights["token_embd"].ctypes.data,
+            Q8_0 if cfg.output_quant == "q8_0" else Q4_0, weights["output"].ctypes.data,
+            weights["output_norm"].ctypes.data, self._layers)
+        self.cfg = cfg
+        self.max_tokens = max_tokens
+        self._r = LIB.zo_run_create(C.byref(self._m), max_tokens, order, threads, simd)
+        if not self._r:
+            raise MemoryError("oracle run allocation failed")
+
+    def close(self):
+        if self._r:
+            LIB.zo_run_destroy(self._r)
+            self._r = None
+
+    def __del__(self):
+        self.close()
+
+    def forward(self, token: int, pos: int) -> np.ndarray:
+        h = np.zeros(self.cfg.hidden, np.float32)
+        rc = LIB.zo_run_forward(self._r, token, pos, _f(h))
+        if rc:
+            raise RuntimeError(f"oracle forward failed: {rc}")
+        return h
+
+    def lm_head(self):
+        logits = np.zeros(self.cfg.vocab_padded, np.float32)
+        tok = C.c_uint32(0)
+        rc = LIB.zo_run_lm_head(self._r, C.byref(tok), _f(logits))
+        return rc, tok.value, logits
+
+    def kv(self) -> np.ndarray:
+        c = self.cfg
+        n = 2 * c.n_layers * self.max_tokens * c.n_kv_heads * c.head_dim
+        return np.ctypeslib.as_array(LIB.zo_run_kv(self._r), shape=(n,)).copy()
+
+    def generate(self, prompt, n_gen: int, want_logits: bool = False):
+        p = np.ascontiguousarray(prompt, np.uint32)
+        toks = np.zeros(n_gen, np.uint32)
+        margins = np.zeros(n_gen, np.float32)
+        logits = np.zeros((n_gen, self.cfg.vocab_padded), np.float32) if want_logits else None
+        rc = LIB.zo_run_generate(self._r, _u(p), p.size, n_gen, _u(toks), _f(margins),
+                                 _f(logits) if want_logits else None)
+        return rc, toks, margins, logits

@@ -1,0 +1,154 @@
+/*
+ * zoracle.h — CPU parity oracle for the zero-llm-inference decode hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is a plain-C restatement of the
+ * reference's CPU algorithms (silicatetech/zero).  Only tests/, the smoke()
+ * check in __graft_entry__.py and bench.py's cpu_baseline / reference arm
+ * may load it, and only as the checker or the timed CPU baseline — never
+ * as part of the product path (zero_b200/ never links or imports it).
+ *
+ * Two orders are restated:
+ *   - "scalar": the crate `crates/zero-llm-inference` (sequential f32,
+ *     unfused multiply-add, libm expf/sinf/cosf/powf/sqrtf), which reads
+ *     plain Q4_0/Q8_0 blocks;
+ *   - "avx512": the kernel-side SIMD path `kernel/src/inference_avx512.rs`
+ *     + `kernel/src/arch/x86_64/math/{linear,activation,trig}.rs`, whose
+ *     16-lane accumulator order, FMA use and horizontal-reduction tree are
+ *     restated lane by lane (portable C with fmaf), and — when the host has
+ *     AVX-512F — also with real intrinsics for the timed baseline.  Both
+ *     forms must agree bit for bit (tested).
+ *
+ * Pinning: the block encoders and X4 permutation are pinned against golden
+ * fixtures generated from the reference's own tools/silicatepack.py
+ * (tests/golden/gen_packer_golden.py); the linear/dequant/rmsnorm/rope
+ * known-answer values come from the reference's unit tests
+ * (ops.rs:531-1160, dequant.rs:553-1088).  The libm crate 0.2.16
+ * (Cargo.lock:331) is not vendored: glibc's expf/powf share its upstream
+ * algorithm; sinf/cosf agreement is at the <=1 ULP level (unpinned).
+ */
+#ifndef ZORACLE_H
+#define ZORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ggml type ids (zero-gguf-parser lib.rs GgmlType) and the .smodel v2 ids. */
+enum { ZO_F32 = 0, ZO_F16 = 1, ZO_Q4_0 = 2, ZO_Q8_0 = 8, ZO_Q4_0X4 = 100, ZO_Q8_0X4 = 101 };
+
+/* Error codes (mirror of the Rust enums the path returns). */
+enum {
+  ZO_OK = 0,
+  ZO_ERR_ARG = 1,
+  ZO_ERR_UNSUPPORTED_QUANT = 2,
+  ZO_ERR_KV_TOKEN_OUT_OF_RANGE = 10,
+  ZO_ERR_KV_LAYER_OUT_OF_RANGE = 11,
+  ZO_ERR_KV_TOKEN_COUNT = 13,
+  ZO_ERR_NUMERICAL_INSTABILITY = 20,
+  ZO_ERR_LM_NON_FINITE = 40,
+  ZO_ERR_LM_PADDING = 41,
+};
+
+/* ---- fp16 / block codecs ------------------------------------------------ */
+float    zo_fp16_to_f32(uint16_t bits);
+uint16_t zo_f64_to_fp16(double v);
+void     zo_dequant_q4_0_block(const uint8_t *blk, float *out32);
+void     zo_dequant_q8_0_block(const uint8_t *blk, float *out32);
+void     zo_quantize_q4_0_block(const float *v32, uint8_t *out18);
+void     zo_quantize_q8_0_block(const float *v32, uint8_t *out34);
+/* Q8_0 activation quantiser (n % 32 == 0): one zo_quantize_q8_0_block per block. */
+void     zo_quantize_row_q8_0(const float *x, uint8_t *out, size_t n);
+/* Plain -> .smodel-v2 4-row interleave.  quant = ZO_Q4_0 or ZO_Q8_0. */
+int      zo_interleave_x4(const uint8_t *plain, uint8_t *x4, size_t rows, size_t cols, int quant);
+
+/* Q4_0 weights (plain) x Q8_0 activation blocks: no counterpart in the
+ * reference decode path; restates ggml's vec_dot_q4_0_q8_0 reference loop
+ * (the GGUF ecosystem's definition of this product, zero-gguf-parser carries
+ * the formats): per block sumi = sum_j (n_j - 8) * q_j exactly, then
+ * acc += (sumi * d_w) * d_x in block order. */
+void     zo_linear_q4_0_q8act(const uint8_t *xq, const uint8_t *w, float *out, size_t in_dim,
+                              size_t out_dim);
+
+/* ---- scalar crate ops --------------------------------------------------- */
+void  zo_rmsnorm(const float *x, const float *w, float *out, size_t n, float eps);
+void  zo_rope_ctx(float freq_base, size_t half, float *inv_freqs);
+void  zo_rope(float *qk, const float *inv_freqs, size_t half, size_t pos);
+void  zo_linear_q4_0(const float *x, const uint8_t *w, float *out, size_t in_dim, size_t out_dim);
+void  zo_linear_q8_0(const float *x, const uint8_t *w, float *out, size_t in_dim, size_t out_dim);
+int   zo_linear_dispatch(const float *x, const uint8_t *w, float *out, size_t in_dim,
+                         size_t out_dim, int quant);
+int   zo_softmax(float *scores, size_t len);
+
+/* ---- AVX-512-order ops (lane-exact restatement) -------------------------- */
+/* threads <= 0 -> all cores.  simd: 0 portable lane emulation, 1 intrinsics
+ * when available (falls back to emulation otherwise). */
+void  zo_linear_q4_0x4_avx512(const float *x, const uint8_t *w_x4, float *out, size_t in_dim,
+                              size_t out_dim, int threads, int simd);
+void  zo_linear_q8_0x4_avx512(const float *x, const uint8_t *w_x4, float *out, size_t in_dim,
+                              size_t out_dim, int threads, int simd);
+/* Same per-row math on the plain layout (linear.rs:710, :1271). */
+void  zo_linear_q4_0_avx512(const float *x, const uint8_t *w, float *out, size_t in_dim,
+                            size_t out_dim, int threads, int simd);
+void  zo_linear_q8_0_avx512(const float *x, const uint8_t *w, float *out, size_t in_dim,
+                            size_t out_dim, int threads, int simd);
+float zo_dot_product_avx512(const float *a, const float *b, size_t len);
+void  zo_weighted_add_avx512(float weight, const float *vec, float *out, size_t len);
+size_t zo_argmax_avx512(const float *v, size_t n, float *max_out);
+void  zo_exp_avx512(const float *x, float *y, size_t n);
+void  zo_silu_mul_avx512(const float *g, const float *u, float *out, size_t n);
+void  zo_rope_sincos_lut_avx512(size_t pos, const float *inv_freqs, float *cos_out,
+                                float *sin_out, size_t len);
+void  zo_rope_apply_avx512(float *qk, const float *cos_lut, const float *sin_lut, size_t half);
+int   zo_have_avx512(void);
+
+/* ---- Qwen3-shaped model ------------------------------------------------- */
+typedef struct zo_qwen3_layer {
+  const float   *attn_norm;   /* [hidden] */
+  const uint8_t *attn_q;      /* plain Q4_0 [q_dim x hidden] */
+  const uint8_t *attn_k;      /* plain Q4_0 [kv_dim x hidden] */
+  const uint8_t *attn_v;      /* plain Q4_0 [kv_dim x hidden] */
+  const uint8_t *attn_o;      /* plain Q4_0 [hidden x q_dim] */
+  const float   *q_norm;      /* [head_dim] */
+  const float   *k_norm;      /* [head_dim] */
+  const float   *ffn_norm;    /* [hidden] */
+  const uint8_t *ffn_gate;    /* plain Q4_0 [ffn x hidden] */
+  const uint8_t *ffn_up;      /* plain Q4_0 [ffn x hidden] */
+  const uint8_t *ffn_down;    /* plain Q4_0 [hidden x ffn] */
+} zo_qwen3_layer;
+
+typedef struct zo_qwen3 {
+  uint32_t n_layers, hidden, ffn, n_q_heads, n_kv_heads, head_dim;
+  uint32_t vocab_padded, vocab_real;
+  float    rms_eps, rope_theta;
+  int      token_embd_quant;   /* ZO_Q8_0 (plain rows) */
+  const uint8_t *token_embd;   /* [vocab x hidden] */
+  int      output_quant;       /* ZO_Q8_0 or ZO_Q4_0 */
+  const uint8_t *output;       /* plain [vocab x hidden] (tied: == token_embd) */
+  const float   *output_norm;  /* [hidden] */
+  const zo_qwen3_layer *layers;
+} zo_qwen3;
+
+/* order: 0 = scalar crate path (forward_pass.rs:515), 1 = AVX-512 kernel path
+ * (inference_avx512.rs:1826).  The run keeps its own f32 KV cache with the
+ * kv_cache.rs:100 layout. */
+typedef struct zo_run zo_run;
+zo_run *zo_run_create(const zo_qwen3 *m, uint32_t max_tokens, int order, int threads, int simd);
+void    zo_run_destroy(zo_run *r);
+int     zo_run_forward(zo_run *r, uint32_t token, uint32_t pos, float *hidden_out);
+/* lm_head_argmax_dynamic (lm_head.rs:98) / lm_head_argmax_avx512 (inference_avx512.rs:1200). */
+int     zo_run_lm_head(zo_run *r, uint32_t *token_out, float *logits_out);
+const float *zo_run_kv(const zo_run *r);
+/* Prefill the prompt (one forward per token) then n_gen greedy steps. tokens_out
+ * receives n_gen ids; margins_out (nullable) the top1-top2 logit gap per step;
+ * logits_last (nullable) the logits of the final step. Returns the status of the
+ * first failing call, or ZO_OK. */
+int     zo_run_generate(zo_run *r, const uint32_t *prompt, uint32_t n_prompt, uint32_t n_gen,
+                        uint32_t *tokens_out, float *margins_out, float *logits_all);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

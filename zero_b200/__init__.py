@@ -1,0 +1,253 @@
+"""zero_b200 — B200 (sm_100a) drop-in for the zero-llm-inference decode hot path.
+
+Python mirror of the crate API the C ABI (include/zgpu.h) exports, used by
+the tests and the benchmark.  The names follow the reference crate
+(crates/zero-llm-inference): ``linear_dispatch`` (ops.rs:486), ``rmsnorm``
+(ops.rs:29), ``KvCache`` (kv_cache.rs:32), ``forward_single_token``
+(forward_pass.rs:515), ``lm_head_argmax_dynamic`` (lm_head.rs:98), and the
+greedy loop of kernel/src/inference.rs:1836.  Errors surface as ZgpuError
+carrying the status code that mirrors the Rust error enum.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from ._lib import LIB, ZgpuOpts, ZgpuPerf, ZgpuQwen3Desc, ZgpuQwen3Layer
+from . import synth
+from .synth import QWEN3_1_7B, Qwen3Config
+
+ABI_VERSION = 1
+F32, F16, Q4_0, Q8_0, Q4_0X4, Q8_0X4 = 0, 1, 2, 8, 100, 101
+FLAG_NO_GRAPH, FLAG_NO_PDL = 0x1, 0x2
+
+STATUS = {
+    0: "OK", 1: "INVALID_ARG", 2: "UNSUPPORTED_QUANT", 3: "UNREGISTERED_WEIGHT",
+    10: "KV_TOKEN_OUT_OF_RANGE", 11: "KV_LAYER_OUT_OF_RANGE", 12: "KV_INVALID_SLICE_LENGTH",
+    13: "KV_TOKEN_COUNT_EXCEEDS_MAX", 20: "NUMERICAL_INSTABILITY", 30: "EMBED_UNSUPPORTED_QUANT",
+    31: "EMBED_DIM_MISALIGNMENT", 40: "LM_NON_FINITE_LOGITS", 41: "LM_ARGMAX_IN_PADDING",
+    90: "NO_DEVICE", 91: "CUDA", 92: "OUT_OF_MEMORY", 93: "DEVICE_TIMEOUT",
+}
+
+
+class ZgpuError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS.get(status, status)}: {message}")
+        self.status = status
+        self.name = STATUS.get(status, str(status))
+
+
+def _ptr(a: np.ndarray) -> int:
+    if not a.flags.c_contiguous:
+        raise ValueError("array must be C-contiguous")
+    return a.ctypes.data
+
+
+class Context:
+    """A device context (zgpu_init).  Keeps every registered host array alive."""
+
+    def __init__(self, device: int = 0, graph: bool = True, pdl: bool = True):
+        flags = (0 if graph else FLAG_NO_GRAPH) | (0 if pdl else FLAG_NO_PDL)
+        opts = ZgpuOpts(ABI_VERSION, device, flags)
+        h = C.c_void_p()
+        st = LIB.zgpu_init(C.byref(opts), C.byref(h))
+        if st:
+            raise ZgpuError(st, LIB.zgpu_status_string(st).decode())
+        self.h = h
+        self._keep: dict[int, np.ndarray] = {}
+
+    def _check(self, st: int):
+        if st:
+            raise ZgpuError(st, (LIB.zgpu_last_error(self.h) or b"").decode())
+
+    def close(self):
+        if getattr(self, "h", None):
+            LIB.zgpu_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def device_info(self) -> tuple[int, int, int]:
+        sm, ma, mi = C.c_int32(), C.c_int32(), C.c_int32()
+        self._check(LIB.zgpu_device_info(self.h, C.byref(sm), C.byref(ma), C.byref(mi)))
+        return sm.value, ma.value, mi.value
+
+    def synchronize(self):
+        self._check(LIB.zgpu_synchronize(self.h))
+
+    # -------------------------------------------------- weight registry
+    def register(self, arr: np.ndarray, dtype: int, rows: int, cols: int) -> int:
+        """weight_layout::register + upload; returns the key (host address)."""
+        self._check(LIB.zgpu_register_weights(self.h, _ptr(arr), arr.nbytes, dtype, rows, cols))
+        self._keep[_ptr(arr)] = arr
+        return _ptr(arr)
+
+    def group_of(self, arr_or_key) -> int:
+        key = arr_or_key if isinstance(arr_or_key, int) else _ptr(arr_or_key)
+        return int(LIB.zgpu_group_of(self.h, key))
+
+    def clear_weights(self):
+        self._check(LIB.zgpu_clear_weights(self.h))
+        self._keep.clear()
+
+    # -------------------------------------------------------- matmul ops
+    def linear_dispatch(self, x: np.ndarray, w, in_dim: int, out_dim: int, quant: int) -> np.ndarray:
+        """linear_dispatch (ops.rs:486) with the registered weight `w` (array or key)."""
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty(out_dim, np.float32)
+        key = w if isinstance(w, int) else _ptr(w)
+        self._check(LIB.zgpu_linear_dispatch(self.h, _ptr(x), key, _ptr(out), in_dim, out_dim, quant))
+        return out
+
+    def linear_dispatch_device(self, d_x: int, w, d_out: int, in_dim: int, out_dim: int, quant: int,
+                               stream: int = 0):
+        key = w if isinstance(w, int) else _ptr(w)
+        self._check(LIB.zgpu_linear_dispatch_device(self.h, d_x, key, d_out, in_dim, out_dim, quant,
+                                                    stream or None))
+
+    def quantize_q8_0(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty(x.size // 32 * 34, np.uint8)
+        self._check(LIB.zgpu_quantize_q8_0(self.h, _ptr(x), _ptr(out), x.size))
+        return out
+
+    def linear_q8act(self, xq: np.ndarray, w, in_dim: int, out_dim: int) -> np.ndarray:
+        out = np.empty(out_dim, np.float32)
+        key = w if isinstance(w, int) else _ptr(w)
+        self._check(LIB.zgpu_linear_q8act(self.h, _ptr(np.ascontiguousarray(xq, np.uint8)), key,
+                                          _ptr(out), in_dim, out_dim))
+        return out
+
+    # ---------------------------------------------------------- small ops
+    def rmsnorm(self, x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        w = np.ascontiguousarray(w, np.float32)
+        out = np.empty_like(x)
+        self._check(LIB.zgpu_rmsnorm(self.h, _ptr(x), _ptr(w), _ptr(out), x.size, eps))
+        return out
+
+    def rope(self, qk: np.ndarray, n_heads: int, head_dim: int, pos: int, base: float) -> np.ndarray:
+        qk = np.ascontiguousarray(qk, np.float32).copy()
+        self._check(LIB.zgpu_rope(self.h, _ptr(qk), n_heads, head_dim, pos, base))
+        return qk
+
+    def silu_mul(self, g: np.ndarray, u: np.ndarray) -> np.ndarray:
+        g = np.ascontiguousarray(g, np.float32)
+        u = np.ascontiguousarray(u, np.float32)
+        out = np.empty_like(g)
+        self._check(LIB.zgpu_silu_mul(self.h, _ptr(g), _ptr(u), _ptr(out), g.size))
+        return out
+
+
+class KvCache:
+    """KvCache::new (kv_cache.rs:100) in device memory, same logical layout."""
+
+    def __init__(self, ctx: Context, max_tokens: int, n_layers: int, n_kv_heads: int, head_dim: int):
+        self.ctx = ctx
+        self.max_tokens, self.n_layers, self.n_kv_heads, self.head_dim = max_tokens, n_layers, n_kv_heads, head_dim
+        h = C.c_void_p()
+        ctx._check(LIB.zgpu_kv_create(ctx.h, max_tokens, n_layers, n_kv_heads, head_dim, C.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            LIB.zgpu_kv_destroy(self.h)
+            self.h = None
+
+    def store_kv(self, layer: int, token: int, k: np.ndarray, v: np.ndarray):
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        self.ctx._check(LIB.zgpu_kv_store(self.h, layer, token, _ptr(k), _ptr(v), k.size))
+
+    def read(self, layer: int, token_count: int):
+        n = token_count * self.n_kv_heads * self.head_dim
+        k = np.empty(n, np.float32)
+        v = np.empty(n, np.float32)
+        self.ctx._check(LIB.zgpu_kv_read(self.h, layer, token_count, _ptr(k), _ptr(v)))
+        return k, v
+
+
+class Qwen3Model:
+    """A Qwen3-shaped model on the device, built from synth.qwen3_weights() tensors.
+
+    Matmul tensors are registered in the .smodel-v2 X4 layout (dtype 100/101)
+    when `<name>_x4` copies exist, else as plain Q4_0 blocks.
+    """
+
+    def __init__(self, ctx: Context, cfg: Qwen3Config, weights: dict):
+        self.ctx, self.cfg, self.w = ctx, cfg, weights
+        H = cfg.hidden
+        eq = Q8_0 if cfg.embd_quant == "q8_0" else Q4_0
+        oq = Q8_0 if cfg.output_quant == "q8_0" else Q4_0
+        emb_key = ctx.register(weights["token_embd"], eq, cfg.vocab_padded, H)
+        if "output_x4" in weights:
+            out_key = ctx.register(weights["output_x4"], Q8_0X4 if oq == Q8_0 else Q4_0X4, cfg.vocab_padded, H)
+        elif weights["output"] is weights["token_embd"]:
+            out_key = emb_key
+        else:
+            out_key = ctx.register(weights["output"], oq, cfg.vocab_padded, H)
+        shapes = synth.layer_shapes(cfg)
+        self._layers = (ZgpuQwen3Layer * cfg.n_layers)()
+        for i, lw in enumerate(weights["layers"]):
+            L = self._layers[i]
+            for name in synth.LAYER_MATS:
+                rows, cols = shapes[name]
+                if name + "_x4" in lw:
+                    key = ctx.register(lw[name + "_x4"], Q4_0X4, rows, cols)
+                else:
+                    key = ctx.register(lw[name], Q4_0, rows, cols)
+                setattr(L, name, key)
+            for name in synth.LAYER_NORMS:
+                setattr(L, name, _ptr(lw[name]))
+        desc = ZgpuQwen3Desc(
+            cfg.n_layers, H, cfg.ffn, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim,
+            cfg.vocab_padded, cfg.vocab_real, cfg.rms_eps, cfg.rope_theta, eq, emb_key, oq, out_key,
+            _ptr(weights["output_norm"]), self._layers)
+        h = C.c_void_p()
+        ctx._check(LIB.zgpu_qwen3_create(ctx.h, C.byref(desc), C.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            LIB.zgpu_qwen3_destroy(self.h)
+            self.h = None
+
+    def new_kv(self, max_tokens: int) -> KvCache:
+        c = self.cfg
+        return KvCache(self.ctx, max_tokens, c.n_layers, c.n_kv_heads, c.head_dim)
+
+    def forward_single_token(self, kv: KvCache, token: int, pos: int) -> np.ndarray:
+        hidden = np.empty(self.cfg.hidden, np.float32)
+        self.ctx._check(LIB.zgpu_forward_single_token(self.h, kv.h, token, pos, _ptr(hidden)))
+        return hidden
+
+    def lm_head_argmax(self, vocab_real: int | None = None, want_logits: bool = True):
+        tok = C.c_uint32()
+        logits = np.empty(self.cfg.vocab_padded, np.float32) if want_logits else None
+        self.ctx._check(LIB.zgpu_lm_head_argmax(
+            self.h, self.cfg.vocab_real if vocab_real is None else vocab_real, C.byref(tok),
+            _ptr(logits) if want_logits else None))
+        return tok.value, logits
+
+    def generate_greedy(self, kv: KvCache, prompt, n_gen: int, want_logits: bool = False):
+        p = np.ascontiguousarray(prompt, np.uint32)
+        toks = np.empty(n_gen, np.uint32)
+        logits = np.empty((n_gen, self.cfg.vocab_padded), np.float32) if want_logits else None
+        self.ctx._check(LIB.zgpu_generate_greedy(self.h, kv.h, _ptr(p), p.size, n_gen, _ptr(toks),
+                                                 _ptr(logits) if want_logits else None))
+        return toks, logits
+
+    def perf(self) -> dict:
+        p = ZgpuPerf()
+        self.ctx._check(LIB.zgpu_perf_snapshot(self.h, C.byref(p)))
+        return {"steps": p.steps, "kernel_launches": p.kernel_launches, "decode_ms": p.decode_ms,
+                "prefill_ms": p.prefill_ms}
+
+
+__all__ = ["Context", "KvCache", "Qwen3Model", "Qwen3Config", "QWEN3_1_7B", "ZgpuError", "synth",
+           "F32", "Q4_0", "Q8_0", "Q4_0X4", "Q8_0X4"]

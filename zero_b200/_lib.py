@@ -1,0 +1,88 @@
+"""ctypes binding of libzgpu.so (the in-tree sm_100a library).
+
+The library must exist: there is no CPU fallback for the decode path.  Build
+it with ``python -m zero_b200.build``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libzgpu.so"
+
+if not LIB_PATH.exists():
+    raise ImportError(
+        f"{LIB_PATH} is missing: build the CUDA extension with `python -m zero_b200.build` "
+        "(zero_b200 has no CPU fallback)"
+    )
+
+LIB = C.CDLL(str(LIB_PATH))
+
+_vp, _u32, _u64, _i32, _f = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int32, C.c_float
+
+
+class ZgpuOpts(C.Structure):
+    _fields_ = [("abi_version", _u32), ("device", _i32), ("flags", _u32)]
+
+
+class ZgpuQwen3Layer(C.Structure):
+    _fields_ = [(n, _vp) for n in (
+        "attn_norm", "attn_q", "attn_k", "attn_v", "attn_o", "q_norm", "k_norm", "ffn_norm",
+        "ffn_gate", "ffn_up", "ffn_down")]
+
+
+class ZgpuQwen3Desc(C.Structure):
+    _fields_ = [
+        ("n_layers", _u32), ("hidden", _u32), ("ffn", _u32), ("n_q_heads", _u32),
+        ("n_kv_heads", _u32), ("head_dim", _u32), ("vocab_padded", _u32), ("vocab_real", _u32),
+        ("rms_eps", _f), ("rope_theta", _f), ("token_embd_quant", _u32), ("token_embd", _vp),
+        ("output_quant", _u32), ("output", _vp), ("output_norm", _vp),
+        ("layers", C.POINTER(ZgpuQwen3Layer)),
+    ]
+
+
+class ZgpuPerf(C.Structure):
+    _fields_ = [("steps", _u64), ("kernel_launches", _u64), ("decode_ms", C.c_double),
+                ("prefill_ms", C.c_double)]
+
+
+_SIGS = {
+    "zgpu_init": (_i32, [C.POINTER(ZgpuOpts), C.POINTER(_vp)]),
+    "zgpu_destroy": (None, [_vp]),
+    "zgpu_last_error": (C.c_char_p, [_vp]),
+    "zgpu_status_string": (C.c_char_p, [_i32]),
+    "zgpu_device_info": (_i32, [_vp, C.POINTER(_i32), C.POINTER(_i32), C.POINTER(_i32)]),
+    "zgpu_synchronize": (_i32, [_vp]),
+    "zgpu_register_weights": (_i32, [_vp, _vp, C.c_size_t, _u32, _u64, _u64]),
+    "zgpu_group_of": (_u32, [_vp, _vp]),
+    "zgpu_clear_weights": (_i32, [_vp]),
+    "zgpu_linear_dispatch": (_i32, [_vp, _vp, _vp, _vp, _u64, _u64, _u32]),
+    "zgpu_linear_dispatch_device": (_i32, [_vp, _vp, _vp, _vp, _u64, _u64, _u32, _vp]),
+    "zgpu_quantize_q8_0": (_i32, [_vp, _vp, _vp, _u64]),
+    "zgpu_linear_q8act": (_i32, [_vp, _vp, _vp, _vp, _u64, _u64]),
+    "zgpu_rmsnorm": (_i32, [_vp, _vp, _vp, _vp, _u64, _f]),
+    "zgpu_rope": (_i32, [_vp, _vp, _u32, _u32, _u32, _f]),
+    "zgpu_silu_mul": (_i32, [_vp, _vp, _vp, _vp, _u64]),
+    "zgpu_kv_create": (_i32, [_vp, _u32, _u32, _u32, _u32, C.POINTER(_vp)]),
+    "zgpu_kv_destroy": (None, [_vp]),
+    "zgpu_kv_store": (_i32, [_vp, _u32, _u32, _vp, _vp, _u64]),
+    "zgpu_kv_read": (_i32, [_vp, _u32, _u32, _vp, _vp]),
+    "zgpu_qwen3_create": (_i32, [_vp, C.POINTER(ZgpuQwen3Desc), C.POINTER(_vp)]),
+    "zgpu_qwen3_destroy": (None, [_vp]),
+    "zgpu_forward_single_token": (_i32, [_vp, _vp, _u32, _u32, _vp]),
+    "zgpu_lm_head_argmax": (_i32, [_vp, _u32, _vp, _vp]),
+    "zgpu_generate_greedy": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp, _vp]),
+    "zgpu_perf_snapshot": (_i32, [_vp, C.POINTER(ZgpuPerf)]),
+    "zgpu_synth_q4_0": (None, [_u64, _u64, _u64, _u64, _f, _vp]),
+    "zgpu_synth_q8_0": (None, [_u64, _u64, _u64, _u64, _f, _vp]),
+    "zgpu_synth_f32": (None, [_u64, _u64, _u64, _f, _f, _vp]),
+    "zgpu_synth_tokens": (None, [_u64, _u64, _u64, _u32, _vp]),
+    "zgpu_pack_x4": (_i32, [_vp, _vp, _u64, _u64, _u32]),
+}
+
+for _name, (_res, _args) in _SIGS.items():
+    _fn = getattr(LIB, _name)
+    _fn.restype = _res
+    _fn.argtypes = _args
+
+EXPORTED = tuple(_SIGS)

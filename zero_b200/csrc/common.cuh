@@ -1,0 +1,190 @@
+// common.cuh — shared device helpers for the zero-b200 sm_100a kernels.
+//
+// PTX wrappers for the Blackwell features the decode path uses: mbarrier
+// phases, the 1-D TMA bulk copy (cp.async.bulk, no multicast), programmatic
+// dependent launch (griddepcontrol) and named barriers.  Every spin on an
+// mbarrier is bounded by a wall-clock limit read from %globaltimer; on expiry
+// the waiter records ZDEV_ERR_TIMEOUT in the kernel's status word and returns
+// false so the caller can skip its remaining work instead of hanging.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace zgpu {
+
+// Device status word bits (read back by the host after a step).
+enum : uint32_t {
+  ZDEV_ERR_TIMEOUT = 1u << 0,
+  ZDEV_ERR_NUMERICAL = 1u << 1,   // softmax max non-finite or sum <= 0
+  ZDEV_ERR_LM_NONFINITE = 1u << 2,
+  ZDEV_ERR_LM_PADDING = 1u << 3,
+  ZDEV_ERR_BOUNDS = 1u << 4,      // a token / position outside the cache
+};
+
+// 1 s bound on any device-side wait.
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity to complete.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t *status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      atomicOr(status, ZDEV_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completion signalled on
+// the mbarrier as transaction bytes.  dst, src and bytes must be multiples
+// of 16.  No multicast: the source is always this GPU's own memory.
+__device__ __forceinline__ void tma_bulk_g2s(uint32_t dst, const void *src, uint32_t bytes,
+                                             uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1], %2, [%3], %4;" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+// L2 policy for weights streamed exactly once per step: evict first, so the
+// KV cache and activations keep their L2 residency.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// Programmatic dependent launch.  Both are no-ops when the kernel was not
+// launched with the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ float h2f(uint16_t bits) {
+  return __half2float(__ushort_as_half(bits));
+}
+
+// ---------------------------------------------------------------------------
+// Restatements of the reference's own AVX-512 polynomials (activation.rs:56-97
+// and trig.rs:60-127), written with explicitly rounded operations so that no
+// contraction changes them; they reproduce the reference lane values bit for
+// bit given the same inputs.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float ref_exp(float x) {
+  const float log2e = 1.44269504f, ln2_hi = 0.6933594f, ln2_lo = -2.1219444e-4f;
+  // _mm512_min_ps / _mm512_max_ps return the second operand on NaN.
+  x = (x < 88.37625f) ? x : 88.37625f;
+  x = (x > -88.37625f) ? x : -88.37625f;
+  float kf = rintf(__fmul_rn(x, log2e));
+  int k = __float2int_rn(kf);
+  float r = __fmaf_rn(-kf, ln2_lo, __fmaf_rn(-kf, ln2_hi, x));
+  float p = __fmaf_rn(r, 8.3333333e-3f, 4.1666667e-2f);
+  p = __fmaf_rn(r, p, 0.16666667f);
+  p = __fmaf_rn(r, p, 0.5f);
+  p = __fmaf_rn(r, p, 1.0f);
+  p = __fmaf_rn(r, p, 1.0f);
+  float two_k = __uint_as_float(static_cast<uint32_t>(k + 127) << 23);
+  return __fmul_rn(p, two_k);
+}
+
+// silu_mul_avx512 (activation.rs:115-148): (g / (1 + exp(0 - g))) * u.
+__device__ __forceinline__ float ref_silu_mul(float g, float u) {
+  float e = ref_exp(__fsub_rn(0.0f, g));
+  float silu = __fdiv_rn(g, __fadd_rn(1.0f, e));
+  return __fmul_rn(silu, u);
+}
+
+// sincos_f32_avx512 (trig.rs:60-127).
+__device__ __forceinline__ void ref_sincos(float x, float *s_out, float *c_out) {
+  float kf = rintf(__fmul_rn(x, 0.63661977f));
+  int k = __float2int_rn(kf);
+  float r = __fmaf_rn(-kf, 7.5497903e-8f, __fmaf_rn(-kf, 1.57079625f, x));
+  float r2 = __fmul_rn(r, r);
+  float sp = __fmaf_rn(r2, -1.98412698e-4f, 8.3333333e-3f);
+  sp = __fmaf_rn(r2, sp, -0.16666667f);
+  sp = __fmaf_rn(r2, sp, 1.0f);
+  float sin_r = __fmul_rn(r, sp);
+  float cp = __fmaf_rn(r2, 2.4801587e-5f, -1.3888889e-3f);
+  cp = __fmaf_rn(r2, cp, 4.1666667e-2f);
+  cp = __fmaf_rn(r2, cp, -0.5f);
+  float cos_r = __fmaf_rn(r2, cp, 1.0f);
+  int q = k & 3, b0 = q & 1, b1 = (q >> 1) & 1;
+  float s = b0 ? cos_r : sin_r;
+  float c = b0 ? sin_r : cos_r;
+  *s_out = b1 ? -s : s;
+  *c_out = (b0 ^ b1) ? -c : c;
+}
+
+// Orderable key for the LM-head argmax: larger value wins, then the smaller
+// index (inference_avx512.rs:1027-1044 merge rule).  NaN never wins (it is
+// mapped to the initial key); -0 is folded onto +0 so ties behave like the
+// reference's `>` comparison.
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
+  if (v != v) v = -INFINITY;
+  v = v + 0.0f;
+  uint32_t b = __float_as_uint(v);
+  uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return (static_cast<unsigned long long>(ord) << 32) | (0xFFFFFFFFu - idx);
+}
+__device__ __forceinline__ float argmax_key_value(unsigned long long key) {
+  uint32_t ord = static_cast<uint32_t>(key >> 32);
+  uint32_t b = (ord & 0x80000000u) ? (ord & 0x7FFFFFFFu) : ~ord;
+  return __uint_as_float(b);
+}
+__device__ __forceinline__ uint32_t argmax_key_index(unsigned long long key) {
+  return 0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFull);
+}
+// Key of (-inf, index 0): what the reference returns when every logit is NaN.
+constexpr unsigned long long kArgmaxInitKey = 0x007FFFFFFFFFFFFFull;
+
+}  // namespace zgpu

@@ -1,0 +1,390 @@
+// ctx.cu — context, weight registry and the op-level C ABI entry points.
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+#include "ops.h"
+
+using zgpu::DeviceTensor;
+
+zgpu_status zgpu_fail(zgpu_ctx *ctx, zgpu_status s, const std::string &msg) {
+  if (ctx) ctx->last_error = msg;
+  return s;
+}
+
+zgpu_status zgpu_cuda_fail(zgpu_ctx *ctx, cudaError_t e, const char *what) {
+  std::string m = std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
+  return zgpu_fail(ctx, e == cudaErrorMemoryAllocation ? ZGPU_ERR_OUT_OF_MEMORY : ZGPU_ERR_CUDA, m);
+}
+
+const DeviceTensor *zgpu_lookup(const zgpu_ctx *ctx, const void *key) {
+  auto it = ctx->weights.find(reinterpret_cast<uintptr_t>(key));
+  return it == ctx->weights.end() ? nullptr : &it->second;
+}
+
+#define ZCHECK(call, what)                                   \
+  do {                                                       \
+    cudaError_t e_ = (call);                                 \
+    if (e_ != cudaSuccess) return zgpu_cuda_fail(ctx, e_, what); \
+  } while (0)
+
+extern "C" {
+
+const char *zgpu_status_string(zgpu_status s) {
+  switch (s) {
+    case ZGPU_OK: return "ok";
+    case ZGPU_ERR_INVALID_ARG: return "invalid argument";
+    case ZGPU_ERR_UNSUPPORTED_QUANT: return "unsupported quant type";
+    case ZGPU_ERR_UNREGISTERED_WEIGHT: return "weight key not registered";
+    case ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE: return "kv cache: token index out of range";
+    case ZGPU_ERR_KV_LAYER_OUT_OF_RANGE: return "kv cache: layer out of range";
+    case ZGPU_ERR_KV_INVALID_SLICE_LENGTH: return "kv cache: invalid slice length";
+    case ZGPU_ERR_KV_TOKEN_COUNT_EXCEEDS_MAX: return "kv cache: token count exceeds max";
+    case ZGPU_ERR_NUMERICAL_INSTABILITY: return "attention: numerical instability";
+    case ZGPU_ERR_EMBED_UNSUPPORTED_QUANT: return "embedding: unsupported quant";
+    case ZGPU_ERR_EMBED_DIM_MISALIGNMENT: return "embedding: dim misalignment";
+    case ZGPU_ERR_LM_NON_FINITE_LOGITS: return "lm head: non-finite logits";
+    case ZGPU_ERR_LM_ARGMAX_IN_PADDING: return "lm head: argmax in padding region";
+    case ZGPU_ERR_NO_DEVICE: return "no usable sm_100 device";
+    case ZGPU_ERR_CUDA: return "cuda error";
+    case ZGPU_ERR_OUT_OF_MEMORY: return "out of device memory";
+    case ZGPU_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+  }
+  return "unknown status";
+}
+
+zgpu_status zgpu_init(const zgpu_opts *opts, zgpu_ctx **out) {
+  if (!out) return ZGPU_ERR_INVALID_ARG;
+  *out = nullptr;
+  if (opts && opts->abi_version != ZGPU_ABI_VERSION) return ZGPU_ERR_INVALID_ARG;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return ZGPU_ERR_NO_DEVICE;
+  }
+  const int dev = opts ? opts->device : 0;
+  if (dev < 0 || dev >= n) return ZGPU_ERR_INVALID_ARG;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return ZGPU_ERR_NO_DEVICE;
+  // The kernels are compiled for sm_100a only.
+  if (prop.major != 10) return ZGPU_ERR_NO_DEVICE;
+  zgpu_ctx *ctx = new (std::nothrow) zgpu_ctx();
+  if (!ctx) return ZGPU_ERR_OUT_OF_MEMORY;
+  ctx->device = dev;
+  ctx->sm_count = prop.multiProcessorCount;
+  ctx->cc_major = prop.major;
+  ctx->cc_minor = prop.minor;
+  ctx->flags = opts ? opts->flags : 0;
+  if (cudaSetDevice(dev) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&ctx->d_status, sizeof(uint32_t)) != cudaSuccess ||
+      cudaMemset(ctx->d_status, 0, sizeof(uint32_t)) != cudaSuccess ||
+      zgpu::gemv_setup() != cudaSuccess) {
+    delete ctx;
+    return ZGPU_ERR_CUDA;
+  }
+  *out = ctx;
+  return ZGPU_OK;
+}
+
+zgpu_status zgpu_clear_weights(zgpu_ctx *ctx) {
+  if (!ctx) return ZGPU_ERR_INVALID_ARG;
+  cudaSetDevice(ctx->device);
+  for (auto &kv : ctx->weights) cudaFree(kv.second.d);
+  ctx->weights.clear();
+  return ZGPU_OK;
+}
+
+void zgpu_destroy(zgpu_ctx *ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  zgpu_clear_weights(ctx);
+  cudaFree(ctx->d_x);
+  cudaFree(ctx->d_y);
+  cudaFree(ctx->d_status);
+  if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+}
+
+const char *zgpu_last_error(const zgpu_ctx *ctx) {
+  return ctx ? ctx->last_error.c_str() : "null context";
+}
+
+zgpu_status zgpu_device_info(const zgpu_ctx *ctx, int32_t *sm_count, int32_t *cc_major,
+                             int32_t *cc_minor) {
+  if (!ctx) return ZGPU_ERR_INVALID_ARG;
+  if (sm_count) *sm_count = ctx->sm_count;
+  if (cc_major) *cc_major = ctx->cc_major;
+  if (cc_minor) *cc_minor = ctx->cc_minor;
+  return ZGPU_OK;
+}
+
+zgpu_status zgpu_synchronize(zgpu_ctx *ctx) {
+  if (!ctx) return ZGPU_ERR_INVALID_ARG;
+  ZCHECK(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  return ZGPU_OK;
+}
+
+zgpu_status zgpu_register_weights(zgpu_ctx *ctx, const void *host_ptr, size_t len, uint32_t dtype,
+                                  uint64_t rows, uint64_t cols) {
+  if (!ctx || !host_ptr) return ZGPU_ERR_INVALID_ARG;
+  cudaSetDevice(ctx->device);
+  DeviceTensor t;
+  t.dtype = dtype;
+  t.rows = rows;
+  t.cols = cols;
+  if (dtype == ZGPU_F32) {
+    if (len != rows * cols * 4) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "f32 length mismatch");
+    t.quant = ZGPU_F32;
+    t.bytes = len;
+    ZCHECK(cudaMalloc(&t.d, len), "cudaMalloc(weights)");
+    ZCHECK(cudaMemcpy(t.d, host_ptr, len, cudaMemcpyHostToDevice), "upload");
+  } else {
+    const bool x4 = (dtype == ZGPU_Q4_0X4 || dtype == ZGPU_Q8_0X4);
+    const uint32_t quant = (dtype == ZGPU_Q4_0 || dtype == ZGPU_Q4_0X4)   ? ZGPU_Q4_0
+                           : (dtype == ZGPU_Q8_0 || dtype == ZGPU_Q8_0X4) ? ZGPU_Q8_0
+                                                                          : 0;
+    if (!quant) return zgpu_fail(ctx, ZGPU_ERR_UNSUPPORTED_QUANT, "unsupported dtype");
+    if (cols == 0 || cols % 32 != 0 || rows == 0)
+      return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "cols must be a positive multiple of 32");
+    if (x4 && rows % 4 != 0)
+      return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "interleaved tensor rows must be a multiple of 4");
+    const uint64_t bb = quant == ZGPU_Q4_0 ? 18 : 34;
+    const uint64_t bpr = cols / 32;
+    if (len != rows * bpr * bb)
+      return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "byte length does not match rows x cols");
+    t.quant = quant;
+    t.interleave = x4 ? 4 : 1;
+    t.groups = (rows + 3) / 4;
+    const uint64_t gb = bpr * bb * 4;          // bytes of one group stream
+    t.gstride = (gb + 15) & ~uint64_t(15);
+    t.bytes = t.groups * t.gstride;
+    // Build the padded X4 image on the host, then upload once.
+    std::vector<uint8_t> img;
+    const uint8_t *src = static_cast<const uint8_t *>(host_ptr);
+    if (!x4 || t.gstride != gb) {
+      try {
+        img.assign(t.bytes, 0);
+      } catch (...) {
+        return zgpu_fail(ctx, ZGPU_ERR_OUT_OF_MEMORY, "host staging allocation failed");
+      }
+      for (uint64_t g = 0; g < t.groups; ++g) {
+        uint8_t *dst = img.data() + g * t.gstride;
+        if (x4) {
+          std::memcpy(dst, src + g * gb, gb);
+          continue;
+        }
+        for (uint64_t b = 0; b < bpr; ++b) {
+          uint8_t *gbk = dst + b * bb * 4;
+          for (uint64_t l = 0; l < 4; ++l) {
+            const uint64_t r = g * 4 + l;
+            if (r >= rows) continue;  // padded rows stay zero blocks
+            const uint8_t *blk = src + (r * bpr + b) * bb;
+            gbk[2 * l] = blk[0];
+            gbk[2 * l + 1] = blk[1];
+            std::memcpy(gbk + 8 + l * (bb - 2), blk + 2, bb - 2);
+          }
+        }
+      }
+      src = img.data();
+    }
+    ZCHECK(cudaMalloc(&t.d, t.bytes), "cudaMalloc(weights)");
+    ZCHECK(cudaMemcpy(t.d, src, t.bytes, cudaMemcpyHostToDevice), "upload");
+  }
+  auto key = reinterpret_cast<uintptr_t>(host_ptr);
+  auto it = ctx->weights.find(key);
+  if (it != ctx->weights.end()) cudaFree(it->second.d);
+  ctx->weights[key] = t;
+  return ZGPU_OK;
+}
+
+uint32_t zgpu_group_of(const zgpu_ctx *ctx, const void *host_ptr) {
+  if (!ctx) return 1;
+  const DeviceTensor *t = zgpu_lookup(ctx, host_ptr);
+  return t ? t->interleave : 1;
+}
+
+}  // extern "C"
+
+static zgpu_status ensure_scratch(zgpu_ctx *ctx, size_t nx, size_t ny) {
+  if (nx > ctx->d_x_cap) {
+    cudaFree(ctx->d_x);
+    ctx->d_x = nullptr;
+    ZCHECK(cudaMalloc(&ctx->d_x, nx * sizeof(float)), "cudaMalloc(scratch x)");
+    ctx->d_x_cap = nx;
+  }
+  if (ny > ctx->d_y_cap) {
+    cudaFree(ctx->d_y);
+    ctx->d_y = nullptr;
+    ZCHECK(cudaMalloc(&ctx->d_y, ny * sizeof(float)), "cudaMalloc(scratch y)");
+    ctx->d_y_cap = ny;
+  }
+  return ZGPU_OK;
+}
+
+static zgpu_status check_status_word(zgpu_ctx *ctx) {
+  uint32_t st = 0;
+  ZCHECK(cudaMemcpyAsync(&st, ctx->d_status, 4, cudaMemcpyDeviceToHost, ctx->stream), "status");
+  ZCHECK(cudaStreamSynchronize(ctx->stream), "sync");
+  if (st) {
+    cudaMemsetAsync(ctx->d_status, 0, 4, ctx->stream);
+    if (st & zgpu::ZDEV_ERR_TIMEOUT)
+      return zgpu_fail(ctx, ZGPU_ERR_DEVICE_TIMEOUT, "device wait timed out");
+    if (st & zgpu::ZDEV_ERR_NUMERICAL)
+      return zgpu_fail(ctx, ZGPU_ERR_NUMERICAL_INSTABILITY, "non-finite input or softmax state");
+    return zgpu_fail(ctx, ZGPU_ERR_CUDA, "device status " + std::to_string(st));
+  }
+  return ZGPU_OK;
+}
+
+static zgpu_status linear_device(zgpu_ctx *ctx, const float *d_x, const void *w_key, float *d_out,
+                                 uint64_t in_dim, uint64_t out_dim, uint32_t quant,
+                                 cudaStream_t stream) {
+  if (quant != ZGPU_Q4_0 && quant != ZGPU_Q8_0)
+    return zgpu_fail(ctx, ZGPU_ERR_UNSUPPORTED_QUANT,
+                     "linear_dispatch: unsupported quant type " + std::to_string(quant));
+  const DeviceTensor *t = zgpu_lookup(ctx, w_key);
+  if (!t) return zgpu_fail(ctx, ZGPU_ERR_UNREGISTERED_WEIGHT, "linear_dispatch: unregistered weight");
+  if (t->quant != quant || t->cols != in_dim || t->rows != out_dim)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "linear_dispatch: shape/quant mismatch with registration");
+  zgpu::GemvDesc g;
+  g.w = t->d;
+  g.gstride = t->gstride;
+  g.quant = t->quant;
+  g.rows = static_cast<uint32_t>(out_dim);
+  g.groups = static_cast<uint32_t>(t->groups);
+  g.in_dim = static_cast<uint32_t>(in_dim);
+  zgpu::GemvIo io;
+  io.x = d_x;
+  io.out = d_out;
+  io.status = ctx->d_status;
+  zgpu::LaunchCfg lc;
+  lc.stream = stream ? stream : ctx->stream;
+  lc.sm_count = ctx->sm_count;
+  lc.launch_counter = &ctx->launches;
+  cudaError_t e = zgpu::launch_gemv(g, zgpu::PRO_PLAIN, zgpu::EPI_STORE, io, lc);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "launch_gemv");
+  return ZGPU_OK;
+}
+
+extern "C" {
+
+zgpu_status zgpu_linear_dispatch_device(zgpu_ctx *ctx, const float *d_x, const void *w_key,
+                                        float *d_out, uint64_t in_dim, uint64_t out_dim,
+                                        uint32_t quant, void *stream) {
+  if (!ctx || !d_x || !d_out) return ZGPU_ERR_INVALID_ARG;
+  cudaSetDevice(ctx->device);
+  return linear_device(ctx, d_x, w_key, d_out, in_dim, out_dim, quant,
+                       static_cast<cudaStream_t>(stream));
+}
+
+zgpu_status zgpu_linear_dispatch(zgpu_ctx *ctx, const float *x, const void *w_key, float *out,
+                                 uint64_t in_dim, uint64_t out_dim, uint32_t quant) {
+  if (!ctx || !x || !out) return ZGPU_ERR_INVALID_ARG;
+  cudaSetDevice(ctx->device);
+  zgpu_status s = ensure_scratch(ctx, in_dim, out_dim);
+  if (s) return s;
+  ZCHECK(cudaMemcpyAsync(ctx->d_x, x, in_dim * 4, cudaMemcpyHostToDevice, ctx->stream), "h2d x");
+  s = linear_device(ctx, ctx->d_x, w_key, ctx->d_y, in_dim, out_dim, quant, ctx->stream);
+  if (s) return s;
+  ZCHECK(cudaMemcpyAsync(out, ctx->d_y, out_dim * 4, cudaMemcpyDeviceToHost, ctx->stream), "d2h out");
+  return check_status_word(ctx);
+}
+
+zgpu_status zgpu_rmsnorm(zgpu_ctx *ctx, const float *x, const float *w, float *out, uint64_t n,
+                         float eps) {
+  if (!ctx || !x || !w || !out || n == 0) return ZGPU_ERR_INVALID_ARG;
+  cudaSetDevice(ctx->device);
+  zgpu_status s = ensure_scratch(ctx, 2 * n, n);
+  if (s) return s;
+  ZCHECK(cudaMemcpyAsync(ctx->d_x, x, n * 4, cudaMemcpyHostToDevice, ctx->stream), "h2d");
+  ZCHECK(cudaMemcpyAsync(ctx->d_x + n, w, n * 4, cudaMemcpyHostToDevice, ctx->stream), "h2d");
+  ZCHECK(zgpu::launch_rmsnorm(ctx->d_x, ctx->d_x + n, ctx->d_y, static_cast<uint32_t>(n), eps,
+                              ctx->stream), "rmsnorm");
+  ++ctx->launches;
+  ZCHECK(cudaMemcpyAsync(out, ctx->d_y, n * 4, cudaMemcpyDeviceToHost, ctx->stream), "d2h");
+  ZCHECK(cudaStreamSynchronize(ctx->stream), "sync");
+  return ZGPU_OK;
+}
+
+zgpu_status zgpu_rope(zgpu_ctx *ctx, float *qk, uint32_t n_heads, uint32_t head_dim, uint32_t pos,
+                      float freq_base) {
+  if (!ctx || !qk || n_heads == 0 || head_dim == 0 || head_dim % 2) return ZGPU_ERR_INVALID_ARG;
+  cudaSetDevice(ctx->device);
+  const uint32_t half = head_dim / 2;
+  std::vector<float> inv(half);
+  // RopeContext::new (ops.rs:79-93): powf(base, -2*i / head_dim) in f32.
+  const float hdf = static_cast<float>(head_dim);
+  for (uint32_t i = 0; i < half; ++i) {
+    const float exponent = -2.0f * static_cast<float>(i) / hdf;
+    inv[i] = powf(freq_base, exponent);
+  }
+  const size_t n = static_cast<size_t>(n_heads) * head_dim;
+  zgpu_status s = ensure_scratch(ctx, n + half, 1);
+  if (s) return s;
+  ZCHECK(cudaMemcpyAsync(ctx->d_x, qk, n * 4, cudaMemcpyHostToDevice, ctx->stream), "h2d");
+  ZCHECK(cudaMemcpyAsync(ctx->d_x + n, inv.data(), half * 4, cudaMemcpyHostToDevice, ctx->stream), "h2d");
+  ZCHECK(zgpu::launch_rope(ctx->d_x, ctx->d_x + n, n_heads, head_dim, pos, ctx->stream), "rope");
+  ++ctx->launches;
+  ZCHECK(cudaMemcpyAsync(qk, ctx->d_x, n * 4, cudaMemcpyDeviceToHost, ctx->stream), "d2h");
+  ZCHECK(cudaStreamSynchronize(ctx->stream), "sync");
+  return ZGPU_OK;
+}
+
+zgpu_status zgpu_silu_mul(zgpu_ctx *ctx, const float *gate, const float *up, float *out, uint64_t n) {
+  if (!ctx || !gate || !up || !out || n == 0) return ZGPU_ERR_INVALID_ARG;
+  cudaSetDevice(ctx->device);
+  zgpu_status s = ensure_scratch(ctx, 2 * n, n);
+  if (s) return s;
+  ZCHECK(cudaMemcpyAsync(ctx->d_x, gate, n * 4, cudaMemcpyHostToDevice, ctx->stream), "h2d");
+  ZCHECK(cudaMemcpyAsync(ctx->d_x + n, up, n * 4, cudaMemcpyHostToDevice, ctx->stream), "h2d");
+  ZCHECK(zgpu::launch_silu_mul(ctx->d_x, ctx->d_x + n, ctx->d_y, n, ctx->stream), "silu_mul");
+  ++ctx->launches;
+  ZCHECK(cudaMemcpyAsync(out, ctx->d_y, n * 4, cudaMemcpyDeviceToHost, ctx->stream), "d2h");
+  ZCHECK(cudaStreamSynchronize(ctx->stream), "sync");
+  return ZGPU_OK;
+}
+
+zgpu_status zgpu_quantize_q8_0(zgpu_ctx *ctx, const float *x, void *blocks_out, uint64_t n) {
+  if (!ctx || !x || !blocks_out || n == 0 || n % 32) return ZGPU_ERR_INVALID_ARG;
+  cudaSetDevice(ctx->device);
+  const size_t nb = n / 32;
+  // x in d_x, blocks in d_y (34 bytes per block fits in 32 floats per block)
+  zgpu_status s = ensure_scratch(ctx, n, (nb * 34 + 3) / 4);
+  if (s) return s;
+  ZCHECK(cudaMemcpyAsync(ctx->d_x, x, n * 4, cudaMemcpyHostToDevice, ctx->stream), "h2d");
+  ZCHECK(zgpu::launch_quantize_q8_0(ctx->d_x, reinterpret_cast<uint8_t *>(ctx->d_y), n,
+                                    ctx->d_status, ctx->stream), "quantize_q8_0");
+  ++ctx->launches;
+  ZCHECK(cudaMemcpyAsync(blocks_out, ctx->d_y, nb * 34, cudaMemcpyDeviceToHost, ctx->stream), "d2h");
+  return check_status_word(ctx);
+}
+
+zgpu_status zgpu_linear_q8act(zgpu_ctx *ctx, const void *xq_blocks, const void *w_key, float *out,
+                              uint64_t in_dim, uint64_t out_dim) {
+  if (!ctx || !xq_blocks || !out || in_dim == 0 || in_dim % 32) return ZGPU_ERR_INVALID_ARG;
+  cudaSetDevice(ctx->device);
+  const DeviceTensor *t = zgpu_lookup(ctx, w_key);
+  if (!t) return zgpu_fail(ctx, ZGPU_ERR_UNREGISTERED_WEIGHT, "linear_q8act: unregistered weight");
+  if (t->quant != ZGPU_Q4_0)
+    return zgpu_fail(ctx, ZGPU_ERR_UNSUPPORTED_QUANT, "linear_q8act: weights must be Q4_0");
+  if (t->cols != in_dim || t->rows != out_dim)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "linear_q8act: shape mismatch with registration");
+  const size_t xbytes = in_dim / 32 * 34;
+  zgpu_status s = ensure_scratch(ctx, (xbytes + 3) / 4, out_dim);
+  if (s) return s;
+  ZCHECK(cudaMemcpyAsync(ctx->d_x, xq_blocks, xbytes, cudaMemcpyHostToDevice, ctx->stream), "h2d");
+  ZCHECK(zgpu::launch_q8act_gemv(t->d, t->gstride, static_cast<uint32_t>(out_dim),
+                                 static_cast<uint32_t>(in_dim / 32),
+                                 reinterpret_cast<const uint8_t *>(ctx->d_x), ctx->d_y, ctx->stream),
+         "q8act gemv");
+  ++ctx->launches;
+  ZCHECK(cudaMemcpyAsync(out, ctx->d_y, out_dim * 4, cudaMemcpyDeviceToHost, ctx->stream), "d2h");
+  ZCHECK(cudaStreamSynchronize(ctx->stream), "sync");
+  return ZGPU_OK;
+}
+
+}  // extern "C"

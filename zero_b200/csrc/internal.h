@@ -1,0 +1,85 @@
+// internal.h — host-side structures shared by the zero-b200 modules.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/zgpu.h"
+
+namespace zgpu {
+
+// Device copy of one registered tensor.  Matmul tensors are always held in
+// the 4-row-interleaved group layout (X4) on the device, whatever layout the
+// caller registered: group g of 4 output rows is one contiguous stream of
+// bpr group-blocks (72 B for Q4_0, 136 B for Q8_0: the four fp16 scales then
+// the four rows' quant bodies, tools/silicatepack.py:982-1022), padded to a
+// multiple of 16 bytes so every group starts on a TMA-legal boundary.
+struct DeviceTensor {
+  uint8_t *d = nullptr;       // device bytes
+  size_t bytes = 0;
+  uint32_t dtype = 0;         // dtype as registered
+  uint32_t quant = 0;         // ZGPU_Q4_0 / ZGPU_Q8_0 / ZGPU_F32
+  uint32_t interleave = 1;    // what group_of reports (registered layout)
+  uint64_t rows = 0, cols = 0;
+  uint64_t groups = 0;        // ceil(rows / 4)
+  uint64_t gstride = 0;       // bytes per group stream on the device
+};
+
+// Geometry of one GEMV launch over an X4 device tensor.
+struct GemvDesc {
+  const uint8_t *w;           // group streams
+  uint64_t gstride;           // bytes between groups
+  uint32_t quant;             // ZGPU_Q4_0 / ZGPU_Q8_0
+  uint32_t rows;              // valid output rows
+  uint32_t groups;            // groups in the launch
+  uint32_t in_dim;
+};
+
+enum GemvPro { PRO_PLAIN = 0, PRO_RMSNORM = 1 };
+enum GemvEpi { EPI_STORE = 0, EPI_RESADD = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
+
+struct GemvIo {
+  const float *x = nullptr;        // input vector (the residual for PRO_RMSNORM)
+  const float *norm_w = nullptr;   // RMSNorm gain (PRO_RMSNORM)
+  float eps = 0.f;
+  float *out = nullptr;            // STORE / RESADD / SWIGLU / ARGMAX (logits)
+  unsigned long long *argmax = nullptr;
+  uint32_t *status = nullptr;
+};
+
+struct LaunchCfg {
+  cudaStream_t stream = nullptr;
+  bool pdl = false;
+  int sm_count = 148;
+  uint32_t *launch_counter = nullptr;   // host-side count of kernel launches
+};
+
+cudaError_t launch_gemv(const GemvDesc &g, GemvPro pro, GemvEpi epi, const GemvIo &io,
+                        const LaunchCfg &lc);
+cudaError_t gemv_setup();
+
+}  // namespace zgpu
+
+struct zgpu_ctx {
+  int device = 0;
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  uint32_t flags = 0;
+  cudaStream_t stream = nullptr;
+  std::string last_error;
+  std::map<uintptr_t, zgpu::DeviceTensor> weights;
+  // scratch for the host-buffer entry points (grown on demand)
+  float *d_x = nullptr, *d_y = nullptr;
+  size_t d_x_cap = 0, d_y_cap = 0;
+  uint32_t *d_status = nullptr;
+  uint32_t launches = 0;
+};
+
+// Record an error message on the context and return the status.
+zgpu_status zgpu_fail(zgpu_ctx *ctx, zgpu_status s, const std::string &msg);
+zgpu_status zgpu_cuda_fail(zgpu_ctx *ctx, cudaError_t e, const char *what);
+const zgpu::DeviceTensor *zgpu_lookup(const zgpu_ctx *ctx, const void *key);

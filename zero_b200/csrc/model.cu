@@ -1,0 +1,680 @@
+// model.cu — the Qwen3-shaped decode step: KV cache, device weight layout,
+// per-step kernel sequence, CUDA-graph capture and the greedy loop.
+//
+// One decode step (forward_single_token_avx512, inference_avx512.rs:1826, then
+// lm_head_argmax_avx512, :1200) is 5 kernels per layer plus 3:
+//   embed (token select + row dequant)
+//   per layer: [RMSNorm + fused Q|K|V GEMV] -> [QK-norm + RoPE + KV append +
+//              split-K attention] -> [O GEMV + residual] -> [RMSNorm + fused
+//              gate|up GEMV + SiLU*up] -> [down GEMV + residual]
+//   [final RMSNorm + LM-head GEMV + argmax] -> finalize (checks, token chain)
+// Every kernel is launched with programmatic dependent launch, so each one's
+// weight prefetch (TMA into shared memory) starts while its predecessor
+// drains; the whole step is captured once into a CUDA graph whose replays
+// read the token and position from device memory.
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+#include "ops.h"
+
+using namespace zgpu;
+
+struct zgpu_kv {
+  zgpu_ctx *ctx = nullptr;
+  float *d = nullptr;
+  uint32_t max_tokens = 0, n_layers = 0, n_kv = 0, head_dim = 0;
+  uint64_t block = 0;   // max_tokens * n_kv * head_dim
+};
+
+struct zgpu_model {
+  zgpu_ctx *ctx = nullptr;
+  zgpu_qwen3_desc desc = {};
+  uint32_t q_dim = 0, kv_dim = 0;
+  // weights (X4 group streams on the device)
+  std::vector<uint8_t *> qkv;       // owned: q|k|v groups concatenated
+  std::vector<uint8_t *> gateup;    // owned: gate/up groups interleaved
+  std::vector<const DeviceTensor *> o, down;
+  uint64_t gs_h = 0;                // group stride for in_dim = hidden
+  uint64_t gs_f = 0;                // group stride for in_dim = ffn (down)
+  uint64_t gs_q = 0;                // group stride for in_dim = q_dim (O)
+  const DeviceTensor *emb = nullptr, *out = nullptr;
+  float *d_norms = nullptr;         // attn[L][H] | ffn[L][H] | qn[L][hd] | kn[L][hd] | out[H]
+  float *d_inv_freqs = nullptr;
+  // activations / state
+  float *d_hidden = nullptr, *d_qkvo = nullptr, *d_attn = nullptr, *d_act = nullptr,
+        *d_logits = nullptr;
+  unsigned long long *d_argmax = nullptr;
+  StepState *d_state = nullptr;
+  uint32_t *d_prompt = nullptr, *d_tokens = nullptr;
+  uint32_t prompt_cap = 0, tokens_cap = 0;
+  float *d_part = nullptr;
+  uint32_t *d_counters = nullptr;
+  uint32_t max_splits = 0, part_tokens = 0;
+  uint32_t *d_status = nullptr;
+  // graphs (replays read token / position from d_state)
+  cudaGraphExec_t step_graph = nullptr;   // embed + layers + LM head + finalize
+  cudaGraphExec_t fwd_graph = nullptr;    // embed + layers
+  cudaGraphExec_t lm_graph = nullptr;     // LM head + finalize
+  zgpu_kv *graph_kv = nullptr;
+  uint32_t step_kernels = 0, fwd_kernels = 0, lm_kernels = 0;
+  zgpu_perf perf = {};
+  cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+};
+
+namespace {
+
+float *norm_attn(zgpu_model *m, uint32_t l) { return m->d_norms + static_cast<size_t>(l) * m->desc.hidden; }
+float *norm_ffn(zgpu_model *m, uint32_t l) {
+  return m->d_norms + static_cast<size_t>(m->desc.n_layers + l) * m->desc.hidden;
+}
+float *norm_q(zgpu_model *m, uint32_t l) {
+  return m->d_norms + static_cast<size_t>(2 * m->desc.n_layers) * m->desc.hidden +
+         static_cast<size_t>(l) * m->desc.head_dim;
+}
+float *norm_k(zgpu_model *m, uint32_t l) {
+  return norm_q(m, 0) + static_cast<size_t>(m->desc.n_layers + l) * m->desc.head_dim;
+}
+float *norm_out(zgpu_model *m) {
+  return norm_q(m, 0) + static_cast<size_t>(2 * m->desc.n_layers) * m->desc.head_dim;
+}
+
+LaunchCfg launch_cfg(zgpu_model *m, uint32_t *counter) {
+  LaunchCfg lc;
+  lc.stream = m->ctx->stream;
+  lc.pdl = !(m->ctx->flags & ZGPU_FLAG_NO_PDL);
+  lc.sm_count = m->ctx->sm_count;
+  lc.launch_counter = counter;
+  return lc;
+}
+
+// Enqueue the forward part of one step (embed + all layers).
+cudaError_t enqueue_forward(zgpu_model *m, zgpu_kv *kv, uint32_t *counter) {
+  const zgpu_qwen3_desc &d = m->desc;
+  LaunchCfg lc = launch_cfg(m, counter);
+  cudaError_t e;
+  EmbedParams ep;
+  ep.emb = m->emb->d;
+  ep.gstride = m->emb->gstride;
+  ep.quant = m->emb->quant;
+  ep.hidden = d.hidden;
+  ep.vocab = static_cast<uint32_t>(m->emb->rows);
+  ep.prompt = m->d_prompt;
+  ep.state = m->d_state;
+  ep.hidden_out = m->d_hidden;
+  ep.status = m->d_status;
+  if ((e = launch_embed(ep, lc)) != cudaSuccess) return e;
+
+  const uint32_t qkv_rows = m->q_dim + 2 * m->kv_dim;
+  for (uint32_t l = 0; l < d.n_layers; ++l) {
+    GemvDesc g;
+    GemvIo io;
+    // RMSNorm + fused Q|K|V projection
+    g.w = m->qkv[l];
+    g.gstride = m->gs_h;
+    g.quant = ZGPU_Q4_0;
+    g.rows = qkv_rows;
+    g.groups = qkv_rows / 4;
+    g.in_dim = d.hidden;
+    io = GemvIo();
+    io.x = m->d_hidden;
+    io.norm_w = norm_attn(m, l);
+    io.eps = d.rms_eps;
+    io.out = m->d_qkvo;
+    io.status = m->d_status;
+    if ((e = launch_gemv(g, PRO_RMSNORM, EPI_STORE, io, lc)) != cudaSuccess) return e;
+
+    AttnParams ap;
+    ap.qkv = m->d_qkvo;
+    ap.q_norm = norm_q(m, l);
+    ap.k_norm = norm_k(m, l);
+    ap.inv_freqs = m->d_inv_freqs;
+    ap.kv_layer = kv->d + static_cast<size_t>(l) * 2 * kv->block;
+    ap.kv_block = kv->block;
+    ap.max_tokens = kv->max_tokens;
+    ap.pos_ptr = &m->d_state->pos;
+    ap.out = m->d_attn;
+    ap.part = m->d_part;
+    ap.counters = m->d_counters;
+    ap.status = m->d_status;
+    ap.n_q = d.n_q_heads;
+    ap.n_kv = d.n_kv_heads;
+    ap.max_splits = m->max_splits;
+    ap.eps = d.rms_eps;
+    ap.scale = 1.0f / sqrtf(static_cast<float>(d.head_dim));
+    if ((e = launch_attention(ap, lc)) != cudaSuccess) return e;
+
+    // O projection + residual
+    g.w = m->o[l]->d;
+    g.gstride = m->gs_q;
+    g.rows = d.hidden;
+    g.groups = d.hidden / 4;
+    g.in_dim = m->q_dim;
+    io = GemvIo();
+    io.x = m->d_attn;
+    io.out = m->d_hidden;
+    io.status = m->d_status;
+    if ((e = launch_gemv(g, PRO_PLAIN, EPI_RESADD, io, lc)) != cudaSuccess) return e;
+
+    // RMSNorm + fused gate|up + SiLU(gate)*up
+    g.w = m->gateup[l];
+    g.gstride = m->gs_h;
+    g.rows = d.ffn;
+    g.groups = 2 * d.ffn / 4;
+    g.in_dim = d.hidden;
+    io = GemvIo();
+    io.x = m->d_hidden;
+    io.norm_w = norm_ffn(m, l);
+    io.eps = d.rms_eps;
+    io.out = m->d_act;
+    io.status = m->d_status;
+    if ((e = launch_gemv(g, PRO_RMSNORM, EPI_SWIGLU, io, lc)) != cudaSuccess) return e;
+
+    // down projection + residual
+    g.w = m->down[l]->d;
+    g.gstride = m->gs_f;
+    g.rows = d.hidden;
+    g.groups = d.hidden / 4;
+    g.in_dim = d.ffn;
+    io = GemvIo();
+    io.x = m->d_act;
+    io.out = m->d_hidden;
+    io.status = m->d_status;
+    if ((e = launch_gemv(g, PRO_PLAIN, EPI_RESADD, io, lc)) != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t enqueue_lm_head(zgpu_model *m, uint32_t *counter) {
+  const zgpu_qwen3_desc &d = m->desc;
+  LaunchCfg lc = launch_cfg(m, counter);
+  GemvDesc g;
+  g.w = m->out->d;
+  g.gstride = m->out->gstride;
+  g.quant = m->out->quant;
+  g.rows = d.vocab_padded;
+  g.groups = static_cast<uint32_t>(m->out->groups);
+  g.in_dim = d.hidden;
+  GemvIo io;
+  io.x = m->d_hidden;
+  io.norm_w = norm_out(m);
+  io.eps = d.rms_eps;
+  io.out = m->d_logits;
+  io.argmax = m->d_argmax;
+  io.status = m->d_status;
+  cudaError_t e = launch_gemv(g, PRO_RMSNORM, EPI_ARGMAX, io, lc);
+  if (e != cudaSuccess) return e;
+  FinalizeParams fp;
+  fp.argmax = m->d_argmax;
+  fp.state = m->d_state;
+  fp.tokens_out = m->d_tokens;
+  fp.status = m->d_status;
+  return launch_finalize(fp, lc);
+}
+
+enum GraphPart { GRAPH_STEP = 0, GRAPH_FWD = 1, GRAPH_LM = 2 };
+
+zgpu_status capture(zgpu_model *m, zgpu_kv *kv, GraphPart part, cudaGraphExec_t *out,
+                    uint32_t *kernels) {
+  zgpu_ctx *ctx = m->ctx;
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "begin capture");
+  uint32_t n = 0;
+  cudaError_t e1 = cudaSuccess;
+  if (part != GRAPH_LM) e1 = enqueue_forward(m, kv, &n);
+  if (e1 == cudaSuccess && part != GRAPH_FWD) e1 = enqueue_lm_head(m, &n);
+  e = cudaStreamEndCapture(ctx->stream, &g);
+  if (e1 != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    return zgpu_cuda_fail(ctx, e1, "capture step");
+  }
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "end capture");
+  e = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "graph instantiate");
+  *kernels = n;
+  return ZGPU_OK;
+}
+
+void drop_graphs(zgpu_model *m) {
+  for (cudaGraphExec_t *g : {&m->step_graph, &m->fwd_graph, &m->lm_graph}) {
+    if (*g) cudaGraphExecDestroy(*g);
+    *g = nullptr;
+  }
+  m->graph_kv = nullptr;
+}
+
+// Capture the three step graphs for this cache (once per cache).
+zgpu_status build_graphs(zgpu_model *m, zgpu_kv *kv) {
+  if (m->step_graph && m->graph_kv == kv) return ZGPU_OK;
+  drop_graphs(m);
+  zgpu_status s = capture(m, kv, GRAPH_STEP, &m->step_graph, &m->step_kernels);
+  if (!s) s = capture(m, kv, GRAPH_FWD, &m->fwd_graph, &m->fwd_kernels);
+  if (!s) s = capture(m, nullptr, GRAPH_LM, &m->lm_graph, &m->lm_kernels);
+  if (s) {
+    drop_graphs(m);
+    return s;
+  }
+  m->graph_kv = kv;
+  return ZGPU_OK;
+}
+
+zgpu_status read_status(zgpu_model *m, uint32_t *st_out) {
+  zgpu_ctx *ctx = m->ctx;
+  uint32_t st = 0;
+  cudaError_t e = cudaMemcpyAsync(&st, m->d_status, 4, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "step status");
+  *st_out = st;
+  if (st) cudaMemsetAsync(m->d_status, 0, 4, ctx->stream);
+  return ZGPU_OK;
+}
+
+zgpu_status map_status(zgpu_ctx *ctx, uint32_t st) {
+  if (!st) return ZGPU_OK;
+  if (st & ZDEV_ERR_TIMEOUT) return zgpu_fail(ctx, ZGPU_ERR_DEVICE_TIMEOUT, "device wait timed out");
+  if (st & ZDEV_ERR_BOUNDS)
+    return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "token or position outside the cache");
+  if (st & ZDEV_ERR_NUMERICAL)
+    return zgpu_fail(ctx, ZGPU_ERR_NUMERICAL_INSTABILITY, "softmax: non-finite max or bad sum");
+  if (st & ZDEV_ERR_LM_NONFINITE)
+    return zgpu_fail(ctx, ZGPU_ERR_LM_NON_FINITE_LOGITS, "lm head: non-finite max logit");
+  if (st & ZDEV_ERR_LM_PADDING)
+    return zgpu_fail(ctx, ZGPU_ERR_LM_ARGMAX_IN_PADDING, "lm head: argmax in padding region");
+  return zgpu_fail(ctx, ZGPU_ERR_CUDA, "device status " + std::to_string(st));
+}
+
+zgpu_status set_state(zgpu_model *m, uint32_t n_prompt, uint32_t pos_base, uint32_t vocab_real,
+                      uint32_t n_gen_cap) {
+  StepState s = {};
+  s.step = 0;
+  s.n_prompt = n_prompt;
+  s.pos_base = pos_base;
+  s.pos = pos_base;
+  s.vocab_real = vocab_real;
+  s.n_gen_cap = n_gen_cap;
+  s.first_err_step = 0xFFFFFFFFu;
+  cudaError_t e = cudaMemcpyAsync(m->d_state, &s, sizeof(s), cudaMemcpyHostToDevice, m->ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(m->ctx, e, "state upload");
+  return ZGPU_OK;
+}
+
+template <class T>
+cudaError_t grow(T **p, uint32_t *cap, uint32_t need) {
+  if (need <= *cap) return cudaSuccess;
+  cudaFree(*p);
+  *p = nullptr;
+  cudaError_t e = cudaMalloc(p, static_cast<size_t>(need) * sizeof(T));
+  if (e == cudaSuccess) *cap = need;
+  return e;
+}
+
+}  // namespace
+
+extern "C" {
+
+zgpu_status zgpu_kv_create(zgpu_ctx *ctx, uint32_t max_tokens, uint32_t n_layers,
+                           uint32_t n_kv_heads, uint32_t head_dim, zgpu_kv **out) {
+  if (!ctx || !out || !max_tokens || !n_layers || !n_kv_heads || !head_dim)
+    return ZGPU_ERR_INVALID_ARG;
+  cudaSetDevice(ctx->device);
+  zgpu_kv *kv = new (std::nothrow) zgpu_kv();
+  if (!kv) return ZGPU_ERR_OUT_OF_MEMORY;
+  kv->ctx = ctx;
+  kv->max_tokens = max_tokens;
+  kv->n_layers = n_layers;
+  kv->n_kv = n_kv_heads;
+  kv->head_dim = head_dim;
+  kv->block = static_cast<uint64_t>(max_tokens) * n_kv_heads * head_dim;
+  const size_t bytes = 2ull * n_layers * kv->block * sizeof(float);
+  cudaError_t e = cudaMalloc(&kv->d, bytes);
+  if (e == cudaSuccess) e = cudaMemset(kv->d, 0, bytes);
+  if (e != cudaSuccess) {
+    delete kv;
+    return zgpu_cuda_fail(ctx, e, "kv cache allocation");
+  }
+  *out = kv;
+  return ZGPU_OK;
+}
+
+void zgpu_kv_destroy(zgpu_kv *kv) {
+  if (!kv) return;
+  cudaSetDevice(kv->ctx->device);
+  cudaFree(kv->d);
+  delete kv;
+}
+
+zgpu_status zgpu_kv_store(zgpu_kv *kv, uint32_t layer, uint32_t token, const float *k,
+                          const float *v, uint64_t len) {
+  if (!kv || !k || !v) return ZGPU_ERR_INVALID_ARG;
+  zgpu_ctx *ctx = kv->ctx;
+  if (layer >= kv->n_layers) return zgpu_fail(ctx, ZGPU_ERR_KV_LAYER_OUT_OF_RANGE, "layer out of range");
+  if (token >= kv->max_tokens)
+    return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "token index out of range");
+  const uint64_t stride = static_cast<uint64_t>(kv->n_kv) * kv->head_dim;
+  if (len != stride) return zgpu_fail(ctx, ZGPU_ERR_KV_INVALID_SLICE_LENGTH, "invalid slice length");
+  cudaSetDevice(ctx->device);
+  float *kd = kv->d + static_cast<size_t>(layer) * 2 * kv->block + token * stride;
+  cudaError_t e = cudaMemcpy(kd, k, stride * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(kd + kv->block, v, stride * 4, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "kv store");
+  return ZGPU_OK;
+}
+
+zgpu_status zgpu_kv_read(zgpu_kv *kv, uint32_t layer, uint32_t token_count, float *k_out,
+                         float *v_out) {
+  if (!kv) return ZGPU_ERR_INVALID_ARG;
+  zgpu_ctx *ctx = kv->ctx;
+  if (layer >= kv->n_layers) return zgpu_fail(ctx, ZGPU_ERR_KV_LAYER_OUT_OF_RANGE, "layer out of range");
+  if (token_count > kv->max_tokens)
+    return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_COUNT_EXCEEDS_MAX, "token count exceeds max");
+  cudaSetDevice(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  const uint64_t n = static_cast<uint64_t>(token_count) * kv->n_kv * kv->head_dim;
+  const float *kd = kv->d + static_cast<size_t>(layer) * 2 * kv->block;
+  cudaError_t e = cudaSuccess;
+  if (k_out) e = cudaMemcpy(k_out, kd, n * 4, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && v_out) e = cudaMemcpy(v_out, kd + kv->block, n * 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "kv read");
+  return ZGPU_OK;
+}
+
+void zgpu_qwen3_destroy(zgpu_model *m) {
+  if (!m) return;
+  cudaSetDevice(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->stream);
+  drop_graphs(m);
+  for (auto p : m->qkv) cudaFree(p);
+  for (auto p : m->gateup) cudaFree(p);
+  cudaFree(m->d_norms);
+  cudaFree(m->d_inv_freqs);
+  cudaFree(m->d_hidden);
+  cudaFree(m->d_qkvo);
+  cudaFree(m->d_attn);
+  cudaFree(m->d_act);
+  cudaFree(m->d_logits);
+  cudaFree(m->d_argmax);
+  cudaFree(m->d_state);
+  cudaFree(m->d_prompt);
+  cudaFree(m->d_tokens);
+  cudaFree(m->d_part);
+  cudaFree(m->d_counters);
+  cudaFree(m->d_status);
+  for (auto &e : m->ev)
+    if (e) cudaEventDestroy(e);
+  delete m;
+}
+
+zgpu_status zgpu_qwen3_create(zgpu_ctx *ctx, const zgpu_qwen3_desc *d, zgpu_model **out) {
+  if (!ctx || !d || !out || !d->layers) return ZGPU_ERR_INVALID_ARG;
+  *out = nullptr;
+  cudaSetDevice(ctx->device);
+  if (d->head_dim != 128)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "decode attention kernel requires head_dim 128");
+  if (!d->n_kv_heads || d->n_q_heads % d->n_kv_heads || d->n_q_heads / d->n_kv_heads > 8)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "unsupported GQA geometry");
+  if (d->hidden % 32 || d->ffn % 32 || d->hidden % 4 || d->ffn % 4)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "hidden/ffn must be multiples of 32");
+  if (d->vocab_real > d->vocab_padded) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "vocab_real > vocab_padded");
+  zgpu_model *m = new (std::nothrow) zgpu_model();
+  if (!m) return ZGPU_ERR_OUT_OF_MEMORY;
+  m->ctx = ctx;
+  m->desc = *d;
+  m->desc.layers = nullptr;
+  m->desc.output_norm = nullptr;
+  m->q_dim = d->n_q_heads * d->head_dim;
+  m->kv_dim = d->n_kv_heads * d->head_dim;
+  const uint32_t H = d->hidden, F = d->ffn, L = d->n_layers, hd = d->head_dim;
+  auto fail = [&](zgpu_status s, const std::string &msg) {
+    zgpu_qwen3_destroy(m);
+    return zgpu_fail(ctx, s, msg);
+  };
+  auto need = [&](const void *key, uint32_t quant, uint64_t rows, uint64_t cols,
+                  const char *what) -> const DeviceTensor * {
+    const DeviceTensor *t = zgpu_lookup(ctx, key);
+    if (!t || t->quant != quant || t->rows != rows || t->cols != cols) {
+      ctx->last_error = std::string("qwen3_create: bad or unregistered tensor ") + what;
+      return nullptr;
+    }
+    return t;
+  };
+  m->emb = need(d->token_embd, d->token_embd_quant, d->vocab_padded, H, "token_embd");
+  if (!m->emb) return fail(ZGPU_ERR_UNREGISTERED_WEIGHT, ctx->last_error);
+  m->out = need(d->output, d->output_quant, d->vocab_padded, H, "output");
+  if (!m->out) return fail(ZGPU_ERR_UNREGISTERED_WEIGHT, ctx->last_error);
+
+  cudaError_t e = cudaSuccess;
+  for (uint32_t l = 0; l < L; ++l) {
+    const zgpu_qwen3_layer &ly = d->layers[l];
+    const DeviceTensor *q = need(ly.attn_q, ZGPU_Q4_0, m->q_dim, H, "attn_q");
+    const DeviceTensor *k = need(ly.attn_k, ZGPU_Q4_0, m->kv_dim, H, "attn_k");
+    const DeviceTensor *v = need(ly.attn_v, ZGPU_Q4_0, m->kv_dim, H, "attn_v");
+    const DeviceTensor *o = need(ly.attn_o, ZGPU_Q4_0, H, m->q_dim, "attn_o");
+    const DeviceTensor *gt = need(ly.ffn_gate, ZGPU_Q4_0, F, H, "ffn_gate");
+    const DeviceTensor *up = need(ly.ffn_up, ZGPU_Q4_0, F, H, "ffn_up");
+    const DeviceTensor *dn = need(ly.ffn_down, ZGPU_Q4_0, H, F, "ffn_down");
+    if (!q || !k || !v || !o || !gt || !up || !dn) return fail(ZGPU_ERR_UNREGISTERED_WEIGHT, ctx->last_error);
+    m->gs_h = q->gstride;
+    m->gs_q = o->gstride;
+    m->gs_f = dn->gstride;
+    uint8_t *cat = nullptr;
+    e = cudaMalloc(&cat, q->bytes + k->bytes + v->bytes);
+    if (e != cudaSuccess) return fail(ZGPU_ERR_OUT_OF_MEMORY, "qkv allocation");
+    m->qkv.push_back(cat);
+    cudaMemcpy(cat, q->d, q->bytes, cudaMemcpyDeviceToDevice);
+    cudaMemcpy(cat + q->bytes, k->d, k->bytes, cudaMemcpyDeviceToDevice);
+    cudaMemcpy(cat + q->bytes + k->bytes, v->d, v->bytes, cudaMemcpyDeviceToDevice);
+    uint8_t *gu = nullptr;
+    e = cudaMalloc(&gu, gt->bytes + up->bytes);
+    if (e != cudaSuccess) return fail(ZGPU_ERR_OUT_OF_MEMORY, "gate/up allocation");
+    m->gateup.push_back(gu);
+    cudaMemcpy2D(gu, 2 * gt->gstride, gt->d, gt->gstride, gt->gstride, gt->groups,
+                 cudaMemcpyDeviceToDevice);
+    cudaMemcpy2D(gu + gt->gstride, 2 * gt->gstride, up->d, up->gstride, up->gstride, up->groups,
+                 cudaMemcpyDeviceToDevice);
+    m->o.push_back(o);
+    m->down.push_back(dn);
+  }
+  // norms
+  const size_t nn = static_cast<size_t>(2) * L * H + static_cast<size_t>(2) * L * hd + H;
+  std::vector<float> norms(nn);
+  for (uint32_t l = 0; l < L; ++l) {
+    std::memcpy(&norms[static_cast<size_t>(l) * H], d->layers[l].attn_norm, H * 4);
+    std::memcpy(&norms[static_cast<size_t>(L + l) * H], d->layers[l].ffn_norm, H * 4);
+    std::memcpy(&norms[static_cast<size_t>(2) * L * H + static_cast<size_t>(l) * hd], d->layers[l].q_norm, hd * 4);
+    std::memcpy(&norms[static_cast<size_t>(2) * L * H + static_cast<size_t>(L + l) * hd], d->layers[l].k_norm,
+                hd * 4);
+  }
+  std::memcpy(&norms[static_cast<size_t>(2) * L * H + static_cast<size_t>(2) * L * hd], d->output_norm, H * 4);
+  if ((e = cudaMalloc(&m->d_norms, nn * 4)) != cudaSuccess) return fail(ZGPU_ERR_OUT_OF_MEMORY, "norms");
+  cudaMemcpy(m->d_norms, norms.data(), nn * 4, cudaMemcpyHostToDevice);
+  // RopeContext::new (ops.rs:79-93)
+  std::vector<float> inv(hd / 2);
+  for (uint32_t i = 0; i < hd / 2; ++i)
+    inv[i] = powf(d->rope_theta, -2.0f * static_cast<float>(i) / static_cast<float>(hd));
+  if ((e = cudaMalloc(&m->d_inv_freqs, inv.size() * 4)) != cudaSuccess) return fail(ZGPU_ERR_OUT_OF_MEMORY, "rope");
+  cudaMemcpy(m->d_inv_freqs, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice);
+
+  const uint32_t qkv_rows = m->q_dim + 2 * m->kv_dim;
+  if (cudaMalloc(&m->d_hidden, H * 4) || cudaMalloc(&m->d_qkvo, qkv_rows * 4) ||
+      cudaMalloc(&m->d_attn, m->q_dim * 4) || cudaMalloc(&m->d_act, F * 4) ||
+      cudaMalloc(&m->d_logits, static_cast<size_t>(d->vocab_padded) * 4) ||
+      cudaMalloc(&m->d_argmax, 8) || cudaMalloc(&m->d_state, sizeof(StepState)) ||
+      cudaMalloc(&m->d_status, 4) || cudaMalloc(&m->d_counters, d->n_kv_heads * 4))
+    return fail(ZGPU_ERR_OUT_OF_MEMORY, "activation buffers");
+  const unsigned long long init = kArgmaxInitKey;
+  cudaMemcpy(m->d_argmax, &init, 8, cudaMemcpyHostToDevice);
+  cudaMemset(m->d_status, 0, 4);
+  cudaMemset(m->d_counters, 0, d->n_kv_heads * 4);
+  cudaMemset(m->d_hidden, 0, H * 4);
+  for (auto &ev : m->ev) cudaEventCreate(&ev);
+  e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail(ZGPU_ERR_CUDA, "model upload");
+  *out = m;
+  return ZGPU_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Size the attention split scratch for a cache; at most 64 tokens per split.
+zgpu_status prepare_kv(zgpu_model *m, zgpu_kv *kv) {
+  zgpu_ctx *ctx = m->ctx;
+  if (kv->n_layers != m->desc.n_layers)
+    return zgpu_fail(ctx, ZGPU_ERR_KV_LAYER_OUT_OF_RANGE, "kv cache layer count differs from the model");
+  if (kv->n_kv != m->desc.n_kv_heads || kv->head_dim != m->desc.head_dim)
+    return zgpu_fail(ctx, ZGPU_ERR_KV_INVALID_SLICE_LENGTH, "kv cache geometry differs from the model");
+  uint32_t splits = 16;
+  while ((kv->max_tokens + splits - 1) / splits > 64) splits *= 2;
+  if (splits != m->max_splits || !m->d_part) {
+    cudaFree(m->d_part);
+    m->d_part = nullptr;
+    const size_t n = static_cast<size_t>(m->desc.n_q_heads) * splits * (m->desc.head_dim + 2);
+    cudaError_t e = cudaMalloc(&m->d_part, n * 4);
+    if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "attention scratch");
+    m->max_splits = splits;
+    drop_graphs(m);
+  }
+  return ZGPU_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+zgpu_status zgpu_forward_single_token(zgpu_model *m, zgpu_kv *kv, uint32_t token, uint32_t pos,
+                                      float *hidden_out) {
+  if (!m || !kv) return ZGPU_ERR_INVALID_ARG;
+  zgpu_ctx *ctx = m->ctx;
+  cudaSetDevice(ctx->device);
+  zgpu_status s = prepare_kv(m, kv);
+  if (s) return s;
+  if (pos >= kv->max_tokens) return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "position beyond the cache");
+  if (token >= m->desc.vocab_padded) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "token id beyond the vocab");
+  cudaError_t e = grow(&m->d_prompt, &m->prompt_cap, 1);
+  if (e == cudaSuccess) e = grow(&m->d_tokens, &m->tokens_cap, 1);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "state buffers");
+  if ((s = set_state(m, 1, pos, m->desc.vocab_real, 1))) return s;
+  const bool use_graph = !(ctx->flags & ZGPU_FLAG_NO_GRAPH);
+  if (use_graph && (s = build_graphs(m, kv))) return s;
+  e = cudaMemcpyAsync(m->d_prompt, &token, 4, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) {
+    if (use_graph) {
+      e = cudaGraphLaunch(m->fwd_graph, ctx->stream);
+      ctx->launches += m->fwd_kernels;
+    } else {
+      e = enqueue_forward(m, kv, &ctx->launches);
+    }
+  }
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "forward");
+  if (hidden_out) {
+    e = cudaMemcpyAsync(hidden_out, m->d_hidden, m->desc.hidden * 4, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "hidden d2h");
+  }
+  uint32_t st = 0;
+  if ((s = read_status(m, &st))) return s;
+  return map_status(ctx, st);
+}
+
+zgpu_status zgpu_lm_head_argmax(zgpu_model *m, uint32_t vocab_real, uint32_t *token_out,
+                                float *logits_out) {
+  if (!m || !token_out) return ZGPU_ERR_INVALID_ARG;
+  zgpu_ctx *ctx = m->ctx;
+  cudaSetDevice(ctx->device);
+  if (vocab_real > m->desc.vocab_padded) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "vocab_real > padded");
+  cudaError_t e = grow(&m->d_prompt, &m->prompt_cap, 1);
+  if (e == cudaSuccess) e = grow(&m->d_tokens, &m->tokens_cap, 1);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "state buffers");
+  zgpu_status s = set_state(m, 1, 0, vocab_real, 1);
+  if (s) return s;
+  const bool use_graph = !(ctx->flags & ZGPU_FLAG_NO_GRAPH) && m->lm_graph;
+  if (use_graph) {
+    e = cudaGraphLaunch(m->lm_graph, ctx->stream);
+    ctx->launches += m->lm_kernels;
+  } else {
+    e = enqueue_lm_head(m, &ctx->launches);
+  }
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "lm head");
+  if (logits_out) {
+    e = cudaMemcpyAsync(logits_out, m->d_logits, static_cast<size_t>(m->desc.vocab_padded) * 4,
+                        cudaMemcpyDeviceToHost, ctx->stream);
+    if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "logits d2h");
+  }
+  e = cudaMemcpyAsync(token_out, m->d_tokens, 4, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "token d2h");
+  uint32_t st = 0;
+  if ((s = read_status(m, &st))) return s;
+  return map_status(ctx, st);
+}
+
+zgpu_status zgpu_generate_greedy(zgpu_model *m, zgpu_kv *kv, const uint32_t *prompt,
+                                 uint32_t n_prompt, uint32_t n_gen, uint32_t *tokens_out,
+                                 float *logits_out) {
+  if (!m || !kv || !prompt || !tokens_out || n_prompt == 0 || n_gen == 0) return ZGPU_ERR_INVALID_ARG;
+  zgpu_ctx *ctx = m->ctx;
+  cudaSetDevice(ctx->device);
+  zgpu_status s = prepare_kv(m, kv);
+  if (s) return s;
+  const uint32_t steps = n_prompt + n_gen - 1;
+  if (steps > kv->max_tokens)
+    return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "prompt + generation exceeds the cache");
+  for (uint32_t i = 0; i < n_prompt; ++i)
+    if (prompt[i] >= m->desc.vocab_padded) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "prompt id beyond the vocab");
+  cudaError_t e = grow(&m->d_prompt, &m->prompt_cap, n_prompt);
+  if (e == cudaSuccess) e = grow(&m->d_tokens, &m->tokens_cap, n_gen);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "state buffers");
+  if ((s = set_state(m, n_prompt, 0, m->desc.vocab_real, n_gen))) return s;
+  e = cudaMemcpyAsync(m->d_prompt, prompt, n_prompt * 4, cudaMemcpyHostToDevice, ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "prompt upload");
+  const bool use_graph = !(ctx->flags & ZGPU_FLAG_NO_GRAPH);
+  if (use_graph && (s = build_graphs(m, kv))) return s;
+  const size_t V = m->desc.vocab_padded;
+  uint32_t launches = 0;
+  auto run_step = [&](uint32_t step) -> cudaError_t {
+    cudaError_t err;
+    if (use_graph) {
+      err = cudaGraphLaunch(m->step_graph, ctx->stream);
+      launches += m->step_kernels;
+    } else {
+      err = enqueue_forward(m, kv, &launches);
+      if (err == cudaSuccess) err = enqueue_lm_head(m, &launches);
+    }
+    if (err == cudaSuccess && logits_out && step + 1 >= n_prompt) {
+      err = cudaMemcpyAsync(logits_out + static_cast<size_t>(step + 1 - n_prompt) * V, m->d_logits,
+                            V * 4, cudaMemcpyDeviceToHost, ctx->stream);
+    }
+    return err;
+  };
+  cudaEventRecord(m->ev[0], ctx->stream);
+  for (uint32_t st = 0; st < n_prompt && e == cudaSuccess; ++st) e = run_step(st);
+  cudaEventRecord(m->ev[1], ctx->stream);
+  for (uint32_t st = n_prompt; st < steps && e == cudaSuccess; ++st) e = run_step(st);
+  cudaEventRecord(m->ev[2], ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "generate");
+  e = cudaMemcpyAsync(tokens_out, m->d_tokens, n_gen * 4, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "tokens d2h");
+  uint32_t st = 0;
+  if ((s = read_status(m, &st))) return s;
+  float pre = 0.f, dec = 0.f;
+  cudaEventElapsedTime(&pre, m->ev[0], m->ev[1]);
+  cudaEventElapsedTime(&dec, m->ev[1], m->ev[2]);
+  m->perf.steps = n_gen - 1;
+  m->perf.kernel_launches = launches;
+  m->perf.prefill_ms = pre;
+  m->perf.decode_ms = dec;
+  ctx->launches += launches;
+  return map_status(ctx, st);
+}
+
+zgpu_status zgpu_perf_snapshot(const zgpu_model *m, zgpu_perf *out) {
+  if (!m || !out) return ZGPU_ERR_INVALID_ARG;
+  *out = m->perf;
+  return ZGPU_OK;
+}
+
+}  // extern "C"

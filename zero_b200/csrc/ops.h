@@ -1,0 +1,75 @@
+// ops.h — parameter blocks and launchers of the non-GEMV kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "internal.h"
+
+namespace zgpu {
+
+// Device-resident decode state: the CUDA graph of one step reads and
+// advances it, so a replay needs no host-side parameter updates.
+struct StepState {
+  uint32_t step;            // forward index since the last reset
+  uint32_t n_prompt;        // steps < n_prompt take their token from the prompt
+  uint32_t pos_base;        // position of step 0
+  uint32_t pos;             // position of the current step (written by embed)
+  uint32_t token;           // token of the current step (written by embed)
+  uint32_t next_token;      // argmax of the last LM head
+  uint32_t n_gen_cap;       // capacity of tokens_out
+  uint32_t vocab_real;
+  uint32_t first_err_step;  // 0xFFFFFFFF when no LM-head error happened
+  float last_max;
+};
+
+struct EmbedParams {
+  const uint8_t *emb;       // X4 device table
+  uint64_t gstride;
+  uint32_t quant;           // ZGPU_Q8_0 / ZGPU_Q4_0
+  uint32_t hidden;
+  uint32_t vocab;           // rows of the table
+  const uint32_t *prompt;
+  StepState *state;
+  float *hidden_out;
+  uint32_t *status;
+};
+
+struct FinalizeParams {
+  unsigned long long *argmax;
+  StepState *state;
+  uint32_t *tokens_out;
+  uint32_t *status;
+};
+
+struct AttnParams {
+  const float *qkv;          // [n_q*hd | n_kv*hd | n_kv*hd] raw projections
+  const float *q_norm, *k_norm;
+  const float *inv_freqs;    // [hd/2] RopeContext (ops.rs:79)
+  float *kv_layer;           // K block of this layer; V block follows at +kv_block
+  uint64_t kv_block;         // max_tokens * n_kv * hd
+  uint32_t max_tokens;
+  const uint32_t *pos_ptr;   // device position of the token
+  float *out;                // [n_q*hd]
+  float *part;               // [n_q][max_splits][hd + 2]
+  uint32_t *counters;        // [n_kv]
+  uint32_t *status;
+  uint32_t n_q, n_kv, max_splits;
+  float eps, scale;
+};
+
+cudaError_t launch_attention(const AttnParams &ap, const LaunchCfg &lc);
+cudaError_t launch_embed(const EmbedParams &p, const LaunchCfg &lc);
+cudaError_t launch_finalize(const FinalizeParams &p, const LaunchCfg &lc);
+cudaError_t launch_rmsnorm(const float *x, const float *w, float *out, uint32_t n, float eps,
+                           cudaStream_t s);
+cudaError_t launch_rope(float *qk, const float *inv_freqs, uint32_t n_heads, uint32_t head_dim,
+                        uint32_t pos, cudaStream_t s);
+cudaError_t launch_silu_mul(const float *g, const float *u, float *out, uint64_t n,
+                            cudaStream_t s);
+cudaError_t launch_q8act_gemv(const uint8_t *w, uint64_t gstride, uint32_t rows, uint32_t bpr,
+                              const uint8_t *xq, float *out, cudaStream_t s);
+cudaError_t launch_quantize_q8_0(const float *x, uint8_t *out, uint64_t n, uint32_t *status,
+                                 cudaStream_t s);
+
+}  // namespace zgpu
