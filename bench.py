@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="zero_b200", choices=["zero_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the per-token C-ABI loop")
+    ap.add_argument("--no-roofline", action="store_true", help="skip the standalone GEMV sweep")
     return ap.parse_args()
 
 
@@ -260,52 +262,67 @@ def main():
     gpu_launches = step_kernels * args.steps
 
     # ------------------------------------------------ e2e through the C ABI
-    kv2 = model.new_kv(max_tokens)
-    for i, t in enumerate(prompt):
-        model.forward_single_token(kv2, int(t), i)
-    tok, _ = model.lm_head_argmax(want_logits=False)
-    barrier()
-    t0 = time.perf_counter()
-    pos = PROMPT_LEN
-    for _ in range(args.steps):
-        model.forward_single_token(kv2, tok, pos)
+    e2e_tok_s = None
+    if not args.no_e2e:
+        kv2 = model.new_kv(max_tokens)
+        for i, t in enumerate(prompt):
+            model.forward_single_token(kv2, int(t), i)
         tok, _ = model.lm_head_argmax(want_logits=False)
-        pos += 1
-    e2e_s = time.perf_counter() - t0
-    if world > 1:
-        t = torch.tensor([e2e_s], device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e_tok_s = world * args.steps / e2e_s
-    kv2.close()
+        barrier()
+        t0 = time.perf_counter()
+        pos = PROMPT_LEN
+        for _ in range(args.steps):
+            model.forward_single_token(kv2, tok, pos)
+            tok, _ = model.lm_head_argmax(want_logits=False)
+            pos += 1
+        e2e_s = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([e2e_s], device="cuda")
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            e2e_s = float(t.item())
+        e2e_tok_s = world * args.steps / e2e_s
+        kv2.close()
 
     # -------------------------------------- roofline of the dominant kernel
-    # Q4_0X4 GEMV 2048 -> 6144 (ffn_gate / ffn_up of every layer: 56 distinct
-    # 7.08 MB tensors, 396 MB per sweep > L2), on a torch stream timed with
-    # CUDA events on that same stream.
-    keys = []
-    for i in range(cfg.n_layers):
-        keys.append(model._layers[i].ffn_gate)
-        keys.append(model._layers[i].ffn_up)
-    x = torch.randn(cfg.hidden, device="cuda", dtype=torch.float32)
-    y = torch.empty(cfg.ffn, device="cuda", dtype=torch.float32)
-    stream = torch.cuda.Stream()
-    sh = stream.cuda_stream
-    reps = 4
-    with torch.cuda.stream(stream):
-        for k in keys:   # warm-up sweep
-            ctx.linear_dispatch_device(x.data_ptr(), k, y.data_ptr(), cfg.hidden, cfg.ffn, zb.Q4_0, sh)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(reps):
+    # Q4_0X4 GEMV 2048 -> 6144 over the ffn_gate / ffn_up tensors of every
+    # layer (56 distinct 7.08 MB tensors, 396 MB per sweep > L2).  The sweep is
+    # captured into a CUDA graph on a torch stream so host launch cost does not
+    # enter, and timed with CUDA events recorded on that stream.
+    peaks = measured_peaks()
+    gemv_bytes = cfg.ffn * cfg.hidden * 18 // 32 + cfg.hidden * 4 + cfg.ffn * 4
+    gemv_ms = None
+    if not args.no_roofline:
+        keys = []
+        for i in range(cfg.n_layers):
+            keys.append(model._layers[i].ffn_gate)
+            keys.append(model._layers[i].ffn_up)
+        x = torch.randn(cfg.hidden, device="cuda", dtype=torch.float32)
+        y = torch.empty(cfg.ffn, device="cuda", dtype=torch.float32)
+        stream = torch.cuda.Stream()
+        sh = stream.cuda_stream
+
+        def sweep():
             for k in keys:
                 ctx.linear_dispatch_device(x.data_ptr(), k, y.data_ptr(), cfg.hidden, cfg.ffn, zb.Q4_0, sh)
-        e1.record(stream)
-    stream.synchronize()
-    gemv_ms = e0.elapsed_time(e1) / (reps * len(keys))
-    gemv_bytes = cfg.ffn * cfg.hidden * 18 // 32 + cfg.hidden * 4 + cfg.ffn * 4
-    gemv_gbs = gemv_bytes / (gemv_ms * 1e-3) / 1e9
-    peaks = measured_peaks()
+
+        with torch.cuda.stream(stream):
+            sweep()                                   # warm-up, eager
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            sweep()
+        reps = 8
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            graph.replay()
+            e0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(stream)
+        stream.synchronize()
+        gemv_ms = e0.elapsed_time(e1) / (reps * len(keys))
+        del graph
+    gemv_gbs = gemv_bytes / (gemv_ms * 1e-3) / 1e9 if gemv_ms else None
     step_bytes = cfg.weight_bytes_per_token()
     step_gbs = step_bytes * (args.steps / (dec_ms / 1000.0)) / 1e9
 
@@ -335,14 +352,16 @@ def main():
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "tokens_first": [int(v) for v in toks[:4]]},
             "roofline": {"bound": "hbm", "kernel": "gemv_x4 Q4_0 2048->6144",
-                         "achieved": round(gemv_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(gemv_gbs / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
+                         "achieved": round(gemv_gbs, 1) if gemv_gbs else None,
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gemv_gbs / peaks["hbm_gbs"], 4) if gemv_gbs else None,
+                         "peak_source": peaks["source"],
                          "traffic": NCU_TRAFFIC_PER_LAUNCH, "algorithmic_bytes": gemv_bytes,
-                         "avg_launch_us": round(gemv_ms * 1000, 3),
+                         "avg_launch_us": round(gemv_ms * 1000, 3) if gemv_ms else None,
                          "step_hbm_gbs": round(step_gbs, 1),
                          "step_frac": round(step_gbs / peaks["hbm_gbs"], 4)},
-            "e2e": {"value": round(e2e_tok_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 84,
-                    "d2h_bytes_per_step": 12},
+            "e2e": {"value": round(e2e_tok_s, 2) if e2e_tok_s else None, "unit": "tok/s",
+                    "h2d_bytes_per_step": 84, "d2h_bytes_per_step": 12},
             "gpu_launches": int(gpu_launches),
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,

@@ -132,6 +132,9 @@ zgpu_status zgpu_quantize_q8_0(zgpu_ctx *ctx, const float *x, void *blocks_out, 
  * scales): out = sum_b d_w*d_x*sum_j (n-8)*q.  Host buffers. */
 zgpu_status zgpu_linear_q8act(zgpu_ctx *ctx, const void *xq_blocks, const void *w_key, float *out,
                               uint64_t in_dim, uint64_t out_dim);
+/* Same with device-resident Q8_0 blocks / output on `stream` (async). */
+zgpu_status zgpu_linear_q8act_device(zgpu_ctx *ctx, const void *d_xq_blocks, const void *w_key,
+                                     float *d_out, uint64_t in_dim, uint64_t out_dim, void *stream);
 
 /* ------------------------------------------------------------- small ops */
 /* rmsnorm (ops.rs:29-52). */

@@ -61,6 +61,22 @@ def test_generate_matches_oracle(cfg):
     m.close(); kv.close(); ctx.close()
 
 
+@pytest.mark.parametrize("cfg", TINY[:2], ids=lambda c: c.name)
+def test_long_context_uses_split_attention(cfg):
+    # > 256 cached tokens: the attention runs as several splits per kv-head
+    # merged by the last CTA (flash-decoding partials).
+    ctx, w, m = build(cfg, seed=25)
+    prompt = synth.prompt_ids(cfg, 530, seed=25)
+    kv = m.new_kv(600)
+    toks, logits = m.generate_greedy(kv, prompt, 6, want_logits=True)
+    r = O.OracleRun(cfg, w, 600, order=O.ORDER_AVX512)
+    rc, ref_t, margins, ref_l = r.generate(prompt, 6, want_logits=True)
+    assert rc == 0
+    assert np.array_equal(toks, ref_t)
+    assert max(rel_l2(logits[s], ref_l[s]) for s in range(6)) < 1e-4
+    m.close(); kv.close(); ctx.close()
+
+
 def test_step_api_matches_generate():
     cfg = TINY[1]
     ctx, w, m = build(cfg, seed=22)

@@ -123,6 +123,10 @@ class Context:
                                           _ptr(out), in_dim, out_dim))
         return out
 
+    def linear_q8act_device(self, d_xq: int, w, d_out: int, in_dim: int, out_dim: int, stream: int = 0):
+        key = w if isinstance(w, int) else _ptr(w)
+        self._check(LIB.zgpu_linear_q8act_device(self.h, d_xq, key, d_out, in_dim, out_dim, stream or None))
+
     # ---------------------------------------------------------- small ops
     def rmsnorm(self, x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
         x = np.ascontiguousarray(x, np.float32)

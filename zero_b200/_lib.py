@@ -1,7 +1,7 @@
 """ctypes binding of libzgpu.so (the in-tree sm_100a library).
 
 The library must exist: there is no CPU fallback for the decode path.  Build
-it with ``python -m zero_b200.build``.
+it with ``python zero_b200/build.py``.
 """
 from __future__ import annotations
 
@@ -12,7 +12,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libzgpu.so"
 
 if not LIB_PATH.exists():
     raise ImportError(
-        f"{LIB_PATH} is missing: build the CUDA extension with `python -m zero_b200.build` "
+        f"{LIB_PATH} is missing: build the CUDA extension with `python zero_b200/build.py` "
         "(zero_b200 has no CPU fallback)"
     )
 
@@ -60,6 +60,7 @@ _SIGS = {
     "zgpu_linear_dispatch_device": (_i32, [_vp, _vp, _vp, _vp, _u64, _u64, _u32, _vp]),
     "zgpu_quantize_q8_0": (_i32, [_vp, _vp, _vp, _u64]),
     "zgpu_linear_q8act": (_i32, [_vp, _vp, _vp, _vp, _u64, _u64]),
+    "zgpu_linear_q8act_device": (_i32, [_vp, _vp, _vp, _vp, _u64, _u64, _vp]),
     "zgpu_rmsnorm": (_i32, [_vp, _vp, _vp, _vp, _u64, _f]),
     "zgpu_rope": (_i32, [_vp, _vp, _u32, _u32, _u32, _f]),
     "zgpu_silu_mul": (_i32, [_vp, _vp, _vp, _vp, _u64]),

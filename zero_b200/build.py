@@ -1,6 +1,7 @@
 """Build libzgpu.so in-tree: hand-written CUDA for sm_100a plus the C++ host runtime.
 
-Run as ``python -m zero_b200.build`` (or through ``__graft_entry__.build()``).
+Run as ``python zero_b200/build.py`` (or through ``__graft_entry__.build()``);
+it does not import the package, which needs the library this script builds.
 Objects go to ``zero_b200/_build/``; the shared library lands next to this
 file so that it travels with the source tree.
 """
@@ -27,6 +28,10 @@ CUDA_FLAGS = ARCH + [
     "--expt-relaxed-constexpr",
 ]
 CXX_FLAGS = ["-O2", "-fPIC", "-std=c++17", "-Wall", "-pthread"]
+# ZGPU_DEVICE_CHECKS=1 builds kernels that bounds-check their shared/global
+# accesses, record the first failure in the status block and skip it.
+if os.environ.get("ZGPU_DEVICE_CHECKS") == "1":
+    CUDA_FLAGS.append("-DZGPU_DEVICE_CHECKS")
 
 CU_SOURCES = ["gemv.cu", "attention.cu", "ops.cu", "ctx.cu", "model.cu"]
 CXX_SOURCES = ["synth.cpp"]

@@ -23,6 +23,27 @@ enum : uint32_t {
   ZDEV_ERR_BOUNDS = 1u << 4,      // a token / position outside the cache
 };
 
+// The status block is kStatusWords uint32: word 0 holds the ZDEV_ERR_* bits;
+// builds with ZGPU_DEVICE_CHECKS record the first failed bounds check in
+// words 1..3 (check code, two values) and skip the offending access.
+constexpr int kStatusWords = 8;
+
+__device__ __forceinline__ void dev_check_fail(uint32_t *status, uint32_t code, uint32_t a,
+                                               uint32_t b) {
+  if (atomicCAS(&status[1], 0u, code) == 0u) {
+    status[2] = a;
+    status[3] = b;
+  }
+  atomicOr(&status[0], ZDEV_ERR_BOUNDS);
+}
+
+#ifdef ZGPU_DEVICE_CHECKS
+#define ZDEV_CHECK(cond, status, code, a, b) \
+  ((cond) ? true : (::zgpu::dev_check_fail((status), (code), (a), (b)), false))
+#else
+#define ZDEV_CHECK(cond, status, code, a, b) true
+#endif
+
 // 1 s bound on any device-side wait.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 

@@ -80,9 +80,10 @@ zgpu_status zgpu_init(const zgpu_opts *opts, zgpu_ctx **out) {
   ctx->flags = opts ? opts->flags : 0;
   if (cudaSetDevice(dev) != cudaSuccess ||
       cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
-      cudaMalloc(&ctx->d_status, sizeof(uint32_t)) != cudaSuccess ||
-      cudaMemset(ctx->d_status, 0, sizeof(uint32_t)) != cudaSuccess ||
-      zgpu::gemv_setup() != cudaSuccess) {
+      cudaMalloc(&ctx->d_status, zgpu::kStatusWords * sizeof(uint32_t)) != cudaSuccess ||
+      cudaMemset(ctx->d_status, 0, zgpu::kStatusWords * sizeof(uint32_t)) != cudaSuccess ||
+      zgpu::gemv_setup() != cudaSuccess || zgpu::attention_setup() != cudaSuccess ||
+      zgpu::ops_setup() != cudaSuccess) {
     delete ctx;
     return ZGPU_ERR_CUDA;
   }
@@ -158,14 +159,15 @@ zgpu_status zgpu_register_weights(zgpu_ctx *ctx, const void *host_ptr, size_t le
       return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "byte length does not match rows x cols");
     t.quant = quant;
     t.interleave = x4 ? 4 : 1;
-    t.groups = (rows + 3) / 4;
+    // groups padded to an even count: the GEMV works on units of two groups
+    t.groups = ((rows + 3) / 4 + 1) & ~uint64_t(1);
     const uint64_t gb = bpr * bb * 4;          // bytes of one group stream
     t.gstride = (gb + 15) & ~uint64_t(15);
     t.bytes = t.groups * t.gstride;
     // Build the padded X4 image on the host, then upload once.
     std::vector<uint8_t> img;
     const uint8_t *src = static_cast<const uint8_t *>(host_ptr);
-    if (!x4 || t.gstride != gb) {
+    if (!x4 || t.gstride != gb || t.groups * 4 != rows) {
       try {
         img.assign(t.bytes, 0);
       } catch (...) {
@@ -174,14 +176,14 @@ zgpu_status zgpu_register_weights(zgpu_ctx *ctx, const void *host_ptr, size_t le
       for (uint64_t g = 0; g < t.groups; ++g) {
         uint8_t *dst = img.data() + g * t.gstride;
         if (x4) {
-          std::memcpy(dst, src + g * gb, gb);
+          if (g * 4 < rows) std::memcpy(dst, src + g * gb, gb);
           continue;
         }
         for (uint64_t b = 0; b < bpr; ++b) {
           uint8_t *gbk = dst + b * bb * 4;
           for (uint64_t l = 0; l < 4; ++l) {
             const uint64_t r = g * 4 + l;
-            if (r >= rows) continue;  // padded rows stay zero blocks
+            if (r >= rows) continue;  // padded rows / groups stay zero blocks
             const uint8_t *blk = src + (r * bpr + b) * bb;
             gbk[2 * l] = blk[0];
             gbk[2 * l + 1] = blk[1];
@@ -226,11 +228,15 @@ static zgpu_status ensure_scratch(zgpu_ctx *ctx, size_t nx, size_t ny) {
 }
 
 static zgpu_status check_status_word(zgpu_ctx *ctx) {
-  uint32_t st = 0;
-  ZCHECK(cudaMemcpyAsync(&st, ctx->d_status, 4, cudaMemcpyDeviceToHost, ctx->stream), "status");
+  uint32_t sw[zgpu::kStatusWords] = {0};
+  ZCHECK(cudaMemcpyAsync(sw, ctx->d_status, sizeof(sw), cudaMemcpyDeviceToHost, ctx->stream), "status");
   ZCHECK(cudaStreamSynchronize(ctx->stream), "sync");
+  const uint32_t st = sw[0];
   if (st) {
-    cudaMemsetAsync(ctx->d_status, 0, 4, ctx->stream);
+    cudaMemsetAsync(ctx->d_status, 0, sizeof(sw), ctx->stream);
+    if (sw[1])
+      return zgpu_fail(ctx, ZGPU_ERR_CUDA, "device bounds check " + std::to_string(sw[1]) + " failed (" +
+                                               std::to_string(sw[2]) + ", " + std::to_string(sw[3]) + ")");
     if (st & zgpu::ZDEV_ERR_TIMEOUT)
       return zgpu_fail(ctx, ZGPU_ERR_DEVICE_TIMEOUT, "device wait timed out");
     if (st & zgpu::ZDEV_ERR_NUMERICAL)
@@ -252,6 +258,7 @@ static zgpu_status linear_device(zgpu_ctx *ctx, const float *d_x, const void *w_
     return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "linear_dispatch: shape/quant mismatch with registration");
   zgpu::GemvDesc g;
   g.w = t->d;
+  g.wbytes = t->bytes;
   g.gstride = t->gstride;
   g.quant = t->quant;
   g.rows = static_cast<uint32_t>(out_dim);
@@ -361,6 +368,25 @@ zgpu_status zgpu_quantize_q8_0(zgpu_ctx *ctx, const float *x, void *blocks_out, 
   ++ctx->launches;
   ZCHECK(cudaMemcpyAsync(blocks_out, ctx->d_y, nb * 34, cudaMemcpyDeviceToHost, ctx->stream), "d2h");
   return check_status_word(ctx);
+}
+
+zgpu_status zgpu_linear_q8act_device(zgpu_ctx *ctx, const void *d_xq, const void *w_key,
+                                     float *d_out, uint64_t in_dim, uint64_t out_dim, void *stream) {
+  if (!ctx || !d_xq || !d_out || in_dim == 0 || in_dim % 32) return ZGPU_ERR_INVALID_ARG;
+  cudaSetDevice(ctx->device);
+  const DeviceTensor *t = zgpu_lookup(ctx, w_key);
+  if (!t) return zgpu_fail(ctx, ZGPU_ERR_UNREGISTERED_WEIGHT, "linear_q8act: unregistered weight");
+  if (t->quant != ZGPU_Q4_0)
+    return zgpu_fail(ctx, ZGPU_ERR_UNSUPPORTED_QUANT, "linear_q8act: weights must be Q4_0");
+  if (t->cols != in_dim || t->rows != out_dim)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "linear_q8act: shape mismatch with registration");
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  ZCHECK(zgpu::launch_q8act_gemv(t->d, t->gstride, static_cast<uint32_t>(out_dim),
+                                 static_cast<uint32_t>(in_dim / 32),
+                                 static_cast<const uint8_t *>(d_xq), d_out, s),
+         "q8act gemv");
+  ++ctx->launches;
+  return ZGPU_OK;
 }
 
 zgpu_status zgpu_linear_q8act(zgpu_ctx *ctx, const void *xq_blocks, const void *w_key, float *out,

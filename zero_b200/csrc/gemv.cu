@@ -5,26 +5,37 @@
 // multi-projection / LM-head-argmax dispatches built on them
 // (kernel/src/inference_avx512.rs:826-945, :1061-1118).
 //
-// Data path (one CTA per SM, persistent over a contiguous range of "units";
-// a unit is U consecutive 4-row groups — U = 2 pairs a gate group with its up
-// group for the SwiGLU epilogue):
-//   * one producer lane streams each unit's group bytes (contiguous on the
-//     device) into a ring of shared-memory slots with 1-D TMA bulk copies
-//     (cp.async.bulk, L2 evict-first), signalling an mbarrier per slot;
-//   * consumer warps are arranged as KS x GW: warp (ks, team) owns K-slice ks
-//     (32 blocks, one per lane) of every unit its team takes, so each lane
-//     keeps its block's 32 activations in registers for the whole launch;
-//   * the lane dequantises its block for the unit's 4U rows in registers:
-//     Q4_0 nibbles become exact floats through the 2^23 exponent trick
-//     (bits OR'd into a float whose exponent makes the nibble's place value
-//     an integer; one packed f32x2 subtract removes the bias), accumulated
-//     with packed f32x2 FMAs against the pre-scaled activations; Q8_0 bytes
-//     go through the same trick after a byte permute;
-//   * a warp reduce-scatter leaves each row's K-slice sum in a lane, K-slices
-//     are combined in fixed order through shared memory, and the epilogue
-//     stores / adds the residual / applies SiLU(gate)*up / tracks the argmax.
-// Every reduction has a fixed order, so results are bitwise reproducible
-// from run to run and independent of the grid size.
+// Work decomposition.  A unit is two consecutive 4-row groups (8 output rows;
+// for the SwiGLU epilogue the device layout pairs gate group g with up group
+// g).  An item is one unit restricted to one K-chunk of 32 blocks (1024
+// inputs), so every lane of a warp handles exactly one 32-element block of
+// the 8 rows.  CTA c owns a contiguous range of units and all their chunks.
+//
+// Data path (2 CTAs per SM):
+//   * prologue: the consumer threads build the activation vector once per CTA
+//     in shared memory — RMSNorm applied (PRO_RMSNORM, fixed-order sum of
+//     squares identical in every CTA), and for Q4_0 each element pre-scaled by
+//     2^-c for its nibble's bit class c, laid out in the float2 pairs the
+//     inner loop consumes, 16-byte chunks XOR-swizzled by block so that lanes
+//     reading different blocks hit different banks;
+//   * consumer warp w takes items w, w+8, ... of the CTA; it owns ring slots
+//     [w*S, (w+1)*S), fed by lane w of the producer warp with two 1-D TMA bulk
+//     copies per item (the chunk of each group stream; cp.async.bulk, L2
+//     evict-first).  One producer lane and one consumer warp per slot keep
+//     every slot's mbarrier phases strictly in order.  The producer starts
+//     before the programmatic-dependent-launch wait, so weights stream while
+//     the previous kernel finishes;
+//   * each lane dequantises its block for the 8 rows in registers: Q4_0
+//     nibbles become exact floats through the 2^23 exponent trick (nibble bits
+//     OR'd into the mantissa of 2^23, one packed f32x2 subtract removes 2^23),
+//     accumulated with packed f32x2 FMAs; d*(sum - 8*sum x) per block; Q8_0
+//     bytes take the same trick after a byte permute;
+//   * a warp reduce-scatter leaves the item's 8 row sums in lanes 4r, which
+//     store them to shared memory; after all items the K-chunks of each row
+//     are added in chunk order and the epilogue stores / adds the residual /
+//     applies SiLU(gate)*up / tracks the LM-head argmax.
+// Every reduction has a fixed order, so results are bitwise reproducible from
+// run to run and independent of the grid size.
 #include <cfloat>
 
 #include "common.cuh"
@@ -34,21 +45,32 @@ namespace zgpu {
 
 namespace {
 
-constexpr int kMaxConsumerWarps = 8;
-constexpr int kThreads = 32 * (kMaxConsumerWarps + 1);
+constexpr int kWarps = 8;                      // consumer warps per CTA
+constexpr int kThreads = 32 * (kWarps + 1);
+constexpr int kConsumers = 32 * kWarps;
+constexpr int kRows = 8;                       // output rows per unit
+constexpr uint32_t kChunkBlocks = 32;          // blocks per K-chunk (one per lane)
 constexpr uint32_t kMagic = 0x4B000000u;       // 2^23 as f32 bits
 constexpr float kTwo23 = 8388608.0f;
-constexpr size_t kRingBudget = 100 * 1024;     // two CTAs (two kernels) fit per SM
+constexpr size_t kSmemBudget = 110 * 1024;     // two CTAs per SM
+constexpr int kCtasPerSm = 2;
+constexpr uint32_t kMaxSlotsPerWarp = 4;
 
 struct KParams {
   const uint8_t *w;
   uint64_t gstride;          // bytes per group stream (multiple of 16)
-  uint32_t rows;             // valid output rows
+  uint64_t wbytes;           // bytes of the weight buffer
+  uint32_t rows;             // valid output rows (SwiGLU: output length)
   uint32_t units;            // total units
   uint32_t units_per_cta;
   uint32_t bpr;              // 32-element blocks per row
+  uint32_t ks;               // K-chunks per unit
   uint32_t in_dim;
-  uint32_t ks, gw, ns;
+  uint32_t spw;              // ring slots per consumer warp
+  uint32_t half_bytes;       // bytes of one group's chunk in a slot (multiple of 16)
+  uint32_t xbytes;           // shared bytes of the prepared activation image
+  uint32_t ring_off;         // offset of the ring (after the image and the partials)
+  uint32_t smem_bytes;       // dynamic shared bytes of the launch
   const float *x;
   const float *norm_w;
   float eps;
@@ -56,6 +78,27 @@ struct KParams {
   unsigned long long *argmax;
   uint32_t *status;
 };
+
+// Position of activation element e (0..31) of a block inside its 32-float
+// shared-memory image, and the power-of-two scale it carries (Q4_0 only).
+// Pair 4m+p holds (x[4m+p] * s_lo(p), x[4m+16+p] * s_hi(p)) — the order in
+// which q4_dot consumes the nibbles of qs word m.
+__device__ __forceinline__ uint32_t q4_slot(uint32_t e) {
+  const uint32_t hi = e >> 4, m = (e & 15) >> 2, p = e & 3;
+  return 2 * (4 * m + p) + hi;
+}
+__device__ __forceinline__ float q4_scale(uint32_t e) {
+  // bit class of the nibble as q4_dot isolates it: low nibbles of bytes
+  // 0..3 sit at bits 0, 8, 16 and (after >>12) 12; high nibbles at 4, 12
+  // (bits 12-15), 8 (bits 20-23 >> 12) and 16 (bits 28-31 >> 12).
+  const uint32_t p = e & 3;
+  if (e < 16) return p == 0 ? 1.0f : p == 1 ? 0.00390625f : p == 2 ? 1.52587890625e-05f : 0.000244140625f;
+  return p == 0 ? 0.0625f : p == 1 ? 0.000244140625f : p == 2 ? 0.00390625f : 1.52587890625e-05f;
+}
+// Float offset of slot s (0..31) of block b in the swizzled image.
+__device__ __forceinline__ uint32_t x_off(uint32_t b, uint32_t s) {
+  return b * 32 + ((((s >> 2) ^ (b & 7)) << 2) | (s & 3));
+}
 
 template <int R>
 __device__ __forceinline__ float reduce_scatter(float (&v)[R], uint32_t lane) {
@@ -78,30 +121,19 @@ __device__ __forceinline__ float reduce_scatter(float (&v)[R], uint32_t lane) {
   return v[0];
 }
 
-template <int R>
-struct RowShift {
-  static constexpr int value = (R == 4) ? 3 : (R == 8) ? 2 : 0;
-};
-
-// One Q4_0 row of one block: sum_j x_j * n_j (x pre-scaled per bit class),
-// returned as d * (sum - 8 * sum_j x_j).
-__device__ __forceinline__ float q4_row(const uint32_t (&q)[4], const float2 (&xs)[16], float d,
-                                        float x8) {
+// sum_j x_j * n_j of one Q4_0 row-block, x pre-scaled per bit class.
+__device__ __forceinline__ float q4_dot(const uint32_t (&q)[4], const float2 (&xs)[16]) {
   const float2 bias = make_float2(-kTwo23, -kTwo23);
   float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int m = 0; m < 4; ++m) {
     const uint32_t w = q[m], w12 = w >> 12;
-    // element 4m (bits 0-3, class 0) and 4m+16 (bits 4-7, class 4)
     float2 f0 = make_float2(__uint_as_float((w & 0x0000000Fu) | kMagic),
                             __uint_as_float((w & 0x000000F0u) | kMagic));
-    // element 4m+1 (bits 8-11, class 8) and 4m+17 (bits 12-15, class 12)
     float2 f1 = make_float2(__uint_as_float((w & 0x00000F00u) | kMagic),
                             __uint_as_float((w & 0x0000F000u) | kMagic));
-    // element 4m+2 (bits 16-19, class 16) and 4m+18 (bits 20-23 -> 8-11, class 8)
     float2 f2 = make_float2(__uint_as_float((w & 0x000F0000u) | kMagic),
                             __uint_as_float((w12 & 0x00000F00u) | kMagic));
-    // element 4m+3 (bits 24-27 -> 12-15, class 12) and 4m+19 (bits 28-31 -> 16-19, class 16)
     float2 f3 = make_float2(__uint_as_float((w12 & 0x0000F000u) | kMagic),
                             __uint_as_float((w12 & 0x000F0000u) | kMagic));
     acc0 = __ffma2_rn(xs[4 * m + 0], __fadd2_rn(f0, bias), acc0);
@@ -109,12 +141,11 @@ __device__ __forceinline__ float q4_row(const uint32_t (&q)[4], const float2 (&x
     acc0 = __ffma2_rn(xs[4 * m + 2], __fadd2_rn(f2, bias), acc0);
     acc1 = __ffma2_rn(xs[4 * m + 3], __fadd2_rn(f3, bias), acc1);
   }
-  float s = (acc0.x + acc0.y) + (acc1.x + acc1.y);
-  return d * (s - x8);
+  return (acc0.x + acc0.y) + (acc1.x + acc1.y);
 }
 
-// One Q8_0 row of one block: d * sum_j x_j * q_j.
-__device__ __forceinline__ float q8_row(const uint32_t (&q)[8], const float2 (&xp)[16], float d) {
+// sum_j x_j * q_j of one Q8_0 row-block.
+__device__ __forceinline__ float q8_dot(const uint32_t (&q)[8], const float2 (&xp)[16]) {
   const float2 bias = make_float2(-(kTwo23 + 128.f), -(kTwo23 + 128.f));
   float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
@@ -127,146 +158,160 @@ __device__ __forceinline__ float q8_row(const uint32_t (&q)[8], const float2 (&x
     acc0 = __ffma2_rn(xp[2 * k + 0], __fadd2_rn(f0, bias), acc0);
     acc1 = __ffma2_rn(xp[2 * k + 1], __fadd2_rn(f1, bias), acc1);
   }
-  float s = (acc0.x + acc0.y) + (acc1.x + acc1.y);
-  return d * s;
+  return (acc0.x + acc0.y) + (acc1.x + acc1.y);
 }
 
-template <int QT, int PRO, int EPI, int U>
-__global__ void __launch_bounds__(kThreads, 2) gemv_x4_kernel(const KParams p) {
-  constexpr int GB = (QT == ZGPU_Q4_0) ? 72 : 136;
-  constexpr int R = 4 * U;
-  constexpr int SH = RowShift<R>::value;
+template <int QT, int PRO, int EPI>
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KParams p) {
+  constexpr uint32_t GB = (QT == ZGPU_Q4_0) ? 72 : 136;
   extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ float red[kWarps];
+  __shared__ unsigned long long best_w[kWarps];
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t KS = p.ks, GW = p.gw, NW = KS * GW, NS = p.ns;
-  const uint32_t slot_bytes = U * static_cast<uint32_t>(p.gstride);
-  uint8_t *ring = smem;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + static_cast<size_t>(NS) * slot_bytes);
-  uint64_t *empty = full + NS;
-  float *red = reinterpret_cast<float *>(empty + NS);      // [GW][2][KS][R]
-  float *ssq_part = red + GW * 2 * KS * R;                  // [KS]
+  const uint32_t S = p.spw;
+  const uint32_t slot_bytes = 2 * p.half_bytes;
+  float *xsm = reinterpret_cast<float *>(smem);                       // bpr * 32 floats
+  float *x8 = reinterpret_cast<float *>(smem + static_cast<size_t>(p.bpr) * 128);
+  float *part = reinterpret_cast<float *>(smem + p.xbytes);           // [items][8]
+  uint8_t *ring = smem + p.ring_off;
+  uint64_t *full = reinterpret_cast<uint64_t *>(ring + static_cast<size_t>(kWarps) * S * slot_bytes);
+  uint64_t *empty = full + kWarps * S;
 
   const uint32_t u0 = blockIdx.x * p.units_per_cta;
   const uint32_t u1 = min(u0 + p.units_per_cta, p.units);
   const uint32_t nloc = u1 > u0 ? u1 - u0 : 0;
+  const uint32_t nitems = nloc * p.ks;
 
   if (threadIdx.x == 0) {
-    for (uint32_t i = 0; i < NS; ++i) {
+    for (uint32_t i = 0; i < kWarps * S; ++i) {
       mbar_init(smem_addr(&full[i]), 1);
-      mbar_init(smem_addr(&empty[i]), KS);
+      mbar_init(smem_addr(&empty[i]), 1);
     }
     fence_barrier_init();
   }
   __syncthreads();
   pdl_launch_dependents();
 
-  if (warp >= NW) {
-    // ---------------- producer ----------------
-    if (warp == NW && lane == 0) {
+  if (warp == kWarps) {
+    // ---------------- producer: lane w feeds consumer warp w's slots ----------
+    if (lane < kWarps) {
       const uint64_t pol = l2_evict_first_policy();
       uint32_t issued = 0;
-      for (uint32_t i = 0; i < nloc; ++i) {
-        const uint32_t slot = i % NS;
-        if (i >= NS && !mbar_wait(smem_addr(&empty[slot]), ((i / NS) - 1) & 1, p.status)) break;
+      for (uint32_t k = lane, j = 0; k < nitems; k += kWarps, ++j) {
+        const uint32_t slot = lane * S + (j % S);
+        if (j >= S && !mbar_wait(smem_addr(&empty[slot]), ((j / S) - 1) & 1, p.status)) break;
+        const uint32_t unit = u0 + k / p.ks, chunk = k % p.ks;
+        const uint32_t nb = min(kChunkBlocks, p.bpr - chunk * kChunkBlocks);
+        const uint32_t bytes = (nb * GB + 15) & ~15u;
+        const uint64_t src = (2ull * unit) * p.gstride + static_cast<uint64_t>(chunk) * kChunkBlocks * GB;
+        if (!ZDEV_CHECK(src + p.gstride + bytes <= p.wbytes && bytes <= p.half_bytes, p.status, 1,
+                        unit, chunk))
+          break;
+        if (!ZDEV_CHECK(p.ring_off + (slot + 1) * slot_bytes <= p.smem_bytes, p.status, 2, slot,
+                        p.smem_bytes))
+          break;
         const uint32_t fb = smem_addr(&full[slot]);
-        mbar_arrive_expect_tx(fb, slot_bytes);
-        tma_bulk_g2s(smem_addr(ring + static_cast<size_t>(slot) * slot_bytes),
-                     p.w + static_cast<uint64_t>(u0 + i) * slot_bytes, slot_bytes, fb, pol);
+        const uint32_t dst = smem_addr(ring + static_cast<size_t>(slot) * slot_bytes);
+        mbar_arrive_expect_tx(fb, 2 * bytes);
+        tma_bulk_g2s(dst, p.w + src, bytes, fb, pol);
+        tma_bulk_g2s(dst + p.half_bytes, p.w + src + p.gstride, bytes, fb, pol);
         ++issued;
       }
       // Drain: never leave a copy in flight when the CTA may exit.
-      for (uint32_t s = 0; s < NS && s < issued; ++s) {
-        const uint32_t last = s + ((issued - 1 - s) / NS) * NS;
-        mbar_wait(smem_addr(&full[s]), (last / NS) & 1, p.status);
+      for (uint32_t s = 0; s < S && s < issued; ++s) {
+        const uint32_t last = s + ((issued - 1 - s) / S) * S;
+        mbar_wait(smem_addr(&full[lane * S + s]), (last / S) & 1, p.status);
       }
     }
     return;
   }
 
-  // ---------------- consumers ----------------
-  const uint32_t ks = warp % KS, team = warp / KS;
-  const uint32_t b = ks * 32 + lane;
-  const bool has_b = b < p.bpr;
-
+  // ---------------- consumers: prepare the activation image ----------------
   pdl_wait();   // the activations are the previous kernel's output
-
-  float xv[32];
-  if (has_b) {
-    const float4 *src = reinterpret_cast<const float4 *>(p.x + static_cast<size_t>(b) * 32);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      float4 t = src[k];
-      xv[4 * k] = t.x; xv[4 * k + 1] = t.y; xv[4 * k + 2] = t.z; xv[4 * k + 3] = t.w;
-    }
-  } else {
-#pragma unroll
-    for (int k = 0; k < 32; ++k) xv[k] = 0.f;
-  }
-
+  const uint32_t tid = threadIdx.x;
+  const uint32_t nf4 = p.in_dim / 4;
+  float inv = 1.0f;
   if (PRO == PRO_RMSNORM) {
-    // rmsnorm (ops.rs:29-52) with a fixed-order parallel sum of squares:
-    // lane-sequential over its 32 values, xor-tree over lanes, then the
-    // K-slices in order.  Every CTA computes the identical value.
+    // rmsnorm (ops.rs:29-52): fixed-order sum of squares (per thread over its
+    // float4s in order, xor-tree in the warp, warps in order).
     float ss = 0.f;
-#pragma unroll
-    for (int k = 0; k < 32; ++k) ss = __fadd_rn(ss, __fmul_rn(xv[k], xv[k]));
+    for (uint32_t f = tid; f < nf4; f += kConsumers) {
+      const float4 t = reinterpret_cast<const float4 *>(p.x)[f];
+      ss = __fadd_rn(ss, __fadd_rn(__fadd_rn(__fmul_rn(t.x, t.x), __fmul_rn(t.y, t.y)),
+                                   __fadd_rn(__fmul_rn(t.z, t.z), __fmul_rn(t.w, t.w))));
+    }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-    if (team == 0 && lane == 0) ssq_part[ks] = ss;
-    named_bar_sync(1, NW * 32);
+    if (lane == 0) red[warp] = ss;
+    named_bar_sync(1, kConsumers);
     float tot = 0.f;
-    for (uint32_t k = 0; k < KS; ++k) tot = __fadd_rn(tot, ssq_part[k]);
-    const float mean = __fdiv_rn(tot, static_cast<float>(p.in_dim));
-    const float rms = __fsqrt_rn(__fadd_rn(mean, p.eps));
-    const float inv = __fdiv_rn(1.0f, rms);
-    if (has_b) {
-      const float4 *wsrc = reinterpret_cast<const float4 *>(p.norm_w + static_cast<size_t>(b) * 32);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        float4 t = wsrc[k];
-        xv[4 * k] = __fmul_rn(__fmul_rn(xv[4 * k], inv), t.x);
-        xv[4 * k + 1] = __fmul_rn(__fmul_rn(xv[4 * k + 1], inv), t.y);
-        xv[4 * k + 2] = __fmul_rn(__fmul_rn(xv[4 * k + 2], inv), t.z);
-        xv[4 * k + 3] = __fmul_rn(__fmul_rn(xv[4 * k + 3], inv), t.w);
+    for (int w = 0; w < kWarps; ++w) tot = __fadd_rn(tot, red[w]);
+    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(p.in_dim)), p.eps)));
+  }
+  // Warp-uniform trip count: the per-block sum below shuffles across the 8
+  // lanes of a block, and nf4 is a multiple of 8, so a block's lanes are
+  // either all in range or all out of range.
+  for (uint32_t f0 = warp * 32; f0 < nf4; f0 += kConsumers) {
+    const uint32_t f = f0 + lane;
+    const bool valid = f < nf4;
+    float4 t = valid ? reinterpret_cast<const float4 *>(p.x)[f] : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (PRO == PRO_RMSNORM && valid) {
+      const float4 g = reinterpret_cast<const float4 *>(p.norm_w)[f];
+      t.x = __fmul_rn(__fmul_rn(t.x, inv), g.x);
+      t.y = __fmul_rn(__fmul_rn(t.y, inv), g.y);
+      t.z = __fmul_rn(__fmul_rn(t.z, inv), g.z);
+      t.w = __fmul_rn(__fmul_rn(t.w, inv), g.w);
+    }
+    const uint32_t b = f >> 3, e0 = (f & 7) * 4;
+    // a failed check only suppresses the writes: every lane still reaches the
+    // shuffles below
+    const bool in_range =
+        valid && ZDEV_CHECK(b < p.bpr && b * 132 + 132 <= p.xbytes, p.status, 3, b, p.xbytes);
+    const float v[4] = {t.x, t.y, t.z, t.w};
+    if (QT == ZGPU_Q4_0) {
+      if (in_range) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) xsm[x_off(b, q4_slot(e0 + k))] = v[k] * q4_scale(e0 + k);
       }
+      // 8 * sum of the block's 32 activations, fixed tree over its 8 lanes.
+      float s = (v[0] + v[1]) + (v[2] + v[3]);
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      s += __shfl_xor_sync(0xffffffffu, s, 4);
+      if (in_range && (f & 7) == 0) x8[b] = 8.0f * s;
+    } else if (in_range) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) xsm[x_off(b, e0 + k)] = v[k];
     }
   }
+  named_bar_sync(1, kConsumers);
 
-  // Per-lane activation operands.
-  float2 xs[16];
-  float x8 = 0.f;
-  if (QT == ZGPU_Q4_0) {
-    // element -> bit class (see q4_row): x scaled by 2^-class so that the
-    // product with (n << class) is exactly x * n.
-    float sx = 0.f;
-#pragma unroll
-    for (int k = 0; k < 32; ++k) sx += xv[k];
-    x8 = 8.0f * sx;
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      xs[4 * m + 0] = make_float2(xv[4 * m], xv[4 * m + 16] * 0.0625f);
-      xs[4 * m + 1] = make_float2(xv[4 * m + 1] * 0.00390625f, xv[4 * m + 17] * 0.000244140625f);
-      xs[4 * m + 2] = make_float2(xv[4 * m + 2] * 1.52587890625e-05f, xv[4 * m + 18] * 0.00390625f);
-      xs[4 * m + 3] = make_float2(xv[4 * m + 3] * 0.000244140625f, xv[4 * m + 19] * 1.52587890625e-05f);
-    }
-  } else {
-#pragma unroll
-    for (int k = 0; k < 16; ++k) xs[k] = make_float2(xv[2 * k], xv[2 * k + 1]);
-  }
-
+  // ---------------- consumers: items ----------------
   bool failed = false;
-  unsigned long long best = kArgmaxInitKey;
-  uint32_t it = 0;
-  for (uint32_t i = team; i < nloc; i += GW, ++it) {
-    const uint32_t slot = i % NS;
-    if (!failed && !mbar_wait(smem_addr(&full[slot]), (i / NS) & 1, p.status)) failed = true;
-    float part[R];
-    const uint8_t *ubase = ring + static_cast<size_t>(slot) * slot_bytes;
+  for (uint32_t k = warp, j = 0; k < nitems; k += kWarps, ++j) {
+    const uint32_t slot = warp * S + (j % S);
+    if (!failed && !mbar_wait(smem_addr(&full[slot]), (j / S) & 1, p.status)) failed = true;
+    const uint32_t chunk = k % p.ks;
+    const uint32_t b = chunk * kChunkBlocks + lane;
+    float acc[kRows];
 #pragma unroll
-    for (int g = 0; g < U; ++g) {
-      const uint8_t *blk = ubase + g * p.gstride + static_cast<size_t>(b) * GB;
-      if (has_b && !failed) {
+    for (int r = 0; r < kRows; ++r) acc[r] = 0.f;
+    if (!failed && b < p.bpr) {
+      const uint8_t *sbase = ring + static_cast<size_t>(slot) * slot_bytes;
+      float2 xs[16];
+      const float4 *xb = reinterpret_cast<const float4 *>(xsm + b * 32);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float4 t = xb[c ^ (b & 7)];
+        xs[2 * c] = make_float2(t.x, t.y);
+        xs[2 * c + 1] = make_float2(t.z, t.w);
+      }
+      const float xb8 = (QT == ZGPU_Q4_0) ? x8[b] : 0.f;
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        const uint8_t *blk = sbase + g * p.half_bytes + lane * GB;
         const uint2 sc = *reinterpret_cast<const uint2 *>(blk);
         const float d[4] = {h2f(sc.x & 0xFFFF), h2f(sc.x >> 16), h2f(sc.y & 0xFFFF),
                             h2f(sc.y >> 16)};
@@ -276,51 +321,50 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_x4_kernel(const KParams p) {
             const uint2 a = *reinterpret_cast<const uint2 *>(blk + 8 + 16 * r);
             const uint2 c = *reinterpret_cast<const uint2 *>(blk + 16 + 16 * r);
             const uint32_t q[4] = {a.x, a.y, c.x, c.y};
-            part[4 * g + r] = q4_row(q, xs, d[r], x8);
+            acc[4 * g + r] = d[r] * (q4_dot(q, xs) - xb8);
           }
         } else {
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
             uint32_t q[8];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint2 a = *reinterpret_cast<const uint2 *>(blk + 8 + 32 * r + 8 * k);
-              q[2 * k] = a.x;
-              q[2 * k + 1] = a.y;
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint2 a = *reinterpret_cast<const uint2 *>(blk + 8 + 32 * r + 8 * kk);
+              q[2 * kk] = a.x;
+              q[2 * kk + 1] = a.y;
             }
-            part[4 * g + r] = q8_row(q, xs, d[r]);
+            acc[4 * g + r] = d[r] * q8_dot(q, xs);
           }
         }
-      } else {
-#pragma unroll
-        for (int r = 0; r < 4; ++r) part[4 * g + r] = 0.f;
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_addr(&empty[slot]));
+    const float v = reduce_scatter<kRows>(acc, lane);        // lane holds row lane >> 2
+    if ((lane & 3) == 0) part[k * kRows + (lane >> 2)] = v;
+  }
+  named_bar_sync(1, kConsumers);
 
-    float v = reduce_scatter<R>(part, lane);
-    float y = 0.f;
-    if (KS > 1) {
-      float *rb = red + (static_cast<size_t>(team) * 2 + (it & 1)) * KS * R;
-      if ((lane & ((1u << SH) - 1)) == 0) rb[ks * R + (lane >> SH)] = v;
-      named_bar_sync(2 + team, KS * 32);
-      if (ks == 0 && lane < R) {
-        for (uint32_t k = 0; k < KS; ++k) y += rb[k * R + lane];
+  // ---------------- epilogue: K-chunks in order, then per row ---------------
+  unsigned long long best = kArgmaxInitKey;
+  if (EPI == EPI_SWIGLU) {
+    // unit = {gate rows 4u..4u+3, up rows 4u..4u+3}
+    for (uint32_t t = tid; t < nloc * 4; t += kConsumers) {
+      const uint32_t ul = t >> 2, r = t & 3;
+      float yg = 0.f, yu = 0.f;
+      for (uint32_t c = 0; c < p.ks; ++c) {
+        yg += part[(ul * p.ks + c) * kRows + r];
+        yu += part[(ul * p.ks + c) * kRows + 4 + r];
       }
-    } else {
-      y = __shfl_sync(0xffffffffu, v, (lane & (R - 1)) << SH);
+      const uint32_t row = (u0 + ul) * 4 + r;
+      if (row < p.rows) p.out[row] = ref_silu_mul(yg, yu);
     }
-    if (ks != 0) continue;
-
-    const uint32_t unit = u0 + i;
-    if (EPI == EPI_SWIGLU) {
-      // unit = {gate rows 4u..4u+3, up rows 4u..4u+3}
-      const float yu = __shfl_down_sync(0xffffffffu, y, 4);
-      const uint32_t row = unit * 4 + lane;
-      if (lane < 4 && row < p.rows) p.out[row] = ref_silu_mul(y, yu);
-    } else if (lane < R) {
-      const uint32_t row = unit * R + lane;
+  } else {
+    for (uint32_t t = tid; t < nloc * kRows; t += kConsumers) {
+      const uint32_t ul = t / kRows, r = t % kRows;
+      float y = 0.f;
+      for (uint32_t c = 0; c < p.ks; ++c) y += part[(ul * p.ks + c) * kRows + r];
+      const uint32_t row = (u0 + ul) * kRows + r;
       if (row < p.rows) {
         if (EPI == EPI_STORE) {
           p.out[row] = y;
@@ -335,38 +379,51 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_x4_kernel(const KParams p) {
     }
   }
 
-  if (EPI == EPI_ARGMAX && ks == 0) {
+  if (EPI == EPI_ARGMAX) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
       unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
       best = o > best ? o : best;
     }
-    if (lane == 0 && best != kArgmaxInitKey) atomicMax(p.argmax, best);
+    if (lane == 0) best_w[warp] = best;
+    named_bar_sync(1, kConsumers);
+    if (threadIdx.x == 0) {
+      unsigned long long b = kArgmaxInitKey;
+      for (int w = 0; w < kWarps; ++w) b = best_w[w] > b ? best_w[w] : b;
+      if (b != kArgmaxInitKey) atomicMax(p.argmax, b);
+    }
   }
 }
 
-template <int QT, int PRO, int EPI, int U>
+// Every kernel of the step asks for the maximum shared-memory carveout: an SM
+// only hosts CTAs of kernels with one carveout at a time, so a uniform
+// carveout is what lets the next kernel's CTAs become resident (and start
+// their weight prefetch) while the current kernel drains.
+template <int QT, int PRO, int EPI>
 cudaError_t configure_one() {
-  return cudaFuncSetAttribute(gemv_x4_kernel<QT, PRO, EPI, U>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(kRingBudget + 16 * 1024));
+  cudaError_t e = cudaFuncSetAttribute(gemv_x4_kernel<QT, PRO, EPI>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(kSmemBudget));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(gemv_x4_kernel<QT, PRO, EPI>,
+                              cudaFuncAttributePreferredSharedMemoryCarveout,
+                              cudaSharedmemCarveoutMaxShared);
 }
 
 template <int QT, int PRO>
 cudaError_t configure_pro() {
   cudaError_t e;
-  if ((e = configure_one<QT, PRO, EPI_STORE, 1>()) != cudaSuccess) return e;
-  if ((e = configure_one<QT, PRO, EPI_RESADD, 1>()) != cudaSuccess) return e;
-  if ((e = configure_one<QT, PRO, EPI_SWIGLU, 2>()) != cudaSuccess) return e;
-  return configure_one<QT, PRO, EPI_ARGMAX, 1>();
+  if ((e = configure_one<QT, PRO, EPI_STORE>()) != cudaSuccess) return e;
+  if ((e = configure_one<QT, PRO, EPI_RESADD>()) != cudaSuccess) return e;
+  if ((e = configure_one<QT, PRO, EPI_SWIGLU>()) != cudaSuccess) return e;
+  return configure_one<QT, PRO, EPI_ARGMAX>();
 }
 
-template <int QT, int PRO, int EPI, int U>
+template <int QT, int PRO, int EPI>
 cudaError_t launch_one(const KParams &kp, uint32_t grid, size_t smem, const LaunchCfg &lc) {
-  auto fn = gemv_x4_kernel<QT, PRO, EPI, U>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(32 * (kp.ks * kp.gw + 1));
+  cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = lc.stream;
   cudaLaunchAttribute attr[1];
@@ -375,25 +432,23 @@ cudaError_t launch_one(const KParams &kp, uint32_t grid, size_t smem, const Laun
   cfg.attrs = attr;
   cfg.numAttrs = lc.pdl ? 1 : 0;
   if (lc.launch_counter) ++*lc.launch_counter;
-  return cudaLaunchKernelEx(&cfg, fn, kp);
+  return cudaLaunchKernelEx(&cfg, gemv_x4_kernel<QT, PRO, EPI>, kp);
 }
 
 template <int QT, int PRO>
 cudaError_t dispatch_epi(GemvEpi epi, const KParams &kp, uint32_t grid, size_t smem,
                          const LaunchCfg &lc) {
   switch (epi) {
-    case EPI_STORE: return launch_one<QT, PRO, EPI_STORE, 1>(kp, grid, smem, lc);
-    case EPI_RESADD: return launch_one<QT, PRO, EPI_RESADD, 1>(kp, grid, smem, lc);
-    case EPI_SWIGLU: return launch_one<QT, PRO, EPI_SWIGLU, 2>(kp, grid, smem, lc);
-    case EPI_ARGMAX: return launch_one<QT, PRO, EPI_ARGMAX, 1>(kp, grid, smem, lc);
+    case EPI_STORE: return launch_one<QT, PRO, EPI_STORE>(kp, grid, smem, lc);
+    case EPI_RESADD: return launch_one<QT, PRO, EPI_RESADD>(kp, grid, smem, lc);
+    case EPI_SWIGLU: return launch_one<QT, PRO, EPI_SWIGLU>(kp, grid, smem, lc);
+    case EPI_ARGMAX: return launch_one<QT, PRO, EPI_ARGMAX>(kp, grid, smem, lc);
   }
   return cudaErrorInvalidValue;
 }
 
 }  // namespace
 
-// Raise the dynamic shared-memory limit of every GEMV instantiation on the
-// current device (called once per context, outside any stream capture).
 cudaError_t gemv_setup() {
   cudaError_t e;
   if ((e = configure_pro<ZGPU_Q4_0, PRO_PLAIN>()) != cudaSuccess) return e;
@@ -404,45 +459,51 @@ cudaError_t gemv_setup() {
 
 cudaError_t launch_gemv(const GemvDesc &g, GemvPro pro, GemvEpi epi, const GemvIo &io,
                         const LaunchCfg &lc) {
-  if (g.in_dim == 0 || g.in_dim % 32 != 0 || g.groups == 0) return cudaErrorInvalidValue;
-  if (g.gstride % 16 != 0) return cudaErrorInvalidValue;
-  if (epi == EPI_SWIGLU && (g.groups % 2 != 0 || g.quant != ZGPU_Q4_0))
+  if (g.in_dim == 0 || g.in_dim % 32 != 0 || g.groups == 0 || g.groups % 2 != 0)
     return cudaErrorInvalidValue;
+  if (g.gstride % 16 != 0) return cudaErrorInvalidValue;
+  if (epi == EPI_SWIGLU && g.quant != ZGPU_Q4_0) return cudaErrorInvalidValue;
+  const uint32_t GB = g.quant == ZGPU_Q4_0 ? 72 : 136;
   KParams kp = {};
   kp.w = g.w;
   kp.gstride = g.gstride;
+  kp.wbytes = g.wbytes ? g.wbytes : static_cast<uint64_t>(g.groups) * g.gstride;
   kp.rows = g.rows;
   kp.bpr = g.in_dim / 32;
+  kp.ks = (kp.bpr + kChunkBlocks - 1) / kChunkBlocks;
   kp.in_dim = g.in_dim;
-  kp.ks = (kp.bpr + 31) / 32;
-  if (kp.ks > static_cast<uint32_t>(kMaxConsumerWarps)) return cudaErrorInvalidValue;
-  kp.gw = kMaxConsumerWarps / kp.ks;
-  const uint32_t U = (epi == EPI_SWIGLU) ? 2 : 1;
-  kp.units = g.groups / U;
-  const uint32_t ctas = static_cast<uint32_t>(lc.sm_count > 0 ? lc.sm_count : 148);
+  kp.units = g.groups / 2;
+  const uint32_t ctas = static_cast<uint32_t>((lc.sm_count > 0 ? lc.sm_count : 148) * kCtasPerSm);
   kp.units_per_cta = (kp.units + ctas - 1) / ctas;
   const uint32_t grid = (kp.units + kp.units_per_cta - 1) / kp.units_per_cta;
-  const size_t slot = static_cast<size_t>(U) * g.gstride;
-  if (slot * 2 > kRingBudget) return cudaErrorInvalidValue;
-  uint32_t ns = static_cast<uint32_t>(kRingBudget / slot);
-  if (ns > kp.units_per_cta) ns = kp.units_per_cta;
-  if (ns > 32) ns = 32;
-  if (ns < 1) ns = 1;
-  kp.ns = ns;
+  kp.half_bytes = (min(kChunkBlocks, kp.bpr) * GB + 15) & ~15u;
+  const size_t slot = 2 * static_cast<size_t>(kp.half_bytes);
+  // activation image (128 B per block) + 8*sum per block, rounded to 128 B
+  kp.xbytes = static_cast<uint32_t>((static_cast<size_t>(kp.bpr) * 132 + 127) & ~size_t(127));
+  const size_t part_bytes =
+      (static_cast<size_t>(kp.units_per_cta) * kp.ks * kRows * sizeof(float) + 127) & ~size_t(127);
+  kp.ring_off = static_cast<uint32_t>(kp.xbytes + part_bytes);
+  const size_t fixed = kp.ring_off + 1024;
+  if (fixed + kWarps * slot > kSmemBudget) return cudaErrorInvalidValue;
+  uint32_t spw = static_cast<uint32_t>((kSmemBudget - fixed) / (kWarps * slot));
+  const uint32_t items_per_warp = (kp.units_per_cta * kp.ks + kWarps - 1) / kWarps;
+  if (spw > items_per_warp) spw = items_per_warp;
+  if (spw > kMaxSlotsPerWarp) spw = kMaxSlotsPerWarp;
+  if (spw < 1) spw = 1;
+  kp.spw = spw;
   kp.x = io.x;
   kp.norm_w = io.norm_w;
   kp.eps = io.eps;
   kp.out = io.out;
   kp.argmax = io.argmax;
   kp.status = io.status;
-  const size_t R = 4 * U;
-  const size_t smem = slot * ns + 16 * ns + sizeof(float) * (kp.gw * 2 * kp.ks * R + kp.ks) + 16;
+  const size_t smem = kp.ring_off + static_cast<size_t>(kWarps) * spw * slot + 16 * kWarps * spw;
+  kp.smem_bytes = static_cast<uint32_t>(smem);
   if (g.quant == ZGPU_Q4_0) {
     return pro == PRO_RMSNORM ? dispatch_epi<ZGPU_Q4_0, PRO_RMSNORM>(epi, kp, grid, smem, lc)
                               : dispatch_epi<ZGPU_Q4_0, PRO_PLAIN>(epi, kp, grid, smem, lc);
   }
   if (g.quant == ZGPU_Q8_0) {
-    if (epi == EPI_SWIGLU) return cudaErrorInvalidValue;
     return pro == PRO_RMSNORM ? dispatch_epi<ZGPU_Q8_0, PRO_RMSNORM>(epi, kp, grid, smem, lc)
                               : dispatch_epi<ZGPU_Q8_0, PRO_PLAIN>(epi, kp, grid, smem, lc);
   }

@@ -37,6 +37,7 @@ struct GemvDesc {
   uint32_t rows;              // valid output rows
   uint32_t groups;            // groups in the launch
   uint32_t in_dim;
+  uint64_t wbytes = 0;        // bytes of the weight buffer (bounds checks)
 };
 
 enum GemvPro { PRO_PLAIN = 0, PRO_RMSNORM = 1 };

@@ -114,6 +114,7 @@ cudaError_t enqueue_forward(zgpu_model *m, zgpu_kv *kv, uint32_t *counter) {
     GemvIo io;
     // RMSNorm + fused Q|K|V projection
     g.w = m->qkv[l];
+    g.wbytes = static_cast<uint64_t>(qkv_rows / 4) * m->gs_h;
     g.gstride = m->gs_h;
     g.quant = ZGPU_Q4_0;
     g.rows = qkv_rows;
@@ -149,6 +150,7 @@ cudaError_t enqueue_forward(zgpu_model *m, zgpu_kv *kv, uint32_t *counter) {
 
     // O projection + residual
     g.w = m->o[l]->d;
+    g.wbytes = m->o[l]->bytes;
     g.gstride = m->gs_q;
     g.rows = d.hidden;
     g.groups = d.hidden / 4;
@@ -161,6 +163,7 @@ cudaError_t enqueue_forward(zgpu_model *m, zgpu_kv *kv, uint32_t *counter) {
 
     // RMSNorm + fused gate|up + SiLU(gate)*up
     g.w = m->gateup[l];
+    g.wbytes = static_cast<uint64_t>(2 * d.ffn / 4) * m->gs_h;
     g.gstride = m->gs_h;
     g.rows = d.ffn;
     g.groups = 2 * d.ffn / 4;
@@ -175,6 +178,7 @@ cudaError_t enqueue_forward(zgpu_model *m, zgpu_kv *kv, uint32_t *counter) {
 
     // down projection + residual
     g.w = m->down[l]->d;
+    g.wbytes = m->down[l]->bytes;
     g.gstride = m->gs_f;
     g.rows = d.hidden;
     g.groups = d.hidden / 4;
@@ -193,6 +197,7 @@ cudaError_t enqueue_lm_head(zgpu_model *m, uint32_t *counter) {
   LaunchCfg lc = launch_cfg(m, counter);
   GemvDesc g;
   g.w = m->out->d;
+  g.wbytes = m->out->bytes;
   g.gstride = m->out->gstride;
   g.quant = m->out->quant;
   g.rows = d.vocab_padded;
@@ -265,12 +270,15 @@ zgpu_status build_graphs(zgpu_model *m, zgpu_kv *kv) {
 
 zgpu_status read_status(zgpu_model *m, uint32_t *st_out) {
   zgpu_ctx *ctx = m->ctx;
-  uint32_t st = 0;
-  cudaError_t e = cudaMemcpyAsync(&st, m->d_status, 4, cudaMemcpyDeviceToHost, ctx->stream);
+  uint32_t sw[kStatusWords] = {0};
+  cudaError_t e = cudaMemcpyAsync(sw, m->d_status, sizeof(sw), cudaMemcpyDeviceToHost, ctx->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "step status");
-  *st_out = st;
-  if (st) cudaMemsetAsync(m->d_status, 0, 4, ctx->stream);
+  *st_out = sw[0];
+  if (sw[0]) cudaMemsetAsync(m->d_status, 0, sizeof(sw), ctx->stream);
+  if (sw[1])
+    return zgpu_fail(ctx, ZGPU_ERR_CUDA, "device bounds check " + std::to_string(sw[1]) + " failed (" +
+                                             std::to_string(sw[2]) + ", " + std::to_string(sw[3]) + ")");
   return ZGPU_OK;
 }
 
@@ -415,7 +423,7 @@ zgpu_status zgpu_qwen3_create(zgpu_ctx *ctx, const zgpu_qwen3_desc *d, zgpu_mode
   cudaSetDevice(ctx->device);
   if (d->head_dim != 128)
     return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "decode attention kernel requires head_dim 128");
-  if (!d->n_kv_heads || d->n_q_heads % d->n_kv_heads || d->n_q_heads / d->n_kv_heads > 8)
+  if (!d->n_kv_heads || d->n_q_heads % d->n_kv_heads || d->n_q_heads / d->n_kv_heads > 4)
     return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "unsupported GQA geometry");
   if (d->hidden % 32 || d->ffn % 32 || d->hidden % 4 || d->ffn % 4)
     return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "hidden/ffn must be multiples of 32");
@@ -458,6 +466,9 @@ zgpu_status zgpu_qwen3_create(zgpu_ctx *ctx, const zgpu_qwen3_desc *d, zgpu_mode
     const DeviceTensor *up = need(ly.ffn_up, ZGPU_Q4_0, F, H, "ffn_up");
     const DeviceTensor *dn = need(ly.ffn_down, ZGPU_Q4_0, H, F, "ffn_down");
     if (!q || !k || !v || !o || !gt || !up || !dn) return fail(ZGPU_ERR_UNREGISTERED_WEIGHT, ctx->last_error);
+    // the fused Q|K|V stream concatenates whole units of two groups
+    if (q->groups * 4 != q->rows || k->groups * 4 != k->rows || v->groups * 4 != v->rows)
+      return fail(ZGPU_ERR_INVALID_ARG, "q/k/v rows must be multiples of 8");
     m->gs_h = q->gstride;
     m->gs_q = o->gstride;
     m->gs_f = dn->gstride;
@@ -504,11 +515,11 @@ zgpu_status zgpu_qwen3_create(zgpu_ctx *ctx, const zgpu_qwen3_desc *d, zgpu_mode
       cudaMalloc(&m->d_attn, m->q_dim * 4) || cudaMalloc(&m->d_act, F * 4) ||
       cudaMalloc(&m->d_logits, static_cast<size_t>(d->vocab_padded) * 4) ||
       cudaMalloc(&m->d_argmax, 8) || cudaMalloc(&m->d_state, sizeof(StepState)) ||
-      cudaMalloc(&m->d_status, 4) || cudaMalloc(&m->d_counters, d->n_kv_heads * 4))
+      cudaMalloc(&m->d_status, kStatusWords * 4) || cudaMalloc(&m->d_counters, d->n_kv_heads * 4))
     return fail(ZGPU_ERR_OUT_OF_MEMORY, "activation buffers");
   const unsigned long long init = kArgmaxInitKey;
   cudaMemcpy(m->d_argmax, &init, 8, cudaMemcpyHostToDevice);
-  cudaMemset(m->d_status, 0, 4);
+  cudaMemset(m->d_status, 0, kStatusWords * 4);
   cudaMemset(m->d_counters, 0, d->n_kv_heads * 4);
   cudaMemset(m->d_hidden, 0, H * 4);
   for (auto &ev : m->ev) cudaEventCreate(&ev);
@@ -522,15 +533,14 @@ zgpu_status zgpu_qwen3_create(zgpu_ctx *ctx, const zgpu_qwen3_desc *d, zgpu_mode
 
 namespace {
 
-// Size the attention split scratch for a cache; at most 64 tokens per split.
+// Size the attention split scratch for a cache (one partial per split).
 zgpu_status prepare_kv(zgpu_model *m, zgpu_kv *kv) {
   zgpu_ctx *ctx = m->ctx;
   if (kv->n_layers != m->desc.n_layers)
     return zgpu_fail(ctx, ZGPU_ERR_KV_LAYER_OUT_OF_RANGE, "kv cache layer count differs from the model");
   if (kv->n_kv != m->desc.n_kv_heads || kv->head_dim != m->desc.head_dim)
     return zgpu_fail(ctx, ZGPU_ERR_KV_INVALID_SLICE_LENGTH, "kv cache geometry differs from the model");
-  uint32_t splits = 16;
-  while ((kv->max_tokens + splits - 1) / splits > 64) splits *= 2;
+  const uint32_t splits = attention_max_splits(kv->max_tokens);
   if (splits != m->max_splits || !m->d_part) {
     cudaFree(m->d_part);
     m->d_part = nullptr;

@@ -29,6 +29,7 @@ __global__ void embed_kernel(const EmbedParams p) {
     st->pos = st->pos_base + step;
   }
   const uint32_t g = token >> 2, lane = token & 3;
+  if (!ZDEV_CHECK(g < (p.vocab + 3) / 4, p.status, 20, token, p.vocab)) return;
   const uint8_t *grp = p.emb + static_cast<uint64_t>(g) * p.gstride;
   for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < p.hidden;
        e += gridDim.x * blockDim.x) {
@@ -68,7 +69,8 @@ __global__ void finalize_kernel(const FinalizeParams p) {
   }
   if (step + 1 >= st->n_prompt) {
     const uint32_t gi = step + 1 - st->n_prompt;
-    if (gi < st->n_gen_cap) p.tokens_out[gi] = idx;
+    if (gi < st->n_gen_cap && ZDEV_CHECK(gi < st->n_gen_cap, p.status, 21, gi, st->n_gen_cap))
+      p.tokens_out[gi] = idx;
   }
   st->next_token = idx;
   st->last_max = val;
@@ -124,6 +126,23 @@ __global__ void silu_mul_kernel(const float *g, const float *u, float *out, uint
     out[i] = ref_silu_mul(g[i], u[i]);
 }
 
+// binary16 bits of a finite double with |v| <= 65504, rounded to nearest-even
+// straight from the double (struct.pack('<e') semantics): scale the value
+// exactly onto the binary16 grid of its binade (a power-of-two ldexp), round
+// with rint, re-encode.  Subnormal results and the carry into the next binade
+// fall out of the continuous encoding.
+__device__ __forceinline__ uint16_t f64_to_f16_rne(double v) {
+  const uint16_t sign = signbit(v) ? 0x8000u : 0u;
+  const double a = fabs(v);
+  if (a == 0.0) return sign;
+  const int e = ilogb(a);
+  const int qe = (e < -14 ? -14 : e) - 10;
+  const double r = rint(ldexp(a, -qe));
+  if (e < -14) return static_cast<uint16_t>(sign | static_cast<uint16_t>(r));
+  if (r >= 2048.0) return static_cast<uint16_t>(sign | ((e + 16) << 10));
+  return static_cast<uint16_t>(sign | ((e + 15) << 10) | static_cast<uint16_t>(r - 1024.0));
+}
+
 // Q8_0 activation quantiser with the packer's rule (tools/silicatepack.py:
 // 893-907): double-precision d = max|x| / 127, q = round-half-even(x / d)
 // clamped to +-127, d stored as binary16 rounded to nearest-even from the
@@ -150,8 +169,7 @@ __global__ void quantize_q8_0_kernel(const float *x, uint8_t *out, uint64_t nblo
   r = fmin(fmax(r, -127.0), 127.0);
   blk[2 + lane] = static_cast<uint8_t>(static_cast<int8_t>(r));
   if (lane == 0) {
-    const double dc = fmin(d, 65504.0);
-    const uint16_t h = __half_as_ushort(__double2half(dc));
+    const uint16_t h = f64_to_f16_rne(fmin(d, 65504.0));
     blk[0] = static_cast<uint8_t>(h & 0xFF);
     blk[1] = static_cast<uint8_t>(h >> 8);
   }
@@ -213,6 +231,14 @@ cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem, const LaunchCfg 
 }
 
 }  // namespace
+
+cudaError_t ops_setup() {
+  cudaError_t e = cudaFuncSetAttribute(embed_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                       cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(finalize_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                              cudaSharedmemCarveoutMaxShared);
+}
 
 cudaError_t launch_embed(const EmbedParams &p, const LaunchCfg &lc) {
   cudaLaunchAttribute attr[1];

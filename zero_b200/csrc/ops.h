@@ -59,6 +59,10 @@ struct AttnParams {
 };
 
 cudaError_t launch_attention(const AttnParams &ap, const LaunchCfg &lc);
+// Number of attention splits (CTAs per kv-head) a cache of max_tokens needs.
+uint32_t attention_max_splits(uint32_t max_tokens);
+cudaError_t attention_setup();
+cudaError_t ops_setup();
 cudaError_t launch_embed(const EmbedParams &p, const LaunchCfg &lc);
 cudaError_t launch_finalize(const FinalizeParams &p, const LaunchCfg &lc);
 cudaError_t launch_rmsnorm(const float *x, const float *w, float *out, uint32_t n, float eps,

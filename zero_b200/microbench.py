@@ -1,0 +1,98 @@
+"""Standalone GEMV sweep: HBM GB/s of the batch-1 kernels.
+
+    python -m zero_b200.microbench [--shape OUTxIN ...] [--act f32|q8] [--reps R]
+
+For each shape, enough distinct seeded weight copies are registered that one
+pass over them streams more than 2x the 126 MB L2, the launches over all
+copies are captured into one CUDA graph on a torch stream, and the graph is
+replayed `reps` times between CUDA events recorded on that stream.  Prints one
+JSON line per shape: average launch time and algorithmic GB/s (weights +
+activation + output bytes per launch).
+
+--act f32 runs the reference's f32-activation GEMV (Q4_0X4 weights,
+linear_dispatch); --act q8 runs the Q4_0 x Q8_0-activation GEMV.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import numpy as np
+
+import zero_b200 as zb
+from zero_b200 import synth
+
+CONFIG1_SHAPES = ["4096x2048", "12288x2048", "2048x6144", "151936x2048"]
+L2_BYTES = 126 * 1024 * 1024
+
+
+def run_shape(ctx, out_dim: int, in_dim: int, act: str, reps: int, copies: int | None, torch):
+    wbytes = out_dim * in_dim * 18 // 32
+    n = copies or max(2, -(-2 * L2_BYTES // wbytes))
+    keys = []
+    for c in range(n):
+        w = synth.q4_0(100 + c, out_dim + 7 * in_dim, out_dim, in_dim, 0.02)
+        if act == "f32":
+            keys.append(ctx.register(synth.pack_x4(w, out_dim, in_dim, "q4_0"), zb.Q4_0X4, out_dim, in_dim))
+        else:
+            keys.append(ctx.register(w, zb.Q4_0, out_dim, in_dim))
+    stream = torch.cuda.Stream()
+    sh = stream.cuda_stream
+    if act == "f32":
+        x = torch.randn(in_dim, device="cuda", dtype=torch.float32)
+        xbytes = in_dim * 4
+    else:
+        xq = ctx.quantize_q8_0(np.random.default_rng(0).standard_normal(in_dim).astype(np.float32))
+        x = torch.from_numpy(xq).cuda()
+        xbytes = in_dim // 32 * 34
+    y = torch.empty(out_dim, device="cuda", dtype=torch.float32)
+
+    def sweep():
+        for k in keys:
+            if act == "f32":
+                ctx.linear_dispatch_device(x.data_ptr(), k, y.data_ptr(), in_dim, out_dim, zb.Q4_0, sh)
+            else:
+                ctx.linear_q8act_device(x.data_ptr(), k, y.data_ptr(), in_dim, out_dim, sh)
+
+    with torch.cuda.stream(stream):
+        sweep()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        sweep()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        graph.replay()
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    stream.synchronize()
+    ms = e0.elapsed_time(e1) / (reps * n)
+    alg = wbytes + xbytes + out_dim * 4
+    del graph
+    ctx.clear_weights()
+    return {"kernel": f"gemv_{'x4_q4_0_f32act' if act == 'f32' else 'q4_0_q8act'}",
+            "shape": f"{in_dim}->{out_dim}", "copies": n, "reps": reps,
+            "avg_launch_us": round(ms * 1000, 3), "algorithmic_bytes": alg,
+            "gbs": round(alg / (ms * 1e-3) / 1e9, 1)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--shape", action="append", help="OUTxIN, repeatable (default: config 1 sweep)")
+    ap.add_argument("--act", default="f32", choices=["f32", "q8"])
+    ap.add_argument("--reps", type=int, default=10)
+    ap.add_argument("--copies", type=int, default=None, help="weight copies (default: > 2x L2)")
+    args = ap.parse_args()
+    import torch
+
+    ctx = zb.Context()
+    for s in args.shape or CONFIG1_SHAPES:
+        o, i = (int(v) for v in s.lower().split("x"))
+        print(json.dumps(run_shape(ctx, o, i, args.act, args.reps, args.copies, torch)), flush=True)
+    ctx.close()
+
+
+if __name__ == "__main__":
+    main()
