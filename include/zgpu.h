@@ -162,6 +162,32 @@ zgpu_status zgpu_kv_store(zgpu_kv *kv, uint32_t layer, uint32_t token, const flo
 zgpu_status zgpu_kv_read(zgpu_kv *kv, uint32_t layer, uint32_t token_count, float *k_out,
                          float *v_out);
 
+/* ------------------------------------------------------ decode attention */
+/* Steps 2-5 of gqa_attention_single_token_dispatch
+ * (crates/zero-llm-inference/src/attention.rs:344-425) for one layer, given
+ * the raw projections qkv = [q (n_q_heads*hd) | k (n_kv*hd) | v (n_kv*hd)]:
+ * per-head QK RMSNorm with q_norm / k_norm [hd] (ops.rs:29-52), RoPE at `pos`
+ * with the RopeContext of freq_base (ops.rs:79-132), KvCache::store_kv of k
+ * and v at `pos` (kv_cache.rs:139), then per q head softmax(q.k/sqrt(hd))
+ * (attention.rs:48-84) over tokens 0..pos and sum_t p_t v_t into
+ * out [n_q_heads*hd].  Requires head_dim 128 and n_q_heads = 1..4 x n_kv.
+ * Errors: ZGPU_ERR_KV_LAYER_OUT_OF_RANGE, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE
+ * (pos >= max_tokens), ZGPU_ERR_NUMERICAL_INSTABILITY (AttentionError::
+ * NumericalInstability).  Synchronous; host buffers. */
+zgpu_status zgpu_gqa_attention_decode(zgpu_ctx *ctx, zgpu_kv *kv, uint32_t layer, uint32_t pos,
+                                      uint32_t n_q_heads, const float *qkv, const float *q_norm,
+                                      const float *k_norm, float freq_base, float eps, float *out);
+/* Device-buffer form: d_inv_freqs is the RopeContext table [hd/2]; launches
+ * on `stream` (NULL = the context stream) without synchronising.  The split
+ * partials live in context-owned device memory grown on first use.  Device-
+ * side numerical errors are recorded in the context status block and
+ * reported by the context's next synchronous entry point. */
+zgpu_status zgpu_gqa_attention_decode_device(zgpu_ctx *ctx, zgpu_kv *kv, uint32_t layer,
+                                             uint32_t pos, uint32_t n_q_heads, const float *d_qkv,
+                                             const float *d_q_norm, const float *d_k_norm,
+                                             const float *d_inv_freqs, float eps, float *d_out,
+                                             void *stream);
+
 /* ------------------------------------------------------------ Qwen3 model */
 /* One decoder layer's tensors, each a registered host key (LayerWeights,
  * forward_pass.rs:226-239).  Matmul tensors are Q4_0 (plain) or Q4_0X4;

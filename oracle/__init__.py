@@ -54,6 +54,9 @@ def _load() -> C.CDLL:
         "zo_linear_q8_0": (None, [_f32p, _u8p, _f32p, sz, sz]),
         "zo_linear_dispatch": (C.c_int, [_f32p, _u8p, _f32p, sz, sz, C.c_int]),
         "zo_softmax": (C.c_int, [_f32p, sz]),
+        "zo_gqa_attention_decode": (C.c_int, [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
+                                              C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+                                              C.c_float, C.c_int, _f32p, _f32p]),
         "zo_linear_q4_0x4_avx512": (None, [_f32p, _u8p, _f32p, sz, sz, C.c_int, C.c_int]),
         "zo_linear_q8_0x4_avx512": (None, [_f32p, _u8p, _f32p, sz, sz, C.c_int, C.c_int]),
         "zo_linear_q4_0_avx512": (None, [_f32p, _u8p, _f32p, sz, sz, C.c_int, C.c_int]),
@@ -210,6 +213,28 @@ def softmax(s: np.ndarray):
     s = np.ascontiguousarray(s, np.float32).copy()
     rc = LIB.zo_softmax(_f(s), s.size)
     return rc, s
+
+
+def gqa_attention_decode(qkv: np.ndarray, q_norm: np.ndarray, k_norm: np.ndarray, inv: np.ndarray,
+                         k_block: np.ndarray, v_block: np.ndarray, pos: int, n_q: int, n_kv: int,
+                         hd: int, eps: float, order: int = 1):
+    """One layer of decode attention (attention.rs:344-425 / inference_avx512.rs:1612-1800).
+
+    k_block / v_block are the layer's cache blocks [max_tokens * n_kv * hd],
+    updated in place at `pos`.  Returns (rc, out[n_q * hd])."""
+    qkv = np.ascontiguousarray(qkv, np.float32)
+    qd, kvd = n_q * hd, n_kv * hd
+    q, k, v = qkv[:qd].copy(), qkv[qd:qd + kvd].copy(), qkv[qd + kvd:qd + 2 * kvd].copy()
+    assert k_block.dtype == np.float32 and k_block.flags.c_contiguous
+    assert v_block.dtype == np.float32 and v_block.flags.c_contiguous
+    max_tokens = k_block.size // kvd
+    work = np.zeros((n_q + n_kv + 1) * hd + max_tokens, np.float32)
+    out = np.zeros(qd, np.float32)
+    rc = LIB.zo_gqa_attention_decode(_f(q), _f(k), _f(v), _f(np.ascontiguousarray(q_norm, np.float32)),
+                                     _f(np.ascontiguousarray(k_norm, np.float32)),
+                                     _f(np.ascontiguousarray(inv, np.float32)), _f(k_block), _f(v_block),
+                                     pos, max_tokens, n_q, n_kv, hd, eps, order, _f(work), _f(out))
+    return rc, out
 
 
 def exp_avx512(x: np.ndarray) -> np.ndarray:

@@ -631,6 +631,63 @@ void zo_rope_apply_avx512(float *qk, const float *c, const float *s, size_t half
  * Qwen3-shaped forward pass
  * ====================================================================== */
 
+/* Steps 2-5 of gqa_attention_single_token_dispatch (attention.rs:344-425;
+ * order 0) and of gqa_attention_single_token_avx512 (inference_avx512.rs:
+ * 1612-1800; order 1) for one layer: per-head QK RMSNorm (ops.rs:29), RoPE at
+ * pos (ops.rs:111 / trig.rs:148,192), KvCache::store_kv (kv_cache.rs:139),
+ * then per q head scores q.k * (1/sqrt(hd)), softmax (attention.rs:48) and
+ * sum_t p_t v_t.  k_block / v_block are this layer's K and V blocks
+ * [max_tokens][n_kv*hd]; work holds (n_q + n_kv + 1)*hd + max_tokens floats. */
+int zo_gqa_attention_decode(const float *q, const float *k, const float *v, const float *q_norm,
+                            const float *k_norm, const float *inv_freqs, float *k_block,
+                            float *v_block, uint32_t pos, uint32_t max_tokens, uint32_t n_q,
+                            uint32_t n_kv, uint32_t hd, float eps, int order, float *work,
+                            float *out) {
+  if (pos >= max_tokens) return ZO_ERR_KV_TOKEN_OUT_OF_RANGE;
+  if (n_kv == 0 || n_q % n_kv || hd % 2 || hd > 512) return ZO_ERR_ARG;
+  const size_t half = hd / 2, kvd = (size_t)n_kv * hd, gqa = n_q / n_kv, total = (size_t)pos + 1;
+  const float scale = 1.0f / sqrtf((float)hd);
+  float *qo = work, *ko = qo + (size_t)n_q * hd, *head = ko + kvd, *sb = head + hd;
+  float cos_lut[256], sin_lut[256];
+  if (order == 1) zo_rope_sincos_lut_avx512(pos, inv_freqs, cos_lut, sin_lut, half);
+  for (size_t h = 0; h < n_q; ++h) zo_rmsnorm(q + h * hd, q_norm, qo + h * hd, hd, eps);
+  for (size_t h = 0; h < n_kv; ++h) zo_rmsnorm(k + h * hd, k_norm, ko + h * hd, hd, eps);
+  for (size_t h = 0; h < n_q; ++h) {
+    if (order == 1) zo_rope_apply_avx512(qo + h * hd, cos_lut, sin_lut, half);
+    else zo_rope(qo + h * hd, inv_freqs, half, pos);
+  }
+  for (size_t h = 0; h < n_kv; ++h) {
+    if (order == 1) zo_rope_apply_avx512(ko + h * hd, cos_lut, sin_lut, half);
+    else zo_rope(ko + h * hd, inv_freqs, half, pos);
+  }
+  memcpy(k_block + (size_t)pos * kvd, ko, kvd * 4);
+  memcpy(v_block + (size_t)pos * kvd, v, kvd * 4);
+  for (size_t qh = 0; qh < n_q; ++qh) {
+    size_t kh = qh / gqa;
+    const float *qv = qo + qh * hd;
+    for (size_t t = 0; t < total; ++t) {
+      const float *kt = k_block + t * kvd + kh * hd;
+      if (order == 1) {
+        sb[t] = zo_dot_product_avx512(qv, kt, hd) * scale;
+      } else {
+        float dot = 0.0f;
+        for (size_t i = 0; i < hd; ++i) dot += qv[i] * kt[i];
+        sb[t] = dot * scale;
+      }
+    }
+    int st = zo_softmax(sb, total);
+    if (st) return st;
+    memset(head, 0, hd * 4);
+    for (size_t t = 0; t < total; ++t) {
+      const float *vt = v_block + t * kvd + kh * hd;
+      if (order == 1) zo_weighted_add_avx512(sb[t], vt, head, hd);
+      else for (size_t i = 0; i < hd; ++i) head[i] += sb[t] * vt[i];
+    }
+    memcpy(out + qh * hd, head, hd * 4);
+  }
+  return ZO_OK;
+}
+
 struct zo_run {
   const zo_qwen3 *m;
   int order, threads, simd;
@@ -639,6 +696,7 @@ struct zo_run {
   float *inv_freqs;
   float *hidden, *norm, *attn_out, *mlp_out, *q, *k, *v, *qo, *ko, *score, *head, *concat;
   float *gate, *up, *hmlp, *logits;
+  float *attn_work;                            /* zo_gqa_attention_decode workspace */
   uint8_t **x4;                                /* per-layer X4 copies for the AVX path */
   uint8_t *out_x4;
 };
@@ -669,6 +727,7 @@ zo_run *zo_run_create(const zo_qwen3 *m, uint32_t max_tokens, int order, int thr
   r->head = calloc(m->head_dim, 4); r->concat = calloc(qd, 4);
   r->gate = calloc(F, 4); r->up = calloc(F, 4); r->hmlp = calloc(F, 4);
   r->logits = calloc(m->vocab_padded, 4);
+  r->attn_work = calloc((size_t)(m->n_q_heads + m->n_kv_heads + 1) * m->head_dim + max_tokens, 4);
   zo_rope_ctx(m->rope_theta, m->head_dim / 2, r->inv_freqs);
   if (order == 1) {
     r->x4 = (uint8_t **)calloc((size_t)m->n_layers * 7, sizeof(uint8_t *));
@@ -698,7 +757,7 @@ void zo_run_destroy(zo_run *r) {
   free(r->kv); free(r->inv_freqs); free(r->hidden); free(r->norm); free(r->attn_out);
   free(r->mlp_out); free(r->q); free(r->k); free(r->v); free(r->qo); free(r->ko);
   free(r->score); free(r->head); free(r->concat); free(r->gate); free(r->up); free(r->hmlp);
-  free(r->logits);
+  free(r->logits); free(r->attn_work);
   free(r);
 }
 
@@ -720,9 +779,8 @@ static void lin(zo_run *r, const float *x, const uint8_t *plain, const uint8_t *
  * :1280-1340 (order 1). */
 int zo_run_forward(zo_run *r, uint32_t token, uint32_t pos, float *hidden_out) {
   const zo_qwen3 *m = r->m;
-  size_t H = m->hidden, F = m->ffn, hd = m->head_dim, half = hd / 2;
+  size_t H = m->hidden, F = m->ffn, hd = m->head_dim;
   size_t nq = m->n_q_heads, nkv = m->n_kv_heads, qd = nq * hd, kvd = nkv * hd;
-  size_t gqa = nq / nkv;
   if (pos >= r->max_tokens) return ZO_ERR_KV_TOKEN_OUT_OF_RANGE;
   if (token >= m->vocab_padded) return ZO_ERR_ARG;
   /* embed_lookup_dispatch (forward_pass.rs:311-370): dequantise one row. */
@@ -738,10 +796,6 @@ int zo_run_forward(zo_run *r, uint32_t token, uint32_t pos, float *hidden_out) {
       return ZO_ERR_UNSUPPORTED_QUANT;
     }
   }
-  float cos_lut[256], sin_lut[256];
-  if (r->order == 1) zo_rope_sincos_lut_avx512(pos, r->inv_freqs, cos_lut, sin_lut, half);
-  const float scale = 1.0f / sqrtf((float)hd);
-  size_t total = (size_t)pos + 1;
   size_t block = (size_t)r->max_tokens * kvd, layer_stride = 2 * block;
 
   for (uint32_t li = 0; li < m->n_layers; ++li) {
@@ -751,43 +805,12 @@ int zo_run_forward(zo_run *r, uint32_t token, uint32_t pos, float *hidden_out) {
     lin(r, r->norm, L->attn_q, x4 ? x4[0] : NULL, r->q, H, qd, ZO_Q4_0);
     lin(r, r->norm, L->attn_k, x4 ? x4[1] : NULL, r->k, H, kvd, ZO_Q4_0);
     lin(r, r->norm, L->attn_v, x4 ? x4[2] : NULL, r->v, H, kvd, ZO_Q4_0);
-    for (size_t h = 0; h < nq; ++h) zo_rmsnorm(r->q + h * hd, L->q_norm, r->qo + h * hd, hd, m->rms_eps);
-    for (size_t h = 0; h < nkv; ++h) zo_rmsnorm(r->k + h * hd, L->k_norm, r->ko + h * hd, hd, m->rms_eps);
-    for (size_t h = 0; h < nq; ++h) {
-      if (r->order == 1) zo_rope_apply_avx512(r->qo + h * hd, cos_lut, sin_lut, half);
-      else zo_rope(r->qo + h * hd, r->inv_freqs, half, pos);
-    }
-    for (size_t h = 0; h < nkv; ++h) {
-      if (r->order == 1) zo_rope_apply_avx512(r->ko + h * hd, cos_lut, sin_lut, half);
-      else zo_rope(r->ko + h * hd, r->inv_freqs, half, pos);
-    }
-    /* KvCache::store_kv (kv_cache.rs:139-183). */
-    float *kbase = r->kv + li * layer_stride, *vbase = kbase + block;
-    memcpy(kbase + (size_t)pos * kvd, r->ko, kvd * 4);
-    memcpy(vbase + (size_t)pos * kvd, r->v, kvd * 4);
-    for (size_t qh = 0; qh < nq; ++qh) {
-      size_t kh = qh / gqa;
-      const float *qv = r->qo + qh * hd;
-      float *sb = r->score + qh * r->max_tokens;
-      for (size_t t = 0; t < total; ++t) {
-        const float *kv = kbase + t * kvd + kh * hd;
-        if (r->order == 1) {
-          sb[t] = zo_dot_product_avx512(qv, kv, hd) * scale;
-        } else {
-          float dot = 0.0f;
-          for (size_t i = 0; i < hd; ++i) dot += qv[i] * kv[i];
-          sb[t] = dot * scale;
-        }
-      }
-      int st = zo_softmax(sb, total);
+    {
+      float *kbase = r->kv + li * layer_stride;
+      int st = zo_gqa_attention_decode(r->q, r->k, r->v, L->q_norm, L->k_norm, r->inv_freqs, kbase,
+                                       kbase + block, pos, r->max_tokens, (uint32_t)nq, (uint32_t)nkv,
+                                       (uint32_t)hd, m->rms_eps, r->order, r->attn_work, r->concat);
       if (st) return st;
-      memset(r->head, 0, hd * 4);
-      for (size_t t = 0; t < total; ++t) {
-        const float *vv = vbase + t * kvd + kh * hd;
-        if (r->order == 1) zo_weighted_add_avx512(sb[t], vv, r->head, hd);
-        else for (size_t i = 0; i < hd; ++i) r->head[i] += sb[t] * vv[i];
-      }
-      memcpy(r->concat + qh * hd, r->head, hd * 4);
     }
     lin(r, r->concat, L->attn_o, x4 ? x4[3] : NULL, r->attn_out, qd, H, ZO_Q4_0);
     for (size_t i = 0; i < H; ++i) r->hidden[i] += r->attn_out[i];

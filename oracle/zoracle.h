@@ -81,6 +81,14 @@ void  zo_linear_q8_0(const float *x, const uint8_t *w, float *out, size_t in_dim
 int   zo_linear_dispatch(const float *x, const uint8_t *w, float *out, size_t in_dim,
                          size_t out_dim, int quant);
 int   zo_softmax(float *scores, size_t len);
+/* One layer of decode attention: QK-norm, RoPE, store_kv, softmax(q.k) . V
+ * (attention.rs:344-425 for order 0, inference_avx512.rs:1612-1800 for
+ * order 1); work = (n_q + n_kv + 1)*hd + max_tokens floats. */
+int   zo_gqa_attention_decode(const float *q, const float *k, const float *v, const float *q_norm,
+                              const float *k_norm, const float *inv_freqs, float *k_block,
+                              float *v_block, uint32_t pos, uint32_t max_tokens, uint32_t n_q,
+                              uint32_t n_kv, uint32_t hd, float eps, int order, float *work,
+                              float *out);
 
 /* ---- AVX-512-order ops (lane-exact restatement) -------------------------- */
 /* threads <= 0 -> all cores.  simd: 0 portable lane emulation, 1 intrinsics

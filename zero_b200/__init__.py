@@ -175,6 +175,20 @@ class KvCache:
         self.ctx._check(LIB.zgpu_kv_read(self.h, layer, token_count, _ptr(k), _ptr(v)))
         return k, v
 
+    def gqa_attention_decode(self, layer: int, pos: int, n_q_heads: int, qkv: np.ndarray,
+                             q_norm: np.ndarray, k_norm: np.ndarray, freq_base: float,
+                             eps: float) -> np.ndarray:
+        """Steps 2-5 of gqa_attention_single_token_dispatch (attention.rs:344-425)
+        for one layer: QK-norm, RoPE, store k/v at `pos`, softmax attention over
+        tokens 0..pos.  Returns the attention output [n_q_heads * head_dim]."""
+        qkv = np.ascontiguousarray(qkv, np.float32)
+        qn = np.ascontiguousarray(q_norm, np.float32)
+        kn = np.ascontiguousarray(k_norm, np.float32)
+        out = np.empty(n_q_heads * self.head_dim, np.float32)
+        self.ctx._check(LIB.zgpu_gqa_attention_decode(self.ctx.h, self.h, layer, pos, n_q_heads, _ptr(qkv),
+                                                      _ptr(qn), _ptr(kn), freq_base, eps, _ptr(out)))
+        return out
+
 
 class Qwen3Model:
     """A Qwen3-shaped model on the device, built from synth.qwen3_weights() tensors.

@@ -89,7 +89,7 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(const AttnParams 
   const uint32_t kvh = blockIdx.x, split = blockIdx.y;
   const uint32_t G = p.n_q / p.n_kv;
   pdl_wait();
-  const uint32_t pos = *p.pos_ptr;
+  const uint32_t pos = p.pos_ptr ? *p.pos_ptr : p.pos_value;
   if (pos >= p.max_tokens) {
     if (tid == 0 && split == 0 && kvh == 0) atomicOr(p.status, ZDEV_ERR_BOUNDS);
     return;

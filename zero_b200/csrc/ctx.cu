@@ -105,6 +105,8 @@ void zgpu_destroy(zgpu_ctx *ctx) {
   zgpu_clear_weights(ctx);
   cudaFree(ctx->d_x);
   cudaFree(ctx->d_y);
+  cudaFree(ctx->d_attn_part);
+  cudaFree(ctx->d_attn_counters);
   cudaFree(ctx->d_status);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
@@ -411,6 +413,130 @@ zgpu_status zgpu_linear_q8act(zgpu_ctx *ctx, const void *xq_blocks, const void *
   ZCHECK(cudaMemcpyAsync(out, ctx->d_y, out_dim * 4, cudaMemcpyDeviceToHost, ctx->stream), "d2h");
   ZCHECK(cudaStreamSynchronize(ctx->stream), "sync");
   return ZGPU_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Single-layer GQA decode attention (steps 2-5 of
+// gqa_attention_single_token_dispatch, crates/zero-llm-inference/src/
+// attention.rs:344-425): per-head QK RMSNorm, RoPE at `pos`, store_kv, then
+// softmax(q.k / sqrt(hd)) . V over tokens 0..pos.
+// ---------------------------------------------------------------------------
+
+// Argument checks shared by both attention entry points; the error codes are
+// the ones the reference's KvCache / attention paths return.
+static zgpu_status attention_check(zgpu_ctx *ctx, const zgpu_kv *kv, uint32_t layer, uint32_t pos,
+                                   uint32_t n_q) {
+  if (kv->ctx != ctx) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "attention: kv cache belongs to another context");
+  if (layer >= kv->n_layers) return zgpu_fail(ctx, ZGPU_ERR_KV_LAYER_OUT_OF_RANGE, "attention: layer out of range");
+  if (pos >= kv->max_tokens)
+    return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "attention: position outside the kv cache");
+  if (kv->head_dim != 128)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "attention: decode kernel requires head_dim 128");
+  if (n_q == 0 || n_q % kv->n_kv != 0 || n_q / kv->n_kv > 4)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "attention: n_q_heads must be 1..4 x n_kv_heads");
+  return ZGPU_OK;
+}
+
+// Grow the context's split partials [n_q][splits][hd + 2] and per-kv-head
+// arrival counters.  Counters start at zero; the kernel's merging CTA resets
+// its counter, so they stay zero between launches.
+static zgpu_status ensure_attn_scratch(zgpu_ctx *ctx, size_t part_floats, uint32_t n_counters) {
+  if (part_floats > ctx->d_attn_part_cap) {
+    cudaFree(ctx->d_attn_part);
+    ctx->d_attn_part = nullptr;
+    ctx->d_attn_part_cap = 0;
+    ZCHECK(cudaMalloc(&ctx->d_attn_part, part_floats * sizeof(float)), "cudaMalloc(attention partials)");
+    ctx->d_attn_part_cap = part_floats;
+  }
+  if (n_counters > ctx->d_attn_counters_cap) {
+    cudaFree(ctx->d_attn_counters);
+    ctx->d_attn_counters = nullptr;
+    ctx->d_attn_counters_cap = 0;
+    ZCHECK(cudaMalloc(&ctx->d_attn_counters, n_counters * sizeof(uint32_t)), "cudaMalloc(attention counters)");
+    ZCHECK(cudaMemset(ctx->d_attn_counters, 0, n_counters * sizeof(uint32_t)), "zero attention counters");
+    ctx->d_attn_counters_cap = n_counters;
+  }
+  return ZGPU_OK;
+}
+
+static zgpu_status attention_device(zgpu_ctx *ctx, zgpu_kv *kv, uint32_t layer, uint32_t pos,
+                                    uint32_t n_q, const float *d_qkv, const float *d_q_norm,
+                                    const float *d_k_norm, const float *d_inv_freqs, float eps,
+                                    float *d_out, cudaStream_t stream) {
+  const uint32_t splits = zgpu::attention_max_splits(kv->max_tokens);
+  zgpu_status s = ensure_attn_scratch(ctx, static_cast<size_t>(n_q) * splits * (kv->head_dim + 2), kv->n_kv);
+  if (s) return s;
+  zgpu::AttnParams ap = {};
+  ap.qkv = d_qkv;
+  ap.q_norm = d_q_norm;
+  ap.k_norm = d_k_norm;
+  ap.inv_freqs = d_inv_freqs;
+  ap.kv_layer = kv->d + static_cast<size_t>(layer) * 2 * kv->block;
+  ap.kv_block = kv->block;
+  ap.max_tokens = kv->max_tokens;
+  ap.pos_ptr = nullptr;
+  ap.pos_value = pos;
+  ap.out = d_out;
+  ap.part = ctx->d_attn_part;
+  ap.counters = ctx->d_attn_counters;
+  ap.status = ctx->d_status;
+  ap.n_q = n_q;
+  ap.n_kv = kv->n_kv;
+  ap.max_splits = splits;
+  ap.eps = eps;
+  ap.scale = 1.0f / sqrtf(static_cast<float>(kv->head_dim));
+  zgpu::LaunchCfg lc;
+  lc.stream = stream;
+  lc.sm_count = ctx->sm_count;
+  lc.launch_counter = &ctx->launches;
+  ZCHECK(zgpu::launch_attention(ap, lc), "launch_attention");
+  return ZGPU_OK;
+}
+
+extern "C" {
+
+zgpu_status zgpu_gqa_attention_decode_device(zgpu_ctx *ctx, zgpu_kv *kv, uint32_t layer,
+                                             uint32_t pos, uint32_t n_q_heads, const float *d_qkv,
+                                             const float *d_q_norm, const float *d_k_norm,
+                                             const float *d_inv_freqs, float eps, float *d_out,
+                                             void *stream) {
+  if (!ctx || !kv || !d_qkv || !d_q_norm || !d_k_norm || !d_inv_freqs || !d_out)
+    return ZGPU_ERR_INVALID_ARG;
+  zgpu_status s = attention_check(ctx, kv, layer, pos, n_q_heads);
+  if (s) return s;
+  cudaSetDevice(ctx->device);
+  return attention_device(ctx, kv, layer, pos, n_q_heads, d_qkv, d_q_norm, d_k_norm, d_inv_freqs,
+                          eps, d_out, stream ? static_cast<cudaStream_t>(stream) : ctx->stream);
+}
+
+zgpu_status zgpu_gqa_attention_decode(zgpu_ctx *ctx, zgpu_kv *kv, uint32_t layer, uint32_t pos,
+                                      uint32_t n_q_heads, const float *qkv, const float *q_norm,
+                                      const float *k_norm, float freq_base, float eps, float *out) {
+  if (!ctx || !kv || !qkv || !q_norm || !k_norm || !out) return ZGPU_ERR_INVALID_ARG;
+  zgpu_status s = attention_check(ctx, kv, layer, pos, n_q_heads);
+  if (s) return s;
+  cudaSetDevice(ctx->device);
+  const uint32_t hd = kv->head_dim, half = hd / 2;
+  // RopeContext::new (ops.rs:79-93): powf(base, -2*i / head_dim) in f32.
+  std::vector<float> inv(half);
+  for (uint32_t i = 0; i < half; ++i)
+    inv[i] = powf(freq_base, -2.0f * static_cast<float>(i) / static_cast<float>(hd));
+  const size_t nqkv = static_cast<size_t>(n_q_heads + 2 * kv->n_kv) * hd;
+  const size_t nout = static_cast<size_t>(n_q_heads) * hd;
+  s = ensure_scratch(ctx, nqkv + 2 * hd + half, nout);
+  if (s) return s;
+  float *d_qkv = ctx->d_x, *d_qn = d_qkv + nqkv, *d_kn = d_qn + hd, *d_inv = d_kn + hd;
+  ZCHECK(cudaMemcpyAsync(d_qkv, qkv, nqkv * 4, cudaMemcpyHostToDevice, ctx->stream), "h2d qkv");
+  ZCHECK(cudaMemcpyAsync(d_qn, q_norm, hd * 4, cudaMemcpyHostToDevice, ctx->stream), "h2d q_norm");
+  ZCHECK(cudaMemcpyAsync(d_kn, k_norm, hd * 4, cudaMemcpyHostToDevice, ctx->stream), "h2d k_norm");
+  ZCHECK(cudaMemcpyAsync(d_inv, inv.data(), half * 4, cudaMemcpyHostToDevice, ctx->stream), "h2d rope");
+  s = attention_device(ctx, kv, layer, pos, n_q_heads, d_qkv, d_qn, d_kn, d_inv, eps, ctx->d_y,
+                       ctx->stream);
+  if (s) return s;
+  ZCHECK(cudaMemcpyAsync(out, ctx->d_y, nout * 4, cudaMemcpyDeviceToHost, ctx->stream), "d2h out");
+  return check_status_word(ctx);
 }
 
 }  // extern "C"

@@ -78,6 +78,20 @@ struct zgpu_ctx {
   size_t d_x_cap = 0, d_y_cap = 0;
   uint32_t *d_status = nullptr;
   uint32_t launches = 0;
+  // split-attention partials / arrival counters of the attention entry points
+  float *d_attn_part = nullptr;
+  size_t d_attn_part_cap = 0;
+  uint32_t *d_attn_counters = nullptr;
+  uint32_t d_attn_counters_cap = 0;
+};
+
+// KV cache: layer-major [L][K block | V block], block = max_tokens x n_kv x
+// head_dim f32, token stride n_kv*head_dim (kv_cache.rs:100-126).
+struct zgpu_kv {
+  zgpu_ctx *ctx = nullptr;
+  float *d = nullptr;
+  uint32_t max_tokens = 0, n_layers = 0, n_kv = 0, head_dim = 0;
+  uint64_t block = 0;   // max_tokens * n_kv * head_dim
 };
 
 // Record an error message on the context and return the status.

@@ -23,13 +23,6 @@
 
 using namespace zgpu;
 
-struct zgpu_kv {
-  zgpu_ctx *ctx = nullptr;
-  float *d = nullptr;
-  uint32_t max_tokens = 0, n_layers = 0, n_kv = 0, head_dim = 0;
-  uint64_t block = 0;   // max_tokens * n_kv * head_dim
-};
-
 struct zgpu_model {
   zgpu_ctx *ctx = nullptr;
   zgpu_qwen3_desc desc = {};
@@ -128,7 +121,7 @@ cudaError_t enqueue_forward(zgpu_model *m, zgpu_kv *kv, uint32_t *counter) {
     io.status = m->d_status;
     if ((e = launch_gemv(g, PRO_RMSNORM, EPI_STORE, io, lc)) != cudaSuccess) return e;
 
-    AttnParams ap;
+    AttnParams ap = {};
     ap.qkv = m->d_qkvo;
     ap.q_norm = norm_q(m, l);
     ap.k_norm = norm_k(m, l);

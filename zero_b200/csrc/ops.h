@@ -49,7 +49,8 @@ struct AttnParams {
   float *kv_layer;           // K block of this layer; V block follows at +kv_block
   uint64_t kv_block;         // max_tokens * n_kv * hd
   uint32_t max_tokens;
-  const uint32_t *pos_ptr;   // device position of the token
+  const uint32_t *pos_ptr;   // device position of the token, or null to use pos_value
+  uint32_t pos_value;
   float *out;                // [n_q*hd]
   float *part;               // [n_q][max_splits][hd + 2]
   uint32_t *counters;        // [n_kv]
