@@ -187,6 +187,27 @@ zgpu_status zgpu_gqa_attention_decode_device(zgpu_ctx *ctx, zgpu_kv *kv, uint32_
                                              const float *d_q_norm, const float *d_k_norm,
                                              const float *d_inv_freqs, float eps, float *d_out,
                                              void *stream);
+/* Has no counterpart in the reference: an added variant of
+ * zgpu_gqa_attention_decode_device (same arguments, same results) for callers
+ * that must not allocate device memory while they run.  Examples are hosts
+ * that reserve all device memory up front and hand out fixed buffers,
+ * per-token loops where an allocation could synchronise the device, and
+ * plugins whose memory belongs to another allocator.  The call allocates
+ * nothing.  Its split partials and counters live in a 1 MiB array built into
+ * the library's device image, which every GPU that loads the library keeps
+ * until the process exits.  Limits: n_q_heads x ceil(max_tokens / 256) x
+ * (head_dim + 2) must be at most 261888 floats (16 q heads: caches up to
+ * 32000 tokens), and n_kv at most 256.  Larger requests return
+ * ZGPU_ERR_INVALID_ARG with a message and launch nothing.  The first call on
+ * a device looks up the array's device address, so make that first call
+ * before any stream capture.  All calls on a device share the one array, and
+ * each call clears the counters on its stream.  Calls that overlap on the GPU
+ * race, whether from other streams or other contexts on the same device. */
+zgpu_status zgpu_gqa_attention_decode_noalloc(zgpu_ctx *ctx, zgpu_kv *kv, uint32_t layer,
+                                              uint32_t pos, uint32_t n_q_heads, const float *d_qkv,
+                                              const float *d_q_norm, const float *d_k_norm,
+                                              const float *d_inv_freqs, float eps, float *d_out,
+                                              void *stream);
 
 /* ------------------------------------------------------------ Qwen3 model */
 /* One decoder layer's tensors, each a registered host key (LayerWeights,

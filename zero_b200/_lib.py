@@ -71,6 +71,8 @@ _SIGS = {
     "zgpu_gqa_attention_decode": (_i32, [_vp, _vp, _u32, _u32, _u32, _vp, _vp, _vp, _f, _f, _vp]),
     "zgpu_gqa_attention_decode_device": (_i32, [_vp, _vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _f, _vp,
                                                 _vp]),
+    "zgpu_gqa_attention_decode_noalloc": (_i32, [_vp, _vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _f, _vp,
+                                                 _vp]),
     "zgpu_qwen3_create": (_i32, [_vp, C.POINTER(ZgpuQwen3Desc), C.POINTER(_vp)]),
     "zgpu_qwen3_destroy": (None, [_vp]),
     "zgpu_forward_single_token": (_i32, [_vp, _vp, _u32, _u32, _vp]),

@@ -33,7 +33,7 @@ CXX_FLAGS = ["-O2", "-fPIC", "-std=c++17", "-Wall", "-pthread"]
 if os.environ.get("ZGPU_DEVICE_CHECKS") == "1":
     CUDA_FLAGS.append("-DZGPU_DEVICE_CHECKS")
 
-CU_SOURCES = ["gemv.cu", "attention.cu", "ops.cu", "ctx.cu", "model.cu"]
+CU_SOURCES = ["gemv.cu", "attention.cu", "attention_static.cu", "ops.cu", "ctx.cu", "model.cu"]
 CXX_SOURCES = ["synth.cpp"]
 
 
