@@ -2,10 +2,12 @@
 #include <cmath>
 #include <cstring>
 #include <new>
+#include <thread>
 #include <vector>
 
 #include "common.cuh"
 #include "internal.h"
+#include "layout.h"
 #include "ops.h"
 
 using zgpu::DeviceTensor;
@@ -163,38 +165,56 @@ zgpu_status zgpu_register_weights(zgpu_ctx *ctx, const void *host_ptr, size_t le
     t.interleave = x4 ? 4 : 1;
     // groups padded to an even count: the GEMV works on units of two groups
     t.groups = ((rows + 3) / 4 + 1) & ~uint64_t(1);
-    const uint64_t gb = bpr * bb * 4;          // bytes of one group stream
-    t.gstride = (gb + 15) & ~uint64_t(15);
+    t.gstride = zgpu::group_stream_bytes(quant, bpr);
     t.bytes = t.groups * t.gstride;
-    // Build the padded X4 image on the host, then upload once.
+    // Re-lay the tensor out as plane chunks (layout.h) on the host, then
+    // upload once.  Padded rows and groups stay zero blocks.
     std::vector<uint8_t> img;
+    try {
+      img.assign(t.bytes, 0);
+    } catch (...) {
+      return zgpu_fail(ctx, ZGPU_ERR_OUT_OF_MEMORY, "host staging allocation failed");
+    }
     const uint8_t *src = static_cast<const uint8_t *>(host_ptr);
-    if (!x4 || t.gstride != gb || t.groups * 4 != rows) {
-      try {
-        img.assign(t.bytes, 0);
-      } catch (...) {
-        return zgpu_fail(ctx, ZGPU_ERR_OUT_OF_MEMORY, "host staging allocation failed");
-      }
-      for (uint64_t g = 0; g < t.groups; ++g) {
+    const uint64_t gb = bpr * bb * 4;          // bytes of one X4 group stream
+    const uint64_t body = bb - 2;              // quant bytes of one row-block
+    const uint32_t P = zgpu::plane_count(quant);
+    auto convert = [&](uint64_t g0, uint64_t g1) {
+      for (uint64_t g = g0; g < g1; ++g) {
         uint8_t *dst = img.data() + g * t.gstride;
-        if (x4) {
-          if (g * 4 < rows) std::memcpy(dst, src + g * gb, gb);
-          continue;
-        }
-        for (uint64_t b = 0; b < bpr; ++b) {
-          uint8_t *gbk = dst + b * bb * 4;
-          for (uint64_t l = 0; l < 4; ++l) {
-            const uint64_t r = g * 4 + l;
-            if (r >= rows) continue;  // padded rows / groups stay zero blocks
-            const uint8_t *blk = src + (r * bpr + b) * bb;
-            gbk[2 * l] = blk[0];
-            gbk[2 * l + 1] = blk[1];
-            std::memcpy(gbk + 8 + l * (bb - 2), blk + 2, bb - 2);
+        for (uint64_t l = 0; l < 4; ++l) {
+          const uint64_t r = g * 4 + l;
+          if (r >= rows) break;
+          for (uint64_t b = 0; b < bpr; ++b) {
+            const uint8_t *d16, *q;
+            if (x4) {
+              const uint8_t *gbk = src + g * gb + b * bb * 4;   // [d0..d3][row0..row3 bodies]
+              d16 = gbk + 2 * l;
+              q = gbk + 8 + l * body;
+            } else {
+              const uint8_t *blk = src + (r * bpr + b) * bb;    // [d][body]
+              d16 = blk;
+              q = blk + 2;
+            }
+            std::memcpy(dst + zgpu::scale_entry(quant, bpr, b) + 2 * l, d16, 2);
+            const uint32_t per_row = P / 4;                     // planes per row
+            for (uint32_t h = 0; h < per_row; ++h)
+              std::memcpy(dst + zgpu::plane_entry(quant, bpr, b, static_cast<uint32_t>(l) * per_row + h),
+                          q + 16 * h, 16);
           }
         }
       }
-      src = img.data();
+    };
+    const uint64_t ng = (rows + 3) / 4;
+    const unsigned nt = ng >= 256 ? 8u : 1u;
+    if (nt == 1) {
+      convert(0, ng);
+    } else {
+      std::vector<std::thread> pool;
+      for (unsigned i = 0; i < nt; ++i) pool.emplace_back(convert, ng * i / nt, ng * (i + 1) / nt);
+      for (auto &th : pool) th.join();
     }
+    src = img.data();
     ZCHECK(cudaMalloc(&t.d, t.bytes), "cudaMalloc(weights)");
     ZCHECK(cudaMemcpy(t.d, src, t.bytes, cudaMemcpyHostToDevice), "upload");
   }

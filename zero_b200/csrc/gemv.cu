@@ -12,12 +12,16 @@
 // the 8 rows.  CTA c owns a contiguous range of units and all their chunks.
 //
 // Data path (2 CTAs per SM):
-//   * prologue: the consumer threads build the activation vector once per CTA
-//     in shared memory — RMSNorm applied (PRO_RMSNORM, fixed-order sum of
-//     squares identical in every CTA), and for Q4_0 each element pre-scaled by
-//     2^-c for its nibble's bit class c, laid out in the float2 pairs the
-//     inner loop consumes, 16-byte chunks XOR-swizzled by block so that lanes
-//     reading different blocks hit different banks;
+//   * prologue: the consumer threads build the activation image once per CTA
+//     in shared memory.  Each 32-element block of x (RMSNorm applied for
+//     PRO_RMSNORM, with a fixed-order sum of squares identical in every CTA)
+//     becomes integers N_i = rint(x_i * 2^-E) with 2^E a power of two that
+//     puts the block maximum in [2^22, 2^23); the three bytes of each N_i
+//     (two unsigned, the top one signed) are stored as packed int8 digit
+//     words, with the block scale 2^E and, for Q4_0, the per-digit offset
+//     -8 * sum_i byte_i that removes the nibble bias.  16-byte chunks are
+//     XOR-swizzled by block so that lanes reading different blocks hit
+//     different banks;
 //   * consumer warp w takes items w, w+8, ... of the CTA; it owns ring slots
 //     [w*S, (w+1)*S), fed by lane w of the producer warp with two 1-D TMA bulk
 //     copies per item (the chunk of each group stream; cp.async.bulk, L2
@@ -25,11 +29,11 @@
 //     every slot's mbarrier phases strictly in order.  The producer starts
 //     before the programmatic-dependent-launch wait, so weights stream while
 //     the previous kernel finishes;
-//   * each lane dequantises its block for the 8 rows in registers: Q4_0
-//     nibbles become exact floats through the 2^23 exponent trick (nibble bits
-//     OR'd into the mantissa of 2^23, one packed f32x2 subtract removes 2^23),
-//     accumulated with packed f32x2 FMAs; d*(sum - 8*sum x) per block; Q8_0
-//     bytes take the same trick after a byte permute;
+//   * each lane takes one block of the item's 8 rows: per row one 16-byte
+//     plane load (two for Q8_0), three dp4a chains (one per digit, exact
+//     int32), then t = (s0 + 256 s1) + 65536 s2 and acc = (d * 2^E) * t.  The
+//     digit image carries x to 2^-23 of its block maximum, so a row's error
+//     stays a few 1e-7 of sum |x w|, like a reordered f32 sum;
 //   * a warp reduce-scatter leaves the item's 8 row sums in lanes 4r, which
 //     store them to shared memory; after all items the K-chunks of each row
 //     are added in chunk order and the epilogue stores / adds the residual /
@@ -40,6 +44,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "layout.h"
 
 namespace zgpu {
 
@@ -49,9 +54,6 @@ constexpr int kWarps = 8;                      // consumer warps per CTA
 constexpr int kThreads = 32 * (kWarps + 1);
 constexpr int kConsumers = 32 * kWarps;
 constexpr int kRows = 8;                       // output rows per unit
-constexpr uint32_t kChunkBlocks = 32;          // blocks per K-chunk (one per lane)
-constexpr uint32_t kMagic = 0x4B000000u;       // 2^23 as f32 bits
-constexpr float kTwo23 = 8388608.0f;
 constexpr size_t kSmemBudget = 110 * 1024;     // two CTAs per SM
 constexpr int kCtasPerSm = 2;
 constexpr uint32_t kMaxSlotsPerWarp = 4;
@@ -79,25 +81,37 @@ struct KParams {
   uint32_t *status;
 };
 
-// Position of activation element e (0..31) of a block inside its 32-float
-// shared-memory image, and the power-of-two scale it carries (Q4_0 only).
-// Pair 4m+p holds (x[4m+p] * s_lo(p), x[4m+16+p] * s_hi(p)) — the order in
-// which q4_dot consumes the nibbles of qs word m.
-__device__ __forceinline__ uint32_t q4_slot(uint32_t e) {
-  const uint32_t hi = e >> 4, m = (e & 15) >> 2, p = e & 3;
-  return 2 * (4 * m + p) + hi;
+// Activation image: 32 words per block, in 16-byte chunks
+//   0-1: digit-0 words, 2-3: digit-1 words, 4-5: digit-2 words,
+//   6: (offset0, offset1, offset2, 2^E as f32 bits), 7: unused;
+// digit word k packs the digit bytes of elements 4k..4k+3 (for Q4_0 words
+// 0-3 meet the low nibbles of qs word k, words 4-7 the high nibbles of qs
+// word k-4; for Q8_0 word k meets qs word k).  Chunk c of block b sits at
+// chunk position c ^ (b & 7).
+__device__ __forceinline__ uint32_t x_word(uint32_t b, uint32_t chunk, uint32_t w) {
+  return b * 32 + ((chunk ^ (b & 7)) << 2) + w;
 }
-__device__ __forceinline__ float q4_scale(uint32_t e) {
-  // bit class of the nibble as q4_dot isolates it: low nibbles of bytes
-  // 0..3 sit at bits 0, 8, 16 and (after >>12) 12; high nibbles at 4, 12
-  // (bits 12-15), 8 (bits 20-23 >> 12) and 16 (bits 28-31 >> 12).
-  const uint32_t p = e & 3;
-  if (e < 16) return p == 0 ? 1.0f : p == 1 ? 0.00390625f : p == 2 ? 1.52587890625e-05f : 0.000244140625f;
-  return p == 0 ? 0.0625f : p == 1 ? 0.000244140625f : p == 2 ? 0.00390625f : 1.52587890625e-05f;
+
+// dp4a with the byte signedness of each operand (PTX dp4a.atype.btype).
+__device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
 }
-// Float offset of slot s (0..31) of block b in the swizzled image.
-__device__ __forceinline__ uint32_t x_off(uint32_t b, uint32_t s) {
-  return b * 32 + ((((s >> 2) ^ (b & 7)) << 2) | (s & 3));
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
 }
 
 template <int R>
@@ -121,49 +135,41 @@ __device__ __forceinline__ float reduce_scatter(float (&v)[R], uint32_t lane) {
   return v[0];
 }
 
-// sum_j x_j * n_j of one Q4_0 row-block, x pre-scaled per bit class.
-__device__ __forceinline__ float q4_dot(const uint32_t (&q)[4], const float2 (&xs)[16]) {
-  const float2 bias = make_float2(-kTwo23, -kTwo23);
-  float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+// sum_j (n_j - 8) * N_j of one Q4_0 row-block from its 16 nibble bytes: the
+// digit offsets start each chain at -8 * sum_j digit_j.
+__device__ __forceinline__ float q4_dot(const uint4 q, const uint32_t (&D)[3][8], const int (&I)[3]) {
+  int s0 = I[0], s1 = I[1], s2 = I[2];
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
   for (int m = 0; m < 4; ++m) {
-    const uint32_t w = q[m], w12 = w >> 12;
-    float2 f0 = make_float2(__uint_as_float((w & 0x0000000Fu) | kMagic),
-                            __uint_as_float((w & 0x000000F0u) | kMagic));
-    float2 f1 = make_float2(__uint_as_float((w & 0x00000F00u) | kMagic),
-                            __uint_as_float((w & 0x0000F000u) | kMagic));
-    float2 f2 = make_float2(__uint_as_float((w & 0x000F0000u) | kMagic),
-                            __uint_as_float((w12 & 0x00000F00u) | kMagic));
-    float2 f3 = make_float2(__uint_as_float((w12 & 0x0000F000u) | kMagic),
-                            __uint_as_float((w12 & 0x000F0000u) | kMagic));
-    acc0 = __ffma2_rn(xs[4 * m + 0], __fadd2_rn(f0, bias), acc0);
-    acc1 = __ffma2_rn(xs[4 * m + 1], __fadd2_rn(f1, bias), acc1);
-    acc0 = __ffma2_rn(xs[4 * m + 2], __fadd2_rn(f2, bias), acc0);
-    acc1 = __ffma2_rn(xs[4 * m + 3], __fadd2_rn(f3, bias), acc1);
+    const uint32_t lo = w[m] & 0x0F0F0F0Fu, hi = (w[m] >> 4) & 0x0F0F0F0Fu;
+    s0 = dp4a_uu(lo, D[0][m], s0);
+    s1 = dp4a_uu(lo, D[1][m], s1);
+    s2 = dp4a_us(lo, D[2][m], s2);
+    s0 = dp4a_uu(hi, D[0][m + 4], s0);
+    s1 = dp4a_uu(hi, D[1][m + 4], s1);
+    s2 = dp4a_us(hi, D[2][m + 4], s2);
   }
-  return (acc0.x + acc0.y) + (acc1.x + acc1.y);
+  // |s0 + 256 s1| < 2^24: exact in int32 and in f32
+  return fmaf(static_cast<float>(s2), 65536.0f, static_cast<float>(s0 + (s1 << 8)));
 }
 
-// sum_j x_j * q_j of one Q8_0 row-block.
-__device__ __forceinline__ float q8_dot(const uint32_t (&q)[8], const float2 (&xp)[16]) {
-  const float2 bias = make_float2(-(kTwo23 + 128.f), -(kTwo23 + 128.f));
-  float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+// sum_j q_j * N_j of one Q8_0 row-block from its two 16-byte halves.
+__device__ __forceinline__ float q8_dot(const uint4 qa, const uint4 qb, const uint32_t (&D)[3][8]) {
+  int s0 = 0, s1 = 0, s2 = 0;
+  const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    const uint32_t w = q[k] ^ 0x80808080u;   // i8 -> u8 + 128
-    float2 f0 = make_float2(__uint_as_float(__byte_perm(w, kMagic, 0x7540)),
-                            __uint_as_float(__byte_perm(w, kMagic, 0x7541)));
-    float2 f1 = make_float2(__uint_as_float(__byte_perm(w, kMagic, 0x7542)),
-                            __uint_as_float(__byte_perm(w, kMagic, 0x7543)));
-    acc0 = __ffma2_rn(xp[2 * k + 0], __fadd2_rn(f0, bias), acc0);
-    acc1 = __ffma2_rn(xp[2 * k + 1], __fadd2_rn(f1, bias), acc1);
+    s0 = dp4a_su(w[k], D[0][k], s0);
+    s1 = dp4a_su(w[k], D[1][k], s1);
+    s2 = dp4a_ss(w[k], D[2][k], s2);
   }
-  return (acc0.x + acc0.y) + (acc1.x + acc1.y);
+  return fmaf(static_cast<float>(s2), 65536.0f, static_cast<float>(s0 + (s1 << 8)));
 }
 
 template <int QT, int PRO, int EPI>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KParams p) {
-  constexpr uint32_t GB = (QT == ZGPU_Q4_0) ? 72 : 136;
+  constexpr uint32_t P = (QT == ZGPU_Q4_0) ? 4 : 8;   // planes per chunk (layout.h)
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float red[kWarps];
   __shared__ unsigned long long best_w[kWarps];
@@ -171,8 +177,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t S = p.spw;
   const uint32_t slot_bytes = 2 * p.half_bytes;
-  float *xsm = reinterpret_cast<float *>(smem);                       // bpr * 32 floats
-  float *x8 = reinterpret_cast<float *>(smem + static_cast<size_t>(p.bpr) * 128);
+  uint32_t *xsm = reinterpret_cast<uint32_t *>(smem);                 // bpr * 32 words
   float *part = reinterpret_cast<float *>(smem + p.xbytes);           // [items][8]
   uint8_t *ring = smem + p.ring_off;
   uint64_t *full = reinterpret_cast<uint64_t *>(ring + static_cast<size_t>(kWarps) * S * slot_bytes);
@@ -202,9 +207,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
         const uint32_t slot = lane * S + (j % S);
         if (j >= S && !mbar_wait(smem_addr(&empty[slot]), ((j / S) - 1) & 1, p.status)) break;
         const uint32_t unit = u0 + k / p.ks, chunk = k % p.ks;
-        const uint32_t nb = min(kChunkBlocks, p.bpr - chunk * kChunkBlocks);
-        const uint32_t bytes = (nb * GB + 15) & ~15u;
-        const uint64_t src = (2ull * unit) * p.gstride + static_cast<uint64_t>(chunk) * kChunkBlocks * GB;
+        const uint32_t bytes = static_cast<uint32_t>(chunk_bytes(QT, chunk_blocks(p.bpr, chunk)));
+        const uint64_t src = (2ull * unit) * p.gstride + chunk_offset(QT, chunk);
         if (!ZDEV_CHECK(src + p.gstride + bytes <= p.wbytes && bytes <= p.half_bytes, p.status, 1,
                         unit, chunk))
           break;
@@ -264,26 +268,55 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
       t.z = __fmul_rn(__fmul_rn(t.z, inv), g.z);
       t.w = __fmul_rn(__fmul_rn(t.w, inv), g.w);
     }
-    const uint32_t b = f >> 3, e0 = (f & 7) * 4;
+    const uint32_t b = f >> 3, k4 = f & 7;
     // a failed check only suppresses the writes: every lane still reaches the
     // shuffles below
     const bool in_range =
-        valid && ZDEV_CHECK(b < p.bpr && b * 132 + 132 <= p.xbytes, p.status, 3, b, p.xbytes);
-    const float v[4] = {t.x, t.y, t.z, t.w};
+        valid && ZDEV_CHECK(b < p.bpr && b * 128 + 128 <= p.xbytes, p.status, 3, b, p.xbytes);
+    // block maximum and non-finite flag over the block's 8 lanes
+    float am = fmaxf(fmaxf(fabsf(t.x), fabsf(t.y)), fmaxf(fabsf(t.z), fabsf(t.w)));
+    uint32_t bad = (fabsf(t.x) <= FLT_MAX && fabsf(t.y) <= FLT_MAX && fabsf(t.z) <= FLT_MAX &&
+                    fabsf(t.w) <= FLT_MAX) ? 0u : 1u;
+#pragma unroll
+    for (int off = 1; off < 8; off <<= 1) {
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+      bad |= __shfl_xor_sync(0xffffffffu, bad, off);
+    }
+    int n[4] = {0, 0, 0, 0};
+    float bscale = 0.0f;                              // all-zero (or negligible) block
+    if (bad) {
+      bscale = __uint_as_float(0x7fc00000u);          // NaN: the rows' sums become NaN
+    } else if (am >= 7.888609052e-31f) {              // 2^-100
+      const int e = static_cast<int>(__float_as_uint(am) >> 23) - 127;   // am in [2^e, 2^(e+1))
+      const float up = __uint_as_float(static_cast<uint32_t>(149 - e) << 23);   // 2^(22-e)
+      bscale = __uint_as_float(static_cast<uint32_t>(105 + e) << 23);          // 2^(e-22)
+      const float v[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) n[k] = min(__float2int_rn(v[k] * up), 0x7FFFFF);
+    }
+    const uint32_t w0 = __byte_perm(__byte_perm(n[0], n[1], 0x0040), __byte_perm(n[2], n[3], 0x0040), 0x5410);
+    const uint32_t w1 = __byte_perm(__byte_perm(n[0], n[1], 0x0051), __byte_perm(n[2], n[3], 0x0051), 0x5410);
+    const uint32_t w2 = __byte_perm(__byte_perm(n[0], n[1], 0x0062), __byte_perm(n[2], n[3], 0x0062), 0x5410);
+    int ds[3] = {0, 0, 0};
     if (QT == ZGPU_Q4_0) {
-      if (in_range) {
+      ds[0] = dp4a_uu(w0, 0x01010101u, 0);
+      ds[1] = dp4a_uu(w1, 0x01010101u, 0);
+      ds[2] = dp4a_us(0x01010101u, w2, 0);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) xsm[x_off(b, q4_slot(e0 + k))] = v[k] * q4_scale(e0 + k);
+      for (int off = 1; off < 8; off <<= 1)
+#pragma unroll
+        for (int d = 0; d < 3; ++d) ds[d] += __shfl_xor_sync(0xffffffffu, ds[d], off);
+    }
+    if (in_range) {
+      xsm[x_word(b, 0 + (k4 >> 2), k4 & 3)] = w0;
+      xsm[x_word(b, 2 + (k4 >> 2), k4 & 3)] = w1;
+      xsm[x_word(b, 4 + (k4 >> 2), k4 & 3)] = w2;
+      if (k4 == 0) {
+        xsm[x_word(b, 6, 0)] = static_cast<uint32_t>(-8 * ds[0]);
+        xsm[x_word(b, 6, 1)] = static_cast<uint32_t>(-8 * ds[1]);
+        xsm[x_word(b, 6, 2)] = static_cast<uint32_t>(-8 * ds[2]);
+        xsm[x_word(b, 6, 3)] = __float_as_uint(bscale);
       }
-      // 8 * sum of the block's 32 activations, fixed tree over its 8 lanes.
-      float s = (v[0] + v[1]) + (v[2] + v[3]);
-      s += __shfl_xor_sync(0xffffffffu, s, 1);
-      s += __shfl_xor_sync(0xffffffffu, s, 2);
-      s += __shfl_xor_sync(0xffffffffu, s, 4);
-      if (in_range && (f & 7) == 0) x8[b] = 8.0f * s;
-    } else if (in_range) {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) xsm[x_off(b, e0 + k)] = v[k];
     }
   }
   named_bar_sync(1, kConsumers);
@@ -300,41 +333,37 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
     for (int r = 0; r < kRows; ++r) acc[r] = 0.f;
     if (!failed && b < p.bpr) {
       const uint8_t *sbase = ring + static_cast<size_t>(slot) * slot_bytes;
-      float2 xs[16];
-      const float4 *xb = reinterpret_cast<const float4 *>(xsm + b * 32);
+      const uint32_t nb = chunk_blocks(p.bpr, chunk);
+      const uint4 *xb = reinterpret_cast<const uint4 *>(xsm + b * 32);
+      const uint32_t sw = b & 7;
+      uint32_t D[3][8];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const float4 t = xb[c ^ (b & 7)];
-        xs[2 * c] = make_float2(t.x, t.y);
-        xs[2 * c + 1] = make_float2(t.z, t.w);
+      for (int c = 0; c < 6; ++c) {
+        const uint4 v = xb[c ^ sw];
+        D[c >> 1][4 * (c & 1) + 0] = v.x;
+        D[c >> 1][4 * (c & 1) + 1] = v.y;
+        D[c >> 1][4 * (c & 1) + 2] = v.z;
+        D[c >> 1][4 * (c & 1) + 3] = v.w;
       }
-      const float xb8 = (QT == ZGPU_Q4_0) ? x8[b] : 0.f;
+      const uint4 meta = xb[6 ^ sw];
+      const int I[3] = {static_cast<int>(meta.x), static_cast<int>(meta.y), static_cast<int>(meta.z)};
+      const float bscale = __uint_as_float(meta.w);
 #pragma unroll
       for (int g = 0; g < 2; ++g) {
-        const uint8_t *blk = sbase + g * p.half_bytes + lane * GB;
-        const uint2 sc = *reinterpret_cast<const uint2 *>(blk);
+        const uint8_t *cb = sbase + g * p.half_bytes;
+        const uint2 sc = *reinterpret_cast<const uint2 *>(cb + P * nb * 16 + lane * 8);
         const float d[4] = {h2f(sc.x & 0xFFFF), h2f(sc.x >> 16), h2f(sc.y & 0xFFFF),
                             h2f(sc.y >> 16)};
-        if (QT == ZGPU_Q4_0) {
 #pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const uint2 a = *reinterpret_cast<const uint2 *>(blk + 8 + 16 * r);
-            const uint2 c = *reinterpret_cast<const uint2 *>(blk + 16 + 16 * r);
-            const uint32_t q[4] = {a.x, a.y, c.x, c.y};
-            acc[4 * g + r] = d[r] * (q4_dot(q, xs) - xb8);
+        for (int r = 0; r < 4; ++r) {
+          float t;
+          if (QT == ZGPU_Q4_0) {
+            t = q4_dot(*reinterpret_cast<const uint4 *>(cb + r * nb * 16 + lane * 16), D, I);
+          } else {
+            t = q8_dot(*reinterpret_cast<const uint4 *>(cb + (2 * r) * nb * 16 + lane * 16),
+                       *reinterpret_cast<const uint4 *>(cb + (2 * r + 1) * nb * 16 + lane * 16), D);
           }
-        } else {
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            uint32_t q[8];
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint2 a = *reinterpret_cast<const uint2 *>(blk + 8 + 32 * r + 8 * kk);
-              q[2 * kk] = a.x;
-              q[2 * kk + 1] = a.y;
-            }
-            acc[4 * g + r] = d[r] * q8_dot(q, xs);
-          }
+          acc[4 * g + r] = __fmul_rn(d[r], bscale) * t;
         }
       }
     }
@@ -463,7 +492,6 @@ cudaError_t launch_gemv(const GemvDesc &g, GemvPro pro, GemvEpi epi, const GemvI
     return cudaErrorInvalidValue;
   if (g.gstride % 16 != 0) return cudaErrorInvalidValue;
   if (epi == EPI_SWIGLU && g.quant != ZGPU_Q4_0) return cudaErrorInvalidValue;
-  const uint32_t GB = g.quant == ZGPU_Q4_0 ? 72 : 136;
   KParams kp = {};
   kp.w = g.w;
   kp.gstride = g.gstride;
@@ -476,10 +504,10 @@ cudaError_t launch_gemv(const GemvDesc &g, GemvPro pro, GemvEpi epi, const GemvI
   const uint32_t ctas = static_cast<uint32_t>((lc.sm_count > 0 ? lc.sm_count : 148) * kCtasPerSm);
   kp.units_per_cta = (kp.units + ctas - 1) / ctas;
   const uint32_t grid = (kp.units + kp.units_per_cta - 1) / kp.units_per_cta;
-  kp.half_bytes = (min(kChunkBlocks, kp.bpr) * GB + 15) & ~15u;
+  kp.half_bytes = static_cast<uint32_t>(chunk_bytes(g.quant, min(kChunkBlocks, kp.bpr)));
   const size_t slot = 2 * static_cast<size_t>(kp.half_bytes);
-  // activation image (128 B per block) + 8*sum per block, rounded to 128 B
-  kp.xbytes = static_cast<uint32_t>((static_cast<size_t>(kp.bpr) * 132 + 127) & ~size_t(127));
+  // activation image: 128 B per block
+  kp.xbytes = static_cast<uint32_t>(static_cast<size_t>(kp.bpr) * 128);
   const size_t part_bytes =
       (static_cast<size_t>(kp.units_per_cta) * kp.ks * kRows * sizeof(float) + 127) & ~size_t(127);
   kp.ring_off = static_cast<uint32_t>(kp.xbytes + part_bytes);

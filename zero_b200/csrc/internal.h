@@ -13,11 +13,9 @@
 namespace zgpu {
 
 // Device copy of one registered tensor.  Matmul tensors are always held in
-// the 4-row-interleaved group layout (X4) on the device, whatever layout the
-// caller registered: group g of 4 output rows is one contiguous stream of
-// bpr group-blocks (72 B for Q4_0, 136 B for Q8_0: the four fp16 scales then
-// the four rows' quant bodies, tools/silicatepack.py:982-1022), padded to a
-// multiple of 16 bytes so every group starts on a TMA-legal boundary.
+// the plane-chunk group layout of layout.h on the device, whatever layout the
+// caller registered (plain rows or the .smodel-v2 X4 groups): group g of 4
+// output rows is one contiguous stream of gstride bytes (a multiple of 16).
 struct DeviceTensor {
   uint8_t *d = nullptr;       // device bytes
   size_t bytes = 0;
@@ -29,7 +27,7 @@ struct DeviceTensor {
   uint64_t gstride = 0;       // bytes per group stream on the device
 };
 
-// Geometry of one GEMV launch over an X4 device tensor.
+// Geometry of one GEMV launch over a device tensor in the layout.h format.
 struct GemvDesc {
   const uint8_t *w;           // group streams
   uint64_t gstride;           // bytes between groups

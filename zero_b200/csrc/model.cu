@@ -27,7 +27,7 @@ struct zgpu_model {
   zgpu_ctx *ctx = nullptr;
   zgpu_qwen3_desc desc = {};
   uint32_t q_dim = 0, kv_dim = 0;
-  // weights (X4 group streams on the device)
+  // weights (group streams in the layout.h format on the device)
   std::vector<uint8_t *> qkv;       // owned: q|k|v groups concatenated
   std::vector<uint8_t *> gateup;    // owned: gate/up groups interleaved
   std::vector<const DeviceTensor *> o, down;

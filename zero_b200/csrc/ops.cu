@@ -4,6 +4,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "layout.h"
 #include "ops.h"
 
 namespace zgpu {
@@ -11,8 +12,8 @@ namespace zgpu {
 namespace {
 
 // embed_lookup_dispatch (crates/zero-llm-inference/src/forward_pass.rs:311-370):
-// dequantise one embedding row.  The table lives on the device in the X4
-// group layout, so row r is lane r%4 of group r/4.  Also selects the step's
+// dequantise one embedding row.  The table lives on the device in the group
+// layout of layout.h, so row r is row r%4 of group r/4.  Also selects the step's
 // token (prompt id or the previous step's argmax) and publishes position.
 __global__ void embed_kernel(const EmbedParams p) {
   pdl_launch_dependents();
@@ -28,21 +29,20 @@ __global__ void embed_kernel(const EmbedParams p) {
     st->token = token;
     st->pos = st->pos_base + step;
   }
-  const uint32_t g = token >> 2, lane = token & 3;
+  const uint32_t g = token >> 2, l = token & 3;
   if (!ZDEV_CHECK(g < (p.vocab + 3) / 4, p.status, 20, token, p.vocab)) return;
   const uint8_t *grp = p.emb + static_cast<uint64_t>(g) * p.gstride;
+  const uint32_t bpr = p.hidden / 32;
   for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < p.hidden;
        e += gridDim.x * blockDim.x) {
     const uint32_t b = e >> 5, j = e & 31;
+    const uint8_t *sc = grp + scale_entry(p.quant, bpr, b) + 2 * l;
+    const float d = h2f(static_cast<uint16_t>(sc[0] | (sc[1] << 8)));
     if (p.quant == ZGPU_Q8_0) {
-      const uint8_t *blk = grp + static_cast<uint64_t>(b) * 136;
-      const float d = h2f(static_cast<uint16_t>(blk[2 * lane] | (blk[2 * lane + 1] << 8)));
-      const int8_t q = static_cast<int8_t>(blk[8 + 32 * lane + j]);
+      const int8_t q = static_cast<int8_t>(grp[plane_entry(p.quant, bpr, b, 2 * l + (j >> 4)) + (j & 15)]);
       p.hidden_out[e] = __fmul_rn(static_cast<float>(q), d);
     } else {
-      const uint8_t *blk = grp + static_cast<uint64_t>(b) * 72;
-      const float d = h2f(static_cast<uint16_t>(blk[2 * lane] | (blk[2 * lane + 1] << 8)));
-      const uint8_t byte = blk[8 + 16 * lane + (j & 15)];
+      const uint8_t byte = grp[plane_entry(p.quant, bpr, b, l) + (j & 15)];
       const int n = (j < 16) ? (byte & 0x0F) : (byte >> 4);
       p.hidden_out[e] = __fmul_rn(static_cast<float>(n - 8), d);
     }
@@ -176,8 +176,8 @@ __global__ void quantize_q8_0_kernel(const float *x, uint8_t *out, uint64_t nblo
 }
 
 // Q4_0 weight x Q8_0 activation GEMV (no counterpart in the reference, whose
-// decode multiplies f32 activations).  One warp per output row over the X4
-// device layout; per block the integer dot sum_j (n_j - 8) * q_j is formed
+// decode multiplies f32 activations).  One warp per output row over the
+// layout.h device layout; per block the integer dot sum_j (n_j - 8) * q_j is formed
 // exactly with dp4a, then scaled as (sumi * d_w) * d_x and accumulated.
 __global__ void q8act_gemv_kernel(const uint8_t *w, uint64_t gstride, uint32_t rows, uint32_t bpr,
                                   const uint8_t *xq, float *out) {
@@ -188,11 +188,10 @@ __global__ void q8act_gemv_kernel(const uint8_t *w, uint64_t gstride, uint32_t r
   const uint8_t *grp = w + static_cast<uint64_t>(row >> 2) * gstride;
   float acc = 0.f;
   for (uint32_t b = lane; b < bpr; b += 32) {
-    const uint8_t *blk = grp + static_cast<uint64_t>(b) * 72;
-    const float dw = h2f(static_cast<uint16_t>(blk[2 * l] | (blk[2 * l + 1] << 8)));
-    const uint2 qa = *reinterpret_cast<const uint2 *>(blk + 8 + 16 * l);
-    const uint2 qb = *reinterpret_cast<const uint2 *>(blk + 16 + 16 * l);
-    const uint32_t q[4] = {qa.x, qa.y, qb.x, qb.y};
+    const uint8_t *sc = grp + scale_entry(ZGPU_Q4_0, bpr, b) + 2 * l;
+    const float dw = h2f(static_cast<uint16_t>(sc[0] | (sc[1] << 8)));
+    const uint4 qv = *reinterpret_cast<const uint4 *>(grp + plane_entry(ZGPU_Q4_0, bpr, b, l));
+    const uint32_t q[4] = {qv.x, qv.y, qv.z, qv.w};
     const uint8_t *xb = xq + static_cast<uint64_t>(b) * 34;
     const float dx = h2f(static_cast<uint16_t>(xb[0] | (xb[1] << 8)));
     uint32_t xw[8];

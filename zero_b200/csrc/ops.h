@@ -24,7 +24,7 @@ struct StepState {
 };
 
 struct EmbedParams {
-  const uint8_t *emb;       // X4 device table
+  const uint8_t *emb;       // device table (layout.h group streams)
   uint64_t gstride;
   uint32_t quant;           // ZGPU_Q8_0 / ZGPU_Q4_0
   uint32_t hidden;
