@@ -257,9 +257,8 @@ def main():
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         dec_ms = float(t.item())
     tok_s = world * args.steps / (dec_ms / 1000.0)
-    # generate() replayed PROMPT_LEN prefill steps and K decode steps of the same graph
-    step_kernels = perf["kernel_launches"] // (PROMPT_LEN + args.steps)
-    gpu_launches = step_kernels * args.steps
+    # kernel launches of this library inside the timed decode steps
+    gpu_launches = perf["decode_launches"]
 
     # ------------------------------------------------ e2e through the C ABI
     e2e_tok_s = None

@@ -87,6 +87,10 @@ typedef struct zgpu_opts {
 #define ZGPU_FLAG_NO_GRAPH 0x1u
 /* Launch kernels with programmatic dependent launch (default on). */
 #define ZGPU_FLAG_NO_PDL 0x2u
+/* Run decode steps as one persistent cooperative kernel per call (default
+ * on where the device and the model geometry allow it); with this flag the
+ * step is a sequence of per-op kernels instead. */
+#define ZGPU_FLAG_NO_PERSISTENT 0x4u
 
 /* ---------------------------------------------------------------- context */
 zgpu_status zgpu_init(const zgpu_opts *opts, zgpu_ctx **out);
@@ -263,9 +267,10 @@ zgpu_status zgpu_generate_greedy(zgpu_model *m, zgpu_kv *kv, const uint32_t *pro
  * zgpu_generate_greedy decode phase. */
 typedef struct zgpu_perf {
   uint64_t steps;
-  uint64_t kernel_launches;   /* of this library's kernels */
+  uint64_t kernel_launches;   /* of this library's kernels, whole call */
   double decode_ms;           /* device time of the decode steps */
   double prefill_ms;
+  uint64_t decode_launches;   /* kernel launches of the decode steps alone */
 } zgpu_perf;
 zgpu_status zgpu_perf_snapshot(const zgpu_model *m, zgpu_perf *out);
 

@@ -4,7 +4,8 @@ The north-star bar: greedy token ids identical, logits within 1e-2 relative
 L2.  The GPU path is held much tighter here (1e-4 on the small models) since
 it reproduces the reference's RoPE/SiLU polynomials bit for bit and differs
 only in reduction order.  Tests run through the C ABI (zgpu_generate_greedy,
-zgpu_forward_single_token, zgpu_lm_head_argmax).
+zgpu_forward_single_token, zgpu_lm_head_argmax), on both execution paths: the
+persistent step kernel (default) and the per-op kernels (persistent=False).
 """
 import numpy as np
 import pytest
@@ -33,13 +34,33 @@ TINY = [
 ]
 
 
+PATHS = [True, False]
+
+
+def assert_path(m, persistent, n_gen):
+    """The last generate_greedy (no logits) ran on the requested path: the
+    persistent kernel runs all decode steps as one launch."""
+    launches = m.perf()["decode_launches"]
+    if persistent:
+        assert launches == 1, launches
+    else:
+        assert launches > n_gen, launches
+
+
+@pytest.mark.parametrize("persistent", PATHS, ids=["persistent", "per_op"])
 @pytest.mark.parametrize("cfg", TINY, ids=lambda c: c.name)
-def test_generate_matches_oracle(cfg):
-    ctx, w, m = build(cfg, seed=21)
+def test_generate_matches_oracle(cfg, persistent):
+    ctx, w, m = build(cfg, seed=21, persistent=persistent)
     prompt = synth.prompt_ids(cfg, 7, seed=21)
     n_gen = 12
     kv = m.new_kv(64)
     toks, logits = m.generate_greedy(kv, prompt, n_gen, want_logits=True)
+    # without logits the decode steps run as one launch: same tokens
+    kv_b = m.new_kv(64)
+    toks_b, _ = m.generate_greedy(kv_b, prompt, n_gen, want_logits=False)
+    assert np.array_equal(toks_b, toks)
+    assert_path(m, persistent, n_gen)
+    kv_b.close()
     r = O.OracleRun(cfg, w, 64, order=O.ORDER_AVX512)
     rc, ref_t, margins, ref_l = r.generate(prompt, n_gen, want_logits=True)
     assert rc == 0
@@ -61,11 +82,12 @@ def test_generate_matches_oracle(cfg):
     m.close(); kv.close(); ctx.close()
 
 
+@pytest.mark.parametrize("persistent", PATHS, ids=["persistent", "per_op"])
 @pytest.mark.parametrize("cfg", TINY[:2], ids=lambda c: c.name)
-def test_long_context_uses_split_attention(cfg):
+def test_long_context_uses_split_attention(cfg, persistent):
     # > 256 cached tokens: the attention runs as several splits per kv-head
     # merged by the last CTA (flash-decoding partials).
-    ctx, w, m = build(cfg, seed=25)
+    ctx, w, m = build(cfg, seed=25, persistent=persistent)
     prompt = synth.prompt_ids(cfg, 530, seed=25)
     kv = m.new_kv(600)
     toks, logits = m.generate_greedy(kv, prompt, 6, want_logits=True)
@@ -77,9 +99,10 @@ def test_long_context_uses_split_attention(cfg):
     m.close(); kv.close(); ctx.close()
 
 
-def test_step_api_matches_generate():
+@pytest.mark.parametrize("persistent", PATHS, ids=["persistent", "per_op"])
+def test_step_api_matches_generate(persistent):
     cfg = TINY[1]
-    ctx, w, m = build(cfg, seed=22)
+    ctx, w, m = build(cfg, seed=22, persistent=persistent)
     prompt = synth.prompt_ids(cfg, 5, seed=22)
     kv = m.new_kv(32)
     toks, logits = m.generate_greedy(kv, prompt, 6, want_logits=True)
@@ -110,15 +133,23 @@ def test_graph_replay_equals_eager_and_is_deterministic():
     w = synth.qwen3_weights(cfg, seed=23, norm_sigma=0.1)
     prompt = synth.prompt_ids(cfg, 6, seed=23)
     outs = []
-    for kw in ({"graph": True}, {"graph": False}, {"graph": True, "pdl": False}, {"graph": True}):
+    per_op = ({"persistent": False, "graph": True}, {"persistent": False, "graph": False},
+              {"persistent": False, "graph": True, "pdl": False}, {"persistent": False, "graph": True})
+    for kw in per_op + ({"persistent": True}, {"persistent": True}):
         ctx = zb.Context(**kw)
         m = zb.Qwen3Model(ctx, cfg, w)
         kv = m.new_kv(40)
         outs.append(m.generate_greedy(kv, prompt, 10, want_logits=True))
         m.close(); kv.close(); ctx.close()
-    for toks, logits in outs[1:]:
+    # per-op kernels: graph, eager, PDL or not -> identical bits
+    for toks, logits in outs[1:4]:
         assert np.array_equal(toks, outs[0][0])
         assert np.array_equal(logits, outs[0][1])
+    # persistent kernel: deterministic run to run; same tokens as the per-op
+    # path, logits equal up to the RMSNorm summation order
+    assert np.array_equal(outs[4][0], outs[5][0]) and np.array_equal(outs[4][1], outs[5][1])
+    assert np.array_equal(outs[4][0], outs[0][0])
+    assert max(rel_l2(outs[4][1][s], outs[0][1][s]) for s in range(10)) < 1e-5
 
 
 def test_errors_follow_the_reference_enums():
@@ -151,10 +182,11 @@ def test_errors_follow_the_reference_enums():
 
 
 @pytest.mark.slow
-def test_config0_full_size_matches_oracle():
+@pytest.mark.parametrize("persistent", PATHS, ids=["persistent", "per_op"])
+def test_config0_full_size_matches_oracle(persistent):
     """Qwen3-1.7B shape, 16 prompt ids, 128 greedy decode steps."""
     cfg = synth.QWEN3_1_7B
-    ctx = zb.Context()
+    ctx = zb.Context(persistent=persistent)
     w = synth.qwen3_weights(cfg, seed=0)
     m = zb.Qwen3Model(ctx, cfg, w)
     prompt = synth.prompt_ids(cfg, 16, seed=0)
@@ -168,4 +200,9 @@ def test_config0_full_size_matches_oracle():
     worst = max(rel_l2(logits[s], ref_l[s]) for s in range(n_gen))
     assert worst < 1e-2, worst
     assert worst < 1e-4, worst          # what this path actually achieves
-    m.close(); kv.close(); ctx.close()
+    # the decode steps as one launch give the same tokens
+    kv_b = m.new_kv(512)
+    toks_b, _ = m.generate_greedy(kv_b, prompt, n_gen, want_logits=False)
+    assert np.array_equal(toks_b, toks)
+    assert_path(m, persistent, n_gen)
+    m.close(); kv.close(); kv_b.close(); ctx.close()

@@ -20,7 +20,7 @@ from .synth import QWEN3_1_7B, Qwen3Config
 
 ABI_VERSION = 1
 F32, F16, Q4_0, Q8_0, Q4_0X4, Q8_0X4 = 0, 1, 2, 8, 100, 101
-FLAG_NO_GRAPH, FLAG_NO_PDL = 0x1, 0x2
+FLAG_NO_GRAPH, FLAG_NO_PDL, FLAG_NO_PERSISTENT = 0x1, 0x2, 0x4
 
 STATUS = {
     0: "OK", 1: "INVALID_ARG", 2: "UNSUPPORTED_QUANT", 3: "UNREGISTERED_WEIGHT",
@@ -47,8 +47,9 @@ def _ptr(a: np.ndarray) -> int:
 class Context:
     """A device context (zgpu_init).  Keeps every registered host array alive."""
 
-    def __init__(self, device: int = 0, graph: bool = True, pdl: bool = True):
-        flags = (0 if graph else FLAG_NO_GRAPH) | (0 if pdl else FLAG_NO_PDL)
+    def __init__(self, device: int = 0, graph: bool = True, pdl: bool = True, persistent: bool = True):
+        flags = ((0 if graph else FLAG_NO_GRAPH) | (0 if pdl else FLAG_NO_PDL)
+                 | (0 if persistent else FLAG_NO_PERSISTENT))
         opts = ZgpuOpts(ABI_VERSION, device, flags)
         h = C.c_void_p()
         st = LIB.zgpu_init(C.byref(opts), C.byref(h))
@@ -264,7 +265,7 @@ class Qwen3Model:
         p = ZgpuPerf()
         self.ctx._check(LIB.zgpu_perf_snapshot(self.h, C.byref(p)))
         return {"steps": p.steps, "kernel_launches": p.kernel_launches, "decode_ms": p.decode_ms,
-                "prefill_ms": p.prefill_ms}
+                "prefill_ms": p.prefill_ms, "decode_launches": p.decode_launches}
 
 
 __all__ = ["Context", "KvCache", "Qwen3Model", "Qwen3Config", "QWEN3_1_7B", "ZgpuError", "synth",

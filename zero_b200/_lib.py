@@ -43,7 +43,7 @@ class ZgpuQwen3Desc(C.Structure):
 
 class ZgpuPerf(C.Structure):
     _fields_ = [("steps", _u64), ("kernel_launches", _u64), ("decode_ms", C.c_double),
-                ("prefill_ms", C.c_double)]
+                ("prefill_ms", C.c_double), ("decode_launches", _u64)]
 
 
 _SIGS = {

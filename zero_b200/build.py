@@ -32,8 +32,12 @@ CXX_FLAGS = ["-O2", "-fPIC", "-std=c++17", "-Wall", "-pthread"]
 # accesses, record the first failure in the status block and skip it.
 if os.environ.get("ZGPU_DEVICE_CHECKS") == "1":
     CUDA_FLAGS.append("-DZGPU_DEVICE_CHECKS")
+# ZGPU_STEP_TRACE=1 records the persistent kernel's stage timeline (CTA 0)
+# and exports zgpu_debug_step_trace to read it.
+if os.environ.get("ZGPU_STEP_TRACE") == "1":
+    CUDA_FLAGS.append("-DZGPU_STEP_TRACE")
 
-CU_SOURCES = ["gemv.cu", "attention.cu", "attention_static.cu", "ops.cu", "ctx.cu", "model.cu"]
+CU_SOURCES = ["gemv.cu", "attention.cu", "attention_static.cu", "step.cu", "ops.cu", "ctx.cu", "model.cu"]
 CXX_SOURCES = ["synth.cpp"]
 
 

@@ -186,6 +186,58 @@ __device__ __forceinline__ void ref_sincos(float x, float *s_out, float *c_out) 
   *c_out = (b0 ^ b1) ? -c : c;
 }
 
+// Tagged activation words (the persistent step kernel's inter-stage
+// vectors): element i is (version << 32) | f32 bits, written with one 64-bit
+// store, so a reader that sees the expected version also sees its value.
+__device__ __forceinline__ unsigned long long tag_word(float x, uint32_t ver) {
+  return (static_cast<unsigned long long>(ver) << 32) | __float_as_uint(x);
+}
+
+__device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Wait until the four words at p (16-byte aligned) carry `ver`, then return
+// their values.  Bounded: gives up (false) when this CTA or the launch is
+// aborting, or after kWaitLimitNs, which also sets ZDEV_ERR_TIMEOUT and the
+// abort flags.
+__device__ __forceinline__ bool tag_wait4(const unsigned long long *p, uint32_t ver, float4 *out,
+                                          uint32_t *status, volatile uint32_t *abort,
+                                          uint32_t *gabort) {
+  const ulonglong2 *q = reinterpret_cast<const ulonglong2 *>(p);
+  ulonglong2 a = __ldcg(q), b = __ldcg(q + 1);
+  auto ready = [&]() {
+    return static_cast<uint32_t>(a.x >> 32) == ver && static_cast<uint32_t>(a.y >> 32) == ver &&
+           static_cast<uint32_t>(b.x >> 32) == ver && static_cast<uint32_t>(b.y >> 32) == ver;
+  };
+  if (!ready()) {
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+      __nanosleep(64);
+      a = __ldcg(q);
+      b = __ldcg(q + 1);
+      if (ready()) break;
+      if (*abort || ld_relaxed_u32(gabort)) {
+        *abort = 1;
+        *out = make_float4(0.f, 0.f, 0.f, 0.f);
+        return false;
+      }
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicOr(status, ZDEV_ERR_TIMEOUT);
+        atomicExch(gabort, 1u);
+        *abort = 1;
+        *out = make_float4(0.f, 0.f, 0.f, 0.f);
+        return false;
+      }
+    }
+  }
+  *out = make_float4(__uint_as_float(static_cast<uint32_t>(a.x)), __uint_as_float(static_cast<uint32_t>(a.y)),
+                     __uint_as_float(static_cast<uint32_t>(b.x)), __uint_as_float(static_cast<uint32_t>(b.y)));
+  return true;
+}
+
 // Orderable key for the LM-head argmax: larger value wins, then the smaller
 // index (inference_avx512.rs:1027-1044 merge rule).  NaN never wins (it is
 // mapped to the initial key); -0 is folded onto +0 so ties behave like the

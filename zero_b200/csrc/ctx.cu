@@ -9,6 +9,7 @@
 #include "internal.h"
 #include "layout.h"
 #include "ops.h"
+#include "step.h"
 
 using zgpu::DeviceTensor;
 
@@ -85,7 +86,7 @@ zgpu_status zgpu_init(const zgpu_opts *opts, zgpu_ctx **out) {
       cudaMalloc(&ctx->d_status, zgpu::kStatusWords * sizeof(uint32_t)) != cudaSuccess ||
       cudaMemset(ctx->d_status, 0, zgpu::kStatusWords * sizeof(uint32_t)) != cudaSuccess ||
       zgpu::gemv_setup() != cudaSuccess || zgpu::attention_setup() != cudaSuccess ||
-      zgpu::ops_setup() != cudaSuccess) {
+      zgpu::ops_setup() != cudaSuccess || zgpu::step_setup() != cudaSuccess) {
     delete ctx;
     return ZGPU_ERR_CUDA;
   }

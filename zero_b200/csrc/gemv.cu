@@ -43,6 +43,7 @@
 #include <cfloat>
 
 #include "common.cuh"
+#include "gemv_body.cuh"
 #include "internal.h"
 #include "layout.h"
 
@@ -81,95 +82,8 @@ struct KParams {
   uint32_t *status;
 };
 
-// Activation image: 32 words per block, in 16-byte chunks
-//   0-1: digit-0 words, 2-3: digit-1 words, 4-5: digit-2 words,
-//   6: (offset0, offset1, offset2, 2^E as f32 bits), 7: unused;
-// digit word k packs the digit bytes of elements 4k..4k+3 (for Q4_0 words
-// 0-3 meet the low nibbles of qs word k, words 4-7 the high nibbles of qs
-// word k-4; for Q8_0 word k meets qs word k).  Chunk c of block b sits at
-// chunk position c ^ (b & 7).
-__device__ __forceinline__ uint32_t x_word(uint32_t b, uint32_t chunk, uint32_t w) {
-  return b * 32 + ((chunk ^ (b & 7)) << 2) + w;
-}
-
-// dp4a with the byte signedness of each operand (PTX dp4a.atype.btype).
-__device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
-  int d;
-  asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
-  int d;
-  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-__device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c) {
-  int d;
-  asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
-  int d;
-  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-
-template <int R>
-__device__ __forceinline__ float reduce_scatter(float (&v)[R], uint32_t lane) {
-#pragma unroll
-  for (int lvl = 0; lvl < 5; ++lvl) {
-    const int off = 16 >> lvl;
-    const int n = R >> lvl;
-    if (n >= 2) {
-      const bool upper = (lane & off) != 0;
-#pragma unroll
-      for (int k = 0; k < n / 2; ++k) {
-        float send = upper ? v[k] : v[k + n / 2];
-        float keep = upper ? v[k + n / 2] : v[k];
-        v[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-      }
-    } else {
-      v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
-    }
-  }
-  return v[0];
-}
-
-// sum_j (n_j - 8) * N_j of one Q4_0 row-block from its 16 nibble bytes: the
-// digit offsets start each chain at -8 * sum_j digit_j.
-__device__ __forceinline__ float q4_dot(const uint4 q, const uint32_t (&D)[3][8], const int (&I)[3]) {
-  int s0 = I[0], s1 = I[1], s2 = I[2];
-  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-  for (int m = 0; m < 4; ++m) {
-    const uint32_t lo = w[m] & 0x0F0F0F0Fu, hi = (w[m] >> 4) & 0x0F0F0F0Fu;
-    s0 = dp4a_uu(lo, D[0][m], s0);
-    s1 = dp4a_uu(lo, D[1][m], s1);
-    s2 = dp4a_us(lo, D[2][m], s2);
-    s0 = dp4a_uu(hi, D[0][m + 4], s0);
-    s1 = dp4a_uu(hi, D[1][m + 4], s1);
-    s2 = dp4a_us(hi, D[2][m + 4], s2);
-  }
-  // |s0 + 256 s1| < 2^24: exact in int32 and in f32
-  return fmaf(static_cast<float>(s2), 65536.0f, static_cast<float>(s0 + (s1 << 8)));
-}
-
-// sum_j q_j * N_j of one Q8_0 row-block from its two 16-byte halves.
-__device__ __forceinline__ float q8_dot(const uint4 qa, const uint4 qb, const uint32_t (&D)[3][8]) {
-  int s0 = 0, s1 = 0, s2 = 0;
-  const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    s0 = dp4a_su(w[k], D[0][k], s0);
-    s1 = dp4a_su(w[k], D[1][k], s1);
-    s2 = dp4a_ss(w[k], D[2][k], s2);
-  }
-  return fmaf(static_cast<float>(s2), 65536.0f, static_cast<float>(s0 + (s1 << 8)));
-}
-
 template <int QT, int PRO, int EPI>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KParams p) {
-  constexpr uint32_t P = (QT == ZGPU_Q4_0) ? 4 : 8;   // planes per chunk (layout.h)
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float red[kWarps];
   __shared__ unsigned long long best_w[kWarps];
@@ -236,31 +150,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
   const uint32_t tid = threadIdx.x;
   const uint32_t nf4 = p.in_dim / 4;
   float inv = 1.0f;
-  if (PRO == PRO_RMSNORM) {
-    // rmsnorm (ops.rs:29-52): fixed-order sum of squares (per thread over its
-    // float4s in order, xor-tree in the warp, warps in order).
-    float ss = 0.f;
-    for (uint32_t f = tid; f < nf4; f += kConsumers) {
-      const float4 t = reinterpret_cast<const float4 *>(p.x)[f];
-      ss = __fadd_rn(ss, __fadd_rn(__fadd_rn(__fmul_rn(t.x, t.x), __fmul_rn(t.y, t.y)),
-                                   __fadd_rn(__fmul_rn(t.z, t.z), __fmul_rn(t.w, t.w))));
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-    if (lane == 0) red[warp] = ss;
-    named_bar_sync(1, kConsumers);
-    float tot = 0.f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) tot = __fadd_rn(tot, red[w]);
-    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(p.in_dim)), p.eps)));
-  }
-  // Warp-uniform trip count: the per-block sum below shuffles across the 8
+  if (PRO == PRO_RMSNORM) inv = rms_inv<kWarps>(p.x, p.in_dim, p.eps, red, tid, 1);
+  // Warp-uniform trip count: the per-block statistics shuffle across the 8
   // lanes of a block, and nf4 is a multiple of 8, so a block's lanes are
   // either all in range or all out of range.
   for (uint32_t f0 = warp * 32; f0 < nf4; f0 += kConsumers) {
     const uint32_t f = f0 + lane;
     const bool valid = f < nf4;
-    float4 t = valid ? reinterpret_cast<const float4 *>(p.x)[f] : make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 t = valid ? __ldcg(reinterpret_cast<const float4 *>(p.x) + f) : make_float4(0.f, 0.f, 0.f, 0.f);
     if (PRO == PRO_RMSNORM && valid) {
       const float4 g = reinterpret_cast<const float4 *>(p.norm_w)[f];
       t.x = __fmul_rn(__fmul_rn(t.x, inv), g.x);
@@ -268,56 +165,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
       t.z = __fmul_rn(__fmul_rn(t.z, inv), g.z);
       t.w = __fmul_rn(__fmul_rn(t.w, inv), g.w);
     }
-    const uint32_t b = f >> 3, k4 = f & 7;
-    // a failed check only suppresses the writes: every lane still reaches the
-    // shuffles below
-    const bool in_range =
-        valid && ZDEV_CHECK(b < p.bpr && b * 128 + 128 <= p.xbytes, p.status, 3, b, p.xbytes);
-    // block maximum and non-finite flag over the block's 8 lanes
-    float am = fmaxf(fmaxf(fabsf(t.x), fabsf(t.y)), fmaxf(fabsf(t.z), fabsf(t.w)));
-    uint32_t bad = (fabsf(t.x) <= FLT_MAX && fabsf(t.y) <= FLT_MAX && fabsf(t.z) <= FLT_MAX &&
-                    fabsf(t.w) <= FLT_MAX) ? 0u : 1u;
-#pragma unroll
-    for (int off = 1; off < 8; off <<= 1) {
-      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
-      bad |= __shfl_xor_sync(0xffffffffu, bad, off);
-    }
-    int n[4] = {0, 0, 0, 0};
-    float bscale = 0.0f;                              // all-zero (or negligible) block
-    if (bad) {
-      bscale = __uint_as_float(0x7fc00000u);          // NaN: the rows' sums become NaN
-    } else if (am >= 7.888609052e-31f) {              // 2^-100
-      const int e = static_cast<int>(__float_as_uint(am) >> 23) - 127;   // am in [2^e, 2^(e+1))
-      const float up = __uint_as_float(static_cast<uint32_t>(149 - e) << 23);   // 2^(22-e)
-      bscale = __uint_as_float(static_cast<uint32_t>(105 + e) << 23);          // 2^(e-22)
-      const float v[4] = {t.x, t.y, t.z, t.w};
-#pragma unroll
-      for (int k = 0; k < 4; ++k) n[k] = min(__float2int_rn(v[k] * up), 0x7FFFFF);
-    }
-    const uint32_t w0 = __byte_perm(__byte_perm(n[0], n[1], 0x0040), __byte_perm(n[2], n[3], 0x0040), 0x5410);
-    const uint32_t w1 = __byte_perm(__byte_perm(n[0], n[1], 0x0051), __byte_perm(n[2], n[3], 0x0051), 0x5410);
-    const uint32_t w2 = __byte_perm(__byte_perm(n[0], n[1], 0x0062), __byte_perm(n[2], n[3], 0x0062), 0x5410);
-    int ds[3] = {0, 0, 0};
-    if (QT == ZGPU_Q4_0) {
-      ds[0] = dp4a_uu(w0, 0x01010101u, 0);
-      ds[1] = dp4a_uu(w1, 0x01010101u, 0);
-      ds[2] = dp4a_us(0x01010101u, w2, 0);
-#pragma unroll
-      for (int off = 1; off < 8; off <<= 1)
-#pragma unroll
-        for (int d = 0; d < 3; ++d) ds[d] += __shfl_xor_sync(0xffffffffu, ds[d], off);
-    }
-    if (in_range) {
-      xsm[x_word(b, 0 + (k4 >> 2), k4 & 3)] = w0;
-      xsm[x_word(b, 2 + (k4 >> 2), k4 & 3)] = w1;
-      xsm[x_word(b, 4 + (k4 >> 2), k4 & 3)] = w2;
-      if (k4 == 0) {
-        xsm[x_word(b, 6, 0)] = static_cast<uint32_t>(-8 * ds[0]);
-        xsm[x_word(b, 6, 1)] = static_cast<uint32_t>(-8 * ds[1]);
-        xsm[x_word(b, 6, 2)] = static_cast<uint32_t>(-8 * ds[2]);
-        xsm[x_word(b, 6, 3)] = __float_as_uint(bscale);
-      }
-    }
+    digitise_f4<QT>(t, f, valid, xsm, p.bpr, p.xbytes, p.status);
   }
   named_bar_sync(1, kConsumers);
 
@@ -333,39 +181,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
     for (int r = 0; r < kRows; ++r) acc[r] = 0.f;
     if (!failed && b < p.bpr) {
       const uint8_t *sbase = ring + static_cast<size_t>(slot) * slot_bytes;
-      const uint32_t nb = chunk_blocks(p.bpr, chunk);
-      const uint4 *xb = reinterpret_cast<const uint4 *>(xsm + b * 32);
-      const uint32_t sw = b & 7;
-      uint32_t D[3][8];
-#pragma unroll
-      for (int c = 0; c < 6; ++c) {
-        const uint4 v = xb[c ^ sw];
-        D[c >> 1][4 * (c & 1) + 0] = v.x;
-        D[c >> 1][4 * (c & 1) + 1] = v.y;
-        D[c >> 1][4 * (c & 1) + 2] = v.z;
-        D[c >> 1][4 * (c & 1) + 3] = v.w;
-      }
-      const uint4 meta = xb[6 ^ sw];
-      const int I[3] = {static_cast<int>(meta.x), static_cast<int>(meta.y), static_cast<int>(meta.z)};
-      const float bscale = __uint_as_float(meta.w);
-#pragma unroll
-      for (int g = 0; g < 2; ++g) {
-        const uint8_t *cb = sbase + g * p.half_bytes;
-        const uint2 sc = *reinterpret_cast<const uint2 *>(cb + P * nb * 16 + lane * 8);
-        const float d[4] = {h2f(sc.x & 0xFFFF), h2f(sc.x >> 16), h2f(sc.y & 0xFFFF),
-                            h2f(sc.y >> 16)};
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          float t;
-          if (QT == ZGPU_Q4_0) {
-            t = q4_dot(*reinterpret_cast<const uint4 *>(cb + r * nb * 16 + lane * 16), D, I);
-          } else {
-            t = q8_dot(*reinterpret_cast<const uint4 *>(cb + (2 * r) * nb * 16 + lane * 16),
-                       *reinterpret_cast<const uint4 *>(cb + (2 * r + 1) * nb * 16 + lane * 16), D);
-          }
-          acc[4 * g + r] = __fmul_rn(d[r], bscale) * t;
-        }
-      }
+      item_rows<QT, 2>(sbase, p.half_bytes, chunk_blocks(p.bpr, chunk), lane, b, xsm, acc);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_addr(&empty[slot]));

@@ -19,7 +19,9 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "layout.h"
 #include "ops.h"
+#include "step.h"
 
 using namespace zgpu;
 
@@ -56,6 +58,17 @@ struct zgpu_model {
   uint32_t step_kernels = 0, fwd_kernels = 0, lm_kernels = 0;
   zgpu_perf perf = {};
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+  // persistent step kernel (step.cu): stage list and launch geometry
+  std::vector<StageDesc> stages;
+  StageDesc *d_stages = nullptr;
+  uint32_t n_layer_stages = 0, lm_stage = 0;
+  uint32_t *d_bar = nullptr;        // grid-barrier counter + abort flag
+  uint32_t step_grid = 0;           // 0: the persistent path is not used
+  StepParams step_geom = {};
+  unsigned long long *d_tv = nullptr;   // tagged vectors: hidden | qkv | attn | act | token
+  unsigned long long *tv[kStepBufs] = {};
+  uint32_t ver[kStepBufs] = {};
+  bool last_fwd_persistent = false; // the path the last forward used (the LM head follows it)
 };
 
 namespace {
@@ -314,6 +327,165 @@ cudaError_t grow(T **p, uint32_t *cap, uint32_t need) {
   return e;
 }
 
+// Stage list of one decode step for the persistent kernel (step.cu).  The
+// model keeps the multi-kernel path when the device or the geometry does not
+// suit the persistent kernel, or when the context asks for it.
+zgpu_status build_step(zgpu_model *m) {
+  zgpu_ctx *ctx = m->ctx;
+  m->step_grid = 0;
+  if (ctx->flags & ZGPU_FLAG_NO_PERSISTENT) return ZGPU_OK;
+  const uint32_t grid = step_max_grid(ctx->sm_count);
+  if (!grid) return ZGPU_OK;
+  const zgpu_qwen3_desc &d = m->desc;
+  const uint32_t H = d.hidden, F = d.ffn, L = d.n_layers;
+  const uint32_t qkv_rows = m->q_dim + 2 * m->kv_dim;
+  auto gemv = [&](uint32_t quant, uint32_t pro, uint32_t epi, uint32_t rows, uint32_t units,
+                  uint32_t in_dim, const uint8_t *w, uint64_t gstride, uint64_t wbytes, uint32_t in_buf,
+                  const float *norm_w, uint32_t out_buf) {
+    StageDesc s = {};
+    s.kind = STG_GEMV;
+    s.quant = quant;
+    s.pro = pro;
+    s.epi = epi;
+    s.rows = rows;
+    s.units = units;
+    s.gpu = quant == ZGPU_Q4_0 ? 2 : 1;
+    s.bpr = in_dim / 32;
+    s.ks = (s.bpr + kChunkBlocks - 1) / kChunkBlocks;
+    s.in_dim = in_dim;
+    s.gbytes = static_cast<uint32_t>(chunk_bytes(quant, s.bpr < kChunkBlocks ? s.bpr : kChunkBlocks));
+    s.w = w;
+    s.gstride = gstride;
+    s.wbytes = wbytes;
+    s.in_buf = in_buf;
+    s.out_buf = out_buf;
+    s.norm_w = norm_w;
+    return s;
+  };
+  // gate/up groups as the registry stores them (padded to an even count)
+  const uint64_t gu_groups = ((F + 3) / 4 + 1) & ~uint64_t(1);
+  std::vector<StageDesc> st;
+  for (uint32_t l = 0; l < L; ++l) {
+    StageDesc q = gemv(ZGPU_Q4_0, PRO_RMSNORM, EPI_STORE, qkv_rows, qkv_rows / 8, H, m->qkv[l], m->gs_h,
+                       static_cast<uint64_t>(qkv_rows / 4) * m->gs_h, BUF_HIDDEN, norm_attn(m, l), BUF_QKV);
+    if (l == 0) q.flags = kStageEmbed;
+    st.push_back(q);
+    StageDesc a = {};
+    a.kind = STG_ATTN;
+    a.layer = l;
+    a.q_norm = norm_q(m, l);
+    a.k_norm = norm_k(m, l);
+    st.push_back(a);
+    const DeviceTensor *o = m->o[l], *dn = m->down[l];
+    st.push_back(gemv(ZGPU_Q4_0, PRO_PLAIN, EPI_RESADD, H, static_cast<uint32_t>(o->groups / 2), m->q_dim,
+                      o->d, o->gstride, o->bytes, BUF_ATTN, nullptr, BUF_HIDDEN));
+    st.push_back(gemv(ZGPU_Q4_0, PRO_RMSNORM, EPI_SWIGLU, F, static_cast<uint32_t>(gu_groups), H, m->gateup[l],
+                      m->gs_h, 2 * gu_groups * m->gs_h, BUF_HIDDEN, norm_ffn(m, l), BUF_ACT));
+    st.push_back(gemv(ZGPU_Q4_0, PRO_PLAIN, EPI_RESADD, H, static_cast<uint32_t>(dn->groups / 2), F, dn->d,
+                      dn->gstride, dn->bytes, BUF_ACT, nullptr, BUF_HIDDEN));
+  }
+  const DeviceTensor *ot = m->out;
+  const uint32_t gpu = ot->quant == ZGPU_Q4_0 ? 2 : 1;
+  const uint32_t lm = static_cast<uint32_t>(st.size());
+  st.push_back(gemv(ot->quant, PRO_RMSNORM, EPI_ARGMAX, d.vocab_padded, static_cast<uint32_t>(ot->groups / gpu),
+                    H, ot->d, ot->gstride, ot->bytes, BUF_HIDDEN, norm_out(m), BUF_NONE));
+  st.back().out = m->d_logits;
+  StepParams g = {};
+  if (!step_geometry(st.data(), static_cast<uint32_t>(st.size()), grid, &g)) return ZGPU_OK;
+  cudaError_t e = cudaMalloc(&m->d_stages, st.size() * sizeof(StageDesc));
+  if (e == cudaSuccess)
+    e = cudaMemcpy(m->d_stages, st.data(), st.size() * sizeof(StageDesc), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMalloc(&m->d_bar, 2 * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemset(m->d_bar, 0, 2 * sizeof(uint32_t));
+  // tagged vectors (version 0 everywhere: nothing written yet)
+  const size_t tv_len[kStepBufs] = {H, qkv_rows, m->q_dim, F, 2};
+  size_t tv_total = 0;
+  for (size_t n : tv_len) tv_total += n;
+  if (e == cudaSuccess) e = cudaMalloc(&m->d_tv, tv_total * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMemset(m->d_tv, 0, tv_total * sizeof(unsigned long long));
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "step kernel set-up");
+  size_t off = 0;
+  for (int b = 0; b < kStepBufs; ++b) {
+    m->tv[b] = m->d_tv + off;
+    off += tv_len[b];
+    m->ver[b] = 0;
+  }
+  m->stages = st;
+  m->n_layer_stages = 5 * L;
+  m->lm_stage = lm;
+  m->step_geom = g;
+  m->step_grid = grid;
+  return ZGPU_OK;
+}
+
+bool step_usable(const zgpu_model *m, const zgpu_kv *kv) {
+  if (!m->step_grid) return false;
+  return !kv || static_cast<uint64_t>(m->desc.n_kv_heads) * m->max_splits <= m->step_grid;
+}
+
+// One persistent launch: `n_steps` steps from global step `step0`.
+cudaError_t run_step(zgpu_model *m, zgpu_kv *kv, StepMode mode, uint32_t step0, uint32_t n_steps,
+                     uint32_t token, uint32_t pos, uint32_t n_prompt) {
+  const zgpu_qwen3_desc &d = m->desc;
+  StepParams p = m->step_geom;
+  p.stages = m->d_stages;
+  p.n_layer_stages = m->n_layer_stages;
+  p.lm_stage = m->lm_stage;
+  p.mode = mode;
+  p.step0 = step0;
+  p.n_steps = n_steps;
+  p.fwd_token = token;
+  p.fwd_pos = pos;
+  p.n_q = d.n_q_heads;
+  p.n_kv = d.n_kv_heads;
+  p.max_splits = m->max_splits;
+  p.max_tokens = kv ? kv->max_tokens : 0;
+  p.eps = d.rms_eps;
+  p.scale = 1.0f / sqrtf(static_cast<float>(d.head_dim));
+  p.emb = m->emb->d;
+  p.emb_gstride = m->emb->gstride;
+  p.emb_quant = m->emb->quant;
+  p.emb_rows = static_cast<uint32_t>(m->emb->rows);
+  p.hidden = d.hidden;
+  for (int b = 0; b < kStepBufs; ++b) {
+    p.tv[b] = m->tv[b];
+    p.ver[b] = m->ver[b];
+  }
+  p.inv_freqs = m->d_inv_freqs;
+  p.kv_base = kv ? kv->d : nullptr;
+  p.kv_block = kv ? kv->block : 0;
+  p.attn_part = m->d_part;
+  p.attn_counters = m->d_counters;
+  p.argmax = m->d_argmax;
+  p.state = m->d_state;
+  p.prompt = m->d_prompt;
+  p.tokens_out = m->d_tokens;
+  p.status = m->d_status;
+  p.bar = m->d_bar;
+  cudaError_t e = cudaMemsetAsync(m->d_bar, 0, 2 * sizeof(uint32_t), m->ctx->stream);
+  if (e != cudaSuccess) return e;
+  e = step_launch(p, m->step_grid, m->ctx->stream);
+  if (e != cudaSuccess) return e;
+  // the versions the launch leaves behind (the kernel walks the same steps)
+  for (uint32_t i = 0; i < n_steps; ++i) {
+    const uint32_t gstep = step0 + i;
+    const bool fwd = mode != STEP_LM;
+    const bool lm = mode == STEP_LM || (mode == STEP_GENERATE && gstep + 1 >= n_prompt);
+    step_advance_versions(m->ver, d.n_layers, fwd, lm);
+  }
+  if (mode != STEP_LM) m->last_fwd_persistent = true;
+  return cudaSuccess;
+}
+
+// After a device-side timeout the tagged vectors may hold any version: start
+// them over.
+void reset_step_tags(zgpu_model *m) {
+  if (!m->d_tv) return;
+  const size_t n = m->desc.hidden + (m->q_dim + 2 * m->kv_dim) + m->q_dim + m->desc.ffn + 2;
+  cudaMemsetAsync(m->d_tv, 0, n * sizeof(unsigned long long), m->ctx->stream);
+  for (int b = 0; b < kStepBufs; ++b) m->ver[b] = 0;
+}
+
 }  // namespace
 
 extern "C" {
@@ -405,6 +577,9 @@ void zgpu_qwen3_destroy(zgpu_model *m) {
   cudaFree(m->d_part);
   cudaFree(m->d_counters);
   cudaFree(m->d_status);
+  cudaFree(m->d_stages);
+  cudaFree(m->d_bar);
+  cudaFree(m->d_tv);
   for (auto &e : m->ev)
     if (e) cudaEventDestroy(e);
   delete m;
@@ -518,6 +693,11 @@ zgpu_status zgpu_qwen3_create(zgpu_ctx *ctx, const zgpu_qwen3_desc *d, zgpu_mode
   for (auto &ev : m->ev) cudaEventCreate(&ev);
   e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return fail(ZGPU_ERR_CUDA, "model upload");
+  zgpu_status bs = build_step(m);
+  if (bs) {
+    zgpu_qwen3_destroy(m);
+    return bs;
+  }
   *out = m;
   return ZGPU_OK;
 }
@@ -563,24 +743,43 @@ zgpu_status zgpu_forward_single_token(zgpu_model *m, zgpu_kv *kv, uint32_t token
   if (e == cudaSuccess) e = grow(&m->d_tokens, &m->tokens_cap, 1);
   if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "state buffers");
   if ((s = set_state(m, 1, pos, m->desc.vocab_real, 1))) return s;
-  const bool use_graph = !(ctx->flags & ZGPU_FLAG_NO_GRAPH);
+  const bool persistent = step_usable(m, kv);
+  const bool use_graph = !persistent && !(ctx->flags & ZGPU_FLAG_NO_GRAPH);
   if (use_graph && (s = build_graphs(m, kv))) return s;
   e = cudaMemcpyAsync(m->d_prompt, &token, 4, cudaMemcpyHostToDevice, ctx->stream);
   if (e == cudaSuccess) {
-    if (use_graph) {
+    if (persistent) {
+      e = run_step(m, kv, STEP_FORWARD, 0, 1, token, pos, 1);
+      ++ctx->launches;
+    } else if (use_graph) {
       e = cudaGraphLaunch(m->fwd_graph, ctx->stream);
       ctx->launches += m->fwd_kernels;
+      m->last_fwd_persistent = false;
     } else {
       e = enqueue_forward(m, kv, &ctx->launches);
+      m->last_fwd_persistent = false;
     }
   }
   if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "forward");
+  std::vector<unsigned long long> tagged;
   if (hidden_out) {
-    e = cudaMemcpyAsync(hidden_out, m->d_hidden, m->desc.hidden * 4, cudaMemcpyDeviceToHost, ctx->stream);
+    if (persistent) {
+      tagged.resize(m->desc.hidden);
+      e = cudaMemcpyAsync(tagged.data(), m->tv[BUF_HIDDEN], m->desc.hidden * sizeof(unsigned long long),
+                          cudaMemcpyDeviceToHost, ctx->stream);
+    } else {
+      e = cudaMemcpyAsync(hidden_out, m->d_hidden, m->desc.hidden * 4, cudaMemcpyDeviceToHost, ctx->stream);
+    }
     if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "hidden d2h");
   }
   uint32_t st = 0;
-  if ((s = read_status(m, &st))) return s;
+  if ((s = read_status(m, &st))) return s;   // synchronises the stream
+  if (persistent && (st & ZDEV_ERR_TIMEOUT)) reset_step_tags(m);
+  if (hidden_out && persistent)
+    for (uint32_t i = 0; i < m->desc.hidden; ++i) {
+      const uint32_t bits = static_cast<uint32_t>(tagged[i]);
+      std::memcpy(&hidden_out[i], &bits, 4);
+    }
   return map_status(ctx, st);
 }
 
@@ -595,8 +794,12 @@ zgpu_status zgpu_lm_head_argmax(zgpu_model *m, uint32_t vocab_real, uint32_t *to
   if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "state buffers");
   zgpu_status s = set_state(m, 1, 0, vocab_real, 1);
   if (s) return s;
-  const bool use_graph = !(ctx->flags & ZGPU_FLAG_NO_GRAPH) && m->lm_graph;
-  if (use_graph) {
+  const bool persistent = step_usable(m, nullptr) && m->last_fwd_persistent;
+  const bool use_graph = !persistent && !(ctx->flags & ZGPU_FLAG_NO_GRAPH) && m->lm_graph;
+  if (persistent) {
+    e = run_step(m, nullptr, STEP_LM, 0, 1, 0, 0, 1);
+    ++ctx->launches;
+  } else if (use_graph) {
     e = cudaGraphLaunch(m->lm_graph, ctx->stream);
     ctx->launches += m->lm_kernels;
   } else {
@@ -612,6 +815,7 @@ zgpu_status zgpu_lm_head_argmax(zgpu_model *m, uint32_t vocab_real, uint32_t *to
   if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "token d2h");
   uint32_t st = 0;
   if ((s = read_status(m, &st))) return s;
+  if (persistent && (st & ZDEV_ERR_TIMEOUT)) reset_step_tags(m);
   return map_status(ctx, st);
 }
 
@@ -634,11 +838,43 @@ zgpu_status zgpu_generate_greedy(zgpu_model *m, zgpu_kv *kv, const uint32_t *pro
   if ((s = set_state(m, n_prompt, 0, m->desc.vocab_real, n_gen))) return s;
   e = cudaMemcpyAsync(m->d_prompt, prompt, n_prompt * 4, cudaMemcpyHostToDevice, ctx->stream);
   if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "prompt upload");
-  const bool use_graph = !(ctx->flags & ZGPU_FLAG_NO_GRAPH);
+  const bool persistent = step_usable(m, kv);
+  const bool use_graph = !persistent && !(ctx->flags & ZGPU_FLAG_NO_GRAPH);
   if (use_graph && (s = build_graphs(m, kv))) return s;
   const size_t V = m->desc.vocab_padded;
-  uint32_t launches = 0;
-  auto run_step = [&](uint32_t step) -> cudaError_t {
+  uint32_t launches = 0, prefill_launches = 0;
+  if (persistent) {
+    // one launch for the prompt (the LM head runs after its last token) and
+    // one for the decode steps; with logits requested, one launch per step so
+    // that each step's logits can be copied out
+    auto copy_logits = [&](uint32_t step) -> cudaError_t {
+      if (!logits_out || step + 1 < n_prompt) return cudaSuccess;
+      return cudaMemcpyAsync(logits_out + static_cast<size_t>(step + 1 - n_prompt) * V, m->d_logits, V * 4,
+                             cudaMemcpyDeviceToHost, ctx->stream);
+    };
+    auto phase = [&](uint32_t first, uint32_t last) -> cudaError_t {
+      cudaError_t err = cudaSuccess;
+      if (first >= last) return err;
+      if (!logits_out) {
+        err = run_step(m, kv, STEP_GENERATE, first, last - first, 0, 0, n_prompt);
+        ++launches;
+        return err;
+      }
+      for (uint32_t st = first; st < last && err == cudaSuccess; ++st) {
+        err = run_step(m, kv, STEP_GENERATE, st, 1, 0, 0, n_prompt);
+        ++launches;
+        if (err == cudaSuccess) err = copy_logits(st);
+      }
+      return err;
+    };
+    cudaEventRecord(m->ev[0], ctx->stream);
+    e = phase(0, n_prompt);
+    prefill_launches = launches;
+    cudaEventRecord(m->ev[1], ctx->stream);
+    if (e == cudaSuccess) e = phase(n_prompt, steps);
+    cudaEventRecord(m->ev[2], ctx->stream);
+  }
+  auto run_step_graph = [&](uint32_t step) -> cudaError_t {
     cudaError_t err;
     if (use_graph) {
       err = cudaGraphLaunch(m->step_graph, ctx->stream);
@@ -653,21 +889,26 @@ zgpu_status zgpu_generate_greedy(zgpu_model *m, zgpu_kv *kv, const uint32_t *pro
     }
     return err;
   };
-  cudaEventRecord(m->ev[0], ctx->stream);
-  for (uint32_t st = 0; st < n_prompt && e == cudaSuccess; ++st) e = run_step(st);
-  cudaEventRecord(m->ev[1], ctx->stream);
-  for (uint32_t st = n_prompt; st < steps && e == cudaSuccess; ++st) e = run_step(st);
-  cudaEventRecord(m->ev[2], ctx->stream);
+  if (!persistent) {
+    cudaEventRecord(m->ev[0], ctx->stream);
+    for (uint32_t st = 0; st < n_prompt && e == cudaSuccess; ++st) e = run_step_graph(st);
+    prefill_launches = launches;
+    cudaEventRecord(m->ev[1], ctx->stream);
+    for (uint32_t st = n_prompt; st < steps && e == cudaSuccess; ++st) e = run_step_graph(st);
+    cudaEventRecord(m->ev[2], ctx->stream);
+  }
   if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "generate");
   e = cudaMemcpyAsync(tokens_out, m->d_tokens, n_gen * 4, cudaMemcpyDeviceToHost, ctx->stream);
   if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "tokens d2h");
   uint32_t st = 0;
   if ((s = read_status(m, &st))) return s;
+  if (persistent && (st & ZDEV_ERR_TIMEOUT)) reset_step_tags(m);
   float pre = 0.f, dec = 0.f;
   cudaEventElapsedTime(&pre, m->ev[0], m->ev[1]);
   cudaEventElapsedTime(&dec, m->ev[1], m->ev[2]);
   m->perf.steps = n_gen - 1;
   m->perf.kernel_launches = launches;
+  m->perf.decode_launches = launches - prefill_launches;
   m->perf.prefill_ms = pre;
   m->perf.decode_ms = dec;
   ctx->launches += launches;

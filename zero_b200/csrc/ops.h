@@ -57,6 +57,13 @@ struct AttnParams {
   uint32_t *status;
   uint32_t n_q, n_kv, max_splits;
   float eps, scale;
+  // tagged mode (persistent step kernel): projections and output are tagged
+  // words (version << 32 | f32 bits) instead of qkv / out
+  const unsigned long long *qkv_t;
+  unsigned long long *out_t;
+  uint32_t ver_in, ver_out;
+  volatile uint32_t *abort;         // this CTA's abort flag (shared memory)
+  uint32_t *gabort;                 // the launch's abort flag
 };
 
 cudaError_t launch_attention(const AttnParams &ap, const LaunchCfg &lc);
