@@ -14,10 +14,11 @@ JSON line on rank 0.
   e2e      the same metric through the reference-facing C ABI per token
            (zgpu_forward_single_token + zgpu_lm_head_argmax), host token in,
            host token out, host wall clock.
-  roofline the dominant kernel class (Q4_0X4 GEMV, 2048 -> 6144 per launch,
-           over the 56 gate/up tensors of the model so every launch streams
-           from HBM): algorithmic bytes / CUDA-event duration vs the measured
-           HBM copy bandwidth.
+  roofline the dominant kernel: the persistent step kernel's decode launch
+           (algorithmic bytes = steps x (1.124 GB of weights + the KV rows
+           read) over its CUDA-event duration) vs the measured HBM copy
+           bandwidth; plus the standalone Q4_0 GEMV 2048 -> 6144 over the 56
+           gate/up tensors as a secondary figure.
   cpu_baseline  the CPU oracle's AVX-512-order restatement of the reference
            decode, all host cores, on a bounded sample (rank 0, N=1 only).
 
@@ -45,9 +46,11 @@ METRIC = "decode tok/s, Qwen3-1.7B-shape Q4_0 b=1; GEMV HBM GB/s vs ~8 TB/s peak
 PUBLISHED_TOK_S = 194.5      # README.md:29 of the reference (EPYC 9354P, AVX-512, CPU only)
 PROMPT_LEN = 16
 SEED = 0
-# dram bytes (read + write) of one 2048->6144 Q4_0X4 GEMV launch, from the ncu
-# capture summarised in profiles/gemv_q4x4_2048x6144.md (None until captured).
-NCU_TRAFFIC_PER_LAUNCH = None
+# DRAM bytes (read + write) per decode step of the persistent step kernel, from
+# the ncu capture summarised in profiles/step_kernel_config0.md (None until
+# captured); the roofline's traffic is this times the steps of the launch.
+NCU_TRAFFIC_PER_STEP = 1_125_293_824
+
 
 
 def parse():
@@ -283,11 +286,21 @@ def main():
         kv2.close()
 
     # -------------------------------------- roofline of the dominant kernel
-    # Q4_0X4 GEMV 2048 -> 6144 over the ffn_gate / ffn_up tensors of every
-    # layer (56 distinct 7.08 MB tensors, 396 MB per sweep > L2).  The sweep is
-    # captured into a CUDA graph on a torch stream so host launch cost does not
-    # enter, and timed with CUDA events recorded on that stream.
+    # The decode steps run as one persistent launch (decode_launches == 1):
+    # algorithmic bytes = K steps x (weights 1.124 GB + the KV rows each step
+    # reads), duration = the CUDA-event time of that launch (decode_ms).  With
+    # the per-op kernels instead, the same bytes over the same device time give
+    # the whole-step figure.
     peaks = measured_peaks()
+    step_bytes = cfg.weight_bytes_per_token()
+    # a step at position p reads the K and V rows of tokens 0..p-1 and writes row p (f32, all layers)
+    kv_row_bytes = 2 * cfg.n_kv_heads * cfg.head_dim * 4 * cfg.n_layers
+    kv_bytes = sum(kv_row_bytes * (PROMPT_LEN + i + 1) for i in range(args.steps))
+    launch_bytes = args.steps * step_bytes + kv_bytes
+    step_gbs = launch_bytes / (dec_ms / 1000.0) / 1e9
+    # secondary: the standalone Q4_0 GEMV 2048 -> 6144 over the 56 gate/up
+    # tensors (396 MB per sweep > L2), captured into a CUDA graph on a torch
+    # stream and timed with CUDA events on that stream
     gemv_bytes = cfg.ffn * cfg.hidden * 18 // 32 + cfg.hidden * 4 + cfg.ffn * 4
     gemv_ms = None
     if not args.no_roofline:
@@ -322,8 +335,6 @@ def main():
         gemv_ms = e0.elapsed_time(e1) / (reps * len(keys))
         del graph
     gemv_gbs = gemv_bytes / (gemv_ms * 1e-3) / 1e9 if gemv_ms else None
-    step_bytes = cfg.weight_bytes_per_token()
-    step_gbs = step_bytes * (args.steps / (dec_ms / 1000.0)) / 1e9
 
     # ------------------------------------------------------- CPU baseline
     cpu = None
@@ -350,15 +361,18 @@ def main():
                        "l2": "inputs larger than L2 (1.12 GB of weights streamed per step)",
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "tokens_first": [int(v) for v in toks[:4]]},
-            "roofline": {"bound": "hbm", "kernel": "gemv_x4 Q4_0 2048->6144",
-                         "achieved": round(gemv_gbs, 1) if gemv_gbs else None,
-                         "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(gemv_gbs / peaks["hbm_gbs"], 4) if gemv_gbs else None,
-                         "peak_source": peaks["source"],
-                         "traffic": NCU_TRAFFIC_PER_LAUNCH, "algorithmic_bytes": gemv_bytes,
-                         "avg_launch_us": round(gemv_ms * 1000, 3) if gemv_ms else None,
-                         "step_hbm_gbs": round(step_gbs, 1),
-                         "step_frac": round(step_gbs / peaks["hbm_gbs"], 4)},
+            "roofline": {"bound": "hbm",
+                         "kernel": "step_kernel (persistent decode, one launch for all timed steps)"
+                                   if gpu_launches == 1 else "per-op decode kernels (whole step)",
+                         "achieved": round(step_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(step_gbs / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
+                         "traffic": (NCU_TRAFFIC_PER_STEP * args.steps) if NCU_TRAFFIC_PER_STEP else None,
+                         "algorithmic_bytes": launch_bytes,
+                         "avg_launch_us": round(dec_ms * 1000 / max(gpu_launches, 1), 1),
+                         "gemv_2048x6144": {"achieved": round(gemv_gbs, 1) if gemv_gbs else None,
+                                            "algorithmic_bytes": gemv_bytes,
+                                            "avg_launch_us": round(gemv_ms * 1000, 3) if gemv_ms else None,
+                                            "frac": round(gemv_gbs / peaks["hbm_gbs"], 4) if gemv_gbs else None}},
             "e2e": {"value": round(e2e_tok_s, 2) if e2e_tok_s else None, "unit": "tok/s",
                     "h2d_bytes_per_step": 84, "d2h_bytes_per_step": 12},
             "gpu_launches": int(gpu_launches),

@@ -21,9 +21,10 @@
 //     dim i+64, held by lane l^16); the (cos, sin) pairs come from the
 //     reference's own sincos polynomial;
 //   * the split whose range holds the current position appends k and v;
-//   * warps take runs of 4 tokens for the scores and for sum_t p_t v_t
-//     (four cache-row loads in flight per warp), then reduce across warps
-//     through shared memory in fixed order.
+//   * each warp takes runs of kAttnUnroll tokens (8, or 4 where registers
+//     are scarcer), loads their K and V rows together and keeps a running max, sum
+//     and unnormalised output per q head (online softmax); the warps' states
+//     are merged in warp order through shared memory.
 // Softmax errors follow the reference: a non-finite max or a non-positive /
 // non-finite sum flags ZDEV_ERR_NUMERICAL.  Every read of data another CTA
 // may have written during the same kernel (projections, cache rows,
@@ -42,16 +43,15 @@ constexpr int kAttnWarps = 8;
 constexpr int kAttnThreads = 32 * kAttnWarps;
 constexpr int kAttnMaxGqa = 4;
 constexpr int kAttnSplitTokens = 256;
-constexpr int kAttnUnroll = 4;           // cache rows in flight per warp
+constexpr int kAttnUnrollMax = 8;        // tokens per warp per round (K and V rows in flight)
 
 struct AttnSmem {
   float cs[kAttnHd / 2], sn[kAttnHd / 2];
   __align__(16) float qs[kAttnMaxGqa][kAttnHd];
   __align__(16) float kn[kAttnHd];
   __align__(16) float vn[kAttnHd];
-  float sc[kAttnMaxGqa][kAttnSplitTokens];
   __align__(16) float opart[kAttnWarps][kAttnMaxGqa][kAttnHd];
-  float stat[kAttnMaxGqa][2];
+  float wm[kAttnWarps][kAttnMaxGqa], wl[kAttnWarps][kAttnMaxGqa];   // per-warp running max / sum
   uint32_t s_last;
 };
 
@@ -111,7 +111,7 @@ __device__ __forceinline__ void attn_store_out(const AttnParams &p, uint32_t i, 
   else p.out[i] = v;
 }
 
-template <class Bar, bool TAGGED = false>
+template <class Bar, bool TAGGED = false, int kAttnUnroll = kAttnUnrollMax>
 __device__ __forceinline__ void attn_decode_block(const AttnParams &p, uint32_t kvh, uint32_t split,
                                                   uint32_t pos, uint32_t tid, AttnSmem &sm, Bar bar) {
   const uint32_t warp = tid >> 5, lane = tid & 31;
@@ -125,7 +125,6 @@ __device__ __forceinline__ void attn_decode_block(const AttnParams &p, uint32_t 
   const uint32_t t0 = split * kAttnSplitTokens;
   if (split >= nact) return;
   const uint32_t t1 = min(t0 + kAttnSplitTokens, total);
-  const uint32_t ntok = t1 - t0;
   const uint32_t qd = p.n_q * kAttnHd, kvd = p.n_kv * kAttnHd;
 
   // RoPE LUT for this position (rope_sincos_lut_avx512, trig.rs:148).
@@ -156,120 +155,105 @@ __device__ __forceinline__ void attn_decode_block(const AttnParams &p, uint32_t 
     vc[static_cast<size_t>(pos) * kvd + kvh * kAttnHd + tid] = sm.vn[tid];
   }
 
-  // Scores; lane holds dims 4l..4l+3.
-  float4 q[kAttnMaxGqa];
+  // Online softmax over this warp's runs of kAttnUnroll tokens; lane holds
+  // dims 4l..4l+3 of q, k, v and of the running output.
+  float4 q[kAttnMaxGqa], o[kAttnMaxGqa];
+  float m[kAttnMaxGqa], l[kAttnMaxGqa];
 #pragma unroll
-  for (int j = 0; j < kAttnMaxGqa; ++j)
+  for (int j = 0; j < kAttnMaxGqa; ++j) {
     q[j] = (j < static_cast<int>(G)) ? *reinterpret_cast<const float4 *>(&sm.qs[j][4 * lane])
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
-  // Warp w takes tokens in runs of kAttnUnroll (w * kAttnUnroll + 8 * kAttnUnroll * i ...):
-  // the run's K rows are loaded before any is used, so each warp keeps
-  // kAttnUnroll cache-row loads in flight.
+    o[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    m[j] = -INFINITY;
+    l[j] = 0.f;
+  }
   for (uint32_t tb = t0 + warp * kAttnUnroll; tb < t1; tb += kAttnWarps * kAttnUnroll) {
-    float4 kk[kAttnUnroll];
+    float4 kk[kAttnUnroll], vv[kAttnUnroll];
 #pragma unroll
     for (int u = 0; u < kAttnUnroll; ++u) {
       const uint32_t t = tb + u;
-      kk[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      kk[u] = vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (t < t1 && ZDEV_CHECK(static_cast<uint64_t>(t + 1) * kvd <= p.kv_block && t - t0 < kAttnSplitTokens,
-                               p.status, 10, t, kvh))
-        kk[u] = (t == pos) ? *reinterpret_cast<const float4 *>(&sm.kn[4 * lane])
-                           : __ldcg(reinterpret_cast<const float4 *>(
-                                 kc + static_cast<size_t>(t) * kvd + kvh * kAttnHd) + lane);
+                               p.status, 10, t, kvh)) {
+        if (t == pos) {
+          kk[u] = *reinterpret_cast<const float4 *>(&sm.kn[4 * lane]);
+          vv[u] = *reinterpret_cast<const float4 *>(&sm.vn[4 * lane]);
+        } else {
+          const size_t row = static_cast<size_t>(t) * kvd + kvh * kAttnHd;
+          kk[u] = __ldcg(reinterpret_cast<const float4 *>(kc + row) + lane);
+          vv[u] = __ldcg(reinterpret_cast<const float4 *>(vc + row) + lane);
+        }
+      }
     }
 #pragma unroll
-    for (int u = 0; u < kAttnUnroll; ++u) {
-      const uint32_t t = tb + u;
-      if (t >= t1) break;   // uniform over the warp
+    for (int j = 0; j < kAttnMaxGqa; ++j) {
+      if (j >= static_cast<int>(G)) break;
+      float sc[kAttnUnroll];
+      float mx = m[j];
 #pragma unroll
-      for (int j = 0; j < kAttnMaxGqa; ++j) {
-        if (j >= static_cast<int>(G)) break;
+      for (int u = 0; u < kAttnUnroll; ++u) {
         float d = __fmaf_rn(q[j].w, kk[u].w,
                             __fmaf_rn(q[j].z, kk[u].z, __fmaf_rn(q[j].y, kk[u].y, __fmul_rn(q[j].x, kk[u].x))));
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
-        if (lane == 0) sm.sc[j][t - t0] = __fmul_rn(d, p.scale);
+        sc[u] = (tb + u < t1) ? __fmul_rn(d, p.scale) : -INFINITY;
+        mx = fmaxf(mx, sc[u]);
       }
+      const float corr = expf(m[j] - mx);
+      float lj = l[j] * corr;
+      float4 oj = make_float4(o[j].x * corr, o[j].y * corr, o[j].z * corr, o[j].w * corr);
+#pragma unroll
+      for (int u = 0; u < kAttnUnroll; ++u) {
+        const float e = (tb + u < t1) ? expf(sc[u] - mx) : 0.f;
+        lj += e;
+        oj.x = __fmaf_rn(e, vv[u].x, oj.x);
+        oj.y = __fmaf_rn(e, vv[u].y, oj.y);
+        oj.z = __fmaf_rn(e, vv[u].z, oj.z);
+        oj.w = __fmaf_rn(e, vv[u].w, oj.w);
+      }
+      m[j] = mx;
+      l[j] = lj;
+      o[j] = oj;
     }
   }
-  bar();
-
-  // Split-local softmax statistics: warp j owns q-head j.
-  if (warp < G) {
-    float m = -INFINITY;
-    for (uint32_t t = lane; t < ntok; t += 32) m = fmaxf(m, sm.sc[warp][t]);
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    float l = 0.f;
-    for (uint32_t t = lane; t < ntok; t += 32) {
-      const float e = expf(sm.sc[warp][t] - m);
-      sm.sc[warp][t] = e;
-      l += e;
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+  for (int j = 0; j < kAttnMaxGqa; ++j) {
+    if (j >= static_cast<int>(G)) break;
+    *reinterpret_cast<float4 *>(&sm.opart[warp][j][4 * lane]) = o[j];
     if (lane == 0) {
-      sm.stat[warp][0] = m;
-      sm.stat[warp][1] = l;
+      sm.wm[warp][j] = m[j];
+      sm.wl[warp][j] = l[j];
     }
   }
   bar();
 
-  // sum_t e_t v_t over the same runs of tokens; lane holds dims 4l..4l+3.
-  float4 o[kAttnMaxGqa];
-#pragma unroll
-  for (int j = 0; j < kAttnMaxGqa; ++j) o[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (uint32_t tb = t0 + warp * kAttnUnroll; tb < t1; tb += kAttnWarps * kAttnUnroll) {
-    float4 vv[kAttnUnroll];
-#pragma unroll
-    for (int u = 0; u < kAttnUnroll; ++u) {
-      const uint32_t t = tb + u;
-      vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (t < t1)
-        vv[u] = (t == pos) ? *reinterpret_cast<const float4 *>(&sm.vn[4 * lane])
-                           : __ldcg(reinterpret_cast<const float4 *>(
-                                 vc + static_cast<size_t>(t) * kvd + kvh * kAttnHd) + lane);
-    }
-#pragma unroll
-    for (int u = 0; u < kAttnUnroll; ++u) {
-      const uint32_t t = tb + u;
-      if (t >= t1) break;   // uniform over the warp
-#pragma unroll
-      for (int j = 0; j < kAttnMaxGqa; ++j) {
-        if (j >= static_cast<int>(G)) break;
-        const float e = sm.sc[j][t - t0];
-        o[j].x = __fmaf_rn(e, vv[u].x, o[j].x);
-        o[j].y = __fmaf_rn(e, vv[u].y, o[j].y);
-        o[j].z = __fmaf_rn(e, vv[u].z, o[j].z);
-        o[j].w = __fmaf_rn(e, vv[u].w, o[j].w);
-      }
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < kAttnMaxGqa; ++j)
-    if (j < static_cast<int>(G)) *reinterpret_cast<float4 *>(&sm.opart[warp][j][4 * lane]) = o[j];
-  bar();
-
-  // Cross-warp sum in warp order; thread (j, d) finalises head j, dim d.
+  // Merge the warps' states in warp order; thread (j, d) finalises head j,
+  // dim d.  Warps without tokens carry m = -inf, l = 0, o = 0.
   const bool single = (nact == 1);
   for (uint32_t idx = tid; idx < G * kAttnHd; idx += kAttnThreads) {
     const uint32_t j = idx / kAttnHd, d = idx % kAttnHd;
-    float acc = 0.f;
+    float mm = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) acc += sm.opart[w][j][d];
-    const float m = sm.stat[j][0], l = sm.stat[j][1];
+    for (int w = 0; w < kAttnWarps; ++w) mm = fmaxf(mm, sm.wm[w][j]);
+    float ll = 0.f, acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float f = (sm.wm[w][j] == -INFINITY) ? 0.f : expf(sm.wm[w][j] - mm);
+      ll = __fmaf_rn(f, sm.wl[w][j], ll);
+      acc = __fmaf_rn(f, sm.opart[w][j][d], acc);
+    }
     const uint32_t qh = kvh * G + j;
     if (single) {
-      if (d == 0 && (!(m > -INFINITY && m < INFINITY) || !(l > 0.f) || !(l < INFINITY)))
+      if (d == 0 && (!(mm > -INFINITY && mm < INFINITY) || !(ll > 0.f) || !(ll < INFINITY)))
         atomicOr(p.status, ZDEV_ERR_NUMERICAL);
-      attn_store_out<TAGGED>(p, qh * kAttnHd + d, __fdiv_rn(acc, l));
+      attn_store_out<TAGGED>(p, qh * kAttnHd + d, __fdiv_rn(acc, ll));
     } else {
       if (!ZDEV_CHECK(qh < p.n_q && split < p.max_splits, p.status, 11, qh, split)) continue;
       float *pp = p.part + (static_cast<size_t>(qh) * p.max_splits + split) * (kAttnHd + 2);
       pp[d] = acc;
       if (d == 0) {
-        pp[kAttnHd] = m;
-        pp[kAttnHd + 1] = l;
+        pp[kAttnHd] = mm;
+        pp[kAttnHd + 1] = ll;
       }
     }
   }

@@ -410,6 +410,14 @@ zgpu_status build_step(zgpu_model *m) {
     off += tv_len[b];
     m->ver[b] = 0;
   }
+  for (StageDesc &sd : st) {
+    if (sd.kind != STG_GEMV) continue;
+    sd.tin = (sd.flags & kStageEmbed) ? nullptr : m->tv[sd.in_buf];
+    sd.tout = sd.out_buf < kStepBufs ? m->tv[sd.out_buf] : nullptr;
+  }
+  if (e == cudaSuccess)
+    e = cudaMemcpy(m->d_stages, st.data(), st.size() * sizeof(StageDesc), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "step kernel set-up");
   m->stages = st;
   m->n_layer_stages = 5 * L;
   m->lm_stage = lm;

@@ -281,7 +281,7 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
   // and the digits.
   constexpr int kXRegs = 4;
   float4 xr[kXRegs];
-  const unsigned long long *xin = EMB ? nullptr : P.tv[sd.in_buf];
+  const unsigned long long *xin = sd.tin;
   const uint32_t vin = EMB ? 0u : ver_of(c, sd.in_buf);
   if (!EMB) {
     // all of this thread's words are polled together, so the wait ends one
@@ -359,9 +359,12 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
     }
   }
   trace(16 + 2 + EPI);
-  float inv = 1.0f;
+  // RMSNorm (ops.rs:29-52) as y = inv * (W . (x * g)): the digits are taken
+  // of x * g right away and the scalar inv = 1/sqrt(mean(x^2) + eps) scales
+  // the row sums in the epilogue, so the sum of squares (fixed order: per
+  // thread over its float4s, xor-tree in the warp, warps in order) needs no
+  // barrier of its own: its per-warp parts cross the image barrier below.
   if (PRO == PRO_RMSNORM) {
-    // rmsnorm (ops.rs:29-52) with a fixed summation order
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < kXRegs; ++i) {
@@ -372,11 +375,6 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
     if (lane == 0) c.red[warp] = ss;
-    named_bar_sync(kBarConsumers, kNC);
-    float tot = 0.f;
-#pragma unroll
-    for (int w = 0; w < kNW; ++w) tot = __fadd_rn(tot, c.red[w]);
-    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(sd.in_dim)), P.eps)));
   }
 #pragma unroll
   for (int i = 0; i < kXRegs; ++i) {
@@ -387,16 +385,23 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
     float4 t = xr[i];
     if (PRO == PRO_RMSNORM && valid) {
       const float4 g = reinterpret_cast<const float4 *>(sd.norm_w)[f];
-      t.x = __fmul_rn(__fmul_rn(t.x, inv), g.x);
-      t.y = __fmul_rn(__fmul_rn(t.y, inv), g.y);
-      t.z = __fmul_rn(__fmul_rn(t.z, inv), g.z);
-      t.w = __fmul_rn(__fmul_rn(t.w, inv), g.w);
+      t.x = __fmul_rn(t.x, g.x);
+      t.y = __fmul_rn(t.y, g.y);
+      t.z = __fmul_rn(t.z, g.z);
+      t.w = __fmul_rn(t.w, g.w);
     }
     digitise_f4<QT>(t, f, valid, c.xsm, sd.bpr, P.xbytes, P.status);
   }
   named_bar_sync(kBarConsumers, kNC);
   trace(32 + 2 + EPI);
   trace_cta(0);
+  float inv = 1.0f;
+  if (PRO == PRO_RMSNORM) {
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kNW; ++w) tot = __fadd_rn(tot, c.red[w]);
+    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(sd.in_dim)), P.eps)));
+  }
 
   // ---- items: warp (k + rot) % kNW takes item k of this CTA's list
   const uint32_t nloc = u1 - u0, nitems = nloc * sd.ks;
@@ -428,7 +433,7 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
   trace_cta(1);
 
   // ---- epilogue: K-chunks in order, then per row
-  unsigned long long *xout = (EPI == EPI_ARGMAX) ? nullptr : P.tv[sd.out_buf];
+  unsigned long long *xout = sd.tout;
   const uint32_t vout = (EPI == EPI_ARGMAX) ? 0u : ver_of(c, sd.out_buf) + 1;
   unsigned long long best = kArgmaxInitKey;
   if (EPI == EPI_SWIGLU) {
@@ -440,6 +445,8 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
         yg += c.part[(ul * sd.ks + ch) * R + r];
         yu += c.part[(ul * sd.ks + ch) * R + 4 + r];
       }
+      yg = __fmul_rn(yg, inv);
+      yu = __fmul_rn(yu, inv);
       const uint32_t row = (u0 + ul) * 4 + r;
       if (row < sd.rows) xout[row] = tag_word(ref_silu_mul(yg, yu), vout);
     }
@@ -448,6 +455,7 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
       const uint32_t ul = t / R, r = t % R;
       float y = 0.f;
       for (uint32_t ch = 0; ch < sd.ks; ++ch) y += c.part[(ul * sd.ks + ch) * R + r];
+      if (PRO == PRO_RMSNORM) y = __fmul_rn(y, inv);
       const uint32_t row = (u0 + ul) * R + r;
       if (row < sd.rows) {
         if (EPI == EPI_STORE) {
@@ -623,7 +631,7 @@ __device__ __forceinline__ void consumer(const StepParams &P, Ctx &c) {
             ap.ver_out = c.v_attn + 1;
             ap.abort = c.abort;
             ap.gabort = &P.bar[1];
-            attn_decode_block<AttnBar, true>(ap, blockIdx.x % P.n_kv, blockIdx.x / P.n_kv, pos, tid,
+            attn_decode_block<AttnBar, true, 4>(ap, blockIdx.x % P.n_kv, blockIdx.x / P.n_kv, pos, tid,
                                              *reinterpret_cast<AttnSmem *>(c.xsm), AttnBar());
           }
           ++c.v_attn;

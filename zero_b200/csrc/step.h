@@ -32,6 +32,8 @@ struct StageDesc {
   uint64_t gstride, wbytes;
   const float *norm_w;              // PRO_RMSNORM gain
   float *out;                       // plain f32 output (the LM head's logits)
+  const unsigned long long *tin;    // tagged input vector (in_buf), or null
+  unsigned long long *tout;         // tagged output vector (out_buf), or null
   const float *q_norm, *k_norm;     // STG_ATTN
 };
 
