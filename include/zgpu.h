@@ -274,6 +274,111 @@ typedef struct zgpu_perf {
 } zgpu_perf;
 zgpu_status zgpu_perf_snapshot(const zgpu_model *m, zgpu_perf *out);
 
+/* ------------------------------------------- DeepSeek2: MoE routing */
+/* MoeRoutingMode (crates/zero-llm-inference/src/moe.rs:55). */
+#define ZGPU_ROUTE_SOFTMAX 0u
+#define ZGPU_ROUTE_SIGMOID_NORMALIZE 1u
+/* moe_route_f32 (moe.rs:132-317) on the GPU with host buffers: scores s_e =
+ * sequential f32 dot(hidden, router row e) in the reference's order (+ bias
+ * in Softmax mode; sigmoid in SigmoidNormalize mode), top-k by replacement of
+ * the current minimum with a strict `>` (slot order, not sorted), weights =
+ * softmax (or normalisation) over the selected k, the uniform 1/k fallback,
+ * then expert_weight_scale.  Expert ids are bit-identical to the
+ * reference's; weights agree to the rounding of expf.  router_key is a
+ * registered ZGPU_F32 tensor [n_experts x dim]; router_bias (host, n_experts
+ * floats) and scores_out (n_experts floats) may be NULL.  Where the
+ * reference panics (top_k == 0 or top_k > n_experts) this returns
+ * ZGPU_ERR_INVALID_ARG; top_k is at most 16 and dim at most 8192. */
+zgpu_status zgpu_moe_route_f32(zgpu_ctx *ctx, const float *hidden, const void *router_key,
+                               const float *router_bias, uint64_t dim, uint32_t n_experts,
+                               uint32_t top_k, uint32_t mode, float expert_weight_scale,
+                               float *scores_out, uint32_t *indices_out, float *weights_out);
+
+/* ------------------------------------------------- DeepSeek2: MLA cache */
+typedef struct zgpu_mla_kv zgpu_mla_kv;
+/* MlaKvCache::new (kv_cache.rs:257-305): per layer max_tokens rows of
+ * [kv_lora_rank | rope_dim] f32 (the normalised latent and the rotated
+ * k_rope) in device memory. */
+zgpu_status zgpu_mla_kv_create(zgpu_ctx *ctx, uint32_t max_tokens, uint32_t n_layers,
+                               uint32_t kv_lora_rank, uint32_t rope_dim, zgpu_mla_kv **out);
+void zgpu_mla_kv_destroy(zgpu_mla_kv *kv);
+/* store_compressed (kv_cache.rs:318-360): c_kv [kv_lora_rank], k_rope
+ * [rope_dim] (host). Errors: LayerOutOfRange, TokenIndexOutOfRange. */
+zgpu_status zgpu_mla_kv_store(zgpu_mla_kv *kv, uint32_t layer, uint32_t token, const float *c_kv,
+                              const float *k_rope);
+/* get_c_kv / get_k_rope (kv_cache.rs:362-407) for tokens [0, token_count):
+ * token_count rows of kv_lora_rank + rope_dim floats copied to host. */
+zgpu_status zgpu_mla_kv_read(zgpu_mla_kv *kv, uint32_t layer, uint32_t token_count,
+                             float *rows_out);
+
+/* ------------------------------------------------- DeepSeek2 model */
+typedef struct zgpu_ds2_model zgpu_ds2_model;
+/* One layer (Deepseek2LayerWeights, forward_pass.rs:640-700).  Matmul
+ * tensors are registered keys (Q4_0 or Q8_0 = attn_quant, plain or X4);
+ * norms are host f32 arrays copied at creation.  MLA: kv_b holds per head
+ * nope rows then v rows; or k_b / v_b (both non-NULL) hold them split
+ * (mla.rs:251-275).  Dense layers (moe == 0) use ffn_gate/up/down; MoE layers
+ * use router_w (registered ZGPU_F32 [n_experts x hidden]), router_b (host,
+ * nullable), the stacked experts gate_exps/up_exps [n_experts*expert_ffn x
+ * hidden] and down_exps [n_experts*hidden x expert_ffn], and the stacked
+ * shared experts (n_shared of width expert_ffn, same layout). */
+typedef struct zgpu_ds2_layer {
+  const float *attn_norm, *ffn_norm;
+  const void *kv_a_mqa;          /* [kv_lora + rope] x hidden */
+  const float *kv_a_norm;        /* [kv_lora] */
+  const void *kv_b;              /* [n_heads*(nope+v)] x kv_lora, or NULL with k_b/v_b */
+  const void *k_b, *v_b;
+  const void *q_a;               /* q_lora x hidden */
+  const float *q_a_norm;         /* [q_lora] */
+  const void *q_b;               /* [n_heads*(nope+rope)] x q_lora */
+  const void *attn_output;       /* hidden x [n_heads*v] */
+  const float *k_norm;           /* [rope] or NULL */
+  uint32_t moe;
+  const void *ffn_gate, *ffn_up, *ffn_down;
+  const void *router_w;
+  const float *router_b;
+  const void *gate_exps, *up_exps, *down_exps;
+  const void *gate_shexp, *up_shexp, *down_shexp;
+} zgpu_ds2_layer;
+
+typedef struct zgpu_ds2_desc {
+  uint32_t n_layers, hidden, ffn, n_heads;
+  uint32_t kv_lora_rank, q_lora_rank, nope_dim, rope_dim, v_dim;
+  uint32_t n_experts, top_k, expert_ffn, n_shared;
+  uint32_t vocab_padded, vocab_real;
+  float rms_eps, rope_theta;
+  uint32_t route_mode;           /* ZGPU_ROUTE_* */
+  float expert_weight_scale;
+  uint32_t attn_quant;           /* ZGPU_Q4_0 or ZGPU_Q8_0: every matmul of the layers */
+  uint32_t token_embd_quant;     /* ZGPU_Q8_0 or ZGPU_Q4_0 */
+  const void *token_embd;
+  uint32_t output_quant;
+  const void *output;
+  const float *output_norm;
+  const zgpu_ds2_layer *layers;
+} zgpu_ds2_desc;
+
+zgpu_status zgpu_ds2_create(zgpu_ctx *ctx, const zgpu_ds2_desc *desc, zgpu_ds2_model **out);
+void zgpu_ds2_destroy(zgpu_ds2_model *m);
+/* forward_single_token_deepseek2 (forward_pass.rs:703-909) for MLA layers:
+ * per layer rmsnorm -> MLA (mla.rs:122-414, with the kv_b projection
+ * absorbed into the query and the output: same results to f32 rounding)
+ * -> residual -> rmsnorm -> dense SwiGLU or moe_ffn -> residual. */
+zgpu_status zgpu_ds2_forward_single_token(zgpu_ds2_model *m, zgpu_mla_kv *kv, uint32_t token,
+                                          uint32_t pos, float *hidden_out);
+/* lm_head_argmax_dynamic (lm_head.rs:98-166) on the model's hidden state. */
+zgpu_status zgpu_ds2_lm_head_argmax(zgpu_ds2_model *m, uint32_t vocab_real, uint32_t *token_out,
+                                    float *logits_out);
+/* Expert ids / weights each MoE layer routed to in the last forward:
+ * [n_layers][top_k] each (zeros for dense layers); either may be NULL. */
+zgpu_status zgpu_ds2_expert_ids(zgpu_ds2_model *m, uint32_t *ids_out, float *weights_out);
+/* Prompt prefill + n_gen greedy steps as zgpu_generate_greedy; the step is
+ * one CUDA graph replay with the token chained on the device. */
+zgpu_status zgpu_ds2_generate_greedy(zgpu_ds2_model *m, zgpu_mla_kv *kv, const uint32_t *prompt,
+                                     uint32_t n_prompt, uint32_t n_gen, uint32_t *tokens_out,
+                                     float *logits_out);
+zgpu_status zgpu_ds2_perf_snapshot(const zgpu_ds2_model *m, zgpu_perf *out);
+
 /* ------------------------------------------ synthetic .smodel generation */
 /* Deterministic seeded tensors for the BASELINE configs (counter-based
  * SplitMix64, so any sub-range is reproducible).  Blocks are written in the

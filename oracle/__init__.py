@@ -33,7 +33,8 @@ def build() -> Path:
 
 
 def _load() -> C.CDLL:
-    if not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < (HERE / "zoracle.c").stat().st_mtime:
+    srcs = [HERE / "zoracle.c", HERE / "zoracle_ds2.c", HERE / "zoracle.h"]
+    if not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < max(p.stat().st_mtime for p in srcs):
         build()
     lib = C.CDLL(str(LIB_PATH))
     sz = C.c_size_t
@@ -75,6 +76,21 @@ def _load() -> C.CDLL:
         "zo_run_lm_head": (C.c_int, [C.c_void_p, _u32p, _f32p]),
         "zo_run_kv": (_f32p, [C.c_void_p]),
         "zo_run_generate": (C.c_int, [C.c_void_p, _u32p, C.c_uint32, C.c_uint32, _u32p, _f32p, _f32p]),
+        "zo_moe_route_f32": (C.c_int, [_f32p, sz, _f32p, _f32p, sz, sz, _f32p, _u32p, _f32p, C.c_int, C.c_float]),
+        "zo_expert_swiglu": (C.c_int, [_f32p, _u8p, _u8p, _u8p, sz, sz, C.c_int, _f32p, _f32p]),
+        "zo_moe_ffn": (C.c_int, [_f32p, _f32p, _f32p, _u8p, _u8p, _u8p, _u8p, _u8p, _u8p, sz, sz, sz, sz,
+                                 sz, C.c_int, C.c_int, C.c_float, _f32p, _u32p, _f32p, _f32p]),
+        "zo_mla_work_floats": (sz, [C.c_void_p, C.c_uint32]),
+        "zo_mla_attention": (C.c_int, [_f32p, C.c_void_p, C.c_void_p, _f32p, C.c_uint32, C.c_uint32, _f32p,
+                                       _f32p]),
+        "zo_ds2_run_create": (C.c_void_p, [C.c_void_p, C.c_uint32]),
+        "zo_ds2_run_destroy": (None, [C.c_void_p]),
+        "zo_ds2_run_forward": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, _f32p]),
+        "zo_ds2_run_lm_head": (C.c_int, [C.c_void_p, _u32p, _f32p]),
+        "zo_ds2_run_generate": (C.c_int, [C.c_void_p, _u32p, C.c_uint32, C.c_uint32, _u32p, _f32p, _f32p]),
+        "zo_ds2_run_cache": (_f32p, [C.c_void_p]),
+        "zo_ds2_run_expert_ids": (_u32p, [C.c_void_p]),
+        "zo_ds2_run_expert_weights": (_f32p, [C.c_void_p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -359,4 +375,185 @@ class OracleRun:
         logits = np.zeros((n_gen, self.cfg.vocab_padded), np.float32) if want_logits else None
         rc = LIB.zo_run_generate(self._r, _u(p), p.size, n_gen, _u(toks), _f(margins),
                                  _f(logits) if want_logits else None)
+        return rc, toks, margins, logits
+
+
+# ------------------------------------------------------------ DeepSeek2
+ROUTE_SOFTMAX, ROUTE_SIGMOID_NORMALIZE = 0, 1
+
+
+def _fopt(a):
+    return None if a is None else _f(np.ascontiguousarray(a, np.float32))
+
+
+def moe_route_f32(hidden, router_w, n_experts: int, top_k: int, mode: int = ROUTE_SOFTMAX,
+                  expert_weight_scale: float = 1.0, router_bias=None):
+    """moe_route_f32 (moe.rs:132-317).  Returns (rc, ids, weights, scores)."""
+    x = np.ascontiguousarray(hidden, np.float32)
+    w = np.ascontiguousarray(router_w, np.float32)
+    b = None if router_bias is None else np.ascontiguousarray(router_bias, np.float32)
+    scores = np.zeros(max(n_experts, 1), np.float32)
+    ids = np.zeros(max(top_k, 1), np.uint32)
+    wts = np.zeros(max(top_k, 1), np.float32)
+    rc = LIB.zo_moe_route_f32(_f(x), x.size, _f(w), None if b is None else _f(b), n_experts, top_k,
+                              _f(scores), _u(ids), _f(wts), mode, expert_weight_scale)
+    return rc, ids[:top_k], wts[:top_k], scores[:n_experts]
+
+
+def expert_swiglu(x, gate, up, down, dim: int, inter: int, quant: int = Q4_0) -> np.ndarray:
+    """expert_swiglu (moe.rs:345-397) on plain blocks."""
+    x = np.ascontiguousarray(x, np.float32)
+    work = np.zeros(3 * inter, np.float32)
+    out = np.zeros(dim, np.float32)
+    rc = LIB.zo_expert_swiglu(_f(x), _b(gate), _b(up), _b(down), dim, inter, quant, _f(work), _f(out))
+    if rc:
+        raise ValueError(f"expert_swiglu failed: {rc}")
+    return out
+
+
+def moe_ffn(x, lw: dict, cfg, quant: int = Q4_0):
+    """moe_ffn (moe.rs:486-590) over one synth.ds2_weights() layer dict.
+    Returns (rc, out, ids, weights)."""
+    x = np.ascontiguousarray(x, np.float32)
+    H, EF, E, K, NS = cfg.hidden, cfg.expert_ffn, cfg.n_experts, cfg.top_k, cfg.n_shared
+    work = np.zeros(E + 3 * EF + H, np.float32)
+    ids = np.zeros(K, np.uint32)
+    wts = np.zeros(K, np.float32)
+    out = np.zeros(H, np.float32)
+    empty = np.zeros(1, np.uint8)
+    rc = LIB.zo_moe_ffn(_f(x), _f(lw["router_w"]), _fopt(lw.get("router_b")), _b(lw["gate_exps"]),
+                        _b(lw["up_exps"]), _b(lw["down_exps"]), _b(lw.get("gate_shexp", empty)),
+                        _b(lw.get("up_shexp", empty)), _b(lw.get("down_shexp", empty)), NS, E, K, H, EF,
+                        quant, cfg.route_mode, cfg.expert_weight_scale, _f(work), _u(ids), _f(wts), _f(out))
+    return rc, out, ids, wts
+
+
+class _MlaDims(C.Structure):
+    _fields_ = [("hidden", C.c_uint32), ("n_heads", C.c_uint32), ("kv_lora_rank", C.c_uint32),
+                ("q_lora_rank", C.c_uint32), ("nope_dim", C.c_uint32), ("rope_dim", C.c_uint32),
+                ("v_dim", C.c_uint32), ("quant", C.c_int), ("eps", C.c_float), ("rope_base", C.c_float)]
+
+
+class _MlaWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("kv_a_mqa", "kv_a_norm", "kv_b", "k_b", "v_b", "q_a", "q_a_norm",
+                                          "q_b", "output", "k_norm")]
+
+
+class _Ds2Layer(C.Structure):
+    _fields_ = [("attn_norm", C.c_void_p), ("ffn_norm", C.c_void_p), ("mla", _MlaWeights), ("moe", C.c_int),
+                ("ffn_gate", C.c_void_p), ("ffn_up", C.c_void_p), ("ffn_down", C.c_void_p),
+                ("router_w", C.c_void_p), ("router_b", C.c_void_p), ("gate_exps", C.c_void_p),
+                ("up_exps", C.c_void_p), ("down_exps", C.c_void_p), ("gate_shexp", C.c_void_p),
+                ("up_shexp", C.c_void_p), ("down_shexp", C.c_void_p)]
+
+
+class _Ds2(C.Structure):
+    _fields_ = [("n_layers", C.c_uint32), ("ffn", C.c_uint32), ("n_experts", C.c_uint32),
+                ("top_k", C.c_uint32), ("expert_ffn", C.c_uint32), ("n_shared", C.c_uint32),
+                ("vocab_padded", C.c_uint32), ("vocab_real", C.c_uint32), ("mla", _MlaDims),
+                ("route_mode", C.c_int), ("expert_weight_scale", C.c_float), ("token_embd_quant", C.c_int),
+                ("token_embd", C.c_void_p), ("output_quant", C.c_int), ("output", C.c_void_p),
+                ("output_norm", C.c_void_p), ("layers", C.POINTER(_Ds2Layer))]
+
+
+def _addr(d: dict, name: str):
+    a = d.get(name)
+    return None if a is None else a.ctypes.data
+
+
+def _mla_dims(cfg) -> _MlaDims:
+    return _MlaDims(cfg.hidden, cfg.n_heads, cfg.kv_lora_rank, cfg.q_lora_rank, cfg.nope_dim, cfg.rope_dim,
+                    cfg.v_dim, Q4_0, cfg.rms_eps, cfg.rope_theta)
+
+
+def _mla_weights(lw: dict) -> _MlaWeights:
+    return _MlaWeights(*[_addr(lw, n) for n in ("kv_a_mqa", "kv_a_norm", "kv_b", "k_b", "v_b", "q_a",
+                                                 "q_a_norm", "q_b", "attn_output", "k_norm")])
+
+
+def mla_attention(x, lw: dict, cfg, cache_layer: np.ndarray, pos: int):
+    """mla_attention_single_token (mla.rs:122-414) for one layer; cache_layer
+    ([max_tokens, kv_lora + rope] f32) is updated in place.  Returns (rc, out)."""
+    x = np.ascontiguousarray(x, np.float32)
+    assert cache_layer.dtype == np.float32 and cache_layer.flags.c_contiguous
+    max_tokens = cache_layer.shape[0]
+    dims = _mla_dims(cfg)
+    w = _mla_weights(lw)
+    work = np.zeros(LIB.zo_mla_work_floats(C.byref(dims), max_tokens), np.float32)
+    out = np.zeros(cfg.hidden, np.float32)
+    rc = LIB.zo_mla_attention(_f(x), C.byref(w), C.byref(dims), _f(cache_layer), pos, max_tokens, _f(work),
+                              _f(out))
+    return rc, out
+
+
+class OracleDs2Run:
+    """A DeepSeek2-shaped decode run on the CPU oracle (scalar crate order,
+    forward_pass.rs:703-909), over synth.ds2_weights() tensors."""
+
+    def __init__(self, cfg, weights, max_tokens: int):
+        self._keep = weights
+        self.cfg = cfg
+        self.max_tokens = max_tokens
+        L = cfg.n_layers
+        self._layers = (_Ds2Layer * L)()
+        for i in range(L):
+            lw = weights["layers"][i]
+            ly = self._layers[i]
+            ly.attn_norm = _addr(lw, "attn_norm")
+            ly.ffn_norm = _addr(lw, "ffn_norm")
+            ly.mla = _mla_weights(lw)
+            ly.moe = 1 if cfg.is_moe(i) else 0
+            for n in ("ffn_gate", "ffn_up", "ffn_down", "router_w", "router_b", "gate_exps", "up_exps",
+                      "down_exps", "gate_shexp", "up_shexp", "down_shexp"):
+                setattr(ly, n, _addr(lw, n))
+        self._m = _Ds2(cfg.n_layers, cfg.ffn, cfg.n_experts, cfg.top_k, cfg.expert_ffn, cfg.n_shared,
+                       cfg.vocab_padded, cfg.vocab_real, _mla_dims(cfg), cfg.route_mode, cfg.expert_weight_scale,
+                       Q8_0 if cfg.embd_quant == "q8_0" else Q4_0, weights["token_embd"].ctypes.data,
+                       Q8_0 if cfg.output_quant == "q8_0" else Q4_0, weights["output"].ctypes.data,
+                       weights["output_norm"].ctypes.data, self._layers)
+        self._r = LIB.zo_ds2_run_create(C.byref(self._m), max_tokens)
+        if not self._r:
+            raise MemoryError("oracle ds2 run allocation failed")
+
+    def close(self):
+        if self._r:
+            LIB.zo_ds2_run_destroy(self._r)
+            self._r = None
+
+    def __del__(self):
+        self.close()
+
+    def forward(self, token: int, pos: int) -> np.ndarray:
+        h = np.zeros(self.cfg.hidden, np.float32)
+        rc = LIB.zo_ds2_run_forward(self._r, token, pos, _f(h))
+        if rc:
+            raise RuntimeError(f"oracle ds2 forward failed: {rc}")
+        return h
+
+    def lm_head(self):
+        logits = np.zeros(self.cfg.vocab_padded, np.float32)
+        tok = C.c_uint32(0)
+        rc = LIB.zo_ds2_run_lm_head(self._r, C.byref(tok), _f(logits))
+        return rc, tok.value, logits
+
+    def cache(self) -> np.ndarray:
+        c = self.cfg
+        n = c.n_layers * self.max_tokens * (c.kv_lora_rank + c.rope_dim)
+        return np.ctypeslib.as_array(LIB.zo_ds2_run_cache(self._r), shape=(n,)).copy().reshape(
+            c.n_layers, self.max_tokens, c.kv_lora_rank + c.rope_dim)
+
+    def expert_ids(self):
+        c = self.cfg
+        n = c.n_layers * c.top_k
+        ids = np.ctypeslib.as_array(LIB.zo_ds2_run_expert_ids(self._r), shape=(n,)).copy()
+        wts = np.ctypeslib.as_array(LIB.zo_ds2_run_expert_weights(self._r), shape=(n,)).copy()
+        return ids.reshape(c.n_layers, c.top_k), wts.reshape(c.n_layers, c.top_k)
+
+    def generate(self, prompt, n_gen: int, want_logits: bool = False):
+        p = np.ascontiguousarray(prompt, np.uint32)
+        toks = np.zeros(n_gen, np.uint32)
+        margins = np.zeros(n_gen, np.float32)
+        logits = np.zeros((n_gen, self.cfg.vocab_padded), np.float32) if want_logits else None
+        rc = LIB.zo_ds2_run_generate(self._r, _u(p), p.size, n_gen, _u(toks), _f(margins),
+                                     _f(logits) if want_logits else None)
         return rc, toks, margins, logits

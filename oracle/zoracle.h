@@ -156,6 +156,90 @@ const float *zo_run_kv(const zo_run *r);
 int     zo_run_generate(zo_run *r, const uint32_t *prompt, uint32_t n_prompt, uint32_t n_gen,
                         uint32_t *tokens_out, float *margins_out, float *logits_all);
 
+/* ---- DeepSeek2: MoE routing / experts / MLA (zoracle_ds2.c) ---------------- */
+/* MoeRoutingMode (moe.rs:55). */
+enum { ZO_ROUTE_SOFTMAX = 0, ZO_ROUTE_SIGMOID_NORMALIZE = 1 };
+
+/* moe.rs:132-317.  router_w f32 [n_experts x dim]; router_bias nullable. */
+int zo_moe_route_f32(const float *hidden, size_t dim, const float *router_w,
+                     const float *router_bias, size_t n_experts, size_t top_k, float *score_buf,
+                     uint32_t *indices, float *weights, int mode, float expert_weight_scale);
+/* moe.rs:345-397; work 3 * inter floats. */
+int zo_expert_swiglu(const float *x, const uint8_t *gate_w, const uint8_t *up_w,
+                     const uint8_t *down_w, size_t dim, size_t inter, int quant, float *work,
+                     float *out);
+/* moe.rs:486-590 with n_shared stacked shared experts of width inter (1 is
+ * the reference's case); work n_experts + 3 * inter + dim floats. */
+int zo_moe_ffn(const float *x, const float *router_w, const float *router_bias,
+               const uint8_t *gate_exps, const uint8_t *up_exps, const uint8_t *down_exps,
+               const uint8_t *gate_sh, const uint8_t *up_sh, const uint8_t *down_sh,
+               size_t n_shared, size_t n_experts, size_t top_k, size_t dim, size_t inter,
+               int quant, int mode, float expert_weight_scale, float *work, uint32_t *ids_out,
+               float *weights_out, float *out);
+
+typedef struct zo_mla_dims {
+  uint32_t hidden, n_heads, kv_lora_rank, q_lora_rank, nope_dim, rope_dim, v_dim;
+  int      quant;        /* attn_quant: ZO_Q4_0 or ZO_Q8_0 (plain rows) */
+  float    eps, rope_base;
+} zo_mla_dims;
+
+/* MlaWeights (mla.rs:47-58); plain row-major blocks. */
+typedef struct zo_mla_weights {
+  const uint8_t *kv_a_mqa;   /* [kv_lora + rope] x hidden */
+  const float   *kv_a_norm;  /* [kv_lora] */
+  const uint8_t *kv_b;       /* [n_heads * (nope + v)] x kv_lora (per head: nope rows, then v rows) */
+  const uint8_t *k_b, *v_b;  /* optional split form: [n_heads*nope] x kv_lora, [n_heads*v] x kv_lora */
+  const uint8_t *q_a;        /* q_lora x hidden */
+  const float   *q_a_norm;   /* [q_lora] */
+  const uint8_t *q_b;        /* [n_heads * (nope + rope)] x q_lora */
+  const uint8_t *output;     /* hidden x [n_heads * v] */
+  const float   *k_norm;     /* [rope] or NULL */
+} zo_mla_weights;
+
+size_t zo_mla_work_floats(const zo_mla_dims *d, uint32_t max_tokens);
+/* mla.rs:122-414; cache_layer = [max_tokens][kv_lora | rope] of this layer. */
+int zo_mla_attention(const float *x, const zo_mla_weights *w, const zo_mla_dims *d,
+                     float *cache_layer, uint32_t pos, uint32_t max_tokens, float *work,
+                     float *out);
+
+typedef struct zo_ds2_layer {
+  const float   *attn_norm, *ffn_norm;   /* [hidden] */
+  zo_mla_weights mla;
+  int            moe;                    /* 0: dense SwiGLU FFN */
+  const uint8_t *ffn_gate, *ffn_up, *ffn_down;            /* dense: [ffn x hidden], [hidden x ffn] */
+  const float   *router_w, *router_b;                     /* f32 [n_experts x hidden], bias nullable */
+  const uint8_t *gate_exps, *up_exps, *down_exps;         /* stacked [n_experts][inter x hidden] ... */
+  const uint8_t *gate_shexp, *up_shexp, *down_shexp;      /* stacked [n_shared][...] */
+} zo_ds2_layer;
+
+typedef struct zo_ds2 {
+  uint32_t n_layers, ffn, n_experts, top_k, expert_ffn, n_shared;
+  uint32_t vocab_padded, vocab_real;
+  zo_mla_dims mla;
+  int      route_mode;
+  float    expert_weight_scale;
+  int      token_embd_quant;   /* plain rows */
+  const uint8_t *token_embd;
+  int      output_quant;
+  const uint8_t *output;       /* plain [vocab x hidden] */
+  const float   *output_norm;
+  const zo_ds2_layer *layers;
+} zo_ds2;
+
+typedef struct zo_ds2_run zo_ds2_run;
+zo_ds2_run *zo_ds2_run_create(const zo_ds2 *m, uint32_t max_tokens);
+void    zo_ds2_run_destroy(zo_ds2_run *r);
+/* forward_pass.rs:703-909 */
+int     zo_ds2_run_forward(zo_ds2_run *r, uint32_t token, uint32_t pos, float *hidden_out);
+int     zo_ds2_run_lm_head(zo_ds2_run *r, uint32_t *token_out, float *logits_out);
+int     zo_ds2_run_generate(zo_ds2_run *r, const uint32_t *prompt, uint32_t n_prompt,
+                            uint32_t n_gen, uint32_t *tokens_out, float *margins_out,
+                            float *logits_all);
+const float    *zo_ds2_run_cache(const zo_ds2_run *r);
+/* [n_layers][top_k] expert ids / weights chosen by the last forward (0 for dense layers). */
+const uint32_t *zo_ds2_run_expert_ids(const zo_ds2_run *r);
+const float    *zo_ds2_run_expert_weights(const zo_ds2_run *r);
+
 #ifdef __cplusplus
 }
 #endif

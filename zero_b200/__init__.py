@@ -14,13 +14,14 @@ import ctypes as C
 
 import numpy as np
 
-from ._lib import LIB, ZgpuOpts, ZgpuPerf, ZgpuQwen3Desc, ZgpuQwen3Layer
+from ._lib import LIB, ZgpuDs2Desc, ZgpuDs2Layer, ZgpuOpts, ZgpuPerf, ZgpuQwen3Desc, ZgpuQwen3Layer
 from . import synth
-from .synth import QWEN3_1_7B, Qwen3Config
+from .synth import DS2_V2_LITE, QWEN3_1_7B, Ds2Config, Qwen3Config
 
 ABI_VERSION = 1
 F32, F16, Q4_0, Q8_0, Q4_0X4, Q8_0X4 = 0, 1, 2, 8, 100, 101
 FLAG_NO_GRAPH, FLAG_NO_PDL, FLAG_NO_PERSISTENT = 0x1, 0x2, 0x4
+ROUTE_SOFTMAX, ROUTE_SIGMOID_NORMALIZE = 0, 1
 
 STATUS = {
     0: "OK", 1: "INVALID_ARG", 2: "UNSUPPORTED_QUANT", 3: "UNREGISTERED_WEIGHT",
@@ -149,6 +150,24 @@ class Context:
         return out
 
 
+    # ------------------------------------------------------- MoE routing
+    def moe_route_f32(self, hidden: np.ndarray, router, n_experts: int, top_k: int,
+                      mode: int = ROUTE_SOFTMAX, expert_weight_scale: float = 1.0,
+                      router_bias: np.ndarray | None = None):
+        """moe_route_f32 (moe.rs:132-317) with a registered f32 router.
+        Returns (indices u32[top_k], weights f32[top_k], scores f32[n_experts])."""
+        x = np.ascontiguousarray(hidden, np.float32)
+        key = router if isinstance(router, int) else _ptr(router)
+        b = None if router_bias is None else np.ascontiguousarray(router_bias, np.float32)
+        idx = np.empty(top_k, np.uint32)
+        wts = np.empty(top_k, np.float32)
+        scores = np.empty(max(n_experts, 1), np.float32)
+        self._check(LIB.zgpu_moe_route_f32(self.h, _ptr(x), key, None if b is None else _ptr(b), x.size,
+                                           n_experts, top_k, mode, expert_weight_scale, _ptr(scores),
+                                           _ptr(idx), _ptr(wts)))
+        return idx, wts, scores[:n_experts]
+
+
 class KvCache:
     """KvCache::new (kv_cache.rs:100) in device memory, same logical layout."""
 
@@ -268,5 +287,112 @@ class Qwen3Model:
                 "prefill_ms": p.prefill_ms, "decode_launches": p.decode_launches}
 
 
+class MlaKvCache:
+    """MlaKvCache::new (kv_cache.rs:257-305) in device memory: per layer
+    max_tokens rows of [kv_lora_rank | rope_dim] f32."""
+
+    def __init__(self, ctx: Context, max_tokens: int, n_layers: int, kv_lora_rank: int, rope_dim: int):
+        self.ctx = ctx
+        self.max_tokens, self.n_layers, self.kv_lora_rank, self.rope_dim = max_tokens, n_layers, kv_lora_rank, rope_dim
+        h = C.c_void_p()
+        ctx._check(LIB.zgpu_mla_kv_create(ctx.h, max_tokens, n_layers, kv_lora_rank, rope_dim, C.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            LIB.zgpu_mla_kv_destroy(self.h)
+            self.h = None
+
+    def store_compressed(self, layer: int, token: int, c_kv: np.ndarray, k_rope: np.ndarray):
+        c = np.ascontiguousarray(c_kv, np.float32)
+        k = np.ascontiguousarray(k_rope, np.float32)
+        if c.size != self.kv_lora_rank or k.size != self.rope_dim:
+            raise ZgpuError(12, "store_compressed: slice length differs from the cache geometry")
+        self.ctx._check(LIB.zgpu_mla_kv_store(self.h, layer, token, _ptr(c), _ptr(k)))
+
+    def read(self, layer: int, token_count: int) -> np.ndarray:
+        out = np.empty((token_count, self.kv_lora_rank + self.rope_dim), np.float32)
+        self.ctx._check(LIB.zgpu_mla_kv_read(self.h, layer, token_count, _ptr(out)))
+        return out
+
+
+class Ds2Model:
+    """A DeepSeek2-shaped (MLA + MoE) model on the device, built from
+    synth.ds2_weights() tensors (plain Q4_0 blocks; routers registered f32)."""
+
+    def __init__(self, ctx: Context, cfg: Ds2Config, weights: dict):
+        self.ctx, self.cfg, self.w = ctx, cfg, weights
+        H = cfg.hidden
+        eq = Q8_0 if cfg.embd_quant == "q8_0" else Q4_0
+        oq = Q8_0 if cfg.output_quant == "q8_0" else Q4_0
+        emb_key = ctx.register(weights["token_embd"], eq, cfg.vocab_padded, H)
+        out_key = ctx.register(weights["output"], oq, cfg.vocab_padded, H)
+        self._layers = (ZgpuDs2Layer * cfg.n_layers)()
+        for i, lw in enumerate(weights["layers"]):
+            L = self._layers[i]
+            for name, (rows, cols) in synth.ds2_layer_shapes(cfg, i).items():
+                setattr(L, name, ctx.register(lw[name], Q4_0, rows, cols))
+            for name in ("attn_norm", "ffn_norm", "kv_a_norm", "q_a_norm", "k_norm", "router_b"):
+                if name in lw:
+                    setattr(L, name, _ptr(lw[name]))
+            if cfg.is_moe(i):
+                L.moe = 1
+                L.router_w = ctx.register(lw["router_w"], F32, cfg.n_experts, H)
+        desc = ZgpuDs2Desc(
+            cfg.n_layers, H, cfg.ffn, cfg.n_heads, cfg.kv_lora_rank, cfg.q_lora_rank, cfg.nope_dim,
+            cfg.rope_dim, cfg.v_dim, cfg.n_experts, cfg.top_k, cfg.expert_ffn, cfg.n_shared,
+            cfg.vocab_padded, cfg.vocab_real, cfg.rms_eps, cfg.rope_theta, cfg.route_mode,
+            cfg.expert_weight_scale, Q4_0, eq, emb_key, oq, out_key, _ptr(weights["output_norm"]),
+            self._layers)
+        h = C.c_void_p()
+        ctx._check(LIB.zgpu_ds2_create(ctx.h, C.byref(desc), C.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            LIB.zgpu_ds2_destroy(self.h)
+            self.h = None
+
+    def new_kv(self, max_tokens: int) -> MlaKvCache:
+        c = self.cfg
+        return MlaKvCache(self.ctx, max_tokens, c.n_layers, c.kv_lora_rank, c.rope_dim)
+
+    def forward_single_token(self, kv: MlaKvCache, token: int, pos: int) -> np.ndarray:
+        hidden = np.empty(self.cfg.hidden, np.float32)
+        self.ctx._check(LIB.zgpu_ds2_forward_single_token(self.h, kv.h, token, pos, _ptr(hidden)))
+        return hidden
+
+    def lm_head_argmax(self, vocab_real: int | None = None, want_logits: bool = True):
+        tok = C.c_uint32()
+        logits = np.empty(self.cfg.vocab_padded, np.float32) if want_logits else None
+        self.ctx._check(LIB.zgpu_ds2_lm_head_argmax(
+            self.h, self.cfg.vocab_real if vocab_real is None else vocab_real, C.byref(tok),
+            _ptr(logits) if want_logits else None))
+        return tok.value, logits
+
+    def expert_ids(self):
+        """[n_layers][top_k] expert ids and weights of the last forward (zeros for dense layers)."""
+        k = self.cfg.top_k
+        ids = np.empty((self.cfg.n_layers, k), np.uint32)
+        wts = np.empty((self.cfg.n_layers, k), np.float32)
+        self.ctx._check(LIB.zgpu_ds2_expert_ids(self.h, _ptr(ids), _ptr(wts)))
+        return ids, wts
+
+    def generate_greedy(self, kv: MlaKvCache, prompt, n_gen: int, want_logits: bool = False):
+        p = np.ascontiguousarray(prompt, np.uint32)
+        toks = np.empty(n_gen, np.uint32)
+        logits = np.empty((n_gen, self.cfg.vocab_padded), np.float32) if want_logits else None
+        self.ctx._check(LIB.zgpu_ds2_generate_greedy(self.h, kv.h, _ptr(p), p.size, n_gen, _ptr(toks),
+                                                     _ptr(logits) if want_logits else None))
+        return toks, logits
+
+    def perf(self) -> dict:
+        p = ZgpuPerf()
+        self.ctx._check(LIB.zgpu_ds2_perf_snapshot(self.h, C.byref(p)))
+        return {"steps": p.steps, "kernel_launches": p.kernel_launches, "decode_ms": p.decode_ms,
+                "prefill_ms": p.prefill_ms, "decode_launches": p.decode_launches}
+
+
 __all__ = ["Context", "KvCache", "Qwen3Model", "Qwen3Config", "QWEN3_1_7B", "ZgpuError", "synth",
+           "MlaKvCache", "Ds2Model", "Ds2Config", "DS2_V2_LITE", "ROUTE_SOFTMAX", "ROUTE_SIGMOID_NORMALIZE",
            "F32", "Q4_0", "Q8_0", "Q4_0X4", "Q8_0X4"]

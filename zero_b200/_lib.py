@@ -41,6 +41,28 @@ class ZgpuQwen3Desc(C.Structure):
     ]
 
 
+class ZgpuDs2Layer(C.Structure):
+    _fields_ = [
+        ("attn_norm", _vp), ("ffn_norm", _vp), ("kv_a_mqa", _vp), ("kv_a_norm", _vp), ("kv_b", _vp),
+        ("k_b", _vp), ("v_b", _vp), ("q_a", _vp), ("q_a_norm", _vp), ("q_b", _vp), ("attn_output", _vp),
+        ("k_norm", _vp), ("moe", _u32), ("ffn_gate", _vp), ("ffn_up", _vp), ("ffn_down", _vp),
+        ("router_w", _vp), ("router_b", _vp), ("gate_exps", _vp), ("up_exps", _vp), ("down_exps", _vp),
+        ("gate_shexp", _vp), ("up_shexp", _vp), ("down_shexp", _vp),
+    ]
+
+
+class ZgpuDs2Desc(C.Structure):
+    _fields_ = [
+        ("n_layers", _u32), ("hidden", _u32), ("ffn", _u32), ("n_heads", _u32),
+        ("kv_lora_rank", _u32), ("q_lora_rank", _u32), ("nope_dim", _u32), ("rope_dim", _u32),
+        ("v_dim", _u32), ("n_experts", _u32), ("top_k", _u32), ("expert_ffn", _u32), ("n_shared", _u32),
+        ("vocab_padded", _u32), ("vocab_real", _u32), ("rms_eps", _f), ("rope_theta", _f),
+        ("route_mode", _u32), ("expert_weight_scale", _f), ("attn_quant", _u32),
+        ("token_embd_quant", _u32), ("token_embd", _vp), ("output_quant", _u32), ("output", _vp),
+        ("output_norm", _vp), ("layers", C.POINTER(ZgpuDs2Layer)),
+    ]
+
+
 class ZgpuPerf(C.Structure):
     _fields_ = [("steps", _u64), ("kernel_launches", _u64), ("decode_ms", C.c_double),
                 ("prefill_ms", C.c_double), ("decode_launches", _u64)]
@@ -79,6 +101,18 @@ _SIGS = {
     "zgpu_lm_head_argmax": (_i32, [_vp, _u32, _vp, _vp]),
     "zgpu_generate_greedy": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp, _vp]),
     "zgpu_perf_snapshot": (_i32, [_vp, C.POINTER(ZgpuPerf)]),
+    "zgpu_moe_route_f32": (_i32, [_vp, _vp, _vp, _vp, _u64, _u32, _u32, _u32, _f, _vp, _vp, _vp]),
+    "zgpu_mla_kv_create": (_i32, [_vp, _u32, _u32, _u32, _u32, C.POINTER(_vp)]),
+    "zgpu_mla_kv_destroy": (None, [_vp]),
+    "zgpu_mla_kv_store": (_i32, [_vp, _u32, _u32, _vp, _vp]),
+    "zgpu_mla_kv_read": (_i32, [_vp, _u32, _u32, _vp]),
+    "zgpu_ds2_create": (_i32, [_vp, C.POINTER(ZgpuDs2Desc), C.POINTER(_vp)]),
+    "zgpu_ds2_destroy": (None, [_vp]),
+    "zgpu_ds2_forward_single_token": (_i32, [_vp, _vp, _u32, _u32, _vp]),
+    "zgpu_ds2_lm_head_argmax": (_i32, [_vp, _u32, _vp, _vp]),
+    "zgpu_ds2_expert_ids": (_i32, [_vp, _vp, _vp]),
+    "zgpu_ds2_generate_greedy": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp, _vp]),
+    "zgpu_ds2_perf_snapshot": (_i32, [_vp, C.POINTER(ZgpuPerf)]),
     "zgpu_synth_q4_0": (None, [_u64, _u64, _u64, _u64, _f, _vp]),
     "zgpu_synth_q8_0": (None, [_u64, _u64, _u64, _u64, _f, _vp]),
     "zgpu_synth_f32": (None, [_u64, _u64, _u64, _f, _f, _vp]),

@@ -10,6 +10,8 @@
 #include "layout.h"
 #include "ops.h"
 #include "step.h"
+#include "mla.h"
+#include "moe.h"
 
 using zgpu::DeviceTensor;
 
@@ -86,7 +88,10 @@ zgpu_status zgpu_init(const zgpu_opts *opts, zgpu_ctx **out) {
       cudaMalloc(&ctx->d_status, zgpu::kStatusWords * sizeof(uint32_t)) != cudaSuccess ||
       cudaMemset(ctx->d_status, 0, zgpu::kStatusWords * sizeof(uint32_t)) != cudaSuccess ||
       zgpu::gemv_setup() != cudaSuccess || zgpu::attention_setup() != cudaSuccess ||
-      zgpu::ops_setup() != cudaSuccess || zgpu::step_setup() != cudaSuccess) {
+      zgpu::ops_setup() != cudaSuccess || zgpu::step_setup() != cudaSuccess ||
+      zgpu::moe_setup() != cudaSuccess || zgpu::mla_setup() != cudaSuccess ||
+      cudaMalloc(&ctx->d_route_counter, sizeof(uint32_t)) != cudaSuccess ||
+      cudaMemset(ctx->d_route_counter, 0, sizeof(uint32_t)) != cudaSuccess) {
     delete ctx;
     return ZGPU_ERR_CUDA;
   }
@@ -110,6 +115,7 @@ void zgpu_destroy(zgpu_ctx *ctx) {
   cudaFree(ctx->d_y);
   cudaFree(ctx->d_attn_part);
   cudaFree(ctx->d_attn_counters);
+  cudaFree(ctx->d_route_counter);
   cudaFree(ctx->d_status);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   delete ctx;

@@ -1,0 +1,966 @@
+// ds2.cu — the DeepSeek2-shaped (MLA + MoE) decode step: compressed-latent
+// cache, device weight layout, per-step kernel sequence, CUDA-graph capture,
+// the greedy loop and the MoE routing entry point.
+//
+// One decode step (forward_single_token_deepseek2, forward_pass.rs:703-909,
+// then lm_head_argmax_dynamic, lm_head.rs:98) is, per layer:
+//   [RMSNorm + fused kv_a_mqa | q_a GEMV]
+//   [RMSNorm(c_q) + q_b GEMV]
+//   [mla_prep: latent RMSNorm, k_rope norm + RoPE, cache append; per-head
+//    query absorption W_kn^T q_nope and q_rope RoPE]
+//   [mla_attn + mla_merge: split-K softmax over the latent cache]
+//   [per-head V GEMV (segmented: head h reads its ctx_h and its v rows)]
+//   [O GEMV + residual]
+// then either the dense FFN
+//   [RMSNorm + fused gate|up GEMV + SiLU*up] [down GEMV + residual]
+// or the MoE FFN (moe_ffn, moe.rs:486-590)
+//   [router: exact-order scores, top-k, weights, dispatch tables]
+//   [grouped gate|up GEMV + SiLU*up over the shared and selected experts]
+//   [grouped down GEMV] [weighted combine in the reference's order + residual]
+// and the LM head [RMSNorm + GEMV + argmax] -> finalize.  Every kernel is
+// launched with programmatic dependent launch and the whole step is captured
+// once into a CUDA graph whose replays read token and position from device
+// memory.  Expert ids never leave the device between the router and the
+// expert GEMVs: the router writes the GEMVs' per-segment weight addresses.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+#include "layout.h"
+#include "mla.h"
+#include "moe.h"
+#include "ops.h"
+
+using namespace zgpu;
+
+struct zgpu_mla_kv {
+  zgpu_ctx *ctx = nullptr;
+  float *d = nullptr;
+  uint32_t max_tokens = 0, n_layers = 0, kv_lora = 0, rope = 0;
+  uint64_t layer_floats = 0;   // max_tokens * (kv_lora + rope)
+};
+
+namespace {
+
+struct Ds2Layer {
+  // attention
+  uint8_t *cat_a = nullptr;          // owned: kv_a groups | q_a groups (| one zero group)
+  uint32_t cat_a_groups = 0;
+  const DeviceTensor *q_b = nullptr, *o = nullptr;
+  const DeviceTensor *kb = nullptr;  // k_nope rows (kv_b or k_b)
+  uint32_t kb_head_rows = 0;
+  unsigned long long *d_vseg = nullptr;   // owned: per-head v-row stream addresses
+  uint64_t v_seg_bytes = 0;
+  uint64_t v_gstride = 0;
+  // ffn
+  uint32_t moe = 0;
+  uint8_t *gateup = nullptr;         // owned: gate/up groups interleaved (dense or routed experts)
+  uint8_t *sh_gateup = nullptr;      // owned: shared experts, interleaved
+  const DeviceTensor *down = nullptr, *sh_down = nullptr, *router = nullptr;
+  float *d_router_b = nullptr;       // owned (nullable)
+  unsigned long long *d_seg_gu = nullptr, *d_seg_dn = nullptr;   // owned [n_shared + top_k]
+  // norms (views into the model's norm block)
+  const float *attn_norm = nullptr, *ffn_norm = nullptr, *kv_a_norm = nullptr, *q_a_norm = nullptr,
+              *k_norm = nullptr;
+};
+
+}  // namespace
+
+struct zgpu_ds2_model {
+  zgpu_ctx *ctx = nullptr;
+  zgpu_ds2_desc desc = {};
+  std::vector<Ds2Layer> layers;
+  uint64_t gs_h = 0, gs_e = 0, gs_f = 0;   // group strides for in_dim hidden / expert_ffn / ffn
+  uint64_t gu_bytes = 0, dn_bytes = 0;     // per expert (interleaved gate/up, down)
+  const DeviceTensor *emb = nullptr, *out = nullptr;
+  float *d_norms = nullptr;                // every f32 vector of the model
+  float *d_out_norm = nullptr;
+  float *d_inv_freqs = nullptr;
+  // activations
+  float *d_hidden = nullptr, *d_ca = nullptr, *d_q = nullptr, *d_qabs = nullptr, *d_qpe = nullptr,
+        *d_ctx = nullptr, *d_concat = nullptr, *d_act = nullptr, *d_expout = nullptr,
+        *d_scores = nullptr, *d_logits = nullptr, *d_wts = nullptr;
+  uint32_t *d_ids = nullptr, *d_route_counter = nullptr;
+  unsigned long long *d_argmax = nullptr;
+  StepState *d_state = nullptr;
+  uint32_t *d_prompt = nullptr, *d_tokens = nullptr;
+  uint32_t prompt_cap = 0, tokens_cap = 0;
+  float *d_part = nullptr;
+  uint32_t max_splits = 0;
+  uint32_t *d_status = nullptr;
+  cudaGraphExec_t step_graph = nullptr, fwd_graph = nullptr, lm_graph = nullptr;
+  zgpu_mla_kv *graph_kv = nullptr;
+  uint32_t step_kernels = 0, fwd_kernels = 0, lm_kernels = 0;
+  zgpu_perf perf = {};
+  cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+};
+
+namespace {
+
+LaunchCfg launch_cfg(zgpu_ds2_model *m, uint32_t *counter) {
+  LaunchCfg lc;
+  lc.stream = m->ctx->stream;
+  lc.pdl = !(m->ctx->flags & ZGPU_FLAG_NO_PDL);
+  lc.sm_count = m->ctx->sm_count;
+  lc.launch_counter = counter;
+  return lc;
+}
+
+// Enqueue embed + all layers of one step.
+cudaError_t ds2_enqueue_forward(zgpu_ds2_model *m, zgpu_mla_kv *kv, uint32_t *counter) {
+  const zgpu_ds2_desc &d = m->desc;
+  LaunchCfg lc = launch_cfg(m, counter);
+  cudaError_t e;
+  EmbedParams ep;
+  ep.emb = m->emb->d;
+  ep.gstride = m->emb->gstride;
+  ep.quant = m->emb->quant;
+  ep.hidden = d.hidden;
+  ep.vocab = static_cast<uint32_t>(m->emb->rows);
+  ep.prompt = m->d_prompt;
+  ep.state = m->d_state;
+  ep.hidden_out = m->d_hidden;
+  ep.status = m->d_status;
+  if ((e = launch_embed(ep, lc)) != cudaSuccess) return e;
+
+  const uint32_t H = d.hidden, R = d.kv_lora_rank, RD = d.rope_dim, QL = d.q_lora_rank;
+  const uint32_t NH = d.n_heads, hq = d.nope_dim + d.rope_dim;
+  const uint32_t n_seg = d.n_shared + d.top_k;
+  for (uint32_t l = 0; l < d.n_layers; ++l) {
+    const Ds2Layer &L = m->layers[l];
+    GemvDesc g;
+    GemvIo io;
+    // RMSNorm + fused kv_a_mqa | q_a
+    g.w = L.cat_a;
+    g.gstride = m->gs_h;
+    g.wbytes = static_cast<uint64_t>(L.cat_a_groups) * m->gs_h;
+    g.quant = d.attn_quant;
+    g.rows = R + RD + QL;
+    g.groups = L.cat_a_groups;
+    g.in_dim = H;
+    io.x = m->d_hidden;
+    io.norm_w = L.attn_norm;
+    io.eps = d.rms_eps;
+    io.out = m->d_ca;
+    io.status = m->d_status;
+    if ((e = launch_gemv(g, PRO_RMSNORM, EPI_STORE, io, lc)) != cudaSuccess) return e;
+    // RMSNorm(c_q, q_a_norm) + q_b
+    g = GemvDesc();
+    g.w = L.q_b->d;
+    g.gstride = L.q_b->gstride;
+    g.wbytes = L.q_b->bytes;
+    g.quant = d.attn_quant;
+    g.rows = NH * hq;
+    g.groups = static_cast<uint32_t>(L.q_b->groups);
+    g.in_dim = QL;
+    io = GemvIo();
+    io.x = m->d_ca + R + RD;
+    io.norm_w = L.q_a_norm;
+    io.eps = d.rms_eps;
+    io.out = m->d_q;
+    io.status = m->d_status;
+    if ((e = launch_gemv(g, PRO_RMSNORM, EPI_STORE, io, lc)) != cudaSuccess) return e;
+    // latent append + query absorption, attention, merge
+    MlaParams mp = {};
+    mp.kv_a = m->d_ca;
+    mp.kv_a_norm = L.kv_a_norm;
+    mp.k_norm = L.k_norm;
+    mp.q = m->d_q;
+    mp.kb = L.kb->d;
+    mp.kb_gstride = L.kb->gstride;
+    mp.kb_quant = L.kb->quant;
+    mp.kb_head_rows = L.kb_head_rows;
+    mp.inv_freqs = m->d_inv_freqs;
+    mp.cache = kv->d + static_cast<size_t>(l) * kv->layer_floats;
+    mp.max_tokens = kv->max_tokens;
+    mp.pos_ptr = &m->d_state->pos;
+    mp.q_abs = m->d_qabs;
+    mp.q_pe = m->d_qpe;
+    mp.ctx = m->d_ctx;
+    mp.part = m->d_part;
+    mp.status = m->d_status;
+    mp.n_heads = NH;
+    mp.kv_lora = R;
+    mp.rope = RD;
+    mp.nope = d.nope_dim;
+    mp.max_splits = m->max_splits;
+    mp.eps = d.rms_eps;
+    mp.scale = 1.0f / sqrtf(static_cast<float>(hq));
+    if ((e = launch_mla_prep(mp, lc)) != cudaSuccess) return e;
+    if ((e = launch_mla_attention(mp, lc)) != cudaSuccess) return e;
+    // per-head V projection of the merged latent context
+    g = GemvDesc();
+    g.gstride = L.v_gstride;
+    g.wbytes = L.v_seg_bytes;
+    g.quant = d.attn_quant;
+    g.rows = d.v_dim;
+    g.groups = d.v_dim / 4;
+    g.in_dim = R;
+    g.seg_w = L.d_vseg;
+    g.seg_count = NH;
+    g.seg_x_stride = R;
+    g.seg_out_stride = d.v_dim;
+    io = GemvIo();
+    io.x = m->d_ctx;
+    io.out = m->d_concat;
+    io.status = m->d_status;
+    if ((e = launch_gemv(g, PRO_PLAIN, EPI_STORE, io, lc)) != cudaSuccess) return e;
+    // O projection + residual
+    g = GemvDesc();
+    g.w = L.o->d;
+    g.gstride = L.o->gstride;
+    g.wbytes = L.o->bytes;
+    g.quant = d.attn_quant;
+    g.rows = H;
+    g.groups = H / 4;
+    g.in_dim = NH * d.v_dim;
+    io = GemvIo();
+    io.x = m->d_concat;
+    io.out = m->d_hidden;
+    io.status = m->d_status;
+    if ((e = launch_gemv(g, PRO_PLAIN, EPI_RESADD, io, lc)) != cudaSuccess) return e;
+
+    if (!L.moe) {
+      g = GemvDesc();
+      g.w = L.gateup;
+      g.gstride = m->gs_h;
+      g.wbytes = static_cast<uint64_t>(2 * d.ffn / 4) * m->gs_h;
+      g.quant = ZGPU_Q4_0;
+      g.rows = d.ffn;
+      g.groups = 2 * d.ffn / 4;
+      g.in_dim = H;
+      io = GemvIo();
+      io.x = m->d_hidden;
+      io.norm_w = L.ffn_norm;
+      io.eps = d.rms_eps;
+      io.out = m->d_act;
+      io.status = m->d_status;
+      if ((e = launch_gemv(g, PRO_RMSNORM, EPI_SWIGLU, io, lc)) != cudaSuccess) return e;
+      g = GemvDesc();
+      g.w = L.down->d;
+      g.gstride = L.down->gstride;
+      g.wbytes = L.down->bytes;
+      g.quant = ZGPU_Q4_0;
+      g.rows = H;
+      g.groups = H / 4;
+      g.in_dim = d.ffn;
+      io = GemvIo();
+      io.x = m->d_act;
+      io.out = m->d_hidden;
+      io.status = m->d_status;
+      if ((e = launch_gemv(g, PRO_PLAIN, EPI_RESADD, io, lc)) != cudaSuccess) return e;
+      continue;
+    }
+    // router: ids / weights of this layer and the expert dispatch tables
+    RouteParams rp = {};
+    rp.x = m->d_hidden;
+    rp.norm_w = L.ffn_norm;
+    rp.eps = d.rms_eps;
+    rp.w = reinterpret_cast<const float *>(L.router->d);
+    rp.bias = L.d_router_b;
+    rp.dim = H;
+    rp.n_experts = d.n_experts;
+    rp.top_k = d.top_k;
+    rp.mode = d.route_mode;
+    rp.scale = d.expert_weight_scale;
+    rp.scores = m->d_scores;
+    rp.ids = m->d_ids + static_cast<size_t>(l) * d.top_k;
+    rp.weights = m->d_wts + static_cast<size_t>(l) * d.top_k;
+    rp.counter = m->d_route_counter;
+    rp.seg_gu = L.d_seg_gu;
+    rp.seg_dn = L.d_seg_dn;
+    rp.gu_base = reinterpret_cast<unsigned long long>(L.gateup);
+    rp.dn_base = reinterpret_cast<unsigned long long>(L.down->d);
+    rp.sh_gu_base = reinterpret_cast<unsigned long long>(L.sh_gateup);
+    rp.sh_dn_base = L.sh_down ? reinterpret_cast<unsigned long long>(L.sh_down->d) : 0ull;
+    rp.gu_bytes = m->gu_bytes;
+    rp.dn_bytes = m->dn_bytes;
+    rp.n_shared = d.n_shared;
+    rp.status = m->d_status;
+    if ((e = launch_moe_route(rp, lc)) != cudaSuccess) return e;
+    // grouped gate|up + SiLU*up: segment s = shared s, then the k-th selected expert
+    g = GemvDesc();
+    g.gstride = m->gs_h;
+    g.wbytes = m->gu_bytes;
+    g.quant = ZGPU_Q4_0;
+    g.rows = d.expert_ffn;
+    g.groups = 2 * d.expert_ffn / 4;
+    g.in_dim = H;
+    g.seg_w = L.d_seg_gu;
+    g.seg_count = n_seg;
+    g.seg_x_stride = 0;
+    g.seg_out_stride = d.expert_ffn;
+    g.seg_dynamic = true;
+    io = GemvIo();
+    io.x = m->d_hidden;
+    io.norm_w = L.ffn_norm;
+    io.eps = d.rms_eps;
+    io.out = m->d_act;
+    io.status = m->d_status;
+    if ((e = launch_gemv(g, PRO_RMSNORM, EPI_SWIGLU, io, lc)) != cudaSuccess) return e;
+    // grouped down projections
+    g = GemvDesc();
+    g.gstride = m->gs_e;
+    g.wbytes = m->dn_bytes;
+    g.quant = ZGPU_Q4_0;
+    g.rows = H;
+    g.groups = H / 4;
+    g.in_dim = d.expert_ffn;
+    g.seg_w = L.d_seg_dn;
+    g.seg_count = n_seg;
+    g.seg_x_stride = d.expert_ffn;
+    g.seg_out_stride = H;
+    g.seg_dynamic = true;
+    io = GemvIo();
+    io.x = m->d_act;
+    io.out = m->d_expout;
+    io.status = m->d_status;
+    if ((e = launch_gemv(g, PRO_PLAIN, EPI_STORE, io, lc)) != cudaSuccess) return e;
+    CombineParams cp = {};
+    cp.exp_out = m->d_expout;
+    cp.weights = m->d_wts + static_cast<size_t>(l) * d.top_k;
+    cp.hidden = m->d_hidden;
+    cp.dim = H;
+    cp.n_shared = d.n_shared;
+    cp.top_k = d.top_k;
+    if ((e = launch_moe_combine(cp, lc)) != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t ds2_enqueue_lm_head(zgpu_ds2_model *m, uint32_t *counter) {
+  const zgpu_ds2_desc &d = m->desc;
+  LaunchCfg lc = launch_cfg(m, counter);
+  GemvDesc g;
+  g.w = m->out->d;
+  g.wbytes = m->out->bytes;
+  g.gstride = m->out->gstride;
+  g.quant = m->out->quant;
+  g.rows = d.vocab_padded;
+  g.groups = static_cast<uint32_t>(m->out->groups);
+  g.in_dim = d.hidden;
+  GemvIo io;
+  io.x = m->d_hidden;
+  io.norm_w = m->d_out_norm;
+  io.eps = d.rms_eps;
+  io.out = m->d_logits;
+  io.argmax = m->d_argmax;
+  io.status = m->d_status;
+  cudaError_t e = launch_gemv(g, PRO_RMSNORM, EPI_ARGMAX, io, lc);
+  if (e != cudaSuccess) return e;
+  FinalizeParams fp;
+  fp.argmax = m->d_argmax;
+  fp.state = m->d_state;
+  fp.tokens_out = m->d_tokens;
+  fp.status = m->d_status;
+  return launch_finalize(fp, lc);
+}
+
+enum GraphPart { GRAPH_STEP = 0, GRAPH_FWD = 1, GRAPH_LM = 2 };
+
+zgpu_status ds2_capture(zgpu_ds2_model *m, zgpu_mla_kv *kv, GraphPart part, cudaGraphExec_t *out,
+                        uint32_t *kernels) {
+  zgpu_ctx *ctx = m->ctx;
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "begin capture");
+  uint32_t n = 0;
+  cudaError_t e1 = cudaSuccess;
+  if (part != GRAPH_LM) e1 = ds2_enqueue_forward(m, kv, &n);
+  if (e1 == cudaSuccess && part != GRAPH_FWD) e1 = ds2_enqueue_lm_head(m, &n);
+  e = cudaStreamEndCapture(ctx->stream, &g);
+  if (e1 != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    return zgpu_cuda_fail(ctx, e1, "capture step");
+  }
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "end capture");
+  e = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "graph instantiate");
+  *kernels = n;
+  return ZGPU_OK;
+}
+
+void ds2_drop_graphs(zgpu_ds2_model *m) {
+  for (cudaGraphExec_t *g : {&m->step_graph, &m->fwd_graph, &m->lm_graph}) {
+    if (*g) cudaGraphExecDestroy(*g);
+    *g = nullptr;
+  }
+  m->graph_kv = nullptr;
+}
+
+zgpu_status ds2_build_graphs(zgpu_ds2_model *m, zgpu_mla_kv *kv) {
+  if (m->step_graph && m->graph_kv == kv) return ZGPU_OK;
+  ds2_drop_graphs(m);
+  zgpu_status s = ds2_capture(m, kv, GRAPH_STEP, &m->step_graph, &m->step_kernels);
+  if (!s) s = ds2_capture(m, kv, GRAPH_FWD, &m->fwd_graph, &m->fwd_kernels);
+  if (!s) s = ds2_capture(m, nullptr, GRAPH_LM, &m->lm_graph, &m->lm_kernels);
+  if (s) {
+    ds2_drop_graphs(m);
+    return s;
+  }
+  m->graph_kv = kv;
+  return ZGPU_OK;
+}
+
+zgpu_status ds2_set_state(zgpu_ds2_model *m, uint32_t n_prompt, uint32_t pos_base, uint32_t vocab_real,
+                          uint32_t n_gen_cap) {
+  StepState s = {};
+  s.n_prompt = n_prompt;
+  s.pos_base = pos_base;
+  s.pos = pos_base;
+  s.vocab_real = vocab_real;
+  s.n_gen_cap = n_gen_cap;
+  s.first_err_step = 0xFFFFFFFFu;
+  cudaError_t e = cudaMemcpyAsync(m->d_state, &s, sizeof(s), cudaMemcpyHostToDevice, m->ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(m->ctx, e, "state upload");
+  return ZGPU_OK;
+}
+
+template <class T>
+cudaError_t grow(T **p, uint32_t *cap, uint32_t need) {
+  if (need <= *cap) return cudaSuccess;
+  cudaFree(*p);
+  *p = nullptr;
+  cudaError_t e = cudaMalloc(p, static_cast<size_t>(need) * sizeof(T));
+  if (e == cudaSuccess) *cap = need;
+  return e;
+}
+
+zgpu_status ds2_prepare_kv(zgpu_ds2_model *m, zgpu_mla_kv *kv) {
+  zgpu_ctx *ctx = m->ctx;
+  if (kv->n_layers != m->desc.n_layers)
+    return zgpu_fail(ctx, ZGPU_ERR_KV_LAYER_OUT_OF_RANGE, "mla cache layer count differs from the model");
+  if (kv->kv_lora != m->desc.kv_lora_rank || kv->rope != m->desc.rope_dim)
+    return zgpu_fail(ctx, ZGPU_ERR_KV_INVALID_SLICE_LENGTH, "mla cache geometry differs from the model");
+  const uint32_t splits = mla_max_splits(kv->max_tokens);
+  if (splits != m->max_splits || !m->d_part) {
+    cudaFree(m->d_part);
+    m->d_part = nullptr;
+    const size_t n = static_cast<size_t>(m->desc.n_heads) * splits * (m->desc.kv_lora_rank + 2);
+    cudaError_t e = cudaMalloc(&m->d_part, n * 4);
+    if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "mla attention scratch");
+    m->max_splits = splits;
+    ds2_drop_graphs(m);
+  }
+  return ZGPU_OK;
+}
+
+// Interleave two tensors' group streams: group j of a at 2j, of b at 2j+1.
+cudaError_t interleave_groups(uint8_t **dst, const DeviceTensor *a, const DeviceTensor *b) {
+  cudaError_t e = cudaMalloc(dst, a->bytes + b->bytes);
+  if (e != cudaSuccess) return e;
+  e = cudaMemcpy2D(*dst, 2 * a->gstride, a->d, a->gstride, a->gstride, a->groups, cudaMemcpyDeviceToDevice);
+  if (e != cudaSuccess) return e;
+  return cudaMemcpy2D(*dst + a->gstride, 2 * a->gstride, b->d, b->gstride, b->gstride, b->groups,
+                      cudaMemcpyDeviceToDevice);
+}
+
+}  // namespace
+
+extern "C" {
+
+// ------------------------------------------------------------ MLA cache
+
+zgpu_status zgpu_mla_kv_create(zgpu_ctx *ctx, uint32_t max_tokens, uint32_t n_layers,
+                               uint32_t kv_lora_rank, uint32_t rope_dim, zgpu_mla_kv **out) {
+  if (!ctx || !out || !max_tokens || !n_layers || !kv_lora_rank) return ZGPU_ERR_INVALID_ARG;
+  *out = nullptr;
+  cudaSetDevice(ctx->device);
+  zgpu_mla_kv *kv = new (std::nothrow) zgpu_mla_kv();
+  if (!kv) return ZGPU_ERR_OUT_OF_MEMORY;
+  kv->ctx = ctx;
+  kv->max_tokens = max_tokens;
+  kv->n_layers = n_layers;
+  kv->kv_lora = kv_lora_rank;
+  kv->rope = rope_dim;
+  kv->layer_floats = static_cast<uint64_t>(max_tokens) * (kv_lora_rank + rope_dim);
+  const size_t bytes = static_cast<size_t>(n_layers) * kv->layer_floats * sizeof(float);
+  cudaError_t e = cudaMalloc(&kv->d, bytes);
+  if (e == cudaSuccess) e = cudaMemset(kv->d, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(kv->d);
+    delete kv;
+    return zgpu_cuda_fail(ctx, e, "mla cache allocation");
+  }
+  *out = kv;
+  return ZGPU_OK;
+}
+
+void zgpu_mla_kv_destroy(zgpu_mla_kv *kv) {
+  if (!kv) return;
+  cudaSetDevice(kv->ctx->device);
+  cudaFree(kv->d);
+  delete kv;
+}
+
+zgpu_status zgpu_mla_kv_store(zgpu_mla_kv *kv, uint32_t layer, uint32_t token, const float *c_kv,
+                              const float *k_rope) {
+  if (!kv || !c_kv || (!k_rope && kv->rope)) return ZGPU_ERR_INVALID_ARG;
+  zgpu_ctx *ctx = kv->ctx;
+  if (layer >= kv->n_layers) return zgpu_fail(ctx, ZGPU_ERR_KV_LAYER_OUT_OF_RANGE, "layer out of range");
+  if (token >= kv->max_tokens) return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "token out of range");
+  cudaSetDevice(ctx->device);
+  float *row = kv->d + layer * kv->layer_floats + static_cast<uint64_t>(token) * (kv->kv_lora + kv->rope);
+  cudaError_t e = cudaMemcpyAsync(row, c_kv, kv->kv_lora * 4, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess && kv->rope)
+    e = cudaMemcpyAsync(row + kv->kv_lora, k_rope, kv->rope * 4, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "mla cache store");
+  return ZGPU_OK;
+}
+
+zgpu_status zgpu_mla_kv_read(zgpu_mla_kv *kv, uint32_t layer, uint32_t token_count, float *rows_out) {
+  if (!kv || !rows_out) return ZGPU_ERR_INVALID_ARG;
+  zgpu_ctx *ctx = kv->ctx;
+  if (layer >= kv->n_layers) return zgpu_fail(ctx, ZGPU_ERR_KV_LAYER_OUT_OF_RANGE, "layer out of range");
+  if (token_count > kv->max_tokens)
+    return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_COUNT_EXCEEDS_MAX, "token count exceeds max_tokens");
+  cudaSetDevice(ctx->device);
+  const size_t n = static_cast<size_t>(token_count) * (kv->kv_lora + kv->rope);
+  cudaError_t e = cudaMemcpyAsync(rows_out, kv->d + layer * kv->layer_floats, n * 4,
+                                  cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "mla cache read");
+  return ZGPU_OK;
+}
+
+// ------------------------------------------------------------ MoE routing
+
+zgpu_status zgpu_moe_route_f32(zgpu_ctx *ctx, const float *hidden, const void *router_key,
+                               const float *router_bias, uint64_t dim, uint32_t n_experts,
+                               uint32_t top_k, uint32_t mode, float expert_weight_scale,
+                               float *scores_out, uint32_t *indices_out, float *weights_out) {
+  if (!ctx || !hidden || !indices_out || !weights_out) return ZGPU_ERR_INVALID_ARG;
+  if (top_k == 0) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "moe_route_f32: top_k must be > 0");
+  if (top_k > n_experts) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "moe_route_f32: top_k must be <= n_experts");
+  if (top_k > kMoeMaxTopK || dim == 0 || dim % 4 || dim > kMoeMaxDim || mode > 1)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "moe_route_f32: unsupported geometry or mode");
+  const DeviceTensor *t = zgpu_lookup(ctx, router_key);
+  if (!t) return zgpu_fail(ctx, ZGPU_ERR_UNREGISTERED_WEIGHT, "router weights not registered");
+  if (t->quant != ZGPU_F32 || t->rows != n_experts || t->cols != dim)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "router weights must be f32 [n_experts x dim]");
+  cudaSetDevice(ctx->device);
+  // scratch: x [dim] | bias [n_experts] | scores [n_experts] | weights [top_k] | ids [top_k]
+  const size_t need = dim + 2 * static_cast<size_t>(n_experts) + 2 * top_k;
+  if (need > ctx->d_x_cap) {
+    cudaFree(ctx->d_x);
+    ctx->d_x = nullptr;
+    cudaError_t e = cudaMalloc(&ctx->d_x, need * sizeof(float));
+    if (e != cudaSuccess) {
+      ctx->d_x_cap = 0;
+      return zgpu_cuda_fail(ctx, e, "router scratch");
+    }
+    ctx->d_x_cap = need;
+  }
+  float *d_x = ctx->d_x, *d_bias = d_x + dim, *d_scores = d_bias + n_experts, *d_w = d_scores + n_experts;
+  uint32_t *d_ids = reinterpret_cast<uint32_t *>(d_w + top_k);
+  cudaError_t e = cudaMemcpyAsync(d_x, hidden, dim * 4, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess && router_bias)
+    e = cudaMemcpyAsync(d_bias, router_bias, n_experts * 4, cudaMemcpyHostToDevice, ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "router upload");
+  RouteParams rp = {};
+  rp.x = d_x;
+  rp.w = reinterpret_cast<const float *>(t->d);
+  rp.bias = router_bias ? d_bias : nullptr;
+  rp.dim = static_cast<uint32_t>(dim);
+  rp.n_experts = n_experts;
+  rp.top_k = top_k;
+  rp.mode = mode;
+  rp.scale = expert_weight_scale;
+  rp.scores = d_scores;
+  rp.ids = d_ids;
+  rp.weights = d_w;
+  rp.counter = ctx->d_route_counter;
+  rp.status = ctx->d_status;
+  LaunchCfg lc;
+  lc.stream = ctx->stream;
+  lc.sm_count = ctx->sm_count;
+  lc.launch_counter = &ctx->launches;
+  e = launch_moe_route(rp, lc);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "router launch");
+  e = cudaMemcpyAsync(indices_out, d_ids, top_k * 4, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(weights_out, d_w, top_k * 4, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess && scores_out)
+    e = cudaMemcpyAsync(scores_out, d_scores, n_experts * 4, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "router results");
+  uint32_t st = 0;
+  zgpu_status s = zgpu_read_device_status(ctx, ctx->d_status, &st);
+  if (s) return s;
+  return zgpu_map_device_status(ctx, st);
+}
+
+// ------------------------------------------------------------ model
+
+void zgpu_ds2_destroy(zgpu_ds2_model *m) {
+  if (!m) return;
+  cudaSetDevice(m->ctx->device);
+  ds2_drop_graphs(m);
+  for (Ds2Layer &L : m->layers) {
+    cudaFree(L.cat_a);
+    cudaFree(L.d_vseg);
+    cudaFree(L.gateup);
+    cudaFree(L.sh_gateup);
+    cudaFree(L.d_router_b);
+    cudaFree(L.d_seg_gu);
+    cudaFree(L.d_seg_dn);
+  }
+  for (float *p : {m->d_norms, m->d_inv_freqs, m->d_hidden, m->d_ca, m->d_q, m->d_qabs, m->d_qpe,
+                   m->d_ctx, m->d_concat, m->d_act, m->d_expout, m->d_scores, m->d_logits, m->d_wts,
+                   m->d_part})
+    cudaFree(p);
+  cudaFree(m->d_ids);
+  cudaFree(m->d_route_counter);
+  cudaFree(m->d_argmax);
+  cudaFree(m->d_state);
+  cudaFree(m->d_prompt);
+  cudaFree(m->d_tokens);
+  cudaFree(m->d_status);
+  for (auto &ev : m->ev)
+    if (ev) cudaEventDestroy(ev);
+  delete m;
+}
+
+zgpu_status zgpu_ds2_create(zgpu_ctx *ctx, const zgpu_ds2_desc *d, zgpu_ds2_model **out) {
+  if (!ctx || !d || !out || !d->layers || !d->output_norm) return ZGPU_ERR_INVALID_ARG;
+  *out = nullptr;
+  cudaSetDevice(ctx->device);
+  const uint32_t H = d->hidden, R = d->kv_lora_rank, RD = d->rope_dim, QL = d->q_lora_rank;
+  const uint32_t NH = d->n_heads, NO = d->nope_dim, VD = d->v_dim, hq = NO + RD, L_ = d->n_layers;
+  auto bad = [&](const char *msg) { return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, msg); };
+  if (!L_ || !NH) return bad("ds2: n_layers and n_heads must be > 0");
+  if (d->attn_quant != ZGPU_Q4_0)
+    return zgpu_fail(ctx, ZGPU_ERR_UNSUPPORTED_QUANT, "ds2: the layers' matmuls must be Q4_0");
+  if (H % 32 || H % 8) return bad("ds2: hidden must be a multiple of 32");
+  if (R == 0 || R % 32 || R > kMlaMaxLatent) return bad("ds2: kv_lora_rank must be a multiple of 32, at most 512");
+  if (RD % 2 || RD > kMlaMaxRope || (R + RD) % 4) return bad("ds2: rope_dim must be even, at most 64");
+  if (NO == 0 || NO % 4 || NO > kMlaMaxNope) return bad("ds2: nope_dim must be a multiple of 4, at most 256");
+  if (VD == 0 || VD % 8 || (NH * VD) % 32) return bad("ds2: v_dim must be a multiple of 8");
+  if (QL == 0 || QL % 32) return bad("ds2: q_lora_rank must be a multiple of 32");
+  if ((NH * hq) % 8 || (R + RD + QL) % 4) return bad("ds2: projection rows must fill 4-row groups");
+  if (d->vocab_real > d->vocab_padded) return bad("ds2: vocab_real > vocab_padded");
+  if (d->route_mode > 1) return bad("ds2: unknown routing mode");
+  bool any_moe = false, any_dense = false;
+  for (uint32_t l = 0; l < L_; ++l) (d->layers[l].moe ? any_moe : any_dense) = true;
+  if (any_dense && (d->ffn == 0 || d->ffn % 32)) return bad("ds2: ffn must be a multiple of 32");
+  if (any_moe) {
+    if (d->top_k == 0 || d->top_k > d->n_experts || d->top_k > kMoeMaxTopK)
+      return bad("ds2: need 0 < top_k <= n_experts, top_k <= 16");
+    if (d->expert_ffn == 0 || d->expert_ffn % 32) return bad("ds2: expert_ffn must be a multiple of 32");
+    if (H > kMoeMaxDim) return bad("ds2: router input above 8192");
+  }
+  zgpu_ds2_model *m = new (std::nothrow) zgpu_ds2_model();
+  if (!m) return ZGPU_ERR_OUT_OF_MEMORY;
+  m->ctx = ctx;
+  m->desc = *d;
+  m->desc.layers = nullptr;
+  m->desc.output_norm = nullptr;
+  m->layers.resize(L_);
+  auto fail = [&](zgpu_status s, const std::string &msg) {
+    zgpu_ds2_destroy(m);
+    return zgpu_fail(ctx, s, msg);
+  };
+  auto need = [&](const void *key, uint32_t quant, uint64_t rows, uint64_t cols,
+                  const char *what) -> const DeviceTensor * {
+    const DeviceTensor *t = zgpu_lookup(ctx, key);
+    if (!t || t->quant != quant || t->rows != rows || t->cols != cols) {
+      ctx->last_error = std::string("ds2_create: bad or unregistered tensor ") + what;
+      return nullptr;
+    }
+    return t;
+  };
+  m->emb = need(d->token_embd, d->token_embd_quant, d->vocab_padded, H, "token_embd");
+  if (!m->emb) return fail(ZGPU_ERR_UNREGISTERED_WEIGHT, ctx->last_error);
+  m->out = need(d->output, d->output_quant, d->vocab_padded, H, "output");
+  if (!m->out) return fail(ZGPU_ERR_UNREGISTERED_WEIGHT, ctx->last_error);
+
+  // f32 vectors: per layer attn | ffn | kv_a_norm | q_a_norm | k_norm, then the output norm
+  const size_t per_layer = 2 * static_cast<size_t>(H) + R + QL + RD;
+  std::vector<float> norms(per_layer * L_ + H, 1.0f);
+  const uint32_t n_seg = d->n_shared + d->top_k;
+  cudaError_t e = cudaSuccess;
+  for (uint32_t l = 0; l < L_; ++l) {
+    const zgpu_ds2_layer &ly = d->layers[l];
+    Ds2Layer &L = m->layers[l];
+    if (!ly.attn_norm || !ly.ffn_norm || !ly.kv_a_norm || !ly.q_a_norm)
+      return fail(ZGPU_ERR_INVALID_ARG, "ds2_create: missing norm weights");
+    float *nb = norms.data() + per_layer * l;
+    std::memcpy(nb, ly.attn_norm, H * 4);
+    std::memcpy(nb + H, ly.ffn_norm, H * 4);
+    std::memcpy(nb + 2 * H, ly.kv_a_norm, R * 4);
+    std::memcpy(nb + 2 * H + R, ly.q_a_norm, QL * 4);
+    if (ly.k_norm) std::memcpy(nb + 2 * H + R + QL, ly.k_norm, RD * 4);
+    const DeviceTensor *kva = need(ly.kv_a_mqa, ZGPU_Q4_0, R + RD, H, "kv_a_mqa");
+    const DeviceTensor *qa = need(ly.q_a, ZGPU_Q4_0, QL, H, "q_a");
+    L.q_b = need(ly.q_b, ZGPU_Q4_0, static_cast<uint64_t>(NH) * hq, QL, "q_b");
+    L.o = need(ly.attn_output, ZGPU_Q4_0, H, static_cast<uint64_t>(NH) * VD, "attn_output");
+    if (!kva || !qa || !L.q_b || !L.o) return fail(ZGPU_ERR_UNREGISTERED_WEIGHT, ctx->last_error);
+    const DeviceTensor *vb = nullptr;
+    if (ly.k_b && ly.v_b) {
+      L.kb = need(ly.k_b, ZGPU_Q4_0, static_cast<uint64_t>(NH) * NO, R, "k_b");
+      vb = need(ly.v_b, ZGPU_Q4_0, static_cast<uint64_t>(NH) * VD, R, "v_b");
+      L.kb_head_rows = NO;
+    } else {
+      L.kb = need(ly.kv_b, ZGPU_Q4_0, static_cast<uint64_t>(NH) * (NO + VD), R, "kv_b");
+      vb = L.kb;
+      L.kb_head_rows = NO + VD;
+    }
+    if (!L.kb || !vb) return fail(ZGPU_ERR_UNREGISTERED_WEIGHT, ctx->last_error);
+    m->gs_h = kva->gstride;
+    // fused kv_a | q_a, padded to an even group count with a zero group
+    const uint32_t ga = static_cast<uint32_t>(kva->groups + qa->groups);
+    L.cat_a_groups = (ga + 1) & ~1u;
+    const size_t cat_bytes = static_cast<size_t>(L.cat_a_groups) * m->gs_h;
+    if ((e = cudaMalloc(&L.cat_a, cat_bytes)) != cudaSuccess) return fail(ZGPU_ERR_OUT_OF_MEMORY, "kv_a|q_a allocation");
+    cudaMemset(L.cat_a, 0, cat_bytes);
+    cudaMemcpy(L.cat_a, kva->d, kva->bytes, cudaMemcpyDeviceToDevice);
+    cudaMemcpy(L.cat_a + kva->bytes, qa->d, qa->bytes, cudaMemcpyDeviceToDevice);
+    // per-head V row streams
+    std::vector<unsigned long long> vseg(NH);
+    for (uint32_t h = 0; h < NH; ++h) {
+      const uint64_t row = (ly.k_b && ly.v_b) ? static_cast<uint64_t>(h) * VD
+                                              : static_cast<uint64_t>(h) * (NO + VD) + NO;
+      vseg[h] = reinterpret_cast<unsigned long long>(vb->d + (row / 4) * vb->gstride);
+    }
+    L.v_gstride = vb->gstride;
+    L.v_seg_bytes = static_cast<uint64_t>(VD / 4) * vb->gstride;
+    if ((e = cudaMalloc(&L.d_vseg, NH * 8)) != cudaSuccess) return fail(ZGPU_ERR_OUT_OF_MEMORY, "v table");
+    cudaMemcpy(L.d_vseg, vseg.data(), NH * 8, cudaMemcpyHostToDevice);
+    L.moe = ly.moe;
+    if (!ly.moe) {
+      const DeviceTensor *gt = need(ly.ffn_gate, ZGPU_Q4_0, d->ffn, H, "ffn_gate");
+      const DeviceTensor *up = need(ly.ffn_up, ZGPU_Q4_0, d->ffn, H, "ffn_up");
+      L.down = need(ly.ffn_down, ZGPU_Q4_0, H, d->ffn, "ffn_down");
+      if (!gt || !up || !L.down) return fail(ZGPU_ERR_UNREGISTERED_WEIGHT, ctx->last_error);
+      if ((e = interleave_groups(&L.gateup, gt, up)) != cudaSuccess) return fail(ZGPU_ERR_OUT_OF_MEMORY, "gate/up");
+      continue;
+    }
+    const uint64_t EF = d->expert_ffn;
+    const DeviceTensor *gt = need(ly.gate_exps, ZGPU_Q4_0, d->n_experts * EF, H, "gate_exps");
+    const DeviceTensor *up = need(ly.up_exps, ZGPU_Q4_0, d->n_experts * EF, H, "up_exps");
+    L.down = need(ly.down_exps, ZGPU_Q4_0, static_cast<uint64_t>(d->n_experts) * H, EF, "down_exps");
+    L.router = need(ly.router_w, ZGPU_F32, d->n_experts, H, "router_w");
+    if (!gt || !up || !L.down || !L.router) return fail(ZGPU_ERR_UNREGISTERED_WEIGHT, ctx->last_error);
+    if ((e = interleave_groups(&L.gateup, gt, up)) != cudaSuccess) return fail(ZGPU_ERR_OUT_OF_MEMORY, "expert gate/up");
+    m->gs_e = L.down->gstride;
+    m->gu_bytes = 2 * (EF / 4) * gt->gstride;
+    m->dn_bytes = (H / 4) * L.down->gstride;
+    if (d->n_shared) {
+      const DeviceTensor *sg = need(ly.gate_shexp, ZGPU_Q4_0, d->n_shared * EF, H, "gate_shexp");
+      const DeviceTensor *su = need(ly.up_shexp, ZGPU_Q4_0, d->n_shared * EF, H, "up_shexp");
+      L.sh_down = need(ly.down_shexp, ZGPU_Q4_0, static_cast<uint64_t>(d->n_shared) * H, EF, "down_shexp");
+      if (!sg || !su || !L.sh_down) return fail(ZGPU_ERR_UNREGISTERED_WEIGHT, ctx->last_error);
+      if ((e = interleave_groups(&L.sh_gateup, sg, su)) != cudaSuccess)
+        return fail(ZGPU_ERR_OUT_OF_MEMORY, "shared gate/up");
+    }
+    if (ly.router_b) {
+      if ((e = cudaMalloc(&L.d_router_b, d->n_experts * 4)) != cudaSuccess) return fail(ZGPU_ERR_OUT_OF_MEMORY, "router bias");
+      cudaMemcpy(L.d_router_b, ly.router_b, d->n_experts * 4, cudaMemcpyHostToDevice);
+    }
+    if (cudaMalloc(&L.d_seg_gu, n_seg * 8) != cudaSuccess || cudaMalloc(&L.d_seg_dn, n_seg * 8) != cudaSuccess)
+      return fail(ZGPU_ERR_OUT_OF_MEMORY, "expert tables");
+    cudaMemset(L.d_seg_gu, 0, n_seg * 8);
+    cudaMemset(L.d_seg_dn, 0, n_seg * 8);
+  }
+  std::memcpy(norms.data() + per_layer * L_, d->output_norm, H * 4);
+  if ((e = cudaMalloc(&m->d_norms, norms.size() * 4)) != cudaSuccess) return fail(ZGPU_ERR_OUT_OF_MEMORY, "norms");
+  cudaMemcpy(m->d_norms, norms.data(), norms.size() * 4, cudaMemcpyHostToDevice);
+  for (uint32_t l = 0; l < L_; ++l) {
+    Ds2Layer &L = m->layers[l];
+    float *nb = m->d_norms + per_layer * l;
+    L.attn_norm = nb;
+    L.ffn_norm = nb + H;
+    L.kv_a_norm = nb + 2 * H;
+    L.q_a_norm = nb + 2 * H + R;
+    L.k_norm = d->layers[l].k_norm ? nb + 2 * H + R + QL : nullptr;
+  }
+  m->d_out_norm = m->d_norms + per_layer * L_;
+  // mla.rs:165-171: freq_i = powf(base, -2 i / rope_dim)
+  std::vector<float> inv(RD / 2 ? RD / 2 : 1, 0.f);
+  for (uint32_t i = 0; i < RD / 2; ++i)
+    inv[i] = powf(d->rope_theta, -2.0f * static_cast<float>(i) / static_cast<float>(RD));
+  if ((e = cudaMalloc(&m->d_inv_freqs, inv.size() * 4)) != cudaSuccess) return fail(ZGPU_ERR_OUT_OF_MEMORY, "rope");
+  cudaMemcpy(m->d_inv_freqs, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice);
+
+  const size_t act = std::max<size_t>(any_dense ? d->ffn : 0, static_cast<size_t>(n_seg) * d->expert_ffn);
+  const size_t topk = any_moe ? d->top_k : 1;
+  if (cudaMalloc(&m->d_hidden, H * 4) || cudaMalloc(&m->d_ca, (R + RD + QL + 8) * 4) ||
+      cudaMalloc(&m->d_q, static_cast<size_t>(NH) * hq * 4) || cudaMalloc(&m->d_qabs, static_cast<size_t>(NH) * R * 4) ||
+      cudaMalloc(&m->d_qpe, static_cast<size_t>(NH) * (RD ? RD : 1) * 4) ||
+      cudaMalloc(&m->d_ctx, static_cast<size_t>(NH) * R * 4) ||
+      cudaMalloc(&m->d_concat, static_cast<size_t>(NH) * VD * 4) || cudaMalloc(&m->d_act, (act ? act : 1) * 4) ||
+      cudaMalloc(&m->d_expout, static_cast<size_t>(n_seg ? n_seg : 1) * H * 4) ||
+      cudaMalloc(&m->d_scores, (d->n_experts ? d->n_experts : 1) * 4) ||
+      cudaMalloc(&m->d_logits, static_cast<size_t>(d->vocab_padded) * 4) ||
+      cudaMalloc(&m->d_wts, L_ * topk * 4) || cudaMalloc(&m->d_ids, L_ * topk * 4) ||
+      cudaMalloc(&m->d_route_counter, 4) || cudaMalloc(&m->d_argmax, 8) ||
+      cudaMalloc(&m->d_state, sizeof(StepState)) || cudaMalloc(&m->d_status, kStatusWords * 4))
+    return fail(ZGPU_ERR_OUT_OF_MEMORY, "activation buffers");
+  const unsigned long long init = kArgmaxInitKey;
+  cudaMemcpy(m->d_argmax, &init, 8, cudaMemcpyHostToDevice);
+  cudaMemset(m->d_status, 0, kStatusWords * 4);
+  cudaMemset(m->d_route_counter, 0, 4);
+  cudaMemset(m->d_hidden, 0, H * 4);
+  cudaMemset(m->d_ids, 0, L_ * topk * 4);
+  cudaMemset(m->d_wts, 0, L_ * topk * 4);
+  for (auto &ev : m->ev) cudaEventCreate(&ev);
+  e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail(ZGPU_ERR_CUDA, std::string("ds2 upload: ") + cudaGetErrorString(e));
+  *out = m;
+  return ZGPU_OK;
+}
+
+zgpu_status zgpu_ds2_forward_single_token(zgpu_ds2_model *m, zgpu_mla_kv *kv, uint32_t token,
+                                          uint32_t pos, float *hidden_out) {
+  if (!m || !kv) return ZGPU_ERR_INVALID_ARG;
+  zgpu_ctx *ctx = m->ctx;
+  cudaSetDevice(ctx->device);
+  zgpu_status s = ds2_prepare_kv(m, kv);
+  if (s) return s;
+  if (pos >= kv->max_tokens) return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "position beyond the cache");
+  if (token >= m->desc.vocab_padded) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "token id beyond the vocab");
+  cudaError_t e = grow(&m->d_prompt, &m->prompt_cap, 1);
+  if (e == cudaSuccess) e = grow(&m->d_tokens, &m->tokens_cap, 1);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "state buffers");
+  if ((s = ds2_set_state(m, 1, pos, m->desc.vocab_real, 1))) return s;
+  const bool use_graph = !(ctx->flags & ZGPU_FLAG_NO_GRAPH);
+  if (use_graph && (s = ds2_build_graphs(m, kv))) return s;
+  e = cudaMemcpyAsync(m->d_prompt, &token, 4, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) {
+    if (use_graph) {
+      e = cudaGraphLaunch(m->fwd_graph, ctx->stream);
+      ctx->launches += m->fwd_kernels;
+    } else {
+      e = ds2_enqueue_forward(m, kv, &ctx->launches);
+    }
+  }
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "forward");
+  if (hidden_out) {
+    e = cudaMemcpyAsync(hidden_out, m->d_hidden, m->desc.hidden * 4, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "hidden d2h");
+  }
+  uint32_t st = 0;
+  if ((s = zgpu_read_device_status(ctx, m->d_status, &st))) return s;
+  return zgpu_map_device_status(ctx, st);
+}
+
+zgpu_status zgpu_ds2_lm_head_argmax(zgpu_ds2_model *m, uint32_t vocab_real, uint32_t *token_out,
+                                    float *logits_out) {
+  if (!m || !token_out) return ZGPU_ERR_INVALID_ARG;
+  zgpu_ctx *ctx = m->ctx;
+  cudaSetDevice(ctx->device);
+  if (vocab_real > m->desc.vocab_padded) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "vocab_real > padded");
+  cudaError_t e = grow(&m->d_prompt, &m->prompt_cap, 1);
+  if (e == cudaSuccess) e = grow(&m->d_tokens, &m->tokens_cap, 1);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "state buffers");
+  zgpu_status s = ds2_set_state(m, 1, 0, vocab_real, 1);
+  if (s) return s;
+  const bool use_graph = !(ctx->flags & ZGPU_FLAG_NO_GRAPH) && m->lm_graph;
+  if (use_graph) {
+    e = cudaGraphLaunch(m->lm_graph, ctx->stream);
+    ctx->launches += m->lm_kernels;
+  } else {
+    e = ds2_enqueue_lm_head(m, &ctx->launches);
+  }
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "lm head");
+  if (logits_out) {
+    e = cudaMemcpyAsync(logits_out, m->d_logits, static_cast<size_t>(m->desc.vocab_padded) * 4,
+                        cudaMemcpyDeviceToHost, ctx->stream);
+    if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "logits d2h");
+  }
+  e = cudaMemcpyAsync(token_out, m->d_tokens, 4, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "token d2h");
+  uint32_t st = 0;
+  if ((s = zgpu_read_device_status(ctx, m->d_status, &st))) return s;
+  return zgpu_map_device_status(ctx, st);
+}
+
+zgpu_status zgpu_ds2_expert_ids(zgpu_ds2_model *m, uint32_t *ids_out, float *weights_out) {
+  if (!m) return ZGPU_ERR_INVALID_ARG;
+  zgpu_ctx *ctx = m->ctx;
+  cudaSetDevice(ctx->device);
+  bool any_moe = false;
+  for (const Ds2Layer &L : m->layers) any_moe |= L.moe != 0;
+  const size_t n = static_cast<size_t>(m->desc.n_layers) * (any_moe ? m->desc.top_k : 1);
+  cudaError_t e = cudaSuccess;
+  if (ids_out) e = cudaMemcpyAsync(ids_out, m->d_ids, n * 4, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess && weights_out)
+    e = cudaMemcpyAsync(weights_out, m->d_wts, n * 4, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "expert ids");
+  return ZGPU_OK;
+}
+
+zgpu_status zgpu_ds2_generate_greedy(zgpu_ds2_model *m, zgpu_mla_kv *kv, const uint32_t *prompt,
+                                     uint32_t n_prompt, uint32_t n_gen, uint32_t *tokens_out,
+                                     float *logits_out) {
+  if (!m || !kv || !prompt || !tokens_out || n_prompt == 0 || n_gen == 0) return ZGPU_ERR_INVALID_ARG;
+  zgpu_ctx *ctx = m->ctx;
+  cudaSetDevice(ctx->device);
+  zgpu_status s = ds2_prepare_kv(m, kv);
+  if (s) return s;
+  const uint32_t steps = n_prompt + n_gen - 1;
+  if (steps > kv->max_tokens)
+    return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "prompt + generation exceeds the cache");
+  for (uint32_t i = 0; i < n_prompt; ++i)
+    if (prompt[i] >= m->desc.vocab_padded) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "prompt id beyond the vocab");
+  cudaError_t e = grow(&m->d_prompt, &m->prompt_cap, n_prompt);
+  if (e == cudaSuccess) e = grow(&m->d_tokens, &m->tokens_cap, n_gen);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "state buffers");
+  if ((s = ds2_set_state(m, n_prompt, 0, m->desc.vocab_real, n_gen))) return s;
+  e = cudaMemcpyAsync(m->d_prompt, prompt, n_prompt * 4, cudaMemcpyHostToDevice, ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "prompt upload");
+  const bool use_graph = !(ctx->flags & ZGPU_FLAG_NO_GRAPH);
+  if (use_graph && (s = ds2_build_graphs(m, kv))) return s;
+  const size_t V = m->desc.vocab_padded;
+  uint32_t launches = 0, prefill_launches = 0;
+  auto run_step = [&](uint32_t step) -> cudaError_t {
+    cudaError_t err;
+    if (use_graph) {
+      err = cudaGraphLaunch(m->step_graph, ctx->stream);
+      launches += m->step_kernels;
+    } else {
+      err = ds2_enqueue_forward(m, kv, &launches);
+      if (err == cudaSuccess) err = ds2_enqueue_lm_head(m, &launches);
+    }
+    if (err == cudaSuccess && logits_out && step + 1 >= n_prompt)
+      err = cudaMemcpyAsync(logits_out + static_cast<size_t>(step + 1 - n_prompt) * V, m->d_logits, V * 4,
+                            cudaMemcpyDeviceToHost, ctx->stream);
+    return err;
+  };
+  cudaEventRecord(m->ev[0], ctx->stream);
+  for (uint32_t st = 0; st < n_prompt && e == cudaSuccess; ++st) e = run_step(st);
+  prefill_launches = launches;
+  cudaEventRecord(m->ev[1], ctx->stream);
+  for (uint32_t st = n_prompt; st < steps && e == cudaSuccess; ++st) e = run_step(st);
+  cudaEventRecord(m->ev[2], ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "generate");
+  e = cudaMemcpyAsync(tokens_out, m->d_tokens, n_gen * 4, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "tokens d2h");
+  uint32_t st = 0;
+  if ((s = zgpu_read_device_status(ctx, m->d_status, &st))) return s;
+  float pre = 0.f, dec = 0.f;
+  cudaEventElapsedTime(&pre, m->ev[0], m->ev[1]);
+  cudaEventElapsedTime(&dec, m->ev[1], m->ev[2]);
+  m->perf.steps = n_gen - 1;
+  m->perf.kernel_launches = launches;
+  m->perf.decode_launches = launches - prefill_launches;
+  m->perf.prefill_ms = pre;
+  m->perf.decode_ms = dec;
+  ctx->launches += launches;
+  return zgpu_map_device_status(ctx, st);
+}
+
+zgpu_status zgpu_ds2_perf_snapshot(const zgpu_ds2_model *m, zgpu_perf *out) {
+  if (!m || !out) return ZGPU_ERR_INVALID_ARG;
+  *out = m->perf;
+  return ZGPU_OK;
+}
+
+}  // extern "C"

@@ -80,6 +80,9 @@ struct KParams {
   float *out;
   unsigned long long *argmax;
   uint32_t *status;
+  // segmented launch (GemvDesc::seg_w): units / wbytes are per segment
+  const unsigned long long *seg_w;
+  uint32_t ctas_per_seg, seg_x_stride, seg_out_stride, seg_dynamic;
 };
 
 template <int QT, int PRO, int EPI>
@@ -97,7 +100,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
   uint64_t *full = reinterpret_cast<uint64_t *>(ring + static_cast<size_t>(kWarps) * S * slot_bytes);
   uint64_t *empty = full + kWarps * S;
 
-  const uint32_t u0 = blockIdx.x * p.units_per_cta;
+  // segment of this CTA (a plain launch is one segment at p.w)
+  uint32_t seg = 0, cta = blockIdx.x;
+  if (p.seg_w) {
+    seg = blockIdx.x / p.ctas_per_seg;
+    cta = blockIdx.x - seg * p.ctas_per_seg;
+  }
+  const float *xin = p.x + static_cast<size_t>(seg) * p.seg_x_stride;
+  float *yout = p.out + static_cast<size_t>(seg) * p.seg_out_stride;
+  const uint32_t u0 = cta * p.units_per_cta;
   const uint32_t u1 = min(u0 + p.units_per_cta, p.units);
   const uint32_t nloc = u1 > u0 ? u1 - u0 : 0;
   const uint32_t nitems = nloc * p.ks;
@@ -116,6 +127,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
     // ---------------- producer: lane w feeds consumer warp w's slots ----------
     if (lane < kWarps) {
       const uint64_t pol = l2_evict_first_policy();
+      const uint8_t *w = p.w;
+      if (p.seg_w) {
+        if (p.seg_dynamic) pdl_wait();   // the table is the previous kernel's output
+        w = reinterpret_cast<const uint8_t *>(__ldcg(p.seg_w + seg));
+      }
       uint32_t issued = 0;
       for (uint32_t k = lane, j = 0; k < nitems; k += kWarps, ++j) {
         const uint32_t slot = lane * S + (j % S);
@@ -132,8 +148,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
         const uint32_t fb = smem_addr(&full[slot]);
         const uint32_t dst = smem_addr(ring + static_cast<size_t>(slot) * slot_bytes);
         mbar_arrive_expect_tx(fb, 2 * bytes);
-        tma_bulk_g2s(dst, p.w + src, bytes, fb, pol);
-        tma_bulk_g2s(dst + p.half_bytes, p.w + src + p.gstride, bytes, fb, pol);
+        tma_bulk_g2s(dst, w + src, bytes, fb, pol);
+        tma_bulk_g2s(dst + p.half_bytes, w + src + p.gstride, bytes, fb, pol);
         ++issued;
       }
       // Drain: never leave a copy in flight when the CTA may exit.
@@ -150,14 +166,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
   const uint32_t tid = threadIdx.x;
   const uint32_t nf4 = p.in_dim / 4;
   float inv = 1.0f;
-  if (PRO == PRO_RMSNORM) inv = rms_inv<kWarps>(p.x, p.in_dim, p.eps, red, tid, 1);
+  if (PRO == PRO_RMSNORM) inv = rms_inv<kWarps>(xin, p.in_dim, p.eps, red, tid, 1);
   // Warp-uniform trip count: the per-block statistics shuffle across the 8
   // lanes of a block, and nf4 is a multiple of 8, so a block's lanes are
   // either all in range or all out of range.
   for (uint32_t f0 = warp * 32; f0 < nf4; f0 += kConsumers) {
     const uint32_t f = f0 + lane;
     const bool valid = f < nf4;
-    float4 t = valid ? __ldcg(reinterpret_cast<const float4 *>(p.x) + f) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 t = valid ? __ldcg(reinterpret_cast<const float4 *>(xin) + f) : make_float4(0.f, 0.f, 0.f, 0.f);
     if (PRO == PRO_RMSNORM && valid) {
       const float4 g = reinterpret_cast<const float4 *>(p.norm_w)[f];
       t.x = __fmul_rn(__fmul_rn(t.x, inv), g.x);
@@ -202,7 +218,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
         yu += part[(ul * p.ks + c) * kRows + 4 + r];
       }
       const uint32_t row = (u0 + ul) * 4 + r;
-      if (row < p.rows) p.out[row] = ref_silu_mul(yg, yu);
+      if (row < p.rows) yout[row] = ref_silu_mul(yg, yu);
     }
   } else {
     for (uint32_t t = tid; t < nloc * kRows; t += kConsumers) {
@@ -212,11 +228,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
       const uint32_t row = (u0 + ul) * kRows + r;
       if (row < p.rows) {
         if (EPI == EPI_STORE) {
-          p.out[row] = y;
+          yout[row] = y;
         } else if (EPI == EPI_RESADD) {
-          p.out[row] = p.out[row] + y;
+          yout[row] = yout[row] + y;
         } else {
-          p.out[row] = y;
+          yout[row] = y;
           const unsigned long long key = argmax_key(y, row);
           best = key > best ? key : best;
         }
@@ -318,8 +334,21 @@ cudaError_t launch_gemv(const GemvDesc &g, GemvPro pro, GemvEpi epi, const GemvI
   kp.in_dim = g.in_dim;
   kp.units = g.groups / 2;
   const uint32_t ctas = static_cast<uint32_t>((lc.sm_count > 0 ? lc.sm_count : 148) * kCtasPerSm);
-  kp.units_per_cta = (kp.units + ctas - 1) / ctas;
-  const uint32_t grid = (kp.units + kp.units_per_cta - 1) / kp.units_per_cta;
+  uint32_t grid = 0;
+  if (g.seg_w) {
+    if (g.seg_count == 0 || !g.wbytes) return cudaErrorInvalidValue;
+    const uint64_t total = static_cast<uint64_t>(kp.units) * g.seg_count;
+    kp.units_per_cta = static_cast<uint32_t>((total + ctas - 1) / ctas);
+    kp.ctas_per_seg = (kp.units + kp.units_per_cta - 1) / kp.units_per_cta;
+    grid = kp.ctas_per_seg * g.seg_count;
+    kp.seg_w = g.seg_w;
+    kp.seg_x_stride = g.seg_x_stride;
+    kp.seg_out_stride = g.seg_out_stride;
+    kp.seg_dynamic = g.seg_dynamic ? 1u : 0u;
+  } else {
+    kp.units_per_cta = (kp.units + ctas - 1) / ctas;
+    grid = (kp.units + kp.units_per_cta - 1) / kp.units_per_cta;
+  }
   kp.half_bytes = static_cast<uint32_t>(chunk_bytes(g.quant, min(kChunkBlocks, kp.bpr)));
   const size_t slot = 2 * static_cast<size_t>(kp.half_bytes);
   // activation image: 128 B per block

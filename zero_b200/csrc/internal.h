@@ -36,6 +36,16 @@ struct GemvDesc {
   uint32_t groups;            // groups in the launch
   uint32_t in_dim;
   uint64_t wbytes = 0;        // bytes of the weight buffer (bounds checks)
+  // Segmented launch: seg_count segments of `groups` groups each.  Segment s
+  // streams its groups from the device address seg_w[s] (wbytes bytes from
+  // there), reads its input at x + s * seg_x_stride and writes out + s *
+  // seg_out_stride (floats).  No CTA spans two segments.  seg_dynamic: the
+  // table is written by the preceding kernel, so the weight prefetch waits
+  // for it (programmatic dependent launch) instead of starting early.
+  const unsigned long long *seg_w = nullptr;
+  uint32_t seg_count = 0;
+  uint32_t seg_x_stride = 0, seg_out_stride = 0;
+  bool seg_dynamic = false;
 };
 
 enum GemvPro { PRO_PLAIN = 0, PRO_RMSNORM = 1 };
@@ -81,6 +91,8 @@ struct zgpu_ctx {
   size_t d_attn_part_cap = 0;
   uint32_t *d_attn_counters = nullptr;
   uint32_t d_attn_counters_cap = 0;
+  // arrival counter of the MoE router entry point (zero between calls)
+  uint32_t *d_route_counter = nullptr;
 };
 
 // KV cache: layer-major [L][K block | V block], block = max_tokens x n_kv x
@@ -96,3 +108,8 @@ struct zgpu_kv {
 zgpu_status zgpu_fail(zgpu_ctx *ctx, zgpu_status s, const std::string &msg);
 zgpu_status zgpu_cuda_fail(zgpu_ctx *ctx, cudaError_t e, const char *what);
 const zgpu::DeviceTensor *zgpu_lookup(const zgpu_ctx *ctx, const void *key);
+// Copy a device status block back (synchronising the context stream), clear
+// it when set and report a failed device bounds check; then map its error
+// bits to a zgpu_status.
+zgpu_status zgpu_read_device_status(zgpu_ctx *ctx, uint32_t *d_status, uint32_t *st_out);
+zgpu_status zgpu_map_device_status(zgpu_ctx *ctx, uint32_t st);

@@ -1,0 +1,283 @@
+// mla.cu — multi-head latent attention (MLA) decode over the compressed
+// latent cache.
+//
+// Replaces mla_attention_single_token (crates/zero-llm-inference/src/mla.rs:
+// 122-414) between the projections.  The reference re-expands every cached
+// latent through kv_b twice per step (O(t * kv_b) work).  Here the
+// projection is absorbed instead:
+//   score_h,t = q_nope_h . (W_kn_h c_t) + q_rope_h . k_rope_t
+//             = (W_kn_h^T q_nope_h) . c_t + q_rope_h . k_rope_t,
+//   out_h     = sum_t p_h,t (W_v_h c_t) = W_v_h (sum_t p_h,t c_t),
+// so attention reads only the cache's [kv_lora | rope] rows, all heads share
+// every row (one CTA walks a token range for all heads), and the V
+// projection is one GEMV per head after the merge (the segmented GEMV of
+// gemv.cu).  The sums are reordered relative to the reference: results agree
+// to f32 rounding, not bit for bit.
+//
+//   mla_prep   CTA h < n_heads: stage head h's k_nope rows of kv_b (one
+//              contiguous slab of group streams) in shared memory, rotate
+//              q_rope (mla.rs:229-252 RoPE), q_abs_h = W_kn_h^T q_nope_h;
+//              last CTA: rmsnorm(c_kv, kv_a_norm), optional k_rope RMS norm,
+//              RoPE at pos, append [c_kv | k_rope] at pos (store_compressed,
+//              kv_cache.rs:318).
+//   mla_attn   CTA s: tokens [16 s, 16 s + 16) of [0, pos]; warp per head,
+//              lane per 32nd latent column: online softmax (scale 1 /
+//              sqrt(nope + rope)), partial (m, l, sum p c) per head.
+//   mla_merge  CTA per (head, 128 columns): merge the splits in order into
+//              ctx_h; a non-finite max or a sum <= 0 raises the
+//              NumericalInstability status (attention.rs:48-84).
+#include <cfloat>
+#include <cmath>
+
+#include "common.cuh"
+#include "internal.h"
+#include "layout.h"
+#include "mla.h"
+#include "ops.h"
+
+namespace zgpu {
+
+namespace {
+
+constexpr size_t kMlaSlabMax = 200 * 1024;
+constexpr uint32_t kMlaAttnWarpsMax = 16;
+constexpr uint32_t kMlaMergeThreads = 128;
+
+__device__ __forceinline__ uint32_t mla_pos(const MlaParams &p) {
+  return p.pos_ptr ? *p.pos_ptr : p.pos_value;
+}
+
+// Fixed-order block sum over kMlaPrepThreads threads (thread partials, xor
+// tree per warp, warps in order).  Every thread gets the total.
+__device__ __forceinline__ float prep_block_sum(float v, float *red) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (uint32_t w = 0; w < kMlaPrepThreads / 32; ++w) s = __fadd_rn(s, red[w]);
+  return s;
+}
+
+__device__ __forceinline__ void rope_pair(float x0, float x1, float theta, float *o0, float *o1) {
+  float s, c;
+  sincosf(theta, &s, &c);
+  *o0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+  *o1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+}
+
+__global__ void __launch_bounds__(kMlaPrepThreads) mla_prep_kernel(const MlaParams p) {
+  extern __shared__ __align__(16) uint8_t slab[];
+  __shared__ float qn[kMlaMaxNope];
+  __shared__ float red[kMlaPrepThreads / 32];
+  __shared__ float kr[kMlaMaxRope];
+  pdl_launch_dependents();
+  const uint32_t tid = threadIdx.x;
+  const uint32_t R = p.kv_lora, RD = p.rope, half = RD / 2;
+  if (blockIdx.x < p.n_heads) {
+    const uint32_t h = blockIdx.x;
+    // the weights do not depend on the previous kernel: stage them first
+    const uint4 *src = reinterpret_cast<const uint4 *>(
+        p.kb + static_cast<uint64_t>(h * p.kb_head_rows / 4) * p.kb_gstride);
+    uint4 *dst = reinterpret_cast<uint4 *>(slab);
+    for (uint32_t i = tid; i < p.slab_bytes / 16; i += kMlaPrepThreads) dst[i] = __ldg(src + i);
+    pdl_wait();
+    const uint32_t pos = mla_pos(p);
+    const float *qh = p.q + static_cast<size_t>(h) * (p.nope + RD);
+    for (uint32_t i = tid; i < p.nope; i += kMlaPrepThreads) qn[i] = __ldcg(qh + i);
+    if (tid < half) {
+      const float theta = __fmul_rn(static_cast<float>(pos), p.inv_freqs[tid]);
+      float o0, o1;
+      rope_pair(__ldcg(qh + p.nope + tid), __ldcg(qh + p.nope + tid + half), theta, &o0, &o1);
+      p.q_pe[static_cast<size_t>(h) * RD + tid] = o0;
+      p.q_pe[static_cast<size_t>(h) * RD + tid + half] = o1;
+    }
+    __syncthreads();
+    const uint32_t bpr = R / 32;
+    for (uint32_t c = tid; c < R; c += kMlaPrepThreads) {
+      const uint32_t b = c >> 5, e = c & 31;
+      const uint64_t sc_off = scale_entry(p.kb_quant, bpr, b);
+      float acc = 0.f;
+      if (p.kb_quant == ZGPU_Q4_0) {
+#pragma unroll 4
+        for (uint32_t i = 0; i < p.nope; ++i) {
+          const uint8_t *g = slab + static_cast<size_t>(i >> 2) * p.kb_gstride;
+          const uint32_t r = i & 3;
+          const float d = h2f(*reinterpret_cast<const uint16_t *>(g + sc_off + 2 * r));
+          const uint8_t byte = g[plane_entry(ZGPU_Q4_0, bpr, b, r) + (e & 15)];
+          const int n = (e < 16) ? (byte & 0x0F) : (byte >> 4);
+          acc = fmaf(qn[i], __fmul_rn(d, static_cast<float>(n - 8)), acc);
+        }
+      } else {
+#pragma unroll 4
+        for (uint32_t i = 0; i < p.nope; ++i) {
+          const uint8_t *g = slab + static_cast<size_t>(i >> 2) * p.kb_gstride;
+          const uint32_t r = i & 3;
+          const float d = h2f(*reinterpret_cast<const uint16_t *>(g + sc_off + 2 * r));
+          const int8_t q = static_cast<int8_t>(g[plane_entry(ZGPU_Q8_0, bpr, b, 2 * r + (e >> 4)) + (e & 15)]);
+          acc = fmaf(qn[i], __fmul_rn(d, static_cast<float>(q)), acc);
+        }
+      }
+      p.q_abs[static_cast<size_t>(h) * R + c] = acc;
+    }
+    return;
+  }
+  // ---- the latent CTA: normalise, rotate and append this token's row ----
+  pdl_wait();
+  const uint32_t pos = mla_pos(p);
+  if (pos >= p.max_tokens) {
+    if (tid == 0) atomicOr(p.status, ZDEV_ERR_BOUNDS);
+    return;
+  }
+  float *row = p.cache + static_cast<size_t>(pos) * (R + RD);
+  float ss = 0.f;
+  for (uint32_t i = tid; i < R; i += kMlaPrepThreads) {
+    const float v = __ldcg(p.kv_a + i);
+    ss = __fadd_rn(ss, __fmul_rn(v, v));
+  }
+  const float tot = prep_block_sum(ss, red);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(R)), p.eps)));
+  for (uint32_t i = tid; i < R; i += kMlaPrepThreads)
+    row[i] = __fmul_rn(__fmul_rn(__ldcg(p.kv_a + i), inv), p.kv_a_norm[i]);
+  float v = tid < RD ? __ldcg(p.kv_a + R + tid) : 0.f;
+  if (p.k_norm) {   // mla.rs:180-196
+    const float t2 = prep_block_sum(__fmul_rn(v, v), red);
+    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(t2, static_cast<float>(RD)), p.eps));
+    const float inv2 = __fdiv_rn(1.0f, rms);
+    if (tid < RD) v = __fmul_rn(__fmul_rn(v, inv2), p.k_norm[tid]);
+  }
+  if (tid < RD) kr[tid] = v;
+  __syncthreads();
+  if (tid < half) {
+    const float theta = __fmul_rn(static_cast<float>(pos), p.inv_freqs[tid]);
+    float o0, o1;
+    rope_pair(kr[tid], kr[tid + half], theta, &o0, &o1);
+    row[R + tid] = o0;
+    row[R + tid + half] = o1;
+  }
+}
+
+__global__ void __launch_bounds__(32 * kMlaAttnWarpsMax) mla_attn_kernel(const MlaParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t pos = mla_pos(p);
+  if (pos >= p.max_tokens) return;   // reported by mla_prep
+  const uint32_t R = p.kv_lora, RD = p.rope, nr = R / 32;
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const uint32_t split = blockIdx.x;
+  const uint32_t t0 = split * kMlaSplitTokens;
+  if (t0 > pos) return;   // beyond the context: the merge reads only splits <= pos / 16
+  const uint32_t t1 = min(t0 + kMlaSplitTokens, pos + 1);
+  for (uint32_t h = warp; h < p.n_heads; h += nw) {
+    float qa[16], acc[16], qp[2];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      qa[j] = (j < static_cast<int>(nr)) ? __ldcg(p.q_abs + static_cast<size_t>(h) * R + lane + 32 * j) : 0.f;
+      acc[j] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+      qp[j] = (lane + 32 * j < RD) ? __ldcg(p.q_pe + static_cast<size_t>(h) * RD + lane + 32 * j) : 0.f;
+    float m = -INFINITY, l = 0.f;
+    for (uint32_t t = t0; t < t1; ++t) {
+      const float *ct = p.cache + static_cast<size_t>(t) * (R + RD);
+      float cv[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) cv[j] = (j < static_cast<int>(nr)) ? __ldg(ct + lane + 32 * j) : 0.f;
+      float d = 0.f;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        if (lane + 32 * j < RD) d = fmaf(qp[j], __ldg(ct + R + lane + 32 * j), d);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) d = fmaf(qa[j], cv[j], d);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+      const float s = __fmul_rn(d, p.scale);
+      const float mn = fmaxf(m, s);
+      const float corr = (m == mn) ? 1.0f : expf(m - mn);
+      const float pe = (s == -INFINITY) ? 0.0f : expf(s - mn);
+      l = fmaf(l, corr, pe);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[j] = fmaf(acc[j], corr, pe * cv[j]);
+      m = mn;
+    }
+    float *pp = p.part + (static_cast<size_t>(h) * p.max_splits + split) * (R + 2);
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < static_cast<int>(nr)) pp[lane + 32 * j] = acc[j];
+    if (lane == 0) {
+      pp[R] = m;
+      pp[R + 1] = l;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kMlaMergeThreads) mla_merge_kernel(const MlaParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t pos = mla_pos(p);
+  if (pos >= p.max_tokens) return;
+  const uint32_t R = p.kv_lora;
+  const uint32_t nq = (R + kMlaMergeThreads - 1) / kMlaMergeThreads;
+  const uint32_t h = blockIdx.x / nq;
+  const uint32_t c = (blockIdx.x % nq) * kMlaMergeThreads + threadIdx.x;
+  const uint32_t nsplit = (pos + kMlaSplitTokens) / kMlaSplitTokens;
+  const float *pb = p.part + static_cast<size_t>(h) * p.max_splits * (R + 2);
+  float M = -INFINITY;
+  for (uint32_t s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(pb + static_cast<size_t>(s) * (R + 2) + R));
+  float L = 0.f, A = 0.f;
+  for (uint32_t s = 0; s < nsplit; ++s) {
+    const float *ps = pb + static_cast<size_t>(s) * (R + 2);
+    const float ms = __ldcg(ps + R);
+    const float f = (ms == -INFINITY) ? 0.0f : expf(ms - M);
+    L = fmaf(f, __ldcg(ps + R + 1), L);
+    if (c < R) A = fmaf(f, __ldcg(ps + c), A);
+  }
+  const bool bad = !(fabsf(M) <= FLT_MAX) || !(L > 0.0f) || !(L <= FLT_MAX);
+  if (bad && c == 0) atomicOr(p.status, ZDEV_ERR_NUMERICAL);
+  if (c < R) p.ctx[static_cast<size_t>(h) * R + c] = bad ? 0.0f : __fdiv_rn(A, L);
+}
+
+}  // namespace
+
+cudaError_t mla_setup() {
+  return cudaFuncSetAttribute(mla_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(kMlaSlabMax));
+}
+
+cudaError_t launch_mla_prep(const MlaParams &mp, const LaunchCfg &lc) {
+  if (mp.kv_lora == 0 || mp.kv_lora % 32 || mp.kv_lora > kMlaMaxLatent || mp.rope % 2 ||
+      mp.rope > kMlaMaxRope || mp.nope == 0 || mp.nope % 4 || mp.nope > kMlaMaxNope ||
+      mp.kb_head_rows % 4 || mp.n_heads == 0 || (mp.kv_lora + mp.rope) % 4 ||
+      (mp.kb_quant != ZGPU_Q4_0 && mp.kb_quant != ZGPU_Q8_0))
+    return cudaErrorInvalidValue;
+  MlaParams p = mp;
+  const uint64_t slab = static_cast<uint64_t>(p.nope / 4) * p.kb_gstride;
+  if (slab > kMlaSlabMax || p.kb_gstride % 16) return cudaErrorInvalidValue;
+  p.slab_bytes = static_cast<uint32_t>(slab);
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = make_launch_cfg(dim3(p.n_heads + 1), dim3(kMlaPrepThreads), slab, lc, attr);
+  if (lc.launch_counter) ++*lc.launch_counter;
+  return cudaLaunchKernelEx(&cfg, mla_prep_kernel, p);
+}
+
+cudaError_t launch_mla_attention(const MlaParams &p, const LaunchCfg &lc) {
+  if (p.kv_lora == 0 || p.kv_lora % 32 || p.kv_lora > kMlaMaxLatent || p.rope > kMlaMaxRope ||
+      p.max_splits < mla_max_splits(p.max_tokens) || p.n_heads == 0)
+    return cudaErrorInvalidValue;
+  const uint32_t warps = p.n_heads < kMlaAttnWarpsMax ? p.n_heads : kMlaAttnWarpsMax;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = make_launch_cfg(dim3(mla_max_splits(p.max_tokens)), dim3(32 * warps), 0, lc, attr);
+  if (lc.launch_counter) ++*lc.launch_counter;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, mla_attn_kernel, p);
+  if (e != cudaSuccess) return e;
+  const uint32_t nq = (p.kv_lora + kMlaMergeThreads - 1) / kMlaMergeThreads;
+  cudaLaunchAttribute attr2[1];
+  cudaLaunchConfig_t cfg2 = make_launch_cfg(dim3(p.n_heads * nq), dim3(kMlaMergeThreads), 0, lc, attr2);
+  if (lc.launch_counter) ++*lc.launch_counter;
+  return cudaLaunchKernelEx(&cfg2, mla_merge_kernel, p);
+}
+
+}  // namespace zgpu

@@ -1,0 +1,52 @@
+// mla.h — multi-head latent attention decode kernels (mla.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "internal.h"
+
+namespace zgpu {
+
+constexpr uint32_t kMlaSplitTokens = 16;   // cached tokens per attention CTA
+constexpr uint32_t kMlaMaxLatent = 512;    // kv_lora_rank
+constexpr uint32_t kMlaMaxRope = 64;       // qk_rope_head_dim
+constexpr uint32_t kMlaMaxNope = 256;      // qk_nope_head_dim
+constexpr uint32_t kMlaPrepThreads = 512;
+
+struct MlaParams {
+  const float *kv_a;          // [kv_lora + rope]: W_kv_a_mqa . rmsnorm(hidden)
+  const float *kv_a_norm;     // [kv_lora]
+  const float *k_norm;        // [rope] or null
+  const float *q;             // [n_heads][nope + rope]: W_q_b . rmsnorm(c_q)
+  const uint8_t *kb;          // group streams holding each head's k_nope rows (kv_b or k_b)
+  uint64_t kb_gstride;
+  uint32_t kb_quant;
+  uint32_t kb_head_rows;      // rows from one head's first k_nope row to the next head's
+  const float *inv_freqs;     // [rope / 2]: powf(base, -2 i / rope)
+  float *cache;               // this layer's [max_tokens][kv_lora + rope]
+  uint32_t max_tokens;
+  const uint32_t *pos_ptr;    // device position, or null for pos_value
+  uint32_t pos_value;
+  float *q_abs;               // [n_heads][kv_lora]: W_k_nope^T q_nope per head
+  float *q_pe;                // [n_heads][rope]: rotated q_rope
+  float *ctx;                 // [n_heads][kv_lora]: sum_t p_t c_kv_t
+  float *part;                // [n_heads][max_splits][kv_lora + 2]
+  uint32_t *status;
+  uint32_t n_heads, kv_lora, rope, nope, max_splits;
+  float eps, scale;
+  uint32_t slab_bytes;        // shared bytes of one head's k_nope slab (set by the launcher)
+};
+
+// Splits (attention CTAs) a cache of max_tokens needs.
+inline uint32_t mla_max_splits(uint32_t max_tokens) {
+  return (max_tokens + kMlaSplitTokens - 1) / kMlaSplitTokens;
+}
+cudaError_t mla_setup();
+// latent RMSNorm + k_rope norm/RoPE + cache append, and the per-head query
+// absorption (q_abs, q_pe)
+cudaError_t launch_mla_prep(const MlaParams &p, const LaunchCfg &lc);
+// split-K attention over the latent cache, then the split merge into ctx
+cudaError_t launch_mla_attention(const MlaParams &p, const LaunchCfg &lc);
+
+}  // namespace zgpu

@@ -71,6 +71,35 @@ struct zgpu_model {
   bool last_fwd_persistent = false; // the path the last forward used (the LM head follows it)
 };
 
+// Status block of a step: copy back (synchronising the stream), clear it
+// when set, report a failed device bounds check.
+zgpu_status zgpu_read_device_status(zgpu_ctx *ctx, uint32_t *d_status, uint32_t *st_out) {
+  uint32_t sw[kStatusWords] = {0};
+  cudaError_t e = cudaMemcpyAsync(sw, d_status, sizeof(sw), cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "step status");
+  *st_out = sw[0];
+  if (sw[0]) cudaMemsetAsync(d_status, 0, sizeof(sw), ctx->stream);
+  if (sw[1])
+    return zgpu_fail(ctx, ZGPU_ERR_CUDA, "device bounds check " + std::to_string(sw[1]) + " failed (" +
+                                             std::to_string(sw[2]) + ", " + std::to_string(sw[3]) + ")");
+  return ZGPU_OK;
+}
+
+zgpu_status zgpu_map_device_status(zgpu_ctx *ctx, uint32_t st) {
+  if (!st) return ZGPU_OK;
+  if (st & ZDEV_ERR_TIMEOUT) return zgpu_fail(ctx, ZGPU_ERR_DEVICE_TIMEOUT, "device wait timed out");
+  if (st & ZDEV_ERR_BOUNDS)
+    return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "token or position outside the cache");
+  if (st & ZDEV_ERR_NUMERICAL)
+    return zgpu_fail(ctx, ZGPU_ERR_NUMERICAL_INSTABILITY, "softmax: non-finite max or bad sum");
+  if (st & ZDEV_ERR_LM_NONFINITE)
+    return zgpu_fail(ctx, ZGPU_ERR_LM_NON_FINITE_LOGITS, "lm head: non-finite max logit");
+  if (st & ZDEV_ERR_LM_PADDING)
+    return zgpu_fail(ctx, ZGPU_ERR_LM_ARGMAX_IN_PADDING, "lm head: argmax in padding region");
+  return zgpu_fail(ctx, ZGPU_ERR_CUDA, "device status " + std::to_string(st));
+}
+
 namespace {
 
 float *norm_attn(zgpu_model *m, uint32_t l) { return m->d_norms + static_cast<size_t>(l) * m->desc.hidden; }
@@ -275,32 +304,10 @@ zgpu_status build_graphs(zgpu_model *m, zgpu_kv *kv) {
 }
 
 zgpu_status read_status(zgpu_model *m, uint32_t *st_out) {
-  zgpu_ctx *ctx = m->ctx;
-  uint32_t sw[kStatusWords] = {0};
-  cudaError_t e = cudaMemcpyAsync(sw, m->d_status, sizeof(sw), cudaMemcpyDeviceToHost, ctx->stream);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
-  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "step status");
-  *st_out = sw[0];
-  if (sw[0]) cudaMemsetAsync(m->d_status, 0, sizeof(sw), ctx->stream);
-  if (sw[1])
-    return zgpu_fail(ctx, ZGPU_ERR_CUDA, "device bounds check " + std::to_string(sw[1]) + " failed (" +
-                                             std::to_string(sw[2]) + ", " + std::to_string(sw[3]) + ")");
-  return ZGPU_OK;
+  return zgpu_read_device_status(m->ctx, m->d_status, st_out);
 }
 
-zgpu_status map_status(zgpu_ctx *ctx, uint32_t st) {
-  if (!st) return ZGPU_OK;
-  if (st & ZDEV_ERR_TIMEOUT) return zgpu_fail(ctx, ZGPU_ERR_DEVICE_TIMEOUT, "device wait timed out");
-  if (st & ZDEV_ERR_BOUNDS)
-    return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "token or position outside the cache");
-  if (st & ZDEV_ERR_NUMERICAL)
-    return zgpu_fail(ctx, ZGPU_ERR_NUMERICAL_INSTABILITY, "softmax: non-finite max or bad sum");
-  if (st & ZDEV_ERR_LM_NONFINITE)
-    return zgpu_fail(ctx, ZGPU_ERR_LM_NON_FINITE_LOGITS, "lm head: non-finite max logit");
-  if (st & ZDEV_ERR_LM_PADDING)
-    return zgpu_fail(ctx, ZGPU_ERR_LM_ARGMAX_IN_PADDING, "lm head: argmax in padding region");
-  return zgpu_fail(ctx, ZGPU_ERR_CUDA, "device status " + std::to_string(st));
-}
+zgpu_status map_status(zgpu_ctx *ctx, uint32_t st) { return zgpu_map_device_status(ctx, st); }
 
 zgpu_status set_state(zgpu_model *m, uint32_t n_prompt, uint32_t pos_base, uint32_t vocab_real,
                       uint32_t n_gen_cap) {

@@ -1,0 +1,236 @@
+// moe.cu — MoE router (moe_route_f32) and the weighted combine of moe_ffn.
+//
+// Router (crates/zero-llm-inference/src/moe.rs:132-317).  Expert ids must be
+// bit-identical to the reference's, so each expert's score is the
+// reference's own sequential f32 dot product: one thread per expert walks
+// the hidden vector in order with separately rounded multiplies and adds
+// (no FMA contraction, no tree).  That chain is latency-bound (dim dependent
+// adds), so the experts are spread over several CTAs that each stage their
+// rows and the input in shared memory with coalesced loads first; the last
+// CTA to finish (arrival counter) runs the replacement-min top-k, the
+// softmax / normalisation over the selected k, the uniform fallbacks and
+// the expert_weight_scale exactly as the reference orders them.  It then
+// writes the dispatch tables of the grouped expert GEMVs: the device
+// address of each selected expert's gate/up and down group streams, shared
+// experts first, so the following launches need no host round trip.
+//
+// Combine (moe.rs:534-589 then forward_pass.rs:894-897): mlp_out = shared
+// outputs (the first written, later ones added), then mlp_out[i] += w_k *
+// expert_k[i] for k in selection order (multiply, then add), then
+// hidden[i] += mlp_out[i].
+#include <cfloat>
+#include <cmath>
+
+#include "common.cuh"
+#include "internal.h"
+#include "moe.h"
+#include "ops.h"
+
+namespace zgpu {
+
+namespace {
+
+constexpr int kRouteThreads = 256;
+constexpr uint32_t kRouteRowFloats = 16384;   // staged router floats per CTA
+
+__device__ __forceinline__ float route_scale(float s) {
+  return (isfinite(s) && s > 0.0f) ? s : 1.0f;
+}
+
+__device__ void route_uniform(float *w, uint32_t k, float scale) {
+  const float u = __fdiv_rn(1.0f, static_cast<float>(k));
+  const float s = route_scale(scale);
+  for (uint32_t i = 0; i < k; ++i) w[i] = (s != 1.0f) ? __fmul_rn(u, s) : u;
+}
+
+__global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const RouteParams p) {
+  extern __shared__ __align__(16) float rsm[];
+  __shared__ float red[kRouteThreads / 32];
+  __shared__ uint32_t s_last;
+  pdl_launch_dependents();
+  const uint32_t tid = threadIdx.x;
+  const uint32_t e0 = blockIdx.x * p.experts_per_cta;
+  const uint32_t e1 = min(e0 + p.experts_per_cta, p.n_experts);
+  const uint32_t ne = e1 > e0 ? e1 - e0 : 0;
+  float *xs = rsm;                       // [dim]
+  float *ws = rsm + p.dim;               // [ne][dim]
+  // the router rows do not depend on the previous kernel: stage them first
+  {
+    const float4 *src = reinterpret_cast<const float4 *>(p.w + static_cast<size_t>(e0) * p.dim);
+    float4 *dst = reinterpret_cast<float4 *>(ws);
+    const uint32_t n4 = ne * p.dim / 4;
+    for (uint32_t i = tid; i < n4; i += kRouteThreads) dst[i] = __ldg(src + i);
+  }
+  pdl_wait();
+  // the routed vector: x itself, or rmsnorm(x) * gain (the model's post-
+  // attention residual) with the GEMV prologue's fixed-order reduction
+  float inv = 1.0f;
+  if (p.norm_w) {
+    float ss = 0.f;
+    for (uint32_t f = tid; f < p.dim / 4; f += kRouteThreads) {
+      const float4 t = __ldcg(reinterpret_cast<const float4 *>(p.x) + f);
+      ss = __fadd_rn(ss, __fadd_rn(__fadd_rn(__fmul_rn(t.x, t.x), __fmul_rn(t.y, t.y)),
+                                   __fadd_rn(__fmul_rn(t.z, t.z), __fmul_rn(t.w, t.w))));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kRouteThreads / 32; ++w) tot = __fadd_rn(tot, red[w]);
+    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(p.dim)), p.eps)));
+  }
+  for (uint32_t i = tid; i < p.dim; i += kRouteThreads) {
+    const float v = __ldcg(p.x + i);
+    xs[i] = p.norm_w ? __fmul_rn(__fmul_rn(v, inv), p.norm_w[i]) : v;
+  }
+  __syncthreads();
+  // moe.rs:168-186: dot += hidden[i] * row[i], i ascending, unfused
+  if (tid < ne) {
+    const float *row = ws + static_cast<size_t>(tid) * p.dim;
+    float dot = 0.0f;
+#pragma unroll 8
+    for (uint32_t i = 0; i < p.dim; ++i) dot = __fadd_rn(dot, __fmul_rn(xs[i], row[i]));
+    const uint32_t e = e0 + tid;
+    float s;
+    if (p.mode == 0) {
+      s = p.bias ? __fadd_rn(dot, p.bias[e]) : dot;
+    } else {
+      s = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-dot)));
+    }
+    p.scores[e] = s;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = (atomicAdd(p.counter, 1u) == gridDim.x - 1) ? 1u : 0u;
+  __syncthreads();
+  if (!s_last || tid != 0) return;
+  __threadfence();
+  *p.counter = 0;   // ready for the next launch (stream-ordered)
+  const uint32_t K = p.top_k;
+  uint32_t idx[kMoeMaxTopK];
+  float wt[kMoeMaxTopK];
+  const bool sel_bias = p.bias && p.mode == 1;
+  // moe.rs:200-232: slots seeded with experts 0..k-1; an expert replaces
+  // the first smallest slot when its key is strictly greater
+  for (uint32_t i = 0; i < K; ++i) {
+    idx[i] = i;
+    wt[i] = sel_bias ? __fadd_rn(__ldcg(p.scores + i), p.bias[i]) : __ldcg(p.scores + i);
+  }
+  uint32_t min_i = 0;
+  float min_v = wt[0];
+  for (uint32_t i = 1; i < K; ++i)
+    if (wt[i] < min_v) { min_v = wt[i]; min_i = i; }
+  for (uint32_t e = K; e < p.n_experts; ++e) {
+    const float key = sel_bias ? __fadd_rn(__ldcg(p.scores + e), p.bias[e]) : __ldcg(p.scores + e);
+    if (key > min_v) {
+      idx[min_i] = e;
+      wt[min_i] = key;
+      min_v = wt[0];
+      min_i = 0;
+      for (uint32_t i = 1; i < K; ++i)
+        if (wt[i] < min_v) { min_v = wt[i]; min_i = i; }
+    }
+  }
+  // moe.rs:238-300: weights from the raw scores of the selected experts
+  for (uint32_t i = 0; i < K; ++i) wt[i] = __ldcg(p.scores + idx[i]);
+  float mx = wt[0];
+  for (uint32_t i = 1; i < K; ++i)
+    if (wt[i] > mx) mx = wt[i];
+  bool uniform = !isfinite(mx);
+  if (!uniform) {
+    float sum = 0.0f;
+    if (p.mode == 0) {
+      for (uint32_t i = 0; i < K; ++i) {
+        wt[i] = expf(__fsub_rn(wt[i], mx));
+        sum = __fadd_rn(sum, wt[i]);
+      }
+    } else {
+      for (uint32_t i = 0; i < K; ++i) sum = __fadd_rn(sum, wt[i]);
+    }
+    if (!isfinite(sum) || sum <= 0.0f) {
+      uniform = true;
+    } else {
+      const float invs = __fdiv_rn(1.0f, sum);
+      for (uint32_t i = 0; i < K; ++i) wt[i] = __fmul_rn(wt[i], invs);
+      const float sc = route_scale(p.scale);
+      if (sc != 1.0f)
+        for (uint32_t i = 0; i < K; ++i) wt[i] = __fmul_rn(wt[i], sc);
+    }
+  }
+  if (uniform) route_uniform(wt, K, p.scale);
+  for (uint32_t i = 0; i < K; ++i) {
+    p.ids[i] = idx[i];
+    p.weights[i] = wt[i];
+  }
+  // dispatch tables: shared experts, then the selected ones in slot order
+  if (p.seg_gu) {
+    for (uint32_t s = 0; s < p.n_shared; ++s) {
+      p.seg_gu[s] = p.sh_gu_base + s * p.gu_bytes;
+      p.seg_dn[s] = p.sh_dn_base + s * p.dn_bytes;
+    }
+    for (uint32_t i = 0; i < K; ++i) {
+      p.seg_gu[p.n_shared + i] = p.gu_base + idx[i] * p.gu_bytes;
+      p.seg_dn[p.n_shared + i] = p.dn_base + idx[i] * p.dn_bytes;
+    }
+  }
+}
+
+__global__ void moe_combine_kernel(const CombineParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= p.dim) return;
+  float o = 0.0f;
+  uint32_t s = 0;
+  if (p.n_shared) {
+    o = __ldcg(p.exp_out + i);
+    for (s = 1; s < p.n_shared; ++s) o = __fadd_rn(o, __ldcg(p.exp_out + static_cast<size_t>(s) * p.dim + i));
+  }
+  for (uint32_t k = 0; k < p.top_k; ++k) {
+    const float w = __ldcg(p.weights + k);
+    o = __fadd_rn(o, __fmul_rn(w, __ldcg(p.exp_out + static_cast<size_t>(p.n_shared + k) * p.dim + i)));
+  }
+  if (p.mlp_out) p.mlp_out[i] = o;
+  if (p.hidden) p.hidden[i] = __fadd_rn(p.hidden[i], o);
+}
+
+}  // namespace
+
+uint32_t route_experts_per_cta(uint32_t dim) {
+  uint32_t e = kRouteRowFloats / dim;
+  return e < 1 ? 1 : (e > kRouteThreads ? kRouteThreads : e);
+}
+
+size_t route_smem_bytes(uint32_t dim) {
+  return (static_cast<size_t>(dim) * (1 + route_experts_per_cta(dim))) * sizeof(float);
+}
+
+cudaError_t moe_setup() {
+  const size_t max_smem = route_smem_bytes(kMoeMaxDim);
+  return cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(max_smem));
+}
+
+cudaError_t launch_moe_route(const RouteParams &rp, const LaunchCfg &lc) {
+  if (rp.dim == 0 || rp.dim % 4 || rp.dim > kMoeMaxDim || rp.top_k == 0 ||
+      rp.top_k > rp.n_experts || rp.top_k > kMoeMaxTopK)
+    return cudaErrorInvalidValue;
+  RouteParams p = rp;
+  p.experts_per_cta = route_experts_per_cta(p.dim);
+  const uint32_t grid = (p.n_experts + p.experts_per_cta - 1) / p.experts_per_cta;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = make_launch_cfg(dim3(grid), dim3(kRouteThreads), route_smem_bytes(p.dim), lc, attr);
+  if (lc.launch_counter) ++*lc.launch_counter;
+  return cudaLaunchKernelEx(&cfg, moe_route_kernel, p);
+}
+
+cudaError_t launch_moe_combine(const CombineParams &p, const LaunchCfg &lc) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = make_launch_cfg(dim3((p.dim + 255) / 256), dim3(256), 0, lc, attr);
+  if (lc.launch_counter) ++*lc.launch_counter;
+  return cudaLaunchKernelEx(&cfg, moe_combine_kernel, p);
+}
+
+}  // namespace zgpu

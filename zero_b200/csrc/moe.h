@@ -1,0 +1,48 @@
+// moe.h — MoE router and combine kernels (moe.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "internal.h"
+
+namespace zgpu {
+
+constexpr uint32_t kMoeMaxTopK = 16;
+constexpr uint32_t kMoeMaxDim = 8192;
+
+struct RouteParams {
+  const float *x;            // hidden [dim]: routed as is, or rmsnorm(x) * norm_w
+  const float *norm_w;       // null: route x unchanged
+  float eps;
+  const float *w;            // router rows f32 [n_experts][dim]
+  const float *bias;         // [n_experts] or null
+  uint32_t dim, n_experts, top_k, mode;   // mode: 0 Softmax, 1 SigmoidNormalize
+  float scale;               // expert_weight_scale
+  float *scores;             // [n_experts]
+  uint32_t *ids;             // [top_k]
+  float *weights;            // [top_k]
+  uint32_t *counter;         // arrival counter, zero between launches
+  // dispatch tables of the grouped expert GEMVs (null: not written)
+  unsigned long long *seg_gu, *seg_dn;       // [n_shared + top_k]
+  unsigned long long gu_base, dn_base;       // routed experts' streams
+  unsigned long long sh_gu_base, sh_dn_base; // shared experts' streams
+  unsigned long long gu_bytes, dn_bytes;     // bytes per expert
+  uint32_t n_shared;
+  uint32_t experts_per_cta;  // set by the launcher
+  uint32_t *status;
+};
+
+struct CombineParams {
+  const float *exp_out;      // [n_shared + top_k][dim]
+  const float *weights;      // [top_k]
+  float *mlp_out;            // [dim] or null
+  float *hidden;             // residual (+= mlp_out) or null
+  uint32_t dim, n_shared, top_k;
+};
+
+cudaError_t moe_setup();
+cudaError_t launch_moe_route(const RouteParams &p, const LaunchCfg &lc);
+cudaError_t launch_moe_combine(const CombineParams &p, const LaunchCfg &lc);
+
+}  // namespace zgpu

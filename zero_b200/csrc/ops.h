@@ -66,6 +66,22 @@ struct AttnParams {
   uint32_t *gabort;                 // the launch's abort flag
 };
 
+// Launch configuration with programmatic dependent launch when lc.pdl is set
+// (attr must outlive the launch call).
+inline cudaLaunchConfig_t make_launch_cfg(dim3 grid, dim3 block, size_t smem, const LaunchCfg &lc,
+                                          cudaLaunchAttribute *attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = lc.stream;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = lc.pdl ? 1 : 0;
+  return cfg;
+}
+
 cudaError_t launch_attention(const AttnParams &ap, const LaunchCfg &lc);
 // Number of attention splits (CTAs per kv-head) a cache of max_tokens needs.
 uint32_t attention_max_splits(uint32_t max_tokens);
