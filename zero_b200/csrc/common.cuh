@@ -112,6 +112,15 @@ __device__ __forceinline__ void tma_bulk_g2s(uint32_t dst, const void *src, uint
       : "memory");
 }
 
+// 1-D bulk copy global -> this CTA's shared memory without a cache hint
+// (same alignment rules; no multicast).
+__device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
 // L2 policy for weights streamed exactly once per step: evict first, so the
 // KV cache and activations keep their L2 residency.
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {

@@ -78,11 +78,17 @@ __global__ void __launch_bounds__(kMlaPrepThreads) mla_prep_kernel(const MlaPara
   const uint32_t R = p.kv_lora, RD = p.rope, half = RD / 2;
   if (blockIdx.x < p.n_heads) {
     const uint32_t h = blockIdx.x;
-    // the weights do not depend on the previous kernel: stage them first
-    const uint4 *src = reinterpret_cast<const uint4 *>(
-        p.kb + static_cast<uint64_t>(h * p.kb_head_rows / 4) * p.kb_gstride);
-    uint4 *dst = reinterpret_cast<uint4 *>(slab);
-    for (uint32_t i = tid; i < p.slab_bytes / 16; i += kMlaPrepThreads) dst[i] = __ldg(src + i);
+    // the weights do not depend on the previous kernel: stage the head's
+    // k_nope rows (one contiguous run of group streams) with one bulk copy
+    __shared__ __align__(8) uint64_t sbar;
+    const uint32_t sb = smem_addr(&sbar);
+    if (tid == 0) {
+      mbar_init(sb, 1);
+      fence_barrier_init();
+      mbar_arrive_expect_tx(sb, p.slab_bytes);
+      bulk_copy_g2s(smem_addr(slab), p.kb + static_cast<uint64_t>(h * p.kb_head_rows / 4) * p.kb_gstride,
+                    p.slab_bytes, sb);
+    }
     pdl_wait();
     const uint32_t pos = mla_pos(p);
     const float *qh = p.q + static_cast<size_t>(h) * (p.nope + RD);
@@ -95,6 +101,7 @@ __global__ void __launch_bounds__(kMlaPrepThreads) mla_prep_kernel(const MlaPara
       p.q_pe[static_cast<size_t>(h) * RD + tid + half] = o1;
     }
     __syncthreads();
+    if (!mbar_wait(sb, 0, p.status)) return;   // timed out: the status word says so
     const uint32_t bpr = R / 32;
     for (uint32_t c = tid; c < R; c += kMlaPrepThreads) {
       const uint32_t b = c >> 5, e = c & 31;
@@ -160,16 +167,31 @@ __global__ void __launch_bounds__(kMlaPrepThreads) mla_prep_kernel(const MlaPara
 }
 
 __global__ void __launch_bounds__(32 * kMlaAttnWarpsMax) mla_attn_kernel(const MlaParams p) {
+  extern __shared__ __align__(128) float chunk[];   // [tokens of this split][kv_lora + rope]
+  __shared__ __align__(8) uint64_t bar;
   pdl_launch_dependents();
   pdl_wait();
   const uint32_t pos = mla_pos(p);
   if (pos >= p.max_tokens) return;   // reported by mla_prep
-  const uint32_t R = p.kv_lora, RD = p.rope, nr = R / 32;
+  const uint32_t R = p.kv_lora, RD = p.rope, nr = R / 32, row = R + RD;
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const uint32_t split = blockIdx.x;
   const uint32_t t0 = split * kMlaSplitTokens;
   if (t0 > pos) return;   // beyond the context: the merge reads only splits <= pos / 16
   const uint32_t t1 = min(t0 + kMlaSplitTokens, pos + 1);
+  const uint32_t nt = t1 - t0;
+  // the split's cache rows are contiguous: one bulk copy (row * 4 is a multiple of 16)
+  const uint32_t b = smem_addr(&bar);
+  if (threadIdx.x == 0) {
+    mbar_init(b, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(b, nt * row * 4);
+    bulk_copy_g2s(smem_addr(chunk), p.cache + static_cast<size_t>(t0) * row, nt * row * 4, b);
+  }
+  const bool ok = mbar_wait(b, 0, p.status);
   for (uint32_t h = warp; h < p.n_heads; h += nw) {
     float qa[16], acc[16], qp[2];
 #pragma unroll
@@ -181,15 +203,15 @@ __global__ void __launch_bounds__(32 * kMlaAttnWarpsMax) mla_attn_kernel(const M
     for (int j = 0; j < 2; ++j)
       qp[j] = (lane + 32 * j < RD) ? __ldcg(p.q_pe + static_cast<size_t>(h) * RD + lane + 32 * j) : 0.f;
     float m = -INFINITY, l = 0.f;
-    for (uint32_t t = t0; t < t1; ++t) {
-      const float *ct = p.cache + static_cast<size_t>(t) * (R + RD);
+    for (uint32_t t = 0; ok && t < nt; ++t) {
+      const float *ct = chunk + t * row;
       float cv[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) cv[j] = (j < static_cast<int>(nr)) ? __ldg(ct + lane + 32 * j) : 0.f;
+      for (int j = 0; j < 16; ++j) cv[j] = (j < static_cast<int>(nr)) ? ct[lane + 32 * j] : 0.f;
       float d = 0.f;
 #pragma unroll
       for (int j = 0; j < 2; ++j)
-        if (lane + 32 * j < RD) d = fmaf(qp[j], __ldg(ct + R + lane + 32 * j), d);
+        if (lane + 32 * j < RD) d = fmaf(qp[j], ct[R + lane + 32 * j], d);
 #pragma unroll
       for (int j = 0; j < 16; ++j) d = fmaf(qa[j], cv[j], d);
 #pragma unroll
@@ -203,6 +225,7 @@ __global__ void __launch_bounds__(32 * kMlaAttnWarpsMax) mla_attn_kernel(const M
       for (int j = 0; j < 16; ++j) acc[j] = fmaf(acc[j], corr, pe * cv[j]);
       m = mn;
     }
+    if (!ok) l = __uint_as_float(0x7fc00000u);   // a failed copy surfaces as NumericalInstability
     float *pp = p.part + (static_cast<size_t>(h) * p.max_splits + split) * (R + 2);
 #pragma unroll
     for (int j = 0; j < 16; ++j)
@@ -265,11 +288,13 @@ cudaError_t launch_mla_prep(const MlaParams &mp, const LaunchCfg &lc) {
 
 cudaError_t launch_mla_attention(const MlaParams &p, const LaunchCfg &lc) {
   if (p.kv_lora == 0 || p.kv_lora % 32 || p.kv_lora > kMlaMaxLatent || p.rope > kMlaMaxRope ||
+      (p.kv_lora + p.rope) % 4 ||
       p.max_splits < mla_max_splits(p.max_tokens) || p.n_heads == 0)
     return cudaErrorInvalidValue;
   const uint32_t warps = p.n_heads < kMlaAttnWarpsMax ? p.n_heads : kMlaAttnWarpsMax;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = make_launch_cfg(dim3(mla_max_splits(p.max_tokens)), dim3(32 * warps), 0, lc, attr);
+  const size_t chunk = static_cast<size_t>(kMlaSplitTokens) * (p.kv_lora + p.rope) * sizeof(float);
+  cudaLaunchConfig_t cfg = make_launch_cfg(dim3(mla_max_splits(p.max_tokens)), dim3(32 * warps), chunk, lc, attr);
   if (lc.launch_counter) ++*lc.launch_counter;
   cudaError_t e = cudaLaunchKernelEx(&cfg, mla_attn_kernel, p);
   if (e != cudaSuccess) return e;

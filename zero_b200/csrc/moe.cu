@@ -32,6 +32,7 @@ namespace {
 
 constexpr int kRouteThreads = 256;
 constexpr uint32_t kRouteRowFloats = 16384;   // staged router floats per CTA
+constexpr uint32_t kRouteRowPad = 4;          // floats of padding per staged row
 
 __device__ __forceinline__ float route_scale(float s) {
   return (isfinite(s) && s > 0.0f) ? s : 1.0f;
@@ -53,13 +54,23 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const RoutePar
   const uint32_t e1 = min(e0 + p.experts_per_cta, p.n_experts);
   const uint32_t ne = e1 > e0 ? e1 - e0 : 0;
   float *xs = rsm;                       // [dim]
-  float *ws = rsm + p.dim;               // [ne][dim]
-  // the router rows do not depend on the previous kernel: stage them first
-  {
-    const float4 *src = reinterpret_cast<const float4 *>(p.w + static_cast<size_t>(e0) * p.dim);
-    float4 *dst = reinterpret_cast<float4 *>(ws);
-    const uint32_t n4 = ne * p.dim / 4;
-    for (uint32_t i = tid; i < n4; i += kRouteThreads) dst[i] = __ldg(src + i);
+  float *ws = rsm + p.dim;               // [ne][dim + 4]: rows padded so that the ne
+                                         // chain threads read distinct banks
+  const uint32_t wstride = p.dim + kRouteRowPad;
+  // the router rows do not depend on the previous kernel: stage them first,
+  // one bulk copy per row into the padded layout
+  __shared__ __align__(8) uint64_t rbar;
+  const uint32_t rb = smem_addr(&rbar);
+  if (tid == 0) {
+    mbar_init(rb, 1);
+    fence_barrier_init();
+    if (ne) {
+      mbar_arrive_expect_tx(rb, ne * p.dim * 4);
+      for (uint32_t e = 0; e < ne; ++e)
+        bulk_copy_g2s(smem_addr(ws + e * wstride), p.w + static_cast<size_t>(e0 + e) * p.dim, p.dim * 4, rb);
+    } else {
+      mbar_arrive(rb);
+    }
   }
   pdl_wait();
   // the routed vector: x itself, or rmsnorm(x) * gain (the model's post-
@@ -86,12 +97,27 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const RoutePar
     xs[i] = p.norm_w ? __fmul_rn(__fmul_rn(v, inv), p.norm_w[i]) : v;
   }
   __syncthreads();
+  // every thread has passed the barrier init above; a failed (timed-out)
+  // copy leaves the scores undefined and sets the status word
+  const bool rows_ok = mbar_wait(rb, 0, p.status);
   // moe.rs:168-186: dot += hidden[i] * row[i], i ascending, unfused
-  if (tid < ne) {
-    const float *row = ws + static_cast<size_t>(tid) * p.dim;
+  if (tid < ne && rows_ok) {
+    const float *row = ws + tid * wstride;
     float dot = 0.0f;
-#pragma unroll 8
-    for (uint32_t i = 0; i < p.dim; ++i) dot = __fadd_rn(dot, __fmul_rn(xs[i], row[i]));
+    // dim % 4 == 0; the products do not depend on the chain, so loads and
+    // multiplies of later steps issue while the adds retire one by one
+    for (uint32_t i = 0; i < p.dim; i += 4) {
+      const float4 xv = *reinterpret_cast<const float4 *>(xs + i);
+      const float4 wv = *reinterpret_cast<const float4 *>(row + i);
+      const float p0 = __fmul_rn(xv.x, wv.x);
+      const float p1 = __fmul_rn(xv.y, wv.y);
+      const float p2 = __fmul_rn(xv.z, wv.z);
+      const float p3 = __fmul_rn(xv.w, wv.w);
+      dot = __fadd_rn(dot, p0);
+      dot = __fadd_rn(dot, p1);
+      dot = __fadd_rn(dot, p2);
+      dot = __fadd_rn(dot, p3);
+    }
     const uint32_t e = e0 + tid;
     float s;
     if (p.mode == 0) {
@@ -204,7 +230,8 @@ uint32_t route_experts_per_cta(uint32_t dim) {
 }
 
 size_t route_smem_bytes(uint32_t dim) {
-  return (static_cast<size_t>(dim) * (1 + route_experts_per_cta(dim))) * sizeof(float);
+  const size_t e = route_experts_per_cta(dim);
+  return (dim + e * (dim + kRouteRowPad)) * sizeof(float);
 }
 
 cudaError_t moe_setup() {
