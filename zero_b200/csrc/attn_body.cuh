@@ -45,15 +45,17 @@ constexpr int kAttnMaxGqa = 4;
 constexpr int kAttnSplitTokens = 256;
 constexpr int kAttnUnrollMax = 8;        // tokens per warp per round (K and V rows in flight)
 
-struct AttnSmem {
+template <int NW>
+struct AttnSmemT {
   float cs[kAttnHd / 2], sn[kAttnHd / 2];
   __align__(16) float qs[kAttnMaxGqa][kAttnHd];
   __align__(16) float kn[kAttnHd];
   __align__(16) float vn[kAttnHd];
-  __align__(16) float opart[kAttnWarps][kAttnMaxGqa][kAttnHd];
-  float wm[kAttnWarps][kAttnMaxGqa], wl[kAttnWarps][kAttnMaxGqa];   // per-warp running max / sum
+  __align__(16) float opart[NW][kAttnMaxGqa][kAttnHd];
+  float wm[NW][kAttnMaxGqa], wl[NW][kAttnMaxGqa];   // per-warp running max / sum
   uint32_t s_last;
 };
+using AttnSmem = AttnSmemT<kAttnWarps>;
 
 // QK-norm (rmsnorm over one head, ops.rs:29) then RoPE (trig.rs:192) for the
 // four dims 4l..4l+3 a lane holds; every lane of the warp participates.
@@ -111,9 +113,10 @@ __device__ __forceinline__ void attn_store_out(const AttnParams &p, uint32_t i, 
   else p.out[i] = v;
 }
 
-template <class Bar, bool TAGGED = false, int kAttnUnroll = kAttnUnrollMax>
+template <class Bar, bool TAGGED = false, int kAttnUnroll = kAttnUnrollMax, int NW = kAttnWarps>
 __device__ __forceinline__ void attn_decode_block(const AttnParams &p, uint32_t kvh, uint32_t split,
-                                                  uint32_t pos, uint32_t tid, AttnSmem &sm, Bar bar) {
+                                                  uint32_t pos, uint32_t tid, AttnSmemT<NW> &sm, Bar bar) {
+  constexpr uint32_t kThreads = 32 * NW;
   const uint32_t warp = tid >> 5, lane = tid & 31;
   const uint32_t G = p.n_q / p.n_kv;
   if (pos >= p.max_tokens) {
@@ -126,6 +129,29 @@ __device__ __forceinline__ void attn_decode_block(const AttnParams &p, uint32_t 
   if (split >= nact) return;
   const uint32_t t1 = min(t0 + kAttnSplitTokens, total);
   const uint32_t qd = p.n_q * kAttnHd, kvd = p.n_kv * kAttnHd;
+  float *kc = p.kv_layer, *vc = p.kv_layer + p.kv_block;
+
+  // The cached rows of tokens before `pos` do not depend on this step: the
+  // warp's first run of K and V rows is loaded before the projections are
+  // waited for, so that round trip overlaps the wait.  The current token's
+  // row is patched in from shared memory once it exists.
+  float4 kk[kAttnUnroll], vv[kAttnUnroll];
+  auto load_run = [&](uint32_t tb) {
+#pragma unroll
+    for (int u = 0; u < kAttnUnroll; ++u) {
+      const uint32_t t = tb + u;
+      kk[u] = vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (t < t1 && t != pos &&
+          ZDEV_CHECK(static_cast<uint64_t>(t + 1) * kvd <= p.kv_block && t - t0 < kAttnSplitTokens, p.status,
+                     10, t, kvh)) {
+        const size_t row = static_cast<size_t>(t) * kvd + kvh * kAttnHd;
+        kk[u] = __ldcg(reinterpret_cast<const float4 *>(kc + row) + lane);
+        vv[u] = __ldcg(reinterpret_cast<const float4 *>(vc + row) + lane);
+      }
+    }
+  };
+  uint32_t tb = t0 + warp * kAttnUnroll;
+  load_run(tb);
 
   // RoPE LUT for this position (rope_sincos_lut_avx512, trig.rs:148).
   if (tid < kAttnHd / 2) {
@@ -148,7 +174,6 @@ __device__ __forceinline__ void attn_decode_block(const AttnParams &p, uint32_t 
   }
   bar();
 
-  float *kc = p.kv_layer, *vc = p.kv_layer + p.kv_block;
   if (t1 == total && tid < kAttnHd) {
     // KvCache::store_kv at `pos` (kv_cache.rs:175-181).
     kc[static_cast<size_t>(pos) * kvd + kvh * kAttnHd + tid] = sm.kn[tid];
@@ -167,21 +192,13 @@ __device__ __forceinline__ void attn_decode_block(const AttnParams &p, uint32_t 
     m[j] = -INFINITY;
     l[j] = 0.f;
   }
-  for (uint32_t tb = t0 + warp * kAttnUnroll; tb < t1; tb += kAttnWarps * kAttnUnroll) {
-    float4 kk[kAttnUnroll], vv[kAttnUnroll];
+  for (; tb < t1; tb += NW * kAttnUnroll) {
+    if (tb + kAttnUnroll > pos && tb <= pos) {   // the run holds the current token
 #pragma unroll
-    for (int u = 0; u < kAttnUnroll; ++u) {
-      const uint32_t t = tb + u;
-      kk[u] = vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (t < t1 && ZDEV_CHECK(static_cast<uint64_t>(t + 1) * kvd <= p.kv_block && t - t0 < kAttnSplitTokens,
-                               p.status, 10, t, kvh)) {
-        if (t == pos) {
+      for (int u = 0; u < kAttnUnroll; ++u) {
+        if (tb + u == pos) {
           kk[u] = *reinterpret_cast<const float4 *>(&sm.kn[4 * lane]);
           vv[u] = *reinterpret_cast<const float4 *>(&sm.vn[4 * lane]);
-        } else {
-          const size_t row = static_cast<size_t>(t) * kvd + kvh * kAttnHd;
-          kk[u] = __ldcg(reinterpret_cast<const float4 *>(kc + row) + lane);
-          vv[u] = __ldcg(reinterpret_cast<const float4 *>(vc + row) + lane);
         }
       }
     }
@@ -215,6 +232,7 @@ __device__ __forceinline__ void attn_decode_block(const AttnParams &p, uint32_t 
       l[j] = lj;
       o[j] = oj;
     }
+    if (tb + NW * kAttnUnroll < t1) load_run(tb + NW * kAttnUnroll);
   }
 #pragma unroll
   for (int j = 0; j < kAttnMaxGqa; ++j) {
@@ -230,14 +248,14 @@ __device__ __forceinline__ void attn_decode_block(const AttnParams &p, uint32_t 
   // Merge the warps' states in warp order; thread (j, d) finalises head j,
   // dim d.  Warps without tokens carry m = -inf, l = 0, o = 0.
   const bool single = (nact == 1);
-  for (uint32_t idx = tid; idx < G * kAttnHd; idx += kAttnThreads) {
+  for (uint32_t idx = tid; idx < G * kAttnHd; idx += kThreads) {
     const uint32_t j = idx / kAttnHd, d = idx % kAttnHd;
     float mm = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) mm = fmaxf(mm, sm.wm[w][j]);
+    for (int w = 0; w < NW; ++w) mm = fmaxf(mm, sm.wm[w][j]);
     float ll = 0.f, acc = 0.f;
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) {
+    for (int w = 0; w < NW; ++w) {
       const float f = (sm.wm[w][j] == -INFINITY) ? 0.f : expf(sm.wm[w][j] - mm);
       ll = __fmaf_rn(f, sm.wl[w][j], ll);
       acc = __fmaf_rn(f, sm.opart[w][j][d], acc);
@@ -269,7 +287,7 @@ __device__ __forceinline__ void attn_decode_block(const AttnParams &p, uint32_t 
   bar();
   if (!sm.s_last) return;
   __threadfence();
-  for (uint32_t idx = tid; idx < G * kAttnHd; idx += kAttnThreads) {
+  for (uint32_t idx = tid; idx < G * kAttnHd; idx += kThreads) {
     const uint32_t j = idx / kAttnHd, d = idx % kAttnHd;
     const uint32_t qh = kvh * G + j;
     const float *base = p.part + static_cast<size_t>(qh) * p.max_splits * (kAttnHd + 2);

@@ -30,8 +30,10 @@
 //     over the CTAs; within a CTA the warps take (unit, K-chunk) items and
 //     the chunk partials are added in chunk order, so results do not depend
 //     on timing.  The arithmetic is the standalone GEMV's (gemv_body.cuh).
-//   * The attention stage runs on n_kv * splits CTAs, 8 warps each
-//     (attn_body.cuh); the other warps and CTAs pass to the barrier.
+//   * The attention stage runs on n_kv * splits CTAs with all their consumer
+//     warps (attn_body.cuh); the other CTAs pass to the next stage.
+//   * A stage's input is polled with two loads in flight per word, half an
+//     L2 round trip apart, so that it is seen soon after it lands.
 // Any bounded wait that gives up sets ZDEV_ERR_TIMEOUT and the launch's abort
 // flag; from then on every wait of every CTA fails at once, producers stop
 // issuing and drain their copies in flight, and the launch runs out.
@@ -53,6 +55,7 @@ constexpr uint32_t kSlotBytes = 4608;          // 2 Q4_0 or 1 Q8_0 group-chunk o
 constexpr uint32_t kBarConsumers = 1;          // named barrier ids (0 = __syncthreads)
 constexpr uint32_t kBarAttn = 2;
 constexpr size_t kStepSmemMax = 227 * 1024;
+constexpr long long kPollStaggerClk = 600;     // ~half an L2 round trip at 1.9 GHz
 
 #ifdef ZGPU_STEP_TRACE
 // Stage timeline of CTA 0 (profiling builds only): entry k holds
@@ -125,8 +128,10 @@ __device__ bool wait_phase(uint32_t bar, uint32_t parity, uint32_t *status, vola
   }
 }
 
+// The attention CTAs run the attention on all their consumer warps.
+using StepAttnSmem = AttnSmemT<kNW>;
 struct AttnBar {
-  __device__ __forceinline__ void operator()() const { named_bar_sync(kBarAttn, kAttnThreads); }
+  __device__ __forceinline__ void operator()() const { named_bar_sync(kBarAttn, kNC); }
 };
 
 // Whether step `gstep` of this launch runs the forward pass / the LM head.
@@ -267,7 +272,10 @@ __device__ __forceinline__ void ver_bump(Ctx &c, uint32_t b) {
   }
 }
 
-template <int QT, int PRO, int EPI, bool EMB>
+// XR: float4s of the input per consumer thread (2 covers a 2048-wide input,
+// 4 the 6144-wide one); inputs of at most 2 per thread are polled with two
+// loads in flight per word.
+template <int QT, int PRO, int EPI, bool EMB, int XR>
 __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc &sd, Ctx &c, uint32_t token) {
   constexpr int GPU = (QT == ZGPU_Q4_0) ? 2 : 1;
   constexpr int R = 4 * GPU;
@@ -279,7 +287,7 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
   // ---- input: each thread takes its float4s of x once (at most kXRegs of
   // them), waiting for the expected version, for both the sum of squares
   // and the digits.
-  constexpr int kXRegs = 4;
+  constexpr int kXRegs = XR;
   float4 xr[kXRegs];
   const unsigned long long *xin = sd.tin;
   const uint32_t vin = EMB ? 0u : ver_of(c, sd.in_buf);
@@ -300,16 +308,23 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
         raw[i][0] = raw[i][1] = make_ulonglong2(0ull, 0ull);
       }
     }
-    auto ready = [&](int i) {
-      return static_cast<uint32_t>(raw[i][0].x >> 32) == vin && static_cast<uint32_t>(raw[i][0].y >> 32) == vin &&
-             static_cast<uint32_t>(raw[i][1].x >> 32) == vin && static_cast<uint32_t>(raw[i][1].y >> 32) == vin;
+    auto ready = [&](const ulonglong2 (&r)[2]) {
+      return static_cast<uint32_t>(r[0].x >> 32) == vin && static_cast<uint32_t>(r[0].y >> 32) == vin &&
+             static_cast<uint32_t>(r[1].x >> 32) == vin && static_cast<uint32_t>(r[1].y >> 32) == vin;
     };
 #pragma unroll
     for (int i = 0; i < kXRegs; ++i)
-      if ((todo >> i & 1u) && ready(i)) todo &= ~(1u << i);
+      if ((todo >> i & 1u) && ready(raw[i])) todo &= ~(1u << i);
     if (todo) {
-      const uint64_t t0 = globaltimer_ns();
-      while (todo) {
+      // Two polls stay in flight, half an L2 round trip apart: the image is
+      // complete about half a round trip after the last word lands instead
+      // of up to a whole one.  Poll B starts kPollStaggerClk after poll A;
+      // from then on each poll is reissued as soon as its result is checked.
+      // The second set covers the first kXAlt float4s of each thread (all of
+      // a 2048-wide input); further words are polled once per round.
+      constexpr int kXAlt = 0;
+      ulonglong2 alt[kXAlt > 0 ? kXAlt : 1][2];
+      auto issue_raw = [&]() {
 #pragma unroll
         for (int i = 0; i < kXRegs; ++i) {
           if (todo >> i & 1u) {
@@ -318,13 +333,55 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
             raw[i][1] = __ldcg(q + 1);
           }
         }
+      };
+      auto issue_alt = [&]() {
+#pragma unroll
+        for (int i = 0; i < kXAlt; ++i) {
+          if (todo >> i & 1u) {
+            const ulonglong2 *q = reinterpret_cast<const ulonglong2 *>(xin + 4 * (warp * 32 + lane + i * kNC));
+            alt[i][0] = __ldcg(q);
+            alt[i][1] = __ldcg(q + 1);
+          }
+        }
+      };
+      auto absorb_raw = [&]() {
 #pragma unroll
         for (int i = 0; i < kXRegs; ++i)
-          if ((todo >> i & 1u) && ready(i)) todo &= ~(1u << i);
-        if (!todo) break;
+          if ((todo >> i & 1u) && ready(raw[i])) todo &= ~(1u << i);
+      };
+      auto absorb_alt = [&]() {
+#pragma unroll
+        for (int i = 0; i < kXAlt; ++i) {
+          if ((todo >> i & 1u) && ready(alt[i])) {
+            raw[i][0] = alt[i][0];
+            raw[i][1] = alt[i][1];
+            todo &= ~(1u << i);
+          }
+        }
+      };
+      auto give_up = [&]() -> bool {
         if (*c.abort || ld_relaxed_u32(&P.bar[1])) {
           *c.abort = 1;
-          break;
+          return true;
+        }
+        return false;
+      };
+      const uint64_t t0 = globaltimer_ns();
+      issue_raw();
+      if (kXAlt > 0) {
+        const long long c0 = clock64();
+        while (clock64() - c0 < kPollStaggerClk) {
+        }
+        issue_alt();
+      }
+      while (true) {
+        absorb_raw();
+        if (!todo || give_up()) break;
+        issue_raw();
+        if (kXAlt > 0) {
+          absorb_alt();
+          if (!todo || give_up()) break;
+          issue_alt();
         }
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
           atomicOr(P.status, ZDEV_ERR_TIMEOUT);
@@ -496,21 +553,23 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
 
 __device__ __forceinline__ void run_gemv(const StepParams &P, const StageDesc &sd, Ctx &c, uint32_t token) {
   const bool emb = (sd.flags & kStageEmbed) != 0;
+  const bool wide = sd.in_dim > 2u * 4u * kNC;
   if (sd.quant == ZGPU_Q4_0) {
     if (sd.pro == PRO_RMSNORM) {
       if (sd.epi == EPI_STORE) {
-        if (emb) gemv_stage<ZGPU_Q4_0, PRO_RMSNORM, EPI_STORE, true>(P, sd, c, token);
-        else gemv_stage<ZGPU_Q4_0, PRO_RMSNORM, EPI_STORE, false>(P, sd, c, token);
+        if (emb) gemv_stage<ZGPU_Q4_0, PRO_RMSNORM, EPI_STORE, true, 2>(P, sd, c, token);
+        else gemv_stage<ZGPU_Q4_0, PRO_RMSNORM, EPI_STORE, false, 2>(P, sd, c, token);
       } else if (sd.epi == EPI_SWIGLU) {
-        gemv_stage<ZGPU_Q4_0, PRO_RMSNORM, EPI_SWIGLU, false>(P, sd, c, token);
+        gemv_stage<ZGPU_Q4_0, PRO_RMSNORM, EPI_SWIGLU, false, 2>(P, sd, c, token);
       } else if (sd.epi == EPI_ARGMAX) {
-        gemv_stage<ZGPU_Q4_0, PRO_RMSNORM, EPI_ARGMAX, false>(P, sd, c, token);
+        gemv_stage<ZGPU_Q4_0, PRO_RMSNORM, EPI_ARGMAX, false, 2>(P, sd, c, token);
       }
     } else if (sd.epi == EPI_RESADD) {
-      gemv_stage<ZGPU_Q4_0, PRO_PLAIN, EPI_RESADD, false>(P, sd, c, token);
+      if (wide) gemv_stage<ZGPU_Q4_0, PRO_PLAIN, EPI_RESADD, false, 4>(P, sd, c, token);
+      else gemv_stage<ZGPU_Q4_0, PRO_PLAIN, EPI_RESADD, false, 2>(P, sd, c, token);
     }
   } else if (sd.pro == PRO_RMSNORM && sd.epi == EPI_ARGMAX) {
-    gemv_stage<ZGPU_Q8_0, PRO_RMSNORM, EPI_ARGMAX, false>(P, sd, c, token);
+    gemv_stage<ZGPU_Q8_0, PRO_RMSNORM, EPI_ARGMAX, false, 2>(P, sd, c, token);
   }
 }
 
@@ -607,7 +666,7 @@ __device__ __forceinline__ void consumer(const StepParams &P, Ctx &c) {
         if (sd.kind == STG_GEMV) {
           run_gemv(P, sd, c, token);
         } else {
-          if (blockIdx.x < P.n_kv * P.max_splits && tid < kAttnThreads) {
+          if (blockIdx.x < P.n_kv * P.max_splits) {
             AttnParams ap = {};
             ap.q_norm = sd.q_norm;
             ap.k_norm = sd.k_norm;
@@ -631,8 +690,8 @@ __device__ __forceinline__ void consumer(const StepParams &P, Ctx &c) {
             ap.ver_out = c.v_attn + 1;
             ap.abort = c.abort;
             ap.gabort = &P.bar[1];
-            attn_decode_block<AttnBar, true, 4>(ap, blockIdx.x % P.n_kv, blockIdx.x / P.n_kv, pos, tid,
-                                             *reinterpret_cast<AttnSmem *>(c.xsm), AttnBar());
+            attn_decode_block<AttnBar, true, 4, kNW>(ap, blockIdx.x % P.n_kv, blockIdx.x / P.n_kv, pos, tid,
+                                                     *reinterpret_cast<StepAttnSmem *>(c.xsm), AttnBar());
           }
           ++c.v_attn;
           // the x image area doubles as the attention's shared memory
@@ -739,14 +798,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepParams 
 }  // namespace
 
 bool step_geometry(const StageDesc *stages, uint32_t n, uint32_t grid, StepParams *p) {
-  size_t xbytes = sizeof(AttnSmem);
+  size_t xbytes = sizeof(StepAttnSmem);
   size_t part = 0;
   uint32_t hunits = 0;
   for (uint32_t i = 0; i < n; ++i) {
     const StageDesc &s = stages[i];
     if (s.kind != STG_GEMV) continue;
     if (s.in_dim % 32 != 0 || s.bpr * 32 != s.in_dim) return false;
-    if (s.in_dim > 4u * 4u * kNC) return false;   // kXRegs float4s per consumer thread
+    if (s.in_dim > 4u * 4u * kNC) return false;   // at most 4 float4s per consumer thread
+    // only the residual-adding (plain prologue) stages have a 4-float4 variant
+    if (s.in_dim > 2u * 4u * kNC && !(s.quant == ZGPU_Q4_0 && s.pro == PRO_PLAIN && s.epi == EPI_RESADD))
+      return false;
     const size_t img = static_cast<size_t>(s.bpr) * 128;
     if (img > xbytes) xbytes = img;
     const size_t upc = (static_cast<size_t>(s.units) + grid - 1) / grid;
