@@ -53,6 +53,8 @@ struct AttnSmemT {
   __align__(16) float vn[kAttnHd];
   __align__(16) float opart[NW][kAttnMaxGqa][kAttnHd];
   float wm[NW][kAttnMaxGqa], wl[NW][kAttnMaxGqa];   // per-warp running max / sum
+  float wf[NW][kAttnMaxGqa];                         // merge weights exp(m_w - max)
+  float wL[kAttnMaxGqa];                             // merged sums
   uint32_t s_last;
 };
 using AttnSmem = AttnSmemT<kAttnWarps>;
@@ -113,9 +115,16 @@ __device__ __forceinline__ void attn_store_out(const AttnParams &p, uint32_t i, 
   else p.out[i] = v;
 }
 
-template <class Bar, bool TAGGED = false, int kAttnUnroll = kAttnUnrollMax, int NW = kAttnWarps>
+// Mark: optional timeline hook (event id) for profiling builds of the caller.
+struct AttnNoMark {
+  __device__ __forceinline__ void operator()(uint32_t) const {}
+};
+
+template <class Bar, bool TAGGED = false, int kAttnUnroll = kAttnUnrollMax, int NW = kAttnWarps,
+          class Mark = AttnNoMark>
 __device__ __forceinline__ void attn_decode_block(const AttnParams &p, uint32_t kvh, uint32_t split,
-                                                  uint32_t pos, uint32_t tid, AttnSmemT<NW> &sm, Bar bar) {
+                                                  uint32_t pos, uint32_t tid, AttnSmemT<NW> &sm, Bar bar,
+                                                  Mark mark = Mark()) {
   constexpr uint32_t kThreads = 32 * NW;
   const uint32_t warp = tid >> 5, lane = tid & 31;
   const uint32_t G = p.n_q / p.n_kv;
@@ -173,6 +182,7 @@ __device__ __forceinline__ void attn_decode_block(const AttnParams &p, uint32_t 
     *reinterpret_cast<float4 *>(&sm.vn[4 * lane]) = attn_load_proj<TAGGED>(p, qd + kvd + kvh * kAttnHd + 4 * lane);
   }
   bar();
+  mark(1);
 
   if (t1 == total && tid < kAttnHd) {
     // KvCache::store_kv at `pos` (kv_cache.rs:175-181).
@@ -234,6 +244,7 @@ __device__ __forceinline__ void attn_decode_block(const AttnParams &p, uint32_t 
     }
     if (tb + NW * kAttnUnroll < t1) load_run(tb + NW * kAttnUnroll);
   }
+  mark(2);
 #pragma unroll
   for (int j = 0; j < kAttnMaxGqa; ++j) {
     if (j >= static_cast<int>(G)) break;
@@ -246,20 +257,33 @@ __device__ __forceinline__ void attn_decode_block(const AttnParams &p, uint32_t 
   bar();
 
   // Merge the warps' states in warp order; thread (j, d) finalises head j,
-  // dim d.  Warps without tokens carry m = -inf, l = 0, o = 0.
+  // dim d.  Warps without tokens carry m = -inf, l = 0, o = 0.  The merge
+  // weights exp(m_w - max) and the merged sum depend only on the head: one
+  // thread per (warp, head) computes each weight, one per head the sum.
   const bool single = (nact == 1);
-  for (uint32_t idx = tid; idx < G * kAttnHd; idx += kThreads) {
-    const uint32_t j = idx / kAttnHd, d = idx % kAttnHd;
+  if (tid < NW * G) {
+    const uint32_t w = tid / G, j = tid % G;
     float mm = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) mm = fmaxf(mm, sm.wm[w][j]);
-    float ll = 0.f, acc = 0.f;
+    for (int v = 0; v < NW; ++v) mm = fmaxf(mm, sm.wm[v][j]);
+    sm.wf[w][j] = (sm.wm[w][j] == -INFINITY) ? 0.f : expf(sm.wm[w][j] - mm);
+    if (w == 0) sm.wL[j] = mm;   // the max, read back below
+  }
+  bar();
+  if (tid < G) {
+    float ll = 0.f;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) {
-      const float f = (sm.wm[w][j] == -INFINITY) ? 0.f : expf(sm.wm[w][j] - mm);
-      ll = __fmaf_rn(f, sm.wl[w][j], ll);
-      acc = __fmaf_rn(f, sm.opart[w][j][d], acc);
-    }
+    for (int w = 0; w < NW; ++w) ll = __fmaf_rn(sm.wf[w][tid], sm.wl[w][tid], ll);
+    sm.wm[0][tid] = sm.wL[tid];   // keep the max for the split partials
+    sm.wL[tid] = ll;
+  }
+  bar();
+  for (uint32_t idx = tid; idx < G * kAttnHd; idx += kThreads) {
+    const uint32_t j = idx / kAttnHd, d = idx % kAttnHd;
+    const float mm = sm.wm[0][j], ll = sm.wL[j];
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) acc = __fmaf_rn(sm.wf[w][j], sm.opart[w][j][d], acc);
     const uint32_t qh = kvh * G + j;
     if (single) {
       if (d == 0 && (!(mm > -INFINITY && mm < INFINITY) || !(ll > 0.f) || !(ll < INFINITY)))
@@ -275,6 +299,7 @@ __device__ __forceinline__ void attn_decode_block(const AttnParams &p, uint32_t 
       }
     }
   }
+  mark(3);
   if (single) return;
 
   // Publish the partials, then let the last split of this kv head merge them.

@@ -224,7 +224,6 @@ __device__ __forceinline__ bool tag_wait4(const unsigned long long *p, uint32_t 
   if (!ready()) {
     const uint64_t t0 = globaltimer_ns();
     while (true) {
-      __nanosleep(64);
       a = __ldcg(q);
       b = __ldcg(q + 1);
       if (ready()) break;

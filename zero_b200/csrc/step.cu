@@ -56,6 +56,7 @@ constexpr uint32_t kBarConsumers = 1;          // named barrier ids (0 = __synct
 constexpr uint32_t kBarAttn = 2;
 constexpr size_t kStepSmemMax = 227 * 1024;
 constexpr long long kPollStaggerClk = 600;     // ~half an L2 round trip at 1.9 GHz
+constexpr uint32_t kMaxUnitsPerCta = 256;      // per-unit arrival counters in shared memory
 
 #ifdef ZGPU_STEP_TRACE
 // Stage timeline of CTA 0 (profiling builds only): entry k holds
@@ -132,6 +133,9 @@ __device__ bool wait_phase(uint32_t bar, uint32_t parity, uint32_t *status, vola
 using StepAttnSmem = AttnSmemT<kNW>;
 struct AttnBar {
   __device__ __forceinline__ void operator()() const { named_bar_sync(kBarAttn, kNC); }
+};
+struct AttnMark {   // attention timeline events 121..123 (profiling builds)
+  __device__ __forceinline__ void operator()(uint32_t e) const { trace(120 + e); }
 };
 
 // Whether step `gstep` of this launch runs the forward pass / the LM head.
@@ -244,7 +248,7 @@ struct Ctx {
   uint8_t *ring;
   uint64_t *full, *empty;
   float *red;
-  unsigned long long *best_w;
+  uint32_t *cnt;     // per-unit K-chunk arrival counters of the current stage
   uint32_t *s_token;
   volatile uint32_t *abort;
   uint32_t j;        // items this warp has consumed (matches its producer lane)
@@ -402,18 +406,7 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
   for (int i = 0; i < kXRegs; ++i) {
     const uint32_t f = warp * 32 + lane + i * kNC;
     if (EMB) xr[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (f < nf4) {
-      if (EMB) {
-        xr[i] = embed_f4(P, token, f);
-        // the embedding is the residual base of the rows this CTA owns
-        const float ev[4] = {xr[i].x, xr[i].y, xr[i].z, xr[i].w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint32_t e = 4 * f + k;
-          if (e >= c.hrow0 && e - c.hrow0 < P.hown_rows) c.hown[e - c.hrow0] = ev[k];
-        }
-      }
-    }
+    if (f < nf4 && EMB) xr[i] = embed_f4(P, token, f);
   }
   trace(16 + 2 + EPI);
   // RMSNorm (ops.rs:29-52) as y = inv * (W . (x * g)): the digits are taken
@@ -421,8 +414,8 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
   // the row sums in the epilogue, so the sum of squares (fixed order: per
   // thread over its float4s, xor-tree in the warp, warps in order) needs no
   // barrier of its own: its per-warp parts cross the image barrier below.
+  float ss = 0.f;
   if (PRO == PRO_RMSNORM) {
-    float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < kXRegs; ++i) {
       const float4 t = xr[i];
@@ -431,7 +424,26 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-    if (lane == 0) c.red[warp] = ss;
+  }
+  // Every warp of this CTA is done with the previous stage (its items read
+  // the image, the partials, the residual rows and the RMS parts) before any
+  // of them is overwritten; the wait for the input above overlaps the
+  // stragglers.
+  named_bar_sync(kBarConsumers, kNC);
+  if (PRO == PRO_RMSNORM && lane == 0) c.red[warp] = ss;
+  if (EMB) {
+    // the embedding is the residual base of the rows this CTA owns
+#pragma unroll
+    for (int i = 0; i < kXRegs; ++i) {
+      const uint32_t f = warp * 32 + lane + i * kNC;
+      if (f >= nf4) continue;
+      const float ev[4] = {xr[i].x, xr[i].y, xr[i].z, xr[i].w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t e = 4 * f + k;
+        if (e >= c.hrow0 && e - c.hrow0 < P.hown_rows) c.hown[e - c.hrow0] = ev[k];
+      }
+    }
   }
 #pragma unroll
   for (int i = 0; i < kXRegs; ++i) {
@@ -460,17 +472,24 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
     inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(sd.in_dim)), P.eps)));
   }
 
-  // ---- items: warp (k + rot) % kNW takes item k of this CTA's list
+  // ---- items: warp (k + rot) % kNW takes item k of this CTA's list.  The
+  // warp that completes a unit's last K-chunk (per-unit arrival counter in
+  // shared memory) adds the chunk partials in chunk order and publishes the
+  // unit's rows at once, so a row never waits for the CTA's slowest warp and
+  // the stage needs no barrier after its items.
   const uint32_t nloc = u1 - u0, nitems = nloc * sd.ks;
   const uint32_t first = (warp + kNW - c.rot) % kNW;
   c.rot = (c.rot + nitems) % kNW;
+  unsigned long long *xout = sd.tout;
+  const uint32_t vout = (EPI == EPI_ARGMAX) ? 0u : ver_of(c, sd.out_buf) + 1;
+  unsigned long long best = kArgmaxInitKey;
   bool failed = false;
   for (uint32_t k = first; k < nitems; k += kNW) {
     const uint32_t slot = warp * kSlots + (c.j % kSlots);
     trace(64);
     if (!failed && !wait_phase(smem_addr(&c.full[slot]), (c.j / kSlots) & 1, P.status, c.abort)) failed = true;
     trace(80);
-    const uint32_t chunk = k % sd.ks;
+    const uint32_t ul = k / sd.ks, chunk = k - ul * sd.ks;
     const uint32_t b = chunk * kChunkBlocks + lane;
     float acc[R];
 #pragma unroll
@@ -484,36 +503,34 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
     ++c.j;
     const float v = reduce_scatter<R>(acc, lane);
     if ((lane & (32 / R - 1)) == 0) c.part[k * R + lane / (32 / R)] = v;
-  }
-  named_bar_sync(kBarConsumers, kNC);
-  trace(48);
-  trace_cta(1);
-
-  // ---- epilogue: K-chunks in order, then per row
-  unsigned long long *xout = sd.tout;
-  const uint32_t vout = (EPI == EPI_ARGMAX) ? 0u : ver_of(c, sd.out_buf) + 1;
-  unsigned long long best = kArgmaxInitKey;
-  if (EPI == EPI_SWIGLU) {
-    // unit = {gate rows 4u..4u+3, up rows 4u..4u+3}
-    for (uint32_t t = tid; t < nloc * 4; t += kNC) {
-      const uint32_t ul = t >> 2, r = t & 3;
-      float yg = 0.f, yu = 0.f;
-      for (uint32_t ch = 0; ch < sd.ks; ++ch) {
-        yg += c.part[(ul * sd.ks + ch) * R + r];
-        yu += c.part[(ul * sd.ks + ch) * R + 4 + r];
-      }
-      yg = __fmul_rn(yg, inv);
-      yu = __fmul_rn(yu, inv);
-      const uint32_t row = (u0 + ul) * 4 + r;
-      if (row < sd.rows) xout[row] = tag_word(ref_silu_mul(yg, yu), vout);
+    __syncwarp();
+    uint32_t done = 0;
+    if (lane == 0) {
+      __threadfence_block();
+      done = atomicAdd(&c.cnt[ul], 1u) + 1;
     }
-  } else {
-    for (uint32_t t = tid; t < nloc * R; t += kNC) {
-      const uint32_t ul = t / R, r = t % R;
+    done = __shfl_sync(0xffffffffu, done, 0);
+    if (done != sd.ks) continue;
+    // ---- this warp finalises unit ul: K-chunks in order, then per row
+    __threadfence_block();
+    if (EPI == EPI_SWIGLU) {
+      // unit = {gate rows 4u..4u+3, up rows 4u..4u+3}
+      if (lane < 4) {
+        float yg = 0.f, yu = 0.f;
+        for (uint32_t ch = 0; ch < sd.ks; ++ch) {
+          yg += c.part[(ul * sd.ks + ch) * R + lane];
+          yu += c.part[(ul * sd.ks + ch) * R + 4 + lane];
+        }
+        yg = __fmul_rn(yg, inv);
+        yu = __fmul_rn(yu, inv);
+        const uint32_t row = (u0 + ul) * 4 + lane;
+        if (row < sd.rows) xout[row] = tag_word(ref_silu_mul(yg, yu), vout);
+      }
+    } else if (lane < R) {
       float y = 0.f;
-      for (uint32_t ch = 0; ch < sd.ks; ++ch) y += c.part[(ul * sd.ks + ch) * R + r];
+      for (uint32_t ch = 0; ch < sd.ks; ++ch) y += c.part[(ul * sd.ks + ch) * R + lane];
       if (PRO == PRO_RMSNORM) y = __fmul_rn(y, inv);
-      const uint32_t row = (u0 + ul) * R + r;
+      const uint32_t row = (u0 + ul) * R + lane;
       if (row < sd.rows) {
         if (EPI == EPI_STORE) {
           xout[row] = tag_word(y, vout);
@@ -529,25 +546,24 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
         }
       }
     }
+    if (lane == 0) c.cnt[ul] = 0;   // ready for the next stage that uses this unit slot
   }
+  trace(48);
   if (EPI == EPI_ARGMAX) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
       const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
       best = o > best ? o : best;
     }
-    if (lane == 0) c.best_w[warp] = best;
-    named_bar_sync(kBarConsumers, kNC);
-    if (tid == 0) {
-      unsigned long long b = kArgmaxInitKey;
-      for (int w = 0; w < kNW; ++w) b = c.best_w[w] > b ? c.best_w[w] : b;
-      if (b != kArgmaxInitKey) atomicMax(P.argmax, b);
+    if (lane == 0 && best != kArgmaxInitKey) {
+      atomicMax(P.argmax, best);
+      __threadfence();   // visible before this CTA's arrival is counted
     }
   } else {
     ver_bump(c, sd.out_buf);
   }
+  trace_cta(1);
   trace_cta(2);
-  named_bar_sync(kBarConsumers, kNC);
   trace_cta(3);
 }
 
@@ -667,6 +683,9 @@ __device__ __forceinline__ void consumer(const StepParams &P, Ctx &c) {
           run_gemv(P, sd, c, token);
         } else {
           if (blockIdx.x < P.n_kv * P.max_splits) {
+            // the previous stage's warps are done with the image area, which
+            // the attention's shared memory reuses
+            named_bar_sync(kBarConsumers, kNC);
             AttnParams ap = {};
             ap.q_norm = sd.q_norm;
             ap.k_norm = sd.k_norm;
@@ -690,8 +709,10 @@ __device__ __forceinline__ void consumer(const StepParams &P, Ctx &c) {
             ap.ver_out = c.v_attn + 1;
             ap.abort = c.abort;
             ap.gabort = &P.bar[1];
-            attn_decode_block<AttnBar, true, 4, kNW>(ap, blockIdx.x % P.n_kv, blockIdx.x / P.n_kv, pos, tid,
-                                                     *reinterpret_cast<StepAttnSmem *>(c.xsm), AttnBar());
+            trace(120);
+            attn_decode_block<AttnBar, true, 4, kNW, AttnMark>(ap, blockIdx.x % P.n_kv, blockIdx.x / P.n_kv,
+                                                               pos, tid, *reinterpret_cast<StepAttnSmem *>(c.xsm),
+                                                               AttnBar(), AttnMark());
           }
           ++c.v_attn;
           // the x image area doubles as the attention's shared memory
@@ -735,7 +756,7 @@ __device__ __forceinline__ void consumer(const StepParams &P, Ctx &c) {
 __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float red[kNW];
-  __shared__ unsigned long long best_w[kNW];
+  __shared__ uint32_t s_cnt[kMaxUnitsPerCta];
   __shared__ uint32_t s_abort, s_token;
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t *ring = smem + P.ring_off;
@@ -749,6 +770,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepParams 
     uint32_t *dst = reinterpret_cast<uint32_t *>(stages);
     for (uint32_t i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
   }
+  for (uint32_t i = threadIdx.x; i < kMaxUnitsPerCta; i += blockDim.x) s_cnt[i] = 0;
   if (threadIdx.x == 0) {
     for (uint32_t i = 0; i < kNW * kSlots; ++i) {
       mbar_init(smem_addr(&full[i]), 1);
@@ -772,7 +794,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepParams 
   c.full = full;
   c.empty = empty;
   c.red = red;
-  c.best_w = best_w;
+  c.cnt = s_cnt;
   c.s_token = &s_token;
   c.abort = abort;
   c.j = 0;
@@ -812,6 +834,7 @@ bool step_geometry(const StageDesc *stages, uint32_t n, uint32_t grid, StepParam
     const size_t img = static_cast<size_t>(s.bpr) * 128;
     if (img > xbytes) xbytes = img;
     const size_t upc = (static_cast<size_t>(s.units) + grid - 1) / grid;
+    if (upc + 1 > kMaxUnitsPerCta) return false;
     const size_t pb = upc * s.ks * 4 * s.gpu * sizeof(float);
     if (pb > part) part = pb;
     const uint64_t cb = chunk_bytes(s.quant, s.bpr < kChunkBlocks ? s.bpr : kChunkBlocks);
