@@ -32,8 +32,6 @@
 //     on timing.  The arithmetic is the standalone GEMV's (gemv_body.cuh).
 //   * The attention stage runs on n_kv * splits CTAs with all their consumer
 //     warps (attn_body.cuh); the other CTAs pass to the next stage.
-//   * A stage's input is polled with two loads in flight per word, half an
-//     L2 round trip apart, so that it is seen soon after it lands.
 // Any bounded wait that gives up sets ZDEV_ERR_TIMEOUT and the launch's abort
 // flag; from then on every wait of every CTA fails at once, producers stop
 // issuing and drain their copies in flight, and the launch runs out.
@@ -55,8 +53,7 @@ constexpr uint32_t kSlotBytes = 4608;          // 2 Q4_0 or 1 Q8_0 group-chunk o
 constexpr uint32_t kBarConsumers = 1;          // named barrier ids (0 = __syncthreads)
 constexpr uint32_t kBarAttn = 2;
 constexpr size_t kStepSmemMax = 227 * 1024;
-constexpr long long kPollStaggerClk = 600;     // ~half an L2 round trip at 1.9 GHz
-constexpr uint32_t kMaxUnitsPerCta = 256;      // per-unit arrival counters in shared memory
+constexpr size_t kStepDynSmemMax = kStepSmemMax - 3072;   // the rest is the kernel's static shared memory
 
 #ifdef ZGPU_STEP_TRACE
 // Stage timeline of CTA 0 (profiling builds only): entry k holds
@@ -248,7 +245,7 @@ struct Ctx {
   uint8_t *ring;
   uint64_t *full, *empty;
   float *red;
-  uint32_t *cnt;     // per-unit K-chunk arrival counters of the current stage
+  unsigned long long *best_w;
   uint32_t *s_token;
   volatile uint32_t *abort;
   uint32_t j;        // items this warp has consumed (matches its producer lane)
@@ -277,8 +274,7 @@ __device__ __forceinline__ void ver_bump(Ctx &c, uint32_t b) {
 }
 
 // XR: float4s of the input per consumer thread (2 covers a 2048-wide input,
-// 4 the 6144-wide one); inputs of at most 2 per thread are polled with two
-// loads in flight per word.
+// 4 the 6144-wide one).
 template <int QT, int PRO, int EPI, bool EMB, int XR>
 __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc &sd, Ctx &c, uint32_t token) {
   constexpr int GPU = (QT == ZGPU_Q4_0) ? 2 : 1;
@@ -320,15 +316,8 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
     for (int i = 0; i < kXRegs; ++i)
       if ((todo >> i & 1u) && ready(raw[i])) todo &= ~(1u << i);
     if (todo) {
-      // Two polls stay in flight, half an L2 round trip apart: the image is
-      // complete about half a round trip after the last word lands instead
-      // of up to a whole one.  Poll B starts kPollStaggerClk after poll A;
-      // from then on each poll is reissued as soon as its result is checked.
-      // The second set covers the first kXAlt float4s of each thread (all of
-      // a 2048-wide input); further words are polled once per round.
-      constexpr int kXAlt = 0;
-      ulonglong2 alt[kXAlt > 0 ? kXAlt : 1][2];
-      auto issue_raw = [&]() {
+      const uint64_t t0 = globaltimer_ns();
+      while (todo) {
 #pragma unroll
         for (int i = 0; i < kXRegs; ++i) {
           if (todo >> i & 1u) {
@@ -337,55 +326,13 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
             raw[i][1] = __ldcg(q + 1);
           }
         }
-      };
-      auto issue_alt = [&]() {
-#pragma unroll
-        for (int i = 0; i < kXAlt; ++i) {
-          if (todo >> i & 1u) {
-            const ulonglong2 *q = reinterpret_cast<const ulonglong2 *>(xin + 4 * (warp * 32 + lane + i * kNC));
-            alt[i][0] = __ldcg(q);
-            alt[i][1] = __ldcg(q + 1);
-          }
-        }
-      };
-      auto absorb_raw = [&]() {
 #pragma unroll
         for (int i = 0; i < kXRegs; ++i)
           if ((todo >> i & 1u) && ready(raw[i])) todo &= ~(1u << i);
-      };
-      auto absorb_alt = [&]() {
-#pragma unroll
-        for (int i = 0; i < kXAlt; ++i) {
-          if ((todo >> i & 1u) && ready(alt[i])) {
-            raw[i][0] = alt[i][0];
-            raw[i][1] = alt[i][1];
-            todo &= ~(1u << i);
-          }
-        }
-      };
-      auto give_up = [&]() -> bool {
+        if (!todo) break;
         if (*c.abort || ld_relaxed_u32(&P.bar[1])) {
           *c.abort = 1;
-          return true;
-        }
-        return false;
-      };
-      const uint64_t t0 = globaltimer_ns();
-      issue_raw();
-      if (kXAlt > 0) {
-        const long long c0 = clock64();
-        while (clock64() - c0 < kPollStaggerClk) {
-        }
-        issue_alt();
-      }
-      while (true) {
-        absorb_raw();
-        if (!todo || give_up()) break;
-        issue_raw();
-        if (kXAlt > 0) {
-          absorb_alt();
-          if (!todo || give_up()) break;
-          issue_alt();
+          break;
         }
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
           atomicOr(P.status, ZDEV_ERR_TIMEOUT);
@@ -406,7 +353,18 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
   for (int i = 0; i < kXRegs; ++i) {
     const uint32_t f = warp * 32 + lane + i * kNC;
     if (EMB) xr[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (f < nf4 && EMB) xr[i] = embed_f4(P, token, f);
+    if (f < nf4) {
+      if (EMB) {
+        xr[i] = embed_f4(P, token, f);
+        // the embedding is the residual base of the rows this CTA owns
+        const float ev[4] = {xr[i].x, xr[i].y, xr[i].z, xr[i].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t e = 4 * f + k;
+          if (e >= c.hrow0 && e - c.hrow0 < P.hown_rows) c.hown[e - c.hrow0] = ev[k];
+        }
+      }
+    }
   }
   trace(16 + 2 + EPI);
   // RMSNorm (ops.rs:29-52) as y = inv * (W . (x * g)): the digits are taken
@@ -414,8 +372,8 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
   // the row sums in the epilogue, so the sum of squares (fixed order: per
   // thread over its float4s, xor-tree in the warp, warps in order) needs no
   // barrier of its own: its per-warp parts cross the image barrier below.
-  float ss = 0.f;
   if (PRO == PRO_RMSNORM) {
+    float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < kXRegs; ++i) {
       const float4 t = xr[i];
@@ -424,26 +382,7 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-  }
-  // Every warp of this CTA is done with the previous stage (its items read
-  // the image, the partials, the residual rows and the RMS parts) before any
-  // of them is overwritten; the wait for the input above overlaps the
-  // stragglers.
-  named_bar_sync(kBarConsumers, kNC);
-  if (PRO == PRO_RMSNORM && lane == 0) c.red[warp] = ss;
-  if (EMB) {
-    // the embedding is the residual base of the rows this CTA owns
-#pragma unroll
-    for (int i = 0; i < kXRegs; ++i) {
-      const uint32_t f = warp * 32 + lane + i * kNC;
-      if (f >= nf4) continue;
-      const float ev[4] = {xr[i].x, xr[i].y, xr[i].z, xr[i].w};
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint32_t e = 4 * f + k;
-        if (e >= c.hrow0 && e - c.hrow0 < P.hown_rows) c.hown[e - c.hrow0] = ev[k];
-      }
-    }
+    if (lane == 0) c.red[warp] = ss;
   }
 #pragma unroll
   for (int i = 0; i < kXRegs; ++i) {
@@ -472,24 +411,17 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
     inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(sd.in_dim)), P.eps)));
   }
 
-  // ---- items: warp (k + rot) % kNW takes item k of this CTA's list.  The
-  // warp that completes a unit's last K-chunk (per-unit arrival counter in
-  // shared memory) adds the chunk partials in chunk order and publishes the
-  // unit's rows at once, so a row never waits for the CTA's slowest warp and
-  // the stage needs no barrier after its items.
+  // ---- items: warp (k + rot) % kNW takes item k of this CTA's list
   const uint32_t nloc = u1 - u0, nitems = nloc * sd.ks;
   const uint32_t first = (warp + kNW - c.rot) % kNW;
   c.rot = (c.rot + nitems) % kNW;
-  unsigned long long *xout = sd.tout;
-  const uint32_t vout = (EPI == EPI_ARGMAX) ? 0u : ver_of(c, sd.out_buf) + 1;
-  unsigned long long best = kArgmaxInitKey;
   bool failed = false;
   for (uint32_t k = first; k < nitems; k += kNW) {
     const uint32_t slot = warp * kSlots + (c.j % kSlots);
     trace(64);
     if (!failed && !wait_phase(smem_addr(&c.full[slot]), (c.j / kSlots) & 1, P.status, c.abort)) failed = true;
     trace(80);
-    const uint32_t ul = k / sd.ks, chunk = k - ul * sd.ks;
+    const uint32_t chunk = k % sd.ks;
     const uint32_t b = chunk * kChunkBlocks + lane;
     float acc[R];
 #pragma unroll
@@ -503,34 +435,36 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
     ++c.j;
     const float v = reduce_scatter<R>(acc, lane);
     if ((lane & (32 / R - 1)) == 0) c.part[k * R + lane / (32 / R)] = v;
-    __syncwarp();
-    uint32_t done = 0;
-    if (lane == 0) {
-      __threadfence_block();
-      done = atomicAdd(&c.cnt[ul], 1u) + 1;
-    }
-    done = __shfl_sync(0xffffffffu, done, 0);
-    if (done != sd.ks) continue;
-    // ---- this warp finalises unit ul: K-chunks in order, then per row
-    __threadfence_block();
-    if (EPI == EPI_SWIGLU) {
-      // unit = {gate rows 4u..4u+3, up rows 4u..4u+3}
-      if (lane < 4) {
-        float yg = 0.f, yu = 0.f;
-        for (uint32_t ch = 0; ch < sd.ks; ++ch) {
-          yg += c.part[(ul * sd.ks + ch) * R + lane];
-          yu += c.part[(ul * sd.ks + ch) * R + 4 + lane];
-        }
-        yg = __fmul_rn(yg, inv);
-        yu = __fmul_rn(yu, inv);
-        const uint32_t row = (u0 + ul) * 4 + lane;
-        if (row < sd.rows) xout[row] = tag_word(ref_silu_mul(yg, yu), vout);
+  }
+  named_bar_sync(kBarConsumers, kNC);
+  trace(48);
+  trace_cta(1);
+
+  // ---- epilogue: K-chunks in order, then per row
+  unsigned long long *xout = sd.tout;
+  const uint32_t vout = (EPI == EPI_ARGMAX) ? 0u : ver_of(c, sd.out_buf) + 1;
+  unsigned long long best = kArgmaxInitKey;
+  if (EPI == EPI_SWIGLU) {
+    // unit = {gate rows 4u..4u+3, up rows 4u..4u+3}
+    for (uint32_t t = tid; t < nloc * 4; t += kNC) {
+      const uint32_t ul = t >> 2, r = t & 3;
+      float yg = 0.f, yu = 0.f;
+      for (uint32_t ch = 0; ch < sd.ks; ++ch) {
+        yg += c.part[(ul * sd.ks + ch) * R + r];
+        yu += c.part[(ul * sd.ks + ch) * R + 4 + r];
       }
-    } else if (lane < R) {
+      yg = __fmul_rn(yg, inv);
+      yu = __fmul_rn(yu, inv);
+      const uint32_t row = (u0 + ul) * 4 + r;
+      if (row < sd.rows) xout[row] = tag_word(ref_silu_mul(yg, yu), vout);
+    }
+  } else {
+    for (uint32_t t = tid; t < nloc * R; t += kNC) {
+      const uint32_t ul = t / R, r = t % R;
       float y = 0.f;
-      for (uint32_t ch = 0; ch < sd.ks; ++ch) y += c.part[(ul * sd.ks + ch) * R + lane];
+      for (uint32_t ch = 0; ch < sd.ks; ++ch) y += c.part[(ul * sd.ks + ch) * R + r];
       if (PRO == PRO_RMSNORM) y = __fmul_rn(y, inv);
-      const uint32_t row = (u0 + ul) * R + lane;
+      const uint32_t row = (u0 + ul) * R + r;
       if (row < sd.rows) {
         if (EPI == EPI_STORE) {
           xout[row] = tag_word(y, vout);
@@ -546,24 +480,25 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
         }
       }
     }
-    if (lane == 0) c.cnt[ul] = 0;   // ready for the next stage that uses this unit slot
   }
-  trace(48);
   if (EPI == EPI_ARGMAX) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
       const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
       best = o > best ? o : best;
     }
-    if (lane == 0 && best != kArgmaxInitKey) {
-      atomicMax(P.argmax, best);
-      __threadfence();   // visible before this CTA's arrival is counted
+    if (lane == 0) c.best_w[warp] = best;
+    named_bar_sync(kBarConsumers, kNC);
+    if (tid == 0) {
+      unsigned long long b = kArgmaxInitKey;
+      for (int w = 0; w < kNW; ++w) b = c.best_w[w] > b ? c.best_w[w] : b;
+      if (b != kArgmaxInitKey) atomicMax(P.argmax, b);
     }
   } else {
     ver_bump(c, sd.out_buf);
   }
-  trace_cta(1);
   trace_cta(2);
+  named_bar_sync(kBarConsumers, kNC);
   trace_cta(3);
 }
 
@@ -683,9 +618,6 @@ __device__ __forceinline__ void consumer(const StepParams &P, Ctx &c) {
           run_gemv(P, sd, c, token);
         } else {
           if (blockIdx.x < P.n_kv * P.max_splits) {
-            // the previous stage's warps are done with the image area, which
-            // the attention's shared memory reuses
-            named_bar_sync(kBarConsumers, kNC);
             AttnParams ap = {};
             ap.q_norm = sd.q_norm;
             ap.k_norm = sd.k_norm;
@@ -756,7 +688,7 @@ __device__ __forceinline__ void consumer(const StepParams &P, Ctx &c) {
 __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float red[kNW];
-  __shared__ uint32_t s_cnt[kMaxUnitsPerCta];
+  __shared__ unsigned long long best_w[kNW];
   __shared__ uint32_t s_abort, s_token;
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t *ring = smem + P.ring_off;
@@ -770,7 +702,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepParams 
     uint32_t *dst = reinterpret_cast<uint32_t *>(stages);
     for (uint32_t i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
   }
-  for (uint32_t i = threadIdx.x; i < kMaxUnitsPerCta; i += blockDim.x) s_cnt[i] = 0;
   if (threadIdx.x == 0) {
     for (uint32_t i = 0; i < kNW * kSlots; ++i) {
       mbar_init(smem_addr(&full[i]), 1);
@@ -794,7 +725,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepParams 
   c.full = full;
   c.empty = empty;
   c.red = red;
-  c.cnt = s_cnt;
+  c.best_w = best_w;
   c.s_token = &s_token;
   c.abort = abort;
   c.j = 0;
@@ -834,7 +765,6 @@ bool step_geometry(const StageDesc *stages, uint32_t n, uint32_t grid, StepParam
     const size_t img = static_cast<size_t>(s.bpr) * 128;
     if (img > xbytes) xbytes = img;
     const size_t upc = (static_cast<size_t>(s.units) + grid - 1) / grid;
-    if (upc + 1 > kMaxUnitsPerCta) return false;
     const size_t pb = upc * s.ks * 4 * s.gpu * sizeof(float);
     if (pb > part) part = pb;
     const uint64_t cb = chunk_bytes(s.quant, s.bpr < kChunkBlocks ? s.bpr : kChunkBlocks);
@@ -856,7 +786,7 @@ bool step_geometry(const StageDesc *stages, uint32_t n, uint32_t grid, StepParam
   const size_t stages_bytes = (static_cast<size_t>(n) * sizeof(StageDesc) + 127) & ~size_t(127);
   const size_t ring_off = stages_off + stages_bytes;
   const size_t smem = ring_off + static_cast<size_t>(kNW) * kSlots * kSlotBytes + 2 * kNW * kSlots * 8;
-  if (smem > kStepSmemMax - 1024) return false;
+  if (smem > kStepDynSmemMax) return false;
   p->xbytes = static_cast<uint32_t>(xbytes);
   p->part_bytes = static_cast<uint32_t>(part);
   p->hown_off = static_cast<uint32_t>(hown_off);
@@ -870,8 +800,12 @@ bool step_geometry(const StageDesc *stages, uint32_t n, uint32_t grid, StepParam
 }
 
 cudaError_t step_setup() {
-  cudaError_t e = cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(kStepSmemMax - 1024));
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, step_kernel);
+  if (e != cudaSuccess) return e;
+  if (fa.sharedSizeBytes + kStepDynSmemMax > kStepSmemMax) return cudaErrorInvalidValue;
+  e = cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(kStepDynSmemMax));
   if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(step_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                               cudaSharedmemCarveoutMaxShared);
@@ -880,7 +814,7 @@ cudaError_t step_setup() {
 uint32_t step_max_grid(int sm_count) {
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, step_kernel, kStepThreads,
-                                                    kStepSmemMax - 4096) != cudaSuccess) {
+                                                    kStepDynSmemMax) != cudaSuccess) {
     cudaGetLastError();
     return 0;
   }
