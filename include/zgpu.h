@@ -140,6 +140,19 @@ zgpu_status zgpu_linear_q8act(zgpu_ctx *ctx, const void *xq_blocks, const void *
 zgpu_status zgpu_linear_q8act_device(zgpu_ctx *ctx, const void *d_xq_blocks, const void *w_key,
                                      float *d_out, uint64_t in_dim, uint64_t out_dim, void *stream);
 
+/* Batched form on the tensor cores (tcgen05 int8 MMA): T rows of f32
+ * activations x[T][in_dim] are quantised per 32-block with the Q8_0 rule
+ * above, then out[t][r] = sum_b d_w*d_x*sum_j (n-8)*q, accumulated in block
+ * order (bit-identical to the single-row product).  No counterpart in the
+ * reference, which decodes one token at a time: this is the prefill /
+ * multi-token path.  out_dim must be a multiple of 128.  Host buffers. */
+zgpu_status zgpu_linear_q8act_batch(zgpu_ctx *ctx, const float *x, const void *w_key, float *out,
+                                    uint64_t T, uint64_t in_dim, uint64_t out_dim);
+/* Same with device-resident f32 activations / output on `stream` (async). */
+zgpu_status zgpu_linear_q8act_batch_device(zgpu_ctx *ctx, const float *d_x, const void *w_key,
+                                           float *d_out, uint64_t T, uint64_t in_dim,
+                                           uint64_t out_dim, void *stream);
+
 /* ------------------------------------------------------------- small ops */
 /* rmsnorm (ops.rs:29-52). */
 zgpu_status zgpu_rmsnorm(zgpu_ctx *ctx, const float *x, const float *w, float *out, uint64_t n,

@@ -129,6 +129,21 @@ class Context:
         key = w if isinstance(w, int) else _ptr(w)
         self._check(LIB.zgpu_linear_q8act_device(self.h, d_xq, key, d_out, in_dim, out_dim, stream or None))
 
+    def linear_q8act_batch(self, x: np.ndarray, w, in_dim: int, out_dim: int) -> np.ndarray:
+        """T rows of activations (x [T, in_dim] f32) quantised to Q8_0 and
+        multiplied by Q4_0 weights on the tcgen05 int8 path; returns [T, out_dim]."""
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, in_dim)
+        out = np.empty((x.shape[0], out_dim), np.float32)
+        key = w if isinstance(w, int) else _ptr(w)
+        self._check(LIB.zgpu_linear_q8act_batch(self.h, _ptr(x), key, _ptr(out), x.shape[0], in_dim, out_dim))
+        return out
+
+    def linear_q8act_batch_device(self, d_x: int, w, d_out: int, T: int, in_dim: int, out_dim: int,
+                                  stream: int = 0):
+        key = w if isinstance(w, int) else _ptr(w)
+        self._check(LIB.zgpu_linear_q8act_batch_device(self.h, d_x, key, d_out, T, in_dim, out_dim,
+                                                       stream or None))
+
     # ---------------------------------------------------------- small ops
     def rmsnorm(self, x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
         x = np.ascontiguousarray(x, np.float32)

@@ -195,6 +195,23 @@ __device__ __forceinline__ void ref_sincos(float x, float *s_out, float *c_out) 
   *c_out = (b0 ^ b1) ? -c : c;
 }
 
+// binary16 bits of a finite double with |v| <= 65504, rounded to nearest-even
+// straight from the double (struct.pack('<e') semantics): scale the value
+// exactly onto the binary16 grid of its binade (a power-of-two ldexp), round
+// with rint, re-encode.  Subnormal results and the carry into the next binade
+// fall out of the continuous encoding.
+__device__ __forceinline__ uint16_t f64_to_f16_rne(double v) {
+  const uint16_t sign = signbit(v) ? 0x8000u : 0u;
+  const double a = fabs(v);
+  if (a == 0.0) return sign;
+  const int e = ilogb(a);
+  const int qe = (e < -14 ? -14 : e) - 10;
+  const double r = rint(ldexp(a, -qe));
+  if (e < -14) return static_cast<uint16_t>(sign | static_cast<uint16_t>(r));
+  if (r >= 2048.0) return static_cast<uint16_t>(sign | ((e + 16) << 10));
+  return static_cast<uint16_t>(sign | ((e + 15) << 10) | static_cast<uint16_t>(r - 1024.0));
+}
+
 // Tagged activation words (the persistent step kernel's inter-stage
 // vectors): element i is (version << 32) | f32 bits, written with one 64-bit
 // store, so a reader that sees the expected version also sees its value.

@@ -116,6 +116,7 @@ void zgpu_destroy(zgpu_ctx *ctx) {
   cudaFree(ctx->d_attn_part);
   cudaFree(ctx->d_attn_counters);
   cudaFree(ctx->d_route_counter);
+  cudaFree(ctx->d_q8);
   cudaFree(ctx->d_status);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
@@ -440,6 +441,66 @@ zgpu_status zgpu_linear_q8act(zgpu_ctx *ctx, const void *xq_blocks, const void *
   ZCHECK(cudaMemcpyAsync(out, ctx->d_y, out_dim * 4, cudaMemcpyDeviceToHost, ctx->stream), "d2h");
   ZCHECK(cudaStreamSynchronize(ctx->stream), "sync");
   return ZGPU_OK;
+}
+
+// Batched form: T rows of f32 activations, quantised to Q8_0 per row on the
+// device, times Q4_0 weights on the tcgen05 int8 path (mma_gemm.cu).
+static zgpu_status q8act_batch(zgpu_ctx *ctx, const float *d_x, const void *w_key, float *d_out, uint64_t T,
+                               uint64_t in_dim, uint64_t out_dim, cudaStream_t s) {
+  const DeviceTensor *t = zgpu_lookup(ctx, w_key);
+  if (!t) return zgpu_fail(ctx, ZGPU_ERR_UNREGISTERED_WEIGHT, "linear_q8act_batch: unregistered weight");
+  if (t->quant != ZGPU_Q4_0)
+    return zgpu_fail(ctx, ZGPU_ERR_UNSUPPORTED_QUANT, "linear_q8act_batch: weights must be Q4_0");
+  if (t->cols != in_dim || t->rows != out_dim)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "linear_q8act_batch: shape mismatch with registration");
+  if (out_dim % 128 || T > 0xFFFFFFu || T * in_dim > (1ull << 34))
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "linear_q8act_batch: rows must be a multiple of 128");
+  // scratch: q int8 [T][in] | d f32 [T][in/32]
+  const size_t qbytes = (T * in_dim + 15) & ~size_t(15), dbytes = T * (in_dim / 32) * 4;
+  if (qbytes + dbytes > ctx->d_q8_cap) {
+    cudaFree(ctx->d_q8);
+    ctx->d_q8 = nullptr;
+    ctx->d_q8_cap = 0;
+    ZCHECK(cudaMalloc(&ctx->d_q8, qbytes + dbytes), "cudaMalloc(q8 scratch)");
+    ctx->d_q8_cap = qbytes + dbytes;
+  }
+  int8_t *q = reinterpret_cast<int8_t *>(ctx->d_q8);
+  float *d = reinterpret_cast<float *>(ctx->d_q8 + qbytes);
+  ZCHECK(zgpu::launch_quantize_q8_0_planar(d_x, q, d, T * in_dim, ctx->d_status, s), "q8 planar");
+  zgpu::MmaGemmParams p = {};
+  p.w = t->d;
+  p.gstride = t->gstride;
+  p.rows = static_cast<uint32_t>(out_dim);
+  p.bpr = static_cast<uint32_t>(in_dim / 32);
+  p.T = static_cast<uint32_t>(T);
+  p.ldy = static_cast<uint32_t>(out_dim);
+  p.xq = q;
+  p.xs = d;
+  p.y = d_out;
+  p.status = ctx->d_status;
+  ZCHECK(zgpu::launch_q4q8_mma(p, s), "q4q8 mma");
+  ctx->launches += 2;
+  return ZGPU_OK;
+}
+
+zgpu_status zgpu_linear_q8act_batch_device(zgpu_ctx *ctx, const float *d_x, const void *w_key, float *d_out,
+                                           uint64_t T, uint64_t in_dim, uint64_t out_dim, void *stream) {
+  if (!ctx || !d_x || !d_out || T == 0 || in_dim == 0 || in_dim % 32) return ZGPU_ERR_INVALID_ARG;
+  cudaSetDevice(ctx->device);
+  return q8act_batch(ctx, d_x, w_key, d_out, T, in_dim, out_dim,
+                     stream ? static_cast<cudaStream_t>(stream) : ctx->stream);
+}
+
+zgpu_status zgpu_linear_q8act_batch(zgpu_ctx *ctx, const float *x, const void *w_key, float *out, uint64_t T,
+                                    uint64_t in_dim, uint64_t out_dim) {
+  if (!ctx || !x || !out || T == 0 || in_dim == 0 || in_dim % 32) return ZGPU_ERR_INVALID_ARG;
+  cudaSetDevice(ctx->device);
+  zgpu_status s = ensure_scratch(ctx, T * in_dim, T * out_dim);
+  if (s) return s;
+  ZCHECK(cudaMemcpyAsync(ctx->d_x, x, T * in_dim * 4, cudaMemcpyHostToDevice, ctx->stream), "h2d");
+  if ((s = q8act_batch(ctx, ctx->d_x, w_key, ctx->d_y, T, in_dim, out_dim, ctx->stream))) return s;
+  ZCHECK(cudaMemcpyAsync(out, ctx->d_y, T * out_dim * 4, cudaMemcpyDeviceToHost, ctx->stream), "d2h");
+  return check_status_word(ctx);
 }
 
 }  // extern "C"

@@ -93,6 +93,9 @@ struct zgpu_ctx {
   uint32_t d_attn_counters_cap = 0;
   // arrival counter of the MoE router entry point (zero between calls)
   uint32_t *d_route_counter = nullptr;
+  // planar Q8_0 activations of the batched entry points
+  uint8_t *d_q8 = nullptr;
+  size_t d_q8_cap = 0;
 };
 
 // KV cache: layer-major [L][K block | V block], block = max_tokens x n_kv x

@@ -1,0 +1,282 @@
+// mma_gemm.cu — batched Q4_0 weight x Q8_0 activation matmul on the 5th-gen
+// tensor cores (tcgen05, int8), for prefill and multi-token decode.
+//
+// Y[t][m] = sum_b d_w[m,b] * d_x[t,b] * sum_{j<32} (n[m,b,j] - 8) * q[t,b,j]
+//
+// Both operands carry one scale per 32-element block, so a block's integer
+// dot product must be scaled before it is added to the next block's.  Each
+// block is therefore one tcgen05.mma.kind::i8 of M = 128 weight rows x N = 64
+// tokens x K = 32 whose int32 result lands in TMEM; the four epilogue warps
+// read it back (tcgen05.ld, lane = row) and add (sumi * d_w) * d_x to f32
+// accumulators in block order.  That is exactly the order of the CPU
+// restatement of the Q4_0 x Q8_0 product (ggml's vec_dot_q4_0_q8_0 loop), so
+// results are bit-identical to it.
+//
+// Data path per block, 128 threads:
+//   * a cp.async ring of kStages stages holds, per block, the 128 rows' 16
+//     nibble bytes (one plane entry of each row's group stream, layout.h), the
+//     32 groups' fp16 scales, the 64 tokens' 32 int8 activations (placed
+//     directly in the MMA's canonical K-major layout) and their scales;
+//   * thread t unpacks row t's nibbles into int8 (n - 8) in the A tile
+//     (canonical K-major layout, no swizzle: 8-row x 16-byte core matrices,
+//     SBO = 256 B between row groups, LBO = 128 B between the two K halves);
+//   * thread 0 issues the MMA and commits it to an mbarrier; all threads wait
+//     (bounded), load their row of D from TMEM and accumulate.
+// Requires rows % 128 == 0 and in_dim % 32 == 0; tokens are zero-filled past T.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "internal.h"
+#include "layout.h"
+#include "ops.h"
+
+namespace zgpu {
+
+namespace {
+
+constexpr uint32_t kTileM = 128;
+constexpr uint32_t kTileN = 64;
+constexpr uint32_t kGemmThreads = 128;
+constexpr uint32_t kStages = 6;
+// stage layout (bytes)
+constexpr uint32_t kRawA = 0;                    // 128 rows x 16 B nibbles
+constexpr uint32_t kScA = 2048;                  // 32 groups x 8 B fp16 scales
+constexpr uint32_t kTileB = 2304;                // 64 tokens x 32 B, canonical K-major
+constexpr uint32_t kScB = 4352;                  // 64 tokens x f32 scales
+constexpr uint32_t kStageBytes = 4608;
+constexpr uint32_t kTmemCols = 64;               // one 128 x 64 int32 accumulator
+
+// Byte offset of (row r, K half h) in a canonical K-major no-swizzle tile of
+// 32-byte rows: core matrix (r / 8, h) holds rows 8(r/8).. x bytes 16h..16h+15.
+__device__ __forceinline__ uint32_t core_off(uint32_t r, uint32_t h) {
+  return (r & 7) * 16 + (r >> 3) * 256 + h * 128;
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// UMMA shared-memory descriptor: K-major, no swizzle (layout type 0),
+// descriptor version 1, LBO / SBO in 16-byte units.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;   // version
+  return d;
+}
+
+// Instruction descriptor of kind::i8: D s32, A and B signed int8, both
+// K-major, N = 64, M = 128, dense.
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((kTileN >> 3) << 17) | ((kTileM >> 4) << 24);
+
+__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t mbar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)
+               : "memory");
+}
+
+// 32 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+        "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+        "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Nibbles n (0..15) of four bytes -> four int8 (n - 8): flip bit 3, then
+// sign-extend it over the high nibble (0x08 * 0x1E = 0xF0, no carries).
+__device__ __forceinline__ uint32_t nib_to_s8(uint32_t n4) {
+  const uint32_t m = n4 ^ 0x08080808u;
+  return m | ((m & 0x08080808u) * 0x1Eu);
+}
+
+__global__ void __launch_bounds__(kGemmThreads) q4q8_mma_kernel(const MmaGemmParams p) {
+  __shared__ __align__(128) uint8_t ring[kStages * kStageBytes];
+  __shared__ __align__(128) uint8_t tileA[kTileM * 32];
+  __shared__ __align__(8) uint64_t mbar;
+  __shared__ uint32_t tmem_base;
+  const uint32_t tid = threadIdx.x, warp = tid >> 5;
+  const uint32_t m0 = blockIdx.x * kTileM, t0 = blockIdx.y * kTileN;
+  const uint32_t bpr = p.bpr, K = bpr * 32;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 0) {
+    mbar_init(smem_addr(&mbar), 1);
+    fence_barrier_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  // issue the copies of block b into its stage
+  const uint32_t row = m0 + tid;                       // this thread's weight row
+  const uint8_t *grp_row = p.w + static_cast<uint64_t>(row >> 2) * p.gstride;
+  const uint32_t tl = tid >> 1, th = tid & 1;          // token / K half this thread copies
+  const bool tok_ok = t0 + tl < p.T;
+  const int8_t *xrow = p.xq + static_cast<uint64_t>(tok_ok ? t0 + tl : 0) * K;
+  auto issue = [&](uint32_t b) {
+    const uint32_t st = smem_addr(ring + (b % kStages) * kStageBytes);
+    cp_async16(st + kRawA + tid * 16, grp_row + plane_entry(ZGPU_Q4_0, bpr, b, row & 3), 16);
+    if (tid < 32)
+      cp_async8(st + kScA + tid * 8,
+                p.w + static_cast<uint64_t>((m0 >> 2) + tid) * p.gstride + scale_entry(ZGPU_Q4_0, bpr, b));
+    cp_async16(st + kTileB + core_off(tl, th), xrow + 32 * b + 16 * th, tok_ok ? 16u : 0u);
+    if (tid < kTileN) {
+      const bool ok = t0 + tid < p.T;
+      cp_async4(st + kScB + tid * 4, p.xs + static_cast<uint64_t>(ok ? t0 + tid : 0) * bpr + b, ok ? 4u : 0u);
+    }
+  };
+#pragma unroll
+  for (uint32_t s = 0; s < kStages - 1; ++s) {
+    if (s < bpr) issue(s);
+    cp_async_commit();
+  }
+
+  float acc[kTileN];
+#pragma unroll
+  for (int j = 0; j < static_cast<int>(kTileN); ++j) acc[j] = 0.f;
+  const uint32_t idesc = kIdesc;
+  const uint64_t adesc = umma_desc(smem_addr(tileA), 128, 256);
+  bool ok = true;
+  for (uint32_t b = 0; b < bpr; ++b) {
+    if (b + kStages - 1 < bpr) issue(b + kStages - 1);
+    cp_async_commit();
+    cp_async_wait<kStages - 1>();   // this thread's copies of block b have landed
+    __syncthreads();                // ... and everyone's
+    uint8_t *st = ring + (b % kStages) * kStageBytes;
+    // A: row tid's nibbles -> int8 (n - 8) in the canonical layout
+    {
+      const uint4 q = *reinterpret_cast<const uint4 *>(st + kRawA + tid * 16);
+      uint4 lo, hi;
+      lo.x = nib_to_s8(q.x & 0x0F0F0F0Fu);
+      lo.y = nib_to_s8(q.y & 0x0F0F0F0Fu);
+      lo.z = nib_to_s8(q.z & 0x0F0F0F0Fu);
+      lo.w = nib_to_s8(q.w & 0x0F0F0F0Fu);
+      hi.x = nib_to_s8((q.x >> 4) & 0x0F0F0F0Fu);
+      hi.y = nib_to_s8((q.y >> 4) & 0x0F0F0F0Fu);
+      hi.z = nib_to_s8((q.z >> 4) & 0x0F0F0F0Fu);
+      hi.w = nib_to_s8((q.w >> 4) & 0x0F0F0F0Fu);
+      *reinterpret_cast<uint4 *>(tileA + core_off(tid, 0)) = lo;
+      *reinterpret_cast<uint4 *>(tileA + core_off(tid, 1)) = hi;
+    }
+    const uint16_t hw = *reinterpret_cast<const uint16_t *>(st + kScA + (tid >> 2) * 8 + (tid & 3) * 2);
+    const float dw = h2f(hw);
+    fence_proxy_async_smem();   // generic-proxy writes of A and B -> visible to the tensor core
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      umma_i8(tmem, adesc, umma_desc(smem_addr(st + kTileB), 128, 256), idesc, 0u);
+      umma_commit(smem_addr(&mbar));
+    }
+    if (ok && !mbar_wait(smem_addr(&mbar), b & 1, p.status)) ok = false;
+    tc_fence_after();
+    uint32_t v0[32], v1[32];
+    const uint32_t taddr = tmem + ((warp * 32u) << 16);
+    tmem_ld32(taddr, v0);
+    tmem_ld32(taddr + 32, v1);
+    tmem_ld_wait();
+    const float *dx = reinterpret_cast<const float *>(st + kScB);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      acc[j] = __fadd_rn(acc[j], __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(v0[j])), dw), dx[j]));
+      acc[32 + j] =
+          __fadd_rn(acc[32 + j], __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(v1[j])), dw), dx[32 + j]));
+    }
+    tc_fence_before();
+    // the next iteration's first barrier orders these TMEM reads and the
+    // reads of this stage before the next MMA and the stage's refill
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int j = 0; j < static_cast<int>(kTileN); ++j)
+    if (t0 + j < p.T) p.y[static_cast<uint64_t>(t0 + j) * p.ldy + row] = ok ? acc[j] : __uint_as_float(0x7fc00000u);
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+}
+
+// Q8_0 activation rows in the planar form the MMA reads: q int8 [T][K] and
+// the block scale d (fp16-rounded, as f32) [T][K/32].  The packer's rule, as
+// quantize_q8_0_kernel.  One warp per block.
+__global__ void quantize_q8_0_planar_kernel(const float *x, int8_t *q, float *d, uint64_t nblocks,
+                                            uint32_t *status) {
+  const uint64_t wb = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const uint32_t lane = threadIdx.x & 31;
+  if (wb >= nblocks) return;
+  const float v = x[wb * 32 + lane];
+  if (!(fabsf(v) < INFINITY)) atomicOr(status, ZDEV_ERR_NUMERICAL);
+  double a = fabs(static_cast<double>(v));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) a = fmax(a, __shfl_xor_sync(0xffffffffu, a, off));
+  if (a == 0.0 || !(a < INFINITY)) {
+    q[wb * 32 + lane] = 0;
+    if (lane == 0) d[wb] = 0.f;
+    return;
+  }
+  const double dd = a / 127.0;
+  double r = rint(static_cast<double>(v) * (1.0 / dd));
+  r = fmin(fmax(r, -127.0), 127.0);
+  q[wb * 32 + lane] = static_cast<int8_t>(r);
+  if (lane == 0) d[wb] = h2f(f64_to_f16_rne(fmin(dd, 65504.0)));
+}
+
+}  // namespace
+
+cudaError_t launch_q4q8_mma(const MmaGemmParams &p, cudaStream_t s) {
+  if (p.rows == 0 || p.rows % kTileM || p.bpr == 0 || p.T == 0 || p.gstride % 16) return cudaErrorInvalidValue;
+  dim3 grid(p.rows / kTileM, (p.T + kTileN - 1) / kTileN);
+  q4q8_mma_kernel<<<grid, kGemmThreads, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_q8_0_planar(const float *x, int8_t *q, float *d, uint64_t n, uint32_t *status,
+                                        cudaStream_t s) {
+  const uint64_t nb = n / 32;
+  quantize_q8_0_planar_kernel<<<static_cast<unsigned>((nb * 32 + 255) / 256), 256, 0, s>>>(x, q, d, nb, status);
+  return cudaGetLastError();
+}
+
+}  // namespace zgpu

@@ -82,6 +82,22 @@ inline cudaLaunchConfig_t make_launch_cfg(dim3 grid, dim3 block, size_t smem, co
   return cfg;
 }
 
+// Batched Q4_0 x Q8_0 matmul on tcgen05 (mma_gemm.cu): y[t * ldy + m] for
+// t < T, m < rows, from the layout.h weight streams and planar Q8_0
+// activations (q int8 [T][bpr*32], d f32 [T][bpr]).
+struct MmaGemmParams {
+  const uint8_t *w;
+  uint64_t gstride;
+  uint32_t rows, bpr, T, ldy;
+  const int8_t *xq;
+  const float *xs;
+  float *y;
+  uint32_t *status;
+};
+cudaError_t launch_q4q8_mma(const MmaGemmParams &p, cudaStream_t s);
+cudaError_t launch_quantize_q8_0_planar(const float *x, int8_t *q, float *d, uint64_t n, uint32_t *status,
+                                        cudaStream_t s);
+
 cudaError_t launch_attention(const AttnParams &ap, const LaunchCfg &lc);
 // Number of attention splits (CTAs per kv-head) a cache of max_tokens needs.
 uint32_t attention_max_splits(uint32_t max_tokens);

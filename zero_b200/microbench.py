@@ -11,6 +11,11 @@ activation + output bytes per launch).
 
 --act f32 runs the reference's f32-activation GEMV (Q4_0X4 weights,
 linear_dispatch); --act q8 runs the Q4_0 x Q8_0-activation GEMV.
+
+--tokens T (prefill) times the batched Q4_0 x Q8_0 matmul
+on the tcgen05 int8 path instead: T activation rows per launch (quantisation
+included), reported as int8 TOPS (2 * rows * in * T per launch) next to the
+weight and activation bytes.
 """
 from __future__ import annotations
 
@@ -78,19 +83,58 @@ def run_shape(ctx, out_dim: int, in_dim: int, act: str, reps: int, copies: int |
             "gbs": round(alg / (ms * 1e-3) / 1e9, 1)}
 
 
+def run_batch(ctx, out_dim: int, in_dim: int, T: int, reps: int, torch):
+    w = synth.q4_0(100, out_dim + 7 * in_dim, out_dim, in_dim, 0.02)
+    key = ctx.register(w, zb.Q4_0, out_dim, in_dim)
+    stream = torch.cuda.Stream()
+    sh = stream.cuda_stream
+    x = torch.randn(T, in_dim, device="cuda", dtype=torch.float32)
+    y = torch.empty(T, out_dim, device="cuda", dtype=torch.float32)
+
+    def launch():
+        ctx.linear_q8act_batch_device(x.data_ptr(), key, y.data_ptr(), T, in_dim, out_dim, sh)
+
+    with torch.cuda.stream(stream):
+        launch()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        launch()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        graph.replay()
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    stream.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    ops = 2.0 * out_dim * in_dim * T
+    del graph
+    ctx.clear_weights()
+    return {"kernel": "q4q8_mma (tcgen05 kind::i8) + q8_0 quantiser", "shape": f"{in_dim}->{out_dim}",
+            "tokens": T, "reps": reps, "avg_launch_us": round(ms * 1000, 2),
+            "tops": round(ops / (ms * 1e-3) / 1e12, 2),
+            "bytes": out_dim * in_dim * 18 // 32 + T * in_dim * 4 + T * out_dim * 4}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--shape", action="append", help="OUTxIN, repeatable (default: config 1 sweep)")
     ap.add_argument("--act", default="f32", choices=["f32", "q8"])
     ap.add_argument("--reps", type=int, default=10)
     ap.add_argument("--copies", type=int, default=None, help="weight copies (default: > 2x L2)")
+    ap.add_argument("--tokens", type=int, default=0, help="time the batched tcgen05 matmul over T tokens")
     args = ap.parse_args()
     import torch
 
     ctx = zb.Context()
     for s in args.shape or CONFIG1_SHAPES:
         o, i = (int(v) for v in s.lower().split("x"))
-        print(json.dumps(run_shape(ctx, o, i, args.act, args.reps, args.copies, torch)), flush=True)
+        if args.tokens:
+            print(json.dumps(run_batch(ctx, o, i, args.tokens, args.reps, torch)), flush=True)
+        else:
+            print(json.dumps(run_shape(ctx, o, i, args.act, args.reps, args.copies, torch)), flush=True)
     ctx.close()
 
 
