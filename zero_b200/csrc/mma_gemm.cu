@@ -5,23 +5,25 @@
 //
 // Both operands carry one scale per 32-element block, so a block's integer
 // dot product must be scaled before it is added to the next block's.  Each
-// block is therefore one tcgen05.mma.kind::i8 of M = 128 weight rows x N = 64
-// tokens x K = 32 whose int32 result lands in TMEM; the four epilogue warps
-// read it back (tcgen05.ld, lane = row) and add (sumi * d_w) * d_x to f32
+// block is therefore one tcgen05.mma.kind::i8 of M = 128 weight rows x N = 128
+// tokens x K = 32 whose int32 result lands in TMEM; eight warps read it back
+// (tcgen05.ld: warp w takes lanes 32(w%4).. = rows, columns 64(w/4)..) and add (sumi * d_w) * d_x to f32
 // accumulators in block order.  That is exactly the order of the CPU
 // restatement of the Q4_0 x Q8_0 product (ggml's vec_dot_q4_0_q8_0 loop), so
 // results are bit-identical to it.
 //
-// Data path per block, 128 threads:
-//   * a cp.async ring of kStages stages holds, per block, the 128 rows' 16
+// Data path per block, 256 threads:
+//   * a cp.async ring of kStages stages (kStages - 2 blocks ahead) holds, per block, the 128 rows' 16
 //     nibble bytes (one plane entry of each row's group stream, layout.h), the
-//     32 groups' fp16 scales, the 64 tokens' 32 int8 activations (placed
+//     32 groups' fp16 scales, the 128 tokens' 32 int8 activations (placed
 //     directly in the MMA's canonical K-major layout) and their scales;
-//   * thread t unpacks row t's nibbles into int8 (n - 8) in the A tile
+//   * thread t < 128 unpacks row t's nibbles into int8 (n - 8) in the A tile
 //     (canonical K-major layout, no swizzle: 8-row x 16-byte core matrices,
 //     SBO = 256 B between row groups, LBO = 128 B between the two K halves);
 //   * thread 0 issues the MMA and commits it to an mbarrier; all threads wait
-//     (bounded), load their row of D from TMEM and accumulate.
+//     (bounded), load their row of D from TMEM and accumulate.  The loop is
+//     software-pipelined: block b+1's unpack and MMA (two A buffers, two TMEM
+//     accumulators) are issued before block b's accumulator is scaled.
 // Requires rows % 128 == 0 and in_dim % 32 == 0; tokens are zero-filled past T.
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -36,16 +38,16 @@ namespace zgpu {
 namespace {
 
 constexpr uint32_t kTileM = 128;
-constexpr uint32_t kTileN = 64;
-constexpr uint32_t kGemmThreads = 128;
-constexpr uint32_t kStages = 6;
+constexpr uint32_t kTileN = 128;
+constexpr uint32_t kGemmThreads = 256;   // 8 warps: (lane quarter, 64-column half) of the accumulator
+constexpr uint32_t kStages = 5;
 // stage layout (bytes)
 constexpr uint32_t kRawA = 0;                    // 128 rows x 16 B nibbles
 constexpr uint32_t kScA = 2048;                  // 32 groups x 8 B fp16 scales
-constexpr uint32_t kTileB = 2304;                // 64 tokens x 32 B, canonical K-major
-constexpr uint32_t kScB = 4352;                  // 64 tokens x f32 scales
-constexpr uint32_t kStageBytes = 4608;
-constexpr uint32_t kTmemCols = 64;               // one 128 x 64 int32 accumulator
+constexpr uint32_t kTileB = 2304;                // 128 tokens x 32 B, canonical K-major
+constexpr uint32_t kScB = 6400;                  // 128 tokens x f32 scales
+constexpr uint32_t kStageBytes = 6912;
+constexpr uint32_t kTmemCols = 256;              // two 128 x 128 int32 accumulators
 
 // Byte offset of (row r, K half h) in a canonical K-major no-swizzle tile of
 // 32-byte rows: core matrix (r / 8, h) holds rows 8(r/8).. x bytes 16h..16h+15.
@@ -119,6 +121,12 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Exact int32 -> f32 for |v| < 2^22 with two full-rate ops: v + 1.5 * 2^23
+// as float bits, minus 1.5 * 2^23 (a block's |sumi| <= 32 * 8 * 127).
+__device__ __forceinline__ float small_i2f(uint32_t v) {
+  return __fsub_rn(__int_as_float(static_cast<int>(v) + 0x4B400000), 12582912.0f);
+}
+
 // Nibbles n (0..15) of four bytes -> four int8 (n - 8): flip bit 3, then
 // sign-extend it over the high nibble (0x08 * 0x1E = 0xF0, no carries).
 __device__ __forceinline__ uint32_t nib_to_s8(uint32_t n4) {
@@ -126,10 +134,10 @@ __device__ __forceinline__ uint32_t nib_to_s8(uint32_t n4) {
   return m | ((m & 0x08080808u) * 0x1Eu);
 }
 
-__global__ void __launch_bounds__(kGemmThreads) q4q8_mma_kernel(const MmaGemmParams p) {
+__global__ void __launch_bounds__(kGemmThreads, 2) q4q8_mma_kernel(const MmaGemmParams p) {
   __shared__ __align__(128) uint8_t ring[kStages * kStageBytes];
-  __shared__ __align__(128) uint8_t tileA[kTileM * 32];
-  __shared__ __align__(8) uint64_t mbar;
+  __shared__ __align__(128) uint8_t tileA[2][kTileM * 32];
+  __shared__ __align__(8) uint64_t mbar[2];
   __shared__ uint32_t tmem_base;
   const uint32_t tid = threadIdx.x, warp = tid >> 5;
   const uint32_t m0 = blockIdx.x * kTileM, t0 = blockIdx.y * kTileN;
@@ -142,7 +150,8 @@ __global__ void __launch_bounds__(kGemmThreads) q4q8_mma_kernel(const MmaGemmPar
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (tid == 0) {
-    mbar_init(smem_addr(&mbar), 1);
+    mbar_init(smem_addr(&mbar[0]), 1);
+    mbar_init(smem_addr(&mbar[1]), 1);
     fence_barrier_init();
   }
   tc_fence_before();
@@ -151,87 +160,126 @@ __global__ void __launch_bounds__(kGemmThreads) q4q8_mma_kernel(const MmaGemmPar
   const uint32_t tmem = tmem_base;
 
   // issue the copies of block b into its stage
-  const uint32_t row = m0 + tid;                       // this thread's weight row
+  // threads 0..127 own a weight row each (copy, unpack, and their rows' scale)
+  const uint32_t arow = tid & (kTileM - 1);
+  const uint32_t row = m0 + arow;
   const uint8_t *grp_row = p.w + static_cast<uint64_t>(row >> 2) * p.gstride;
   const uint32_t tl = tid >> 1, th = tid & 1;          // token / K half this thread copies
   const bool tok_ok = t0 + tl < p.T;
   const int8_t *xrow = p.xq + static_cast<uint64_t>(tok_ok ? t0 + tl : 0) * K;
   auto issue = [&](uint32_t b) {
     const uint32_t st = smem_addr(ring + (b % kStages) * kStageBytes);
-    cp_async16(st + kRawA + tid * 16, grp_row + plane_entry(ZGPU_Q4_0, bpr, b, row & 3), 16);
-    if (tid < 32)
-      cp_async8(st + kScA + tid * 8,
-                p.w + static_cast<uint64_t>((m0 >> 2) + tid) * p.gstride + scale_entry(ZGPU_Q4_0, bpr, b));
+    if (tid < kTileM) cp_async16(st + kRawA + tid * 16, grp_row + plane_entry(ZGPU_Q4_0, bpr, b, row & 3), 16);
+    else if (tid < kTileM + 32)
+      cp_async8(st + kScA + (tid - kTileM) * 8,
+                p.w + static_cast<uint64_t>((m0 >> 2) + tid - kTileM) * p.gstride + scale_entry(ZGPU_Q4_0, bpr, b));
     cp_async16(st + kTileB + core_off(tl, th), xrow + 32 * b + 16 * th, tok_ok ? 16u : 0u);
     if (tid < kTileN) {
       const bool ok = t0 + tid < p.T;
       cp_async4(st + kScB + tid * 4, p.xs + static_cast<uint64_t>(ok ? t0 + tid : 0) * bpr + b, ok ? 4u : 0u);
     }
   };
+  // The ring runs kStages - 2 blocks ahead: prepare(c) refills the stage of
+  // block c - 2, whose MMA and epilogue are complete by then (block c - 1's
+  // MMA and block c - 1's epilogue may still use theirs).
 #pragma unroll
-  for (uint32_t s = 0; s < kStages - 1; ++s) {
+  for (uint32_t s = 0; s < kStages - 2; ++s) {
     if (s < bpr) issue(s);
     cp_async_commit();
   }
 
-  float acc[kTileN];
+  constexpr int kCols = 64;   // accumulator columns (tokens) per thread
+  const uint32_t chalf = warp >> 2;
+  float acc[kCols];
 #pragma unroll
-  for (int j = 0; j < static_cast<int>(kTileN); ++j) acc[j] = 0.f;
-  const uint32_t idesc = kIdesc;
-  const uint64_t adesc = umma_desc(smem_addr(tileA), 128, 256);
-  bool ok = true;
-  for (uint32_t b = 0; b < bpr; ++b) {
-    if (b + kStages - 1 < bpr) issue(b + kStages - 1);
+  for (int j = 0; j < kCols; ++j) acc[j] = 0.f;
+
+  // Stage b's data is complete (all threads' copies), then row tid's nibbles
+  // become int8 (n - 8) in A buffer b % 2; returns this row's scale d_w.
+  auto prepare = [&](uint32_t b) -> float {
+    if (b + kStages - 2 < bpr) issue(b + kStages - 2);
     cp_async_commit();
-    cp_async_wait<kStages - 1>();   // this thread's copies of block b have landed
-    __syncthreads();                // ... and everyone's
-    uint8_t *st = ring + (b % kStages) * kStageBytes;
-    // A: row tid's nibbles -> int8 (n - 8) in the canonical layout
-    {
-      const uint4 q = *reinterpret_cast<const uint4 *>(st + kRawA + tid * 16);
-      uint4 lo, hi;
-      lo.x = nib_to_s8(q.x & 0x0F0F0F0Fu);
-      lo.y = nib_to_s8(q.y & 0x0F0F0F0Fu);
-      lo.z = nib_to_s8(q.z & 0x0F0F0F0Fu);
-      lo.w = nib_to_s8(q.w & 0x0F0F0F0Fu);
-      hi.x = nib_to_s8((q.x >> 4) & 0x0F0F0F0Fu);
-      hi.y = nib_to_s8((q.y >> 4) & 0x0F0F0F0Fu);
-      hi.z = nib_to_s8((q.z >> 4) & 0x0F0F0F0Fu);
-      hi.w = nib_to_s8((q.w >> 4) & 0x0F0F0F0Fu);
-      *reinterpret_cast<uint4 *>(tileA + core_off(tid, 0)) = lo;
-      *reinterpret_cast<uint4 *>(tileA + core_off(tid, 1)) = hi;
+    cp_async_wait<kStages - 2>();   // this thread's copies of block b have landed
+    __syncthreads();                // ... and everyone's; A buffer b % 2 is free (its MMA completed)
+    const uint8_t *st = ring + (b % kStages) * kStageBytes;
+    uint8_t *ta = tileA[b & 1];
+    const uint16_t hw = *reinterpret_cast<const uint16_t *>(st + kScA + (arow >> 2) * 8 + (arow & 3) * 2);
+    if (tid >= kTileM) {
+      fence_proxy_async_smem();
+      return h2f(hw);
     }
-    const uint16_t hw = *reinterpret_cast<const uint16_t *>(st + kScA + (tid >> 2) * 8 + (tid & 3) * 2);
-    const float dw = h2f(hw);
+    const uint4 q = *reinterpret_cast<const uint4 *>(st + kRawA + tid * 16);
+    uint4 lo, hi;
+    lo.x = nib_to_s8(q.x & 0x0F0F0F0Fu);
+    lo.y = nib_to_s8(q.y & 0x0F0F0F0Fu);
+    lo.z = nib_to_s8(q.z & 0x0F0F0F0Fu);
+    lo.w = nib_to_s8(q.w & 0x0F0F0F0Fu);
+    hi.x = nib_to_s8((q.x >> 4) & 0x0F0F0F0Fu);
+    hi.y = nib_to_s8((q.y >> 4) & 0x0F0F0F0Fu);
+    hi.z = nib_to_s8((q.z >> 4) & 0x0F0F0F0Fu);
+    hi.w = nib_to_s8((q.w >> 4) & 0x0F0F0F0Fu);
+    *reinterpret_cast<uint4 *>(ta + core_off(tid, 0)) = lo;
+    *reinterpret_cast<uint4 *>(ta + core_off(tid, 1)) = hi;
     fence_proxy_async_smem();   // generic-proxy writes of A and B -> visible to the tensor core
-    __syncthreads();
+    return h2f(hw);
+  };
+  // thread 0: MMA of block b into accumulator b % 2, committed to mbar[b % 2]
+  auto mma = [&](uint32_t b) {
     if (tid == 0) {
       tc_fence_after();
-      umma_i8(tmem, adesc, umma_desc(smem_addr(st + kTileB), 128, 256), idesc, 0u);
-      umma_commit(smem_addr(&mbar));
+      const uint8_t *st = ring + (b % kStages) * kStageBytes;
+      umma_i8(tmem + (b & 1) * kTileN, umma_desc(smem_addr(tileA[b & 1]), 128, 256),
+              umma_desc(smem_addr(st + kTileB), 128, 256), kIdesc, 0u);
+      umma_commit(smem_addr(&mbar[b & 1]));
     }
-    if (ok && !mbar_wait(smem_addr(&mbar), b & 1, p.status)) ok = false;
+  };
+
+  // Software pipeline: block b+1 is prepared and its MMA issued before block
+  // b's accumulator is read back and scaled, so the tensor core and the
+  // copies run under the epilogue's arithmetic.  Two A buffers and two TMEM
+  // accumulators; a buffer is reused two blocks later, after the barrier in
+  // prepare() that follows everyone's reads of it.
+  bool ok = true;
+  float dw_cur = prepare(0);
+  __syncthreads();
+  mma(0);
+  for (uint32_t b = 0; b < bpr; ++b) {
+    float dw_next = 0.f;
+    if (b + 1 < bpr) {
+      dw_next = prepare(b + 1);
+      __syncthreads();
+      mma(b + 1);
+    }
+    if (ok && !mbar_wait(smem_addr(&mbar[b & 1]), (b >> 1) & 1, p.status)) ok = false;
     tc_fence_after();
-    uint32_t v0[32], v1[32];
-    const uint32_t taddr = tmem + ((warp * 32u) << 16);
-    tmem_ld32(taddr, v0);
-    tmem_ld32(taddr + 32, v1);
-    tmem_ld_wait();
-    const float *dx = reinterpret_cast<const float *>(st + kScB);
+    const uint32_t taddr = tmem + (((warp & 3) * 32u) << 16) + (b & 1) * kTileN + chalf * kCols;
+    const float4 *dx4 =
+        reinterpret_cast<const float4 *>(ring + (b % kStages) * kStageBytes + kScB) + chalf * (kCols / 4);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      acc[j] = __fadd_rn(acc[j], __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(v0[j])), dw), dx[j]));
-      acc[32 + j] =
-          __fadd_rn(acc[32 + j], __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(v1[j])), dw), dx[32 + j]));
+    for (int h = 0; h < 2; ++h) {
+      uint32_t v[32];
+      tmem_ld32(taddr + 32 * h, v);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 d4 = dx4[8 * h + j4];
+        const float dxv[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int j = 32 * h + 4 * j4 + k;
+          acc[j] = __fadd_rn(acc[j], __fmul_rn(__fmul_rn(small_i2f(v[4 * j4 + k]), dw_cur), dxv[k]));
+        }
+      }
     }
     tc_fence_before();
-    // the next iteration's first barrier orders these TMEM reads and the
-    // reads of this stage before the next MMA and the stage's refill
+    dw_cur = dw_next;
   }
   cp_async_wait<0>();
 #pragma unroll
-  for (int j = 0; j < static_cast<int>(kTileN); ++j)
-    if (t0 + j < p.T) p.y[static_cast<uint64_t>(t0 + j) * p.ldy + row] = ok ? acc[j] : __uint_as_float(0x7fc00000u);
+  for (int j = 0; j < kCols; ++j) {
+    const uint32_t t = t0 + chalf * kCols + j;
+    if (t < p.T) p.y[static_cast<uint64_t>(t) * p.ldy + row] = ok ? acc[j] : __uint_as_float(0x7fc00000u);
+  }
   __syncthreads();
   tc_fence_after();
   if (warp == 0)
