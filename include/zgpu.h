@@ -275,6 +275,18 @@ zgpu_status zgpu_generate_greedy(zgpu_model *m, zgpu_kv *kv, const uint32_t *pro
                                  uint32_t n_prompt, uint32_t n_gen, uint32_t *tokens_out,
                                  float *logits_out);
 
+/* Prompt prefill on the token-parallel path (no counterpart in the
+ * reference, which runs forward_single_token per prompt token,
+ * inference.rs:1188-1320): each layer's projections are batched Q4_0 x Q8_0
+ * matmuls over all n tokens on the tensor cores (tcgen05 int8), attention is
+ * causal over the prompt.  Writes cache positions [0, n) and returns the
+ * LM-head argmax after the last token (logits_out, nullable: vocab_padded
+ * floats).  Matmul inputs are quantised to Q8_0, so results agree with the
+ * per-token path to that rounding.  Requires hidden, q+2kv and 2*ffn to be
+ * multiples of 128.  zgpu_perf_snapshot's prefill_ms gives the device time. */
+zgpu_status zgpu_prefill(zgpu_model *m, zgpu_kv *kv, const uint32_t *tokens, uint32_t n,
+                         uint32_t *token_out, float *logits_out);
+
 /* Per-kernel-class counters, mirroring Avx512PerfCounters
  * (inference_avx512.rs:274-330): calls and device milliseconds of the last
  * zgpu_generate_greedy decode phase. */

@@ -1,0 +1,76 @@
+"""Token-parallel prompt prefill (zgpu_prefill) against the reference's
+per-token path (the oracle runs forward_single_token once per prompt token).
+
+The prefill's projections run on the tcgen05 int8 path with Q8_0-quantised
+activations (each batched matmul is bit-exact with the Q4_0 x Q8_0 product,
+tests/test_gpu_mma.py), so the KV cache and logits differ from the f32
+per-token path by that quantisation.  Bars: logits within the north-star
+1e-2 relative L2, the same next token where the oracle's top-1/top-2 margin
+is clear, KV cache within 1e-2 relative L2 per layer.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+import zero_b200 as zb
+from zero_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+
+CASES = [
+    (synth.small_config(n_layers=2, hidden=256, ffn=512, n_q=4, n_kv=2, vocab=512), 24),
+    (synth.small_config(n_layers=3, hidden=512, ffn=1024, n_q=8, n_kv=2, vocab=1024), 300),
+]
+
+
+def top2_gap(v):
+    s = np.sort(v)
+    return float(s[-1] - s[-2])
+
+
+def check_prefill(cfg, n, seed, max_tokens):
+    ctx = zb.Context()
+    w = synth.qwen3_weights(cfg, seed=seed, norm_sigma=0.1)
+    m = zb.Qwen3Model(ctx, cfg, w)
+    prompt = synth.prompt_ids(cfg, n, seed=seed)
+    kv = m.new_kv(max_tokens)
+    tok, logits = m.prefill(kv, prompt)
+    assert m.perf()["prefill_ms"] > 0
+    r = O.OracleRun(cfg, w, max_tokens, order=O.ORDER_AVX512)
+    for i, t in enumerate(prompt):
+        r.forward(int(t), i)
+    rc, rtok, rlog = r.lm_head()
+    assert rc == 0
+    err = rel_l2(logits, rlog)
+    ref_kv = r.kv().reshape(cfg.n_layers, 2, max_tokens, cfg.kv_dim)
+    kv_err = 0.0
+    for layer in range(cfg.n_layers):
+        k, v = kv.read(layer, n)
+        kv_err = max(kv_err, rel_l2(k, ref_kv[layer, 0, :n].ravel()), rel_l2(v, ref_kv[layer, 1, :n].ravel()))
+    print(f"{cfg.name} n={n}: logits rel L2 {err:.2e}, kv rel L2 {kv_err:.2e}, tok {tok} vs {rtok}, "
+          f"margin {top2_gap(rlog):.3e}")
+    assert err < 1e-2, err
+    assert kv_err < 1e-2, kv_err
+    if top2_gap(rlog) > 20 * err * float(np.abs(rlog).max()):
+        assert tok == rtok
+    kv.close()
+    m.close()
+    ctx.close()
+    return err
+
+
+@pytest.mark.parametrize("cfg,n", CASES, ids=[f"{c.name}-n{n}" for c, n in CASES])
+def test_prefill_matches_per_token_path(cfg, n):
+    check_prefill(cfg, n, seed=41, max_tokens=n + 8)
+
+
+def test_prefill_config0_full_size():
+    """BASELINE config 0 weights (28 layers, hidden 2048, vocab 151936), 128-token prompt."""
+    check_prefill(synth.QWEN3_1_7B, 128, seed=0, max_tokens=160)

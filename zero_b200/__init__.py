@@ -295,6 +295,16 @@ class Qwen3Model:
                                                  _ptr(logits) if want_logits else None))
         return toks, logits
 
+    def prefill(self, kv: KvCache, tokens, want_logits: bool = True):
+        """Token-parallel prompt prefill on the tensor cores (zgpu_prefill):
+        fills cache positions [0, n) and returns (next token, logits)."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        tok = C.c_uint32()
+        logits = np.empty(self.cfg.vocab_padded, np.float32) if want_logits else None
+        self.ctx._check(LIB.zgpu_prefill(self.h, kv.h, _ptr(t), t.size, C.byref(tok),
+                                         _ptr(logits) if want_logits else None))
+        return tok.value, logits
+
     def perf(self) -> dict:
         p = ZgpuPerf()
         self.ctx._check(LIB.zgpu_perf_snapshot(self.h, C.byref(p)))

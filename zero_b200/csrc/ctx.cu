@@ -90,6 +90,7 @@ zgpu_status zgpu_init(const zgpu_opts *opts, zgpu_ctx **out) {
       zgpu::gemv_setup() != cudaSuccess || zgpu::attention_setup() != cudaSuccess ||
       zgpu::ops_setup() != cudaSuccess || zgpu::step_setup() != cudaSuccess ||
       zgpu::moe_setup() != cudaSuccess || zgpu::mla_setup() != cudaSuccess ||
+      zgpu::prefill_setup() != cudaSuccess ||
       cudaMalloc(&ctx->d_route_counter, sizeof(uint32_t)) != cudaSuccess ||
       cudaMemset(ctx->d_route_counter, 0, sizeof(uint32_t)) != cudaSuccess) {
     delete ctx;

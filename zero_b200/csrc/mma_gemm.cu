@@ -278,7 +278,11 @@ __global__ void __launch_bounds__(kGemmThreads, 2) q4q8_mma_kernel(const MmaGemm
 #pragma unroll
   for (int j = 0; j < kCols; ++j) {
     const uint32_t t = t0 + chalf * kCols + j;
-    if (t < p.T) p.y[static_cast<uint64_t>(t) * p.ldy + row] = ok ? acc[j] : __uint_as_float(0x7fc00000u);
+    if (t < p.T) {
+      float *dst = p.y + static_cast<uint64_t>(t) * p.ldy + row;
+      const float v = ok ? acc[j] : __uint_as_float(0x7fc00000u);
+      *dst = p.resadd ? __fadd_rn(*dst, v) : v;
+    }
   }
   __syncthreads();
   tc_fence_after();

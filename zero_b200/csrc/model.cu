@@ -12,6 +12,7 @@
 // weight prefetch (TMA into shared memory) starts while its predecessor
 // drains; the whole step is captured once into a CUDA graph whose replays
 // read the token and position from device memory.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <new>
@@ -69,6 +70,9 @@ struct zgpu_model {
   unsigned long long *tv[kStepBufs] = {};
   uint32_t ver[kStepBufs] = {};
   bool last_fwd_persistent = false; // the path the last forward used (the LM head follows it)
+  // token-parallel prefill scratch (grown on demand)
+  uint8_t *d_pf = nullptr;
+  size_t pf_cap = 0;
 };
 
 // Status block of a step: copy back (synchronising the stream), clear it
@@ -572,6 +576,7 @@ zgpu_status zgpu_kv_read(zgpu_kv *kv, uint32_t layer, uint32_t token_count, floa
 }
 
 void zgpu_qwen3_destroy(zgpu_model *m) {
+  if (m) cudaFree(m->d_pf);
   if (!m) return;
   cudaSetDevice(m->ctx->device);
   cudaStreamSynchronize(m->ctx->stream);
@@ -934,6 +939,126 @@ zgpu_status zgpu_perf_snapshot(const zgpu_model *m, zgpu_perf *out) {
   if (!m || !out) return ZGPU_ERR_INVALID_ARG;
   *out = m->perf;
   return ZGPU_OK;
+}
+
+}  // extern "C"
+
+extern "C" {
+
+// Prompt prefill on the token-parallel path: every projection of a layer is
+// one batched Q4_0 x Q8_0 matmul over all prompt tokens on the tensor cores
+// (mma_gemm.cu), attention is causal over the prompt (prefill.cu).  The
+// reference runs forward_single_token once per prompt token
+// (inference.rs:1188-1320) with f32 activations; this path quantises the
+// matmul inputs to Q8_0, so its KV cache and logits agree to that rounding,
+// not bit for bit.  Fills cache positions [0, n) and returns the LM-head
+// argmax after the last prompt token (lm_head.rs:98-166).
+zgpu_status zgpu_prefill(zgpu_model *m, zgpu_kv *kv, const uint32_t *tokens, uint32_t n, uint32_t *token_out,
+                         float *logits_out) {
+  if (!m || !kv || !tokens || !token_out || n == 0) return ZGPU_ERR_INVALID_ARG;
+  zgpu_ctx *ctx = m->ctx;
+  cudaSetDevice(ctx->device);
+  const zgpu_qwen3_desc &d = m->desc;
+  zgpu_status st = prepare_kv(m, kv);
+  if (st) return st;
+  if (n > kv->max_tokens) return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "prompt longer than the cache");
+  for (uint32_t i = 0; i < n; ++i)
+    if (tokens[i] >= d.vocab_padded) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "prompt id beyond the vocab");
+  const uint32_t H = d.hidden, F = d.ffn, QD = m->q_dim, KVD = m->kv_dim, QKV = QD + 2 * KVD;
+  if (H % 128 || QKV % 128 || (2 * F) % 128 || QD % 32 || F % 32)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "prefill: projection rows must be multiples of 128");
+  // scratch: tokens | hidden [n][H] | qkv [n][QKV] | qrot [n][QD] | attn [n][QD] | gu [n][2F] | act [n][F]
+  //          | q8 [n][maxK] int8 | d8 [n][maxK/32] f32
+  const size_t N = n, maxk = std::max(std::max(H, QD), F);
+  auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
+  const size_t o_tok = 0, o_hid = al(N * 4), o_qkv = o_hid + al(N * H * 4), o_qr = o_qkv + al(N * QKV * 4),
+               o_at = o_qr + al(N * QD * 4), o_gu = o_at + al(N * QD * 4), o_act = o_gu + al(N * 2 * F * 4),
+               o_q8 = o_act + al(N * F * 4), o_d8 = o_q8 + al(N * maxk), total = o_d8 + al(N * (maxk / 32) * 4);
+  if (total > m->pf_cap) {
+    cudaFree(m->d_pf);
+    m->d_pf = nullptr;
+    m->pf_cap = 0;
+    cudaError_t e = cudaMalloc(&m->d_pf, total);
+    if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "prefill scratch");
+    m->pf_cap = total;
+  }
+  uint8_t *B = m->d_pf;
+  uint32_t *d_tok = reinterpret_cast<uint32_t *>(B + o_tok);
+  float *hid = reinterpret_cast<float *>(B + o_hid), *qkv = reinterpret_cast<float *>(B + o_qkv),
+        *qr = reinterpret_cast<float *>(B + o_qr), *at = reinterpret_cast<float *>(B + o_at),
+        *gu = reinterpret_cast<float *>(B + o_gu), *act = reinterpret_cast<float *>(B + o_act);
+  int8_t *q8 = reinterpret_cast<int8_t *>(B + o_q8);
+  float *d8 = reinterpret_cast<float *>(B + o_d8);
+  cudaStream_t s = ctx->stream;
+  uint32_t launches = 0;
+  auto gemm = [&](const uint8_t *w, uint64_t gstride, uint32_t rows, uint32_t in_dim, float *y, bool resadd) {
+    MmaGemmParams p = {};
+    p.w = w;
+    p.gstride = gstride;
+    p.rows = rows;
+    p.bpr = in_dim / 32;
+    p.T = n;
+    p.ldy = rows;
+    p.xq = q8;
+    p.xs = d8;
+    p.y = y;
+    p.status = m->d_status;
+    p.resadd = resadd ? 1u : 0u;
+    ++launches;
+    return launch_q4q8_mma(p, s);
+  };
+  cudaError_t e = cudaMemcpyAsync(d_tok, tokens, N * 4, cudaMemcpyHostToDevice, s);
+  cudaEventRecord(m->ev[0], s);
+  if (e == cudaSuccess)
+    e = launch_rows_embed(m->emb->d, m->emb->gstride, m->emb->quant, H, static_cast<uint32_t>(m->emb->rows), d_tok,
+                          n, hid, m->d_status, s), ++launches;
+  const float scale = 1.0f / sqrtf(static_cast<float>(d.head_dim));
+  for (uint32_t l = 0; l < d.n_layers && e == cudaSuccess; ++l) {
+    float *kvl = kv->d + static_cast<size_t>(l) * 2 * kv->block;
+    if ((e = launch_rows_rmsnorm_quant(hid, norm_attn(m, l), d.rms_eps, n, H, q8, d8, m->d_status, s))) break;
+    if ((e = gemm(m->qkv[l], m->gs_h, QKV, H, qkv, false))) break;
+    if ((e = launch_qk_rope_kv(qkv, norm_q(m, l), norm_k(m, l), m->d_inv_freqs, kvl, kv->block, d.n_q_heads,
+                               d.n_kv_heads, 0, n, d.rms_eps, qr, s)))
+      break;
+    if ((e = launch_causal_attn(qr, kvl, kv->block, d.n_q_heads, d.n_kv_heads, 0, n, scale, at, m->d_status, s)))
+      break;
+    if ((e = launch_quantize_q8_0_planar(at, q8, d8, N * QD, m->d_status, s))) break;
+    if ((e = gemm(m->o[l]->d, m->o[l]->gstride, H, QD, hid, true))) break;
+    if ((e = launch_rows_rmsnorm_quant(hid, norm_ffn(m, l), d.rms_eps, n, H, q8, d8, m->d_status, s))) break;
+    if ((e = gemm(m->gateup[l], m->gs_h, 2 * F, H, gu, false))) break;
+    if ((e = launch_swiglu_rows(gu, act, n, F, s))) break;
+    if ((e = launch_quantize_q8_0_planar(act, q8, d8, N * F, m->d_status, s))) break;
+    if ((e = gemm(m->down[l]->d, m->down[l]->gstride, H, F, hid, true))) break;
+    launches += 7;
+  }
+  cudaEventRecord(m->ev[1], s);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "prefill");
+  // LM head on the last prompt token's hidden state
+  cudaError_t e2 = grow(&m->d_prompt, &m->prompt_cap, 1);
+  if (e2 == cudaSuccess) e2 = grow(&m->d_tokens, &m->tokens_cap, 1);
+  if (e2 != cudaSuccess) return zgpu_cuda_fail(ctx, e2, "state buffers");
+  if ((st = set_state(m, 1, n - 1, d.vocab_real, 1))) return st;
+  e = cudaMemcpyAsync(m->d_hidden, hid + N * H - H, H * 4, cudaMemcpyDeviceToDevice, s);
+  if (e == cudaSuccess) e = enqueue_lm_head(m, &launches);
+  m->last_fwd_persistent = false;
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "prefill lm head");
+  if (logits_out)
+    if ((e = cudaMemcpyAsync(logits_out, m->d_logits, static_cast<size_t>(d.vocab_padded) * 4,
+                             cudaMemcpyDeviceToHost, s)) != cudaSuccess)
+      return zgpu_cuda_fail(ctx, e, "logits d2h");
+  if ((e = cudaMemcpyAsync(token_out, m->d_tokens, 4, cudaMemcpyDeviceToHost, s)) != cudaSuccess)
+    return zgpu_cuda_fail(ctx, e, "token d2h");
+  uint32_t sw = 0;
+  if ((st = read_status(m, &sw))) return st;
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, m->ev[0], m->ev[1]);
+  m->perf.prefill_ms = ms;
+  m->perf.kernel_launches = launches;
+  m->perf.steps = 0;
+  m->perf.decode_ms = 0;
+  m->perf.decode_launches = 0;
+  ctx->launches += launches;
+  return map_status(ctx, sw);
 }
 
 }  // extern "C"

@@ -93,8 +93,23 @@ struct MmaGemmParams {
   const float *xs;
   float *y;
   uint32_t *status;
+  uint32_t resadd;          // 0: y = result; 1: y = y + result (residual add)
 };
 cudaError_t launch_q4q8_mma(const MmaGemmParams &p, cudaStream_t s);
+
+// Token-parallel prefill kernels (prefill.cu).
+cudaError_t prefill_setup();
+cudaError_t launch_rows_rmsnorm_quant(const float *x, const float *g, float eps, uint32_t T, uint32_t n, int8_t *q,
+                                      float *d, uint32_t *status, cudaStream_t s);
+cudaError_t launch_rows_embed(const uint8_t *emb, uint64_t gstride, uint32_t quant, uint32_t hidden, uint32_t vocab,
+                              const uint32_t *tokens, uint32_t T, float *out, uint32_t *status, cudaStream_t s);
+cudaError_t launch_qk_rope_kv(const float *qkv, const float *q_norm, const float *k_norm, const float *inv_freqs,
+                              float *kv_layer, uint64_t kv_block, uint32_t n_q, uint32_t n_kv, uint32_t pos0,
+                              uint32_t T, float eps, float *q_out, cudaStream_t s);
+cudaError_t launch_causal_attn(const float *q, const float *kv_layer, uint64_t kv_block, uint32_t n_q, uint32_t n_kv,
+                               uint32_t pos0, uint32_t T, float scale, float *out, uint32_t *status,
+                               cudaStream_t s);
+cudaError_t launch_swiglu_rows(const float *y, float *act, uint32_t T, uint32_t ffn, cudaStream_t s);
 cudaError_t launch_quantize_q8_0_planar(const float *x, int8_t *q, float *d, uint64_t n, uint32_t *status,
                                         cudaStream_t s);
 

@@ -1,0 +1,304 @@
+// prefill.cu — the token-parallel kernels of a Qwen3 prompt prefill: all
+// prompt tokens go through a layer at once, so the projections are batched
+// matmuls on the tensor cores (mma_gemm.cu) and the rest are these row-wise
+// kernels.  The reference has no prefill of its own: it runs
+// forward_single_token once per prompt token (inference.rs:1188-1320); this
+// path produces the same KV cache and LM-head token to the tolerance that the
+// Q8_0 activation quantisation allows.
+//
+//   rows_embed        embed_lookup_dispatch (forward_pass.rs:311-370) per token
+//   rows_rmsnorm_quant rmsnorm (ops.rs:29-52) of each row, then the Q8_0
+//                     activation rule (the planar form the matmul reads)
+//   qk_rope_kv        per token: QK RMSNorm + RoPE of every head (the
+//                     reference's sincos polynomial, trig.rs:60-127) and the
+//                     KV-cache append of k and v (kv_cache.rs:139)
+//   causal_attn       per (query tile, q head): softmax(q.k / sqrt(hd)) . V
+//                     over keys 0..pos, online softmax over 32-key tiles staged
+//                     in shared memory; NumericalInstability as attention.rs:48
+//   swiglu_rows       SiLU(gate) * up on the gate/up matmul's unit layout
+//                     (silu_mul_avx512, activation.rs:115-148)
+#include <cfloat>
+#include <cmath>
+
+#include "attn_body.cuh"
+#include "common.cuh"
+#include "internal.h"
+#include "layout.h"
+#include "ops.h"
+
+namespace zgpu {
+
+namespace {
+
+constexpr uint32_t kRowThreads = 256;
+
+__device__ __forceinline__ float row_block_sum(float v, float *red) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (uint32_t w = 0; w < kRowThreads / 32; ++w) s = __fadd_rn(s, red[w]);
+  return s;
+}
+
+// Q8_0 rule of one 32-element block held by the 32 lanes of a warp.
+__device__ __forceinline__ void quant_block_lane(float v, int8_t *q, float *d, uint32_t lane, uint32_t *status) {
+  if (!(fabsf(v) < INFINITY)) atomicOr(status, ZDEV_ERR_NUMERICAL);
+  double a = fabs(static_cast<double>(v));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) a = fmax(a, __shfl_xor_sync(0xffffffffu, a, off));
+  if (a == 0.0 || !(a < INFINITY)) {
+    q[lane] = 0;
+    if (lane == 0) *d = 0.f;
+    return;
+  }
+  const double dd = a / 127.0;
+  double r = rint(static_cast<double>(v) * (1.0 / dd));
+  r = fmin(fmax(r, -127.0), 127.0);
+  q[lane] = static_cast<int8_t>(r);
+  if (lane == 0) *d = h2f(f64_to_f16_rne(fmin(dd, 65504.0)));
+}
+
+__global__ void __launch_bounds__(kRowThreads) rows_rmsnorm_quant_kernel(const float *x, const float *g, float eps,
+                                                                         uint32_t n, int8_t *q, float *d,
+                                                                         uint32_t *status) {
+  __shared__ float red[kRowThreads / 32];
+  const uint32_t t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const float *xr = x + static_cast<size_t>(t) * n;
+  float ss = 0.f;
+  for (uint32_t i = tid; i < n; i += kRowThreads) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+  const float tot = row_block_sum(ss, red);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(n)), eps)));
+  for (uint32_t b = warp; b < n / 32; b += kRowThreads / 32) {
+    const uint32_t i = 32 * b + lane;
+    const float y = __fmul_rn(__fmul_rn(xr[i], inv), g[i]);
+    quant_block_lane(y, q + static_cast<size_t>(t) * n + 32 * b, d + static_cast<size_t>(t) * (n / 32) + b, lane,
+                     status);
+  }
+}
+
+__global__ void rows_embed_kernel(const uint8_t *emb, uint64_t gstride, uint32_t quant, uint32_t hidden,
+                                  uint32_t vocab, const uint32_t *tokens, float *out, uint32_t *status) {
+  const uint32_t t = blockIdx.x;
+  uint32_t token = tokens[t];
+  if (token >= vocab) {
+    if (threadIdx.x == 0) atomicOr(status, ZDEV_ERR_BOUNDS);
+    token = 0;
+  }
+  const uint8_t *grp = emb + static_cast<uint64_t>(token >> 2) * gstride;
+  const uint32_t l = token & 3, bpr = hidden / 32;
+  for (uint32_t e = threadIdx.x; e < hidden; e += blockDim.x) {
+    const uint32_t b = e >> 5, j = e & 31;
+    const uint8_t *sc = grp + scale_entry(quant, bpr, b) + 2 * l;
+    const float dsc = h2f(static_cast<uint16_t>(sc[0] | (sc[1] << 8)));
+    float v;
+    if (quant == ZGPU_Q8_0) {
+      v = __fmul_rn(static_cast<float>(static_cast<int8_t>(grp[plane_entry(quant, bpr, b, 2 * l + (j >> 4)) + (j & 15)])),
+                    dsc);
+    } else {
+      const uint8_t byte = grp[plane_entry(quant, bpr, b, l) + (j & 15)];
+      v = __fmul_rn(static_cast<float>(((j < 16) ? (byte & 0x0F) : (byte >> 4)) - 8), dsc);
+    }
+    out[static_cast<size_t>(t) * hidden + e] = v;
+  }
+}
+
+// One CTA per token, one warp per head (q heads, then k heads, then v heads).
+__global__ void qk_rope_kv_kernel(const float *qkv, const float *q_norm, const float *k_norm,
+                                  const float *inv_freqs, float *kv_layer, uint64_t kv_block, uint32_t n_q,
+                                  uint32_t n_kv, uint32_t pos0, float eps, float *q_out) {
+  __shared__ float cs[kAttnHd / 2], sn[kAttnHd / 2];
+  const uint32_t t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t pos = pos0 + t;
+  if (threadIdx.x < kAttnHd / 2) {
+    float s, c;
+    ref_sincos(__fmul_rn(static_cast<float>(pos), inv_freqs[threadIdx.x]), &s, &c);
+    cs[threadIdx.x] = c;
+    sn[threadIdx.x] = s;
+  }
+  __syncthreads();
+  const uint32_t qd = n_q * kAttnHd, kvd = n_kv * kAttnHd;
+  const float *row = qkv + static_cast<size_t>(t) * (qd + 2 * kvd);
+  for (uint32_t h = warp; h < n_q + 2 * n_kv; h += blockDim.x >> 5) {
+    const float4 x = reinterpret_cast<const float4 *>(row + h * kAttnHd)[lane];
+    if (h < n_q) {
+      const float4 w = reinterpret_cast<const float4 *>(q_norm)[lane];
+      reinterpret_cast<float4 *>(q_out + static_cast<size_t>(t) * qd + h * kAttnHd)[lane] =
+          attn_norm_rope_lane(x, w, eps, cs, sn, lane);
+    } else if (h < n_q + n_kv) {
+      const float4 w = reinterpret_cast<const float4 *>(k_norm)[lane];
+      reinterpret_cast<float4 *>(kv_layer + static_cast<size_t>(pos) * kvd + (h - n_q) * kAttnHd)[lane] =
+          attn_norm_rope_lane(x, w, eps, cs, sn, lane);
+    } else {
+      reinterpret_cast<float4 *>(kv_layer + kv_block + static_cast<size_t>(pos) * kvd +
+                                 (h - n_q - n_kv) * kAttnHd)[lane] = x;
+    }
+  }
+}
+
+constexpr uint32_t kQTile = 64;            // query rows per CTA
+constexpr uint32_t kKTile = 32;            // keys per staged tile
+constexpr uint32_t kAttnRowsPerWarp = 16;  // 4 warps x 16 rows
+constexpr uint32_t kKPad = kAttnHd + 1;    // padded K rows: lane j reads row j conflict-free
+
+// Causal attention of one (query tile, q head).  Lane j of a warp scores key
+// j of the staged tile against the warp's current query row; the row's
+// running max / sum / output (4 dims per lane) stay in registers for the
+// warp's 16 rows.
+__global__ void __launch_bounds__(128) causal_attn_kernel(const float *q, const float *kv_layer, uint64_t kv_block,
+                                                          uint32_t n_q, uint32_t n_kv, uint32_t pos0, uint32_t T,
+                                                          float scale, float *out, uint32_t *status) {
+  extern __shared__ __align__(16) float asmem[];
+  float *qs = asmem;                                   // [kQTile][128]
+  float *ks = qs + kQTile * kAttnHd;                   // [kKTile][129]
+  float *vs = ks + kKTile * kKPad;                     // [kKTile][128]
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t h = blockIdx.y, kvh = h / (n_q / n_kv);
+  const uint32_t i0 = blockIdx.x * kQTile;             // first query row (token index)
+  const uint32_t qd = n_q * kAttnHd, kvd = n_kv * kAttnHd;
+  const uint32_t rows = min(kQTile, T - i0);
+  for (uint32_t e = tid; e < kQTile * kAttnHd / 4; e += blockDim.x) {
+    const uint32_t r = e / (kAttnHd / 4), c4 = e % (kAttnHd / 4);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < rows) v = reinterpret_cast<const float4 *>(q + static_cast<size_t>(i0 + r) * qd + h * kAttnHd)[c4];
+    reinterpret_cast<float4 *>(qs + r * kAttnHd)[c4] = v;
+  }
+  float m[kAttnRowsPerWarp], l[kAttnRowsPerWarp];
+  float4 o[kAttnRowsPerWarp];
+#pragma unroll
+  for (int r = 0; r < static_cast<int>(kAttnRowsPerWarp); ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+    o[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const uint32_t last_key = pos0 + i0 + rows - 1;      // keys 0..last_key are needed
+  for (uint32_t k0 = 0; k0 <= last_key; k0 += kKTile) {
+    __syncthreads();   // previous tile consumed (and the Q tile written, first time)
+    for (uint32_t e = tid; e < kKTile * kAttnHd / 4; e += blockDim.x) {
+      const uint32_t r = e / (kAttnHd / 4), c4 = e % (kAttnHd / 4);
+      float4 kv4 = make_float4(0.f, 0.f, 0.f, 0.f), vv4 = kv4;
+      if (k0 + r <= last_key) {
+        const size_t off = static_cast<size_t>(k0 + r) * kvd + kvh * kAttnHd;
+        kv4 = reinterpret_cast<const float4 *>(kv_layer + off)[c4];
+        vv4 = reinterpret_cast<const float4 *>(kv_layer + kv_block + off)[c4];
+      }
+      float *kr = ks + r * kKPad + 4 * c4;
+      kr[0] = kv4.x;
+      kr[1] = kv4.y;
+      kr[2] = kv4.z;
+      kr[3] = kv4.w;
+      reinterpret_cast<float4 *>(vs + r * kAttnHd)[c4] = vv4;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int rr = 0; rr < static_cast<int>(kAttnRowsPerWarp); ++rr) {
+      const uint32_t r = warp * kAttnRowsPerWarp + rr;
+      if (r >= rows) break;   // warp-uniform
+      const uint32_t pos_i = pos0 + i0 + r;
+      if (k0 > pos_i) continue;
+      const float *qr = qs + r * kAttnHd;
+      const float *kr = ks + lane * kKPad;
+      float s = 0.f;
+#pragma unroll 8
+      for (uint32_t c = 0; c < kAttnHd; ++c) s = fmaf(qr[c], kr[c], s);
+      s = (k0 + lane <= pos_i) ? __fmul_rn(s, scale) : -INFINITY;
+      float mx = s;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float mn = fmaxf(m[rr], mx);
+      const float corr = (m[rr] == mn) ? 1.0f : expf(m[rr] - mn);
+      const float p = (s == -INFINITY) ? 0.0f : expf(s - mn);
+      float psum = p;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
+      l[rr] = fmaf(l[rr], corr, psum);
+      float4 acc = make_float4(o[rr].x * corr, o[rr].y * corr, o[rr].z * corr, o[rr].w * corr);
+#pragma unroll 8
+      for (uint32_t j = 0; j < kKTile; ++j) {
+        const float pj = __shfl_sync(0xffffffffu, p, j);
+        const float4 v = reinterpret_cast<const float4 *>(vs + j * kAttnHd)[lane];
+        acc.x = fmaf(pj, v.x, acc.x);
+        acc.y = fmaf(pj, v.y, acc.y);
+        acc.z = fmaf(pj, v.z, acc.z);
+        acc.w = fmaf(pj, v.w, acc.w);
+      }
+      m[rr] = mn;
+      o[rr] = acc;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < static_cast<int>(kAttnRowsPerWarp); ++k) {
+    const uint32_t r = warp * kAttnRowsPerWarp + k;
+    if (r >= rows) break;
+    if (!(m[k] > -INFINITY && m[k] < INFINITY) || !(l[k] > 0.f) || !(l[k] < INFINITY)) {
+      if (lane == 0) atomicOr(status, ZDEV_ERR_NUMERICAL);
+    }
+    const float inv = __fdiv_rn(1.0f, l[k]);
+    reinterpret_cast<float4 *>(out + static_cast<size_t>(i0 + r) * qd + h * kAttnHd)[lane] =
+        make_float4(o[k].x * inv, o[k].y * inv, o[k].z * inv, o[k].w * inv);
+  }
+}
+
+// act[t][4u + r] = silu(y[t][8u + r]) * y[t][8u + 4 + r]: the gate/up stream
+// interleaves gate group u and up group u (layout of the fused gate/up).
+__global__ void swiglu_rows_kernel(const float *y, float *act, uint32_t ffn, uint64_t n) {
+  const uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
+  if (i >= n) return;
+  const uint64_t t = i / ffn, f = i % ffn;
+  const uint64_t u = f >> 2, r = f & 3;
+  const float *yr = y + t * 2 * ffn;
+  act[i] = ref_silu_mul(yr[8 * u + r], yr[8 * u + 4 + r]);
+}
+
+}  // namespace
+
+cudaError_t launch_rows_rmsnorm_quant(const float *x, const float *g, float eps, uint32_t T, uint32_t n, int8_t *q,
+                                      float *d, uint32_t *status, cudaStream_t s) {
+  if (n % 32) return cudaErrorInvalidValue;
+  rows_rmsnorm_quant_kernel<<<T, kRowThreads, 0, s>>>(x, g, eps, n, q, d, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rows_embed(const uint8_t *emb, uint64_t gstride, uint32_t quant, uint32_t hidden, uint32_t vocab,
+                              const uint32_t *tokens, uint32_t T, float *out, uint32_t *status, cudaStream_t s) {
+  rows_embed_kernel<<<T, 256, 0, s>>>(emb, gstride, quant, hidden, vocab, tokens, out, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_qk_rope_kv(const float *qkv, const float *q_norm, const float *k_norm, const float *inv_freqs,
+                              float *kv_layer, uint64_t kv_block, uint32_t n_q, uint32_t n_kv, uint32_t pos0,
+                              uint32_t T, float eps, float *q_out, cudaStream_t s) {
+  qk_rope_kv_kernel<<<T, 32 * (n_q + 2 * n_kv) > 1024 ? 1024 : 32 * (n_q + 2 * n_kv), 0, s>>>(
+      qkv, q_norm, k_norm, inv_freqs, kv_layer, kv_block, n_q, n_kv, pos0, eps, q_out);
+  return cudaGetLastError();
+}
+
+size_t causal_attn_smem() {
+  return (static_cast<size_t>(kQTile) * kAttnHd + kKTile * kKPad + kKTile * kAttnHd) * sizeof(float);
+}
+
+cudaError_t prefill_setup() {
+  return cudaFuncSetAttribute(causal_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(causal_attn_smem()));
+}
+
+cudaError_t launch_causal_attn(const float *q, const float *kv_layer, uint64_t kv_block, uint32_t n_q, uint32_t n_kv,
+                               uint32_t pos0, uint32_t T, float scale, float *out, uint32_t *status,
+                               cudaStream_t s) {
+  if (!n_kv || n_q % n_kv) return cudaErrorInvalidValue;
+  dim3 grid((T + kQTile - 1) / kQTile, n_q);
+  causal_attn_kernel<<<grid, 128, causal_attn_smem(), s>>>(q, kv_layer, kv_block, n_q, n_kv, pos0, T, scale, out,
+                                                           status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu_rows(const float *y, float *act, uint32_t T, uint32_t ffn, cudaStream_t s) {
+  const uint64_t n = static_cast<uint64_t>(T) * ffn;
+  swiglu_rows_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(y, act, ffn, n);
+  return cudaGetLastError();
+}
+
+}  // namespace zgpu
