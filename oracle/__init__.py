@@ -75,6 +75,7 @@ def _load() -> C.CDLL:
         "zo_run_forward": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, _f32p]),
         "zo_run_lm_head": (C.c_int, [C.c_void_p, _u32p, _f32p]),
         "zo_run_kv": (_f32p, [C.c_void_p]),
+        "zo_run_set_q8act": (None, [C.c_void_p, C.c_int]),
         "zo_run_generate": (C.c_int, [C.c_void_p, _u32p, C.c_uint32, C.c_uint32, _u32p, _f32p, _f32p]),
         "zo_moe_route_f32": (C.c_int, [_f32p, sz, _f32p, _f32p, sz, sz, _f32p, _u32p, _f32p, C.c_int, C.c_float]),
         "zo_expert_swiglu": (C.c_int, [_f32p, _u8p, _u8p, _u8p, sz, sz, C.c_int, _f32p, _f32p]),
@@ -349,6 +350,10 @@ class OracleRun:
 
     def __del__(self):
         self.close()
+
+    def set_q8act(self, on: bool = True):
+        """Q4_0 matmuls on Q8_0-quantised inputs (the prefill path's arithmetic)."""
+        LIB.zo_run_set_q8act(self._r, 1 if on else 0)
 
     def forward(self, token: int, pos: int) -> np.ndarray:
         h = np.zeros(self.cfg.hidden, np.float32)

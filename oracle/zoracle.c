@@ -691,6 +691,8 @@ int zo_gqa_attention_decode(const float *q, const float *k, const float *v, cons
 struct zo_run {
   const zo_qwen3 *m;
   int order, threads, simd;
+  int q8act;                                   /* Q4_0 matmuls on Q8_0-quantised inputs */
+  uint8_t *xq;                                 /* their Q8_0 blocks */
   uint32_t max_tokens;
   float *kv;                                   /* kv_cache.rs:100 layout */
   float *inv_freqs;
@@ -728,6 +730,11 @@ zo_run *zo_run_create(const zo_qwen3 *m, uint32_t max_tokens, int order, int thr
   r->gate = calloc(F, 4); r->up = calloc(F, 4); r->hmlp = calloc(F, 4);
   r->logits = calloc(m->vocab_padded, 4);
   r->attn_work = calloc((size_t)(m->n_q_heads + m->n_kv_heads + 1) * m->head_dim + max_tokens, 4);
+  {
+    size_t mx = H > F ? H : F;
+    if (qd > mx) mx = qd;
+    r->xq = (uint8_t *)calloc(mx / 32 * 34, 1);
+  }
   zo_rope_ctx(m->rope_theta, m->head_dim / 2, r->inv_freqs);
   if (order == 1) {
     r->x4 = (uint8_t **)calloc((size_t)m->n_layers * 7, sizeof(uint8_t *));
@@ -757,14 +764,24 @@ void zo_run_destroy(zo_run *r) {
   free(r->kv); free(r->inv_freqs); free(r->hidden); free(r->norm); free(r->attn_out);
   free(r->mlp_out); free(r->q); free(r->k); free(r->v); free(r->qo); free(r->ko);
   free(r->score); free(r->head); free(r->concat); free(r->gate); free(r->up); free(r->hmlp);
-  free(r->logits); free(r->attn_work);
+  free(r->logits); free(r->attn_work); free(r->xq);
   free(r);
 }
 
 const float *zo_run_kv(const zo_run *r) { return r->kv; }
 
+/* Q4_0 matmuls of the run take Q8_0-quantised inputs (zo_quantize_row_q8_0,
+ * then zo_linear_q4_0_q8act): the arithmetic of the prefill path, whose
+ * batched matmuls quantise their activations. */
+void zo_run_set_q8act(zo_run *r, int on) { r->q8act = on; }
+
 static void lin(zo_run *r, const float *x, const uint8_t *plain, const uint8_t *x4, float *out,
                 size_t in, size_t outd, int quant) {
+  if (r->q8act && quant == ZO_Q4_0) {
+    zo_quantize_row_q8_0(x, r->xq, in);
+    zo_linear_q4_0_q8act(r->xq, plain, out, in, outd);
+    return;
+  }
   if (r->order == 0) {
     zo_linear_dispatch(x, plain, out, in, outd, quant);
   } else if (quant == ZO_Q4_0) {

@@ -149,6 +149,8 @@ int     zo_run_forward(zo_run *r, uint32_t token, uint32_t pos, float *hidden_ou
 /* lm_head_argmax_dynamic (lm_head.rs:98) / lm_head_argmax_avx512 (inference_avx512.rs:1200). */
 int     zo_run_lm_head(zo_run *r, uint32_t *token_out, float *logits_out);
 const float *zo_run_kv(const zo_run *r);
+/* Q4_0 matmuls on Q8_0-quantised inputs (the prefill path's arithmetic). */
+void    zo_run_set_q8act(zo_run *r, int on);
 /* Prefill the prompt (one forward per token) then n_gen greedy steps. tokens_out
  * receives n_gen ids; margins_out (nullable) the top1-top2 logit gap per step;
  * logits_last (nullable) the logits of the final step. Returns the status of the

@@ -3,10 +3,18 @@ per-token path (the oracle runs forward_single_token once per prompt token).
 
 The prefill's projections run on the tcgen05 int8 path with Q8_0-quantised
 activations (each batched matmul is bit-exact with the Q4_0 x Q8_0 product,
-tests/test_gpu_mma.py), so the KV cache and logits differ from the f32
-per-token path by that quantisation.  Bars: logits within the north-star
-1e-2 relative L2, the same next token where the oracle's top-1/top-2 margin
-is clear, KV cache within 1e-2 relative L2 per layer.
+tests/test_gpu_mma.py).  Two references:
+  * the per-token path with the same Q8_0 activation rounding (oracle run in
+    q8act mode): logits within 5e-3 and the KV cache within 2e-2 relative L2,
+    the same next token.  RMSNorm and attention reduce in another order than
+    the oracle; a last-bit difference flips the Q8_0 rounding of an element
+    now and then (about 1.5e-5 of the elements), which moves that token's
+    projections by ~1e-3 (measured: < 1e-4 at 24 tokens, 6e-4 logits /
+    3.4e-3 cache at 300 tokens);
+  * the reference's f32 per-token path: logits within the north-star 1e-2
+    relative L2 and the same next token where the top-1/top-2 margin is clear.
+    Its KV cache is not compared: Q8_0 rounding of a block that holds an
+    outlier activation moves single cache rows by far more than 1e-2.
 """
 import numpy as np
 import pytest
@@ -49,15 +57,24 @@ def check_prefill(cfg, n, seed, max_tokens):
     rc, rtok, rlog = r.lm_head()
     assert rc == 0
     err = rel_l2(logits, rlog)
-    ref_kv = r.kv().reshape(cfg.n_layers, 2, max_tokens, cfg.kv_dim)
+    rq = O.OracleRun(cfg, w, max_tokens, order=O.ORDER_AVX512)
+    rq.set_q8act(True)
+    for i, t in enumerate(prompt):
+        rq.forward(int(t), i)
+    rcq, qtok, qlog = rq.lm_head()
+    assert rcq == 0
+    errq = rel_l2(logits, qlog)
+    ref_kv = rq.kv().reshape(cfg.n_layers, 2, max_tokens, cfg.kv_dim)
     kv_err = 0.0
     for layer in range(cfg.n_layers):
         k, v = kv.read(layer, n)
         kv_err = max(kv_err, rel_l2(k, ref_kv[layer, 0, :n].ravel()), rel_l2(v, ref_kv[layer, 1, :n].ravel()))
-    print(f"{cfg.name} n={n}: logits rel L2 {err:.2e}, kv rel L2 {kv_err:.2e}, tok {tok} vs {rtok}, "
-          f"margin {top2_gap(rlog):.3e}")
+    print(f"{cfg.name} n={n}: logits vs f32 path {err:.2e}, vs q8 path {errq:.2e}, kv vs q8 path {kv_err:.2e}, "
+          f"tok {tok} / f32 {rtok} / q8 {qtok}, margin {top2_gap(rlog):.3e}")
+    assert errq < 5e-3, errq
+    assert kv_err < 2e-2, kv_err
+    assert tok == qtok
     assert err < 1e-2, err
-    assert kv_err < 1e-2, kv_err
     if top2_gap(rlog) > 20 * err * float(np.abs(rlog).max()):
         assert tok == rtok
     kv.close()
