@@ -62,7 +62,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the per-token C-ABI loop")
     ap.add_argument("--no-roofline", action="store_true", help="skip the standalone GEMV sweep")
-    ap.add_argument("--workload", default="qwen3", choices=["qwen3", "ds2"],
+    ap.add_argument("--workload", default="qwen3", choices=["qwen3", "ds2", "prefill"],
                     help="qwen3: BASELINE config 0 (the headline); ds2: the config-3 DeepSeek2 "
                          "MLA+MoE model, one sequence, as a secondary line")
     ap.add_argument("--context", type=int, default=2048, help="ds2: tokens in the cache before decode")
@@ -91,8 +91,9 @@ def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": d.get("hbm_gbs", 6650.0), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": d.get("hbm_gbs", 6650.0), "bf16_tflops": d.get("bf16_tflops", 1590.0),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
 class ClockSampler:
@@ -311,6 +312,129 @@ def run_ds2(args, rank, world, local):
     ctx.close()
 
 
+PREFILL_METRIC = "prefill tok/s, Qwen3-1.7B-shape Q4_0, 2048-token prompt; int8 tensor-core TOPS"
+PREFILL_LEN = 2048
+
+
+def prefill_gemm_ops(cfg, n: int) -> int:
+    """Integer multiply-adds x 2 of the projection GEMMs of one n-token prefill
+    (QKV, O, gate/up, down per layer; the LM head runs on the last token only)."""
+    per_layer = (cfg.q_dim + 2 * cfg.kv_dim) * cfg.hidden + cfg.hidden * cfg.q_dim \
+        + 2 * cfg.ffn * cfg.hidden + cfg.hidden * cfg.ffn
+    return 2 * n * cfg.n_layers * per_layer
+
+
+def cpu_prefill(cfg, weights, prompt, threads: int):
+    """The reference's prompt loop (forward_single_token per prompt token,
+    inference.rs:1938-1999) on the CPU oracle's AVX-512 path."""
+    import oracle as O
+
+    r = O.OracleRun(cfg, weights, len(prompt) + 2, order=O.ORDER_AVX512, threads=threads)
+    t0 = time.perf_counter()
+    for i, t in enumerate(prompt):
+        r.forward(int(t), i)
+    rc, tok, _ = r.lm_head()
+    dt = time.perf_counter() - t0
+    r.close()
+    return len(prompt) / dt, dt
+
+
+def run_prefill(args, rank, world, local):
+    """BASELINE config 4 at batch 1: a 2048-token seeded prompt through the
+    token-parallel prefill (tcgen05 int8 projections, causal attention writing
+    the KV cache, LM head on the last token).  A step is one whole prefill."""
+    from zero_b200 import synth
+
+    cfg = synth.QWEN3_1_7B
+    n_cpu = 64
+    if args.impl == "reference":
+        if rank == 0:
+            weights = synth.qwen3_weights(cfg, seed=SEED, x4=False)
+            prompt = synth.prompt_ids(cfg, PREFILL_LEN, seed=SEED)
+            cores = physical_cores()
+            tok_s, dt = cpu_prefill(cfg, weights, prompt[:n_cpu], cores)
+            print(json.dumps({
+                "impl": "reference", "metric": PREFILL_METRIC, "value": round(tok_s, 3), "unit": "tok/s",
+                "n_gpus": args.gpus, "steps": 1, "warmup": 0, "ms_per_step": round(1000 * dt, 3),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded random-init .smodel v2 weights)",
+                "config": {"workload": "qwen3-1.7b-shape q4_0 prefill b=1 (BASELINE config 4)",
+                           "prompt": PREFILL_LEN, "parallelism": "cpu threads"},
+                "cpu_baseline": {"value": round(tok_s, 3), "unit": "tok/s", "cores": cores, "kind": "port",
+                                 "sample": f"the first {n_cpu} prompt tokens, one forward_single_token each"},
+                "e2e": {"value": round(tok_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    import torch
+
+    import zero_b200 as zb
+
+    weights = synth.qwen3_weights(cfg, seed=SEED)
+    prompt = synth.prompt_ids(cfg, PREFILL_LEN, seed=SEED)
+    ctx = zb.Context(device=local)
+    model = zb.Qwen3Model(ctx, cfg, weights)
+    kv = model.new_kv(PREFILL_LEN + 8)
+    for _ in range(args.warmup):
+        model.prefill(kv, prompt, want_logits=False)
+    torch.cuda.synchronize()
+    dev_ms, gemm_ms, attn_ms, wall = [], [], [], []
+    with ClockSampler(physical_gpu_index(local)) as clocks:
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            tok, _ = model.prefill(kv, prompt, want_logits=False)
+            wall.append(time.perf_counter() - t0)
+            p = model.perf()
+            dev_ms.append(p["prefill_ms"])
+            gemm_ms.append(p["prefill_gemm_ms"])
+            attn_ms.append(p["prefill_attn_ms"])
+    launches = int(model.perf()["kernel_launches"])
+    tok_s = PREFILL_LEN / (statistics.mean(dev_ms) / 1000.0)
+    e2e_tok_s = PREFILL_LEN * args.steps / sum(wall)
+    ops = prefill_gemm_ops(cfg, PREFILL_LEN)
+    g_ms = statistics.mean(gemm_ms)
+    tops = ops / (g_ms / 1000.0) / 1e12
+    peaks = measured_peaks()
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cores = physical_cores()
+        w_plain = synth.qwen3_weights(cfg, seed=SEED, x4=False)
+        c_tok_s, c_dt = cpu_prefill(cfg, w_plain, prompt[:n_cpu], cores)
+        cpu = {"value": round(c_tok_s, 3), "unit": "tok/s", "cores": cores, "kind": "port",
+               "sample": f"the first {n_cpu} prompt tokens through the AVX-512-order restatement of the "
+                         f"reference's per-token prompt loop, {c_dt:.1f} s"}
+    if rank == 0:
+        line = {
+            "metric": PREFILL_METRIC, "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(statistics.mean(dev_ms), 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> int32 (Q8_0 x Q4_0), f32 elsewhere",
+            "data": "synthetic (seeded random-init .smodel v2 weights, BASELINE config 4)",
+            "config": {"workload": "qwen3-1.7b-shape q4_0 prefill b=1 (BASELINE config 4)",
+                       "prompt": PREFILL_LEN, "batch": 1, "layers": cfg.n_layers,
+                       "l2": "inputs larger than L2 (793 MB of projection weights per prefill)",
+                       "parallelism": "single GPU", "next_token": int(tok),
+                       "gemm_ms": round(g_ms, 3), "attention_ms": round(statistics.mean(attn_ms), 3),
+                       "other_ms": round(statistics.mean(dev_ms) - g_ms - statistics.mean(attn_ms), 3)},
+            "roofline": {"bound": "tensor", "kernel": "q4q8_mma (tcgen05 int8, all projection GEMMs)",
+                         "achieved": round(tops, 1), "peak": round(int8_peak, 1), "unit": "TOPS",
+                         "frac": round(tops / int8_peak, 4),
+                         "peak_source": f"2 x measured bf16 burst ({peaks['source']}): int8 MMA issues at "
+                                        f"twice the bf16 rate",
+                         "traffic": None, "algorithmic_ops": ops,
+                         "avg_launch_us": round(g_ms * 1000 / (4 * cfg.n_layers), 2)},
+            "e2e": {"value": round(e2e_tok_s, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * PREFILL_LEN,
+                    "d2h_bytes_per_step": 8},
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    kv.close()
+    model.close()
+    ctx.close()
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
@@ -320,6 +444,13 @@ def main():
 
             torch.cuda.set_device(local)
         run_ds2(args, rank, world, local)
+        return
+    if args.workload == "prefill":
+        if args.impl != "reference":
+            import torch
+
+            torch.cuda.set_device(local)
+        run_prefill(args, rank, world, local)
         return
     if args.impl == "reference":
         run_reference(args, rank)

@@ -191,6 +191,16 @@ zgpu_status zgpu_kv_read(zgpu_kv *kv, uint32_t layer, uint32_t token_count, floa
  * Errors: ZGPU_ERR_KV_LAYER_OUT_OF_RANGE, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE
  * (pos >= max_tokens), ZGPU_ERR_NUMERICAL_INSTABILITY (AttentionError::
  * NumericalInstability).  Synchronous; host buffers. */
+/* The prefill's causal attention over a cache layer: T queries q
+ * [T][n_q_heads*128] (already QK-normed and rotated) at positions pos0 ..
+ * pos0+T-1; query i attends to cached tokens 0..pos0+i with
+ * softmax(q.k/sqrt(hd)) and writes out [T][n_q_heads*128] — the per-token
+ * attention of gqa_attention_single_token_dispatch (attention.rs:278-433)
+ * for a run of prompt tokens, in another f32 summation order.  The keys
+ * must be in the cache (zgpu_kv_store or a prefill).  Errors as
+ * zgpu_gqa_attention_decode.  Synchronous; host buffers. */
+zgpu_status zgpu_causal_attention(zgpu_ctx *ctx, zgpu_kv *kv, uint32_t layer, uint32_t pos0, uint32_t T,
+                                  uint32_t n_q_heads, const float *q, float *out);
 zgpu_status zgpu_gqa_attention_decode(zgpu_ctx *ctx, zgpu_kv *kv, uint32_t layer, uint32_t pos,
                                       uint32_t n_q_heads, const float *qkv, const float *q_norm,
                                       const float *k_norm, float freq_base, float eps, float *out);
@@ -296,6 +306,8 @@ typedef struct zgpu_perf {
   double decode_ms;           /* device time of the decode steps */
   double prefill_ms;
   uint64_t decode_launches;   /* kernel launches of the decode steps alone */
+  double prefill_gemm_ms;     /* zgpu_prefill: device time of the projection GEMMs */
+  double prefill_attn_ms;     /* zgpu_prefill: device time of the causal attention */
 } zgpu_perf;
 zgpu_status zgpu_perf_snapshot(const zgpu_model *m, zgpu_perf *out);
 

@@ -210,6 +210,16 @@ class KvCache:
         self.ctx._check(LIB.zgpu_kv_read(self.h, layer, token_count, _ptr(k), _ptr(v)))
         return k, v
 
+    def causal_attention(self, layer: int, pos0: int, n_q_heads: int, q: np.ndarray) -> np.ndarray:
+        """The prefill's causal attention (zgpu_causal_attention): rotated
+        queries q [T, n_q_heads * head_dim] at positions pos0.. over the cached
+        keys of `layer`; returns [T, n_q_heads * head_dim]."""
+        q = np.ascontiguousarray(q, np.float32)
+        T = q.shape[0]
+        out = np.empty((T, n_q_heads * self.head_dim), np.float32)
+        self.ctx._check(LIB.zgpu_causal_attention(self.ctx.h, self.h, layer, pos0, T, n_q_heads, _ptr(q), _ptr(out)))
+        return out
+
     def gqa_attention_decode(self, layer: int, pos: int, n_q_heads: int, qkv: np.ndarray,
                              q_norm: np.ndarray, k_norm: np.ndarray, freq_base: float,
                              eps: float) -> np.ndarray:
@@ -309,7 +319,8 @@ class Qwen3Model:
         p = ZgpuPerf()
         self.ctx._check(LIB.zgpu_perf_snapshot(self.h, C.byref(p)))
         return {"steps": p.steps, "kernel_launches": p.kernel_launches, "decode_ms": p.decode_ms,
-                "prefill_ms": p.prefill_ms, "decode_launches": p.decode_launches}
+                "prefill_ms": p.prefill_ms, "decode_launches": p.decode_launches,
+                "prefill_gemm_ms": p.prefill_gemm_ms, "prefill_attn_ms": p.prefill_attn_ms}
 
 
 class MlaKvCache:
@@ -415,7 +426,8 @@ class Ds2Model:
         p = ZgpuPerf()
         self.ctx._check(LIB.zgpu_ds2_perf_snapshot(self.h, C.byref(p)))
         return {"steps": p.steps, "kernel_launches": p.kernel_launches, "decode_ms": p.decode_ms,
-                "prefill_ms": p.prefill_ms, "decode_launches": p.decode_launches}
+                "prefill_ms": p.prefill_ms, "decode_launches": p.decode_launches,
+                "prefill_gemm_ms": p.prefill_gemm_ms, "prefill_attn_ms": p.prefill_attn_ms}
 
 
 __all__ = ["Context", "KvCache", "Qwen3Model", "Qwen3Config", "QWEN3_1_7B", "ZgpuError", "synth",

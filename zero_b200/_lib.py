@@ -65,7 +65,8 @@ class ZgpuDs2Desc(C.Structure):
 
 class ZgpuPerf(C.Structure):
     _fields_ = [("steps", _u64), ("kernel_launches", _u64), ("decode_ms", C.c_double),
-                ("prefill_ms", C.c_double), ("decode_launches", _u64)]
+                ("prefill_ms", C.c_double), ("decode_launches", _u64),
+                ("prefill_gemm_ms", C.c_double), ("prefill_attn_ms", C.c_double)]
 
 
 _SIGS = {
@@ -92,6 +93,7 @@ _SIGS = {
     "zgpu_kv_destroy": (None, [_vp]),
     "zgpu_kv_store": (_i32, [_vp, _u32, _u32, _vp, _vp, _u64]),
     "zgpu_kv_read": (_i32, [_vp, _u32, _u32, _vp, _vp]),
+    "zgpu_causal_attention": (_i32, [_vp, _vp, _u32, _u32, _u32, _u32, _vp, _vp]),
     "zgpu_gqa_attention_decode": (_i32, [_vp, _vp, _u32, _u32, _u32, _vp, _vp, _vp, _f, _f, _vp]),
     "zgpu_gqa_attention_decode_device": (_i32, [_vp, _vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _f, _vp,
                                                 _vp]),

@@ -121,6 +121,23 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void *src, uin
       : "memory");
 }
 
+// cp.async copies global -> shared (Ampere form, no mbarrier).  src_bytes <
+// the copy size zero-fills the rest (0: a pure zero fill, src unread).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // L2 policy for weights streamed exactly once per step: evict first, so the
 // KV cache and activations keep their L2 residency.
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {

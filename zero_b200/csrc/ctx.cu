@@ -600,6 +600,28 @@ zgpu_status zgpu_gqa_attention_decode_device(zgpu_ctx *ctx, zgpu_kv *kv, uint32_
                           eps, d_out, stream ? static_cast<cudaStream_t>(stream) : ctx->stream);
 }
 
+zgpu_status zgpu_causal_attention(zgpu_ctx *ctx, zgpu_kv *kv, uint32_t layer, uint32_t pos0, uint32_t T,
+                                  uint32_t n_q_heads, const float *q, float *out) {
+  if (!ctx || !kv || !q || !out || T == 0) return ZGPU_ERR_INVALID_ARG;
+  if (layer >= kv->n_layers) return zgpu_fail(ctx, ZGPU_ERR_KV_LAYER_OUT_OF_RANGE, "layer out of range");
+  if (static_cast<uint64_t>(pos0) + T > kv->max_tokens)
+    return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "query positions beyond the cache");
+  if (kv->head_dim != 128 || !n_q_heads || n_q_heads % kv->n_kv)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "causal attention requires head_dim 128 and n_q a multiple of n_kv");
+  cudaSetDevice(ctx->device);
+  const size_t n = static_cast<size_t>(T) * n_q_heads * kv->head_dim;
+  zgpu_status s = ensure_scratch(ctx, n, n);
+  if (s) return s;
+  ZCHECK(cudaMemcpyAsync(ctx->d_x, q, n * 4, cudaMemcpyHostToDevice, ctx->stream), "h2d q");
+  ZCHECK(zgpu::launch_causal_attn(ctx->d_x, kv->d + static_cast<size_t>(layer) * 2 * kv->block, kv->block, n_q_heads,
+                                  kv->n_kv, pos0, T, 1.0f / sqrtf(static_cast<float>(kv->head_dim)), ctx->d_y,
+                                  ctx->d_status, ctx->stream),
+         "launch_causal_attn");
+  ++ctx->launches;
+  ZCHECK(cudaMemcpyAsync(out, ctx->d_y, n * 4, cudaMemcpyDeviceToHost, ctx->stream), "d2h out");
+  return check_status_word(ctx);
+}
+
 zgpu_status zgpu_gqa_attention_decode(zgpu_ctx *ctx, zgpu_kv *kv, uint32_t layer, uint32_t pos,
                                       uint32_t n_q_heads, const float *qkv, const float *q_norm,
                                       const float *k_norm, float freq_base, float eps, float *out) {

@@ -73,6 +73,7 @@ struct zgpu_model {
   // token-parallel prefill scratch (grown on demand)
   uint8_t *d_pf = nullptr;
   size_t pf_cap = 0;
+  std::vector<cudaEvent_t> pf_ev;   // one pair per timed prefill launch (GEMM / attention)
 };
 
 // Status block of a step: copy back (synchronising the stream), clear it
@@ -602,6 +603,7 @@ void zgpu_qwen3_destroy(zgpu_model *m) {
   cudaFree(m->d_tv);
   for (auto &e : m->ev)
     if (e) cudaEventDestroy(e);
+  for (auto &e : m->pf_ev) cudaEventDestroy(e);
   delete m;
 }
 
@@ -931,6 +933,8 @@ zgpu_status zgpu_generate_greedy(zgpu_model *m, zgpu_kv *kv, const uint32_t *pro
   m->perf.decode_launches = launches - prefill_launches;
   m->perf.prefill_ms = pre;
   m->perf.decode_ms = dec;
+  m->perf.prefill_gemm_ms = 0;
+  m->perf.prefill_attn_ms = 0;
   ctx->launches += launches;
   return map_status(ctx, st);
 }
@@ -991,6 +995,16 @@ zgpu_status zgpu_prefill(zgpu_model *m, zgpu_kv *kv, const uint32_t *tokens, uin
   float *d8 = reinterpret_cast<float *>(B + o_d8);
   cudaStream_t s = ctx->stream;
   uint32_t launches = 0;
+  // an event pair around every GEMM and attention launch: per-class device time
+  const size_t n_ev = static_cast<size_t>(d.n_layers) * 10;
+  while (m->pf_ev.size() < n_ev) {
+    cudaEvent_t ev;
+    cudaError_t ee = cudaEventCreate(&ev);
+    if (ee != cudaSuccess) return zgpu_cuda_fail(ctx, ee, "prefill events");
+    m->pf_ev.push_back(ev);
+  }
+  size_t ev_i = 0;
+  auto mark = [&]() { cudaEventRecord(m->pf_ev[ev_i++], s); };
   auto gemm = [&](const uint8_t *w, uint64_t gstride, uint32_t rows, uint32_t in_dim, float *y, bool resadd) {
     MmaGemmParams p = {};
     p.w = w;
@@ -1005,7 +1019,10 @@ zgpu_status zgpu_prefill(zgpu_model *m, zgpu_kv *kv, const uint32_t *tokens, uin
     p.status = m->d_status;
     p.resadd = resadd ? 1u : 0u;
     ++launches;
-    return launch_q4q8_mma(p, s);
+    mark();
+    cudaError_t ge = launch_q4q8_mma(p, s);
+    mark();
+    return ge;
   };
   cudaError_t e = cudaMemcpyAsync(d_tok, tokens, N * 4, cudaMemcpyHostToDevice, s);
   cudaEventRecord(m->ev[0], s);
@@ -1020,8 +1037,10 @@ zgpu_status zgpu_prefill(zgpu_model *m, zgpu_kv *kv, const uint32_t *tokens, uin
     if ((e = launch_qk_rope_kv(qkv, norm_q(m, l), norm_k(m, l), m->d_inv_freqs, kvl, kv->block, d.n_q_heads,
                                d.n_kv_heads, 0, n, d.rms_eps, qr, s)))
       break;
-    if ((e = launch_causal_attn(qr, kvl, kv->block, d.n_q_heads, d.n_kv_heads, 0, n, scale, at, m->d_status, s)))
-      break;
+    mark();
+    e = launch_causal_attn(qr, kvl, kv->block, d.n_q_heads, d.n_kv_heads, 0, n, scale, at, m->d_status, s);
+    mark();
+    if (e) break;
     if ((e = launch_quantize_q8_0_planar(at, q8, d8, N * QD, m->d_status, s))) break;
     if ((e = gemm(m->o[l]->d, m->o[l]->gstride, H, QD, hid, true))) break;
     if ((e = launch_rows_rmsnorm_quant(hid, norm_ffn(m, l), d.rms_eps, n, H, q8, d8, m->d_status, s))) break;
@@ -1053,6 +1072,18 @@ zgpu_status zgpu_prefill(zgpu_model *m, zgpu_kv *kv, const uint32_t *tokens, uin
   float ms = 0.f;
   cudaEventElapsedTime(&ms, m->ev[0], m->ev[1]);
   m->perf.prefill_ms = ms;
+  // five event pairs per layer, in launch order: QKV GEMM, attention, O, gate/up and down GEMMs
+  double gemm_ms = 0, attn_ms = 0;
+  for (size_t i = 0; i + 1 < ev_i; i += 2) {
+    float t = 0.f;
+    cudaEventElapsedTime(&t, m->pf_ev[i], m->pf_ev[i + 1]);
+    if ((i / 2) % 5 == 1)
+      attn_ms += t;
+    else
+      gemm_ms += t;
+  }
+  m->perf.prefill_gemm_ms = gemm_ms;
+  m->perf.prefill_attn_ms = attn_ms;
   m->perf.kernel_launches = launches;
   m->perf.steps = 0;
   m->perf.decode_ms = 0;

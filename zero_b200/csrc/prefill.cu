@@ -12,9 +12,11 @@
 //   qk_rope_kv        per token: QK RMSNorm + RoPE of every head (the
 //                     reference's sincos polynomial, trig.rs:60-127) and the
 //                     KV-cache append of k and v (kv_cache.rs:139)
-//   causal_attn       per (query tile, q head): softmax(q.k / sqrt(hd)) . V
-//                     over keys 0..pos, online softmax over 32-key tiles staged
-//                     in shared memory; NumericalInstability as attention.rs:48
+//   causal_attn       softmax(q.k / sqrt(hd)) . V over keys 0..pos: the
+//                     register-tiled kernel (a CTA per kv head x 128 query
+//                     rows of its GQA group, 64-key tiles) for power-of-two
+//                     groups, else a warp-per-row kernel over 32-key tiles;
+//                     NumericalInstability as attention.rs:48
 //   swiglu_rows       SiLU(gate) * up on the gate/up matmul's unit layout
 //                     (silu_mul_avx512, activation.rs:115-148)
 #include <cfloat>
@@ -242,6 +244,180 @@ __global__ void __launch_bounds__(128) causal_attn_kernel(const float *q, const 
   }
 }
 
+// Register-tiled causal attention: one CTA per (kv head, 128 query rows),
+// the rows being the G = n_q / n_kv query heads of the group times 128 / G
+// tokens, so the group shares every staged K/V tile.  Keys go in tiles of
+// 64, double-buffered by cp.async.  Thread (rg, cg) of 16 x 16:
+//   S phase   rows 8rg..8rg+7 x keys cg + 16j (j < 4): per 4 dims three
+//             shared loads feed 32 FMAs (the 8 Q rows broadcast, the 4 K
+//             rows conflict-free on the padded stride);
+//   softmax   online, per row: the tile max over the 16 lanes of the row
+//             group (4 shuffles), running max m, partial sum l per thread
+//             (reduced once at the end), O rescaled by exp(m_old - m_new);
+//   PV phase  P^T is written over the consumed K buffer; rows 8rg.. x dims
+//             4cg..4cg+3 and 64+4cg..: per key four shared loads feed 64 FMAs.
+// Query tiles are launched heaviest (latest) first.  f32 throughout, the
+// reference's scaled dot / max-trick softmax (attention.rs:48-84,278-433)
+// in another summation order; NumericalInstability as attention.rs:48.
+constexpr uint32_t kFaRows = 128;
+constexpr uint32_t kFaKeys = 64;
+constexpr uint32_t kFaStride = kAttnHd + 4;   // padded Q / K / P^T rows
+constexpr uint32_t kFaThreads = 256;
+constexpr size_t kFaSmemBytes =
+    (static_cast<size_t>(kFaRows) * kFaStride + 2 * kFaKeys * kFaStride + 2 * kFaKeys * kAttnHd) * sizeof(float);
+static_assert(kFaRows == kFaKeys * 2, "P^T [keys][rows] must fit a K buffer [keys][stride]");
+
+__global__ void __launch_bounds__(kFaThreads, 1)
+    causal_attn_tiled_kernel(const float *q, const float *kv_layer, uint64_t kv_block, uint32_t n_q, uint32_t n_kv,
+                             uint32_t pos0, uint32_t T, float scale, float *out, uint32_t *status) {
+  extern __shared__ __align__(16) float fsm[];
+  float *Qs = fsm;                                   // [kFaRows][kFaStride]
+  float *KP = Qs + kFaRows * kFaStride;              // 2 x [kFaKeys][kFaStride]: K, then P^T
+  float *Vs = KP + 2 * kFaKeys * kFaStride;          // 2 x [kFaKeys][kAttnHd]
+  const uint32_t tid = threadIdx.x, rg = tid >> 4, cg = tid & 15;
+  const uint32_t G = n_q / n_kv, TQ = kFaRows / G;
+  const uint32_t kvh = blockIdx.x;
+  const uint32_t n_qt = (T + TQ - 1) / TQ;
+  const uint32_t i0 = (n_qt - 1 - blockIdx.y) * TQ;  // heaviest query tiles first
+  const uint32_t rows_tok = min(TQ, T - i0);
+  const uint32_t qd = n_q * kAttnHd, kvd = n_kv * kAttnHd;
+  const uint32_t last_key = pos0 + i0 + rows_tok - 1;
+  const uint32_t n_tiles = last_key / kFaKeys + 1;
+
+  for (uint32_t e = tid; e < kFaRows * (kAttnHd / 4); e += kFaThreads) {
+    const uint32_t r = e >> 5, c = e & 31;
+    const uint32_t hl = r / TQ, tk = r % TQ;
+    const bool ok = tk < rows_tok;
+    const float *src = q + static_cast<size_t>(i0 + (ok ? tk : 0u)) * qd + (kvh * G + hl) * kAttnHd + 4 * c;
+    cp_async16(smem_addr(Qs + r * kFaStride + 4 * c), src, ok ? 16u : 0u);
+  }
+  auto load_kv = [&](uint32_t t, uint32_t b) {
+    const uint32_t k0 = t * kFaKeys;
+    float *Kb = KP + b * kFaKeys * kFaStride;
+    float *Vb = Vs + b * kFaKeys * kAttnHd;
+    for (uint32_t e = tid; e < kFaKeys * (kAttnHd / 4); e += kFaThreads) {
+      const uint32_t r = e >> 5, c = e & 31;
+      const bool ok = k0 + r <= last_key;
+      const size_t off = static_cast<size_t>(ok ? k0 + r : 0u) * kvd + kvh * kAttnHd + 4 * c;
+      cp_async16(smem_addr(Kb + r * kFaStride + 4 * c), kv_layer + off, ok ? 16u : 0u);
+      cp_async16(smem_addr(Vb + r * kAttnHd + 4 * c), kv_layer + kv_block + off, ok ? 16u : 0u);
+    }
+  };
+  load_kv(0, 0);
+  cp_async_commit();
+
+  const uint32_t pos_r0 = pos0 + i0 + (rg * 8) % TQ;   // position of row 8rg (TQ is a multiple of 8)
+  float m[8], l[8], o[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) o[i][c] = 0.f;
+  }
+  for (uint32_t t = 0; t < n_tiles; ++t) {
+    const uint32_t b = t & 1, k0 = t * kFaKeys;
+    __syncthreads();                       // tile t-1's P^T and V are consumed
+    if (t + 1 < n_tiles) load_kv(t + 1, b ^ 1u);
+    cp_async_commit();
+    cp_async_wait<1>();                    // tile t (and Q) have landed
+    __syncthreads();
+    float *Kb = KP + b * kFaKeys * kFaStride;
+    const float *Vb = Vs + b * kFaKeys * kAttnHd;
+    float sc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sc[i][j] = 0.f;
+#pragma unroll 2
+    for (uint32_t d4 = 0; d4 < kAttnHd / 4; ++d4) {
+      float4 kk[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) kk[j] = *reinterpret_cast<const float4 *>(Kb + (cg + 16 * j) * kFaStride + 4 * d4);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 qq = *reinterpret_cast<const float4 *>(Qs + (rg * 8 + i) * kFaStride + 4 * d4);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sc[i][j] = fmaf(qq.x, kk[j].x, sc[i][j]);
+          sc[i][j] = fmaf(qq.y, kk[j].y, sc[i][j]);
+          sc[i][j] = fmaf(qq.z, kk[j].z, sc[i][j]);
+          sc[i][j] = fmaf(qq.w, kk[j].w, sc[i][j]);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t pos_i = pos_r0 + i;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float v = (k0 + cg + 16 * j <= pos_i) ? __fmul_rn(sc[i][j], scale) : -INFINITY;
+        sc[i][j] = v;
+        mx = fmaxf(mx, v);
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float mn = fmaxf(m[i], mx);
+      const float corr = (m[i] == mn) ? 1.0f : expf(m[i] - mn);
+      float ps = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float p = (sc[i][j] == -INFINITY) ? 0.0f : expf(sc[i][j] - mn);
+        sc[i][j] = p;
+        ps += p;
+      }
+      l[i] = fmaf(l[i], corr, ps);
+      m[i] = mn;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) o[i][c] *= corr;
+    }
+    __syncthreads();                       // every thread is done reading K of tile t
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float *pr = Kb + (cg + 16 * j) * kFaStride + rg * 8;
+      *reinterpret_cast<float4 *>(pr) = make_float4(sc[0][j], sc[1][j], sc[2][j], sc[3][j]);
+      *reinterpret_cast<float4 *>(pr + 4) = make_float4(sc[4][j], sc[5][j], sc[6][j], sc[7][j]);
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (uint32_t key = 0; key < kFaKeys; ++key) {
+      const float4 p0 = *reinterpret_cast<const float4 *>(Kb + key * kFaStride + rg * 8);
+      const float4 p1 = *reinterpret_cast<const float4 *>(Kb + key * kFaStride + rg * 8 + 4);
+      const float4 v0 = *reinterpret_cast<const float4 *>(Vb + key * kAttnHd + 4 * cg);
+      const float4 v1 = *reinterpret_cast<const float4 *>(Vb + key * kAttnHd + 64 + 4 * cg);
+      const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        o[i][0] = fmaf(pv[i], v0.x, o[i][0]);
+        o[i][1] = fmaf(pv[i], v0.y, o[i][1]);
+        o[i][2] = fmaf(pv[i], v0.z, o[i][2]);
+        o[i][3] = fmaf(pv[i], v0.w, o[i][3]);
+        o[i][4] = fmaf(pv[i], v1.x, o[i][4]);
+        o[i][5] = fmaf(pv[i], v1.y, o[i][5]);
+        o[i][6] = fmaf(pv[i], v1.z, o[i][6]);
+        o[i][7] = fmaf(pv[i], v1.w, o[i][7]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float L = l[i];
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    const uint32_t r = rg * 8 + i, hl = r / TQ, tk = r % TQ;
+    if (tk >= rows_tok) continue;
+    if (!(m[i] > -INFINITY && m[i] < INFINITY) || !(L > 0.f) || !(L < INFINITY)) {
+      if (cg == 0) atomicOr(status, ZDEV_ERR_NUMERICAL);
+    }
+    const float inv = __fdiv_rn(1.0f, L);
+    float *dst = out + static_cast<size_t>(i0 + tk) * qd + (kvh * G + hl) * kAttnHd;
+    *reinterpret_cast<float4 *>(dst + 4 * cg) = make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
+    *reinterpret_cast<float4 *>(dst + 64 + 4 * cg) =
+        make_float4(o[i][4] * inv, o[i][5] * inv, o[i][6] * inv, o[i][7] * inv);
+  }
+}
+
 // act[t][4u + r] = silu(y[t][8u + r]) * y[t][8u + 4 + r]: the gate/up stream
 // interleaves gate group u and up group u (layout of the fused gate/up).
 __global__ void swiglu_rows_kernel(const float *y, float *act, uint32_t ffn, uint64_t n) {
@@ -281,14 +457,26 @@ size_t causal_attn_smem() {
 }
 
 cudaError_t prefill_setup() {
-  return cudaFuncSetAttribute(causal_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(causal_attn_smem()));
+  cudaError_t e = cudaFuncSetAttribute(causal_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(causal_attn_smem()));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(causal_attn_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kFaSmemBytes));
+  return e;
 }
 
 cudaError_t launch_causal_attn(const float *q, const float *kv_layer, uint64_t kv_block, uint32_t n_q, uint32_t n_kv,
                                uint32_t pos0, uint32_t T, float scale, float *out, uint32_t *status,
                                cudaStream_t s) {
-  if (!n_kv || n_q % n_kv) return cudaErrorInvalidValue;
+  if (!n_kv || n_q % n_kv || T == 0) return cudaErrorInvalidValue;
+  const uint32_t G = n_q / n_kv;
+  if (G <= 16 && (G & (G - 1)) == 0) {   // 128 / G query tokens per CTA, a multiple of 8
+    const uint32_t TQ = kFaRows / G;
+    dim3 grid(n_kv, (T + TQ - 1) / TQ);
+    causal_attn_tiled_kernel<<<grid, kFaThreads, kFaSmemBytes, s>>>(q, kv_layer, kv_block, n_q, n_kv, pos0, T, scale,
+                                                                     out, status);
+    return cudaGetLastError();
+  }
   dim3 grid((T + kQTile - 1) / kQTile, n_q);
   causal_attn_kernel<<<grid, 128, causal_attn_smem(), s>>>(q, kv_layer, kv_block, n_q, n_kv, pos0, T, scale, out,
                                                            status);
