@@ -31,6 +31,9 @@ TINY = [
     synth.small_config(n_layers=2, hidden=256, ffn=512, n_q=4, n_kv=2, vocab=512),
     synth.small_config(n_layers=3, hidden=512, ffn=1024, n_q=8, n_kv=2, vocab=1024),   # GQA 4
     synth.small_config(n_layers=2, hidden=1024, ffn=3072, n_q=8, n_kv=8, vocab=2048),  # MHA
+    # BASELINE config 2 widths (Qwen3-8B: hidden 4096, FFN 12288, 32 q / 8 kv heads):
+    # inputs wider than one round of float4s per consumer thread
+    synth.small_config(n_layers=2, hidden=4096, ffn=12288, n_q=32, n_kv=8, vocab=1024),
 ]
 
 

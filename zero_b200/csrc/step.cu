@@ -241,7 +241,8 @@ struct Ctx {
   uint32_t *xsm;
   float *part;
   float *hown;       // this CTA's residual rows
-  uint32_t hrow0;    // first residual row this CTA owns
+  uint32_t hrow0;    // first residual row this CTA owns (in this rank's row slice)
+  uint32_t hrow0g;   // the same row in the whole hidden vector
   uint8_t *ring;
   uint64_t *full, *empty;
   float *red;
@@ -284,121 +285,125 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
   uint32_t u0, u1;
   unit_range(sd.units, &u0, &u1);
 
-  // ---- input: each thread takes its float4s of x once (at most kXRegs of
-  // them), waiting for the expected version, for both the sum of squares
-  // and the digits.
-  constexpr int kXRegs = XR;
-  float4 xr[kXRegs];
+  // ---- input: each thread takes its float4s of x, XR at a time (one round
+  // covers XR * kNC float4s), waiting for the expected version, for both the
+  // sum of squares and the digits.  Within a round all of the thread's words
+  // are polled together, so the wait ends one L2 round trip after the last
+  // of them is published.
   const unsigned long long *xin = sd.tin;
   const uint32_t vin = EMB ? 0u : ver_of(c, sd.in_buf);
-  if (!EMB) {
-    // all of this thread's words are polled together, so the wait ends one
-    // L2 round trip after the last of them is published
-    ulonglong2 raw[kXRegs][2];
-    uint32_t todo = 0;
+  float ss = 0.f;   // RMSNorm: this thread's sum of squares, its float4s in index order
+  for (uint32_t base = 0; base < nf4; base += XR * kNC) {
+    float4 xr[XR];
+    if (!EMB) {
+      ulonglong2 raw[XR][2];
+      uint32_t todo = 0;
 #pragma unroll
-    for (int i = 0; i < kXRegs; ++i) {
-      const uint32_t f = warp * 32 + lane + i * kNC;
-      if (f < nf4) {
-        const ulonglong2 *q = reinterpret_cast<const ulonglong2 *>(xin + 4 * f);
-        raw[i][0] = __ldcg(q);
-        raw[i][1] = __ldcg(q + 1);
-        todo |= 1u << i;
-      } else {
-        raw[i][0] = raw[i][1] = make_ulonglong2(0ull, 0ull);
+      for (int i = 0; i < XR; ++i) {
+        const uint32_t f = base + warp * 32 + lane + i * kNC;
+        if (f < nf4) {
+          const ulonglong2 *q = reinterpret_cast<const ulonglong2 *>(xin + 4 * f);
+          raw[i][0] = __ldcg(q);
+          raw[i][1] = __ldcg(q + 1);
+          todo |= 1u << i;
+        } else {
+          raw[i][0] = raw[i][1] = make_ulonglong2(0ull, 0ull);
+        }
       }
-    }
-    auto ready = [&](const ulonglong2 (&r)[2]) {
-      return static_cast<uint32_t>(r[0].x >> 32) == vin && static_cast<uint32_t>(r[0].y >> 32) == vin &&
-             static_cast<uint32_t>(r[1].x >> 32) == vin && static_cast<uint32_t>(r[1].y >> 32) == vin;
-    };
+      auto ready = [&](const ulonglong2 (&r)[2]) {
+        return static_cast<uint32_t>(r[0].x >> 32) == vin && static_cast<uint32_t>(r[0].y >> 32) == vin &&
+               static_cast<uint32_t>(r[1].x >> 32) == vin && static_cast<uint32_t>(r[1].y >> 32) == vin;
+      };
 #pragma unroll
-    for (int i = 0; i < kXRegs; ++i)
-      if ((todo >> i & 1u) && ready(raw[i])) todo &= ~(1u << i);
-    if (todo) {
-      const uint64_t t0 = globaltimer_ns();
-      while (todo) {
+      for (int i = 0; i < XR; ++i)
+        if ((todo >> i & 1u) && ready(raw[i])) todo &= ~(1u << i);
+      if (todo) {
+        const uint64_t t0 = globaltimer_ns();
+        while (todo) {
 #pragma unroll
-        for (int i = 0; i < kXRegs; ++i) {
-          if (todo >> i & 1u) {
-            const ulonglong2 *q = reinterpret_cast<const ulonglong2 *>(xin + 4 * (warp * 32 + lane + i * kNC));
-            raw[i][0] = __ldcg(q);
-            raw[i][1] = __ldcg(q + 1);
+          for (int i = 0; i < XR; ++i) {
+            if (todo >> i & 1u) {
+              const ulonglong2 *q =
+                  reinterpret_cast<const ulonglong2 *>(xin + 4 * (base + warp * 32 + lane + i * kNC));
+              raw[i][0] = __ldcg(q);
+              raw[i][1] = __ldcg(q + 1);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < XR; ++i)
+            if ((todo >> i & 1u) && ready(raw[i])) todo &= ~(1u << i);
+          if (!todo) break;
+          if (*c.abort || ld_relaxed_u32(&P.bar[1])) {
+            *c.abort = 1;
+            break;
+          }
+          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(P.status, ZDEV_ERR_TIMEOUT);
+            atomicExch(&P.bar[1], 1u);
+            *c.abort = 1;
+            break;
           }
         }
+      }
 #pragma unroll
-        for (int i = 0; i < kXRegs; ++i)
-          if ((todo >> i & 1u) && ready(raw[i])) todo &= ~(1u << i);
-        if (!todo) break;
-        if (*c.abort || ld_relaxed_u32(&P.bar[1])) {
-          *c.abort = 1;
-          break;
-        }
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-          atomicOr(P.status, ZDEV_ERR_TIMEOUT);
-          atomicExch(&P.bar[1], 1u);
-          *c.abort = 1;
-          break;
+      for (int i = 0; i < XR; ++i)
+        xr[i] = make_float4(__uint_as_float(static_cast<uint32_t>(raw[i][0].x)),
+                            __uint_as_float(static_cast<uint32_t>(raw[i][0].y)),
+                            __uint_as_float(static_cast<uint32_t>(raw[i][1].x)),
+                            __uint_as_float(static_cast<uint32_t>(raw[i][1].y)));
+    }
+#pragma unroll
+    for (int i = 0; i < XR; ++i) {
+      const uint32_t f = base + warp * 32 + lane + i * kNC;
+      if (EMB) xr[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (f < nf4) {
+        if (EMB) {
+          xr[i] = embed_f4(P, token, f);
+          // the embedding is the residual base of the rows this CTA owns
+          const float ev[4] = {xr[i].x, xr[i].y, xr[i].z, xr[i].w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t e = 4 * f + k;
+            if (e >= c.hrow0g && e - c.hrow0g < P.hown_rows) c.hown[e - c.hrow0g] = ev[k];
+          }
         }
       }
     }
+    trace(16 + 2 + EPI);
+    // RMSNorm (ops.rs:29-52) as y = inv * (W . (x * g)): the digits are taken
+    // of x * g right away and the scalar inv = 1/sqrt(mean(x^2) + eps) scales
+    // the row sums in the epilogue, so the sum of squares (fixed order: per
+    // thread over its float4s, xor-tree in the warp, warps in order) needs no
+    // barrier of its own: its per-warp parts cross the image barrier below.
+    if (PRO == PRO_RMSNORM) {
 #pragma unroll
-    for (int i = 0; i < kXRegs; ++i)
-      xr[i] = make_float4(__uint_as_float(static_cast<uint32_t>(raw[i][0].x)),
-                          __uint_as_float(static_cast<uint32_t>(raw[i][0].y)),
-                          __uint_as_float(static_cast<uint32_t>(raw[i][1].x)),
-                          __uint_as_float(static_cast<uint32_t>(raw[i][1].y)));
-  }
-#pragma unroll
-  for (int i = 0; i < kXRegs; ++i) {
-    const uint32_t f = warp * 32 + lane + i * kNC;
-    if (EMB) xr[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (f < nf4) {
-      if (EMB) {
-        xr[i] = embed_f4(P, token, f);
-        // the embedding is the residual base of the rows this CTA owns
-        const float ev[4] = {xr[i].x, xr[i].y, xr[i].z, xr[i].w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint32_t e = 4 * f + k;
-          if (e >= c.hrow0 && e - c.hrow0 < P.hown_rows) c.hown[e - c.hrow0] = ev[k];
-        }
+      for (int i = 0; i < XR; ++i) {
+        const float4 t = xr[i];
+        ss = __fadd_rn(ss, __fadd_rn(__fadd_rn(__fmul_rn(t.x, t.x), __fmul_rn(t.y, t.y)),
+                                     __fadd_rn(__fmul_rn(t.z, t.z), __fmul_rn(t.w, t.w))));
       }
     }
+#pragma unroll
+    for (int i = 0; i < XR; ++i) {
+      const uint32_t f0 = base + warp * 32 + i * kNC;
+      if (f0 >= nf4) break;   // warp-uniform
+      const uint32_t f = f0 + lane;
+      const bool valid = f < nf4;
+      float4 t = xr[i];
+      if (PRO == PRO_RMSNORM && valid) {
+        const float4 g = reinterpret_cast<const float4 *>(sd.norm_w)[f];
+        t.x = __fmul_rn(t.x, g.x);
+        t.y = __fmul_rn(t.y, g.y);
+        t.z = __fmul_rn(t.z, g.z);
+        t.w = __fmul_rn(t.w, g.w);
+      }
+      digitise_f4<QT>(t, f, valid, c.xsm, sd.bpr, P.xbytes, P.status);
+    }
   }
-  trace(16 + 2 + EPI);
-  // RMSNorm (ops.rs:29-52) as y = inv * (W . (x * g)): the digits are taken
-  // of x * g right away and the scalar inv = 1/sqrt(mean(x^2) + eps) scales
-  // the row sums in the epilogue, so the sum of squares (fixed order: per
-  // thread over its float4s, xor-tree in the warp, warps in order) needs no
-  // barrier of its own: its per-warp parts cross the image barrier below.
   if (PRO == PRO_RMSNORM) {
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < kXRegs; ++i) {
-      const float4 t = xr[i];
-      ss = __fadd_rn(ss, __fadd_rn(__fadd_rn(__fmul_rn(t.x, t.x), __fmul_rn(t.y, t.y)),
-                                   __fadd_rn(__fmul_rn(t.z, t.z), __fmul_rn(t.w, t.w))));
-    }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
     if (lane == 0) c.red[warp] = ss;
-  }
-#pragma unroll
-  for (int i = 0; i < kXRegs; ++i) {
-    const uint32_t f0 = warp * 32 + i * kNC;
-    if (f0 >= nf4) break;   // warp-uniform
-    const uint32_t f = f0 + lane;
-    const bool valid = f < nf4;
-    float4 t = xr[i];
-    if (PRO == PRO_RMSNORM && valid) {
-      const float4 g = reinterpret_cast<const float4 *>(sd.norm_w)[f];
-      t.x = __fmul_rn(t.x, g.x);
-      t.y = __fmul_rn(t.y, g.y);
-      t.z = __fmul_rn(t.z, g.z);
-      t.w = __fmul_rn(t.w, g.w);
-    }
-    digitise_f4<QT>(t, f, valid, c.xsm, sd.bpr, P.xbytes, P.status);
   }
   named_bar_sync(kBarConsumers, kNC);
   trace(32 + 2 + EPI);
@@ -741,6 +746,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepParams 
     uint32_t u0, u1;
     unit_range(P.hown_units, &u0, &u1);
     c.hrow0 = u0 * 8;
+    c.hrow0g = P.hid_row0 + u0 * 8;
   }
   trace_begin();
   consumer(P, c);
@@ -758,10 +764,6 @@ bool step_geometry(const StageDesc *stages, uint32_t n, uint32_t grid, StepParam
     const StageDesc &s = stages[i];
     if (s.kind != STG_GEMV) continue;
     if (s.in_dim % 32 != 0 || s.bpr * 32 != s.in_dim) return false;
-    if (s.in_dim > 4u * 4u * kNC) return false;   // at most 4 float4s per consumer thread
-    // only the residual-adding (plain prologue) stages have a 4-float4 variant
-    if (s.in_dim > 2u * 4u * kNC && !(s.quant == ZGPU_Q4_0 && s.pro == PRO_PLAIN && s.epi == EPI_RESADD))
-      return false;
     const size_t img = static_cast<size_t>(s.bpr) * 128;
     if (img > xbytes) xbytes = img;
     const size_t upc = (static_cast<size_t>(s.units) + grid - 1) / grid;

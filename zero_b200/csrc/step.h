@@ -72,6 +72,7 @@ struct StepParams {
   uint32_t *bar;                    // [0] LM-head arrival counter, [1] abort flag (zero at launch)
   uint32_t xbytes, part_bytes, hown_off, ring_off, smem_bytes;
   uint32_t hown_units, hown_rows;  // residual rows kept per CTA (units of 8 rows)
+  uint32_t hid_row0;               // first hidden row of this rank's residual slice (0 on one GPU)
   uint32_t stages_off, n_stages;   // shared-memory copy of the stage list
 };
 
