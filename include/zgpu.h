@@ -262,6 +262,30 @@ typedef struct zgpu_qwen3_desc {
 
 zgpu_status zgpu_qwen3_create(zgpu_ctx *ctx, const zgpu_qwen3_desc *desc, zgpu_model **out);
 void zgpu_qwen3_destroy(zgpu_model *m);
+
+/* Tensor parallelism (output rows sharded over 1-8 GPUs,
+ * one process per GPU).  Rank `rank` of `world` keeps the q/k/v rows of its
+ * kv heads (n_kv_heads / world of them; its attention and KV cache are
+ * local: create the cache with n_kv_heads / world heads), gate/up SwiGLU
+ * units, and row slices of O, down and the LM head, the slices the
+ * reference's SMP partition splits by 4-row groups (smp_partition.rs:108-183)
+ * spread over GPUs.  The decode step is one persistent kernel per GPU whose
+ * stage epilogues store their rows straight into every rank's copy of the
+ * activation vector over NVLink (peer stores of tagged words): the
+ * all-gather is part of the kernel.  The LM head merges the ranks' argmax
+ * (larger logit, smaller row on ties).  Every output row is reduced as on one
+ * GPU, so tokens and logits equal the one-GPU decode bit for bit.
+ * Requires n_kv_heads, hidden / 8, ffn / 8 and the LM-head units to divide by
+ * world.  After creating every rank: zgpu_qwen3_tp_export on each, exchange
+ * the handles (ZGPU_IPC_HANDLE_BYTES each, rank order), then
+ * zgpu_qwen3_tp_connect on each.  A rank decodes through
+ * zgpu_generate_greedy only (all ranks call it with the same arguments);
+ * logits_out then receives the rank's vocab_padded / world rows per step. */
+#define ZGPU_IPC_HANDLE_BYTES 64
+zgpu_status zgpu_qwen3_create_tp(zgpu_ctx *ctx, const zgpu_qwen3_desc *desc, uint32_t rank, uint32_t world,
+                                 zgpu_model **out);
+zgpu_status zgpu_qwen3_tp_export(zgpu_model *m, void *handle_out);
+zgpu_status zgpu_qwen3_tp_connect(zgpu_model *m, const void *handles);
 /* forward_single_token (forward_pass.rs:515-631) /
  * forward_single_token_avx512 (inference_avx512.rs:1826-1987): token at
  * position `pos` through all layers, updating `kv`; the final hidden state

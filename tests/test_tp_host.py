@@ -1,0 +1,73 @@
+"""Host side of the tensor-parallel decode, on CPU: the shard plan tiles
+every output vector with whole 4-row groups in rank order, the
+divisibility rule refuses what the C side refuses, and the handle exchange
+over a 2-rank gloo group hands every rank all handles in rank order."""
+import socket
+
+import pytest
+import torch.multiprocessing as mp
+
+from zero_b200 import synth, tp
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+@pytest.mark.parametrize("cfg", [synth.QWEN3_8B, synth.QWEN3_1_7B], ids=lambda c: c.name)
+def test_shard_plan_tiles_every_vector(cfg, world):
+    plan = tp.shard_plan(cfg, world)
+    full = {"q": cfg.q_dim, "kv": cfg.kv_dim, "hidden": cfg.hidden, "act": cfg.ffn, "vocab": cfg.vocab_padded}
+    for name, n in full.items():
+        pos = 0
+        for r in range(world):
+            sl = plan[r][name]
+            assert sl.start == pos and sl.size == n // world
+            assert sl.start % 4 == 0 and sl.size % 4 == 0   # whole groups
+            pos = sl.stop
+        assert pos == n
+    for r in range(world):
+        # a rank's q heads are the q heads of its kv heads (GQA groups stay whole)
+        g = cfg.n_q_heads // cfg.n_kv_heads
+        assert plan[r]["q"].start == plan[r]["kv"].start * g
+
+
+def test_shardable_rule():
+    tp.check_shardable(synth.QWEN3_8B, 8)
+    with pytest.raises(ValueError):
+        tp.check_shardable(synth.QWEN3_8B, 3)        # 8 kv heads over 3 ranks
+    with pytest.raises(ValueError):
+        tp.check_shardable(synth.QWEN3_8B, 16)       # at most 8 ranks
+    with pytest.raises(ValueError):
+        tp.check_shardable(synth.small_config(n_q=4, n_kv=2), 4)
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _exchange_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        got = tp.exchange_handles(bytes([rank + 1]) * 64)
+        q.put((rank, got))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_handle_exchange_over_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(2):
+        assert res[r] == [bytes([1]) * 64, bytes([2]) * 64]

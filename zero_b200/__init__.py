@@ -20,6 +20,7 @@ from .synth import DS2_V2_LITE, QWEN3_1_7B, Ds2Config, Qwen3Config
 
 ABI_VERSION = 1
 F32, F16, Q4_0, Q8_0, Q4_0X4, Q8_0X4 = 0, 1, 2, 8, 100, 101
+IPC_HANDLE_BYTES = 64   # ZGPU_IPC_HANDLE_BYTES
 FLAG_NO_GRAPH, FLAG_NO_PDL, FLAG_NO_PERSISTENT = 0x1, 0x2, 0x4
 ROUTE_SOFTMAX, ROUTE_SIGMOID_NORMALIZE = 0, 1
 
@@ -242,8 +243,12 @@ class Qwen3Model:
     when `<name>_x4` copies exist, else as plain Q4_0 blocks.
     """
 
-    def __init__(self, ctx: Context, cfg: Qwen3Config, weights: dict):
+    def __init__(self, ctx: Context, cfg: Qwen3Config, weights: dict, rank: int = 0, world: int = 1):
+        """rank / world > 1: one tensor-parallel rank (zgpu_qwen3_create_tp);
+        call tp_export() on every rank, exchange the handles, then
+        tp_connect(handles) before decoding."""
         self.ctx, self.cfg, self.w = ctx, cfg, weights
+        self.rank, self.world = rank, world
         H = cfg.hidden
         eq = Q8_0 if cfg.embd_quant == "q8_0" else Q4_0
         oq = Q8_0 if cfg.output_quant == "q8_0" else Q4_0
@@ -272,7 +277,10 @@ class Qwen3Model:
             cfg.vocab_padded, cfg.vocab_real, cfg.rms_eps, cfg.rope_theta, eq, emb_key, oq, out_key,
             _ptr(weights["output_norm"]), self._layers)
         h = C.c_void_p()
-        ctx._check(LIB.zgpu_qwen3_create(ctx.h, C.byref(desc), C.byref(h)))
+        if world == 1:
+            ctx._check(LIB.zgpu_qwen3_create(ctx.h, C.byref(desc), C.byref(h)))
+        else:
+            ctx._check(LIB.zgpu_qwen3_create_tp(ctx.h, C.byref(desc), rank, world, C.byref(h)))
         self.h = h
 
     def close(self):
@@ -280,9 +288,27 @@ class Qwen3Model:
             LIB.zgpu_qwen3_destroy(self.h)
             self.h = None
 
+    def tp_export(self) -> bytes:
+        """This rank's CUDA IPC handle of its activation vectors (zgpu_qwen3_tp_export)."""
+        buf = (C.c_uint8 * IPC_HANDLE_BYTES)()
+        self.ctx._check(LIB.zgpu_qwen3_tp_export(self.h, buf))
+        return bytes(buf)
+
+    def tp_connect(self, handles) -> None:
+        """Map every rank's activation vectors (handles in rank order)."""
+        if len(handles) != self.world or any(len(x) != IPC_HANDLE_BYTES for x in handles):
+            raise ZgpuError(3, "tp_connect: one handle per rank")
+        blob = (C.c_uint8 * (IPC_HANDLE_BYTES * self.world)).from_buffer_copy(b"".join(handles))
+        self.ctx._check(LIB.zgpu_qwen3_tp_connect(self.h, blob))
+
+    @property
+    def vocab_rows(self) -> int:
+        """LM-head rows (logits) of this rank."""
+        return self.cfg.vocab_padded // self.world
+
     def new_kv(self, max_tokens: int) -> KvCache:
         c = self.cfg
-        return KvCache(self.ctx, max_tokens, c.n_layers, c.n_kv_heads, c.head_dim)
+        return KvCache(self.ctx, max_tokens, c.n_layers, c.n_kv_heads // self.world, c.head_dim)
 
     def forward_single_token(self, kv: KvCache, token: int, pos: int) -> np.ndarray:
         hidden = np.empty(self.cfg.hidden, np.float32)
@@ -300,7 +326,7 @@ class Qwen3Model:
     def generate_greedy(self, kv: KvCache, prompt, n_gen: int, want_logits: bool = False):
         p = np.ascontiguousarray(prompt, np.uint32)
         toks = np.empty(n_gen, np.uint32)
-        logits = np.empty((n_gen, self.cfg.vocab_padded), np.float32) if want_logits else None
+        logits = np.empty((n_gen, self.vocab_rows), np.float32) if want_logits else None
         self.ctx._check(LIB.zgpu_generate_greedy(self.h, kv.h, _ptr(p), p.size, n_gen, _ptr(toks),
                                                  _ptr(logits) if want_logits else None))
         return toks, logits

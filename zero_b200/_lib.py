@@ -99,6 +99,9 @@ _SIGS = {
                                                 _vp]),
     "zgpu_gqa_attention_decode_noalloc": (_i32, [_vp, _vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _f, _vp,
                                                  _vp]),
+    "zgpu_qwen3_create_tp": (_i32, [_vp, C.POINTER(ZgpuQwen3Desc), _u32, _u32, C.POINTER(_vp)]),
+    "zgpu_qwen3_tp_export": (_i32, [_vp, _vp]),
+    "zgpu_qwen3_tp_connect": (_i32, [_vp, _vp]),
     "zgpu_qwen3_create": (_i32, [_vp, C.POINTER(ZgpuQwen3Desc), C.POINTER(_vp)]),
     "zgpu_qwen3_destroy": (None, [_vp]),
     "zgpu_forward_single_token": (_i32, [_vp, _vp, _u32, _u32, _vp]),

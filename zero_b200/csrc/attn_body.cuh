@@ -111,8 +111,16 @@ __device__ __forceinline__ float4 attn_load_proj(const AttnParams &p, uint32_t o
 
 template <bool TAGGED>
 __device__ __forceinline__ void attn_store_out(const AttnParams &p, uint32_t i, float v) {
-  if (TAGGED) p.out_t[i] = tag_word(v, p.ver_out);
-  else p.out[i] = v;
+  if (TAGGED) {
+    const unsigned long long w = tag_word(v, p.ver_out);
+    if (p.n_out == 0) {
+      p.out_t[i] = w;
+    } else {
+      for (uint32_t d = 0; d < p.n_out; ++d) p.out_dst[d][i] = w;
+    }
+  } else {
+    p.out[i] = v;
+  }
 }
 
 // Mark: optional timeline hook (event id) for profiling builds of the caller.

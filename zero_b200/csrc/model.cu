@@ -74,6 +74,18 @@ struct zgpu_model {
   uint8_t *d_pf = nullptr;
   size_t pf_cap = 0;
   std::vector<cudaEvent_t> pf_ev;   // one pair per timed prefill launch (GEMM / attention)
+  // tensor parallelism (world > 1): this rank's slice of every stage
+  uint32_t rank = 0, world = 1;
+  uint32_t q_loc = 0, kv_loc = 0;   // this rank's q / k rows (all of them on one GPU)
+  uint32_t lm_rows = 0;             // LM-head (vocabulary) rows on this rank
+  std::vector<DeviceTensor *> owned;   // row slices made for this rank (O, down, LM head)
+  size_t tv_words = 0, arg_off = 0;    // tagged arena size; its argmax slots (words)
+  size_t tv_off[kStepBufs] = {};
+  bool tp_connected = false;
+  std::vector<void *> ipc_opened;      // peers' arenas mapped into this process
+  unsigned long long **d_peer_tv = nullptr;
+  ArgSlot **d_peer_arg = nullptr;
+  unsigned long long **d_attn_dst = nullptr;
 };
 
 // Status block of a step: copy back (synchronising the stream), clear it
@@ -350,7 +362,9 @@ zgpu_status build_step(zgpu_model *m) {
   if (!grid) return ZGPU_OK;
   const zgpu_qwen3_desc &d = m->desc;
   const uint32_t H = d.hidden, F = d.ffn, L = d.n_layers;
-  const uint32_t qkv_rows = m->q_dim + 2 * m->kv_dim;
+  const uint32_t N = m->world, r = m->rank;
+  const uint32_t qkv_rows = m->q_loc + 2 * m->kv_loc;   // this rank's heads only: attention is local
+  const uint32_t H_loc = H / N, F_loc = F / N;
   auto gemv = [&](uint32_t quant, uint32_t pro, uint32_t epi, uint32_t rows, uint32_t units,
                   uint32_t in_dim, const uint8_t *w, uint64_t gstride, uint64_t wbytes, uint32_t in_buf,
                   const float *norm_w, uint32_t out_buf) {
@@ -374,8 +388,16 @@ zgpu_status build_step(zgpu_model *m) {
     s.norm_w = norm_w;
     return s;
   };
-  // gate/up groups as the registry stores them (padded to an even count)
-  const uint64_t gu_groups = ((F + 3) / 4 + 1) & ~uint64_t(1);
+  // gate/up units (a gate group and its up group each) as the model stores
+  // them: padded to an even count on one GPU, F / 4 / N on a rank
+  const uint64_t gu_groups = N == 1 ? (((F + 3) / 4 + 1) & ~uint64_t(1)) : F_loc / 4;
+  // tensor parallel: the O, gate/up, down and LM-head stages own a row slice
+  // and store it into every rank's copy of the vector
+  auto slice = [&](StageDesc s, uint32_t row0) {
+    s.out_row0 = row0;
+    s.bcast = N > 1 ? 1u : 0u;
+    return s;
+  };
   std::vector<StageDesc> st;
   for (uint32_t l = 0; l < L; ++l) {
     StageDesc q = gemv(ZGPU_Q4_0, PRO_RMSNORM, EPI_STORE, qkv_rows, qkv_rows / 8, H, m->qkv[l], m->gs_h,
@@ -389,37 +411,51 @@ zgpu_status build_step(zgpu_model *m) {
     a.k_norm = norm_k(m, l);
     st.push_back(a);
     const DeviceTensor *o = m->o[l], *dn = m->down[l];
-    st.push_back(gemv(ZGPU_Q4_0, PRO_PLAIN, EPI_RESADD, H, static_cast<uint32_t>(o->groups / 2), m->q_dim,
-                      o->d, o->gstride, o->bytes, BUF_ATTN, nullptr, BUF_HIDDEN));
-    st.push_back(gemv(ZGPU_Q4_0, PRO_RMSNORM, EPI_SWIGLU, F, static_cast<uint32_t>(gu_groups), H, m->gateup[l],
-                      m->gs_h, 2 * gu_groups * m->gs_h, BUF_HIDDEN, norm_ffn(m, l), BUF_ACT));
-    st.push_back(gemv(ZGPU_Q4_0, PRO_PLAIN, EPI_RESADD, H, static_cast<uint32_t>(dn->groups / 2), F, dn->d,
-                      dn->gstride, dn->bytes, BUF_ACT, nullptr, BUF_HIDDEN));
+    st.push_back(slice(gemv(ZGPU_Q4_0, PRO_PLAIN, EPI_RESADD, H_loc, static_cast<uint32_t>(o->groups / 2),
+                            m->q_dim, o->d, o->gstride, o->bytes, BUF_ATTN, nullptr, BUF_HIDDEN),
+                       r * H_loc));
+    st.push_back(slice(gemv(ZGPU_Q4_0, PRO_RMSNORM, EPI_SWIGLU, F_loc, static_cast<uint32_t>(gu_groups), H,
+                            m->gateup[l], m->gs_h, 2 * gu_groups * m->gs_h, BUF_HIDDEN, norm_ffn(m, l), BUF_ACT),
+                       r * F_loc));
+    st.push_back(slice(gemv(ZGPU_Q4_0, PRO_PLAIN, EPI_RESADD, H_loc, static_cast<uint32_t>(dn->groups / 2), F,
+                            dn->d, dn->gstride, dn->bytes, BUF_ACT, nullptr, BUF_HIDDEN),
+                       r * H_loc));
   }
   const DeviceTensor *ot = m->out;
   const uint32_t gpu = ot->quant == ZGPU_Q4_0 ? 2 : 1;
   const uint32_t lm = static_cast<uint32_t>(st.size());
-  st.push_back(gemv(ot->quant, PRO_RMSNORM, EPI_ARGMAX, d.vocab_padded, static_cast<uint32_t>(ot->groups / gpu),
-                    H, ot->d, ot->gstride, ot->bytes, BUF_HIDDEN, norm_out(m), BUF_NONE));
+  st.push_back(slice(gemv(ot->quant, PRO_RMSNORM, EPI_ARGMAX, m->lm_rows, static_cast<uint32_t>(ot->groups / gpu),
+                          H, ot->d, ot->gstride, ot->bytes, BUF_HIDDEN, norm_out(m), BUF_NONE),
+                     r * m->lm_rows));
+  st.back().bcast = 0;   // the argmax keys meet in the LM head's own exchange
   st.back().out = m->d_logits;
   StepParams g = {};
   if (!step_geometry(st.data(), static_cast<uint32_t>(st.size()), grid, &g)) return ZGPU_OK;
+  g.hid_row0 = r * H_loc;
+  g.rank = r;
+  g.world = N;
   cudaError_t e = cudaMalloc(&m->d_stages, st.size() * sizeof(StageDesc));
   if (e == cudaSuccess)
     e = cudaMemcpy(m->d_stages, st.data(), st.size() * sizeof(StageDesc), cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMalloc(&m->d_bar, 2 * sizeof(uint32_t));
   if (e == cudaSuccess) e = cudaMemset(m->d_bar, 0, 2 * sizeof(uint32_t));
-  // tagged vectors (version 0 everywhere: nothing written yet)
+  // tagged vectors (version 0 everywhere: nothing written yet), then the
+  // argmax slots of the tensor-parallel LM head; every rank lays its arena
+  // out the same way
   const size_t tv_len[kStepBufs] = {H, qkv_rows, m->q_dim, F, 2};
   size_t tv_total = 0;
-  for (size_t n : tv_len) tv_total += n;
+  for (int b = 0; b < kStepBufs; ++b) {
+    m->tv_off[b] = tv_total;
+    tv_total += tv_len[b];
+  }
+  m->arg_off = tv_total;
+  tv_total += 2 * kMaxRanks;
+  m->tv_words = tv_total;
   if (e == cudaSuccess) e = cudaMalloc(&m->d_tv, tv_total * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMemset(m->d_tv, 0, tv_total * sizeof(unsigned long long));
   if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "step kernel set-up");
-  size_t off = 0;
   for (int b = 0; b < kStepBufs; ++b) {
-    m->tv[b] = m->d_tv + off;
-    off += tv_len[b];
+    m->tv[b] = m->d_tv + m->tv_off[b];
     m->ver[b] = 0;
   }
   for (StageDesc &sd : st) {
@@ -440,7 +476,7 @@ zgpu_status build_step(zgpu_model *m) {
 
 bool step_usable(const zgpu_model *m, const zgpu_kv *kv) {
   if (!m->step_grid) return false;
-  return !kv || static_cast<uint64_t>(m->desc.n_kv_heads) * m->max_splits <= m->step_grid;
+  return !kv || static_cast<uint64_t>(m->desc.n_kv_heads / m->world) * m->max_splits <= m->step_grid;
 }
 
 // One persistent launch: `n_steps` steps from global step `step0`.
@@ -456,8 +492,11 @@ cudaError_t run_step(zgpu_model *m, zgpu_kv *kv, StepMode mode, uint32_t step0, 
   p.n_steps = n_steps;
   p.fwd_token = token;
   p.fwd_pos = pos;
-  p.n_q = d.n_q_heads;
-  p.n_kv = d.n_kv_heads;
+  p.n_q = d.n_q_heads / m->world;
+  p.n_kv = d.n_kv_heads / m->world;
+  p.peer_tv = m->d_peer_tv;
+  p.peer_arg = m->d_peer_arg;
+  p.attn_dst = m->d_attn_dst;
   p.max_splits = m->max_splits;
   p.max_tokens = kv ? kv->max_tokens : 0;
   p.eps = d.rms_eps;
@@ -501,8 +540,7 @@ cudaError_t run_step(zgpu_model *m, zgpu_kv *kv, StepMode mode, uint32_t step0, 
 // them over.
 void reset_step_tags(zgpu_model *m) {
   if (!m->d_tv) return;
-  const size_t n = m->desc.hidden + (m->q_dim + 2 * m->kv_dim) + m->q_dim + m->desc.ffn + 2;
-  cudaMemsetAsync(m->d_tv, 0, n * sizeof(unsigned long long), m->ctx->stream);
+  cudaMemsetAsync(m->d_tv, 0, m->tv_words * sizeof(unsigned long long), m->ctx->stream);
   for (int b = 0; b < kStepBufs; ++b) m->ver[b] = 0;
 }
 
@@ -604,10 +642,25 @@ void zgpu_qwen3_destroy(zgpu_model *m) {
   for (auto &e : m->ev)
     if (e) cudaEventDestroy(e);
   for (auto &e : m->pf_ev) cudaEventDestroy(e);
+  for (DeviceTensor *t : m->owned) {
+    cudaFree(t->d);
+    delete t;
+  }
+  for (void *p : m->ipc_opened) cudaIpcCloseMemHandle(p);
+  cudaFree(m->d_peer_tv);
+  cudaFree(m->d_peer_arg);
+  cudaFree(m->d_attn_dst);
   delete m;
 }
 
-zgpu_status zgpu_qwen3_create(zgpu_ctx *ctx, const zgpu_qwen3_desc *d, zgpu_model **out) {
+}  // extern "C"
+
+namespace {
+
+// A model, or (world > 1) rank `rank` of a tensor-parallel model: the rank
+// keeps q/k/v rows of its kv heads, gate/up units, and O / down / LM-head
+// row slices; the embedding and the norms are whole on every rank.
+zgpu_status create_model(zgpu_ctx *ctx, const zgpu_qwen3_desc *d, uint32_t rank, uint32_t world, zgpu_model **out) {
   if (!ctx || !d || !out || !d->layers) return ZGPU_ERR_INVALID_ARG;
   *out = nullptr;
   cudaSetDevice(ctx->device);
@@ -618,6 +671,13 @@ zgpu_status zgpu_qwen3_create(zgpu_ctx *ctx, const zgpu_qwen3_desc *d, zgpu_mode
   if (d->hidden % 32 || d->ffn % 32 || d->hidden % 4 || d->ffn % 4)
     return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "hidden/ffn must be multiples of 32");
   if (d->vocab_real > d->vocab_padded) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "vocab_real > vocab_padded");
+  if (world == 0 || world > kMaxRanks || rank >= world)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "tensor parallel: 1..8 ranks");
+  const uint32_t lm_unit = d->output_quant == ZGPU_Q4_0 ? 8u : 4u;
+  if (world > 1 && (d->n_kv_heads % world || d->hidden % (8 * world) || d->ffn % (8 * world) ||
+                    d->vocab_padded % (lm_unit * world)))
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG,
+                     "tensor parallel: kv heads, hidden / 8, ffn / 8 and the LM-head units must divide by the ranks");
   zgpu_model *m = new (std::nothrow) zgpu_model();
   if (!m) return ZGPU_ERR_OUT_OF_MEMORY;
   m->ctx = ctx;
@@ -626,10 +686,33 @@ zgpu_status zgpu_qwen3_create(zgpu_ctx *ctx, const zgpu_qwen3_desc *d, zgpu_mode
   m->desc.output_norm = nullptr;
   m->q_dim = d->n_q_heads * d->head_dim;
   m->kv_dim = d->n_kv_heads * d->head_dim;
+  m->rank = rank;
+  m->world = world;
+  m->q_loc = m->q_dim / world;
+  m->kv_loc = m->kv_dim / world;
+  m->lm_rows = d->vocab_padded / world;
   const uint32_t H = d->hidden, F = d->ffn, L = d->n_layers, hd = d->head_dim;
   auto fail = [&](zgpu_status s, const std::string &msg) {
     zgpu_qwen3_destroy(m);
     return zgpu_fail(ctx, s, msg);
+  };
+  // rows [row0, row0 + rows) of a registered tensor as a tensor of this rank
+  // (group streams: whole groups of 4 rows)
+  auto row_slice = [&](const DeviceTensor *t, uint64_t row0, uint64_t rows) -> const DeviceTensor * {
+    if (world == 1) return t;
+    DeviceTensor *sl = new (std::nothrow) DeviceTensor(*t);
+    if (!sl) return nullptr;
+    sl->rows = rows;
+    sl->groups = rows / 4;
+    sl->bytes = sl->groups * t->gstride;
+    sl->d = nullptr;
+    if (cudaMalloc(&sl->d, sl->bytes) != cudaSuccess) {
+      delete sl;
+      return nullptr;
+    }
+    m->owned.push_back(sl);
+    cudaMemcpy(sl->d, t->d + (row0 / 4) * t->gstride, sl->bytes, cudaMemcpyDeviceToDevice);
+    return sl;
   };
   auto need = [&](const void *key, uint32_t quant, uint64_t rows, uint64_t cols,
                   const char *what) -> const DeviceTensor * {
@@ -644,6 +727,8 @@ zgpu_status zgpu_qwen3_create(zgpu_ctx *ctx, const zgpu_qwen3_desc *d, zgpu_mode
   if (!m->emb) return fail(ZGPU_ERR_UNREGISTERED_WEIGHT, ctx->last_error);
   m->out = need(d->output, d->output_quant, d->vocab_padded, H, "output");
   if (!m->out) return fail(ZGPU_ERR_UNREGISTERED_WEIGHT, ctx->last_error);
+  m->out = row_slice(m->out, static_cast<uint64_t>(rank) * m->lm_rows, m->lm_rows);
+  if (!m->out) return fail(ZGPU_ERR_OUT_OF_MEMORY, "LM-head slice");
 
   cudaError_t e = cudaSuccess;
   for (uint32_t l = 0; l < L; ++l) {
@@ -662,23 +747,32 @@ zgpu_status zgpu_qwen3_create(zgpu_ctx *ctx, const zgpu_qwen3_desc *d, zgpu_mode
     m->gs_h = q->gstride;
     m->gs_q = o->gstride;
     m->gs_f = dn->gstride;
+    // fused Q|K|V of this rank's heads: q rows of its q heads, then the k and
+    // v rows of its kv heads (everything on one GPU)
+    const uint64_t qb = static_cast<uint64_t>(m->q_loc / 4) * q->gstride;
+    const uint64_t kb = static_cast<uint64_t>(m->kv_loc / 4) * k->gstride;
     uint8_t *cat = nullptr;
-    e = cudaMalloc(&cat, q->bytes + k->bytes + v->bytes);
+    e = cudaMalloc(&cat, qb + 2 * kb);
     if (e != cudaSuccess) return fail(ZGPU_ERR_OUT_OF_MEMORY, "qkv allocation");
     m->qkv.push_back(cat);
-    cudaMemcpy(cat, q->d, q->bytes, cudaMemcpyDeviceToDevice);
-    cudaMemcpy(cat + q->bytes, k->d, k->bytes, cudaMemcpyDeviceToDevice);
-    cudaMemcpy(cat + q->bytes + k->bytes, v->d, v->bytes, cudaMemcpyDeviceToDevice);
+    cudaMemcpy(cat, q->d + rank * qb, qb, cudaMemcpyDeviceToDevice);
+    cudaMemcpy(cat + qb, k->d + rank * kb, kb, cudaMemcpyDeviceToDevice);
+    cudaMemcpy(cat + qb + kb, v->d + rank * kb, kb, cudaMemcpyDeviceToDevice);
+    // gate/up units of this rank, interleaved (gate group u, up group u)
+    const uint64_t gu_n = world == 1 ? gt->groups : F / 4 / world, gu_0 = world == 1 ? 0 : rank * gu_n;
     uint8_t *gu = nullptr;
-    e = cudaMalloc(&gu, gt->bytes + up->bytes);
+    e = cudaMalloc(&gu, world == 1 ? gt->bytes + up->bytes : 2 * gu_n * gt->gstride);
     if (e != cudaSuccess) return fail(ZGPU_ERR_OUT_OF_MEMORY, "gate/up allocation");
     m->gateup.push_back(gu);
-    cudaMemcpy2D(gu, 2 * gt->gstride, gt->d, gt->gstride, gt->gstride, gt->groups,
+    cudaMemcpy2D(gu, 2 * gt->gstride, gt->d + gu_0 * gt->gstride, gt->gstride, gt->gstride, gu_n,
                  cudaMemcpyDeviceToDevice);
-    cudaMemcpy2D(gu + gt->gstride, 2 * gt->gstride, up->d, up->gstride, up->gstride, up->groups,
+    cudaMemcpy2D(gu + gt->gstride, 2 * gt->gstride, up->d + gu_0 * up->gstride, up->gstride, up->gstride, gu_n,
                  cudaMemcpyDeviceToDevice);
-    m->o.push_back(o);
-    m->down.push_back(dn);
+    const DeviceTensor *os = row_slice(o, static_cast<uint64_t>(rank) * (H / world), H / world);
+    const DeviceTensor *ds = row_slice(dn, static_cast<uint64_t>(rank) * (H / world), H / world);
+    if (!os || !ds) return fail(ZGPU_ERR_OUT_OF_MEMORY, "O / down slices");
+    m->o.push_back(os);
+    m->down.push_back(ds);
   }
   // norms
   const size_t nn = static_cast<size_t>(2) * L * H + static_cast<size_t>(2) * L * hd + H;
@@ -720,7 +814,72 @@ zgpu_status zgpu_qwen3_create(zgpu_ctx *ctx, const zgpu_qwen3_desc *d, zgpu_mode
     zgpu_qwen3_destroy(m);
     return bs;
   }
+  if (world > 1 && !m->step_grid)
+    return fail(ZGPU_ERR_INVALID_ARG, "tensor parallel: the persistent step kernel does not fit this model");
   *out = m;
+  return ZGPU_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+zgpu_status zgpu_qwen3_create(zgpu_ctx *ctx, const zgpu_qwen3_desc *d, zgpu_model **out) {
+  return create_model(ctx, d, 0, 1, out);
+}
+
+zgpu_status zgpu_qwen3_create_tp(zgpu_ctx *ctx, const zgpu_qwen3_desc *d, uint32_t rank, uint32_t world,
+                                 zgpu_model **out) {
+  return create_model(ctx, d, rank, world, out);
+}
+
+zgpu_status zgpu_qwen3_tp_export(zgpu_model *m, void *handle_out) {
+  if (!m || !handle_out || m->world < 2 || !m->d_tv) return ZGPU_ERR_INVALID_ARG;
+  cudaSetDevice(m->ctx->device);
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, m->d_tv);
+  if (e != cudaSuccess) return zgpu_cuda_fail(m->ctx, e, "tensor parallel: export the tagged vectors");
+  std::memcpy(handle_out, &h, sizeof(h));
+  return ZGPU_OK;
+}
+
+zgpu_status zgpu_qwen3_tp_connect(zgpu_model *m, const void *handles) {
+  if (!m || !handles || m->world < 2 || !m->d_tv) return ZGPU_ERR_INVALID_ARG;
+  if (m->tp_connected) return zgpu_fail(m->ctx, ZGPU_ERR_INVALID_ARG, "tensor parallel: already connected");
+  zgpu_ctx *ctx = m->ctx;
+  cudaSetDevice(ctx->device);
+  const uint32_t N = m->world;
+  std::vector<unsigned long long *> base(N, nullptr);
+  for (uint32_t d = 0; d < N; ++d) {
+    if (d == m->rank) {
+      base[d] = m->d_tv;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, static_cast<const uint8_t *>(handles) + static_cast<size_t>(d) * sizeof(h), sizeof(h));
+    void *p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "tensor parallel: open a peer's tagged vectors");
+    m->ipc_opened.push_back(p);
+    base[d] = static_cast<unsigned long long *>(p);
+  }
+  std::vector<unsigned long long *> tv(static_cast<size_t>(N) * kStepBufs), dst(N);
+  std::vector<ArgSlot *> arg(N);
+  for (uint32_t d = 0; d < N; ++d) {
+    for (int b = 0; b < kStepBufs; ++b) tv[static_cast<size_t>(d) * kStepBufs + b] = base[d] + m->tv_off[b];
+    arg[d] = reinterpret_cast<ArgSlot *>(base[d] + m->arg_off);
+    dst[d] = base[d] + m->tv_off[BUF_ATTN] + static_cast<size_t>(m->rank) * m->q_loc;
+  }
+  cudaError_t e = cudaMalloc(&m->d_peer_tv, tv.size() * sizeof(void *));
+  if (e == cudaSuccess) e = cudaMalloc(&m->d_peer_arg, arg.size() * sizeof(void *));
+  if (e == cudaSuccess) e = cudaMalloc(&m->d_attn_dst, dst.size() * sizeof(void *));
+  if (e == cudaSuccess) e = cudaMemcpy(m->d_peer_tv, tv.data(), tv.size() * sizeof(void *), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(m->d_peer_arg, arg.data(), arg.size() * sizeof(void *), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(m->d_attn_dst, dst.data(), dst.size() * sizeof(void *), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "tensor parallel: peer tables");
+  m->tp_connected = true;
   return ZGPU_OK;
 }
 
@@ -733,7 +892,8 @@ zgpu_status prepare_kv(zgpu_model *m, zgpu_kv *kv) {
   zgpu_ctx *ctx = m->ctx;
   if (kv->n_layers != m->desc.n_layers)
     return zgpu_fail(ctx, ZGPU_ERR_KV_LAYER_OUT_OF_RANGE, "kv cache layer count differs from the model");
-  if (kv->n_kv != m->desc.n_kv_heads || kv->head_dim != m->desc.head_dim)
+  // a tensor-parallel rank caches its own kv heads only
+  if (kv->n_kv != m->desc.n_kv_heads / m->world || kv->head_dim != m->desc.head_dim)
     return zgpu_fail(ctx, ZGPU_ERR_KV_INVALID_SLICE_LENGTH, "kv cache geometry differs from the model");
   const uint32_t splits = attention_max_splits(kv->max_tokens);
   if (splits != m->max_splits || !m->d_part) {
@@ -755,6 +915,8 @@ extern "C" {
 zgpu_status zgpu_forward_single_token(zgpu_model *m, zgpu_kv *kv, uint32_t token, uint32_t pos,
                                       float *hidden_out) {
   if (!m || !kv) return ZGPU_ERR_INVALID_ARG;
+  if (m->world > 1)
+    return zgpu_fail(m->ctx, ZGPU_ERR_INVALID_ARG, "tensor-parallel ranks decode through zgpu_generate_greedy");
   zgpu_ctx *ctx = m->ctx;
   cudaSetDevice(ctx->device);
   zgpu_status s = prepare_kv(m, kv);
@@ -808,6 +970,8 @@ zgpu_status zgpu_forward_single_token(zgpu_model *m, zgpu_kv *kv, uint32_t token
 zgpu_status zgpu_lm_head_argmax(zgpu_model *m, uint32_t vocab_real, uint32_t *token_out,
                                 float *logits_out) {
   if (!m || !token_out) return ZGPU_ERR_INVALID_ARG;
+  if (m->world > 1)
+    return zgpu_fail(m->ctx, ZGPU_ERR_INVALID_ARG, "tensor-parallel ranks decode through zgpu_generate_greedy");
   zgpu_ctx *ctx = m->ctx;
   cudaSetDevice(ctx->device);
   if (vocab_real > m->desc.vocab_padded) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "vocab_real > padded");
@@ -847,6 +1011,8 @@ zgpu_status zgpu_generate_greedy(zgpu_model *m, zgpu_kv *kv, const uint32_t *pro
   if (!m || !kv || !prompt || !tokens_out || n_prompt == 0 || n_gen == 0) return ZGPU_ERR_INVALID_ARG;
   zgpu_ctx *ctx = m->ctx;
   cudaSetDevice(ctx->device);
+  if (m->world > 1 && !m->tp_connected)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "tensor parallel: zgpu_qwen3_tp_connect first");
   zgpu_status s = prepare_kv(m, kv);
   if (s) return s;
   const uint32_t steps = n_prompt + n_gen - 1;
@@ -861,6 +1027,8 @@ zgpu_status zgpu_generate_greedy(zgpu_model *m, zgpu_kv *kv, const uint32_t *pro
   e = cudaMemcpyAsync(m->d_prompt, prompt, n_prompt * 4, cudaMemcpyHostToDevice, ctx->stream);
   if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "prompt upload");
   const bool persistent = step_usable(m, kv);
+  if (m->world > 1 && !persistent)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "tensor parallel: the cache needs more attention CTAs than the step kernel has");
   const bool use_graph = !persistent && !(ctx->flags & ZGPU_FLAG_NO_GRAPH);
   if (use_graph && (s = build_graphs(m, kv))) return s;
   const size_t V = m->desc.vocab_padded;
@@ -869,9 +1037,11 @@ zgpu_status zgpu_generate_greedy(zgpu_model *m, zgpu_kv *kv, const uint32_t *pro
     // one launch for the prompt (the LM head runs after its last token) and
     // one for the decode steps; with logits requested, one launch per step so
     // that each step's logits can be copied out
+    // (a tensor-parallel rank has the logits of its own vocabulary rows)
+    const size_t VL = m->lm_rows;
     auto copy_logits = [&](uint32_t step) -> cudaError_t {
       if (!logits_out || step + 1 < n_prompt) return cudaSuccess;
-      return cudaMemcpyAsync(logits_out + static_cast<size_t>(step + 1 - n_prompt) * V, m->d_logits, V * 4,
+      return cudaMemcpyAsync(logits_out + static_cast<size_t>(step + 1 - n_prompt) * VL, m->d_logits, VL * 4,
                              cudaMemcpyDeviceToHost, ctx->stream);
     };
     auto phase = [&](uint32_t first, uint32_t last) -> cudaError_t {
@@ -960,6 +1130,8 @@ extern "C" {
 zgpu_status zgpu_prefill(zgpu_model *m, zgpu_kv *kv, const uint32_t *tokens, uint32_t n, uint32_t *token_out,
                          float *logits_out) {
   if (!m || !kv || !tokens || !token_out || n == 0) return ZGPU_ERR_INVALID_ARG;
+  if (m->world > 1)
+    return zgpu_fail(m->ctx, ZGPU_ERR_INVALID_ARG, "tensor-parallel ranks decode through zgpu_generate_greedy");
   zgpu_ctx *ctx = m->ctx;
   cudaSetDevice(ctx->device);
   const zgpu_qwen3_desc &d = m->desc;

@@ -62,6 +62,10 @@ struct AttnParams {
   const unsigned long long *qkv_t;
   unsigned long long *out_t;
   uint32_t ver_in, ver_out;
+  // tensor parallel: the output goes to the n_out copies out_dst[0..n_out)
+  // (device table, each offset to this rank's heads); n_out == 0 writes out_t
+  unsigned long long *const *out_dst;
+  uint32_t n_out;
   volatile uint32_t *abort;         // this CTA's abort flag (shared memory)
   uint32_t *gabort;                 // the launch's abort flag
 };

@@ -448,6 +448,15 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
   // ---- epilogue: K-chunks in order, then per row
   unsigned long long *xout = sd.tout;
   const uint32_t vout = (EPI == EPI_ARGMAX) ? 0u : ver_of(c, sd.out_buf) + 1;
+  // output word of local row `row`: this rank's vector, or (tensor parallel)
+  // every rank's copy at the slice's place in the whole vector
+  auto put = [&](uint32_t row, unsigned long long w) {
+    if (sd.bcast) {
+      for (uint32_t d = 0; d < P.world; ++d) P.peer_tv[d * kStepBufs + sd.out_buf][sd.out_row0 + row] = w;
+    } else {
+      xout[row] = w;
+    }
+  };
   unsigned long long best = kArgmaxInitKey;
   if (EPI == EPI_SWIGLU) {
     // unit = {gate rows 4u..4u+3, up rows 4u..4u+3}
@@ -461,7 +470,7 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
       yg = __fmul_rn(yg, inv);
       yu = __fmul_rn(yu, inv);
       const uint32_t row = (u0 + ul) * 4 + r;
-      if (row < sd.rows) xout[row] = tag_word(ref_silu_mul(yg, yu), vout);
+      if (row < sd.rows) put(row, tag_word(ref_silu_mul(yg, yu), vout));
     }
   } else {
     for (uint32_t t = tid; t < nloc * R; t += kNC) {
@@ -472,15 +481,15 @@ __device__ __forceinline__ void gemv_stage(const StepParams &P, const StageDesc 
       const uint32_t row = (u0 + ul) * R + r;
       if (row < sd.rows) {
         if (EPI == EPI_STORE) {
-          xout[row] = tag_word(y, vout);
+          put(row, tag_word(y, vout));
         } else if (EPI == EPI_RESADD) {
           const uint32_t hr = row - c.hrow0;   // < hown_rows: this CTA owns the row
           const float h = c.hown[hr] + y;
           c.hown[hr] = h;
-          xout[row] = tag_word(h, vout);
+          put(row, tag_word(h, vout));
         } else {
           sd.out[row] = y;
-          const unsigned long long key = argmax_key(y, row);
+          const unsigned long long key = argmax_key(y, sd.out_row0 + row);
           best = key > best ? key : best;
         }
       }
@@ -533,9 +542,9 @@ __device__ __forceinline__ void run_gemv(const StepParams &P, const StageDesc &s
 // arrived): decode the argmax key, apply the non-finite and padding checks of
 // lm_head.rs:157-163, record the token, publish it for the next step, reset
 // the key and advance the step.
-__device__ void finalize(const StepParams &P, uint32_t gstep, uint32_t n_prompt, uint32_t tok_ver) {
+__device__ void finalize(const StepParams &P, uint32_t gstep, uint32_t n_prompt, uint32_t tok_ver,
+                         unsigned long long key) {
   StepState *st = P.state;
-  const unsigned long long key = __ldcg(P.argmax);
   const uint32_t idx = argmax_key_index(key);
   const float val = argmax_key_value(key);
   uint32_t err = 0;
@@ -554,6 +563,51 @@ __device__ void finalize(const StepParams &P, uint32_t gstep, uint32_t n_prompt,
   st->step = gstep + 1;
   *P.argmax = kArgmaxInitKey;
   P.tv[BUF_TOKEN][0] = (static_cast<unsigned long long>(tok_ver) << 32) | idx;
+}
+
+__device__ __forceinline__ void st_relaxed_sys(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Tensor parallel LM head (CTA 0, one thread): publish this rank's argmax key
+// into slot [rank] of every rank (the key, then the version with release
+// semantics), wait (bounded) until every slot of this rank carries `ver`, and
+// merge: the larger key wins, i.e. the larger logit and, on ties, the
+// smaller vocabulary row, as the one-GPU argmax over the whole vocabulary.
+__device__ bool exchange_argmax(const StepParams &P, unsigned long long key, uint32_t ver,
+                                unsigned long long *merged) {
+  for (uint32_t d = 0; d < P.world; ++d) st_relaxed_sys(&P.peer_arg[d][P.rank].key, key);
+  for (uint32_t d = 0; d < P.world; ++d) st_release_sys(&P.peer_arg[d][P.rank].ver, ver);
+  ArgSlot *mine = P.peer_arg[P.rank];
+  unsigned long long best = kArgmaxInitKey;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t r = 0; r < P.world; ++r) {
+    while (ld_acquire_sys(&mine[r].ver) != ver) {
+      if (ld_relaxed_u32(&P.bar[1])) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicOr(P.status, ZDEV_ERR_TIMEOUT);
+        atomicExch(&P.bar[1], 1u);
+        return false;
+      }
+    }
+    const unsigned long long k = ld_relaxed_sys(&mine[r].key);
+    best = k > best ? k : best;
+  }
+  *merged = best;
+  return true;
 }
 
 // The step's token: a prompt id, the previous step's argmax (waiting for its
@@ -642,6 +696,8 @@ __device__ __forceinline__ void consumer(const StepParams &P, Ctx &c) {
             ap.scale = P.scale;
             ap.qkv_t = P.tv[BUF_QKV];
             ap.out_t = P.tv[BUF_ATTN];
+            ap.n_out = P.world > 1 ? P.world : 0;
+            ap.out_dst = P.attn_dst;
             ap.ver_in = c.v_qkv;
             ap.ver_out = c.v_attn + 1;
             ap.abort = c.abort;
@@ -681,7 +737,9 @@ __device__ __forceinline__ void consumer(const StepParams &P, Ctx &c) {
             break;
           }
         }
-        if (ok) finalize(P, gstep, n_prompt, c.v_token + 1);
+        unsigned long long key = __ldcg(P.argmax);
+        if (ok && P.world > 1) ok = exchange_argmax(P, key, c.v_token + 1, &key);
+        if (ok) finalize(P, gstep, n_prompt, c.v_token + 1, key);
         else *c.abort = 1;
       }
       ++c.v_token;

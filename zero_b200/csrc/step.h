@@ -27,6 +27,8 @@ struct StageDesc {
   uint32_t gbytes;                  // slot offset of the unit's second group
   uint32_t layer;                   // STG_ATTN
   uint32_t in_buf, out_buf;         // StepBuf of the input / output vector
+  uint32_t out_row0;                // first row of this rank's slice in the output vector
+  uint32_t bcast;                   // 1: store the output into every rank's copy (tensor parallel)
   uint32_t pad;
   const uint8_t *w;
   uint64_t gstride, wbytes;
@@ -45,6 +47,14 @@ enum StepBuf : uint32_t { BUF_HIDDEN = 0, BUF_QKV = 1, BUF_ATTN = 2, BUF_ACT = 3
 constexpr int kStepBufs = 5;
 
 enum StepMode : uint32_t { STEP_GENERATE = 0, STEP_FORWARD = 1, STEP_LM = 2 };
+
+// Tensor parallelism: ranks of one model, each running the step kernel on
+// its own GPU over its slice of every stage's output rows.
+constexpr uint32_t kMaxRanks = 8;
+// Per-rank argmax slot of the LM head: {key, version} (8-byte words).
+struct ArgSlot {
+  unsigned long long key, ver;
+};
 
 struct StepParams {
   const StageDesc *stages;
@@ -73,6 +83,15 @@ struct StepParams {
   uint32_t xbytes, part_bytes, hown_off, ring_off, smem_bytes;
   uint32_t hown_units, hown_rows;  // residual rows kept per CTA (units of 8 rows)
   uint32_t hid_row0;               // first hidden row of this rank's residual slice (0 on one GPU)
+  uint32_t rank, world;            // tensor-parallel rank / ranks (0 / 1 on one GPU)
+  uint32_t attn_out_off;           // words: this rank's first q head in the attention vector
+  uint32_t pad2;
+  // device tables (world > 1): peer_tv[d * kStepBufs + b] = rank d's tagged
+  // vector b; peer_arg[d] = rank d's argmax slots [kMaxRanks]; attn_dst[d] =
+  // rank d's attention vector at this rank's heads
+  unsigned long long *const *peer_tv;
+  ArgSlot *const *peer_arg;
+  unsigned long long *const *attn_dst;
   uint32_t stages_off, n_stages;   // shared-memory copy of the stage list
 };
 
