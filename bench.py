@@ -62,7 +62,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the per-token C-ABI loop")
     ap.add_argument("--no-roofline", action="store_true", help="skip the standalone GEMV sweep")
-    ap.add_argument("--workload", default="qwen3", choices=["qwen3", "ds2", "prefill"],
+    ap.add_argument("--workload", default="qwen3", choices=["qwen3", "ds2", "prefill", "qwen3-8b"],
                     help="qwen3: BASELINE config 0 (the headline); ds2: the config-3 DeepSeek2 "
                          "MLA+MoE model, one sequence, as a secondary line")
     ap.add_argument("--context", type=int, default=2048, help="ds2: tokens in the cache before decode")
@@ -173,6 +173,26 @@ def cpu_decode(cfg, weights, prompt, steps: int, threads: int):
     import oracle as O
 
     r = O.OracleRun(cfg, weights, PROMPT_LEN + steps + 2, order=O.ORDER_AVX512, threads=threads)
+    for i, t in enumerate(prompt):
+        r.forward(int(t), i)
+    rc, tok, _ = r.lm_head()
+    pos = len(prompt)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        r.forward(tok, pos)
+        rc, tok, _ = r.lm_head()
+        pos += 1
+    dt = time.perf_counter() - t0
+    r.close()
+    return steps / dt, dt
+
+
+def cpu_decode_sample(cfg, weights, prompt, steps: int, threads: int):
+    """The reference's decode loop on the CPU oracle (AVX-512 order) for a
+    short prompt: tok/s of `steps` decode steps after it."""
+    import oracle as O
+
+    r = O.OracleRun(cfg, weights, len(prompt) + steps + 2, order=O.ORDER_AVX512, threads=threads)
     for i, t in enumerate(prompt):
         r.forward(int(t), i)
     rc, tok, _ = r.lm_head()
@@ -312,6 +332,134 @@ def run_ds2(args, rank, world, local):
     ctx.close()
 
 
+TP_METRIC = "decode tok/s, Qwen3-8B-shape Q4_0 b=1, context 4096, tensor parallel over N GPUs"
+TP_CONTEXT = 4096
+
+
+def run_qwen3_tp(args, rank, world, local):
+    """BASELINE config 2 at batch 1: the Qwen3-8B shape, the cache filled to
+    4096 seeded tokens, then K greedy steps, tensor parallel over the N GPUs
+    of the launch (one rank per GPU; at N = 1 the plain one-GPU model).  The
+    stage outputs cross NVLink inside the persistent step kernel (peer stores
+    of tagged words), so a step is one kernel per GPU.  Strong scaling: one
+    sequence, its weights split N ways."""
+    from zero_b200 import synth
+
+    cfg = synth.QWEN3_8B
+    n_cpu_prompt, n_cpu_gen = 4, 4
+    if args.impl == "reference":
+        if rank == 0:
+            weights = synth.qwen3_weights(cfg, seed=SEED, x4=False)
+            prompt = synth.prompt_ids(cfg, n_cpu_prompt, seed=SEED)
+            cores = physical_cores()
+            tok_s, dt = cpu_decode_sample(cfg, weights, prompt, n_cpu_gen, cores)
+            print(json.dumps({
+                "impl": "reference", "metric": TP_METRIC, "value": round(tok_s, 3), "unit": "tok/s",
+                "n_gpus": args.gpus, "steps": n_cpu_gen, "warmup": 0, "ms_per_step": round(1000 * dt / n_cpu_gen, 3),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded random-init .smodel v2 weights, BASELINE config 2 shapes)",
+                "config": {"workload": "qwen3-8b-shape q4_0 decode b=1 (BASELINE config 2)",
+                           "parallelism": "cpu threads"},
+                "cpu_baseline": {"value": round(tok_s, 3), "unit": "tok/s", "cores": cores, "kind": "port",
+                                 "sample": f"{n_cpu_gen} decode steps after a {n_cpu_prompt}-token prompt "
+                                           f"(context <= {n_cpu_prompt + n_cpu_gen}, not 4096)"},
+                "e2e": {"value": round(tok_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import zero_b200 as zb
+    from zero_b200 import tp
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    weights = synth.qwen3_weights(cfg, seed=SEED)
+    prompt = synth.prompt_ids(cfg, TP_CONTEXT, seed=SEED)
+    ctx = zb.Context(device=local)
+    model = zb.Qwen3Model(ctx, cfg, weights, rank=rank, world=world)
+    del weights
+    if world > 1:
+        tp.connect(model)
+    max_tokens = TP_CONTEXT + args.steps + 2
+    kv = model.new_kv(max_tokens)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    model.generate_greedy(kv, prompt[:16], args.warmup + 1)      # warm-up
+    barrier()
+    with ClockSampler(physical_gpu_index(local)) as clocks:
+        t0 = time.perf_counter()
+        toks, _ = model.generate_greedy(kv, prompt, args.steps + 1)
+        wall = time.perf_counter() - t0
+        barrier()
+    perf = model.perf()
+    dec_ms = max_over_ranks(float(perf["decode_ms"]))
+    fill_ms = max_over_ranks(float(perf["prefill_ms"]))
+    wall = max_over_ranks(wall)
+    tok_s = args.steps / (dec_ms / 1000.0)
+    peaks = measured_peaks()
+    # per GPU and step: its weight slice (1/N of the 4.57 GB; the embedding row
+    # and norms are whole on every rank) and its kv heads' rows of the cache
+    step_bytes = cfg.weight_bytes_per_token() / world
+    kv_row_bytes = 2 * (cfg.n_kv_heads // world) * cfg.head_dim * 4 * cfg.n_layers
+    kv_bytes = sum(kv_row_bytes * (TP_CONTEXT + i + 1) for i in range(args.steps))
+    launch_bytes = args.steps * step_bytes + kv_bytes
+    gbs = launch_bytes / (dec_ms / 1000.0) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        del model, kv
+        w_plain = synth.qwen3_weights(cfg, seed=SEED, x4=False)
+        c_tok_s, c_dt = cpu_decode_sample(cfg, w_plain, prompt[:n_cpu_prompt], n_cpu_gen, physical_cores())
+        cpu = {"value": round(c_tok_s, 3), "unit": "tok/s", "cores": physical_cores(), "kind": "port",
+               "sample": f"{n_cpu_gen} decode steps after a {n_cpu_prompt}-token prompt (context <= "
+                         f"{n_cpu_prompt + n_cpu_gen}, not {TP_CONTEXT}), AVX-512-order restatement, {c_dt:.1f} s"}
+    if rank == 0:
+        line = {
+            "metric": TP_METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dec_ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random-init .smodel v2 weights, BASELINE config 2 shapes)",
+            "config": {"workload": "qwen3-8b-shape q4_0 decode b=1 (BASELINE config 2)",
+                       "context": TP_CONTEXT, "decode_steps": args.steps, "layers": cfg.n_layers,
+                       "hidden": cfg.hidden, "ffn": cfg.ffn, "batch": 1,
+                       "parallelism": f"tp{world}" if world > 1 else "single GPU",
+                       "context_fill_ms": round(fill_ms, 1),
+                       "l2": "inputs larger than L2 (4.57 GB of weights / N per GPU per step)",
+                       "tokens_first": [int(v) for v in toks[:4]]},
+            "roofline": {"bound": "hbm", "kernel": "persistent step kernel (all decode steps, one launch per GPU)",
+                         "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
+                         "per": "GPU", "traffic": None, "algorithmic_bytes": int(launch_bytes)},
+            "e2e": {"value": round((TP_CONTEXT + args.steps) / wall, 2), "unit": "tok/s",
+                    "scope": f"zgpu_generate_greedy wall clock: {TP_CONTEXT}-token context fill + "
+                             f"{args.steps} greedy steps, tokens processed per second",
+                    "h2d_bytes_per_step": 4 * TP_CONTEXT // (TP_CONTEXT + args.steps),
+                    "d2h_bytes_per_step": 4},
+            "gpu_launches": int(perf["decode_launches"]),
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+
+
 PREFILL_METRIC = "prefill tok/s, Qwen3-1.7B-shape Q4_0, 2048-token prompt; int8 tensor-core TOPS"
 PREFILL_LEN = 2048
 
@@ -444,6 +592,9 @@ def main():
 
             torch.cuda.set_device(local)
         run_ds2(args, rank, world, local)
+        return
+    if args.workload == "qwen3-8b":
+        run_qwen3_tp(args, rank, world, local)
         return
     if args.workload == "prefill":
         if args.impl != "reference":

@@ -758,12 +758,15 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const StepParams 
   uint64_t *full = reinterpret_cast<uint64_t *>(ring + static_cast<size_t>(kNW) * kSlots * kSlotBytes);
   uint64_t *empty = full + kNW * kSlots;
   // the stage list, read at every stage boundary, lives in shared memory
-  StageDesc *stages = reinterpret_cast<StageDesc *>(smem + P.stages_off);
-  {
+  // unless it did not fit there
+  const StageDesc *stages = P.stages;
+  if (P.stages_off != kStagesInGlobal) {
+    StageDesc *sm = reinterpret_cast<StageDesc *>(smem + P.stages_off);
     const uint32_t words = P.n_stages * static_cast<uint32_t>(sizeof(StageDesc) / 4);
     const uint32_t *src = reinterpret_cast<const uint32_t *>(P.stages);
-    uint32_t *dst = reinterpret_cast<uint32_t *>(stages);
+    uint32_t *dst = reinterpret_cast<uint32_t *>(sm);
     for (uint32_t i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+    stages = sm;
   }
   if (threadIdx.x == 0) {
     for (uint32_t i = 0; i < kNW * kSlots; ++i) {
@@ -843,14 +846,18 @@ bool step_geometry(const StageDesc *stages, uint32_t n, uint32_t grid, StepParam
   part = (part + 127) & ~size_t(127);
   const size_t hown_off = xbytes + part;
   const size_t stages_off = hown_off + hown;
-  const size_t stages_bytes = (static_cast<size_t>(n) * sizeof(StageDesc) + 127) & ~size_t(127);
+  size_t stages_bytes = (static_cast<size_t>(n) * sizeof(StageDesc) + 127) & ~size_t(127);
+  const size_t ring_bytes = static_cast<size_t>(kNW) * kSlots * kSlotBytes + 2 * kNW * kSlots * 8;
+  // the stage list is copied to shared memory where it fits, else read from
+  // global memory (one broadcast read per stage)
+  if (stages_off + stages_bytes + ring_bytes > kStepDynSmemMax) stages_bytes = 0;
   const size_t ring_off = stages_off + stages_bytes;
-  const size_t smem = ring_off + static_cast<size_t>(kNW) * kSlots * kSlotBytes + 2 * kNW * kSlots * 8;
+  const size_t smem = ring_off + ring_bytes;
   if (smem > kStepDynSmemMax) return false;
   p->xbytes = static_cast<uint32_t>(xbytes);
   p->part_bytes = static_cast<uint32_t>(part);
   p->hown_off = static_cast<uint32_t>(hown_off);
-  p->stages_off = static_cast<uint32_t>(stages_off);
+  p->stages_off = stages_bytes ? static_cast<uint32_t>(stages_off) : kStagesInGlobal;
   p->n_stages = n;
   p->hown_units = hunits;
   p->hown_rows = static_cast<uint32_t>((static_cast<size_t>(hunits) + grid - 1) / grid * 8);

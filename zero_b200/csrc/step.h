@@ -46,6 +46,8 @@ enum StepBuf : uint32_t { BUF_HIDDEN = 0, BUF_QKV = 1, BUF_ATTN = 2, BUF_ACT = 3
                           BUF_NONE = 5 };
 constexpr int kStepBufs = 5;
 
+constexpr uint32_t kStagesInGlobal = 0xFFFFFFFFu;
+
 enum StepMode : uint32_t { STEP_GENERATE = 0, STEP_FORWARD = 1, STEP_LM = 2 };
 
 // Tensor parallelism: ranks of one model, each running the step kernel on
@@ -92,7 +94,7 @@ struct StepParams {
   unsigned long long *const *peer_tv;
   ArgSlot *const *peer_arg;
   unsigned long long *const *attn_dst;
-  uint32_t stages_off, n_stages;   // shared-memory copy of the stage list
+  uint32_t stages_off, n_stages;   // shared-memory copy of the stage list (kStagesInGlobal: none)
 };
 
 // Version advances of the tagged vectors for one step (what the kernel
