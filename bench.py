@@ -66,6 +66,7 @@ def parse():
                     help="qwen3: BASELINE config 0 (the headline); ds2: the config-3 DeepSeek2 "
                          "MLA+MoE model, one sequence, as a secondary line")
     ap.add_argument("--context", type=int, default=2048, help="ds2: tokens in the cache before decode")
+    ap.add_argument("--batch", type=int, default=1, help="prefill: prompts per step (BASELINE config 4: 1 or 8)")
     return ap.parse_args()
 
 
@@ -518,27 +519,36 @@ def run_prefill(args, rank, world, local):
     import zero_b200 as zb
 
     weights = synth.qwen3_weights(cfg, seed=SEED)
-    prompt = synth.prompt_ids(cfg, PREFILL_LEN, seed=SEED)
+    B = args.batch
+    prompts = np.stack([synth.prompt_ids(cfg, PREFILL_LEN, seed=SEED + i) for i in range(B)])
+    prompt = prompts[0]
     ctx = zb.Context(device=local)
     model = zb.Qwen3Model(ctx, cfg, weights)
-    kv = model.new_kv(PREFILL_LEN + 8)
+    kvs = [model.new_kv(PREFILL_LEN + 8) for _ in range(B)]
+    kv = kvs[0]
+
+    def one_step():
+        if B == 1:
+            return model.prefill(kv, prompt, want_logits=False)[0]
+        return int(model.prefill_batch(kvs, prompts, want_logits=False)[0][0])
+
     for _ in range(args.warmup):
-        model.prefill(kv, prompt, want_logits=False)
+        one_step()
     torch.cuda.synchronize()
     dev_ms, gemm_ms, attn_ms, wall = [], [], [], []
     with ClockSampler(physical_gpu_index(local)) as clocks:
         for _ in range(args.steps):
             t0 = time.perf_counter()
-            tok, _ = model.prefill(kv, prompt, want_logits=False)
+            tok = one_step()
             wall.append(time.perf_counter() - t0)
             p = model.perf()
             dev_ms.append(p["prefill_ms"])
             gemm_ms.append(p["prefill_gemm_ms"])
             attn_ms.append(p["prefill_attn_ms"])
     launches = int(model.perf()["kernel_launches"])
-    tok_s = PREFILL_LEN / (statistics.mean(dev_ms) / 1000.0)
-    e2e_tok_s = PREFILL_LEN * args.steps / sum(wall)
-    ops = prefill_gemm_ops(cfg, PREFILL_LEN)
+    tok_s = B * PREFILL_LEN / (statistics.mean(dev_ms) / 1000.0)
+    e2e_tok_s = B * PREFILL_LEN * args.steps / sum(wall)
+    ops = prefill_gemm_ops(cfg, B * PREFILL_LEN)
     g_ms = statistics.mean(gemm_ms)
     tops = ops / (g_ms / 1000.0) / 1e12
     peaks = measured_peaks()
@@ -558,8 +568,8 @@ def run_prefill(args, rank, world, local):
             "ms_per_step": round(statistics.mean(dev_ms), 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> int32 (Q8_0 x Q4_0), f32 elsewhere",
             "data": "synthetic (seeded random-init .smodel v2 weights, BASELINE config 4)",
-            "config": {"workload": "qwen3-1.7b-shape q4_0 prefill b=1 (BASELINE config 4)",
-                       "prompt": PREFILL_LEN, "batch": 1, "layers": cfg.n_layers,
+            "config": {"workload": f"qwen3-1.7b-shape q4_0 prefill b={B} (BASELINE config 4)",
+                       "prompt": PREFILL_LEN, "batch": B, "layers": cfg.n_layers,
                        "l2": "inputs larger than L2 (793 MB of projection weights per prefill)",
                        "parallelism": "single GPU", "next_token": int(tok),
                        "gemm_ms": round(g_ms, 3), "attention_ms": round(statistics.mean(attn_ms), 3),
@@ -571,14 +581,15 @@ def run_prefill(args, rank, world, local):
                                         f"twice the bf16 rate",
                          "traffic": None, "algorithmic_ops": ops,
                          "avg_launch_us": round(g_ms * 1000 / (4 * cfg.n_layers), 2)},
-            "e2e": {"value": round(e2e_tok_s, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * PREFILL_LEN,
-                    "d2h_bytes_per_step": 8},
+            "e2e": {"value": round(e2e_tok_s, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * PREFILL_LEN * B,
+                    "d2h_bytes_per_step": 4 * B},
             "gpu_launches": launches,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
-    kv.close()
+    for k in kvs:
+        k.close()
     model.close()
     ctx.close()
 

@@ -320,6 +320,14 @@ zgpu_status zgpu_generate_greedy(zgpu_model *m, zgpu_kv *kv, const uint32_t *pro
  * multiples of 128.  zgpu_perf_snapshot's prefill_ms gives the device time. */
 zgpu_status zgpu_prefill(zgpu_model *m, zgpu_kv *kv, const uint32_t *tokens, uint32_t n,
                          uint32_t *token_out, float *logits_out);
+/* zgpu_prefill for n_seq prompts of n tokens each at once (BASELINE config 4
+ * batch 8): sequence i's ids at tokens[i*n .. i*n+n), its cache kvs[i] (one
+ * distinct cache per sequence), its next token in tokens_out[i] and (when
+ * logits_out is non-NULL) its logits at logits_out[i*vocab_padded].  The
+ * projections run over all n_seq*n rows; every result equals a one-sequence
+ * zgpu_prefill of that prompt bit for bit. */
+zgpu_status zgpu_prefill_batch(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, const uint32_t *tokens,
+                               uint32_t n, uint32_t *tokens_out, float *logits_out);
 
 /* Per-kernel-class counters, mirroring Avx512PerfCounters
  * (inference_avx512.rs:274-330): calls and device milliseconds of the last

@@ -140,3 +140,34 @@ def test_causal_attention_matches_float64(ctx, n_q, n_kv, T, pos0):
     err = float(np.abs(out - ref).max() / np.abs(ref).max())
     assert err < 2e-5, err
     kv.close()
+
+
+def test_prefill_batch_equals_single_prefills():
+    """zgpu_prefill_batch (BASELINE config 4's batch form): the projections run
+    over all sequences' rows at once, attention and the cache per sequence;
+    tokens, logits and every cache equal one-sequence prefills bit for bit."""
+    cfg = synth.small_config(n_layers=2, hidden=512, ffn=1024, n_q=8, n_kv=2, vocab=1024)
+    ctx = zb.Context()
+    w = synth.qwen3_weights(cfg, seed=5, norm_sigma=0.1)
+    m = zb.Qwen3Model(ctx, cfg, w)
+    n_seq, n = 3, 150
+    prompts = np.stack([synth.prompt_ids(cfg, n, seed=100 + i) for i in range(n_seq)])
+    kvs = [m.new_kv(n + 4) for _ in range(n_seq)]
+    toks, logits = m.prefill_batch(kvs, prompts)
+    for i in range(n_seq):
+        kv1 = m.new_kv(n + 4)
+        t1, l1 = m.prefill(kv1, prompts[i])
+        assert toks[i] == t1
+        assert np.array_equal(logits[i].view(np.uint32), l1.view(np.uint32))
+        for layer in range(cfg.n_layers):
+            ka, va = kvs[i].read(layer, n)
+            kb, vb = kv1.read(layer, n)
+            assert np.array_equal(ka.view(np.uint32), kb.view(np.uint32))
+            assert np.array_equal(va.view(np.uint32), vb.view(np.uint32))
+        kv1.close()
+    with pytest.raises(zb.ZgpuError):
+        m.prefill_batch([kvs[0], kvs[0]], prompts[:2])   # one cache per sequence
+    for kv in kvs:
+        kv.close()
+    m.close()
+    ctx.close()

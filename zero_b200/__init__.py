@@ -341,6 +341,18 @@ class Qwen3Model:
                                          _ptr(logits) if want_logits else None))
         return tok.value, logits
 
+    def prefill_batch(self, kvs, prompts, want_logits: bool = True):
+        """zgpu_prefill_batch: prompts [n_seq, n] (equal lengths), one cache per
+        sequence; returns (next tokens [n_seq], logits [n_seq, vocab] or None)."""
+        t = np.ascontiguousarray(prompts, np.uint32)
+        n_seq, n = t.shape
+        handles = (C.c_void_p * n_seq)(*[kv.h.value if isinstance(kv.h, C.c_void_p) else kv.h for kv in kvs])
+        toks = np.empty(n_seq, np.uint32)
+        logits = np.empty((n_seq, self.cfg.vocab_padded), np.float32) if want_logits else None
+        self.ctx._check(LIB.zgpu_prefill_batch(self.h, handles, n_seq, _ptr(t), n, _ptr(toks),
+                                               _ptr(logits) if want_logits else None))
+        return toks, logits
+
     def perf(self) -> dict:
         p = ZgpuPerf()
         self.ctx._check(LIB.zgpu_perf_snapshot(self.h, C.byref(p)))

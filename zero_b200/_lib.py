@@ -108,6 +108,7 @@ _SIGS = {
     "zgpu_lm_head_argmax": (_i32, [_vp, _u32, _vp, _vp]),
     "zgpu_generate_greedy": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp, _vp]),
     "zgpu_perf_snapshot": (_i32, [_vp, C.POINTER(ZgpuPerf)]),
+    "zgpu_prefill_batch": (_i32, [_vp, _vp, _u32, _vp, _u32, _vp, _vp]),
     "zgpu_prefill": (_i32, [_vp, _vp, _vp, _u32, _vp, _vp]),
     "zgpu_moe_route_f32": (_i32, [_vp, _vp, _vp, _vp, _u64, _u32, _u32, _u32, _f, _vp, _vp, _vp]),
     "zgpu_mla_kv_create": (_i32, [_vp, _u32, _u32, _u32, _u32, C.POINTER(_vp)]),

@@ -1127,25 +1127,43 @@ extern "C" {
 // matmul inputs to Q8_0, so its KV cache and logits agree to that rounding,
 // not bit for bit.  Fills cache positions [0, n) and returns the LM-head
 // argmax after the last prompt token (lm_head.rs:98-166).
-zgpu_status zgpu_prefill(zgpu_model *m, zgpu_kv *kv, const uint32_t *tokens, uint32_t n, uint32_t *token_out,
-                         float *logits_out) {
-  if (!m || !kv || !tokens || !token_out || n == 0) return ZGPU_ERR_INVALID_ARG;
+}  // extern "C"
+
+namespace {
+
+// Token-parallel prefill of n_seq prompts of n tokens each (sequence i's
+// tokens at tokens[i*n ..], its cache kvs[i]).  Embedding, RMSNorm + Q8_0,
+// the projections and SwiGLU run over all n_seq * n rows at once; QK-norm /
+// RoPE / KV append and the causal attention run per sequence into its own
+// cache; the LM head runs on each sequence's last token.  Every row is
+// computed exactly as a one-sequence prefill computes it.
+zgpu_status prefill_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, const uint32_t *tokens, uint32_t n,
+                        uint32_t *tokens_out, float *logits_out) {
+  if (!m || !kvs || !tokens || !tokens_out || n == 0 || n_seq == 0) return ZGPU_ERR_INVALID_ARG;
   if (m->world > 1)
     return zgpu_fail(m->ctx, ZGPU_ERR_INVALID_ARG, "tensor-parallel ranks decode through zgpu_generate_greedy");
   zgpu_ctx *ctx = m->ctx;
   cudaSetDevice(ctx->device);
   const zgpu_qwen3_desc &d = m->desc;
-  zgpu_status st = prepare_kv(m, kv);
-  if (st) return st;
-  if (n > kv->max_tokens) return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "prompt longer than the cache");
-  for (uint32_t i = 0; i < n; ++i)
+  zgpu_status st;
+  for (uint32_t i = 0; i < n_seq; ++i) {
+    if (!kvs[i]) return ZGPU_ERR_INVALID_ARG;
+    if ((st = prepare_kv(m, kvs[i]))) return st;
+    if (n > kvs[i]->max_tokens)
+      return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "prompt longer than the cache");
+    for (uint32_t j = 0; j < i; ++j)
+      if (kvs[j] == kvs[i]) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "prefill: one cache per sequence");
+  }
+  const uint64_t NT = static_cast<uint64_t>(n_seq) * n;   // rows through the projections
+  if (NT > 0xFFFFFFFFull / 16) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "prefill: too many tokens");
+  for (uint64_t i = 0; i < NT; ++i)
     if (tokens[i] >= d.vocab_padded) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "prompt id beyond the vocab");
   const uint32_t H = d.hidden, F = d.ffn, QD = m->q_dim, KVD = m->kv_dim, QKV = QD + 2 * KVD;
   if (H % 128 || QKV % 128 || (2 * F) % 128 || QD % 32 || F % 32)
     return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "prefill: projection rows must be multiples of 128");
-  // scratch: tokens | hidden [n][H] | qkv [n][QKV] | qrot [n][QD] | attn [n][QD] | gu [n][2F] | act [n][F]
-  //          | q8 [n][maxK] int8 | d8 [n][maxK/32] f32
-  const size_t N = n, maxk = std::max(std::max(H, QD), F);
+  // scratch: tokens | hidden [NT][H] | qkv [NT][QKV] | qrot [NT][QD] | attn [NT][QD] | gu [NT][2F] | act [NT][F]
+  //          | q8 [NT][maxK] int8 | d8 [NT][maxK/32] f32
+  const size_t N = NT, maxk = std::max(std::max(H, QD), F);
   auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
   const size_t o_tok = 0, o_hid = al(N * 4), o_qkv = o_hid + al(N * H * 4), o_qr = o_qkv + al(N * QKV * 4),
                o_at = o_qr + al(N * QD * 4), o_gu = o_at + al(N * QD * 4), o_act = o_gu + al(N * 2 * F * 4),
@@ -1167,7 +1185,7 @@ zgpu_status zgpu_prefill(zgpu_model *m, zgpu_kv *kv, const uint32_t *tokens, uin
   float *d8 = reinterpret_cast<float *>(B + o_d8);
   cudaStream_t s = ctx->stream;
   uint32_t launches = 0;
-  // an event pair around every GEMM and attention launch: per-class device time
+  // an event pair around every GEMM and attention phase: per-class device time
   const size_t n_ev = static_cast<size_t>(d.n_layers) * 10;
   while (m->pf_ev.size() < n_ev) {
     cudaEvent_t ev;
@@ -1183,7 +1201,7 @@ zgpu_status zgpu_prefill(zgpu_model *m, zgpu_kv *kv, const uint32_t *tokens, uin
     p.gstride = gstride;
     p.rows = rows;
     p.bpr = in_dim / 32;
-    p.T = n;
+    p.T = static_cast<uint32_t>(NT);
     p.ldy = rows;
     p.xq = q8;
     p.xs = d8;
@@ -1200,45 +1218,57 @@ zgpu_status zgpu_prefill(zgpu_model *m, zgpu_kv *kv, const uint32_t *tokens, uin
   cudaEventRecord(m->ev[0], s);
   if (e == cudaSuccess)
     e = launch_rows_embed(m->emb->d, m->emb->gstride, m->emb->quant, H, static_cast<uint32_t>(m->emb->rows), d_tok,
-                          n, hid, m->d_status, s), ++launches;
+                          static_cast<uint32_t>(NT), hid, m->d_status, s), ++launches;
   const float scale = 1.0f / sqrtf(static_cast<float>(d.head_dim));
+  const uint32_t T = static_cast<uint32_t>(NT);
   for (uint32_t l = 0; l < d.n_layers && e == cudaSuccess; ++l) {
-    float *kvl = kv->d + static_cast<size_t>(l) * 2 * kv->block;
-    if ((e = launch_rows_rmsnorm_quant(hid, norm_attn(m, l), d.rms_eps, n, H, q8, d8, m->d_status, s))) break;
+    if ((e = launch_rows_rmsnorm_quant(hid, norm_attn(m, l), d.rms_eps, T, H, q8, d8, m->d_status, s))) break;
     if ((e = gemm(m->qkv[l], m->gs_h, QKV, H, qkv, false))) break;
-    if ((e = launch_qk_rope_kv(qkv, norm_q(m, l), norm_k(m, l), m->d_inv_freqs, kvl, kv->block, d.n_q_heads,
-                               d.n_kv_heads, 0, n, d.rms_eps, qr, s)))
-      break;
+    for (uint32_t i = 0; i < n_seq && e == cudaSuccess; ++i, ++launches) {
+      float *kvl = kvs[i]->d + static_cast<size_t>(l) * 2 * kvs[i]->block;
+      const size_t r0 = static_cast<size_t>(i) * n;
+      e = launch_qk_rope_kv(qkv + r0 * QKV, norm_q(m, l), norm_k(m, l), m->d_inv_freqs, kvl, kvs[i]->block,
+                            d.n_q_heads, d.n_kv_heads, 0, n, d.rms_eps, qr + r0 * QD, s);
+    }
+    if (e) break;
     mark();
-    e = launch_causal_attn(qr, kvl, kv->block, d.n_q_heads, d.n_kv_heads, 0, n, scale, at, m->d_status, s);
+    for (uint32_t i = 0; i < n_seq && e == cudaSuccess; ++i, ++launches) {
+      float *kvl = kvs[i]->d + static_cast<size_t>(l) * 2 * kvs[i]->block;
+      const size_t r0 = static_cast<size_t>(i) * n;
+      e = launch_causal_attn(qr + r0 * QD, kvl, kvs[i]->block, d.n_q_heads, d.n_kv_heads, 0, n, scale, at + r0 * QD,
+                             m->d_status, s);
+    }
     mark();
     if (e) break;
     if ((e = launch_quantize_q8_0_planar(at, q8, d8, N * QD, m->d_status, s))) break;
     if ((e = gemm(m->o[l]->d, m->o[l]->gstride, H, QD, hid, true))) break;
-    if ((e = launch_rows_rmsnorm_quant(hid, norm_ffn(m, l), d.rms_eps, n, H, q8, d8, m->d_status, s))) break;
+    if ((e = launch_rows_rmsnorm_quant(hid, norm_ffn(m, l), d.rms_eps, T, H, q8, d8, m->d_status, s))) break;
     if ((e = gemm(m->gateup[l], m->gs_h, 2 * F, H, gu, false))) break;
-    if ((e = launch_swiglu_rows(gu, act, n, F, s))) break;
+    if ((e = launch_swiglu_rows(gu, act, T, F, s))) break;
     if ((e = launch_quantize_q8_0_planar(act, q8, d8, N * F, m->d_status, s))) break;
     if ((e = gemm(m->down[l]->d, m->down[l]->gstride, H, F, hid, true))) break;
-    launches += 7;
+    launches += 5;
   }
   cudaEventRecord(m->ev[1], s);
   if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "prefill");
-  // LM head on the last prompt token's hidden state
+  // LM head on each sequence's last prompt token
   cudaError_t e2 = grow(&m->d_prompt, &m->prompt_cap, 1);
   if (e2 == cudaSuccess) e2 = grow(&m->d_tokens, &m->tokens_cap, 1);
   if (e2 != cudaSuccess) return zgpu_cuda_fail(ctx, e2, "state buffers");
-  if ((st = set_state(m, 1, n - 1, d.vocab_real, 1))) return st;
-  e = cudaMemcpyAsync(m->d_hidden, hid + N * H - H, H * 4, cudaMemcpyDeviceToDevice, s);
-  if (e == cudaSuccess) e = enqueue_lm_head(m, &launches);
-  m->last_fwd_persistent = false;
-  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "prefill lm head");
-  if (logits_out)
-    if ((e = cudaMemcpyAsync(logits_out, m->d_logits, static_cast<size_t>(d.vocab_padded) * 4,
-                             cudaMemcpyDeviceToHost, s)) != cudaSuccess)
-      return zgpu_cuda_fail(ctx, e, "logits d2h");
-  if ((e = cudaMemcpyAsync(token_out, m->d_tokens, 4, cudaMemcpyDeviceToHost, s)) != cudaSuccess)
-    return zgpu_cuda_fail(ctx, e, "token d2h");
+  const size_t V = d.vocab_padded;
+  for (uint32_t i = 0; i < n_seq; ++i) {
+    if ((st = set_state(m, 1, n - 1, d.vocab_real, 1))) return st;
+    e = cudaMemcpyAsync(m->d_hidden, hid + (static_cast<size_t>(i) * n + n - 1) * H, H * 4, cudaMemcpyDeviceToDevice,
+                        s);
+    if (e == cudaSuccess) e = enqueue_lm_head(m, &launches);
+    m->last_fwd_persistent = false;
+    if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "prefill lm head");
+    if (logits_out)
+      if ((e = cudaMemcpyAsync(logits_out + i * V, m->d_logits, V * 4, cudaMemcpyDeviceToHost, s)) != cudaSuccess)
+        return zgpu_cuda_fail(ctx, e, "logits d2h");
+    if ((e = cudaMemcpyAsync(tokens_out + i, m->d_tokens, 4, cudaMemcpyDeviceToHost, s)) != cudaSuccess)
+      return zgpu_cuda_fail(ctx, e, "token d2h");
+  }
   uint32_t sw = 0;
   if ((st = read_status(m, &sw))) return st;
   float ms = 0.f;
@@ -1262,6 +1292,21 @@ zgpu_status zgpu_prefill(zgpu_model *m, zgpu_kv *kv, const uint32_t *tokens, uin
   m->perf.decode_launches = 0;
   ctx->launches += launches;
   return map_status(ctx, sw);
+}
+
+}  // namespace
+
+extern "C" {
+
+zgpu_status zgpu_prefill(zgpu_model *m, zgpu_kv *kv, const uint32_t *tokens, uint32_t n, uint32_t *token_out,
+                         float *logits_out) {
+  if (!kv) return ZGPU_ERR_INVALID_ARG;
+  return prefill_run(m, &kv, 1, tokens, n, token_out, logits_out);
+}
+
+zgpu_status zgpu_prefill_batch(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, const uint32_t *tokens, uint32_t n,
+                               uint32_t *tokens_out, float *logits_out) {
+  return prefill_run(m, kvs, n_seq, tokens, n, tokens_out, logits_out);
 }
 
 }  // extern "C"
