@@ -260,20 +260,42 @@ def run_ds2(args, rank, world, local):
                               "context 2048); see cpu_baseline on the zero_b200 line"}), flush=True)
         return
     cfg = synth.DS2_V2_LITE
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        from zero_b200 import tp
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
     weights = synth.ds2_weights(cfg, seed=SEED)
     prompt = synth.ds2_prompt_ids(cfg, args.context, seed=SEED)
     ctx = zb.Context(device=local)
-    model = zb.Ds2Model(ctx, cfg, weights)
+    # N > 1: expert parallel, experts [r E/N, (r+1) E/N) on rank r (zgpu_ds2_create_ep)
+    model = zb.Ds2Model(ctx, cfg, weights, rank=rank, world=world)
+    if world > 1:
+        tp.connect(model)
     max_tokens = args.context + args.steps + 2
     kv = model.new_kv(max_tokens)
-    torch.cuda.synchronize()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    barrier()
     model.generate_greedy(kv, prompt[: min(len(prompt), 64)], args.warmup + 1)   # warm-up, graphs captured
-    torch.cuda.synchronize()
+    barrier()
     with ClockSampler(physical_gpu_index(local)) as clocks:
         toks, _ = model.generate_greedy(kv, prompt, args.steps + 1)
-        torch.cuda.synchronize()
+        barrier()
     perf = model.perf()
     dec_ms = float(perf["decode_ms"])
+    if world > 1:
+        t = torch.tensor([dec_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dec_ms = float(t.item())
     tok_s = args.steps / (dec_ms / 1000.0)
     # e2e: the per-token C ABI with host token in / token out, a few steps
     n_e2e = min(args.steps, 16)
@@ -283,7 +305,12 @@ def run_ds2(args, rank, world, local):
     for i in range(n_e2e):
         model.forward_single_token(kv, tok, pos + i)
         tok, _ = model.lm_head_argmax(want_logits=False)
-    e2e_tok_s = n_e2e / (time.perf_counter() - t0)
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_tok_s = n_e2e / e2e_s
     peaks = measured_peaks()
     step_w = cfg.weight_bytes_per_token()
     cache_b = sum(cfg.cache_bytes_per_token() * (args.context + i + 1) for i in range(args.steps))
@@ -293,7 +320,7 @@ def run_ds2(args, rank, world, local):
     # (forward_pass.rs:703-909 re-expands every cached latent through kv_b),
     # on a bounded sample: 2 steps after a 4-token prompt on the same weights
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle as O
 
         r = O.OracleDs2Run(cfg, weights, 8)
@@ -305,9 +332,9 @@ def run_ds2(args, rank, world, local):
                          f"restatement, 1 thread, {dt:.1f} s; rc={rc}"}
     if rank == 0:
         line = {
-            "metric": DS2_METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": 1,
+            "metric": DS2_METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dec_ms / args.steps, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init, BASELINE config 3 shapes)",
             "config": {"workload": "deepseek-v2-lite-shape mla+moe q4_0 decode, 1 sequence (BASELINE config 3 model)",
                        "context": args.context, "decode_steps": args.steps, "layers": cfg.n_layers,
@@ -315,8 +342,11 @@ def run_ds2(args, rank, world, local):
                        "q_lora_rank": cfg.q_lora_rank, "batch": 1,
                        "weight_bytes_per_step": step_w,
                        "l2": "inputs larger than L2 (1.5 GB of weights streamed per step)",
-                       "parallelism": "single GPU", "tokens_first": [int(v) for v in toks[:4]]},
+                       "parallelism": f"ep{world} (experts sharded; router, attention, shared experts "
+                                      f"replicated)" if world > 1 else "single GPU",
+                       "tokens_first": [int(v) for v in toks[:4]]},
             "roofline": {"bound": "hbm", "kernel": "per-op decode kernels (whole step, CUDA graph)",
+                         "per": "GPU" if world == 1 else "step (all ranks' bytes over the slowest rank's time)",
                          "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
                          "traffic": None, "algorithmic_bytes": launch_bytes,
@@ -331,6 +361,9 @@ def run_ds2(args, rank, world, local):
     kv.close()
     model.close()
     ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 TP_METRIC = "decode tok/s, Qwen3-8B-shape Q4_0 b=1, context 4096, tensor parallel over N GPUs"

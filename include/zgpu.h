@@ -429,6 +429,23 @@ typedef struct zgpu_ds2_desc {
 
 zgpu_status zgpu_ds2_create(zgpu_ctx *ctx, const zgpu_ds2_desc *desc, zgpu_ds2_model **out);
 void zgpu_ds2_destroy(zgpu_ds2_model *m);
+/* Expert parallelism (experts sharded over 1-8 GPUs, one
+ * process per GPU).  Rank `rank` of `world` runs routed experts
+ * [rank*E/world, (rank+1)*E/world) of every MoE layer (moe_ffn, moe.rs:486-590);
+ * the router, attention, dense layers, shared experts and LM head run on
+ * every rank.  After the grouped expert GEMVs, a rank stores its selected
+ * experts' outputs as tagged words into slot k of every rank's exchange
+ * buffer over NVLink, and every rank's combine waits (bounded) for all top_k
+ * slots and adds them in the reference's k order, so tokens, logits and
+ * expert ids equal the one-GPU model bit for bit.  Requires n_experts to
+ * divide by world.  Bring-up as zgpu_qwen3_create_tp: create every rank,
+ * zgpu_ds2_ep_export on each, exchange the ZGPU_IPC_HANDLE_BYTES handles in
+ * rank order, zgpu_ds2_ep_connect on each; then every rank makes the same
+ * calls (forward, LM head, generate) with the same arguments. */
+zgpu_status zgpu_ds2_create_ep(zgpu_ctx *ctx, const zgpu_ds2_desc *desc, uint32_t rank, uint32_t world,
+                               zgpu_ds2_model **out);
+zgpu_status zgpu_ds2_ep_export(zgpu_ds2_model *m, void *handle_out);
+zgpu_status zgpu_ds2_ep_connect(zgpu_ds2_model *m, const void *handles);
 /* forward_single_token_deepseek2 (forward_pass.rs:703-909) for MLA layers:
  * per layer rmsnorm -> MLA (mla.rs:122-414, with the kv_b projection
  * absorbed into the query and the output: same results to f32 rounding)

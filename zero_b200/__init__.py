@@ -394,7 +394,11 @@ class Ds2Model:
     """A DeepSeek2-shaped (MLA + MoE) model on the device, built from
     synth.ds2_weights() tensors (plain Q4_0 blocks; routers registered f32)."""
 
-    def __init__(self, ctx: Context, cfg: Ds2Config, weights: dict):
+    def __init__(self, ctx: Context, cfg: Ds2Config, weights: dict, rank: int = 0, world: int = 1):
+        """rank / world > 1: one expert-parallel rank (zgpu_ds2_create_ep);
+        call tp_export() on every rank, exchange the handles, then
+        tp_connect(handles) (zero_b200.tp.connect does both) before use."""
+        self.rank, self.world = rank, world
         self.ctx, self.cfg, self.w = ctx, cfg, weights
         H = cfg.hidden
         eq = Q8_0 if cfg.embd_quant == "q8_0" else Q4_0
@@ -419,8 +423,24 @@ class Ds2Model:
             cfg.expert_weight_scale, Q4_0, eq, emb_key, oq, out_key, _ptr(weights["output_norm"]),
             self._layers)
         h = C.c_void_p()
-        ctx._check(LIB.zgpu_ds2_create(ctx.h, C.byref(desc), C.byref(h)))
+        if world == 1:
+            ctx._check(LIB.zgpu_ds2_create(ctx.h, C.byref(desc), C.byref(h)))
+        else:
+            ctx._check(LIB.zgpu_ds2_create_ep(ctx.h, C.byref(desc), rank, world, C.byref(h)))
         self.h = h
+
+    def tp_export(self) -> bytes:
+        """This rank's CUDA IPC handle of its expert exchange buffer (zgpu_ds2_ep_export)."""
+        buf = (C.c_uint8 * IPC_HANDLE_BYTES)()
+        self.ctx._check(LIB.zgpu_ds2_ep_export(self.h, buf))
+        return bytes(buf)
+
+    def tp_connect(self, handles) -> None:
+        """Map every rank's exchange buffer (handles in rank order)."""
+        if len(handles) != self.world or any(len(x) != IPC_HANDLE_BYTES for x in handles):
+            raise ZgpuError(3, "tp_connect: one handle per rank")
+        blob = (C.c_uint8 * (IPC_HANDLE_BYTES * self.world)).from_buffer_copy(b"".join(handles))
+        self.ctx._check(LIB.zgpu_ds2_ep_connect(self.h, blob))
 
     def close(self):
         if getattr(self, "h", None):

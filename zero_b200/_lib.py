@@ -115,6 +115,9 @@ _SIGS = {
     "zgpu_mla_kv_destroy": (None, [_vp]),
     "zgpu_mla_kv_store": (_i32, [_vp, _u32, _u32, _vp, _vp]),
     "zgpu_mla_kv_read": (_i32, [_vp, _u32, _u32, _vp]),
+    "zgpu_ds2_create_ep": (_i32, [_vp, C.POINTER(ZgpuDs2Desc), _u32, _u32, C.POINTER(_vp)]),
+    "zgpu_ds2_ep_export": (_i32, [_vp, _vp]),
+    "zgpu_ds2_ep_connect": (_i32, [_vp, _vp]),
     "zgpu_ds2_create": (_i32, [_vp, C.POINTER(ZgpuDs2Desc), C.POINTER(_vp)]),
     "zgpu_ds2_destroy": (None, [_vp]),
     "zgpu_ds2_forward_single_token": (_i32, [_vp, _vp, _u32, _u32, _vp]),

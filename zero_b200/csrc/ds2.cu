@@ -47,6 +47,8 @@ struct zgpu_mla_kv {
 
 namespace {
 
+constexpr uint32_t kMaxEpRanks = 8;
+
 struct Ds2Layer {
   // attention
   uint8_t *cat_a = nullptr;          // owned: kv_a groups | q_a groups (| one zero group)
@@ -98,6 +100,15 @@ struct zgpu_ds2_model {
   uint32_t step_kernels = 0, fwd_kernels = 0, lm_kernels = 0;
   zgpu_perf perf = {};
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+  // expert parallelism (world > 1): rank `rank` runs routed experts
+  // [rank * ep_per_rank, (rank + 1) * ep_per_rank); everything else is
+  // replicated.  Selected experts' outputs cross over the exchange buffers.
+  uint32_t rank = 0, world = 1, ep_per_rank = 0;
+  unsigned long long *d_xslots = nullptr;   // this rank's exchange buffer [2][top_k][hidden] (tagged)
+  uint32_t *d_ep_seq = nullptr;             // MoE invocations so far (the exchange version)
+  unsigned long long **d_ep_dst = nullptr;  // [world] every rank's exchange buffer
+  std::vector<void *> ipc_opened;
+  bool ep_connected = false;
 };
 
 namespace {
@@ -282,6 +293,8 @@ cudaError_t ds2_enqueue_forward(zgpu_ds2_model *m, zgpu_mla_kv *kv, uint32_t *co
     rp.dn_bytes = m->dn_bytes;
     rp.n_shared = d.n_shared;
     rp.status = m->d_status;
+    rp.ep_rank = m->rank;
+    rp.ep_per_rank = m->world > 1 ? m->ep_per_rank : 0;
     if ((e = launch_moe_route(rp, lc)) != cudaSuccess) return e;
     // grouped gate|up + SiLU*up: segment s = shared s, then the k-th selected expert
     g = GemvDesc();
@@ -321,6 +334,21 @@ cudaError_t ds2_enqueue_forward(zgpu_ds2_model *m, zgpu_mla_kv *kv, uint32_t *co
     io.out = m->d_expout;
     io.status = m->d_status;
     if ((e = launch_gemv(g, PRO_PLAIN, EPI_STORE, io, lc)) != cudaSuccess) return e;
+    if (m->world > 1) {
+      // this rank's selected experts' outputs into every rank's exchange buffer
+      EpPublishParams pp = {};
+      pp.exp_out = m->d_expout;
+      pp.ids = m->d_ids + static_cast<size_t>(l) * d.top_k;
+      pp.dst = m->d_ep_dst;
+      pp.ep_seq = m->d_ep_seq;
+      pp.dim = H;
+      pp.n_shared = d.n_shared;
+      pp.top_k = d.top_k;
+      pp.world = m->world;
+      pp.ep_rank = m->rank;
+      pp.ep_per_rank = m->ep_per_rank;
+      if ((e = launch_moe_ep_publish(pp, lc)) != cudaSuccess) return e;
+    }
     CombineParams cp = {};
     cp.exp_out = m->d_expout;
     cp.weights = m->d_wts + static_cast<size_t>(l) * d.top_k;
@@ -328,7 +356,11 @@ cudaError_t ds2_enqueue_forward(zgpu_ds2_model *m, zgpu_mla_kv *kv, uint32_t *co
     cp.dim = H;
     cp.n_shared = d.n_shared;
     cp.top_k = d.top_k;
+    cp.xslots = m->world > 1 ? m->d_xslots : nullptr;
+    cp.ep_seq = m->d_ep_seq;
+    cp.status = m->d_status;
     if ((e = launch_moe_combine(cp, lc)) != cudaSuccess) return e;
+    if (m->world > 1 && (e = launch_moe_ep_advance(m->d_ep_seq, lc)) != cudaSuccess) return e;
   }
   return cudaSuccess;
 }
@@ -624,12 +656,24 @@ void zgpu_ds2_destroy(zgpu_ds2_model *m) {
   cudaFree(m->d_status);
   for (auto &ev : m->ev)
     if (ev) cudaEventDestroy(ev);
+  for (void *p : m->ipc_opened) cudaIpcCloseMemHandle(p);
+  cudaFree(m->d_xslots);
+  cudaFree(m->d_ep_seq);
+  cudaFree(m->d_ep_dst);
   delete m;
 }
 
-zgpu_status zgpu_ds2_create(zgpu_ctx *ctx, const zgpu_ds2_desc *d, zgpu_ds2_model **out) {
+}  // extern "C"
+
+namespace {
+
+zgpu_status ds2_create(zgpu_ctx *ctx, const zgpu_ds2_desc *d, uint32_t rank, uint32_t world, zgpu_ds2_model **out) {
   if (!ctx || !d || !out || !d->layers || !d->output_norm) return ZGPU_ERR_INVALID_ARG;
   *out = nullptr;
+  if (world == 0 || world > kMaxEpRanks || rank >= world)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "expert parallel: 1..8 ranks");
+  if (world > 1 && (d->n_experts == 0 || d->n_experts % world))
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "expert parallel: n_experts must divide by the ranks");
   cudaSetDevice(ctx->device);
   const uint32_t H = d->hidden, R = d->kv_lora_rank, RD = d->rope_dim, QL = d->q_lora_rank;
   const uint32_t NH = d->n_heads, NO = d->nope_dim, VD = d->v_dim, hq = NO + RD, L_ = d->n_layers;
@@ -810,15 +854,76 @@ zgpu_status zgpu_ds2_create(zgpu_ctx *ctx, const zgpu_ds2_desc *d, zgpu_ds2_mode
   cudaMemset(m->d_ids, 0, L_ * topk * 4);
   cudaMemset(m->d_wts, 0, L_ * topk * 4);
   for (auto &ev : m->ev) cudaEventCreate(&ev);
+  m->rank = rank;
+  m->world = world;
+  m->ep_per_rank = world > 1 ? d->n_experts / world : 0;
+  if (world > 1) {
+    const size_t xw = 2 * static_cast<size_t>(d->top_k) * H;
+    if (cudaMalloc(&m->d_xslots, xw * 8) || cudaMalloc(&m->d_ep_seq, 4))
+      return fail(ZGPU_ERR_OUT_OF_MEMORY, "expert-parallel exchange buffers");
+    cudaMemset(m->d_xslots, 0, xw * 8);
+    cudaMemset(m->d_ep_seq, 0, 4);
+  }
   e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return fail(ZGPU_ERR_CUDA, std::string("ds2 upload: ") + cudaGetErrorString(e));
   *out = m;
   return ZGPU_OK;
 }
 
+}  // namespace
+
+extern "C" {
+
+zgpu_status zgpu_ds2_create(zgpu_ctx *ctx, const zgpu_ds2_desc *d, zgpu_ds2_model **out) {
+  return ds2_create(ctx, d, 0, 1, out);
+}
+
+zgpu_status zgpu_ds2_create_ep(zgpu_ctx *ctx, const zgpu_ds2_desc *d, uint32_t rank, uint32_t world,
+                               zgpu_ds2_model **out) {
+  return ds2_create(ctx, d, rank, world, out);
+}
+
+zgpu_status zgpu_ds2_ep_export(zgpu_ds2_model *m, void *handle_out) {
+  if (!m || !handle_out || m->world < 2 || !m->d_xslots) return ZGPU_ERR_INVALID_ARG;
+  cudaSetDevice(m->ctx->device);
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, m->d_xslots);
+  if (e != cudaSuccess) return zgpu_cuda_fail(m->ctx, e, "expert parallel: export the exchange buffer");
+  std::memcpy(handle_out, &h, sizeof(h));
+  return ZGPU_OK;
+}
+
+zgpu_status zgpu_ds2_ep_connect(zgpu_ds2_model *m, const void *handles) {
+  if (!m || !handles || m->world < 2 || !m->d_xslots) return ZGPU_ERR_INVALID_ARG;
+  if (m->ep_connected) return zgpu_fail(m->ctx, ZGPU_ERR_INVALID_ARG, "expert parallel: already connected");
+  zgpu_ctx *ctx = m->ctx;
+  cudaSetDevice(ctx->device);
+  std::vector<unsigned long long *> dst(m->world, nullptr);
+  for (uint32_t r = 0; r < m->world; ++r) {
+    if (r == m->rank) {
+      dst[r] = m->d_xslots;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, static_cast<const uint8_t *>(handles) + static_cast<size_t>(r) * sizeof(h), sizeof(h));
+    void *p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "expert parallel: open a peer's exchange buffer");
+    m->ipc_opened.push_back(p);
+    dst[r] = static_cast<unsigned long long *>(p);
+  }
+  cudaError_t e = cudaMalloc(&m->d_ep_dst, m->world * sizeof(void *));
+  if (e == cudaSuccess) e = cudaMemcpy(m->d_ep_dst, dst.data(), m->world * sizeof(void *), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "expert parallel: peer table");
+  m->ep_connected = true;
+  return ZGPU_OK;
+}
+
 zgpu_status zgpu_ds2_forward_single_token(zgpu_ds2_model *m, zgpu_mla_kv *kv, uint32_t token,
                                           uint32_t pos, float *hidden_out) {
   if (!m || !kv) return ZGPU_ERR_INVALID_ARG;
+  if (m->world > 1 && !m->ep_connected)
+    return zgpu_fail(m->ctx, ZGPU_ERR_INVALID_ARG, "expert parallel: zgpu_ds2_ep_connect first");
   zgpu_ctx *ctx = m->ctx;
   cudaSetDevice(ctx->device);
   zgpu_status s = ds2_prepare_kv(m, kv);
@@ -901,6 +1006,8 @@ zgpu_status zgpu_ds2_generate_greedy(zgpu_ds2_model *m, zgpu_mla_kv *kv, const u
                                      uint32_t n_prompt, uint32_t n_gen, uint32_t *tokens_out,
                                      float *logits_out) {
   if (!m || !kv || !prompt || !tokens_out || n_prompt == 0 || n_gen == 0) return ZGPU_ERR_INVALID_ARG;
+  if (m->world > 1 && !m->ep_connected)
+    return zgpu_fail(m->ctx, ZGPU_ERR_INVALID_ARG, "expert parallel: zgpu_ds2_ep_connect first");
   zgpu_ctx *ctx = m->ctx;
   cudaSetDevice(ctx->device);
   zgpu_status s = ds2_prepare_kv(m, kv);

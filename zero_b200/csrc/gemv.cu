@@ -131,6 +131,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
       if (p.seg_w) {
         if (p.seg_dynamic) pdl_wait();   // the table is the previous kernel's output
         w = reinterpret_cast<const uint8_t *>(__ldcg(p.seg_w + seg));
+        if (!w) return;   // a segment of no work (another rank's expert)
       }
       uint32_t issued = 0;
       for (uint32_t k = lane, j = 0; k < nitems; k += kWarps, ++j) {
@@ -163,6 +164,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
 
   // ---------------- consumers: prepare the activation image ----------------
   pdl_wait();   // the activations are the previous kernel's output
+  // a zero table entry: the segment does nothing (expert parallelism leaves
+  // another rank's experts out); uniform over the CTA, before any barrier
+  if (p.seg_w && p.seg_dynamic && __ldcg(p.seg_w + seg) == 0ull) return;
   const uint32_t tid = threadIdx.x;
   const uint32_t nf4 = p.in_dim / 4;
   float inv = 1.0f;

@@ -197,8 +197,9 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const RoutePar
       p.seg_dn[s] = p.sh_dn_base + s * p.dn_bytes;
     }
     for (uint32_t i = 0; i < K; ++i) {
-      p.seg_gu[p.n_shared + i] = p.gu_base + idx[i] * p.gu_bytes;
-      p.seg_dn[p.n_shared + i] = p.dn_base + idx[i] * p.dn_bytes;
+      const bool mine = p.ep_per_rank == 0 || idx[i] / p.ep_per_rank == p.ep_rank;
+      p.seg_gu[p.n_shared + i] = mine ? p.gu_base + idx[i] * p.gu_bytes : 0ull;
+      p.seg_dn[p.n_shared + i] = mine ? p.dn_base + idx[i] * p.dn_bytes : 0ull;
     }
   }
 }
@@ -214,12 +215,58 @@ __global__ void moe_combine_kernel(const CombineParams p) {
     o = __ldcg(p.exp_out + i);
     for (s = 1; s < p.n_shared; ++s) o = __fadd_rn(o, __ldcg(p.exp_out + static_cast<size_t>(s) * p.dim + i));
   }
+  const uint32_t ver = p.xslots ? __ldcg(p.ep_seq) + 1 : 0u;
+  bool gave_up = false;   // after one expired wait the others are not waited for
   for (uint32_t k = 0; k < p.top_k; ++k) {
     const float w = __ldcg(p.weights + k);
-    o = __fadd_rn(o, __fmul_rn(w, __ldcg(p.exp_out + static_cast<size_t>(p.n_shared + k) * p.dim + i)));
+    float y;
+    if (p.xslots) {
+      // the slot's output from whichever rank ran its expert (bounded wait)
+      const unsigned long long *src = p.xslots + (static_cast<size_t>(ver & 1u) * p.top_k + k) * p.dim + i;
+      unsigned long long t = __ldcg(src);
+      if (gave_up) {
+        t = static_cast<unsigned long long>(0x7fc00000u);
+      } else if (static_cast<uint32_t>(t >> 32) != ver) {
+        const uint64_t t0 = globaltimer_ns();
+        while (static_cast<uint32_t>(t >> 32) != ver) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(p.status, ZDEV_ERR_TIMEOUT);
+            t = static_cast<unsigned long long>(0x7fc00000u);
+            gave_up = true;
+            break;
+          }
+          t = __ldcg(src);
+        }
+      }
+      y = __uint_as_float(static_cast<uint32_t>(t));
+    } else {
+      y = __ldcg(p.exp_out + static_cast<size_t>(p.n_shared + k) * p.dim + i);
+    }
+    o = __fadd_rn(o, __fmul_rn(w, y));
   }
   if (p.mlp_out) p.mlp_out[i] = o;
   if (p.hidden) p.hidden[i] = __fadd_rn(p.hidden[i], o);
+}
+
+// grid (ceil(dim / 256), top_k): slot k's row, when this rank ran its expert
+__global__ void moe_ep_publish_kernel(const EpPublishParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t k = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= p.dim) return;
+  const uint32_t e = __ldcg(p.ids + k);
+  if (e / p.ep_per_rank != p.ep_rank) return;
+  const uint32_t ver = __ldcg(p.ep_seq) + 1;
+  const unsigned long long w =
+      tag_word(__ldcg(p.exp_out + static_cast<size_t>(p.n_shared + k) * p.dim + i), ver);
+  const size_t off = (static_cast<size_t>(ver & 1u) * p.top_k + k) * p.dim + i;
+  for (uint32_t d = 0; d < p.world; ++d) p.dst[d][off] = w;
+}
+
+__global__ void moe_ep_advance_kernel(uint32_t *ep_seq) {
+  pdl_launch_dependents();
+  pdl_wait();
+  if (threadIdx.x == 0) *ep_seq += 1;
 }
 
 }  // namespace
@@ -258,6 +305,21 @@ cudaError_t launch_moe_combine(const CombineParams &p, const LaunchCfg &lc) {
   cudaLaunchConfig_t cfg = make_launch_cfg(dim3((p.dim + 255) / 256), dim3(256), 0, lc, attr);
   if (lc.launch_counter) ++*lc.launch_counter;
   return cudaLaunchKernelEx(&cfg, moe_combine_kernel, p);
+}
+
+cudaError_t launch_moe_ep_publish(const EpPublishParams &p, const LaunchCfg &lc) {
+  if (p.dim == 0 || p.top_k == 0 || p.world == 0 || p.ep_per_rank == 0) return cudaErrorInvalidValue;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = make_launch_cfg(dim3((p.dim + 255) / 256, p.top_k), dim3(256), 0, lc, attr);
+  if (lc.launch_counter) ++*lc.launch_counter;
+  return cudaLaunchKernelEx(&cfg, moe_ep_publish_kernel, p);
+}
+
+cudaError_t launch_moe_ep_advance(uint32_t *ep_seq, const LaunchCfg &lc) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = make_launch_cfg(dim3(1), dim3(32), 0, lc, attr);
+  if (lc.launch_counter) ++*lc.launch_counter;
+  return cudaLaunchKernelEx(&cfg, moe_ep_advance_kernel, ep_seq);
 }
 
 }  // namespace zgpu

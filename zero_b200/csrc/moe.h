@@ -31,6 +31,10 @@ struct RouteParams {
   uint32_t n_shared;
   uint32_t experts_per_cta;  // set by the launcher
   uint32_t *status;
+  // expert parallelism: this rank runs experts [ep_rank * ep_per_rank,
+  // (ep_rank + 1) * ep_per_rank); a selected expert of another rank gets a
+  // zero table entry (its GEMV segments do nothing).  ep_per_rank == 0: all.
+  uint32_t ep_rank, ep_per_rank;
 };
 
 struct CombineParams {
@@ -39,10 +43,30 @@ struct CombineParams {
   float *mlp_out;            // [dim] or null
   float *hidden;             // residual (+= mlp_out) or null
   uint32_t dim, n_shared, top_k;
+  // expert parallelism: the routed slots' outputs come from this rank's
+  // exchange buffer (tagged words [2][top_k][dim], filled by every rank's
+  // moe_ep_publish) at version *ep_seq + 1; null: from exp_out
+  const unsigned long long *xslots;
+  const uint32_t *ep_seq;
+  uint32_t *status;
+};
+
+// Expert parallelism: the outputs of this rank's selected experts, as tagged
+// words into slot k of every rank's exchange buffer (buffer (v & 1), v =
+// *ep_seq + 1: a rank can run at most one MoE layer ahead of another).
+struct EpPublishParams {
+  const float *exp_out;                    // [n_shared + top_k][dim]
+  const uint32_t *ids;                     // [top_k] this layer's experts
+  unsigned long long *const *dst;          // [world] every rank's exchange buffer
+  const uint32_t *ep_seq;
+  uint32_t dim, n_shared, top_k, world, ep_rank, ep_per_rank;
 };
 
 cudaError_t moe_setup();
 cudaError_t launch_moe_route(const RouteParams &p, const LaunchCfg &lc);
 cudaError_t launch_moe_combine(const CombineParams &p, const LaunchCfg &lc);
+cudaError_t launch_moe_ep_publish(const EpPublishParams &p, const LaunchCfg &lc);
+// ++*ep_seq (one thread), after the layer's combine
+cudaError_t launch_moe_ep_advance(uint32_t *ep_seq, const LaunchCfg &lc);
 
 }  // namespace zgpu
