@@ -232,6 +232,27 @@ __device__ __forceinline__ uint16_t f64_to_f16_rne(double v) {
 // Tagged activation words (the persistent step kernel's inter-stage
 // vectors): element i is (version << 32) | f32 bits, written with one 64-bit
 // store, so a reader that sees the expected version also sees its value.
+// The packer's Q8_0 rule for one 32-element block (silicatepack.py:893-907),
+// one lane per element: d = amax / 127 in f64, q = rint(x / d) clamped to
+// +-127, d stored as fp16 (read back as f32).  Lane j writes its digit to
+// *qa; lane 0 writes the scale to *da.  An all-zero block gives zeros.
+__device__ __forceinline__ void quant_lane_q8_0(float v, int8_t *qa, float *da, uint32_t lane, uint32_t *status) {
+  if (!(fabsf(v) < INFINITY)) atomicOr(status, ZDEV_ERR_NUMERICAL);
+  double a = fabs(static_cast<double>(v));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) a = fmax(a, __shfl_xor_sync(0xffffffffu, a, off));
+  if (a == 0.0 || !(a < INFINITY)) {
+    *qa = 0;
+    if (lane == 0) *da = 0.f;
+    return;
+  }
+  const double dd = a / 127.0;
+  double r = rint(static_cast<double>(v) * (1.0 / dd));
+  r = fmin(fmax(r, -127.0), 127.0);
+  *qa = static_cast<int8_t>(r);
+  if (lane == 0) *da = h2f(f64_to_f16_rne(fmin(dd, 65504.0)));
+}
+
 __device__ __forceinline__ unsigned long long tag_word(float x, uint32_t ver) {
   return (static_cast<unsigned long long>(ver) << 32) | __float_as_uint(x);
 }

@@ -90,7 +90,7 @@ zgpu_status zgpu_init(const zgpu_opts *opts, zgpu_ctx **out) {
       zgpu::gemv_setup() != cudaSuccess || zgpu::attention_setup() != cudaSuccess ||
       zgpu::ops_setup() != cudaSuccess || zgpu::step_setup() != cudaSuccess ||
       zgpu::moe_setup() != cudaSuccess || zgpu::mla_setup() != cudaSuccess ||
-      zgpu::prefill_setup() != cudaSuccess ||
+      zgpu::prefill_setup() != cudaSuccess || zgpu::mma_setup() != cudaSuccess ||
       cudaMalloc(&ctx->d_route_counter, sizeof(uint32_t)) != cudaSuccess ||
       cudaMemset(ctx->d_route_counter, 0, sizeof(uint32_t)) != cudaSuccess) {
     delete ctx;
@@ -103,7 +103,11 @@ zgpu_status zgpu_init(const zgpu_opts *opts, zgpu_ctx **out) {
 zgpu_status zgpu_clear_weights(zgpu_ctx *ctx) {
   if (!ctx) return ZGPU_ERR_INVALID_ARG;
   cudaSetDevice(ctx->device);
-  for (auto &kv : ctx->weights) cudaFree(kv.second.d);
+  for (auto &kv : ctx->weights) {
+    cudaFree(kv.second.d);
+    cudaFree(kv.second.w8);
+    cudaFree(kv.second.ws8);
+  }
   ctx->weights.clear();
   return ZGPU_OK;
 }
@@ -229,7 +233,11 @@ zgpu_status zgpu_register_weights(zgpu_ctx *ctx, const void *host_ptr, size_t le
   }
   auto key = reinterpret_cast<uintptr_t>(host_ptr);
   auto it = ctx->weights.find(key);
-  if (it != ctx->weights.end()) cudaFree(it->second.d);
+  if (it != ctx->weights.end()) {
+    cudaFree(it->second.d);
+    cudaFree(it->second.w8);
+    cudaFree(it->second.ws8);
+  }
   ctx->weights[key] = t;
   return ZGPU_OK;
 }
@@ -456,8 +464,18 @@ static zgpu_status q8act_batch(zgpu_ctx *ctx, const float *d_x, const void *w_ke
     return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "linear_q8act_batch: shape mismatch with registration");
   if (out_dim % 128 || T > 0xFFFFFFu || T * in_dim > (1ull << 34))
     return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "linear_q8act_batch: rows must be a multiple of 128");
-  // scratch: q int8 [T][in] | d f32 [T][in/32]
-  const size_t qbytes = (T * in_dim + 15) & ~size_t(15), dbytes = T * (in_dim / 32) * 4;
+  const uint32_t bpr = static_cast<uint32_t>(in_dim / 32);
+  // the weights' operand tiles, once per tensor
+  DeviceTensor *wt = const_cast<DeviceTensor *>(t);
+  if (!wt->w8) {
+    ZCHECK(cudaMalloc(&wt->w8, zgpu::mma_tile_bytes(out_dim, bpr)), "cudaMalloc(weight tiles)");
+    ZCHECK(cudaMalloc(&wt->ws8, zgpu::mma_scale_bytes(out_dim, bpr)), "cudaMalloc(weight tile scales)");
+    ZCHECK(zgpu::launch_build_w8_tiles(wt->d, wt->gstride, static_cast<uint32_t>(out_dim), bpr, wt->w8, wt->ws8, s),
+           "weight tiles");
+    ++ctx->launches;
+  }
+  // scratch: activation tiles | their scales
+  const size_t qbytes = zgpu::mma_tile_bytes(T, bpr), dbytes = zgpu::mma_scale_bytes(T, bpr);
   if (qbytes + dbytes > ctx->d_q8_cap) {
     cudaFree(ctx->d_q8);
     ctx->d_q8 = nullptr;
@@ -467,16 +485,18 @@ static zgpu_status q8act_batch(zgpu_ctx *ctx, const float *d_x, const void *w_ke
   }
   int8_t *q = reinterpret_cast<int8_t *>(ctx->d_q8);
   float *d = reinterpret_cast<float *>(ctx->d_q8 + qbytes);
-  ZCHECK(zgpu::launch_quantize_q8_0_planar(d_x, q, d, T * in_dim, ctx->d_status, s), "q8 planar");
+  ZCHECK(zgpu::launch_quantize_q8_0_tiles(d_x, q, d, static_cast<uint32_t>(T), static_cast<uint32_t>(in_dim),
+                                         ctx->d_status, s),
+         "q8 tiles");
   zgpu::MmaGemmParams p = {};
-  p.w = t->d;
-  p.gstride = t->gstride;
+  p.wt = wt->w8;
+  p.ws = wt->ws8;
+  p.xt = q;
+  p.xs = d;
   p.rows = static_cast<uint32_t>(out_dim);
-  p.bpr = static_cast<uint32_t>(in_dim / 32);
+  p.bpr = bpr;
   p.T = static_cast<uint32_t>(T);
   p.ldy = static_cast<uint32_t>(out_dim);
-  p.xq = q;
-  p.xs = d;
   p.y = d_out;
   p.status = ctx->d_status;
   ZCHECK(zgpu::launch_q4q8_mma(p, s), "q4q8 mma");

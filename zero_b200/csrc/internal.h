@@ -25,6 +25,9 @@ struct DeviceTensor {
   uint64_t rows = 0, cols = 0;
   uint64_t groups = 0;        // ceil(rows / 4)
   uint64_t gstride = 0;       // bytes per group stream on the device
+  // batched-matmul operand tiles (ops.h), built on first batched use (Q4_0)
+  int8_t *w8 = nullptr;
+  float *ws8 = nullptr;
 };
 
 // Geometry of one GEMV launch over a device tensor in the layout.h format.

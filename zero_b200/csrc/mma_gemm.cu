@@ -6,25 +6,28 @@
 // Both operands carry one scale per 32-element block, so a block's integer
 // dot product must be scaled before it is added to the next block's.  Each
 // block is therefore one tcgen05.mma.kind::i8 of M = 128 weight rows x N = 128
-// tokens x K = 32 whose int32 result lands in TMEM; eight warps read it back
-// (tcgen05.ld: warp w takes lanes 32(w%4).. = rows, columns 64(w/4)..) and add (sumi * d_w) * d_x to f32
-// accumulators in block order.  That is exactly the order of the CPU
-// restatement of the Q4_0 x Q8_0 product (ggml's vec_dot_q4_0_q8_0 loop), so
-// results are bit-identical to it.
+// tokens x K = 32 into a TMEM accumulator, read back with tcgen05.ld and added
+// as (sumi * d_w) * d_x in block order: the order of the CPU restatement of
+// the Q4_0 x Q8_0 product (ggml's vec_dot_q4_0_q8_0 loop), bit for bit.
 //
-// Data path per block, 256 threads:
-//   * a cp.async ring of kStages stages (kStages - 2 blocks ahead) holds, per block, the 128 rows' 16
-//     nibble bytes (one plane entry of each row's group stream, layout.h), the
-//     32 groups' fp16 scales, the 128 tokens' 32 int8 activations (placed
-//     directly in the MMA's canonical K-major layout) and their scales;
-//   * thread t < 128 unpacks row t's nibbles into int8 (n - 8) in the A tile
-//     (canonical K-major layout, no swizzle: 8-row x 16-byte core matrices,
-//     SBO = 256 B between row groups, LBO = 128 B between the two K halves);
-//   * thread 0 issues the MMA and commits it to an mbarrier; all threads wait
-//     (bounded), load their row of D from TMEM and accumulate.  The loop is
-//     software-pipelined: block b+1's unpack and MMA (two A buffers, two TMEM
-//     accumulators) are issued before block b's accumulator is scaled.
-// Requires rows % 128 == 0 and in_dim % 32 == 0; tokens are zero-filled past T.
+// Operands come pre-tiled (ops.h): weights as int8 (n - 8) tiles built once
+// per tensor (build_w8_tiles), activations as Q8_0 tiles written by the
+// quantisers, each 128 x 32 block a contiguous 4 KB in the MMA's canonical
+// layout, plus f32 scale vectors.  One CTA per SM, warp-specialised, no
+// CTA-wide barrier inside the block loop:
+//   warp 0      producer: per block, four 1-D bulk copies (A, B, d_w, d_x)
+//               into one of 4 shared-memory stages, completion on full[s];
+//   warp 1      MMA issuer: waits full[s], one tcgen05.mma into accumulator
+//               s (4 x 128 TMEM columns), tcgen05.commit to done[s];
+//   warps 2-17  epilogue: warp w reads TMEM lanes 32 (w % 4).. (weight rows)
+//               x columns 32 ((w - 2) / 4).. (tokens) of accumulator s, scales
+//               and accumulates in f32 registers, then arrives on empty[s],
+//               which frees stage s and accumulator s for block b + 4.
+// Every wait is bounded (status ZDEV_ERR_TIMEOUT); on an expired wait each
+// role stops, the producer drains its copies in flight and the MMA issuer its
+// MMAs before TMEM is freed.  The launch asks for more than half an SM's
+// shared memory so that two CTAs never meet on one SM: the second CTA's
+// 512-column TMEM allocation would wait for the first.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -39,25 +42,18 @@ namespace {
 
 constexpr uint32_t kTileM = 128;
 constexpr uint32_t kTileN = 128;
-constexpr uint32_t kGemmThreads = 256;   // 8 warps: (lane quarter, 64-column half) of the accumulator
-constexpr uint32_t kStages = 5;
+constexpr uint32_t kStages = 4;                  // = TMEM accumulators
+constexpr uint32_t kEpiWarps = 16;
+constexpr uint32_t kGemmThreads = 32 * (2 + kEpiWarps);
 // stage layout (bytes)
-constexpr uint32_t kRawA = 0;                    // 128 rows x 16 B nibbles
-constexpr uint32_t kScA = 2048;                  // 32 groups x 8 B fp16 scales
-constexpr uint32_t kTileB = 2304;                // 128 tokens x 32 B, canonical K-major
-constexpr uint32_t kScB = 6400;                  // 128 tokens x f32 scales
-constexpr uint32_t kStageBytes = 6912;
-constexpr uint32_t kTmemCols = 256;              // two 128 x 128 int32 accumulators
-
-// Byte offset of (row r, K half h) in a canonical K-major no-swizzle tile of
-// 32-byte rows: core matrix (r / 8, h) holds rows 8(r/8).. x bytes 16h..16h+15.
-__device__ __forceinline__ uint32_t core_off(uint32_t r, uint32_t h) {
-  return (r & 7) * 16 + (r >> 3) * 256 + h * 128;
+constexpr uint32_t kStA = 0, kStB = 4096, kStW = 8192, kStX = 8192 + 512, kStageBytes = 8192 + 1024;
+constexpr uint32_t kTmemCols = kStages * kTileN; // 512: the whole TMEM of the SM
+constexpr uint32_t kDynSmem = 120 * 1024;        // > half of an SM: one CTA per SM
+static_assert(kStages * kStageBytes <= kDynSmem, "stages fit the dynamic shared memory");
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
+namespace {
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -119,14 +115,13 @@ __device__ __forceinline__ uint32_t nib_to_s8(uint32_t n4) {
   return m | ((m & 0x08080808u) * 0x1Eu);
 }
 
-__global__ void __launch_bounds__(kGemmThreads, 2) q4q8_mma_kernel(const MmaGemmParams p) {
-  __shared__ __align__(128) uint8_t ring[kStages * kStageBytes];
-  __shared__ __align__(128) uint8_t tileA[2][kTileM * 32];
-  __shared__ __align__(8) uint64_t mbar[2];
+__global__ void __launch_bounds__(kGemmThreads, 1) q4q8_mma_kernel(const MmaGemmParams p) {
+  extern __shared__ __align__(1024) uint8_t ring[];
+  __shared__ __align__(8) uint64_t full[kStages], done[kStages], empty[kStages], drain;
   __shared__ uint32_t tmem_base;
-  const uint32_t tid = threadIdx.x, warp = tid >> 5;
-  const uint32_t m0 = blockIdx.x * kTileM, t0 = blockIdx.y * kTileN;
-  const uint32_t bpr = p.bpr, K = bpr * 32;
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t mt = blockIdx.x, nt = blockIdx.y;
+  const uint32_t bpr = p.bpr;
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
@@ -134,9 +129,13 @@ __global__ void __launch_bounds__(kGemmThreads, 2) q4q8_mma_kernel(const MmaGemm
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (tid == 0) {
-    mbar_init(smem_addr(&mbar[0]), 1);
-    mbar_init(smem_addr(&mbar[1]), 1);
+  if (tid == 32) {
+    for (uint32_t s = 0; s < kStages; ++s) {
+      mbar_init(smem_addr(&full[s]), 1);
+      mbar_init(smem_addr(&done[s]), 1);
+      mbar_init(smem_addr(&empty[s]), kEpiWarps);
+    }
+    mbar_init(smem_addr(&drain), 1);
     fence_barrier_init();
   }
   tc_fence_before();
@@ -144,175 +143,164 @@ __global__ void __launch_bounds__(kGemmThreads, 2) q4q8_mma_kernel(const MmaGemm
   tc_fence_after();
   const uint32_t tmem = tmem_base;
 
-  // issue the copies of block b into its stage
-  // threads 0..127 own a weight row each (copy, unpack, and their rows' scale)
-  const uint32_t arow = tid & (kTileM - 1);
-  const uint32_t row = m0 + arow;
-  const uint8_t *grp_row = p.w + static_cast<uint64_t>(row >> 2) * p.gstride;
-  const uint32_t tl = tid >> 1, th = tid & 1;          // token / K half this thread copies
-  const bool tok_ok = t0 + tl < p.T;
-  const int8_t *xrow = p.xq + static_cast<uint64_t>(tok_ok ? t0 + tl : 0) * K;
-  auto issue = [&](uint32_t b) {
-    const uint32_t st = smem_addr(ring + (b % kStages) * kStageBytes);
-    if (tid < kTileM) cp_async16(st + kRawA + tid * 16, grp_row + plane_entry(ZGPU_Q4_0, bpr, b, row & 3), 16);
-    else if (tid < kTileM + 32)
-      cp_async8(st + kScA + (tid - kTileM) * 8,
-                p.w + static_cast<uint64_t>((m0 >> 2) + tid - kTileM) * p.gstride + scale_entry(ZGPU_Q4_0, bpr, b));
-    cp_async16(st + kTileB + core_off(tl, th), xrow + 32 * b + 16 * th, tok_ok ? 16u : 0u);
-    if (tid < kTileN) {
-      const bool ok = t0 + tid < p.T;
-      cp_async4(st + kScB + tid * 4, p.xs + static_cast<uint64_t>(ok ? t0 + tid : 0) * bpr + b, ok ? 4u : 0u);
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      const int8_t *wa = p.wt + static_cast<size_t>(mt) * bpr * 4096u;
+      const int8_t *xa = p.xt + static_cast<size_t>(nt) * bpr * 4096u;
+      const float *ws = p.ws + static_cast<size_t>(mt) * bpr * kTileM;
+      const float *xs = p.xs + static_cast<size_t>(nt) * bpr * kTileN;
+      uint32_t issued = 0;
+      for (uint32_t b = 0; b < bpr; ++b) {
+        const uint32_t s = b % kStages;
+        if (b >= kStages && !mbar_wait(smem_addr(&empty[s]), ((b / kStages) - 1) & 1, p.status)) break;
+        const uint32_t st = smem_addr(ring + s * kStageBytes), fb = smem_addr(&full[s]);
+        mbar_arrive_expect_tx(fb, kStageBytes);
+        bulk_copy_g2s(st + kStA, wa + static_cast<size_t>(b) * 4096u, 4096, fb);
+        bulk_copy_g2s(st + kStB, xa + static_cast<size_t>(b) * 4096u, 4096, fb);
+        bulk_copy_g2s(st + kStW, ws + static_cast<size_t>(b) * kTileM, 512, fb);
+        bulk_copy_g2s(st + kStX, xs + static_cast<size_t>(b) * kTileN, 512, fb);
+        ++issued;
+      }
+      // never leave a copy in flight when the CTA may exit
+      for (uint32_t j = issued > kStages ? issued - kStages : 0; j < issued; ++j)
+        mbar_wait(smem_addr(&full[j % kStages]), (j / kStages) & 1, p.status);
     }
-  };
-  // The ring runs kStages - 2 blocks ahead: prepare(c) refills the stage of
-  // block c - 2, whose MMA and epilogue are complete by then (block c - 1's
-  // MMA and block c - 1's epilogue may still use theirs).
-#pragma unroll
-  for (uint32_t s = 0; s < kStages - 2; ++s) {
-    if (s < bpr) issue(s);
-    cp_async_commit();
-  }
-
-  constexpr int kCols = 64;   // accumulator columns (tokens) per thread
-  const uint32_t chalf = warp >> 2;
-  float acc[kCols];
-#pragma unroll
-  for (int j = 0; j < kCols; ++j) acc[j] = 0.f;
-
-  // Stage b's data is complete (all threads' copies), then row tid's nibbles
-  // become int8 (n - 8) in A buffer b % 2; returns this row's scale d_w.
-  auto prepare = [&](uint32_t b) -> float {
-    if (b + kStages - 2 < bpr) issue(b + kStages - 2);
-    cp_async_commit();
-    cp_async_wait<kStages - 2>();   // this thread's copies of block b have landed
-    __syncthreads();                // ... and everyone's; A buffer b % 2 is free (its MMA completed)
-    const uint8_t *st = ring + (b % kStages) * kStageBytes;
-    uint8_t *ta = tileA[b & 1];
-    const uint16_t hw = *reinterpret_cast<const uint16_t *>(st + kScA + (arow >> 2) * 8 + (arow & 3) * 2);
-    if (tid >= kTileM) {
-      fence_proxy_async_smem();
-      return h2f(hw);
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      for (uint32_t b = 0; b < bpr; ++b) {
+        const uint32_t s = b % kStages;
+        if (!mbar_wait(smem_addr(&full[s]), (b / kStages) & 1, p.status)) break;
+        tc_fence_after();
+        const uint32_t st = smem_addr(ring + s * kStageBytes);
+        umma_i8(tmem + s * kTileN, umma_desc(st + kStA, 128, 256), umma_desc(st + kStB, 128, 256), kIdesc, 0u);
+        umma_commit(smem_addr(&done[s]));
+      }
+      // every MMA of this thread has completed before TMEM is freed
+      umma_commit(smem_addr(&drain));
+      mbar_wait(smem_addr(&drain), 0, p.status);
     }
-    const uint4 q = *reinterpret_cast<const uint4 *>(st + kRawA + tid * 16);
-    uint4 lo, hi;
-    lo.x = nib_to_s8(q.x & 0x0F0F0F0Fu);
-    lo.y = nib_to_s8(q.y & 0x0F0F0F0Fu);
-    lo.z = nib_to_s8(q.z & 0x0F0F0F0Fu);
-    lo.w = nib_to_s8(q.w & 0x0F0F0F0Fu);
-    hi.x = nib_to_s8((q.x >> 4) & 0x0F0F0F0Fu);
-    hi.y = nib_to_s8((q.y >> 4) & 0x0F0F0F0Fu);
-    hi.z = nib_to_s8((q.z >> 4) & 0x0F0F0F0Fu);
-    hi.w = nib_to_s8((q.w >> 4) & 0x0F0F0F0Fu);
-    *reinterpret_cast<uint4 *>(ta + core_off(tid, 0)) = lo;
-    *reinterpret_cast<uint4 *>(ta + core_off(tid, 1)) = hi;
-    fence_proxy_async_smem();   // generic-proxy writes of A and B -> visible to the tensor core
-    return h2f(hw);
-  };
-  // thread 0: MMA of block b into accumulator b % 2, committed to mbar[b % 2]
-  auto mma = [&](uint32_t b) {
-    if (tid == 0) {
+  } else {
+    // ---------------- epilogue ----------------
+    const uint32_t q = warp & 3, c = (warp - 2) >> 2;   // TMEM lane quarter, token quarter
+    float acc[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+    bool ok = true;
+    for (uint32_t b = 0; b < bpr && ok; ++b) {
+      const uint32_t s = b % kStages, par = (b / kStages) & 1;
+      if (!mbar_wait(smem_addr(&done[s]), par, p.status) || !mbar_wait(smem_addr(&full[s]), par, p.status)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
-      const uint8_t *st = ring + (b % kStages) * kStageBytes;
-      umma_i8(tmem + (b & 1) * kTileN, umma_desc(smem_addr(tileA[b & 1]), 128, 256),
-              umma_desc(smem_addr(st + kTileB), 128, 256), kIdesc, 0u);
-      umma_commit(smem_addr(&mbar[b & 1]));
-    }
-  };
-
-  // Software pipeline: block b+1 is prepared and its MMA issued before block
-  // b's accumulator is read back and scaled, so the tensor core and the
-  // copies run under the epilogue's arithmetic.  Two A buffers and two TMEM
-  // accumulators; a buffer is reused two blocks later, after the barrier in
-  // prepare() that follows everyone's reads of it.
-  bool ok = true;
-  float dw_cur = prepare(0);
-  __syncthreads();
-  mma(0);
-  for (uint32_t b = 0; b < bpr; ++b) {
-    float dw_next = 0.f;
-    if (b + 1 < bpr) {
-      dw_next = prepare(b + 1);
-      __syncthreads();
-      mma(b + 1);
-    }
-    if (ok && !mbar_wait(smem_addr(&mbar[b & 1]), (b >> 1) & 1, p.status)) ok = false;
-    tc_fence_after();
-    const uint32_t taddr = tmem + (((warp & 3) * 32u) << 16) + (b & 1) * kTileN + chalf * kCols;
-    const float4 *dx4 =
-        reinterpret_cast<const float4 *>(ring + (b % kStages) * kStageBytes + kScB) + chalf * (kCols / 4);
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
+      const uint8_t *st = ring + s * kStageBytes;
+      const float dw = reinterpret_cast<const float *>(st + kStW)[32 * q + lane];
+      const float4 *dx4 = reinterpret_cast<const float4 *>(st + kStX) + 8 * c;
       uint32_t v[32];
-      tmem_ld32(taddr + 32 * h, v);
+      tmem_ld32(tmem + ((32u * q) << 16) + s * kTileN + 32 * c, v);
       tmem_ld_wait();
 #pragma unroll
       for (int j4 = 0; j4 < 8; ++j4) {
-        const float4 d4 = dx4[8 * h + j4];
+        const float4 d4 = dx4[j4];
         const float dxv[4] = {d4.x, d4.y, d4.z, d4.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const int j = 32 * h + 4 * j4 + k;
-          acc[j] = __fadd_rn(acc[j], __fmul_rn(__fmul_rn(small_i2f(v[4 * j4 + k]), dw_cur), dxv[k]));
+          const int j = 4 * j4 + k;
+          acc[j] = __fadd_rn(acc[j], __fmul_rn(__fmul_rn(small_i2f(v[j]), dw), dxv[k]));
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&empty[s]));
     }
-    tc_fence_before();
-    dw_cur = dw_next;
-  }
-  cp_async_wait<0>();
+    const uint32_t row = mt * kTileM + 32 * q + lane;
 #pragma unroll
-  for (int j = 0; j < kCols; ++j) {
-    const uint32_t t = t0 + chalf * kCols + j;
-    if (t < p.T) {
-      float *dst = p.y + static_cast<uint64_t>(t) * p.ldy + row;
-      const float v = ok ? acc[j] : __uint_as_float(0x7fc00000u);
-      *dst = p.resadd ? __fadd_rn(*dst, v) : v;
+    for (int j = 0; j < 32; ++j) {
+      const uint32_t t = nt * kTileN + 32 * c + j;
+      if (t < p.T) {
+        float *dst = p.y + static_cast<uint64_t>(t) * p.ldy + row;
+        const float val = ok ? acc[j] : __uint_as_float(0x7fc00000u);
+        *dst = p.resadd ? __fadd_rn(*dst, val) : val;
+      }
     }
   }
+  tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
 }
 
-// Q8_0 activation rows in the planar form the MMA reads: q int8 [T][K] and
-// the block scale d (fp16-rounded, as f32) [T][K/32].  The packer's rule, as
-// quantize_q8_0_kernel.  One warp per block.
-__global__ void quantize_q8_0_planar_kernel(const float *x, int8_t *q, float *d, uint64_t nblocks,
-                                            uint32_t *status) {
+// Q4_0 group streams -> weight tiles: CTA (row tile, block), thread = row.
+__global__ void build_w8_tiles_kernel(const uint8_t *w, uint64_t gstride, uint32_t bpr, int8_t *wt, float *ws) {
+  const uint32_t row = blockIdx.x * kTileM + threadIdx.x, b = blockIdx.y;
+  const uint8_t *grp = w + static_cast<uint64_t>(row >> 2) * gstride;
+  const uint4 qv = *reinterpret_cast<const uint4 *>(grp + plane_entry(ZGPU_Q4_0, bpr, b, row & 3));
+  const uint8_t *sc = grp + scale_entry(ZGPU_Q4_0, bpr, b) + 2 * (row & 3);
+  uint4 lo, hi;
+  lo.x = nib_to_s8(qv.x & 0x0F0F0F0Fu);
+  lo.y = nib_to_s8(qv.y & 0x0F0F0F0Fu);
+  lo.z = nib_to_s8(qv.z & 0x0F0F0F0Fu);
+  lo.w = nib_to_s8(qv.w & 0x0F0F0F0Fu);
+  hi.x = nib_to_s8((qv.x >> 4) & 0x0F0F0F0Fu);
+  hi.y = nib_to_s8((qv.y >> 4) & 0x0F0F0F0Fu);
+  hi.z = nib_to_s8((qv.z >> 4) & 0x0F0F0F0Fu);
+  hi.w = nib_to_s8((qv.w >> 4) & 0x0F0F0F0Fu);
+  *reinterpret_cast<uint4 *>(wt + mma_tile_off(row, b, bpr, 0)) = lo;
+  *reinterpret_cast<uint4 *>(wt + mma_tile_off(row, b, bpr, 1)) = hi;
+  ws[mma_scale_off(row, b, bpr)] = h2f(static_cast<uint16_t>(sc[0] | (sc[1] << 8)));
+}
+
+// Q8_0 activation tiles: one warp per (row, block) of the padded row count;
+// rows past T become zero digits and scale 0.  The packer's rule, as
+// quantize_q8_0_kernel.
+__global__ void quantize_q8_0_tiles_kernel(const float *x, int8_t *xt, float *xs, uint32_t T, uint32_t bpr,
+                                           uint64_t nwarps, uint32_t *status) {
   const uint64_t wb = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) >> 5;
   const uint32_t lane = threadIdx.x & 31;
-  if (wb >= nblocks) return;
-  const float v = x[wb * 32 + lane];
-  if (!(fabsf(v) < INFINITY)) atomicOr(status, ZDEV_ERR_NUMERICAL);
-  double a = fabs(static_cast<double>(v));
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) a = fmax(a, __shfl_xor_sync(0xffffffffu, a, off));
-  if (a == 0.0 || !(a < INFINITY)) {
-    q[wb * 32 + lane] = 0;
-    if (lane == 0) d[wb] = 0.f;
+  if (wb >= nwarps) return;
+  const uint32_t t = static_cast<uint32_t>(wb / bpr), b = static_cast<uint32_t>(wb % bpr);
+  int8_t *qa = xt + mma_tile_off(t, b, bpr, lane >> 4) + (lane & 15);
+  float *da = xs + mma_scale_off(t, b, bpr);
+  if (t >= T) {
+    *qa = 0;
+    if (lane == 0) *da = 0.f;
     return;
   }
-  const double dd = a / 127.0;
-  double r = rint(static_cast<double>(v) * (1.0 / dd));
-  r = fmin(fmax(r, -127.0), 127.0);
-  q[wb * 32 + lane] = static_cast<int8_t>(r);
-  if (lane == 0) d[wb] = h2f(f64_to_f16_rne(fmin(dd, 65504.0)));
+  quant_lane_q8_0(x[static_cast<uint64_t>(t) * bpr * 32 + 32 * b + lane], qa, da, lane, status);
 }
 
 }  // namespace
 
+cudaError_t mma_setup() {
+  return cudaFuncSetAttribute(q4q8_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem);
+}
+
 cudaError_t launch_q4q8_mma(const MmaGemmParams &p, cudaStream_t s) {
-  if (p.rows == 0 || p.rows % kTileM || p.bpr == 0 || p.T == 0 || p.gstride % 16) return cudaErrorInvalidValue;
+  if (p.rows == 0 || p.rows % kTileM || p.bpr == 0 || p.T == 0 || !p.wt || !p.ws || !p.xt || !p.xs)
+    return cudaErrorInvalidValue;
   dim3 grid(p.rows / kTileM, (p.T + kTileN - 1) / kTileN);
-  q4q8_mma_kernel<<<grid, kGemmThreads, 0, s>>>(p);
+  q4q8_mma_kernel<<<grid, kGemmThreads, kDynSmem, s>>>(p);
   return cudaGetLastError();
 }
 
-cudaError_t launch_quantize_q8_0_planar(const float *x, int8_t *q, float *d, uint64_t n, uint32_t *status,
-                                        cudaStream_t s) {
-  const uint64_t nb = n / 32;
-  quantize_q8_0_planar_kernel<<<static_cast<unsigned>((nb * 32 + 255) / 256), 256, 0, s>>>(x, q, d, nb, status);
+cudaError_t launch_build_w8_tiles(const uint8_t *w, uint64_t gstride, uint32_t rows, uint32_t bpr, int8_t *wt,
+                                  float *ws, cudaStream_t s) {
+  if (rows == 0 || rows % kTileM || bpr == 0 || gstride % 16) return cudaErrorInvalidValue;
+  build_w8_tiles_kernel<<<dim3(rows / kTileM, bpr), kTileM, 0, s>>>(w, gstride, bpr, wt, ws);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_q8_0_tiles(const float *x, int8_t *xt, float *xs, uint32_t T, uint32_t K,
+                                       uint32_t *status, cudaStream_t s) {
+  if (T == 0 || K == 0 || K % 32) return cudaErrorInvalidValue;
+  const uint32_t bpr = K / 32;
+  const uint64_t rows = (static_cast<uint64_t>(T) + kMmaTile - 1) / kMmaTile * kMmaTile;
+  const uint64_t nwarps = rows * bpr;
+  quantize_q8_0_tiles_kernel<<<static_cast<unsigned>((nwarps * 32 + 255) / 256), 256, 0, s>>>(x, xt, xs, T, bpr,
+                                                                                            nwarps, status);
   return cudaGetLastError();
 }
 

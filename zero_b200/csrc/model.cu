@@ -74,6 +74,10 @@ struct zgpu_model {
   uint8_t *d_pf = nullptr;
   size_t pf_cap = 0;
   std::vector<cudaEvent_t> pf_ev;   // one pair per timed prefill launch (GEMM / attention)
+  // the prefill's weight operand tiles (ops.h), built on the first prefill:
+  // per layer QKV, O, gate/up, down
+  std::vector<int8_t *> pf_w8;
+  std::vector<float *> pf_ws8;
   // tensor parallelism (world > 1): this rank's slice of every stage
   uint32_t rank = 0, world = 1;
   uint32_t q_loc = 0, kv_loc = 0;   // this rank's q / k rows (all of them on one GPU)
@@ -642,6 +646,8 @@ void zgpu_qwen3_destroy(zgpu_model *m) {
   for (auto &e : m->ev)
     if (e) cudaEventDestroy(e);
   for (auto &e : m->pf_ev) cudaEventDestroy(e);
+  for (int8_t *p : m->pf_w8) cudaFree(p);
+  for (float *p : m->pf_ws8) cudaFree(p);
   for (DeviceTensor *t : m->owned) {
     cudaFree(t->d);
     delete t;
@@ -1161,13 +1167,44 @@ zgpu_status prefill_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, cons
   const uint32_t H = d.hidden, F = d.ffn, QD = m->q_dim, KVD = m->kv_dim, QKV = QD + 2 * KVD;
   if (H % 128 || QKV % 128 || (2 * F) % 128 || QD % 32 || F % 32)
     return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "prefill: projection rows must be multiples of 128");
+  // weight operand tiles of every projection, once per model
+  if (m->pf_w8.empty()) {
+    struct Mat {
+      const uint8_t *w;
+      uint64_t gstride;
+      uint32_t rows, in_dim;
+    };
+    for (uint32_t l = 0; l < d.n_layers; ++l) {
+      const Mat mats[4] = {{m->qkv[l], m->gs_h, QKV, H},
+                           {m->o[l]->d, m->o[l]->gstride, H, QD},
+                           {m->gateup[l], m->gs_h, 2 * F, H},
+                           {m->down[l]->d, m->down[l]->gstride, H, F}};
+      for (const Mat &mt : mats) {
+        int8_t *wt = nullptr;
+        float *ws = nullptr;
+        cudaError_t e = cudaMalloc(&wt, mma_tile_bytes(mt.rows, mt.in_dim / 32));
+        if (e == cudaSuccess) e = cudaMalloc(&ws, mma_scale_bytes(mt.rows, mt.in_dim / 32));
+        m->pf_w8.push_back(wt);
+        m->pf_ws8.push_back(ws);
+        if (e == cudaSuccess) e = launch_build_w8_tiles(mt.w, mt.gstride, mt.rows, mt.in_dim / 32, wt, ws, ctx->stream);
+        if (e != cudaSuccess) {
+          for (int8_t *p : m->pf_w8) cudaFree(p);
+          for (float *p : m->pf_ws8) cudaFree(p);
+          m->pf_w8.clear();
+          m->pf_ws8.clear();
+          return zgpu_cuda_fail(ctx, e, "prefill weight tiles");
+        }
+      }
+    }
+  }
   // scratch: tokens | hidden [NT][H] | qkv [NT][QKV] | qrot [NT][QD] | attn [NT][QD] | gu [NT][2F] | act [NT][F]
-  //          | q8 [NT][maxK] int8 | d8 [NT][maxK/32] f32
+  //          | activation tiles and scales for the widest input
   const size_t N = NT, maxk = std::max(std::max(H, QD), F);
   auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
   const size_t o_tok = 0, o_hid = al(N * 4), o_qkv = o_hid + al(N * H * 4), o_qr = o_qkv + al(N * QKV * 4),
                o_at = o_qr + al(N * QD * 4), o_gu = o_at + al(N * QD * 4), o_act = o_gu + al(N * 2 * F * 4),
-               o_q8 = o_act + al(N * F * 4), o_d8 = o_q8 + al(N * maxk), total = o_d8 + al(N * (maxk / 32) * 4);
+               o_q8 = o_act + al(N * F * 4), o_d8 = o_q8 + al(mma_tile_bytes(N, maxk / 32)),
+               total = o_d8 + al(mma_scale_bytes(N, maxk / 32));
   if (total > m->pf_cap) {
     cudaFree(m->d_pf);
     m->d_pf = nullptr;
@@ -1195,15 +1232,15 @@ zgpu_status prefill_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, cons
   }
   size_t ev_i = 0;
   auto mark = [&]() { cudaEventRecord(m->pf_ev[ev_i++], s); };
-  auto gemm = [&](const uint8_t *w, uint64_t gstride, uint32_t rows, uint32_t in_dim, float *y, bool resadd) {
+  auto gemm = [&](uint32_t l, uint32_t which, uint32_t rows, uint32_t in_dim, float *y, bool resadd) {
     MmaGemmParams p = {};
-    p.w = w;
-    p.gstride = gstride;
+    p.wt = m->pf_w8[4 * l + which];
+    p.ws = m->pf_ws8[4 * l + which];
     p.rows = rows;
     p.bpr = in_dim / 32;
     p.T = static_cast<uint32_t>(NT);
     p.ldy = rows;
-    p.xq = q8;
+    p.xt = q8;
     p.xs = d8;
     p.y = y;
     p.status = m->d_status;
@@ -1223,7 +1260,7 @@ zgpu_status prefill_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, cons
   const uint32_t T = static_cast<uint32_t>(NT);
   for (uint32_t l = 0; l < d.n_layers && e == cudaSuccess; ++l) {
     if ((e = launch_rows_rmsnorm_quant(hid, norm_attn(m, l), d.rms_eps, T, H, q8, d8, m->d_status, s))) break;
-    if ((e = gemm(m->qkv[l], m->gs_h, QKV, H, qkv, false))) break;
+    if ((e = gemm(l, 0, QKV, H, qkv, false))) break;
     for (uint32_t i = 0; i < n_seq && e == cudaSuccess; ++i, ++launches) {
       float *kvl = kvs[i]->d + static_cast<size_t>(l) * 2 * kvs[i]->block;
       const size_t r0 = static_cast<size_t>(i) * n;
@@ -1240,13 +1277,13 @@ zgpu_status prefill_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, cons
     }
     mark();
     if (e) break;
-    if ((e = launch_quantize_q8_0_planar(at, q8, d8, N * QD, m->d_status, s))) break;
-    if ((e = gemm(m->o[l]->d, m->o[l]->gstride, H, QD, hid, true))) break;
+    if ((e = launch_quantize_q8_0_tiles(at, q8, d8, T, QD, m->d_status, s))) break;
+    if ((e = gemm(l, 1, H, QD, hid, true))) break;
     if ((e = launch_rows_rmsnorm_quant(hid, norm_ffn(m, l), d.rms_eps, T, H, q8, d8, m->d_status, s))) break;
-    if ((e = gemm(m->gateup[l], m->gs_h, 2 * F, H, gu, false))) break;
+    if ((e = gemm(l, 2, 2 * F, H, gu, false))) break;
     if ((e = launch_swiglu_rows(gu, act, T, F, s))) break;
-    if ((e = launch_quantize_q8_0_planar(act, q8, d8, N * F, m->d_status, s))) break;
-    if ((e = gemm(m->down[l]->d, m->down[l]->gstride, H, F, hid, true))) break;
+    if ((e = launch_quantize_q8_0_tiles(act, q8, d8, T, F, m->d_status, s))) break;
+    if ((e = gemm(l, 3, H, F, hid, true))) break;
     launches += 5;
   }
   cudaEventRecord(m->ev[1], s);

@@ -89,22 +89,52 @@ inline cudaLaunchConfig_t make_launch_cfg(dim3 grid, dim3 block, size_t smem, co
 // Batched Q4_0 x Q8_0 matmul on tcgen05 (mma_gemm.cu): y[t * ldy + m] for
 // t < T, m < rows, from the layout.h weight streams and planar Q8_0
 // activations (q int8 [T][bpr*32], d f32 [T][bpr]).
+// Operand tiles of the batched Q4_0 x Q8_0 matmul (mma_gemm.cu): per
+// 128-row (or 128-token) tile and 32-element block, 4096 bytes of int8 in the
+// tensor core's canonical K-major layout (8-row x 16-byte core matrices, row r
+// and K half h at (r % 8) * 16 + (r / 8) * 256 + h * 128), tiles laid out
+// [tile][block]; scales f32 [tile][block][128].  Weights hold n - 8 of their
+// Q4_0 nibbles; activations the Q8_0 digits, rows past T zero.
+constexpr uint32_t kMmaTile = 128;
+inline size_t mma_tile_bytes(uint64_t rows, uint32_t bpr) {
+  return ((rows + kMmaTile - 1) / kMmaTile) * bpr * 4096ull;
+}
+inline size_t mma_scale_bytes(uint64_t rows, uint32_t bpr) {
+  return ((rows + kMmaTile - 1) / kMmaTile) * bpr * kMmaTile * 4ull;
+}
+__host__ __device__ inline size_t mma_tile_off(uint32_t r, uint32_t b, uint32_t bpr, uint32_t h) {
+  return (static_cast<size_t>(r / kMmaTile) * bpr + b) * 4096u + (r % 8) * 16u + ((r % kMmaTile) / 8) * 256u +
+         h * 128u;
+}
+__host__ __device__ inline size_t mma_scale_off(uint32_t r, uint32_t b, uint32_t bpr) {
+  return (static_cast<size_t>(r / kMmaTile) * bpr + b) * kMmaTile + r % kMmaTile;
+}
+
 struct MmaGemmParams {
-  const uint8_t *w;
-  uint64_t gstride;
+  const int8_t *wt;         // weight tiles, rows / 128 of them
+  const float *ws;          // weight block scales
+  const int8_t *xt;         // activation tiles, ceil(T / 128)
+  const float *xs;          // activation block scales
+  float *y;                 // [T][ldy], columns [0, rows)
   uint32_t rows, bpr, T, ldy;
-  const int8_t *xq;
-  const float *xs;
-  float *y;
   uint32_t *status;
   uint32_t resadd;          // 0: y = result; 1: y = y + result (residual add)
 };
+cudaError_t mma_setup();
 cudaError_t launch_q4q8_mma(const MmaGemmParams &p, cudaStream_t s);
+// Q4_0 group streams (layout.h) -> weight tiles + scales; rows % 128 == 0.
+cudaError_t launch_build_w8_tiles(const uint8_t *w, uint64_t gstride, uint32_t rows, uint32_t bpr, int8_t *wt,
+                                  float *ws, cudaStream_t s);
+// x [T][K] f32 -> Q8_0 activation tiles + scales (the packer's rule); the
+// padding rows of the last tile are zeroed.
+cudaError_t launch_quantize_q8_0_tiles(const float *x, int8_t *xt, float *xs, uint32_t T, uint32_t K,
+                                       uint32_t *status, cudaStream_t s);
 
 // Token-parallel prefill kernels (prefill.cu).
 cudaError_t prefill_setup();
-cudaError_t launch_rows_rmsnorm_quant(const float *x, const float *g, float eps, uint32_t T, uint32_t n, int8_t *q,
-                                      float *d, uint32_t *status, cudaStream_t s);
+// RMSNorm of each row, then Q8_0 into activation tiles (as launch_quantize_q8_0_tiles)
+cudaError_t launch_rows_rmsnorm_quant(const float *x, const float *g, float eps, uint32_t T, uint32_t n, int8_t *xt,
+                                      float *xs, uint32_t *status, cudaStream_t s);
 cudaError_t launch_rows_embed(const uint8_t *emb, uint64_t gstride, uint32_t quant, uint32_t hidden, uint32_t vocab,
                               const uint32_t *tokens, uint32_t T, float *out, uint32_t *status, cudaStream_t s);
 cudaError_t launch_qk_rope_kv(const float *qkv, const float *q_norm, const float *k_norm, const float *inv_freqs,
@@ -114,8 +144,6 @@ cudaError_t launch_causal_attn(const float *q, const float *kv_layer, uint64_t k
                                uint32_t pos0, uint32_t T, float scale, float *out, uint32_t *status,
                                cudaStream_t s);
 cudaError_t launch_swiglu_rows(const float *y, float *act, uint32_t T, uint32_t ffn, cudaStream_t s);
-cudaError_t launch_quantize_q8_0_planar(const float *x, int8_t *q, float *d, uint64_t n, uint32_t *status,
-                                        cudaStream_t s);
 
 cudaError_t launch_attention(const AttnParams &ap, const LaunchCfg &lc);
 // Number of attention splits (CTAs per kv-head) a cache of max_tokens needs.

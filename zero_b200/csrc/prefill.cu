@@ -47,38 +47,31 @@ __device__ __forceinline__ float row_block_sum(float v, float *red) {
 }
 
 // Q8_0 rule of one 32-element block held by the 32 lanes of a warp.
-__device__ __forceinline__ void quant_block_lane(float v, int8_t *q, float *d, uint32_t lane, uint32_t *status) {
-  if (!(fabsf(v) < INFINITY)) atomicOr(status, ZDEV_ERR_NUMERICAL);
-  double a = fabs(static_cast<double>(v));
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) a = fmax(a, __shfl_xor_sync(0xffffffffu, a, off));
-  if (a == 0.0 || !(a < INFINITY)) {
-    q[lane] = 0;
-    if (lane == 0) *d = 0.f;
-    return;
-  }
-  const double dd = a / 127.0;
-  double r = rint(static_cast<double>(v) * (1.0 / dd));
-  r = fmin(fmax(r, -127.0), 127.0);
-  q[lane] = static_cast<int8_t>(r);
-  if (lane == 0) *d = h2f(f64_to_f16_rne(fmin(dd, 65504.0)));
-}
-
+// CTA per row of the padded row count (a multiple of 128): RMSNorm, then the
+// Q8_0 rule into the matmul's activation tiles (ops.h); rows past T are zero.
 __global__ void __launch_bounds__(kRowThreads) rows_rmsnorm_quant_kernel(const float *x, const float *g, float eps,
-                                                                         uint32_t n, int8_t *q, float *d,
-                                                                         uint32_t *status) {
+                                                                         uint32_t T, uint32_t n, int8_t *xt,
+                                                                         float *xs, uint32_t *status) {
   __shared__ float red[kRowThreads / 32];
   const uint32_t t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t bpr = n / 32;
+  if (t >= T) {
+    for (uint32_t b = warp; b < bpr; b += kRowThreads / 32) {
+      xt[mma_tile_off(t, b, bpr, lane >> 4) + (lane & 15)] = 0;
+      if (lane == 0) xs[mma_scale_off(t, b, bpr)] = 0.f;
+    }
+    return;
+  }
   const float *xr = x + static_cast<size_t>(t) * n;
   float ss = 0.f;
   for (uint32_t i = tid; i < n; i += kRowThreads) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
   const float tot = row_block_sum(ss, red);
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(n)), eps)));
-  for (uint32_t b = warp; b < n / 32; b += kRowThreads / 32) {
+  for (uint32_t b = warp; b < bpr; b += kRowThreads / 32) {
     const uint32_t i = 32 * b + lane;
     const float y = __fmul_rn(__fmul_rn(xr[i], inv), g[i]);
-    quant_block_lane(y, q + static_cast<size_t>(t) * n + 32 * b, d + static_cast<size_t>(t) * (n / 32) + b, lane,
-                     status);
+    quant_lane_q8_0(y, xt + mma_tile_off(t, b, bpr, lane >> 4) + (lane & 15), xs + mma_scale_off(t, b, bpr), lane,
+                    status);
   }
 }
 
@@ -431,10 +424,11 @@ __global__ void swiglu_rows_kernel(const float *y, float *act, uint32_t ffn, uin
 
 }  // namespace
 
-cudaError_t launch_rows_rmsnorm_quant(const float *x, const float *g, float eps, uint32_t T, uint32_t n, int8_t *q,
-                                      float *d, uint32_t *status, cudaStream_t s) {
-  if (n % 32) return cudaErrorInvalidValue;
-  rows_rmsnorm_quant_kernel<<<T, kRowThreads, 0, s>>>(x, g, eps, n, q, d, status);
+cudaError_t launch_rows_rmsnorm_quant(const float *x, const float *g, float eps, uint32_t T, uint32_t n, int8_t *xt,
+                                      float *xs, uint32_t *status, cudaStream_t s) {
+  if (n % 32 || T == 0) return cudaErrorInvalidValue;
+  const uint32_t rows = (T + kMmaTile - 1) / kMmaTile * kMmaTile;
+  rows_rmsnorm_quant_kernel<<<rows, kRowThreads, 0, s>>>(x, g, eps, T, n, xt, xs, status);
   return cudaGetLastError();
 }
 
