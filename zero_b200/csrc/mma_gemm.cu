@@ -108,6 +108,29 @@ __device__ __forceinline__ float small_i2f(uint32_t v) {
   return __fsub_rn(__int_as_float(static_cast<int>(v) + 0x4B400000), 12582912.0f);
 }
 
+// Packed f32x2 add / multiply, each lane rounded to nearest.  The explicit
+// .rn keeps every one a separate rounding (PTX never contracts an add or mul
+// that carries a rounding modifier into an fma), so two columns at a time
+// follow the scalar order exactly: the exact magic-number subtract, then
+// (x * d_w) * d_x.  The accumulation itself stays scalar: a packed add did
+// not reproduce the scalar sums bit for bit.
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+  uint64_t r;
+  asm("{\n\t.reg .b64 pa, pb;\n\tmov.b64 pa, {%1, %2};\n\tmov.b64 pb, {%3, %4};\n\t"
+      "add.rn.f32x2 %0, pa, pb;\n\t}"
+      : "=l"(r)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return make_float2(__uint_as_float(static_cast<uint32_t>(r)), __uint_as_float(static_cast<uint32_t>(r >> 32)));
+}
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  uint64_t r;
+  asm("{\n\t.reg .b64 pa, pb;\n\tmov.b64 pa, {%1, %2};\n\tmov.b64 pb, {%3, %4};\n\t"
+      "mul.rn.f32x2 %0, pa, pb;\n\t}"
+      : "=l"(r)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return make_float2(__uint_as_float(static_cast<uint32_t>(r)), __uint_as_float(static_cast<uint32_t>(r >> 32)));
+}
+
 // Nibbles n (0..15) of four bytes -> four int8 (n - 8): flip bit 3, then
 // sign-extend it over the high nibble (0x08 * 0x1E = 0xF0, no carries).
 __device__ __forceinline__ uint32_t nib_to_s8(uint32_t n4) {
@@ -201,14 +224,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q4q8_mma_kernel(const MmaGemm
       uint32_t v[32];
       tmem_ld32(tmem + ((32u * q) << 16) + s * kTileN + 32 * c, v);
       tmem_ld_wait();
+      // acc += (sumi * d_w) * d_x, two columns per packed instruction (sumi
+      // -> f32 exactly as small_i2f: magic-number add, exact subtract)
+      const float2 dw2 = make_float2(dw, dw), magic = make_float2(-12582912.0f, -12582912.0f);
 #pragma unroll
       for (int j4 = 0; j4 < 8; ++j4) {
         const float4 d4 = dx4[j4];
-        const float dxv[4] = {d4.x, d4.y, d4.z, d4.w};
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int j = 4 * j4 + k;
-          acc[j] = __fadd_rn(acc[j], __fmul_rn(__fmul_rn(small_i2f(v[j]), dw), dxv[k]));
+        for (int k = 0; k < 2; ++k) {
+          const int j = 4 * j4 + 2 * k;
+          float2 f = make_float2(__int_as_float(static_cast<int>(v[j]) + 0x4B400000),
+                                 __int_as_float(static_cast<int>(v[j + 1]) + 0x4B400000));
+          f = mul2_rn(mul2_rn(add2_rn(f, magic), dw2), k ? make_float2(d4.z, d4.w) : make_float2(d4.x, d4.y));
+          acc[j] = __fadd_rn(acc[j], f.x);
+          acc[j + 1] = __fadd_rn(acc[j + 1], f.y);
         }
       }
       tc_fence_before();
