@@ -64,6 +64,13 @@ typedef enum zgpu_status {
   /* LmHeadError (lm_head.rs:31-38). */
   ZGPU_ERR_LM_NON_FINITE_LOGITS = 40,
   ZGPU_ERR_LM_ARGMAX_IN_PADDING = 41,
+  /* LoadError (kernel/src/model_loader.rs:151-160) of a .smodel container:
+   * MagicMismatch, UnsupportedFormat, InvalidContainer; and a file that
+   * cannot be opened or mapped. */
+  ZGPU_ERR_MODEL_MAGIC = 50,
+  ZGPU_ERR_MODEL_UNSUPPORTED = 51,
+  ZGPU_ERR_MODEL_INVALID = 52,
+  ZGPU_ERR_MODEL_IO = 53,
   /* runtime */
   ZGPU_ERR_NO_DEVICE = 90,
   ZGPU_ERR_CUDA = 91,
@@ -484,6 +491,48 @@ void zgpu_synth_tokens(uint64_t seed, uint64_t stream, uint64_t n, uint32_t voca
 /* Plain -> X4 (quant ZGPU_Q4_0 or ZGPU_Q8_0); rows % 4 == 0, cols % 32 == 0. */
 zgpu_status zgpu_pack_x4(const void *plain, void *x4, uint64_t rows, uint64_t cols,
                          uint32_t quant);
+
+/* ------------------------------------------------ .smodel containers */
+/* The SilicatePack native container (.smodel v1/v2) the reference's loader
+ * boots from (kernel/src/model_loader.rs:256-661; writer
+ * tools/silicatepack.py:1097-1410), mapped read-only with the loader's
+ * validation: header, SIDX index (<= 10000 entries of 104 bytes), names,
+ * tensor ranges, row-interleaved dtypes only on rank-2 tensors with rows a
+ * multiple of 4.  Only native payloads are read (a GGUF-compat payload gives
+ * ZGPU_ERR_MODEL_UNSUPPORTED). */
+typedef struct zgpu_smodel zgpu_smodel;
+typedef struct zgpu_smodel_info {
+  uint32_t version, payload_kind, flags, tensor_count;
+  uint64_t manifest_offset, manifest_len, payload_offset, payload_len, data_base;
+  /* the SIDX model fields (ModelConfig, model_loader.rs:430-480); 0xFFFFFFFF: none */
+  uint32_t architecture_id, block_count, context_length, embedding_length, feed_forward_length;
+  uint32_t head_count, head_count_kv, key_length, value_length;
+  float rope_freq_base, layer_norm_rms_epsilon;
+  uint32_t vocab_size, eos_token_id, expert_count, expert_used_count, expert_shared_count;
+  uint32_t expert_feed_forward_length, kv_lora_rank, q_lora_rank, qk_nope_head_dim, qk_rope_head_dim;
+  uint32_t v_head_dim;
+  float expert_weights_scale;
+} zgpu_smodel_info;
+typedef struct zgpu_smodel_tensor {
+  const char *name;             /* owned by the handle */
+  uint32_t dtype, rank;         /* SIDX dtype id (0 F32, 2 Q4_0, 8 Q8_0, 100 Q4_0X4, 101 Q8_0X4, ...) */
+  uint64_t shape[8];            /* HF order: shape[0] = output rows of a matmul */
+  uint64_t payload_offset, byte_len, elements;
+  const void *data;             /* the mapped bytes (the tensor's registry key) */
+} zgpu_smodel_tensor;
+zgpu_status zgpu_smodel_open(const char *path, zgpu_smodel **out);
+void zgpu_smodel_close(zgpu_smodel *m);
+/* message of the last zgpu_smodel_* failure of this thread */
+const char *zgpu_smodel_error(void);
+zgpu_status zgpu_smodel_info_get(const zgpu_smodel *m, zgpu_smodel_info *out);
+zgpu_status zgpu_smodel_manifest(const zgpu_smodel *m, const char **json, uint64_t *len);
+zgpu_status zgpu_smodel_tensor_at(const zgpu_smodel *m, uint32_t i, zgpu_smodel_tensor *out);
+zgpu_status zgpu_smodel_find(const zgpu_smodel *m, const char *name, zgpu_smodel_tensor *out);
+/* zgpu_register_weights for every rank-2 F32 / Q4_0 / Q8_0 / Q4_0X4 / Q8_0X4
+ * tensor, keyed by its mapped address (weight_layout::register keys by the
+ * same address, model_loader.rs:560-566); keep the container open while
+ * models built from it are created. */
+zgpu_status zgpu_smodel_register(zgpu_ctx *ctx, const zgpu_smodel *m, uint32_t *registered);
 
 #ifdef __cplusplus
 }

@@ -90,6 +90,13 @@ class Context:
         self._keep[_ptr(arr)] = arr
         return _ptr(arr)
 
+    def register_smodel(self, smodel) -> int:
+        """zgpu_smodel_register: every rank-2 matmul tensor of an open
+        SmodelFile, keyed by its mapped address; returns how many."""
+        n = C.c_uint32()
+        self._check(LIB.zgpu_smodel_register(self.h, smodel.h, C.byref(n)))
+        return n.value
+
     def group_of(self, arr_or_key) -> int:
         key = arr_or_key if isinstance(arr_or_key, int) else _ptr(arr_or_key)
         return int(LIB.zgpu_group_of(self.h, key))

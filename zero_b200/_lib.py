@@ -69,6 +69,25 @@ class ZgpuPerf(C.Structure):
                 ("prefill_gemm_ms", C.c_double), ("prefill_attn_ms", C.c_double)]
 
 
+class ZgpuSmodelInfo(C.Structure):
+    _fields_ = [("version", _u32), ("payload_kind", _u32), ("flags", _u32), ("tensor_count", _u32),
+                ("manifest_offset", _u64), ("manifest_len", _u64), ("payload_offset", _u64), ("payload_len", _u64),
+                ("data_base", _u64),
+                ("architecture_id", _u32), ("block_count", _u32), ("context_length", _u32),
+                ("embedding_length", _u32), ("feed_forward_length", _u32),
+                ("head_count", _u32), ("head_count_kv", _u32), ("key_length", _u32), ("value_length", _u32),
+                ("rope_freq_base", _f), ("layer_norm_rms_epsilon", _f),
+                ("vocab_size", _u32), ("eos_token_id", _u32), ("expert_count", _u32), ("expert_used_count", _u32),
+                ("expert_shared_count", _u32), ("expert_feed_forward_length", _u32), ("kv_lora_rank", _u32),
+                ("q_lora_rank", _u32), ("qk_nope_head_dim", _u32), ("qk_rope_head_dim", _u32),
+                ("v_head_dim", _u32), ("expert_weights_scale", _f)]
+
+
+class ZgpuSmodelTensor(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("dtype", _u32), ("rank", _u32), ("shape", _u64 * 8),
+                ("payload_offset", _u64), ("byte_len", _u64), ("elements", _u64), ("data", _vp)]
+
+
 _SIGS = {
     "zgpu_init": (_i32, [C.POINTER(ZgpuOpts), C.POINTER(_vp)]),
     "zgpu_destroy": (None, [_vp]),
@@ -102,6 +121,14 @@ _SIGS = {
     "zgpu_qwen3_create_tp": (_i32, [_vp, C.POINTER(ZgpuQwen3Desc), _u32, _u32, C.POINTER(_vp)]),
     "zgpu_qwen3_tp_export": (_i32, [_vp, _vp]),
     "zgpu_qwen3_tp_connect": (_i32, [_vp, _vp]),
+    "zgpu_smodel_open": (_i32, [C.c_char_p, C.POINTER(_vp)]),
+    "zgpu_smodel_close": (None, [_vp]),
+    "zgpu_smodel_error": (C.c_char_p, []),
+    "zgpu_smodel_info_get": (_i32, [_vp, C.POINTER(ZgpuSmodelInfo)]),
+    "zgpu_smodel_manifest": (_i32, [_vp, C.POINTER(C.c_void_p), C.POINTER(_u64)]),
+    "zgpu_smodel_tensor_at": (_i32, [_vp, _u32, C.POINTER(ZgpuSmodelTensor)]),
+    "zgpu_smodel_find": (_i32, [_vp, C.c_char_p, C.POINTER(ZgpuSmodelTensor)]),
+    "zgpu_smodel_register": (_i32, [_vp, _vp, C.POINTER(_u32)]),
     "zgpu_qwen3_create": (_i32, [_vp, C.POINTER(ZgpuQwen3Desc), C.POINTER(_vp)]),
     "zgpu_qwen3_destroy": (None, [_vp]),
     "zgpu_forward_single_token": (_i32, [_vp, _vp, _u32, _u32, _vp]),

@@ -53,6 +53,10 @@ const char *zgpu_status_string(zgpu_status s) {
     case ZGPU_ERR_EMBED_DIM_MISALIGNMENT: return "embedding: dim misalignment";
     case ZGPU_ERR_LM_NON_FINITE_LOGITS: return "lm head: non-finite logits";
     case ZGPU_ERR_LM_ARGMAX_IN_PADDING: return "lm head: argmax in padding region";
+    case ZGPU_ERR_MODEL_MAGIC: return "model file: magic mismatch";
+    case ZGPU_ERR_MODEL_UNSUPPORTED: return "model file: unsupported format";
+    case ZGPU_ERR_MODEL_INVALID: return "model file: invalid container";
+    case ZGPU_ERR_MODEL_IO: return "model file: cannot open or map";
     case ZGPU_ERR_NO_DEVICE: return "no usable sm_100 device";
     case ZGPU_ERR_CUDA: return "cuda error";
     case ZGPU_ERR_OUT_OF_MEMORY: return "out of device memory";

@@ -102,11 +102,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Exact int32 -> f32 for |v| < 2^22 with two full-rate ops: v + 1.5 * 2^23
-// as float bits, minus 1.5 * 2^23 (a block's |sumi| <= 32 * 8 * 127).
-__device__ __forceinline__ float small_i2f(uint32_t v) {
-  return __fsub_rn(__int_as_float(static_cast<int>(v) + 0x4B400000), 12582912.0f);
-}
 
 // Packed f32x2 add / multiply, each lane rounded to nearest.  The explicit
 // .rn keeps every one a separate rounding (PTX never contracts an add or mul
@@ -224,8 +219,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q4q8_mma_kernel(const MmaGemm
       uint32_t v[32];
       tmem_ld32(tmem + ((32u * q) << 16) + s * kTileN + 32 * c, v);
       tmem_ld_wait();
-      // acc += (sumi * d_w) * d_x, two columns per packed instruction (sumi
-      // -> f32 exactly as small_i2f: magic-number add, exact subtract)
+      // acc += (sumi * d_w) * d_x, two columns per packed instruction.  sumi
+      // -> f32 exactly: |sumi| <= 32 * 8 * 127 < 2^22, so sumi + 1.5 * 2^23
+      // taken as float bits, minus 1.5 * 2^23, is sumi
       const float2 dw2 = make_float2(dw, dw), magic = make_float2(-12582912.0f, -12582912.0f);
 #pragma unroll
       for (int j4 = 0; j4 < 8; ++j4) {
