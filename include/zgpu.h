@@ -492,6 +492,23 @@ void zgpu_synth_tokens(uint64_t seed, uint64_t stream, uint64_t n, uint32_t voca
 zgpu_status zgpu_pack_x4(const void *plain, void *x4, uint64_t rows, uint64_t cols,
                          uint32_t quant);
 
+/* ------------------------------------------------------------ sampling */
+/* lm_head_sample (kernel/src/sampler.rs:41-163) on the GPU: top-40 of
+ * logits[0, min(len, vocab_real)) kept as the reference keeps them (the
+ * running minimum replaced on a strict >, slot order preserved), scaled by
+ * 1 / temperature, softmax with the reference's exp_approx, one draw
+ * r = next_u32 / u32::MAX of the xorshift64 state *rng_state (rng.rs:23-46;
+ * Rng::new(0) starts from 0x853c49e6748fea9b, the caller's job) against the
+ * cumulative sum.  *rng_state advances by one draw.  Token and state equal
+ * the reference's bit for bit.  The reference fixes vocab_real to 151643.
+ * zgpu_sample_top_k takes host logits; zgpu_lm_head_sample samples the
+ * model's logits of its last LM-head call (as inference.rs:2024 follows
+ * lm_head with lm_head_sample). */
+zgpu_status zgpu_sample_top_k(zgpu_ctx *ctx, const float *logits, uint32_t len, uint32_t vocab_real, float temperature,
+                              uint64_t *rng_state, uint32_t *token_out);
+zgpu_status zgpu_lm_head_sample(zgpu_model *m, uint32_t vocab_real, float temperature, uint64_t *rng_state,
+                                uint32_t *token_out);
+
 /* ------------------------------------------------ .smodel containers */
 /* The SilicatePack native container (.smodel v1/v2) the reference's loader
  * boots from (kernel/src/model_loader.rs:256-661; writer

@@ -46,6 +46,9 @@ def _load() -> C.CDLL:
         "zo_quantize_q4_0_block": (None, [_f32p, _u8p]),
         "zo_quantize_q8_0_block": (None, [_f32p, _u8p]),
         "zo_quantize_row_q8_0": (None, [_f32p, _u8p, sz]),
+        "zo_rng_next_u32": (C.c_uint32, [C.POINTER(C.c_uint64)]),
+        "zo_exp_approx": (C.c_float, [C.c_float]),
+        "zo_lm_head_sample": (C.c_uint32, [_f32p, C.c_uint32, C.POINTER(C.c_uint64), C.c_float, C.c_uint32]),
         "zo_linear_q4_0_q8act": (None, [_u8p, _u8p, _f32p, sz, sz]),
         "zo_interleave_x4": (C.c_int, [_u8p, _u8p, sz, sz, C.c_int]),
         "zo_rmsnorm": (None, [_f32p, _f32p, _f32p, sz, C.c_float]),
@@ -146,6 +149,25 @@ def quantize_row_q8_0(x: np.ndarray) -> np.ndarray:
     out = np.zeros(x.size // 32 * 34, np.uint8)
     LIB.zo_quantize_row_q8_0(_f(x), _b(out), x.size)
     return out
+
+
+RNG_ZERO_SEED = 0x853C49E6748FEA9B   # Rng::new(0) (rng.rs:27-33)
+
+
+def rng_seed(seed: int) -> int:
+    return seed if seed != 0 else RNG_ZERO_SEED
+
+
+def lm_head_sample(logits: np.ndarray, rng_state: int, temperature: float, vocab_real: int = 151643):
+    """sampler.rs:41-120: returns (token, the advanced rng state)."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    st = C.c_uint64(rng_state)
+    tok = LIB.zo_lm_head_sample(_f(x), x.size, C.byref(st), C.c_float(temperature), vocab_real)
+    return int(tok), int(st.value)
+
+
+def exp_approx(x: float) -> float:
+    return float(LIB.zo_exp_approx(C.c_float(x)))
 
 
 def linear_q4_0_q8act(xq: np.ndarray, w: np.ndarray, in_dim: int, out_dim: int) -> np.ndarray:

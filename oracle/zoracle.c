@@ -898,3 +898,80 @@ int zo_run_generate(zo_run *r, const uint32_t *prompt, uint32_t n_prompt, uint32
   }
   return ZO_OK;
 }
+
+
+/* ------------------------------------------------------------ sampler */
+/* rng.rs:23-46 (Marsaglia xorshift64; a zero seed is replaced by
+ * 0x853c49e6748fea9b in Rng::new, which the caller applies). */
+uint32_t zo_rng_next_u32(uint64_t *state) {
+  uint64_t x = *state;
+  x ^= x << 13;
+  x ^= x >> 7;
+  x ^= x << 17;
+  *state = x;
+  return (uint32_t)(x >> 32);
+}
+
+/* sampler.rs:123-163, operation by operation (every multiply and add
+ * rounded on its own: the Makefile turns contraction off). */
+float zo_exp_approx(float x) {
+  if (x < -87.0f) x = -87.0f;
+  else if (x > 88.0f) x = 88.0f;
+  const float log2e = 1.44269504f;
+  const float a = x * log2e;
+  const int32_t ai = (a != a) ? 0 : (int32_t)a;   /* Rust `as i32`: truncation, NaN -> 0 */
+  const float af = a - (float)ai;
+  const float c1 = 0.69314718f, c2 = 0.2402265f, c3 = 0.0555041f;
+  const float frac = 1.0f + af * (c1 + af * (c2 + af * c3));
+  const uint32_t exp_bits = ((uint32_t)(127 + ai)) << 23;
+  float pow2_int;
+  memcpy(&pow2_int, &exp_bits, 4);
+  return pow2_int * frac;
+}
+
+uint32_t zo_lm_head_sample(const float *logits, uint32_t len, uint64_t *rng_state, float temperature,
+                           uint32_t vocab_real) {
+  enum { K = 40 };
+  const uint32_t vocab_len = len < vocab_real ? len : vocab_real;
+  float top_vals[K];
+  uint32_t top_idxs[K];
+  for (int k = 0; k < K; ++k) {
+    top_vals[k] = -INFINITY;
+    top_idxs[k] = 0;
+  }
+  float min_val = -INFINITY;
+  int min_pos = 0;
+  for (uint32_t i = 0; i < vocab_len; ++i) {
+    const float v = logits[i];
+    if (v > min_val) {
+      top_vals[min_pos] = v;
+      top_idxs[min_pos] = i;
+      min_val = INFINITY;
+      for (int k = 0; k < K; ++k)
+        if (top_vals[k] < min_val) {
+          min_val = top_vals[k];
+          min_pos = k;
+        }
+    }
+  }
+  const float inv_temp = 1.0f / temperature;
+  for (int k = 0; k < K; ++k) top_vals[k] *= inv_temp;
+  float max_logit = -INFINITY;
+  for (int k = 0; k < K; ++k)
+    if (top_vals[k] > max_logit) max_logit = top_vals[k];
+  float exp_sum = 0.0f;
+  for (int k = 0; k < K; ++k) {
+    const float e = zo_exp_approx(top_vals[k] - max_logit);
+    top_vals[k] = e;
+    exp_sum += e;
+  }
+  const float inv_sum = 1.0f / exp_sum;
+  for (int k = 0; k < K; ++k) top_vals[k] *= inv_sum;
+  const float r = (float)zo_rng_next_u32(rng_state) / (float)UINT32_MAX;
+  float cumulative = 0.0f;
+  for (int k = 0; k < K; ++k) {
+    cumulative += top_vals[k];
+    if (r < cumulative) return top_idxs[k];
+  }
+  return top_idxs[K - 1];
+}

@@ -61,6 +61,17 @@ void     zo_quantize_q4_0_block(const float *v32, uint8_t *out18);
 void     zo_quantize_q8_0_block(const float *v32, uint8_t *out34);
 /* Q8_0 activation quantiser (n % 32 == 0): one zo_quantize_q8_0_block per block. */
 void     zo_quantize_row_q8_0(const float *x, uint8_t *out, size_t n);
+/* rng.rs:23-46: xorshift64 (13, 7, 17); next_u32 = high half of next_u64. */
+uint32_t zo_rng_next_u32(uint64_t *state);
+/* sampler.rs:123-163: the sampler's own exp approximation. */
+float    zo_exp_approx(float x);
+/* sampler.rs:41-120 lm_head_sample: top-40 of logits[0 .. min(len,
+ * vocab_real)) by replacement of the running minimum (strict >, slot order
+ * kept), / temperature, softmax with zo_exp_approx, one draw r =
+ * next_u32 / u32::MAX against the cumulative sum in slot order.  The
+ * reference fixes vocab_real to 151643. */
+uint32_t zo_lm_head_sample(const float *logits, uint32_t len, uint64_t *rng_state, float temperature,
+                           uint32_t vocab_real);
 /* Plain -> .smodel-v2 4-row interleave.  quant = ZO_Q4_0 or ZO_Q8_0. */
 int      zo_interleave_x4(const uint8_t *plain, uint8_t *x4, size_t rows, size_t cols, int quant);
 

@@ -90,6 +90,14 @@ class Context:
         self._keep[_ptr(arr)] = arr
         return _ptr(arr)
 
+    def sample_top_k(self, logits: np.ndarray, rng_state: int, temperature: float, vocab_real: int = 151643):
+        """lm_head_sample (sampler.rs:41-163) on the GPU: (token, advanced rng state)."""
+        x = np.ascontiguousarray(logits, np.float32)
+        st, tok = C.c_uint64(rng_state), C.c_uint32()
+        self._check(LIB.zgpu_sample_top_k(self.h, _ptr(x), x.size, vocab_real, C.c_float(temperature),
+                                          C.byref(st), C.byref(tok)))
+        return tok.value, st.value
+
     def register_smodel(self, smodel) -> int:
         """zgpu_smodel_register: every rank-2 matmul tensor of an open
         SmodelFile, keyed by its mapped address; returns how many."""
@@ -337,6 +345,13 @@ class Qwen3Model:
         self.ctx._check(LIB.zgpu_generate_greedy(self.h, kv.h, _ptr(p), p.size, n_gen, _ptr(toks),
                                                  _ptr(logits) if want_logits else None))
         return toks, logits
+
+    def lm_head_sample(self, rng_state: int, temperature: float, vocab_real: int | None = None):
+        """lm_head_sample on the logits of the last LM-head call: (token, advanced rng state)."""
+        st, tok = C.c_uint64(rng_state), C.c_uint32()
+        self.ctx._check(LIB.zgpu_lm_head_sample(self.h, self.cfg.vocab_real if vocab_real is None else vocab_real,
+                                                C.c_float(temperature), C.byref(st), C.byref(tok)))
+        return tok.value, st.value
 
     def prefill(self, kv: KvCache, tokens, want_logits: bool = True):
         """Token-parallel prompt prefill on the tensor cores (zgpu_prefill):

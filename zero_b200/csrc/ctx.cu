@@ -624,6 +624,25 @@ zgpu_status zgpu_gqa_attention_decode_device(zgpu_ctx *ctx, zgpu_kv *kv, uint32_
                           eps, d_out, stream ? static_cast<cudaStream_t>(stream) : ctx->stream);
 }
 
+zgpu_status zgpu_sample_top_k(zgpu_ctx *ctx, const float *logits, uint32_t len, uint32_t vocab_real, float temperature,
+                              uint64_t *rng_state, uint32_t *token_out) {
+  if (!ctx || !logits || !rng_state || !token_out || len == 0 || vocab_real == 0) return ZGPU_ERR_INVALID_ARG;
+  cudaSetDevice(ctx->device);
+  zgpu_status s = ensure_scratch(ctx, len, 4);   // y: rng state (2 words) | token
+  if (s) return s;
+  unsigned long long *d_rng = reinterpret_cast<unsigned long long *>(ctx->d_y);
+  uint32_t *d_tok = reinterpret_cast<uint32_t *>(ctx->d_y + 2);
+  ZCHECK(cudaMemcpyAsync(ctx->d_x, logits, static_cast<size_t>(len) * 4, cudaMemcpyHostToDevice, ctx->stream),
+         "h2d logits");
+  ZCHECK(cudaMemcpyAsync(d_rng, rng_state, 8, cudaMemcpyHostToDevice, ctx->stream), "h2d rng");
+  ZCHECK(zgpu::launch_sample_topk(ctx->d_x, len, vocab_real, temperature, d_rng, d_tok, ctx->stream), "sample");
+  ++ctx->launches;
+  ZCHECK(cudaMemcpyAsync(token_out, d_tok, 4, cudaMemcpyDeviceToHost, ctx->stream), "d2h token");
+  ZCHECK(cudaMemcpyAsync(rng_state, d_rng, 8, cudaMemcpyDeviceToHost, ctx->stream), "d2h rng");
+  ZCHECK(cudaStreamSynchronize(ctx->stream), "sync");
+  return ZGPU_OK;
+}
+
 zgpu_status zgpu_causal_attention(zgpu_ctx *ctx, zgpu_kv *kv, uint32_t layer, uint32_t pos0, uint32_t T,
                                   uint32_t n_q_heads, const float *q, float *out) {
   if (!ctx || !kv || !q || !out || T == 0) return ZGPU_ERR_INVALID_ARG;

@@ -138,7 +138,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q4q8_mma_kernel(const MmaGemm
   __shared__ __align__(8) uint64_t full[kStages], done[kStages], empty[kStages], drain;
   __shared__ uint32_t tmem_base;
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t mt = blockIdx.x, nt = blockIdx.y;
   const uint32_t bpr = p.bpr;
 
   if (warp == 0) {
@@ -161,39 +160,58 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q4q8_mma_kernel(const MmaGemm
   tc_fence_after();
   const uint32_t tmem = tmem_base;
 
+  // Persistent tile loop: CTA c takes tiles c, c + gridDim.x, ...; tile i is
+  // (weight tile i % n_mt, token tile i / n_mt), so the CTAs of one wave share
+  // their token tile through L2.  gb counts this CTA's blocks over all its
+  // tiles and drives every stage / phase, so one tile's epilogue overlaps
+  // the next tile's copies and MMAs.
+  const uint32_t n_mt = p.rows / kTileM, n_tiles = n_mt * ((p.T + kTileN - 1) / kTileN);
   if (warp == 0) {
     // ---------------- producer ----------------
     if (lane == 0) {
-      const int8_t *wa = p.wt + static_cast<size_t>(mt) * bpr * 4096u;
-      const int8_t *xa = p.xt + static_cast<size_t>(nt) * bpr * 4096u;
-      const float *ws = p.ws + static_cast<size_t>(mt) * bpr * kTileM;
-      const float *xs = p.xs + static_cast<size_t>(nt) * bpr * kTileN;
-      uint32_t issued = 0;
-      for (uint32_t b = 0; b < bpr; ++b) {
-        const uint32_t s = b % kStages;
-        if (b >= kStages && !mbar_wait(smem_addr(&empty[s]), ((b / kStages) - 1) & 1, p.status)) break;
-        const uint32_t st = smem_addr(ring + s * kStageBytes), fb = smem_addr(&full[s]);
-        mbar_arrive_expect_tx(fb, kStageBytes);
-        bulk_copy_g2s(st + kStA, wa + static_cast<size_t>(b) * 4096u, 4096, fb);
-        bulk_copy_g2s(st + kStB, xa + static_cast<size_t>(b) * 4096u, 4096, fb);
-        bulk_copy_g2s(st + kStW, ws + static_cast<size_t>(b) * kTileM, 512, fb);
-        bulk_copy_g2s(st + kStX, xs + static_cast<size_t>(b) * kTileN, 512, fb);
-        ++issued;
+      uint32_t gb = 0;
+      bool stop = false;
+      for (uint32_t tix = blockIdx.x; tix < n_tiles && !stop; tix += gridDim.x) {
+        const uint32_t mt = tix % n_mt, nt = tix / n_mt;
+        const int8_t *wa = p.wt + static_cast<size_t>(mt) * bpr * 4096u;
+        const int8_t *xa = p.xt + static_cast<size_t>(nt) * bpr * 4096u;
+        const float *ws = p.ws + static_cast<size_t>(mt) * bpr * kTileM;
+        const float *xs = p.xs + static_cast<size_t>(nt) * bpr * kTileN;
+        for (uint32_t b = 0; b < bpr; ++b, ++gb) {
+          const uint32_t s = gb % kStages;
+          if (gb >= kStages && !mbar_wait(smem_addr(&empty[s]), ((gb / kStages) - 1) & 1, p.status)) {
+            stop = true;
+            break;
+          }
+          const uint32_t st = smem_addr(ring + s * kStageBytes), fb = smem_addr(&full[s]);
+          mbar_arrive_expect_tx(fb, kStageBytes);
+          bulk_copy_g2s(st + kStA, wa + static_cast<size_t>(b) * 4096u, 4096, fb);
+          bulk_copy_g2s(st + kStB, xa + static_cast<size_t>(b) * 4096u, 4096, fb);
+          bulk_copy_g2s(st + kStW, ws + static_cast<size_t>(b) * kTileM, 512, fb);
+          bulk_copy_g2s(st + kStX, xs + static_cast<size_t>(b) * kTileN, 512, fb);
+        }
       }
       // never leave a copy in flight when the CTA may exit
-      for (uint32_t j = issued > kStages ? issued - kStages : 0; j < issued; ++j)
+      for (uint32_t j = gb > kStages ? gb - kStages : 0; j < gb; ++j)
         mbar_wait(smem_addr(&full[j % kStages]), (j / kStages) & 1, p.status);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      for (uint32_t b = 0; b < bpr; ++b) {
-        const uint32_t s = b % kStages;
-        if (!mbar_wait(smem_addr(&full[s]), (b / kStages) & 1, p.status)) break;
-        tc_fence_after();
-        const uint32_t st = smem_addr(ring + s * kStageBytes);
-        umma_i8(tmem + s * kTileN, umma_desc(st + kStA, 128, 256), umma_desc(st + kStB, 128, 256), kIdesc, 0u);
-        umma_commit(smem_addr(&done[s]));
+      uint32_t gb = 0;
+      bool stop = false;
+      for (uint32_t tix = blockIdx.x; tix < n_tiles && !stop; tix += gridDim.x) {
+        for (uint32_t b = 0; b < bpr; ++b, ++gb) {
+          const uint32_t s = gb % kStages;
+          if (!mbar_wait(smem_addr(&full[s]), (gb / kStages) & 1, p.status)) {
+            stop = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_addr(ring + s * kStageBytes);
+          umma_i8(tmem + s * kTileN, umma_desc(st + kStA, 128, 256), umma_desc(st + kStB, 128, 256), kIdesc, 0u);
+          umma_commit(smem_addr(&done[s]));
+        }
       }
       // every MMA of this thread has completed before TMEM is freed
       umma_commit(smem_addr(&drain));
@@ -202,52 +220,56 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q4q8_mma_kernel(const MmaGemm
   } else {
     // ---------------- epilogue ----------------
     const uint32_t q = warp & 3, c = (warp - 2) >> 2;   // TMEM lane quarter, token quarter
-    float acc[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+    uint32_t gb = 0;
     bool ok = true;
-    for (uint32_t b = 0; b < bpr && ok; ++b) {
-      const uint32_t s = b % kStages, par = (b / kStages) & 1;
-      if (!mbar_wait(smem_addr(&done[s]), par, p.status) || !mbar_wait(smem_addr(&full[s]), par, p.status)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint8_t *st = ring + s * kStageBytes;
-      const float dw = reinterpret_cast<const float *>(st + kStW)[32 * q + lane];
-      const float4 *dx4 = reinterpret_cast<const float4 *>(st + kStX) + 8 * c;
-      uint32_t v[32];
-      tmem_ld32(tmem + ((32u * q) << 16) + s * kTileN + 32 * c, v);
-      tmem_ld_wait();
-      // acc += (sumi * d_w) * d_x, two columns per packed instruction.  sumi
-      // -> f32 exactly: |sumi| <= 32 * 8 * 127 < 2^22, so sumi + 1.5 * 2^23
-      // taken as float bits, minus 1.5 * 2^23, is sumi
-      const float2 dw2 = make_float2(dw, dw), magic = make_float2(-12582912.0f, -12582912.0f);
+    for (uint32_t tix = blockIdx.x; tix < n_tiles; tix += gridDim.x) {
+      const uint32_t mt = tix % n_mt, nt = tix / n_mt;
+      float acc[32];
 #pragma unroll
-      for (int j4 = 0; j4 < 8; ++j4) {
-        const float4 d4 = dx4[j4];
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int j = 4 * j4 + 2 * k;
-          float2 f = make_float2(__int_as_float(static_cast<int>(v[j]) + 0x4B400000),
-                                 __int_as_float(static_cast<int>(v[j + 1]) + 0x4B400000));
-          f = mul2_rn(mul2_rn(add2_rn(f, magic), dw2), k ? make_float2(d4.z, d4.w) : make_float2(d4.x, d4.y));
-          acc[j] = __fadd_rn(acc[j], f.x);
-          acc[j + 1] = __fadd_rn(acc[j + 1], f.y);
+      for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+      for (uint32_t b = 0; b < bpr && ok; ++b, ++gb) {
+        const uint32_t s = gb % kStages, par = (gb / kStages) & 1;
+        if (!mbar_wait(smem_addr(&done[s]), par, p.status) || !mbar_wait(smem_addr(&full[s]), par, p.status)) {
+          ok = false;
+          break;
         }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&empty[s]));
-    }
-    const uint32_t row = mt * kTileM + 32 * q + lane;
+        tc_fence_after();
+        const uint8_t *st = ring + s * kStageBytes;
+        const float dw = reinterpret_cast<const float *>(st + kStW)[32 * q + lane];
+        const float4 *dx4 = reinterpret_cast<const float4 *>(st + kStX) + 8 * c;
+        uint32_t v[32];
+        tmem_ld32(tmem + ((32u * q) << 16) + s * kTileN + 32 * c, v);
+        tmem_ld_wait();
+        // acc += (sumi * d_w) * d_x, two columns per packed instruction.  sumi
+        // -> f32 exactly: |sumi| <= 32 * 8 * 127 < 2^22, so sumi + 1.5 * 2^23
+        // taken as float bits, minus 1.5 * 2^23, is sumi
+        const float2 dw2 = make_float2(dw, dw), magic = make_float2(-12582912.0f, -12582912.0f);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const uint32_t t = nt * kTileN + 32 * c + j;
-      if (t < p.T) {
-        float *dst = p.y + static_cast<uint64_t>(t) * p.ldy + row;
-        const float val = ok ? acc[j] : __uint_as_float(0x7fc00000u);
-        *dst = p.resadd ? __fadd_rn(*dst, val) : val;
+        for (int j4 = 0; j4 < 8; ++j4) {
+          const float4 d4 = dx4[j4];
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const int j = 4 * j4 + 2 * k;
+            float2 f = make_float2(__int_as_float(static_cast<int>(v[j]) + 0x4B400000),
+                                   __int_as_float(static_cast<int>(v[j + 1]) + 0x4B400000));
+            f = mul2_rn(mul2_rn(add2_rn(f, magic), dw2), k ? make_float2(d4.z, d4.w) : make_float2(d4.x, d4.y));
+            acc[j] = __fadd_rn(acc[j], f.x);
+            acc[j + 1] = __fadd_rn(acc[j + 1], f.y);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(&empty[s]));
+      }
+      const uint32_t row = mt * kTileM + 32 * q + lane;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const uint32_t t = nt * kTileN + 32 * c + j;
+        if (t < p.T) {
+          float *dst = p.y + static_cast<uint64_t>(t) * p.ldy + row;
+          const float val = ok ? acc[j] : __uint_as_float(0x7fc00000u);
+          *dst = p.resadd ? __fadd_rn(*dst, val) : val;
+        }
       }
     }
   }
@@ -299,14 +321,24 @@ __global__ void quantize_q8_0_tiles_kernel(const float *x, int8_t *xt, float *xs
 
 }  // namespace
 
+namespace {
+int g_sm_count = 0;   // SMs of the device (one resident CTA each)
+}
+
 cudaError_t mma_setup() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(q4q8_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem);
 }
 
 cudaError_t launch_q4q8_mma(const MmaGemmParams &p, cudaStream_t s) {
-  if (p.rows == 0 || p.rows % kTileM || p.bpr == 0 || p.T == 0 || !p.wt || !p.ws || !p.xt || !p.xs)
+  if (p.rows == 0 || p.rows % kTileM || p.bpr == 0 || p.T == 0 || !p.wt || !p.ws || !p.xt || !p.xs ||
+      g_sm_count <= 0)
     return cudaErrorInvalidValue;
-  dim3 grid(p.rows / kTileM, (p.T + kTileN - 1) / kTileN);
+  const uint64_t tiles = static_cast<uint64_t>(p.rows / kTileM) * ((p.T + kTileN - 1) / kTileN);
+  const unsigned grid = static_cast<unsigned>(tiles < static_cast<uint64_t>(g_sm_count) ? tiles : g_sm_count);
   q4q8_mma_kernel<<<grid, kGemmThreads, kDynSmem, s>>>(p);
   return cudaGetLastError();
 }

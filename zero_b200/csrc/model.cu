@@ -1115,6 +1115,30 @@ zgpu_status zgpu_generate_greedy(zgpu_model *m, zgpu_kv *kv, const uint32_t *pro
   return map_status(ctx, st);
 }
 
+zgpu_status zgpu_lm_head_sample(zgpu_model *m, uint32_t vocab_real, float temperature, uint64_t *rng_state,
+                                uint32_t *token_out) {
+  if (!m || !rng_state || !token_out || vocab_real == 0) return ZGPU_ERR_INVALID_ARG;
+  if (m->world > 1)
+    return zgpu_fail(m->ctx, ZGPU_ERR_INVALID_ARG, "tensor-parallel ranks decode through zgpu_generate_greedy");
+  zgpu_ctx *ctx = m->ctx;
+  cudaSetDevice(ctx->device);
+  cudaError_t e = grow(&m->d_tokens, &m->tokens_cap, 1);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "state buffers");
+  unsigned long long *d_rng = nullptr;
+  if ((e = cudaMallocAsync(reinterpret_cast<void **>(&d_rng), 8, ctx->stream)) != cudaSuccess)
+    return zgpu_cuda_fail(ctx, e, "rng state");
+  e = cudaMemcpyAsync(d_rng, rng_state, 8, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess)
+    e = launch_sample_topk(m->d_logits, m->desc.vocab_padded, vocab_real, temperature, d_rng, m->d_tokens, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(token_out, m->d_tokens, 4, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(rng_state, d_rng, 8, cudaMemcpyDeviceToHost, ctx->stream);
+  cudaFreeAsync(d_rng, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "lm_head_sample");
+  ++ctx->launches;
+  return ZGPU_OK;
+}
+
 zgpu_status zgpu_perf_snapshot(const zgpu_model *m, zgpu_perf *out) {
   if (!m || !out) return ZGPU_ERR_INVALID_ARG;
   *out = m->perf;
@@ -1197,13 +1221,13 @@ zgpu_status prefill_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, cons
       }
     }
   }
-  // scratch: tokens | hidden [NT][H] | qkv [NT][QKV] | qrot [NT][QD] | attn [NT][QD] | gu [NT][2F] | act [NT][F]
+  // scratch: tokens | hidden [NT][H] | qkv [NT][QKV] | qrot [NT][QD] | attn [NT][QD] | gu [NT][2F]
   //          | activation tiles and scales for the widest input
   const size_t N = NT, maxk = std::max(std::max(H, QD), F);
   auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
   const size_t o_tok = 0, o_hid = al(N * 4), o_qkv = o_hid + al(N * H * 4), o_qr = o_qkv + al(N * QKV * 4),
-               o_at = o_qr + al(N * QD * 4), o_gu = o_at + al(N * QD * 4), o_act = o_gu + al(N * 2 * F * 4),
-               o_q8 = o_act + al(N * F * 4), o_d8 = o_q8 + al(mma_tile_bytes(N, maxk / 32)),
+               o_at = o_qr + al(N * QD * 4), o_gu = o_at + al(N * QD * 4), o_q8 = o_gu + al(N * 2 * F * 4),
+               o_d8 = o_q8 + al(mma_tile_bytes(N, maxk / 32)),
                total = o_d8 + al(mma_scale_bytes(N, maxk / 32));
   if (total > m->pf_cap) {
     cudaFree(m->d_pf);
@@ -1217,7 +1241,7 @@ zgpu_status prefill_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, cons
   uint32_t *d_tok = reinterpret_cast<uint32_t *>(B + o_tok);
   float *hid = reinterpret_cast<float *>(B + o_hid), *qkv = reinterpret_cast<float *>(B + o_qkv),
         *qr = reinterpret_cast<float *>(B + o_qr), *at = reinterpret_cast<float *>(B + o_at),
-        *gu = reinterpret_cast<float *>(B + o_gu), *act = reinterpret_cast<float *>(B + o_act);
+        *gu = reinterpret_cast<float *>(B + o_gu);
   int8_t *q8 = reinterpret_cast<int8_t *>(B + o_q8);
   float *d8 = reinterpret_cast<float *>(B + o_d8);
   cudaStream_t s = ctx->stream;
@@ -1281,10 +1305,9 @@ zgpu_status prefill_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, cons
     if ((e = gemm(l, 1, H, QD, hid, true))) break;
     if ((e = launch_rows_rmsnorm_quant(hid, norm_ffn(m, l), d.rms_eps, T, H, q8, d8, m->d_status, s))) break;
     if ((e = gemm(l, 2, 2 * F, H, gu, false))) break;
-    if ((e = launch_swiglu_rows(gu, act, T, F, s))) break;
-    if ((e = launch_quantize_q8_0_tiles(act, q8, d8, T, F, m->d_status, s))) break;
+    if ((e = launch_swiglu_quant_tiles(gu, q8, d8, T, F, m->d_status, s))) break;
     if ((e = gemm(l, 3, H, F, hid, true))) break;
-    launches += 5;
+    launches += 4;
   }
   cudaEventRecord(m->ev[1], s);
   if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "prefill");

@@ -144,6 +144,15 @@ cudaError_t launch_causal_attn(const float *q, const float *kv_layer, uint64_t k
                                uint32_t pos0, uint32_t T, float scale, float *out, uint32_t *status,
                                cudaStream_t s);
 cudaError_t launch_swiglu_rows(const float *y, float *act, uint32_t T, uint32_t ffn, cudaStream_t s);
+// SwiGLU of the gate/up rows, Q8_0-quantised into activation tiles (as
+// launch_quantize_q8_0_tiles of swiglu_rows' output, in one pass)
+cudaError_t launch_swiglu_quant_tiles(const float *y, int8_t *xt, float *xs, uint32_t T, uint32_t ffn,
+                                      uint32_t *status, cudaStream_t s);
+
+// lm_head_sample (sampler.rs:41-163) over logits[0, min(len, vocab_real)):
+// one warp; *rng is the xorshift64 state, advanced by one draw; *out the token.
+cudaError_t launch_sample_topk(const float *logits, uint32_t len, uint32_t vocab_real, float temperature,
+                               unsigned long long *rng, uint32_t *out, cudaStream_t s);
 
 cudaError_t launch_attention(const AttnParams &ap, const LaunchCfg &lc);
 // Number of attention splits (CTAs per kv-head) a cache of max_tokens needs.

@@ -18,7 +18,9 @@
 //                     groups, else a warp-per-row kernel over 32-key tiles;
 //                     NumericalInstability as attention.rs:48
 //   swiglu_rows       SiLU(gate) * up on the gate/up matmul's unit layout
-//                     (silu_mul_avx512, activation.rs:115-148)
+//                     (silu_mul_avx512, activation.rs:115-148); the prefill
+//                     uses swiglu_quant_tiles, the same product quantised
+//                     straight into the down projection's Q8_0 tiles
 #include <cfloat>
 #include <cmath>
 
@@ -422,7 +424,41 @@ __global__ void swiglu_rows_kernel(const float *y, float *act, uint32_t ffn, uin
   act[i] = ref_silu_mul(yr[8 * u + r], yr[8 * u + 4 + r]);
 }
 
+// SwiGLU fused with the Q8_0 rule into the down projection's activation
+// tiles: warp (row t, block b) of the padded row count; lane j is feature
+// f = 32b + j = 4u + r of the gate/up unit layout, act = silu(y[8u + r]) *
+// y[8u + 4 + r], then quantised as quantize_q8_0_tiles does (rows past T:
+// zero digits, scale 0).
+__global__ void swiglu_quant_tiles_kernel(const float *y, int8_t *xt, float *xs, uint32_t T, uint32_t ffn,
+                                          uint64_t nwarps, uint32_t *status) {
+  const uint64_t wb = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const uint32_t lane = threadIdx.x & 31;
+  if (wb >= nwarps) return;
+  const uint32_t bpr = ffn / 32;
+  const uint32_t t = static_cast<uint32_t>(wb / bpr), b = static_cast<uint32_t>(wb % bpr);
+  int8_t *qa = xt + mma_tile_off(t, b, bpr, lane >> 4) + (lane & 15);
+  float *da = xs + mma_scale_off(t, b, bpr);
+  if (t >= T) {
+    *qa = 0;
+    if (lane == 0) *da = 0.f;
+    return;
+  }
+  const uint32_t f = 32 * b + lane, u = f >> 2, r = f & 3;
+  const float *yr = y + static_cast<uint64_t>(t) * 2 * ffn;
+  quant_lane_q8_0(ref_silu_mul(yr[8 * u + r], yr[8 * u + 4 + r]), qa, da, lane, status);
+}
+
 }  // namespace
+
+cudaError_t launch_swiglu_quant_tiles(const float *y, int8_t *xt, float *xs, uint32_t T, uint32_t ffn,
+                                      uint32_t *status, cudaStream_t s) {
+  if (T == 0 || ffn == 0 || ffn % 32) return cudaErrorInvalidValue;
+  const uint64_t rows = (static_cast<uint64_t>(T) + kMmaTile - 1) / kMmaTile * kMmaTile;
+  const uint64_t nwarps = rows * (ffn / 32);
+  swiglu_quant_tiles_kernel<<<static_cast<unsigned>((nwarps * 32 + 255) / 256), 256, 0, s>>>(y, xt, xs, T, ffn,
+                                                                                           nwarps, status);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_rows_rmsnorm_quant(const float *x, const float *g, float eps, uint32_t T, uint32_t n, int8_t *xt,
                                       float *xs, uint32_t *status, cudaStream_t s) {
