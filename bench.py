@@ -62,7 +62,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the per-token C-ABI loop")
     ap.add_argument("--no-roofline", action="store_true", help="skip the standalone GEMV sweep")
-    ap.add_argument("--workload", default="qwen3", choices=["qwen3", "ds2", "prefill", "qwen3-8b"],
+    ap.add_argument("--workload", default="qwen3", choices=["qwen3", "ds2", "prefill", "qwen3-8b", "kquant"],
                     help="qwen3: BASELINE config 0 (the headline); ds2: the config-3 DeepSeek2 "
                          "MLA+MoE model, one sequence, as a secondary line")
     ap.add_argument("--context", type=int, default=2048, help="ds2: tokens in the cache before decode")
@@ -627,9 +627,181 @@ def run_prefill(args, rank, world, local):
     ctx.close()
 
 
+KQUANT_METRIC = "K-quant GEMV weight GB/s, one token's matmuls of a Qwen3-1.7B-shape Q4_K/Q6_K model"
+
+
+def kquant_mats(cfg) -> list[tuple[str, str, int, int]]:
+    """(name, quant, rows, cols) of one token's matmuls in a Q4_K_M-style mix:
+    Q6_K for the V projection, the FFN down projection and the LM head, Q4_K
+    for the rest (the GGUF-compat path's linear_q4k / linear_q6k)."""
+    h, q, kv, f = cfg.hidden, cfg.q_dim, cfg.kv_dim, cfg.ffn
+    mats = []
+    for i in range(cfg.n_layers):
+        mats += [(f"blk.{i}.attn_q", "q4_k", q, h), (f"blk.{i}.attn_k", "q4_k", kv, h),
+                 (f"blk.{i}.attn_v", "q6_k", kv, h), (f"blk.{i}.attn_output", "q4_k", h, q),
+                 (f"blk.{i}.ffn_gate", "q4_k", f, h), (f"blk.{i}.ffn_up", "q4_k", f, h),
+                 (f"blk.{i}.ffn_down", "q6_k", h, f)]
+    mats.append(("output", "q6_k", cfg.vocab_padded, h))
+    return mats
+
+
+def kquant_bytes(quant: str, rows: int, cols: int) -> int:
+    return rows * (cols // 256) * (144 if quant == "q4_k" else 210)
+
+
+def cpu_kquant(mats, weights, xs, threads: int, budget_s: float = 20.0):
+    """The oracle's linear_q4k / linear_q6k restatement over the matmuls in
+    order, rows split across `threads` (ctypes drops the GIL); stops after
+    budget_s.  Returns (GB/s, matrices done, seconds)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    import oracle as O
+
+    done, nbytes, t0 = 0, 0, time.perf_counter()
+    with ThreadPoolExecutor(threads) as pool:
+        for (name, quant, rows, cols), w in zip(mats, weights):
+            x = xs[cols]
+            per = (rows + threads - 1) // threads
+            bpr = kquant_bytes(quant, 1, cols)
+            parts = [(r0, min(rows, r0 + per)) for r0 in range(0, rows, per)]
+            list(pool.map(lambda p: O.linear_kquant(x, w[p[0] * bpr:p[1] * bpr], cols, p[1] - p[0], quant),
+                          parts))
+            done += 1
+            nbytes += w.nbytes
+            if time.perf_counter() - t0 > budget_s:
+                break
+    dt = time.perf_counter() - t0
+    return nbytes / dt / 1e9, done, dt
+
+
+def run_kquant(args, rank, world, local):
+    """The GGUF-compat matmul path at Qwen3-1.7B shape: a step is one token's
+    197 GEMVs (28 layers x 7 + the LM head) through zgpu_linear_dispatch_device,
+    captured once as a CUDA graph and replayed.  The 1.15 GB of weights is
+    far above the 126 MB L2, so no flush is needed between steps."""
+    from zero_b200 import synth
+
+    if world > 1:
+        raise SystemExit("the kquant workload runs on one GPU")
+    cfg = synth.QWEN3_1_7B
+    mats = kquant_mats(cfg)
+    weights = [synth.kquant(SEED + i, rows, cols, quant) for i, (_, quant, rows, cols) in enumerate(mats)]
+    step_bytes = sum(w.nbytes for w in weights)
+    rng = np.random.default_rng(SEED)
+    xs = {c: rng.standard_normal(c).astype(np.float32) for c in {m[3] for m in mats}}
+    cores = physical_cores()
+    if args.impl == "reference":
+        gbs, done, dt = cpu_kquant(mats, weights, xs, cores)
+        sample = f"the first {done} of {len(mats)} matmuls of one step, {dt:.1f} s"
+        print(json.dumps({
+            "impl": "reference", "metric": KQUANT_METRIC, "value": round(gbs, 3), "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": 1, "warmup": 0, "ms_per_step": round(1000 * step_bytes / 1e9 / gbs, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random Q4_K / Q6_K super-blocks)",
+            "config": {"workload": "qwen3-1.7b-shape q4_k_m-style decode matmuls b=1", "parallelism": "cpu threads"},
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+            flush=True)
+        return
+    import torch
+
+    import zero_b200 as zb
+
+    ctx = zb.Context(device=local)
+    qt = {"q4_k": zb.Q4_K, "q6_k": zb.Q6_K}
+    keys = [ctx.register(w, qt[q], rows, cols) for w, (_, q, rows, cols) in zip(weights, mats)]
+    d_x = {c: torch.from_numpy(v).cuda() for c, v in xs.items()}
+    d_y = torch.empty(max(m[2] for m in mats), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+
+    def sweep(s):
+        for key, (_, q, rows, cols) in zip(keys, mats):
+            ctx.linear_dispatch_device(d_x[cols].data_ptr(), key, d_y.data_ptr(), cols, rows, qt[q], s)
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            sweep(stream.cuda_stream)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            sweep(torch.cuda.current_stream().cuda_stream)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(physical_gpu_index(local)) as clocks:
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        step_ms = e0.elapsed_time(e1) / args.steps
+        # the dominant kernel alone: the Q6_K LM head GEMV (255 MB per launch)
+        key, (_, q, rows, cols) = keys[-1], mats[-1]
+        reps = 64
+        with torch.cuda.stream(stream):
+            ctx.linear_dispatch_device(d_x[cols].data_ptr(), key, d_y.data_ptr(), cols, rows, qt[q],
+                                       stream.cuda_stream)
+            e0.record(stream)
+            for _ in range(reps):
+                ctx.linear_dispatch_device(d_x[cols].data_ptr(), key, d_y.data_ptr(), cols, rows, qt[q],
+                                           stream.cuda_stream)
+            e1.record(stream)
+        torch.cuda.synchronize()
+        lm_us = 1000 * e0.elapsed_time(e1) / reps
+    launches = len(mats) * args.steps   # kernels the timed graph replays launch
+    # e2e: the reference-facing host-buffer call per matmul (x in, y out every call)
+    t0 = time.perf_counter()
+    for key, (_, q, rows, cols) in zip(keys, mats):
+        ctx.linear_dispatch(xs[cols], key, cols, rows, qt[q])
+    e2e_s = time.perf_counter() - t0
+    h2d = sum(4 * m[3] for m in mats)
+    d2h = sum(4 * m[2] for m in mats)
+    peaks = measured_peaks()
+    gbs = step_bytes / (step_ms / 1000) / 1e9
+    lm_bytes = weights[-1].nbytes + 4 * (mats[-1][3] + mats[-1][2])
+    lm_gbs = lm_bytes / (lm_us / 1e6) / 1e9
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        c_gbs, done, dt = cpu_kquant(mats, weights, xs, cores)
+        cpu = {"value": round(c_gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+               "sample": f"the first {done} of {len(mats)} matmuls of one step through the oracle's "
+                         f"linear_q4k / linear_q6k, rows across {cores} threads, {dt:.1f} s"}
+    print(json.dumps({
+        "metric": KQUANT_METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (weights Q4_K / Q6_K)",
+        "data": "synthetic (seeded random Q4_K / Q6_K super-blocks)",
+        "config": {"workload": "qwen3-1.7b-shape q4_k_m-style decode matmuls b=1", "matmuls_per_step": len(mats),
+                   "weight_bytes_per_step": step_bytes, "tok_s_equivalent": round(1000 / step_ms, 1),
+                   "l2": "inputs larger than L2 (1.15 GB of weights per step)", "parallelism": "single GPU",
+                   "cuda_graph": True},
+        "roofline": {"bound": "hbm", "kernel": "gemv_kquant_kernel<Q6_K> (LM head 151936 x 2048)",
+                     "achieved": round(lm_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(lm_gbs / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
+                     "traffic": None, "algorithmic_bytes": lm_bytes, "avg_launch_us": round(lm_us, 2)},
+        "e2e": {"value": round(step_bytes / e2e_s / 1e9, 2), "unit": "GB/s",
+                "scope": "zgpu_linear_dispatch per matmul with host x / y buffers, host wall clock",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+        "cpu_baseline": cpu,
+    }), flush=True)
+    ctx.close()
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
+    if args.workload == "kquant":
+        if args.impl != "reference":
+            import torch
+
+            torch.cuda.set_device(local)
+        run_kquant(args, rank, world, local)
+        return
     if args.workload == "ds2":
         if args.impl != "reference":
             import torch

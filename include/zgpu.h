@@ -38,6 +38,10 @@ enum zgpu_dtype {
   ZGPU_F16 = 1,
   ZGPU_Q4_0 = 2,
   ZGPU_Q8_0 = 8,
+  /* GGUF K-quants, plain rows of 256-element super-blocks (the GGUF-compat
+   * path: dequant.rs:63-138, 286-356): 144 / 210 bytes per super-block. */
+  ZGPU_Q4_K = 12,
+  ZGPU_Q6_K = 14,
   ZGPU_Q4_0X4 = 100,
   ZGPU_Q8_0X4 = 101
 };
@@ -112,8 +116,10 @@ zgpu_status zgpu_synchronize(zgpu_ctx *ctx);
 /* ------------------------------------------------------- weight registry */
 /* Upload one tensor and key it by `host_ptr` (weight_layout.rs:40 register,
  * model_loader.rs:532-570).  dtype is ZGPU_Q4_0 / ZGPU_Q8_0 (plain row
- * blocks), ZGPU_Q4_0X4 / ZGPU_Q8_0X4 (.smodel v2 4-row interleave) or
- * ZGPU_F32.  rows/cols give the logical matrix (cols = in_dim). */
+ * blocks), ZGPU_Q4_0X4 / ZGPU_Q8_0X4 (.smodel v2 4-row interleave),
+ * ZGPU_Q4_K / ZGPU_Q6_K (plain rows of 144 / 210-byte super-blocks, cols a
+ * multiple of 256) or ZGPU_F32.  rows/cols give the logical matrix
+ * (cols = in_dim). */
 zgpu_status zgpu_register_weights(zgpu_ctx *ctx, const void *host_ptr, size_t len,
                                   uint32_t dtype, uint64_t rows, uint64_t cols);
 /* weight_layout.rs:133 group_of: 4 for an interleaved registration, 1
@@ -126,9 +132,11 @@ zgpu_status zgpu_clear_weights(zgpu_ctx *ctx);
 /* out[out_dim] = W[out_dim x in_dim] . x[in_dim] with host x/out buffers.
  * Mirrors linear_dispatch (ops.rs:486-523) and linear_dispatch_avx512
  * (inference_avx512.rs:1147-1185); `w_key` is the registered host address.
- * quant is the ggml type of the tensor (Q4_0 or Q8_0); the stored layout
- * (plain or X4) comes from the registry, as group_of decides at
- * inference_avx512.rs:638. */
+ * quant is the ggml type of the tensor (Q4_0, Q8_0, Q4_K or Q6_K: the four
+ * linear_dispatch accepts; any other is ZGPU_ERR_UNSUPPORTED_QUANT where the
+ * reference panics); the stored layout (plain or X4) comes from the
+ * registry, as group_of decides at inference_avx512.rs:638.  Q4_K / Q6_K
+ * follow linear_q4k / linear_q6k (ops.rs:179-292). */
 zgpu_status zgpu_linear_dispatch(zgpu_ctx *ctx, const float *x, const void *w_key, float *out,
                                  uint64_t in_dim, uint64_t out_dim, uint32_t quant);
 /* Same with device-resident x/out on `stream` (no host copies, async). */

@@ -47,6 +47,10 @@ def _load() -> C.CDLL:
         "zo_quantize_q8_0_block": (None, [_f32p, _u8p]),
         "zo_quantize_row_q8_0": (None, [_f32p, _u8p, sz]),
         "zo_rng_next_u32": (C.c_uint32, [C.POINTER(C.c_uint64)]),
+        "zo_dequant_q4_k_block": (None, [_u8p, _f32p]),
+        "zo_dequant_q6_k_block": (None, [_u8p, _f32p]),
+        "zo_linear_q4_k": (None, [_f32p, _u8p, _f32p, sz, sz]),
+        "zo_linear_q6_k": (None, [_f32p, _u8p, _f32p, sz, sz]),
         "zo_exp_approx": (C.c_float, [C.c_float]),
         "zo_lm_head_sample": (C.c_uint32, [_f32p, C.c_uint32, C.POINTER(C.c_uint64), C.c_float, C.c_uint32]),
         "zo_linear_q4_0_q8act": (None, [_u8p, _u8p, _f32p, sz, sz]),
@@ -164,6 +168,22 @@ def lm_head_sample(logits: np.ndarray, rng_state: int, temperature: float, vocab
     st = C.c_uint64(rng_state)
     tok = LIB.zo_lm_head_sample(_f(x), x.size, C.byref(st), C.c_float(temperature), vocab_real)
     return int(tok), int(st.value)
+
+
+def dequant_kquant_block(blk, quant: str) -> np.ndarray:
+    """One Q4_K (144 bytes) or Q6_K (210 bytes) super-block -> 256 floats."""
+    b = np.ascontiguousarray(np.frombuffer(bytes(blk), np.uint8))
+    out = np.zeros(256, np.float32)
+    (LIB.zo_dequant_q4_k_block if quant == "q4_k" else LIB.zo_dequant_q6_k_block)(_b(b), _f(out))
+    return out
+
+
+def linear_kquant(x: np.ndarray, w: np.ndarray, in_dim: int, out_dim: int, quant: str) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros(out_dim, np.float32)
+    (LIB.zo_linear_q4_k if quant == "q4_k" else LIB.zo_linear_q6_k)(_f(x), _b(np.ascontiguousarray(w, np.uint8)),
+                                                                    _f(out), in_dim, out_dim)
+    return out
 
 
 def exp_approx(x: float) -> float:

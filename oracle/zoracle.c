@@ -260,10 +260,88 @@ void zo_linear_q8_0(const float *x, const uint8_t *w, float *out, size_t in_dim,
 
 /* ops.rs:486-523 (linear_dispatch).  The reference panics on an
  * unsupported quant; the oracle returns ZO_ERR_UNSUPPORTED_QUANT. */
+/* dequant.rs:75-85 get_scale_min_k4: 6-bit sub-block scale and min j of
+ * the 12 packed bytes. */
+static void q4k_scale_min(const uint8_t *sc, int j, uint8_t *d, uint8_t *m) {
+  if (j < 4) {
+    *d = sc[j] & 0x3F;
+    *m = sc[j + 4] & 0x3F;
+  } else {
+    *d = (uint8_t)((sc[j + 4] & 0x0F) | ((sc[j - 4] >> 6) << 4));
+    *m = (uint8_t)((sc[j + 4] >> 4) | ((sc[j] >> 6) << 4));
+  }
+}
+
+/* dequant_q4k_block (zero-gguf-parser/src/dequant.rs:98-138, scales by
+ * get_scale_min_k4 at :75-85): d, dmin fp16; four 64-element groups, the low nibbles
+ * of qs[32 g ..] with sub-block 2g's scale / min, the high nibbles with 2g+1's;
+ * out = (d * sc) * q - dmin * mn, each product rounded on its own. */
+void zo_dequant_q4_k_block(const uint8_t *blk, float *out) {
+  const float d = zo_fp16_to_f32(rd16(blk)), dmin = zo_fp16_to_f32(rd16(blk + 2));
+  const uint8_t *sc = blk + 4, *qs = blk + 16;
+  for (int g = 0; g < 4; ++g) {
+    uint8_t s0, m0, s1, m1;
+    q4k_scale_min(sc, 2 * g, &s0, &m0);
+    q4k_scale_min(sc, 2 * g + 1, &s1, &m1);
+    const float d1 = d * (float)s0, mn1 = dmin * (float)m0;
+    const float d2 = d * (float)s1, mn2 = dmin * (float)m1;
+    for (int l = 0; l < 32; ++l) out[64 * g + l] = d1 * (float)(qs[32 * g + l] & 0xF) - mn1;
+    for (int l = 0; l < 32; ++l) out[64 * g + 32 + l] = d2 * (float)(qs[32 * g + l] >> 4) - mn2;
+  }
+}
+
+/* dequant_q6k_block (zero-gguf-parser/src/dequant.rs:328-360, the ggml
+ * dequantize_row_q6_K order): two 128-element halves; element 128 h + l + 32 k
+ * takes a 4-bit part of ql and a 2-bit part of qh, minus 32, times
+ * d * scale (left to right) with scale = int8 sc[8 h + l / 16 + 2 k]. */
+void zo_dequant_q6_k_block(const uint8_t *blk, float *out) {
+  const float d = zo_fp16_to_f32(rd16(blk + 208));
+  const uint8_t *ql = blk, *qh = blk + 128, *sc = blk + 192;
+  for (int h = 0; h < 2; ++h) {
+    const uint8_t *l0 = ql + 64 * h, *h0 = qh + 32 * h;
+    const int8_t *s0 = (const int8_t *)sc + 8 * h;
+    for (int l = 0; l < 32; ++l) {
+      const int is = l / 16;
+      const int q1 = ((l0[l] & 0xF) | ((h0[l] & 3) << 4)) - 32;
+      const int q2 = ((l0[l + 32] & 0xF) | (((h0[l] >> 2) & 3) << 4)) - 32;
+      const int q3 = ((l0[l] >> 4) | (((h0[l] >> 4) & 3) << 4)) - 32;
+      const int q4 = ((l0[l + 32] >> 4) | (((h0[l] >> 6) & 3) << 4)) - 32;
+      out[128 * h + l] = d * (float)s0[is] * (float)q1;
+      out[128 * h + l + 32] = d * (float)s0[is + 2] * (float)q2;
+      out[128 * h + l + 64] = d * (float)s0[is + 4] * (float)q3;
+      out[128 * h + l + 96] = d * (float)s0[is + 6] * (float)q4;
+    }
+  }
+}
+
+/* ops.rs:179-292: per row, per super-block dequantise, then acc += x * w
+ * over its 256 elements in order. */
+static void linear_kquant(const float *x, const uint8_t *w, float *out, size_t in_dim, size_t out_dim, size_t bb,
+                          void (*deq)(const uint8_t *, float *)) {
+  const size_t bpr = in_dim / 256;
+  float buf[256];
+  for (size_t i = 0; i < out_dim; ++i) {
+    float acc = 0.0f;
+    for (size_t b = 0; b < bpr; ++b) {
+      deq(w + (i * bpr + b) * bb, buf);
+      for (int k = 0; k < 256; ++k) acc += x[b * 256 + k] * buf[k];
+    }
+    out[i] = acc;
+  }
+}
+void zo_linear_q4_k(const float *x, const uint8_t *w, float *out, size_t in_dim, size_t out_dim) {
+  linear_kquant(x, w, out, in_dim, out_dim, 144, zo_dequant_q4_k_block);
+}
+void zo_linear_q6_k(const float *x, const uint8_t *w, float *out, size_t in_dim, size_t out_dim) {
+  linear_kquant(x, w, out, in_dim, out_dim, 210, zo_dequant_q6_k_block);
+}
+
 int zo_linear_dispatch(const float *x, const uint8_t *w, float *out, size_t in_dim,
                        size_t out_dim, int quant) {
   if (quant == ZO_Q4_0) { zo_linear_q4_0(x, w, out, in_dim, out_dim); return ZO_OK; }
   if (quant == ZO_Q8_0) { zo_linear_q8_0(x, w, out, in_dim, out_dim); return ZO_OK; }
+  if (quant == ZO_Q4_K) { zo_linear_q4_k(x, w, out, in_dim, out_dim); return ZO_OK; }
+  if (quant == ZO_Q6_K) { zo_linear_q6_k(x, w, out, in_dim, out_dim); return ZO_OK; }
   return ZO_ERR_UNSUPPORTED_QUANT;
 }
 

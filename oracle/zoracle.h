@@ -37,7 +37,7 @@ extern "C" {
 #endif
 
 /* ggml type ids (zero-gguf-parser lib.rs GgmlType) and the .smodel v2 ids. */
-enum { ZO_F32 = 0, ZO_F16 = 1, ZO_Q4_0 = 2, ZO_Q8_0 = 8, ZO_Q4_0X4 = 100, ZO_Q8_0X4 = 101 };
+enum { ZO_F32 = 0, ZO_F16 = 1, ZO_Q4_0 = 2, ZO_Q8_0 = 8, ZO_Q4_K = 12, ZO_Q6_K = 14, ZO_Q4_0X4 = 100, ZO_Q8_0X4 = 101 };
 
 /* Error codes (mirror of the Rust enums the path returns). */
 enum {
@@ -61,6 +61,14 @@ void     zo_quantize_q4_0_block(const float *v32, uint8_t *out18);
 void     zo_quantize_q8_0_block(const float *v32, uint8_t *out34);
 /* Q8_0 activation quantiser (n % 32 == 0): one zo_quantize_q8_0_block per block. */
 void     zo_quantize_row_q8_0(const float *x, uint8_t *out, size_t n);
+/* dequant.rs:63-138: Q4_K super-block (144 bytes -> 256 floats). */
+void     zo_dequant_q4_k_block(const uint8_t *blk, float *out);
+/* dequant.rs:286-356: Q6_K super-block (210 bytes -> 256 floats), the
+ * canonical half-half layout ("pattern C"). */
+void     zo_dequant_q6_k_block(const uint8_t *blk, float *out);
+/* ops.rs:179-292: linear_q4k / linear_q6k, plain rows of super-blocks. */
+void     zo_linear_q4_k(const float *x, const uint8_t *w, float *out, size_t in_dim, size_t out_dim);
+void     zo_linear_q6_k(const float *x, const uint8_t *w, float *out, size_t in_dim, size_t out_dim);
 /* rng.rs:23-46: xorshift64 (13, 7, 17); next_u32 = high half of next_u64. */
 uint32_t zo_rng_next_u32(uint64_t *state);
 /* sampler.rs:123-163: the sampler's own exp approximation. */

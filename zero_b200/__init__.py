@@ -20,6 +20,7 @@ from .synth import DS2_V2_LITE, QWEN3_1_7B, Ds2Config, Qwen3Config
 
 ABI_VERSION = 1
 F32, F16, Q4_0, Q8_0, Q4_0X4, Q8_0X4 = 0, 1, 2, 8, 100, 101
+Q4_K, Q6_K = 12, 14     # GGUF K-quants (plain rows of 256-element super-blocks)
 IPC_HANDLE_BYTES = 64   # ZGPU_IPC_HANDLE_BYTES
 FLAG_NO_GRAPH, FLAG_NO_PDL, FLAG_NO_PERSISTENT = 0x1, 0x2, 0x4
 ROUTE_SOFTMAX, ROUTE_SIGMOID_NORMALIZE = 0, 1
@@ -512,4 +513,4 @@ class Ds2Model:
 
 __all__ = ["Context", "KvCache", "Qwen3Model", "Qwen3Config", "QWEN3_1_7B", "ZgpuError", "synth",
            "MlaKvCache", "Ds2Model", "Ds2Config", "DS2_V2_LITE", "ROUTE_SOFTMAX", "ROUTE_SIGMOID_NORMALIZE",
-           "F32", "Q4_0", "Q8_0", "Q4_0X4", "Q8_0X4"]
+           "F32", "Q4_0", "Q8_0", "Q4_0X4", "Q8_0X4", "Q4_K", "Q6_K"]

@@ -164,6 +164,16 @@ zgpu_status zgpu_register_weights(zgpu_ctx *ctx, const void *host_ptr, size_t le
     t.bytes = len;
     ZCHECK(cudaMalloc(&t.d, len), "cudaMalloc(weights)");
     ZCHECK(cudaMemcpy(t.d, host_ptr, len, cudaMemcpyHostToDevice), "upload");
+  } else if (dtype == ZGPU_Q4_K || dtype == ZGPU_Q6_K) {
+    // K-quants stay in their plain row layout
+    if (cols == 0 || cols % 256 != 0 || rows == 0)
+      return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "K-quant cols must be a positive multiple of 256");
+    if (len != rows * (cols / 256) * (dtype == ZGPU_Q4_K ? 144 : 210))
+      return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "byte length does not match rows x cols");
+    t.quant = dtype;
+    t.bytes = len;
+    ZCHECK(cudaMalloc(&t.d, len), "cudaMalloc(weights)");
+    ZCHECK(cudaMemcpy(t.d, host_ptr, len, cudaMemcpyHostToDevice), "upload");
   } else {
     const bool x4 = (dtype == ZGPU_Q4_0X4 || dtype == ZGPU_Q8_0X4);
     const uint32_t quant = (dtype == ZGPU_Q4_0 || dtype == ZGPU_Q4_0X4)   ? ZGPU_Q4_0
@@ -292,13 +302,20 @@ static zgpu_status check_status_word(zgpu_ctx *ctx) {
 static zgpu_status linear_device(zgpu_ctx *ctx, const float *d_x, const void *w_key, float *d_out,
                                  uint64_t in_dim, uint64_t out_dim, uint32_t quant,
                                  cudaStream_t stream) {
-  if (quant != ZGPU_Q4_0 && quant != ZGPU_Q8_0)
+  if (quant != ZGPU_Q4_0 && quant != ZGPU_Q8_0 && quant != ZGPU_Q4_K && quant != ZGPU_Q6_K)
     return zgpu_fail(ctx, ZGPU_ERR_UNSUPPORTED_QUANT,
                      "linear_dispatch: unsupported quant type " + std::to_string(quant));
   const DeviceTensor *t = zgpu_lookup(ctx, w_key);
   if (!t) return zgpu_fail(ctx, ZGPU_ERR_UNREGISTERED_WEIGHT, "linear_dispatch: unregistered weight");
   if (t->quant != quant || t->cols != in_dim || t->rows != out_dim)
     return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "linear_dispatch: shape/quant mismatch with registration");
+  if (quant == ZGPU_Q4_K || quant == ZGPU_Q6_K) {
+    ZCHECK(zgpu::launch_gemv_kquant(t->d, quant, static_cast<uint32_t>(out_dim), static_cast<uint32_t>(in_dim), d_x,
+                                    d_out, stream),
+           "K-quant GEMV");
+    ++ctx->launches;
+    return ZGPU_OK;
+  }
   zgpu::GemvDesc g;
   g.w = t->d;
   g.wbytes = t->bytes;

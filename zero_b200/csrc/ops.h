@@ -149,6 +149,10 @@ cudaError_t launch_swiglu_rows(const float *y, float *act, uint32_t T, uint32_t 
 cudaError_t launch_swiglu_quant_tiles(const float *y, int8_t *xt, float *xs, uint32_t T, uint32_t ffn,
                                       uint32_t *status, cudaStream_t s);
 
+// y = W x over K-quant rows (kquant.cu): quant ZGPU_Q4_K or ZGPU_Q6_K, in_dim % 256 == 0.
+cudaError_t launch_gemv_kquant(const uint8_t *w, uint32_t quant, uint32_t rows, uint32_t in_dim, const float *x,
+                               float *y, cudaStream_t s);
+
 // lm_head_sample (sampler.rs:41-163) over logits[0, min(len, vocab_real)):
 // one warp; *rng is the xorshift64 state, advanced by one draw; *out the token.
 cudaError_t launch_sample_topk(const float *logits, uint32_t len, uint32_t vocab_real, float temperature,
