@@ -157,8 +157,9 @@ zgpu_status zgpu_linear_q8act_device(zgpu_ctx *ctx, const void *d_xq_blocks, con
 
 /* Batched form on the tensor cores (tcgen05 int8 MMA): T rows of f32
  * activations x[T][in_dim] are quantised per 32-block with the Q8_0 rule
- * above, then out[t][r] = sum_b d_w*d_x*sum_j (n-8)*q, accumulated in block
- * order (bit-identical to the single-row product).  No counterpart in the
+ * above, then out[t][r] = sum_b (sum_j w_j*q_j * d_w) * d_x, accumulated in
+ * block order, with w_j = n-8 for Q4_0 weights and the int8 value for Q8_0
+ * weights (bit-identical to the single-row product).  No counterpart in the
  * reference, which decodes one token at a time: this is the prefill /
  * multi-token path.  out_dim must be a multiple of 128.  Host buffers. */
 zgpu_status zgpu_linear_q8act_batch(zgpu_ctx *ctx, const float *x, const void *w_key, float *out,

@@ -54,6 +54,7 @@ def _load() -> C.CDLL:
         "zo_exp_approx": (C.c_float, [C.c_float]),
         "zo_lm_head_sample": (C.c_uint32, [_f32p, C.c_uint32, C.POINTER(C.c_uint64), C.c_float, C.c_uint32]),
         "zo_linear_q4_0_q8act": (None, [_u8p, _u8p, _f32p, sz, sz]),
+        "zo_linear_q8_0_q8act": (None, [_u8p, _u8p, _f32p, sz, sz]),
         "zo_interleave_x4": (C.c_int, [_u8p, _u8p, sz, sz, C.c_int]),
         "zo_rmsnorm": (None, [_f32p, _f32p, _f32p, sz, C.c_float]),
         "zo_rope_ctx": (None, [C.c_float, sz, _f32p]),
@@ -188,6 +189,13 @@ def linear_kquant(x: np.ndarray, w: np.ndarray, in_dim: int, out_dim: int, quant
 
 def exp_approx(x: float) -> float:
     return float(LIB.zo_exp_approx(C.c_float(x)))
+
+
+def linear_q8_0_q8act(xq: np.ndarray, w: np.ndarray, in_dim: int, out_dim: int) -> np.ndarray:
+    out = np.zeros(out_dim, np.float32)
+    LIB.zo_linear_q8_0_q8act(_b(np.ascontiguousarray(xq, np.uint8)), _b(np.ascontiguousarray(w, np.uint8)),
+                             _f(out), in_dim, out_dim)
+    return out
 
 
 def linear_q4_0_q8act(xq: np.ndarray, w: np.ndarray, in_dim: int, out_dim: int) -> np.ndarray:
@@ -393,9 +401,11 @@ class OracleRun:
     def __del__(self):
         self.close()
 
-    def set_q8act(self, on: bool = True):
-        """Q4_0 matmuls on Q8_0-quantised inputs (the prefill path's arithmetic)."""
-        LIB.zo_run_set_q8act(self._r, 1 if on else 0)
+    def set_q8act(self, on=True):
+        """Q4_0 matmuls on Q8_0-quantised inputs (the prefill path's
+        arithmetic); on=2 quantises the Q8_0 LM head's input too (the batched
+        decode path)."""
+        LIB.zo_run_set_q8act(self._r, 2 if on == 2 else (1 if on else 0))
 
     def forward(self, token: int, pos: int) -> np.ndarray:
         h = np.zeros(self.cfg.hidden, np.float32)

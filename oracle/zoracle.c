@@ -193,6 +193,25 @@ void zo_linear_q4_0_q8act(const uint8_t *xq, const uint8_t *w, float *out, size_
   }
 }
 
+/* Q8_0 weights on Q8_0-quantised inputs, the batched path's LM head: per
+ * block the exact integer dot, then (sumi * d_w) * d_x added in block order
+ * (the arithmetic of zo_linear_q4_0_q8act with int8 weights). */
+void zo_linear_q8_0_q8act(const uint8_t *xq, const uint8_t *w, float *out, size_t in_dim,
+                          size_t out_dim) {
+  size_t bpr = in_dim / 32;
+  for (size_t i = 0; i < out_dim; ++i) {
+    float acc = 0.0f;
+    for (size_t b = 0; b < bpr; ++b) {
+      const uint8_t *wb = w + (i * bpr + b) * 34;
+      const uint8_t *xb = xq + b * 34;
+      int sumi = 0;
+      for (int j = 0; j < 32; ++j) sumi += (int8_t)wb[2 + j] * (int8_t)xb[2 + j];
+      acc += ((float)sumi * zo_fp16_to_f32(rd16(wb))) * zo_fp16_to_f32(rd16(xb));
+    }
+    out[i] = acc;
+  }
+}
+
 /* ======================================================================
  * Scalar crate ops (crates/zero-llm-inference/src)
  * ====================================================================== */
@@ -848,9 +867,10 @@ void zo_run_destroy(zo_run *r) {
 
 const float *zo_run_kv(const zo_run *r) { return r->kv; }
 
-/* Q4_0 matmuls of the run take Q8_0-quantised inputs (zo_quantize_row_q8_0,
- * then zo_linear_q4_0_q8act): the arithmetic of the prefill path, whose
- * batched matmuls quantise their activations. */
+/* mode 1: the Q4_0 matmuls of the run take Q8_0-quantised inputs
+ * (zo_quantize_row_q8_0, then zo_linear_q4_0_q8act), the arithmetic of the
+ * prefill path, whose batched matmuls quantise their activations; mode 2:
+ * the Q8_0 LM head too (zo_linear_q8_0_q8act), the batched decode path. */
 void zo_run_set_q8act(zo_run *r, int on) { r->q8act = on; }
 
 static void lin(zo_run *r, const float *x, const uint8_t *plain, const uint8_t *x4, float *out,
@@ -858,6 +878,11 @@ static void lin(zo_run *r, const float *x, const uint8_t *plain, const uint8_t *
   if (r->q8act && quant == ZO_Q4_0) {
     zo_quantize_row_q8_0(x, r->xq, in);
     zo_linear_q4_0_q8act(r->xq, plain, out, in, outd);
+    return;
+  }
+  if (r->q8act == 2 && quant == ZO_Q8_0) {
+    zo_quantize_row_q8_0(x, r->xq, in);
+    zo_linear_q8_0_q8act(r->xq, plain, out, in, outd);
     return;
   }
   if (r->order == 0) {

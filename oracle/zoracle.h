@@ -88,6 +88,8 @@ int      zo_interleave_x4(const uint8_t *plain, uint8_t *x4, size_t rows, size_t
  * (the GGUF ecosystem's definition of this product, zero-gguf-parser carries
  * the formats): per block sumi = sum_j (n_j - 8) * q_j exactly, then
  * acc += (sumi * d_w) * d_x in block order. */
+void     zo_linear_q8_0_q8act(const uint8_t *xq, const uint8_t *w, float *out, size_t in_dim,
+                              size_t out_dim);
 void     zo_linear_q4_0_q8act(const uint8_t *xq, const uint8_t *w, float *out, size_t in_dim,
                               size_t out_dim);
 

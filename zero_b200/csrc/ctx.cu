@@ -479,8 +479,8 @@ static zgpu_status q8act_batch(zgpu_ctx *ctx, const float *d_x, const void *w_ke
                                uint64_t in_dim, uint64_t out_dim, cudaStream_t s) {
   const DeviceTensor *t = zgpu_lookup(ctx, w_key);
   if (!t) return zgpu_fail(ctx, ZGPU_ERR_UNREGISTERED_WEIGHT, "linear_q8act_batch: unregistered weight");
-  if (t->quant != ZGPU_Q4_0)
-    return zgpu_fail(ctx, ZGPU_ERR_UNSUPPORTED_QUANT, "linear_q8act_batch: weights must be Q4_0");
+  if (t->quant != ZGPU_Q4_0 && t->quant != ZGPU_Q8_0)
+    return zgpu_fail(ctx, ZGPU_ERR_UNSUPPORTED_QUANT, "linear_q8act_batch: weights must be Q4_0 or Q8_0");
   if (t->cols != in_dim || t->rows != out_dim)
     return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "linear_q8act_batch: shape mismatch with registration");
   if (out_dim % 128 || T > 0xFFFFFFu || T * in_dim > (1ull << 34))
@@ -491,7 +491,7 @@ static zgpu_status q8act_batch(zgpu_ctx *ctx, const float *d_x, const void *w_ke
   if (!wt->w8) {
     ZCHECK(cudaMalloc(&wt->w8, zgpu::mma_tile_bytes(out_dim, bpr)), "cudaMalloc(weight tiles)");
     ZCHECK(cudaMalloc(&wt->ws8, zgpu::mma_scale_bytes(out_dim, bpr)), "cudaMalloc(weight tile scales)");
-    ZCHECK(zgpu::launch_build_w8_tiles(wt->d, wt->gstride, static_cast<uint32_t>(out_dim), bpr, wt->w8, wt->ws8, s),
+    ZCHECK(zgpu::launch_build_w8_tiles(wt->d, wt->gstride, static_cast<uint32_t>(out_dim), bpr, t->quant, wt->w8, wt->ws8, s),
            "weight tiles");
     ++ctx->launches;
   }

@@ -10,6 +10,8 @@
 //         scale / min, the high nibbles (32 further) with 2 g + 1's;
 //   Q6_K  element l + 32 k of both 128-element halves (k < 4), from
 //         ql[64 h + l], ql[64 h + l + 32] and qh[32 h + l].
+// The super-block loop is unrolled four deep so that a warp has four
+// blocks' loads in flight (a 2048-wide row is only eight super-blocks).
 // Every weight is rebuilt exactly as the reference dequantises it (each
 // product rounded on its own); the dot product accumulates with fmaf per
 // lane and a warp tree, another order than the reference's sequential sum
@@ -40,14 +42,16 @@ __device__ __forceinline__ void q4k_scale_min(const uint8_t *sc, int j, float *d
 }
 
 template <uint32_t QT>
-__global__ void __launch_bounds__(32 * kRowsPerCta) gemv_kquant_kernel(const uint8_t *w, uint32_t rows, uint32_t spr,
-                                                                     const float *x, float *y) {
+__global__ void __launch_bounds__(32 * kRowsPerCta) gemv_kquant_kernel(const uint8_t *__restrict__ w, uint32_t rows,
+                                                                     uint32_t spr, const float *__restrict__ x,
+                                                                     float *__restrict__ y) {
   const uint32_t row = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   float acc = 0.f;
   if (QT == ZGPU_Q4_K) {
     const uint8_t *wr = w + static_cast<size_t>(row) * spr * 144;
     const uint32_t g = lane >> 3, p = (lane & 7) * 4;
+#pragma unroll 4
     for (uint32_t b = 0; b < spr; ++b) {
       const uint8_t *blk = wr + static_cast<size_t>(b) * 144;
       const float d = h2f(static_cast<uint16_t>(blk[0] | (blk[1] << 8)));
@@ -70,6 +74,7 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) gemv_kquant_kernel(const uin
     }
   } else {
     const uint8_t *wr = w + static_cast<size_t>(row) * spr * 210;
+#pragma unroll 4
     for (uint32_t b = 0; b < spr; ++b) {
       const uint8_t *blk = wr + static_cast<size_t>(b) * 210;
       const float d = h2f(static_cast<uint16_t>(blk[208] | (blk[209] << 8)));

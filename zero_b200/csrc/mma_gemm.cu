@@ -280,21 +280,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q4q8_mma_kernel(const MmaGemm
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
 }
 
-// Q4_0 group streams -> weight tiles: CTA (row tile, block), thread = row.
+// Q4_0 or Q8_0 group streams -> weight tiles: CTA (row tile, block), thread
+// = row.  Q4_0 nibbles become q - 8 (elements 0..15 from the low nibbles,
+// 16..31 from the high); Q8_0's two 16-byte planes of a row are its halves.
+template <uint32_t QT>
 __global__ void build_w8_tiles_kernel(const uint8_t *w, uint64_t gstride, uint32_t bpr, int8_t *wt, float *ws) {
   const uint32_t row = blockIdx.x * kTileM + threadIdx.x, b = blockIdx.y;
   const uint8_t *grp = w + static_cast<uint64_t>(row >> 2) * gstride;
-  const uint4 qv = *reinterpret_cast<const uint4 *>(grp + plane_entry(ZGPU_Q4_0, bpr, b, row & 3));
-  const uint8_t *sc = grp + scale_entry(ZGPU_Q4_0, bpr, b) + 2 * (row & 3);
+  const uint8_t *sc = grp + scale_entry(QT, bpr, b) + 2 * (row & 3);
   uint4 lo, hi;
-  lo.x = nib_to_s8(qv.x & 0x0F0F0F0Fu);
-  lo.y = nib_to_s8(qv.y & 0x0F0F0F0Fu);
-  lo.z = nib_to_s8(qv.z & 0x0F0F0F0Fu);
-  lo.w = nib_to_s8(qv.w & 0x0F0F0F0Fu);
-  hi.x = nib_to_s8((qv.x >> 4) & 0x0F0F0F0Fu);
-  hi.y = nib_to_s8((qv.y >> 4) & 0x0F0F0F0Fu);
-  hi.z = nib_to_s8((qv.z >> 4) & 0x0F0F0F0Fu);
-  hi.w = nib_to_s8((qv.w >> 4) & 0x0F0F0F0Fu);
+  if (QT == ZGPU_Q4_0) {
+    const uint4 qv = *reinterpret_cast<const uint4 *>(grp + plane_entry(QT, bpr, b, row & 3));
+    lo.x = nib_to_s8(qv.x & 0x0F0F0F0Fu);
+    lo.y = nib_to_s8(qv.y & 0x0F0F0F0Fu);
+    lo.z = nib_to_s8(qv.z & 0x0F0F0F0Fu);
+    lo.w = nib_to_s8(qv.w & 0x0F0F0F0Fu);
+    hi.x = nib_to_s8((qv.x >> 4) & 0x0F0F0F0Fu);
+    hi.y = nib_to_s8((qv.y >> 4) & 0x0F0F0F0Fu);
+    hi.z = nib_to_s8((qv.z >> 4) & 0x0F0F0F0Fu);
+    hi.w = nib_to_s8((qv.w >> 4) & 0x0F0F0F0Fu);
+  } else {
+    lo = *reinterpret_cast<const uint4 *>(grp + plane_entry(QT, bpr, b, 2 * (row & 3)));
+    hi = *reinterpret_cast<const uint4 *>(grp + plane_entry(QT, bpr, b, 2 * (row & 3) + 1));
+  }
   *reinterpret_cast<uint4 *>(wt + mma_tile_off(row, b, bpr, 0)) = lo;
   *reinterpret_cast<uint4 *>(wt + mma_tile_off(row, b, bpr, 1)) = hi;
   ws[mma_scale_off(row, b, bpr)] = h2f(static_cast<uint16_t>(sc[0] | (sc[1] << 8)));
@@ -343,10 +351,15 @@ cudaError_t launch_q4q8_mma(const MmaGemmParams &p, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-cudaError_t launch_build_w8_tiles(const uint8_t *w, uint64_t gstride, uint32_t rows, uint32_t bpr, int8_t *wt,
-                                  float *ws, cudaStream_t s) {
+cudaError_t launch_build_w8_tiles(const uint8_t *w, uint64_t gstride, uint32_t rows, uint32_t bpr, uint32_t quant,
+                                  int8_t *wt, float *ws, cudaStream_t s) {
   if (rows == 0 || rows % kTileM || bpr == 0 || gstride % 16) return cudaErrorInvalidValue;
-  build_w8_tiles_kernel<<<dim3(rows / kTileM, bpr), kTileM, 0, s>>>(w, gstride, bpr, wt, ws);
+  if (quant == ZGPU_Q4_0)
+    build_w8_tiles_kernel<ZGPU_Q4_0><<<dim3(rows / kTileM, bpr), kTileM, 0, s>>>(w, gstride, bpr, wt, ws);
+  else if (quant == ZGPU_Q8_0)
+    build_w8_tiles_kernel<ZGPU_Q8_0><<<dim3(rows / kTileM, bpr), kTileM, 0, s>>>(w, gstride, bpr, wt, ws);
+  else
+    return cudaErrorInvalidValue;
   return cudaGetLastError();
 }
 

@@ -1210,7 +1210,7 @@ zgpu_status prefill_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, cons
         if (e == cudaSuccess) e = cudaMalloc(&ws, mma_scale_bytes(mt.rows, mt.in_dim / 32));
         m->pf_w8.push_back(wt);
         m->pf_ws8.push_back(ws);
-        if (e == cudaSuccess) e = launch_build_w8_tiles(mt.w, mt.gstride, mt.rows, mt.in_dim / 32, wt, ws, ctx->stream);
+        if (e == cudaSuccess) e = launch_build_w8_tiles(mt.w, mt.gstride, mt.rows, mt.in_dim / 32, ZGPU_Q4_0, wt, ws, ctx->stream);
         if (e != cudaSuccess) {
           for (int8_t *p : m->pf_w8) cudaFree(p);
           for (float *p : m->pf_ws8) cudaFree(p);

@@ -123,8 +123,8 @@ struct MmaGemmParams {
 cudaError_t mma_setup();
 cudaError_t launch_q4q8_mma(const MmaGemmParams &p, cudaStream_t s);
 // Q4_0 group streams (layout.h) -> weight tiles + scales; rows % 128 == 0.
-cudaError_t launch_build_w8_tiles(const uint8_t *w, uint64_t gstride, uint32_t rows, uint32_t bpr, int8_t *wt,
-                                  float *ws, cudaStream_t s);
+cudaError_t launch_build_w8_tiles(const uint8_t *w, uint64_t gstride, uint32_t rows, uint32_t bpr, uint32_t quant,
+                                  int8_t *wt, float *ws, cudaStream_t s);
 // x [T][K] f32 -> Q8_0 activation tiles + scales (the packer's rule); the
 // padding rows of the last tile are zeroed.
 cudaError_t launch_quantize_q8_0_tiles(const float *x, int8_t *xt, float *xs, uint32_t T, uint32_t K,
@@ -159,6 +159,22 @@ cudaError_t launch_sample_topk(const float *logits, uint32_t len, uint32_t vocab
                                unsigned long long *rng, uint32_t *out, cudaStream_t s);
 
 cudaError_t launch_attention(const AttnParams &ap, const LaunchCfg &lc);
+// One sequence of a batched decode step: its cache (K block of layer 0;
+// layer l starts 2 l block floats further), block size, capacity and the
+// position of its token.
+struct AttnBatchSeq {
+  float *kv;
+  uint64_t block;
+  uint32_t max_tokens, pos;
+};
+// The decode attention of one layer for n_seq sequences at once (grid z =
+// sequence): sequence z reads qkv + z * qkv_stride, writes out + z *
+// out_stride, and uses its own partials and arrival counters (part + z *
+// n_q * max_splits * (hd + 2), counters + z * n_kv); ap.kv_layer / kv_block /
+// max_tokens / pos come from seqs[z] (device).  ap.max_splits must cover
+// every sequence's cache.
+cudaError_t launch_attention_batch(const AttnParams &ap, const AttnBatchSeq *seqs, uint32_t layer, uint32_t n_seq,
+                                   uint32_t qkv_stride, uint32_t out_stride, const LaunchCfg &lc);
 // Number of attention splits (CTAs per kv-head) a cache of max_tokens needs.
 uint32_t attention_max_splits(uint32_t max_tokens);
 cudaError_t attention_setup();
