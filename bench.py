@@ -66,7 +66,8 @@ def parse():
                     help="qwen3: BASELINE config 0 (the headline); ds2: the config-3 DeepSeek2 "
                          "MLA+MoE model, one sequence, as a secondary line")
     ap.add_argument("--context", type=int, default=2048, help="ds2: tokens in the cache before decode")
-    ap.add_argument("--batch", type=int, default=1, help="prefill: prompts per step (BASELINE config 4: 1 or 8)")
+    ap.add_argument("--batch", type=int, default=1, help="prefill: prompts per step (BASELINE config 4: 1 or 8); "
+                    "qwen3-8b: sequences decoded together (BASELINE config 2: 1 or 16)")
     return ap.parse_args()
 
 
@@ -494,6 +495,135 @@ def run_qwen3_tp(args, rank, world, local):
         dist.destroy_process_group()
 
 
+BATCH_METRIC = "decode tok/s (all sequences), Qwen3-8B-shape Q4_0, batch B, context 4096"
+
+
+def run_qwen3_batch(args, rank, world, local):
+    """BASELINE config 2 at batch B (16): B sequences, each cache filled to
+    4096 seeded tokens (zgpu_prefill_batch, four sequences at a time), then K
+    greedy steps of all B sequences at once (zgpu_decode_batch: tcgen05 int8
+    projections and LM head over Q8_0 activation rows, the decode attention
+    with a sequence grid dimension).  One GPU; value = B x K tokens over the
+    device time of the K steps."""
+    from zero_b200 import synth
+
+    cfg = synth.QWEN3_8B
+    B = args.batch
+    n_cpu_prompt, n_cpu_gen = 4, 4
+    if world > 1:
+        raise SystemExit("batched decode runs on one GPU")
+    if args.impl == "reference":
+        weights = synth.qwen3_weights(cfg, seed=SEED, x4=False)
+        prompt = synth.prompt_ids(cfg, n_cpu_prompt, seed=SEED)
+        cores = physical_cores()
+        tok_s, dt = cpu_decode_sample(cfg, weights, prompt, n_cpu_gen, cores)
+        print(json.dumps({
+            "impl": "reference", "metric": BATCH_METRIC, "value": round(tok_s, 3), "unit": "tok/s",
+            "n_gpus": args.gpus, "steps": n_cpu_gen, "warmup": 0, "ms_per_step": round(1000 * dt / n_cpu_gen, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random-init .smodel v2 weights, BASELINE config 2 shapes)",
+            "config": {"workload": f"qwen3-8b-shape q4_0 decode b={B} (BASELINE config 2)",
+                       "parallelism": "cpu threads"},
+            "cpu_baseline": {"value": round(tok_s, 3), "unit": "tok/s", "cores": cores, "kind": "port",
+                             "sample": f"one sequence: {n_cpu_gen} decode steps after a {n_cpu_prompt}-token "
+                                       f"prompt (the reference decodes the sequences of a batch one after "
+                                       f"another, so its batch rate is its single-sequence rate)"},
+            "e2e": {"value": round(tok_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+            flush=True)
+        return
+    import torch
+
+    import zero_b200 as zb
+
+    torch.cuda.set_device(local)
+    weights = synth.qwen3_weights(cfg, seed=SEED)
+    ctx = zb.Context(device=local)
+    model = zb.Qwen3Model(ctx, cfg, weights)
+    del weights
+    max_tokens = TP_CONTEXT + args.warmup + args.steps + 2
+    kvs = [model.new_kv(max_tokens) for _ in range(B)]
+    prompts = np.stack([synth.prompt_ids(cfg, TP_CONTEXT, seed=SEED + i) for i in range(B)])
+    toks = np.empty(B, np.uint32)
+    t0 = time.perf_counter()
+    for g in range(0, B, 4):
+        toks[g:g + 4] = model.prefill_batch(kvs[g:g + 4], prompts[g:g + 4], want_logits=False)[0]
+    fill_s = time.perf_counter() - t0
+    pos = TP_CONTEXT
+    for _ in range(args.warmup):
+        toks, _ = model.decode_batch(kvs, toks, np.full(B, pos), want_logits=False)
+        pos += 1
+    torch.cuda.synchronize()
+    dev_ms, gemm_ms, attn_ms, wall = [], [], [], []
+    kv_bytes = 0
+    kv_row = 2 * cfg.n_kv_heads * cfg.head_dim * 4          # K and V of one token, one layer
+    first = []
+    with ClockSampler(physical_gpu_index(local)) as clocks:
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            toks, _ = model.decode_batch(kvs, toks, np.full(B, pos), want_logits=False)
+            wall.append(time.perf_counter() - t0)
+            p = model.perf()
+            dev_ms.append(p["decode_ms"])
+            gemm_ms.append(p["batch_gemm_ms"])
+            attn_ms.append(p["batch_attn_ms"])
+            kv_bytes += B * (pos + 1) * kv_row * cfg.n_layers
+            pos += 1
+            if len(first) < 4:
+                first.append(int(toks[0]))
+    launches = int(model.perf()["decode_launches"])
+    K = args.steps
+    tok_s = B * K / (sum(dev_ms) / 1000.0)
+    peaks = measured_peaks()
+    attn_launch_bytes = kv_bytes / (K * cfg.n_layers)
+    attn_us = 1000.0 * sum(attn_ms) / (K * cfg.n_layers)
+    attn_gbs = attn_launch_bytes / (attn_us / 1e6) / 1e9
+    tile_bytes = (cfg.n_layers * ((cfg.q_dim + 2 * cfg.kv_dim) * cfg.hidden + cfg.hidden * cfg.q_dim
+                                  + 2 * cfg.ffn * cfg.hidden + cfg.hidden * cfg.ffn)
+                  + cfg.vocab_padded * cfg.hidden) * 9 // 8        # int8 tiles + one f32 scale per 32
+    gemm_gbs = tile_bytes / (statistics.mean(gemm_ms) / 1000.0) / 1e9
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        for kv in kvs:
+            kv.close()
+        model.close()
+        w_plain = synth.qwen3_weights(cfg, seed=SEED, x4=False)
+        c_tok_s, c_dt = cpu_decode_sample(cfg, w_plain, prompts[0][:n_cpu_prompt], n_cpu_gen, physical_cores())
+        cpu = {"value": round(c_tok_s, 3), "unit": "tok/s", "cores": physical_cores(), "kind": "port",
+               "sample": f"one sequence, {n_cpu_gen} decode steps after a {n_cpu_prompt}-token prompt (context <= "
+                         f"{n_cpu_prompt + n_cpu_gen}, not {TP_CONTEXT}), AVX-512-order restatement, {c_dt:.1f} s; "
+                         f"the reference decodes a batch's sequences one after another"}
+    print(json.dumps({
+        "metric": BATCH_METRIC, "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": 1, "steps": K,
+        "warmup": args.warmup, "ms_per_step": round(statistics.mean(dev_ms), 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> int32 (Q8_0 x Q4_0 / Q8_0), f32 elsewhere",
+        "data": "synthetic (seeded random-init .smodel v2 weights, BASELINE config 2 shapes)",
+        "config": {"workload": f"qwen3-8b-shape q4_0 decode b={B} (BASELINE config 2)", "batch": B,
+                   "context": TP_CONTEXT, "decode_steps": K, "layers": cfg.n_layers,
+                   "parallelism": "single GPU", "context_fill_s": round(fill_s, 1),
+                   "gemm_ms_per_step": round(statistics.mean(gemm_ms), 4),
+                   "attention_ms_per_step": round(statistics.mean(attn_ms), 4),
+                   "gemm_tile_gbs": round(gemm_gbs, 1),
+                   "l2": "inputs larger than L2 (9.9 GB of weight tiles and 19 GB of KV rows per step)",
+                   "tokens_first_seq0": first},
+        "roofline": {"bound": "hbm", "kernel": "attn_decode_batch_kernel (one layer, all sequences)",
+                     "achieved": round(attn_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(attn_gbs / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
+                     "traffic": None, "algorithmic_bytes": int(attn_launch_bytes),
+                     "avg_launch_us": round(attn_us, 2)},
+        "e2e": {"value": round(B * K / sum(wall), 1), "unit": "tok/s",
+                "scope": "zgpu_decode_batch per step with host tokens in and out, host wall clock",
+                "h2d_bytes_per_step": 4 * B + 24 * B, "d2h_bytes_per_step": 8 * B},
+        "gpu_launches": launches * K,
+        "clocks": clocks.summary(),
+        "cpu_baseline": cpu,
+    }), flush=True)
+    if cpu is None:
+        for kv in kvs:
+            kv.close()
+        model.close()
+    ctx.close()
+
+
 PREFILL_METRIC = "prefill tok/s, Qwen3-1.7B-shape Q4_0, 2048-token prompt; int8 tensor-core TOPS"
 PREFILL_LEN = 2048
 
@@ -810,7 +940,10 @@ def main():
         run_ds2(args, rank, world, local)
         return
     if args.workload == "qwen3-8b":
-        run_qwen3_tp(args, rank, world, local)
+        if args.batch > 1:
+            run_qwen3_batch(args, rank, world, local)
+        else:
+            run_qwen3_tp(args, rank, world, local)
         return
     if args.workload == "prefill":
         if args.impl != "reference":

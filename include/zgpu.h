@@ -344,6 +344,19 @@ zgpu_status zgpu_prefill(zgpu_model *m, zgpu_kv *kv, const uint32_t *tokens, uin
  * zgpu_prefill of that prompt bit for bit. */
 zgpu_status zgpu_prefill_batch(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, const uint32_t *tokens,
                                uint32_t n, uint32_t *tokens_out, float *logits_out);
+/* One greedy decode step for n_seq (1..256) independent sequences, each
+ * with its own cache at its own position: per sequence the results of
+ * zgpu_forward_single_token(kvs[i], tokens[i], positions[i]) followed by
+ * zgpu_lm_head_argmax (forward_pass.rs:515-631, lm_head.rs:98-166), computed
+ * as one batch.  The projections and the LM head run on the tensor cores over
+ * Q8_0-quantised activation rows, as the prefill does (logits within the
+ * prefill's tolerance of the per-token path, not bit-identical); the KV rows
+ * are appended at positions[i].  tokens_out [n_seq]; logits_out
+ * [n_seq][vocab_padded] or NULL.  An LM-head error of any sequence is
+ * returned (its tokens_out entry still written).  Single-GPU models only;
+ * head_dim 128, vocab_padded a multiple of 128. */
+zgpu_status zgpu_decode_batch(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, const uint32_t *tokens,
+                              const uint32_t *positions, uint32_t *tokens_out, float *logits_out);
 
 /* Per-kernel-class counters, mirroring Avx512PerfCounters
  * (inference_avx512.rs:274-330): calls and device milliseconds of the last
@@ -356,6 +369,8 @@ typedef struct zgpu_perf {
   uint64_t decode_launches;   /* kernel launches of the decode steps alone */
   double prefill_gemm_ms;     /* zgpu_prefill: device time of the projection GEMMs */
   double prefill_attn_ms;     /* zgpu_prefill: device time of the causal attention */
+  double batch_gemm_ms;       /* zgpu_decode_batch: device time of the projection and LM-head GEMMs */
+  double batch_attn_ms;       /* zgpu_decode_batch: device time of the attention launches */
 } zgpu_perf;
 zgpu_status zgpu_perf_snapshot(const zgpu_model *m, zgpu_perf *out);
 

@@ -1,0 +1,183 @@
+"""Batched greedy decode (zgpu_decode_batch): several sequences, each with its
+own cache at its own position, one step at a time.
+
+Per sequence, the step is forward_single_token + the LM head pick
+(forward_pass.rs:515-631, lm_head.rs:98-166).  The batch computes the
+projections and the LM head on the tcgen05 int8 path over Q8_0-quantised
+activation rows, so the reference for it is the oracle's per-token path with
+the same rounding (q8act mode 2: every matmul input, the LM head's included,
+quantised to Q8_0 first).  The prompt goes through zgpu_prefill, whose LM
+head is f32 (q8act mode 1).  Bars, as for the prefill: logits within 1e-2
+relative L2 of that path at every step (RMSNorm and attention reduce in
+another order; a last-bit difference flips the Q8_0 rounding of an element
+now and then), the KV cache within 2e-2, the same next token wherever the
+oracle's top-1/top-2 margin is clear; the oracle is fed the GPU's tokens so
+both stay on one sequence.
+
+A batch is also bit-identical to the same sequences decoded one at a time:
+every matmul row, attention and argmax of a sequence is computed the same
+way whatever else is in the batch.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+import zero_b200 as zb
+from zero_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+
+def top2_gap(v):
+    s = np.sort(v)
+    return float(s[-1] - s[-2])
+
+
+CASES = [
+    # cfg, prompt lengths (one per sequence), decode steps
+    (synth.small_config(n_layers=2, hidden=256, ffn=512, n_q=4, n_kv=2, vocab=512), [5, 17, 33, 9], 6),
+    (synth.small_config(n_layers=3, hidden=512, ffn=1024, n_q=8, n_kv=2, vocab=1024), [300, 12, 64], 5),
+    # config-2 widths (hidden 4096, 32 / 8 heads, FFN 12288) on two layers, a short vocabulary
+    (synth.small_config(n_layers=2, hidden=4096, ffn=12288, n_q=32, n_kv=8, vocab=1024), [40, 7], 4),
+]
+
+
+def run_case(cfg, lens, steps, seed=43):
+    ctx = zb.Context()
+    w = synth.qwen3_weights(cfg, seed=seed, norm_sigma=0.1)
+    m = zb.Qwen3Model(ctx, cfg, w)
+    max_tokens = max(lens) + steps + 8
+    prompts = [synth.prompt_ids(cfg, n, seed=seed + i) for i, n in enumerate(lens)]
+    kvs = [m.new_kv(max_tokens) for _ in lens]
+    toks = np.array([m.prefill(kv, p, want_logits=False)[0] for kv, p in zip(kvs, prompts)], np.uint32)
+    refs = []
+    for p in prompts:
+        r = O.OracleRun(cfg, w, max_tokens, order=O.ORDER_AVX512)
+        r.set_q8act(1)
+        for i, t in enumerate(p):
+            r.forward(int(t), i)
+        rc, rtok, _ = r.lm_head()
+        assert rc == 0
+        r.set_q8act(2)
+        refs.append(r)
+    worst, kv_worst = 0.0, 0.0
+    for s in range(steps):
+        pos = np.array([n + s for n in lens], np.uint32)
+        nxt, logits = m.decode_batch(kvs, toks, pos)
+        assert m.perf()["decode_ms"] > 0
+        for i, r in enumerate(refs):
+            r.forward(int(toks[i]), int(pos[i]))
+            rc, rtok, rlog = r.lm_head()
+            assert rc == 0
+            err = rel_l2(logits[i], rlog)
+            worst = max(worst, err)
+            assert err < 1e-2, (s, i, err)
+            if top2_gap(rlog) > 20 * err * float(np.abs(rlog).max()):
+                assert nxt[i] == rtok, (s, i)
+        toks = nxt
+    for i, (r, kv) in enumerate(zip(refs, kvs)):
+        n = lens[i] + steps
+        ref_kv = r.kv().reshape(cfg.n_layers, 2, max_tokens, cfg.kv_dim)
+        for layer in range(cfg.n_layers):
+            k, v = kv.read(layer, n)
+            kv_worst = max(kv_worst, rel_l2(k, ref_kv[layer, 0, :n].ravel()), rel_l2(v, ref_kv[layer, 1, :n].ravel()))
+    assert kv_worst < 2e-2, kv_worst
+    print(f"{cfg.name} lens={lens}: worst logits {worst:.2e}, kv {kv_worst:.2e}")
+    for kv in kvs:
+        kv.close()
+    m.close()
+    ctx.close()
+
+
+@pytest.mark.parametrize("cfg,lens,steps", CASES, ids=[f"{c.name}-b{len(l)}" for c, l, _ in CASES])
+def test_decode_batch_matches_per_token_q8_path(cfg, lens, steps):
+    run_case(cfg, lens, steps)
+
+
+def test_decode_batch_config0_full_size():
+    """BASELINE config 0 weights (28 layers, hidden 2048, vocab 151936), two sequences."""
+    run_case(synth.QWEN3_1_7B, [16, 23], 3, seed=0)
+
+
+def test_batch_equals_sequences_alone():
+    cfg = synth.small_config(n_layers=2, hidden=512, ffn=1024, n_q=8, n_kv=2, vocab=1024)
+    ctx = zb.Context()
+    w = synth.qwen3_weights(cfg, seed=5, norm_sigma=0.1)
+    m = zb.Qwen3Model(ctx, cfg, w)
+    lens = [3, 40, 300, 17, 1]
+    prompts = [synth.prompt_ids(cfg, n, seed=70 + i) for i, n in enumerate(lens)]
+    a = [m.new_kv(320) for _ in lens]
+    b = [m.new_kv(320) for _ in lens]
+    ta = np.array([m.prefill(kv, p, want_logits=False)[0] for kv, p in zip(a, prompts)], np.uint32)
+    tb = np.array([m.prefill(kv, p, want_logits=False)[0] for kv, p in zip(b, prompts)], np.uint32)
+    assert np.array_equal(ta, tb)
+    for s in range(4):
+        pos = np.array([n + s for n in lens], np.uint32)
+        na, la = m.decode_batch(a, ta, pos)
+        for i in range(len(lens)):
+            nb, lb = m.decode_batch([b[i]], tb[i:i + 1], pos[i:i + 1])
+            assert nb[0] == na[i]
+            assert np.array_equal(lb[0].view(np.uint32), la[i].view(np.uint32)), (s, i)
+            tb[i] = nb[0]
+        ta = na
+    for i, n in enumerate(lens):
+        for layer in range(cfg.n_layers):
+            ka, va = a[i].read(layer, n + 4)
+            kb, vb = b[i].read(layer, n + 4)
+            assert np.array_equal(ka, kb) and np.array_equal(va, vb)
+    for kv in a + b:
+        kv.close()
+    m.close()
+    ctx.close()
+
+
+def test_generate_batch_runs_prefill_then_steps():
+    cfg = synth.small_config(n_layers=2, hidden=256, ffn=512, n_q=4, n_kv=2, vocab=512)
+    ctx = zb.Context()
+    w = synth.qwen3_weights(cfg, seed=9, norm_sigma=0.1)
+    m = zb.Qwen3Model(ctx, cfg, w)
+    prompts = np.stack([synth.prompt_ids(cfg, 12, seed=90 + i) for i in range(3)])
+    kvs = [m.new_kv(40) for _ in range(3)]
+    out, _ = m.generate_batch(kvs, prompts, 5)
+    kv2 = [m.new_kv(40) for _ in range(3)]
+    tok, _ = m.prefill_batch(kv2, prompts, want_logits=False)
+    assert np.array_equal(out[:, 0], tok)
+    for s in range(1, 5):
+        tok, _ = m.decode_batch(kv2, tok, np.full(3, 12 + s - 1), want_logits=False)
+        assert np.array_equal(out[:, s], tok)
+    for kv in kvs + kv2:
+        kv.close()
+    m.close()
+    ctx.close()
+
+
+def test_decode_batch_errors():
+    cfg = synth.small_config(n_layers=2, hidden=256, ffn=512, n_q=4, n_kv=2, vocab=512)
+    ctx = zb.Context()
+    w = synth.qwen3_weights(cfg, seed=3)
+    m = zb.Qwen3Model(ctx, cfg, w)
+    a, b = m.new_kv(16), m.new_kv(16)
+    with pytest.raises(zb.ZgpuError) as e:
+        m.decode_batch([a, b], [1, 2], [3, 16])          # position at the capacity
+    assert e.value.status == 10
+    with pytest.raises(zb.ZgpuError) as e:
+        m.decode_batch([a, a], [1, 2], [0, 1])           # one cache per sequence
+    assert e.value.status == 1
+    with pytest.raises(zb.ZgpuError) as e:
+        m.decode_batch([a], [cfg.vocab_padded], [0])     # token beyond the vocabulary
+    assert e.value.status == 1
+    other = zb.KvCache(ctx, 16, cfg.n_layers, 1, cfg.head_dim)
+    with pytest.raises(zb.ZgpuError):
+        m.decode_batch([other], [1], [0])                # kv geometry
+    toks, _ = m.decode_batch([a, b], [1, 2], [0, 0])     # a valid step still runs after the errors
+    assert toks.shape == (2,)
+    for kv in (a, b, other):
+        kv.close()
+    m.close()
+    ctx.close()

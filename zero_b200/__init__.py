@@ -376,12 +376,48 @@ class Qwen3Model:
                                                _ptr(logits) if want_logits else None))
         return toks, logits
 
+    def decode_batch(self, kvs, tokens, positions, want_logits: bool = True):
+        """zgpu_decode_batch: one greedy step for len(kvs) sequences, sequence
+        i feeding tokens[i] at positions[i] of its own cache; returns (next
+        tokens [n_seq], logits [n_seq, vocab] or None)."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        pos = np.ascontiguousarray(positions, np.uint32)
+        n_seq = len(kvs)
+        if t.size != n_seq or pos.size != n_seq:
+            raise ValueError("one token and one position per sequence")
+        handles = (C.c_void_p * n_seq)(*[kv.h.value if isinstance(kv.h, C.c_void_p) else kv.h for kv in kvs])
+        toks = np.empty(n_seq, np.uint32)
+        logits = np.empty((n_seq, self.cfg.vocab_padded), np.float32) if want_logits else None
+        self.ctx._check(LIB.zgpu_decode_batch(self.h, handles, n_seq, _ptr(t), _ptr(pos), _ptr(toks),
+                                              _ptr(logits) if want_logits else None))
+        return toks, logits
+
+    def generate_batch(self, kvs, prompts, n_gen: int, want_logits: bool = False):
+        """Greedy generation for several sequences: the prompts [n_seq, n]
+        through zgpu_prefill_batch, then n_gen - 1 zgpu_decode_batch steps.
+        Returns (tokens [n_seq, n_gen], logits [n_gen, n_seq, vocab] or None)."""
+        p = np.ascontiguousarray(prompts, np.uint32)
+        n_seq, n = p.shape
+        out = np.empty((n_seq, n_gen), np.uint32)
+        lg = [] if want_logits else None
+        tok, logits = self.prefill_batch(kvs, p, want_logits)
+        out[:, 0] = tok
+        if want_logits:
+            lg.append(logits)
+        for s in range(1, n_gen):
+            tok, logits = self.decode_batch(kvs, tok, np.full(n_seq, n + s - 1), want_logits)
+            out[:, s] = tok
+            if want_logits:
+                lg.append(logits)
+        return out, (np.stack(lg) if want_logits else None)
+
     def perf(self) -> dict:
         p = ZgpuPerf()
         self.ctx._check(LIB.zgpu_perf_snapshot(self.h, C.byref(p)))
         return {"steps": p.steps, "kernel_launches": p.kernel_launches, "decode_ms": p.decode_ms,
                 "prefill_ms": p.prefill_ms, "decode_launches": p.decode_launches,
-                "prefill_gemm_ms": p.prefill_gemm_ms, "prefill_attn_ms": p.prefill_attn_ms}
+                "prefill_gemm_ms": p.prefill_gemm_ms, "prefill_attn_ms": p.prefill_attn_ms,
+                "batch_gemm_ms": p.batch_gemm_ms, "batch_attn_ms": p.batch_attn_ms}
 
 
 class MlaKvCache:

@@ -66,7 +66,8 @@ class ZgpuDs2Desc(C.Structure):
 class ZgpuPerf(C.Structure):
     _fields_ = [("steps", _u64), ("kernel_launches", _u64), ("decode_ms", C.c_double),
                 ("prefill_ms", C.c_double), ("decode_launches", _u64),
-                ("prefill_gemm_ms", C.c_double), ("prefill_attn_ms", C.c_double)]
+                ("prefill_gemm_ms", C.c_double), ("prefill_attn_ms", C.c_double),
+                ("batch_gemm_ms", C.c_double), ("batch_attn_ms", C.c_double)]
 
 
 class ZgpuSmodelInfo(C.Structure):
@@ -138,6 +139,7 @@ _SIGS = {
     "zgpu_generate_greedy": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp, _vp]),
     "zgpu_perf_snapshot": (_i32, [_vp, C.POINTER(ZgpuPerf)]),
     "zgpu_prefill_batch": (_i32, [_vp, _vp, _u32, _vp, _u32, _vp, _vp]),
+    "zgpu_decode_batch": (_i32, [_vp, _vp, _u32, _vp, _vp, _vp, _vp]),
     "zgpu_prefill": (_i32, [_vp, _vp, _vp, _u32, _vp, _vp]),
     "zgpu_moe_route_f32": (_i32, [_vp, _vp, _vp, _vp, _u64, _u32, _u32, _u32, _f, _vp, _vp, _vp]),
     "zgpu_mla_kv_create": (_i32, [_vp, _u32, _u32, _u32, _u32, C.POINTER(_vp)]),

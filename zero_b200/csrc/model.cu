@@ -26,6 +26,10 @@
 
 using namespace zgpu;
 
+namespace {
+constexpr uint32_t kMaxDecodeBatch = 256;
+}
+
 struct zgpu_model {
   zgpu_ctx *ctx = nullptr;
   zgpu_qwen3_desc desc = {};
@@ -78,6 +82,13 @@ struct zgpu_model {
   // per layer QKV, O, gate/up, down
   std::vector<int8_t *> pf_w8;
   std::vector<float *> pf_ws8;
+  // batched decode (zgpu_decode_batch): the LM head's operand tiles, and a
+  // block holding the sequence table, attention partials and arrival
+  // counters, logits, tokens and per-row codes
+  int8_t *lm_w8 = nullptr;
+  float *lm_ws8 = nullptr;
+  uint8_t *d_bd = nullptr;
+  size_t bd_cap = 0;
   // tensor parallelism (world > 1): this rank's slice of every stage
   uint32_t rank = 0, world = 1;
   uint32_t q_loc = 0, kv_loc = 0;   // this rank's q / k rows (all of them on one GPU)
@@ -648,6 +659,9 @@ void zgpu_qwen3_destroy(zgpu_model *m) {
   for (auto &e : m->pf_ev) cudaEventDestroy(e);
   for (int8_t *p : m->pf_w8) cudaFree(p);
   for (float *p : m->pf_ws8) cudaFree(p);
+  cudaFree(m->lm_w8);
+  cudaFree(m->lm_ws8);
+  cudaFree(m->d_bd);
   for (DeviceTensor *t : m->owned) {
     cudaFree(t->d);
     delete t;
@@ -1167,6 +1181,43 @@ namespace {
 // RoPE / KV append and the causal attention run per sequence into its own
 // cache; the LM head runs on each sequence's last token.  Every row is
 // computed exactly as a one-sequence prefill computes it.
+// The tensor-core operand tiles (ops.h) of every projection, built once per
+// model on the first multi-token call: per layer QKV, O, gate/up, down.
+zgpu_status ensure_pf_tiles(zgpu_model *m) {
+  if (!m->pf_w8.empty()) return ZGPU_OK;
+  const zgpu_qwen3_desc &d = m->desc;
+  const uint32_t H = d.hidden, F = d.ffn, QD = m->q_dim, QKV = QD + 2 * m->kv_dim;
+  struct Mat {
+    const uint8_t *w;
+    uint64_t gstride;
+    uint32_t rows, in_dim;
+  };
+  for (uint32_t l = 0; l < d.n_layers; ++l) {
+    const Mat mats[4] = {{m->qkv[l], m->gs_h, QKV, H},
+                         {m->o[l]->d, m->o[l]->gstride, H, QD},
+                         {m->gateup[l], m->gs_h, 2 * F, H},
+                         {m->down[l]->d, m->down[l]->gstride, H, F}};
+    for (const Mat &mt : mats) {
+      int8_t *wt = nullptr;
+      float *ws = nullptr;
+      cudaError_t e = cudaMalloc(&wt, mma_tile_bytes(mt.rows, mt.in_dim / 32));
+      if (e == cudaSuccess) e = cudaMalloc(&ws, mma_scale_bytes(mt.rows, mt.in_dim / 32));
+      m->pf_w8.push_back(wt);
+      m->pf_ws8.push_back(ws);
+      if (e == cudaSuccess)
+        e = launch_build_w8_tiles(mt.w, mt.gstride, mt.rows, mt.in_dim / 32, ZGPU_Q4_0, wt, ws, m->ctx->stream);
+      if (e != cudaSuccess) {
+        for (int8_t *p : m->pf_w8) cudaFree(p);
+        for (float *p : m->pf_ws8) cudaFree(p);
+        m->pf_w8.clear();
+        m->pf_ws8.clear();
+        return zgpu_cuda_fail(m->ctx, e, "prefill weight tiles");
+      }
+    }
+  }
+  return ZGPU_OK;
+}
+
 zgpu_status prefill_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, const uint32_t *tokens, uint32_t n,
                         uint32_t *tokens_out, float *logits_out) {
   if (!m || !kvs || !tokens || !tokens_out || n == 0 || n_seq == 0) return ZGPU_ERR_INVALID_ARG;
@@ -1191,36 +1242,7 @@ zgpu_status prefill_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, cons
   const uint32_t H = d.hidden, F = d.ffn, QD = m->q_dim, KVD = m->kv_dim, QKV = QD + 2 * KVD;
   if (H % 128 || QKV % 128 || (2 * F) % 128 || QD % 32 || F % 32)
     return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "prefill: projection rows must be multiples of 128");
-  // weight operand tiles of every projection, once per model
-  if (m->pf_w8.empty()) {
-    struct Mat {
-      const uint8_t *w;
-      uint64_t gstride;
-      uint32_t rows, in_dim;
-    };
-    for (uint32_t l = 0; l < d.n_layers; ++l) {
-      const Mat mats[4] = {{m->qkv[l], m->gs_h, QKV, H},
-                           {m->o[l]->d, m->o[l]->gstride, H, QD},
-                           {m->gateup[l], m->gs_h, 2 * F, H},
-                           {m->down[l]->d, m->down[l]->gstride, H, F}};
-      for (const Mat &mt : mats) {
-        int8_t *wt = nullptr;
-        float *ws = nullptr;
-        cudaError_t e = cudaMalloc(&wt, mma_tile_bytes(mt.rows, mt.in_dim / 32));
-        if (e == cudaSuccess) e = cudaMalloc(&ws, mma_scale_bytes(mt.rows, mt.in_dim / 32));
-        m->pf_w8.push_back(wt);
-        m->pf_ws8.push_back(ws);
-        if (e == cudaSuccess) e = launch_build_w8_tiles(mt.w, mt.gstride, mt.rows, mt.in_dim / 32, ZGPU_Q4_0, wt, ws, ctx->stream);
-        if (e != cudaSuccess) {
-          for (int8_t *p : m->pf_w8) cudaFree(p);
-          for (float *p : m->pf_ws8) cudaFree(p);
-          m->pf_w8.clear();
-          m->pf_ws8.clear();
-          return zgpu_cuda_fail(ctx, e, "prefill weight tiles");
-        }
-      }
-    }
-  }
+  if ((st = ensure_pf_tiles(m))) return st;
   // scratch: tokens | hidden [NT][H] | qkv [NT][QKV] | qrot [NT][QD] | attn [NT][QD] | gu [NT][2F]
   //          | activation tiles and scales for the widest input
   const size_t N = NT, maxk = std::max(std::max(H, QD), F);
@@ -1354,6 +1376,224 @@ zgpu_status prefill_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, cons
   return map_status(ctx, sw);
 }
 
+// One greedy decode step for n_seq independent sequences, each at its own
+// position: forward_single_token (forward_pass.rs:515-631) + the LM head pick
+// (lm_head.rs:98-166) per sequence, computed as one batch.  The projections
+// and the LM head run on the tensor cores over Q8_0-quantised activation rows
+// (the prefill arithmetic, with the LM head's Q8_0 weights as int8 tiles);
+// the attention is the decode kernel with a sequence grid dimension.
+zgpu_status decode_batch_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, const uint32_t *tokens,
+                             const uint32_t *positions, uint32_t *tokens_out, float *logits_out) {
+  if (!m || !kvs || !tokens || !positions || !tokens_out || n_seq == 0) return ZGPU_ERR_INVALID_ARG;
+  zgpu_ctx *ctx = m->ctx;
+  if (m->world > 1)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "tensor-parallel ranks decode through zgpu_generate_greedy");
+  if (n_seq > kMaxDecodeBatch) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "decode batch: at most 256 sequences");
+  cudaSetDevice(ctx->device);
+  const zgpu_qwen3_desc &d = m->desc;
+  const uint32_t H = d.hidden, F = d.ffn, QD = m->q_dim, KVD = m->kv_dim, QKV = QD + 2 * KVD;
+  const uint32_t V = d.vocab_padded, hd = d.head_dim;
+  if (H % 128 || QKV % 128 || (2 * F) % 128 || QD % 32 || F % 32 || V % 128)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG,
+                     "decode batch: projection and vocabulary rows must be multiples of 128");
+  if (hd != 128)   // the decode attention kernel's head size
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "decode batch: head_dim must be 128");
+  uint32_t splits = 0;
+  std::vector<AttnBatchSeq> seqs(n_seq);
+  for (uint32_t i = 0; i < n_seq; ++i) {
+    const zgpu_kv *kv = kvs[i];
+    if (!kv) return ZGPU_ERR_INVALID_ARG;
+    if (kv->n_layers != d.n_layers)
+      return zgpu_fail(ctx, ZGPU_ERR_KV_LAYER_OUT_OF_RANGE, "kv cache layer count differs from the model");
+    if (kv->n_kv != d.n_kv_heads || kv->head_dim != hd)
+      return zgpu_fail(ctx, ZGPU_ERR_KV_INVALID_SLICE_LENGTH, "kv cache geometry differs from the model");
+    if (positions[i] >= kv->max_tokens)
+      return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "decode batch: position beyond the cache");
+    if (tokens[i] >= d.vocab_padded) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "token id beyond the vocab");
+    for (uint32_t j = 0; j < i; ++j)
+      if (kvs[j] == kv) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "decode batch: one cache per sequence");
+    seqs[i] = {kv->d, kv->block, kv->max_tokens, positions[i]};
+    splits = std::max(splits, attention_max_splits(kv->max_tokens));
+  }
+  zgpu_status st;
+  if ((st = ensure_pf_tiles(m))) return st;
+  cudaStream_t s = ctx->stream;
+  cudaError_t e = cudaSuccess;
+  if (!m->lm_w8) {
+    e = cudaMalloc(&m->lm_w8, mma_tile_bytes(V, H / 32));
+    if (e == cudaSuccess) e = cudaMalloc(&m->lm_ws8, mma_scale_bytes(V, H / 32));
+    if (e == cudaSuccess)
+      e = launch_build_w8_tiles(m->out->d, m->out->gstride, V, H / 32, m->out->quant, m->lm_w8, m->lm_ws8, s);
+    if (e != cudaSuccess) {
+      cudaFree(m->lm_w8);
+      cudaFree(m->lm_ws8);
+      m->lm_w8 = nullptr;
+      m->lm_ws8 = nullptr;
+      return zgpu_cuda_fail(ctx, e, "LM head tiles");
+    }
+  }
+  // projection scratch (the prefill layout, n_seq rows)
+  const size_t N = n_seq, maxk = std::max(std::max(H, QD), F);
+  auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
+  const size_t o_tok = 0, o_hid = al(N * 4), o_qkv = o_hid + al(N * H * 4), o_at = o_qkv + al(N * QKV * 4),
+               o_gu = o_at + al(N * QD * 4), o_q8 = o_gu + al(N * 2 * F * 4),
+               o_d8 = o_q8 + al(mma_tile_bytes(N, maxk / 32)), total = o_d8 + al(mma_scale_bytes(N, maxk / 32));
+  if (total > m->pf_cap) {
+    cudaFree(m->d_pf);
+    m->d_pf = nullptr;
+    m->pf_cap = 0;
+    if ((e = cudaMalloc(&m->d_pf, total)) != cudaSuccess) return zgpu_cuda_fail(ctx, e, "decode batch scratch");
+    m->pf_cap = total;
+  }
+  // batch block: seq table | partials | counters | logits | tokens | codes
+  const size_t b_seq = 0, b_part = al(N * sizeof(AttnBatchSeq)),
+               b_cnt = b_part + al(N * d.n_q_heads * splits * (hd + 2) * 4),
+               b_log = b_cnt + al(N * d.n_kv_heads * 4), b_tok = b_log + al(N * V * 4), b_code = b_tok + al(N * 4),
+               b_total = b_code + al(N * 4);
+  if (b_total > m->bd_cap) {
+    cudaFree(m->d_bd);
+    m->d_bd = nullptr;
+    m->bd_cap = 0;
+    if ((e = cudaMalloc(&m->d_bd, b_total)) != cudaSuccess) return zgpu_cuda_fail(ctx, e, "decode batch buffers");
+    m->bd_cap = b_total;
+  }
+  // the arrival counters start at zero (their offset moves with n_seq and the
+  // split count; within the step the attention resets them after use)
+  if ((e = cudaMemsetAsync(m->d_bd + b_cnt, 0, N * d.n_kv_heads * 4, s)) != cudaSuccess)
+    return zgpu_cuda_fail(ctx, e, "memset");
+  uint8_t *B = m->d_pf, *BB = m->d_bd;
+  uint32_t *d_tok = reinterpret_cast<uint32_t *>(B + o_tok);
+  float *hid = reinterpret_cast<float *>(B + o_hid), *qkv = reinterpret_cast<float *>(B + o_qkv),
+        *at = reinterpret_cast<float *>(B + o_at), *gu = reinterpret_cast<float *>(B + o_gu);
+  int8_t *q8 = reinterpret_cast<int8_t *>(B + o_q8);
+  float *d8 = reinterpret_cast<float *>(B + o_d8);
+  AttnBatchSeq *d_seqs = reinterpret_cast<AttnBatchSeq *>(BB + b_seq);
+  float *logits = reinterpret_cast<float *>(BB + b_log);
+  uint32_t *d_out_tok = reinterpret_cast<uint32_t *>(BB + b_tok),
+           *d_codes = reinterpret_cast<uint32_t *>(BB + b_code);
+  const uint32_t T = n_seq;
+  uint32_t launches = 0;
+  // an event pair around every GEMM and attention launch: per-class device time
+  const size_t n_ev = static_cast<size_t>(d.n_layers) * 10 + 2;
+  while (m->pf_ev.size() < n_ev) {
+    cudaEvent_t ev;
+    if ((e = cudaEventCreate(&ev)) != cudaSuccess) return zgpu_cuda_fail(ctx, e, "decode batch events");
+    m->pf_ev.push_back(ev);
+  }
+  size_t ev_i = 0;
+  std::vector<uint8_t> ev_attn;   // per event pair: 1 for an attention launch
+  auto mark = [&]() { cudaEventRecord(m->pf_ev[ev_i++], s); };
+  auto gemm = [&](const int8_t *wt, const float *ws, uint32_t rows, uint32_t in_dim, float *y, bool resadd) {
+    MmaGemmParams p = {};
+    p.wt = wt;
+    p.ws = ws;
+    p.rows = rows;
+    p.bpr = in_dim / 32;
+    p.T = T;
+    p.ldy = rows;
+    p.xt = q8;
+    p.xs = d8;
+    p.y = y;
+    p.status = m->d_status;
+    p.resadd = resadd ? 1u : 0u;
+    ++launches;
+    mark();
+    ev_attn.push_back(0);
+    const cudaError_t ge = launch_q4q8_mma(p, s);
+    mark();
+    return ge;
+  };
+  e = cudaMemcpyAsync(d_tok, tokens, N * 4, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(d_seqs, seqs.data(), N * sizeof(AttnBatchSeq), cudaMemcpyHostToDevice, s);
+  cudaEventRecord(m->ev[0], s);
+  if (e == cudaSuccess) {
+    e = launch_rows_embed(m->emb->d, m->emb->gstride, m->emb->quant, H, static_cast<uint32_t>(m->emb->rows), d_tok,
+                          T, hid, m->d_status, s);
+    ++launches;
+  }
+  LaunchCfg lc;
+  lc.stream = s;
+  lc.pdl = false;
+  lc.sm_count = ctx->sm_count;
+  lc.launch_counter = &launches;
+  AttnParams ap = {};
+  ap.qkv = qkv;
+  ap.inv_freqs = m->d_inv_freqs;
+  ap.out = at;
+  ap.part = reinterpret_cast<float *>(BB + b_part);
+  ap.counters = reinterpret_cast<uint32_t *>(BB + b_cnt);
+  ap.status = m->d_status;
+  ap.n_q = d.n_q_heads;
+  ap.n_kv = d.n_kv_heads;
+  ap.max_splits = splits;
+  ap.eps = d.rms_eps;
+  ap.scale = 1.0f / sqrtf(static_cast<float>(hd));
+  for (uint32_t l = 0; l < d.n_layers && e == cudaSuccess; ++l) {
+    const int8_t *const *w8 = m->pf_w8.data() + 4 * l;
+    const float *const *ws8 = m->pf_ws8.data() + 4 * l;
+    if ((e = launch_rows_rmsnorm_quant(hid, norm_attn(m, l), d.rms_eps, T, H, q8, d8, m->d_status, s))) break;
+    if ((e = gemm(w8[0], ws8[0], QKV, H, qkv, false))) break;
+    ap.q_norm = norm_q(m, l);
+    ap.k_norm = norm_k(m, l);
+    mark();
+    ev_attn.push_back(1);
+    e = launch_attention_batch(ap, d_seqs, l, T, QKV, QD, lc);
+    mark();
+    if (e) break;
+    if ((e = launch_quantize_q8_0_tiles(at, q8, d8, T, QD, m->d_status, s))) break;
+    if ((e = gemm(w8[1], ws8[1], H, QD, hid, true))) break;
+    if ((e = launch_rows_rmsnorm_quant(hid, norm_ffn(m, l), d.rms_eps, T, H, q8, d8, m->d_status, s))) break;
+    if ((e = gemm(w8[2], ws8[2], 2 * F, H, gu, false))) break;
+    if ((e = launch_swiglu_quant_tiles(gu, q8, d8, T, F, m->d_status, s))) break;
+    if ((e = gemm(w8[3], ws8[3], H, F, hid, true))) break;
+    launches += 4;   // two row norms, the attention output and SwiGLU quantisers
+  }
+  if (e == cudaSuccess) {
+    e = launch_rows_rmsnorm_quant(hid, norm_out(m), d.rms_eps, T, H, q8, d8, m->d_status, s);
+    ++launches;
+  }
+  if (e == cudaSuccess) e = gemm(m->lm_w8, m->lm_ws8, V, H, logits, false);
+  if (e == cudaSuccess) {
+    e = launch_rows_argmax(logits, T, V, d.vocab_real, d_out_tok, d_codes, m->d_status, s);
+    ++launches;
+  }
+  cudaEventRecord(m->ev[1], s);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "decode batch");
+  std::vector<uint32_t> codes(N);
+  if ((e = cudaMemcpyAsync(tokens_out, d_out_tok, N * 4, cudaMemcpyDeviceToHost, s)) != cudaSuccess ||
+      (e = cudaMemcpyAsync(codes.data(), d_codes, N * 4, cudaMemcpyDeviceToHost, s)) != cudaSuccess)
+    return zgpu_cuda_fail(ctx, e, "tokens d2h");
+  if (logits_out && (e = cudaMemcpyAsync(logits_out, logits, N * V * 4, cudaMemcpyDeviceToHost, s)) != cudaSuccess)
+    return zgpu_cuda_fail(ctx, e, "logits d2h");
+  uint32_t sw = 0;
+  if ((st = read_status(m, &sw))) return st;   // synchronises the stream
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, m->ev[0], m->ev[1]);
+  m->perf.decode_ms = ms;
+  double gemm_ms = 0, attn_ms = 0;
+  for (size_t i = 0; i + 1 < ev_i; i += 2) {
+    float t = 0.f;
+    cudaEventElapsedTime(&t, m->pf_ev[i], m->pf_ev[i + 1]);
+    (ev_attn[i / 2] ? attn_ms : gemm_ms) += t;
+  }
+  m->perf.batch_gemm_ms = gemm_ms;
+  m->perf.batch_attn_ms = attn_ms;
+  m->perf.steps = 1;
+  m->perf.kernel_launches = launches;
+  m->perf.decode_launches = launches;
+  ctx->launches += launches;
+  m->last_fwd_persistent = false;
+  // the LM-head error of each sequence, as its own call would report it
+  for (uint32_t i = 0; i < n_seq; ++i)
+    if (codes[i])
+      return zgpu_fail(ctx, static_cast<zgpu_status>(codes[i]),
+                       "sequence " + std::to_string(i) +
+                           (codes[i] == ZGPU_ERR_LM_NON_FINITE_LOGITS ? ": non-finite max logit"
+                                                                       : ": argmax in padding region"));
+  return map_status(ctx, sw);
+}
+
 }  // namespace
 
 extern "C" {
@@ -1367,6 +1607,11 @@ zgpu_status zgpu_prefill(zgpu_model *m, zgpu_kv *kv, const uint32_t *tokens, uin
 zgpu_status zgpu_prefill_batch(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, const uint32_t *tokens, uint32_t n,
                                uint32_t *tokens_out, float *logits_out) {
   return prefill_run(m, kvs, n_seq, tokens, n, tokens_out, logits_out);
+}
+
+zgpu_status zgpu_decode_batch(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, const uint32_t *tokens,
+                              const uint32_t *positions, uint32_t *tokens_out, float *logits_out) {
+  return decode_batch_run(m, kvs, n_seq, tokens, positions, tokens_out, logits_out);
 }
 
 }  // extern "C"

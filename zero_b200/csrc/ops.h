@@ -133,6 +133,11 @@ cudaError_t launch_quantize_q8_0_tiles(const float *x, int8_t *xt, float *xs, ui
 // Token-parallel prefill kernels (prefill.cu).
 cudaError_t prefill_setup();
 // RMSNorm of each row, then Q8_0 into activation tiles (as launch_quantize_q8_0_tiles)
+// Per row of n logits: the reference's greedy pick, tok[row], and its LM-head
+// error (0, ZGPU_ERR_LM_NON_FINITE_LOGITS or ZGPU_ERR_LM_ARGMAX_IN_PADDING) in
+// codes[row]; errors also set the status bits.
+cudaError_t launch_rows_argmax(const float *logits, uint32_t rows, uint32_t n, uint32_t vocab_real, uint32_t *tok,
+                               uint32_t *codes, uint32_t *status, cudaStream_t s);
 cudaError_t launch_rows_rmsnorm_quant(const float *x, const float *g, float eps, uint32_t T, uint32_t n, int8_t *xt,
                                       float *xs, uint32_t *status, cudaStream_t s);
 cudaError_t launch_rows_embed(const uint8_t *emb, uint64_t gstride, uint32_t quant, uint32_t hidden, uint32_t vocab,

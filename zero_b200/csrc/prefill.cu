@@ -448,7 +448,73 @@ __global__ void swiglu_quant_tiles_kernel(const float *y, int8_t *xt, float *xs,
   quant_lane_q8_0(ref_silu_mul(yr[8 * u + r], yr[8 * u + 4 + r]), qa, da, lane, status);
 }
 
+// Greedy pick per row of n logits (lm_head_argmax_dynamic, lm_head.rs:98-166,
+// applied to each sequence of a batch): the first index holding the largest
+// value (a NaN never wins; a row of -inf / NaN keeps index 0), then a
+// non-finite maximum is ZGPU_ERR_LM_NON_FINITE_LOGITS and an index at or past
+// vocab_real ZGPU_ERR_LM_ARGMAX_IN_PADDING, recorded in codes[row] and in the
+// status bits.  One CTA per row: strided first-max per thread, then a tree
+// in which the larger value wins and equal values go to the smaller index,
+// the same pick as the sequential scan.
+constexpr uint32_t kArgmaxThreads = 512;
+
+__global__ void __launch_bounds__(kArgmaxThreads)
+    rows_argmax_kernel(const float *logits, uint32_t n, uint32_t vocab_real, uint32_t *tok, uint32_t *codes,
+                       uint32_t *status) {
+  __shared__ float bv[kArgmaxThreads / 32];
+  __shared__ uint32_t bi[kArgmaxThreads / 32];
+  const float *row = logits + static_cast<size_t>(blockIdx.x) * n;
+  float v = -INFINITY;
+  uint32_t idx = 0xFFFFFFFFu;
+  for (uint32_t i = threadIdx.x; i < n; i += kArgmaxThreads) {
+    const float x = row[i];
+    if (x > v) {
+      v = x;
+      idx = i;
+    }
+  }
+  auto better = [](float a, uint32_t ia, float b, uint32_t ib) { return b > a || (b == a && ib < ia); };
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, off);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, idx, off);
+    if (better(v, idx, ov, oi)) {
+      v = ov;
+      idx = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    bv[threadIdx.x >> 5] = v;
+    bi[threadIdx.x >> 5] = idx;
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  for (uint32_t w = 1; w < kArgmaxThreads / 32; ++w)
+    if (better(v, idx, bv[w], bi[w])) {
+      v = bv[w];
+      idx = bi[w];
+    }
+  if (idx == 0xFFFFFFFFu) idx = 0;
+  uint32_t code = 0;
+  if (!(fabsf(v) < INFINITY)) {
+    code = ZGPU_ERR_LM_NON_FINITE_LOGITS;
+    atomicOr(status, ZDEV_ERR_LM_NONFINITE);
+  } else if (idx >= vocab_real) {
+    code = ZGPU_ERR_LM_ARGMAX_IN_PADDING;
+    atomicOr(status, ZDEV_ERR_LM_PADDING);
+  }
+  tok[blockIdx.x] = idx;
+  codes[blockIdx.x] = code;
+}
+
 }  // namespace
+
+cudaError_t launch_rows_argmax(const float *logits, uint32_t rows, uint32_t n, uint32_t vocab_real, uint32_t *tok,
+                               uint32_t *codes, uint32_t *status, cudaStream_t s) {
+  if (rows == 0 || n == 0) return cudaErrorInvalidValue;
+  rows_argmax_kernel<<<rows, kArgmaxThreads, 0, s>>>(logits, n, vocab_real, tok, codes, status);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_swiglu_quant_tiles(const float *y, int8_t *xt, float *xs, uint32_t T, uint32_t ffn,
                                       uint32_t *status, cudaStream_t s) {
