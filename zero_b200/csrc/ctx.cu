@@ -170,10 +170,22 @@ zgpu_status zgpu_register_weights(zgpu_ctx *ctx, const void *host_ptr, size_t le
       return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "K-quant cols must be a positive multiple of 256");
     if (len != rows * (cols / 256) * (dtype == ZGPU_Q4_K ? 144 : 210))
       return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "byte length does not match rows x cols");
+    if (cols > 65536) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "K-quant cols above 65536");
     t.quant = dtype;
-    t.bytes = len;
-    ZCHECK(cudaMalloc(&t.d, len), "cudaMalloc(weights)");
-    ZCHECK(cudaMemcpy(t.d, host_ptr, len, cudaMemcpyHostToDevice), "upload");
+    if (dtype == ZGPU_Q4_K) {
+      t.bytes = len;
+      ZCHECK(cudaMalloc(&t.d, len), "cudaMalloc(weights)");
+      ZCHECK(cudaMemcpy(t.d, host_ptr, len, cudaMemcpyHostToDevice), "upload");
+    } else {
+      // Q6_K: each 210-byte super-block padded to kQ6kStride bytes
+      const size_t nb = len / 210;
+      std::vector<uint8_t> pad(nb * zgpu::kQ6kStride, 0);
+      const uint8_t *src = static_cast<const uint8_t *>(host_ptr);
+      for (size_t b = 0; b < nb; ++b) std::memcpy(pad.data() + b * zgpu::kQ6kStride, src + b * 210, 210);
+      t.bytes = pad.size();
+      ZCHECK(cudaMalloc(&t.d, t.bytes), "cudaMalloc(weights)");
+      ZCHECK(cudaMemcpy(t.d, pad.data(), t.bytes, cudaMemcpyHostToDevice), "upload");
+    }
   } else {
     const bool x4 = (dtype == ZGPU_Q4_0X4 || dtype == ZGPU_Q8_0X4);
     const uint32_t quant = (dtype == ZGPU_Q4_0 || dtype == ZGPU_Q4_0X4)   ? ZGPU_Q4_0

@@ -23,12 +23,23 @@
 //               x columns 32 ((w - 2) / 4).. (tokens) of accumulator s, scales
 //               and accumulates in f32 registers, then arrives on empty[s],
 //               which frees stage s and accumulator s for block b + 4.
+// For a few tokens (T <= 32, batched decode) the token tile is 32 wide:
+// 16 stages / accumulators of 32 TMEM columns each, a 1 KB activation copy
+// per block and 4 epilogue warps, so that 16 blocks of weights are in flight
+// per SM instead of 4.  A weight with few 128-row tiles can also be split
+// along K (MmaGemmParams::ksplit): each split sums its block range in order
+// into a partial, and a reduce kernel adds the partials in split order.  The
+// split count depends on the weight's shape alone, so a token's result does
+// not depend on how many tokens share the launch; with a split the block sum
+// is regrouped (no longer the CPU restatement's order bit for bit).
 // Every wait is bounded (status ZDEV_ERR_TIMEOUT); on an expired wait each
 // role stops, the producer drains its copies in flight and the MMA issuer its
 // MMAs before TMEM is freed.  The launch asks for more than half an SM's
 // shared memory so that two CTAs never meet on one SM: the second CTA's
 // 512-column TMEM allocation would wait for the first.
 #include <cuda_runtime.h>
+
+#include <algorithm>
 #include <stdint.h>
 
 #include "common.cuh"
@@ -41,15 +52,28 @@ namespace zgpu {
 namespace {
 
 constexpr uint32_t kTileM = 128;
-constexpr uint32_t kTileN = 128;
-constexpr uint32_t kStages = 4;                  // = TMEM accumulators
-constexpr uint32_t kEpiWarps = 16;
-constexpr uint32_t kGemmThreads = 32 * (2 + kEpiWarps);
-// stage layout (bytes)
-constexpr uint32_t kStA = 0, kStB = 4096, kStW = 8192, kStX = 8192 + 512, kStageBytes = 8192 + 1024;
-constexpr uint32_t kTmemCols = kStages * kTileN; // 512: the whole TMEM of the SM
+constexpr uint32_t kTmemCols = 512;              // the whole TMEM of the SM
 constexpr uint32_t kDynSmem = 120 * 1024;        // > half of an SM: one CTA per SM
-static_assert(kStages * kStageBytes <= kDynSmem, "stages fit the dynamic shared memory");
+
+// Geometry of the kernel for a token tile of NT columns: 128 for many tokens
+// (prefill), 32 for a few (batched decode), where a 32-wide tile leaves TMEM
+// room for 16 block accumulators in flight instead of 4.  A stage holds one
+// 32-element block: the weight tile (128 rows), the first NT rows of the
+// activation tile, and both tiles' block scales.
+template <uint32_t NT>
+struct MmaCfg {
+  static constexpr uint32_t kTileN = NT;
+  static constexpr uint32_t kStages = kTmemCols / NT;          // = TMEM accumulators
+  static constexpr uint32_t kEpiWarps = NT == 128 ? 16 : 4;
+  static constexpr uint32_t kThreads = 32 * (2 + kEpiWarps);
+  static constexpr uint32_t kStA = 0, kStB = 4096, kStW = 4096 + NT * 32, kStX = kStW + 512;
+  static constexpr uint32_t kStageLoad = kStX + NT * 4;        // bytes copied per stage
+  static constexpr uint32_t kStageBytes = (kStageLoad + 1023) / 1024 * 1024;
+  // instruction descriptor of kind::i8: D s32, A and B signed int8, both
+  // K-major, N = NT, M = 128, dense
+  static constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((NT >> 3) << 17) | ((kTileM >> 4) << 24);
+  static_assert(kStages * kStageBytes <= kDynSmem, "stages fit the dynamic shared memory");
+};
 }
 
 namespace {
@@ -68,9 +92,6 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint
   return d;
 }
 
-// Instruction descriptor of kind::i8: D s32, A and B signed int8, both
-// K-major, N = 64, M = 128, dense.
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((kTileN >> 3) << 17) | ((kTileM >> 4) << 24);
 
 __device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                         uint32_t accumulate) {
@@ -133,9 +154,15 @@ __device__ __forceinline__ uint32_t nib_to_s8(uint32_t n4) {
   return m | ((m & 0x08080808u) * 0x1Eu);
 }
 
-__global__ void __launch_bounds__(kGemmThreads, 1) q4q8_mma_kernel(const MmaGemmParams p) {
+template <uint32_t NT>
+__global__ void __launch_bounds__(MmaCfg<NT>::kThreads, 1) q4q8_mma_kernel(const MmaGemmParams p) {
+  using Cfg = MmaCfg<NT>;
+  constexpr uint32_t kTileN = Cfg::kTileN, kStages = Cfg::kStages, kEpiWarps = Cfg::kEpiWarps;
+  constexpr uint32_t kStA = Cfg::kStA, kStB = Cfg::kStB, kStW = Cfg::kStW, kStX = Cfg::kStX;
+  constexpr uint32_t kStageBytes = Cfg::kStageBytes, kIdesc = Cfg::kIdesc;
   extern __shared__ __align__(1024) uint8_t ring[];
-  __shared__ __align__(8) uint64_t full[kStages], done[kStages], empty[kStages], drain;
+  __shared__ __align__(8) uint64_t full[MmaCfg<NT>::kStages], done[MmaCfg<NT>::kStages],
+      empty[MmaCfg<NT>::kStages], drain;
   __shared__ uint32_t tmem_base;
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t bpr = p.bpr;
@@ -165,30 +192,44 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q4q8_mma_kernel(const MmaGemm
   // their token tile through L2.  gb counts this CTA's blocks over all its
   // tiles and drives every stage / phase, so one tile's epilogue overlaps
   // the next tile's copies and MMAs.
-  const uint32_t n_mt = p.rows / kTileM, n_tiles = n_mt * ((p.T + kTileN - 1) / kTileN);
+  // With a K split, tile i also names its block range: (weight tile, token
+  // tile, split); split ks covers blocks [ks * bpr / S, (ks + 1) * bpr / S).
+  const uint32_t S = p.ksplit > 1 ? p.ksplit : 1u;
+  const uint32_t n_mt = p.rows / kTileM, n_nt = (p.T + kTileN - 1) / kTileN, n_tiles = n_mt * n_nt * S;
+  auto tile_of = [&](uint32_t tix, uint32_t &mt, uint32_t &nt, uint32_t &b0, uint32_t &b1) {
+    mt = tix % n_mt;
+    const uint32_t r = tix / n_mt, ks = r / n_nt;
+    nt = r % n_nt;
+    b0 = static_cast<uint32_t>(static_cast<uint64_t>(ks) * bpr / S);
+    b1 = static_cast<uint32_t>(static_cast<uint64_t>(ks + 1) * bpr / S);
+  };
   if (warp == 0) {
     // ---------------- producer ----------------
     if (lane == 0) {
       uint32_t gb = 0;
       bool stop = false;
       for (uint32_t tix = blockIdx.x; tix < n_tiles && !stop; tix += gridDim.x) {
-        const uint32_t mt = tix % n_mt, nt = tix / n_mt;
+        uint32_t mt, nt, b0, b1;
+        tile_of(tix, mt, nt, b0, b1);
+        // token tile nt: rows [nt NT, nt NT + NT) of the 128-row activation
+        // tiles, which in the canonical layout are NT * 32 contiguous bytes
+        const uint32_t tt = nt * kTileN / kMmaTile, r0 = nt * kTileN % kMmaTile;
         const int8_t *wa = p.wt + static_cast<size_t>(mt) * bpr * 4096u;
-        const int8_t *xa = p.xt + static_cast<size_t>(nt) * bpr * 4096u;
+        const int8_t *xa = p.xt + static_cast<size_t>(tt) * bpr * 4096u + r0 * 32u;
         const float *ws = p.ws + static_cast<size_t>(mt) * bpr * kTileM;
-        const float *xs = p.xs + static_cast<size_t>(nt) * bpr * kTileN;
-        for (uint32_t b = 0; b < bpr; ++b, ++gb) {
+        const float *xs = p.xs + static_cast<size_t>(tt) * bpr * kMmaTile + r0;
+        for (uint32_t b = b0; b < b1; ++b, ++gb) {
           const uint32_t s = gb % kStages;
           if (gb >= kStages && !mbar_wait(smem_addr(&empty[s]), ((gb / kStages) - 1) & 1, p.status)) {
             stop = true;
             break;
           }
           const uint32_t st = smem_addr(ring + s * kStageBytes), fb = smem_addr(&full[s]);
-          mbar_arrive_expect_tx(fb, kStageBytes);
+          mbar_arrive_expect_tx(fb, Cfg::kStageLoad);
           bulk_copy_g2s(st + kStA, wa + static_cast<size_t>(b) * 4096u, 4096, fb);
-          bulk_copy_g2s(st + kStB, xa + static_cast<size_t>(b) * 4096u, 4096, fb);
+          bulk_copy_g2s(st + kStB, xa + static_cast<size_t>(b) * 4096u, kTileN * 32, fb);
           bulk_copy_g2s(st + kStW, ws + static_cast<size_t>(b) * kTileM, 512, fb);
-          bulk_copy_g2s(st + kStX, xs + static_cast<size_t>(b) * kTileN, 512, fb);
+          bulk_copy_g2s(st + kStX, xs + static_cast<size_t>(b) * kMmaTile, kTileN * 4, fb);
         }
       }
       // never leave a copy in flight when the CTA may exit
@@ -201,7 +242,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q4q8_mma_kernel(const MmaGemm
       uint32_t gb = 0;
       bool stop = false;
       for (uint32_t tix = blockIdx.x; tix < n_tiles && !stop; tix += gridDim.x) {
-        for (uint32_t b = 0; b < bpr; ++b, ++gb) {
+        uint32_t mt, nt, b0, b1;
+        tile_of(tix, mt, nt, b0, b1);
+        for (uint32_t b = b0; b < b1; ++b, ++gb) {
           const uint32_t s = gb % kStages;
           if (!mbar_wait(smem_addr(&full[s]), (gb / kStages) & 1, p.status)) {
             stop = true;
@@ -219,15 +262,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q4q8_mma_kernel(const MmaGemm
     }
   } else {
     // ---------------- epilogue ----------------
-    const uint32_t q = warp & 3, c = (warp - 2) >> 2;   // TMEM lane quarter, token quarter
+    // TMEM lane quarter (a warp reads the quarter warp % 4), 32-token column group
+    const uint32_t q = warp & 3, c = kTileN == 128 ? (warp - 2) >> 2 : 0;
     uint32_t gb = 0;
     bool ok = true;
     for (uint32_t tix = blockIdx.x; tix < n_tiles; tix += gridDim.x) {
-      const uint32_t mt = tix % n_mt, nt = tix / n_mt;
+      uint32_t mt, nt, b0, b1;
+      tile_of(tix, mt, nt, b0, b1);
       float acc[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) acc[j] = 0.f;
-      for (uint32_t b = 0; b < bpr && ok; ++b, ++gb) {
+      for (uint32_t b = b0; b < b1 && ok; ++b, ++gb) {
         const uint32_t s = gb % kStages, par = (gb / kStages) & 1;
         if (!mbar_wait(smem_addr(&done[s]), par, p.status) || !mbar_wait(smem_addr(&full[s]), par, p.status)) {
           ok = false;
@@ -266,9 +311,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q4q8_mma_kernel(const MmaGemm
       for (int j = 0; j < 32; ++j) {
         const uint32_t t = nt * kTileN + 32 * c + j;
         if (t < p.T) {
-          float *dst = p.y + static_cast<uint64_t>(t) * p.ldy + row;
           const float val = ok ? acc[j] : __uint_as_float(0x7fc00000u);
-          *dst = p.resadd ? __fadd_rn(*dst, val) : val;
+          if (S > 1) {   // this split's partial; the reduce kernel adds the splits in order
+            const uint32_t ks = tix / (n_mt * n_nt);
+            p.part[(static_cast<uint64_t>(ks) * p.T + t) * p.rows + row] = val;
+          } else {
+            float *dst = p.y + static_cast<uint64_t>(t) * p.ldy + row;
+            *dst = p.resadd ? __fadd_rn(*dst, val) : val;
+          }
         }
       }
     }
@@ -278,6 +328,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q4q8_mma_kernel(const MmaGemm
   tc_fence_after();
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+}
+
+// y[t][r] = (resadd ? y[t][r] : 0) + sum over splits, added in split order.
+__global__ void mma_split_reduce_kernel(const float *part, float *y, uint32_t rows, uint32_t T, uint32_t ldy,
+                                        uint32_t S, uint32_t resadd) {
+  const uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
+  if (i >= static_cast<uint64_t>(rows) * T) return;
+  const uint32_t t = static_cast<uint32_t>(i / rows), r = static_cast<uint32_t>(i % rows);
+  float acc = part[i];
+  for (uint32_t ks = 1; ks < S; ++ks) acc = __fadd_rn(acc, part[static_cast<uint64_t>(ks) * rows * T + i]);
+  float *dst = y + static_cast<uint64_t>(t) * ldy + r;
+  *dst = resadd ? __fadd_rn(*dst, acc) : acc;
 }
 
 // Q4_0 or Q8_0 group streams -> weight tiles: CTA (row tile, block), thread
@@ -338,17 +400,42 @@ cudaError_t mma_setup() {
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(q4q8_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem);
+  e = cudaFuncSetAttribute(q4q8_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(q4q8_mma_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem);
+  return e;
 }
 
 cudaError_t launch_q4q8_mma(const MmaGemmParams &p, cudaStream_t s) {
   if (p.rows == 0 || p.rows % kTileM || p.bpr == 0 || p.T == 0 || !p.wt || !p.ws || !p.xt || !p.xs ||
       g_sm_count <= 0)
     return cudaErrorInvalidValue;
-  const uint64_t tiles = static_cast<uint64_t>(p.rows / kTileM) * ((p.T + kTileN - 1) / kTileN);
+  const uint32_t S = p.ksplit > 1 ? p.ksplit : 1u;
+  if (S > p.bpr || (S > 1 && !p.part)) return cudaErrorInvalidValue;
+  // a few tokens (batched decode): 32-token tiles, 16 blocks in flight; the
+  // per-row arithmetic is the same for both widths
+  const uint32_t nt_w = p.T <= 32 ? 32u : 128u;
+  const uint64_t tiles = static_cast<uint64_t>(p.rows / kTileM) * ((p.T + nt_w - 1) / nt_w) * S;
   const unsigned grid = static_cast<unsigned>(tiles < static_cast<uint64_t>(g_sm_count) ? tiles : g_sm_count);
-  q4q8_mma_kernel<<<grid, kGemmThreads, kDynSmem, s>>>(p);
+  if (nt_w == 32)
+    q4q8_mma_kernel<32><<<grid, MmaCfg<32>::kThreads, kDynSmem, s>>>(p);
+  else
+    q4q8_mma_kernel<128><<<grid, MmaCfg<128>::kThreads, kDynSmem, s>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || S == 1) return e;
+  const uint64_t n = static_cast<uint64_t>(p.rows) * p.T;
+  mma_split_reduce_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(p.part, p.y, p.rows, p.T, p.ldy, S,
+                                                                              p.resadd);
   return cudaGetLastError();
+}
+
+uint32_t mma_ksplit(uint32_t rows, uint32_t bpr) {
+  // enough (weight tile, split) pairs to give every SM two, at least 4 blocks per split
+  const uint32_t n_mt = rows / kTileM, sms = g_sm_count > 0 ? static_cast<uint32_t>(g_sm_count) : 148u;
+  if (n_mt == 0 || n_mt >= 2 * sms) return 1;
+  uint32_t S = (2 * sms + n_mt - 1) / n_mt;
+  S = std::min(S, std::max(1u, bpr / 4));
+  return std::min(S, kMmaMaxSplit);
 }
 
 cudaError_t launch_build_w8_tiles(const uint8_t *w, uint64_t gstride, uint32_t rows, uint32_t bpr, uint32_t quant,

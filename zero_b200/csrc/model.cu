@@ -1445,11 +1445,18 @@ zgpu_status decode_batch_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq,
     if ((e = cudaMalloc(&m->d_pf, total)) != cudaSuccess) return zgpu_cuda_fail(ctx, e, "decode batch scratch");
     m->pf_cap = total;
   }
-  // batch block: seq table | partials | counters | logits | tokens | codes
+  // GEMM K-split partials: the largest split x rows of the step's matmuls
+  size_t split_rows = 0;
+  {
+    const uint32_t shapes[5][2] = {{QKV, H}, {H, QD}, {2 * F, H}, {H, F}, {V, H}};
+    for (const auto &sh : shapes)
+      split_rows = std::max(split_rows, static_cast<size_t>(mma_ksplit(sh[0], sh[1] / 32)) * sh[0]);
+  }
+  // batch block: seq table | partials | counters | logits | tokens | codes | GEMM partials
   const size_t b_seq = 0, b_part = al(N * sizeof(AttnBatchSeq)),
                b_cnt = b_part + al(N * d.n_q_heads * splits * (hd + 2) * 4),
                b_log = b_cnt + al(N * d.n_kv_heads * 4), b_tok = b_log + al(N * V * 4), b_code = b_tok + al(N * 4),
-               b_total = b_code + al(N * 4);
+               b_gpart = b_code + al(N * 4), b_total = b_gpart + al(split_rows * N * 4);
   if (b_total > m->bd_cap) {
     cudaFree(m->d_bd);
     m->d_bd = nullptr;
@@ -1496,7 +1503,9 @@ zgpu_status decode_batch_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq,
     p.y = y;
     p.status = m->d_status;
     p.resadd = resadd ? 1u : 0u;
-    ++launches;
+    p.ksplit = mma_ksplit(rows, in_dim / 32);
+    p.part = reinterpret_cast<float *>(BB + b_gpart);
+    launches += p.ksplit > 1 ? 2 : 1;
     mark();
     ev_attn.push_back(0);
     const cudaError_t ge = launch_q4q8_mma(p, s);

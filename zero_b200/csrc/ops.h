@@ -119,9 +119,18 @@ struct MmaGemmParams {
   uint32_t rows, bpr, T, ldy;
   uint32_t *status;
   uint32_t resadd;          // 0: y = result; 1: y = y + result (residual add)
+  // K split (small T): ksplit > 1 runs each weight tile as ksplit block
+  // ranges in parallel, each summed in block order into part [ksplit][T][rows]
+  // (scratch), then added in split order; 0 or 1: no split
+  uint32_t ksplit;
+  float *part;
 };
+constexpr uint32_t kMmaMaxSplit = 16;
 cudaError_t mma_setup();
 cudaError_t launch_q4q8_mma(const MmaGemmParams &p, cudaStream_t s);
+// The K split for a weight of rows x (32 bpr): a function of the weight's
+// shape alone, so a row's result never depends on T.
+uint32_t mma_ksplit(uint32_t rows, uint32_t bpr);
 // Q4_0 group streams (layout.h) -> weight tiles + scales; rows % 128 == 0.
 cudaError_t launch_build_w8_tiles(const uint8_t *w, uint64_t gstride, uint32_t rows, uint32_t bpr, uint32_t quant,
                                   int8_t *wt, float *ws, cudaStream_t s);
@@ -154,7 +163,11 @@ cudaError_t launch_swiglu_rows(const float *y, float *act, uint32_t T, uint32_t 
 cudaError_t launch_swiglu_quant_tiles(const float *y, int8_t *xt, float *xs, uint32_t T, uint32_t ffn,
                                       uint32_t *status, cudaStream_t s);
 
-// y = W x over K-quant rows (kquant.cu): quant ZGPU_Q4_K or ZGPU_Q6_K, in_dim % 256 == 0.
+// Device bytes per Q6_K super-block: the 210-byte block padded so that its
+// fields start on 8-byte boundaries (registration pads, kquant.cu reads).
+constexpr uint32_t kQ6kStride = 224;
+// y = W x over K-quant rows (kquant.cu): quant ZGPU_Q4_K (plain rows) or
+// ZGPU_Q6_K (kQ6kStride-byte blocks), in_dim % 256 == 0, at most 65536.
 cudaError_t launch_gemv_kquant(const uint8_t *w, uint32_t quant, uint32_t rows, uint32_t in_dim, const float *x,
                                float *y, cudaStream_t s);
 
