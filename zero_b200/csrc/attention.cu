@@ -24,7 +24,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
 
 // Grid (n_kv_heads, max_splits, n_seq): the same block as above on
 // sequence blockIdx.z's rows, cache and position.
-__global__ void __launch_bounds__(kAttnThreads)
+__global__ void __launch_bounds__(kAttnThreads, 2)
     attn_decode_batch_kernel(const AttnParams p, const AttnBatchSeq *seqs, uint32_t layer, uint32_t qkv_stride,
                              uint32_t out_stride) {
   __shared__ AttnSmem sm;
@@ -40,7 +40,7 @@ __global__ void __launch_bounds__(kAttnThreads)
   q.kv_layer = sq.kv + static_cast<size_t>(layer) * 2 * sq.block;
   q.kv_block = sq.block;
   q.max_tokens = sq.max_tokens;
-  attn_decode_block(q, blockIdx.x, blockIdx.y, sq.pos, threadIdx.x, sm, BlockBar());
+  attn_decode_block<BlockBar, false, 4>(q, blockIdx.x, blockIdx.y, sq.pos, threadIdx.x, sm, BlockBar());
 }
 
 }  // namespace
