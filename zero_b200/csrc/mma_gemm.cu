@@ -25,8 +25,8 @@
 //               which frees stage s and accumulator s for block b + 4.
 // For a few tokens (T <= 32, batched decode) the token tile is 32 wide:
 // 16 stages / accumulators of 32 TMEM columns each, a 1 KB activation copy
-// per block and 4 epilogue warps, so that 16 blocks of weights are in flight
-// per SM instead of 4.  A weight with few 128-row tiles can also be split
+// per block and 16 epilogue warps of 8 columns each, so that 16 blocks of
+// weights are in flight per SM instead of 4.  A weight with few 128-row tiles can also be split
 // along K (MmaGemmParams::ksplit): each split sums its block range in order
 // into a partial, and a reduce kernel adds the partials in split order.  The
 // split count depends on the weight's shape alone, so a token's result does
@@ -64,7 +64,8 @@ template <uint32_t NT>
 struct MmaCfg {
   static constexpr uint32_t kTileN = NT;
   static constexpr uint32_t kStages = kTmemCols / NT;          // = TMEM accumulators
-  static constexpr uint32_t kEpiWarps = NT == 128 ? 16 : 4;
+  static constexpr uint32_t kEpiWarps = 16;                     // 4 lane quarters x 4 column groups
+  static constexpr uint32_t kCols = NT / 4;                      // token columns per epilogue warp
   static constexpr uint32_t kThreads = 32 * (2 + kEpiWarps);
   static constexpr uint32_t kStA = 0, kStB = 4096, kStW = 4096 + NT * 32, kStX = kStW + 512;
   static constexpr uint32_t kStageLoad = kStX + NT * 4;        // bytes copied per stage
@@ -120,6 +121,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
       : "r"(taddr)
       : "memory");
+}
+// 8 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr)
+               : "memory");
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
@@ -262,16 +270,17 @@ __global__ void __launch_bounds__(MmaCfg<NT>::kThreads, 1) q4q8_mma_kernel(const
     }
   } else {
     // ---------------- epilogue ----------------
-    // TMEM lane quarter (a warp reads the quarter warp % 4), 32-token column group
-    const uint32_t q = warp & 3, c = kTileN == 128 ? (warp - 2) >> 2 : 0;
+    // TMEM lane quarter (a warp reads the quarter warp % 4) and group of CW token columns
+    constexpr uint32_t CW = Cfg::kCols;
+    const uint32_t q = warp & 3, c = (warp - 2) >> 2;
     uint32_t gb = 0;
     bool ok = true;
     for (uint32_t tix = blockIdx.x; tix < n_tiles; tix += gridDim.x) {
       uint32_t mt, nt, b0, b1;
       tile_of(tix, mt, nt, b0, b1);
-      float acc[32];
+      float acc[CW];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+      for (int j = 0; j < static_cast<int>(CW); ++j) acc[j] = 0.f;
       for (uint32_t b = b0; b < b1 && ok; ++b, ++gb) {
         const uint32_t s = gb % kStages, par = (gb / kStages) & 1;
         if (!mbar_wait(smem_addr(&done[s]), par, p.status) || !mbar_wait(smem_addr(&full[s]), par, p.status)) {
@@ -281,16 +290,19 @@ __global__ void __launch_bounds__(MmaCfg<NT>::kThreads, 1) q4q8_mma_kernel(const
         tc_fence_after();
         const uint8_t *st = ring + s * kStageBytes;
         const float dw = reinterpret_cast<const float *>(st + kStW)[32 * q + lane];
-        const float4 *dx4 = reinterpret_cast<const float4 *>(st + kStX) + 8 * c;
-        uint32_t v[32];
-        tmem_ld32(tmem + ((32u * q) << 16) + s * kTileN + 32 * c, v);
+        const float4 *dx4 = reinterpret_cast<const float4 *>(st + kStX) + (CW / 4) * c;
+        uint32_t v[CW];
+        if constexpr (CW == 32)
+          tmem_ld32(tmem + ((32u * q) << 16) + s * kTileN + CW * c, v);
+        else
+          tmem_ld8(tmem + ((32u * q) << 16) + s * kTileN + CW * c, v);
         tmem_ld_wait();
         // acc += (sumi * d_w) * d_x, two columns per packed instruction.  sumi
         // -> f32 exactly: |sumi| <= 32 * 8 * 127 < 2^22, so sumi + 1.5 * 2^23
         // taken as float bits, minus 1.5 * 2^23, is sumi
         const float2 dw2 = make_float2(dw, dw), magic = make_float2(-12582912.0f, -12582912.0f);
 #pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
+        for (int j4 = 0; j4 < static_cast<int>(CW / 4); ++j4) {
           const float4 d4 = dx4[j4];
 #pragma unroll
           for (int k = 0; k < 2; ++k) {
@@ -308,8 +320,8 @@ __global__ void __launch_bounds__(MmaCfg<NT>::kThreads, 1) q4q8_mma_kernel(const
       }
       const uint32_t row = mt * kTileM + 32 * q + lane;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const uint32_t t = nt * kTileN + 32 * c + j;
+      for (int j = 0; j < static_cast<int>(CW); ++j) {
+        const uint32_t t = nt * kTileN + CW * c + j;
         if (t < p.T) {
           const float val = ok ? acc[j] : __uint_as_float(0x7fc00000u);
           if (S > 1) {   // this split's partial; the reduce kernel adds the splits in order
@@ -430,12 +442,23 @@ cudaError_t launch_q4q8_mma(const MmaGemmParams &p, cudaStream_t s) {
 }
 
 uint32_t mma_ksplit(uint32_t rows, uint32_t bpr) {
-  // enough (weight tile, split) pairs to give every SM two, at least 4 blocks per split
+  // The split that minimises the blocks the busiest CTA streams: waves of
+  // (weight tile, split) pairs over the SMs times the blocks of one split,
+  // plus a few blocks' worth of per-tile start-up; at least 4 blocks a split.
   const uint32_t n_mt = rows / kTileM, sms = g_sm_count > 0 ? static_cast<uint32_t>(g_sm_count) : 148u;
-  if (n_mt == 0 || n_mt >= 2 * sms) return 1;
-  uint32_t S = (2 * sms + n_mt - 1) / n_mt;
-  S = std::min(S, std::max(1u, bpr / 4));
-  return std::min(S, kMmaMaxSplit);
+  if (n_mt == 0) return 1;
+  const uint32_t s_max = std::min(kMmaMaxSplit, std::max(1u, bpr / 4));
+  uint32_t best = 1;
+  uint64_t best_cost = ~0ull;
+  for (uint32_t S = 1; S <= s_max; ++S) {
+    const uint64_t waves = (static_cast<uint64_t>(n_mt) * S + sms - 1) / sms;
+    const uint64_t cost = waves * ((bpr + S - 1) / S + 4);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = S;
+    }
+  }
+  return best;
 }
 
 cudaError_t launch_build_w8_tiles(const uint8_t *w, uint64_t gstride, uint32_t rows, uint32_t bpr, uint32_t quant,
