@@ -98,6 +98,10 @@ def _load() -> C.CDLL:
         "zo_ds2_run_lm_head": (C.c_int, [C.c_void_p, _u32p, _f32p]),
         "zo_ds2_run_generate": (C.c_int, [C.c_void_p, _u32p, C.c_uint32, C.c_uint32, _u32p, _f32p, _f32p]),
         "zo_ds2_run_cache": (_f32p, [C.c_void_p]),
+        "zo_ds2_run_mha_cache": (_f32p, [C.c_void_p]),
+        "zo_mha_work_floats": (sz, [C.c_void_p, C.c_uint32, C.c_uint32]),
+        "zo_mha_attention": (C.c_int, [_f32p, _u8p, _u8p, _u8p, _u8p, C.c_void_p, C.c_uint32, _f32p, _f32p,
+                                       C.c_uint32, C.c_uint32, _f32p, _f32p]),
         "zo_ds2_run_expert_ids": (_u32p, [C.c_void_p]),
         "zo_ds2_run_expert_weights": (_f32p, [C.c_void_p]),
     }
@@ -501,7 +505,8 @@ class _Ds2Layer(C.Structure):
                 ("ffn_gate", C.c_void_p), ("ffn_up", C.c_void_p), ("ffn_down", C.c_void_p),
                 ("router_w", C.c_void_p), ("router_b", C.c_void_p), ("gate_exps", C.c_void_p),
                 ("up_exps", C.c_void_p), ("down_exps", C.c_void_p), ("gate_shexp", C.c_void_p),
-                ("up_shexp", C.c_void_p), ("down_shexp", C.c_void_p)]
+                ("up_shexp", C.c_void_p), ("down_shexp", C.c_void_p), ("mha", C.c_int),
+                ("q_mha", C.c_void_p), ("k_mha", C.c_void_p), ("v_mha", C.c_void_p)]
 
 
 class _Ds2(C.Structure):
@@ -510,7 +515,7 @@ class _Ds2(C.Structure):
                 ("vocab_padded", C.c_uint32), ("vocab_real", C.c_uint32), ("mla", _MlaDims),
                 ("route_mode", C.c_int), ("expert_weight_scale", C.c_float), ("token_embd_quant", C.c_int),
                 ("token_embd", C.c_void_p), ("output_quant", C.c_int), ("output", C.c_void_p),
-                ("output_norm", C.c_void_p), ("layers", C.POINTER(_Ds2Layer))]
+                ("output_norm", C.c_void_p), ("layers", C.POINTER(_Ds2Layer)), ("n_kv_heads", C.c_uint32)]
 
 
 def _addr(d: dict, name: str):
@@ -543,6 +548,23 @@ def mla_attention(x, lw: dict, cfg, cache_layer: np.ndarray, pos: int):
     return rc, out
 
 
+def mha_attention(x, lw: dict, cfg, k_cache: np.ndarray, v_cache: np.ndarray, pos: int):
+    """mha_attention_single_token (mla.rs:449-618) for one MHA layer; the K / V
+    blocks ([max_tokens, n_kv * q_head], [max_tokens, n_kv * v_dim] f32) are
+    updated in place.  Returns (rc, out)."""
+    x = np.ascontiguousarray(x, np.float32)
+    for c in (k_cache, v_cache):
+        assert c.dtype == np.float32 and c.flags.c_contiguous
+    max_tokens = k_cache.shape[0]
+    dims = _mla_dims(cfg)
+    work = np.zeros(LIB.zo_mha_work_floats(C.byref(dims), cfg.kv_heads, max_tokens), np.float32)
+    out = np.zeros(cfg.hidden, np.float32)
+    rc = LIB.zo_mha_attention(_f(x), *(_b(lw[n]) for n in ("q_mha", "k_mha", "v_mha", "attn_output")),
+                              C.byref(dims), cfg.kv_heads, _f(k_cache), _f(v_cache), pos, max_tokens, _f(work),
+                              _f(out))
+    return rc, out
+
+
 class OracleDs2Run:
     """A DeepSeek2-shaped decode run on the CPU oracle (scalar crate order,
     forward_pass.rs:703-909), over synth.ds2_weights() tensors."""
@@ -560,6 +582,9 @@ class OracleDs2Run:
             ly.ffn_norm = _addr(lw, "ffn_norm")
             ly.mla = _mla_weights(lw)
             ly.moe = 1 if cfg.is_moe(i) else 0
+            if cfg.is_mha(i):
+                ly.mha = 1
+                ly.q_mha, ly.k_mha, ly.v_mha = (_addr(lw, n) for n in ("q_mha", "k_mha", "v_mha"))
             for n in ("ffn_gate", "ffn_up", "ffn_down", "router_w", "router_b", "gate_exps", "up_exps",
                       "down_exps", "gate_shexp", "up_shexp", "down_shexp"):
                 setattr(ly, n, _addr(lw, n))
@@ -567,7 +592,7 @@ class OracleDs2Run:
                        cfg.vocab_padded, cfg.vocab_real, _mla_dims(cfg), cfg.route_mode, cfg.expert_weight_scale,
                        Q8_0 if cfg.embd_quant == "q8_0" else Q4_0, weights["token_embd"].ctypes.data,
                        Q8_0 if cfg.output_quant == "q8_0" else Q4_0, weights["output"].ctypes.data,
-                       weights["output_norm"].ctypes.data, self._layers)
+                       weights["output_norm"].ctypes.data, self._layers, cfg.kv_heads)
         self._r = LIB.zo_ds2_run_create(C.byref(self._m), max_tokens)
         if not self._r:
             raise MemoryError("oracle ds2 run allocation failed")
@@ -592,6 +617,15 @@ class OracleDs2Run:
         tok = C.c_uint32(0)
         rc = LIB.zo_ds2_run_lm_head(self._r, C.byref(tok), _f(logits))
         return rc, tok.value, logits
+
+    def mha_cache(self):
+        """[(K [max_tokens, n_kv * q_head], V [max_tokens, n_kv * v_dim])] per MHA layer, in layer order."""
+        c = self.cfg
+        kb, vb = self.max_tokens * c.kv_heads * c.q_head, self.max_tokens * c.kv_heads * c.v_dim
+        n = len(c.mha_layers)
+        a = np.ctypeslib.as_array(LIB.zo_ds2_run_mha_cache(self._r), shape=(max(n, 1) * (kb + vb),)).copy()
+        return [(a[i * (kb + vb):i * (kb + vb) + kb].reshape(self.max_tokens, -1),
+                 a[i * (kb + vb) + kb:(i + 1) * (kb + vb)].reshape(self.max_tokens, -1)) for i in range(n)]
 
     def cache(self) -> np.ndarray:
         c = self.cfg

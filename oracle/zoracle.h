@@ -233,6 +233,9 @@ typedef struct zo_ds2_layer {
   const float   *router_w, *router_b;                     /* f32 [n_experts x hidden], bias nullable */
   const uint8_t *gate_exps, *up_exps, *down_exps;         /* stacked [n_experts][inter x hidden] ... */
   const uint8_t *gate_shexp, *up_shexp, *down_shexp;      /* stacked [n_shared][...] */
+  int            mha;                    /* AttnType::Mha: standard attention instead of mla */
+  const uint8_t *q_mha, *k_mha, *v_mha;  /* [n_heads*(nope+rope)], [n_kv*(nope+rope)], [n_kv*v] x hidden;
+                                            the output projection is mla.output */
 } zo_ds2_layer;
 
 typedef struct zo_ds2 {
@@ -247,7 +250,17 @@ typedef struct zo_ds2 {
   const uint8_t *output;       /* plain [vocab x hidden] */
   const float   *output_norm;
   const zo_ds2_layer *layers;
+  uint32_t n_kv_heads;         /* MHA layers' kv heads (0: n_heads) */
 } zo_ds2;
+
+/* mla.rs:449-618 (mha_attention_single_token): k_cache / v_cache are this
+ * MHA layer's K and V blocks ([max_tokens][n_kv * (nope + rope)] and
+ * [max_tokens][n_kv * v], kv_cache.rs:433-560 MhaKvCache); work:
+ * zo_mha_work_floats floats. */
+size_t zo_mha_work_floats(const zo_mla_dims *d, uint32_t n_kv, uint32_t max_tokens);
+int zo_mha_attention(const float *x, const uint8_t *wq, const uint8_t *wk, const uint8_t *wv,
+                     const uint8_t *wo, const zo_mla_dims *d, uint32_t n_kv, float *k_cache,
+                     float *v_cache, uint32_t pos, uint32_t max_tokens, float *work, float *out);
 
 typedef struct zo_ds2_run zo_ds2_run;
 zo_ds2_run *zo_ds2_run_create(const zo_ds2 *m, uint32_t max_tokens);
@@ -259,6 +272,8 @@ int     zo_ds2_run_generate(zo_ds2_run *r, const uint32_t *prompt, uint32_t n_pr
                             uint32_t n_gen, uint32_t *tokens_out, float *margins_out,
                             float *logits_all);
 const float    *zo_ds2_run_cache(const zo_ds2_run *r);
+/* The MHA layers' cache: per MHA layer (in layer order) the K block then the V block. */
+const float    *zo_ds2_run_mha_cache(const zo_ds2_run *r);
 /* [n_layers][top_k] expert ids / weights chosen by the last forward (0 for dense layers). */
 const uint32_t *zo_ds2_run_expert_ids(const zo_ds2_run *r);
 const float    *zo_ds2_run_expert_weights(const zo_ds2_run *r);

@@ -290,6 +290,60 @@ int zo_mla_attention(const float *x, const zo_mla_weights *w, const zo_mla_dims 
   return zo_linear_dispatch(concat, w->output, out, v_out, H, quant);
 }
 
+size_t zo_mha_work_floats(const zo_mla_dims *d, uint32_t n_kv, uint32_t max_tokens) {
+  size_t hq = d->nope_dim + d->rope_dim;
+  return (size_t)d->n_heads * hq + (size_t)n_kv * hq + (size_t)n_kv * d->v_dim +
+         (size_t)d->n_heads * max_tokens + (size_t)d->n_heads * d->v_dim;
+}
+
+/* mla.rs:449-618 (mha_attention_single_token):
+ *   q = W_q . x, k = W_k . x, v = W_v . x (head width nope + rope for q / k);
+ *   RoPE (mla_rope above) on the rope part of every q head and k head;
+ *   store k, v at pos (MhaKvCache::store_kv, kv_cache.rs:487-531);
+ *   per q head h (kv head h / (n_heads / n_kv)): scores over [0, pos] as the
+ *   sequential dot q . k_t times 1 / sqrtf(nope + rope), softmax
+ *   (attention.rs:48), concat_h = sum_t p_t v_t in token order;
+ *   out = W_o . concat. */
+int zo_mha_attention(const float *x, const uint8_t *wq, const uint8_t *wk, const uint8_t *wv,
+                     const uint8_t *wo, const zo_mla_dims *d, uint32_t n_kv, float *k_cache,
+                     float *v_cache, uint32_t pos, uint32_t max_tokens, float *work, float *out) {
+  const size_t H = d->hidden, NH = d->n_heads, NO = d->nope_dim, RD = d->rope_dim, VD = d->v_dim;
+  const size_t hq = NO + RD, q_out = NH * hq, k_out = (size_t)n_kv * hq, v_out = (size_t)n_kv * VD;
+  const size_t total = (size_t)pos + 1, G = n_kv ? NH / n_kv : 1;
+  const int quant = d->quant;
+  int st;
+  if (pos >= max_tokens) return ZO_ERR_KV_TOKEN_OUT_OF_RANGE;
+  float *q = work, *k = q + q_out, *v = k + k_out, *score = v + v_out, *concat = score + NH * max_tokens;
+  if ((st = zo_linear_dispatch(x, wq, q, H, q_out, quant))) return st;
+  if ((st = zo_linear_dispatch(x, wk, k, H, k_out, quant))) return st;
+  if ((st = zo_linear_dispatch(x, wv, v, H, v_out, quant))) return st;
+  for (size_t h = 0; h < NH; ++h) mla_rope(q + h * hq + NO, RD, pos, d->rope_base);
+  for (size_t h = 0; h < n_kv; ++h) mla_rope(k + h * hq + NO, RD, pos, d->rope_base);
+  memcpy(k_cache + (size_t)pos * k_out, k, k_out * sizeof(float));
+  memcpy(v_cache + (size_t)pos * v_out, v, v_out * sizeof(float));
+  const float scale = 1.0f / sqrtf((float)hq);
+  for (size_t qh = 0; qh < NH; ++qh) {
+    const size_t kvh = G ? qh / G : 0;
+    const float *qv = q + qh * hq;
+    float *sc = score + qh * max_tokens;
+    for (size_t t = 0; t < total; ++t) {
+      const float *kt = k_cache + t * k_out + kvh * hq;
+      float dot = 0.0f;
+      for (size_t i = 0; i < hq; ++i) dot += qv[i] * kt[i];
+      sc[t] = dot * scale;
+    }
+    if (zo_softmax(sc, total)) return ZO_ERR_NUMERICAL_INSTABILITY;
+    float *o = concat + qh * VD;
+    memset(o, 0, VD * sizeof(float));
+    for (size_t t = 0; t < total; ++t) {
+      const float *vt = v_cache + t * v_out + kvh * VD;
+      const float w = sc[t];
+      for (size_t i = 0; i < VD; ++i) o[i] += w * vt[i];
+    }
+  }
+  return zo_linear_dispatch(concat, wo, out, NH * VD, H, quant);
+}
+
 /* ======================================================================
  * DeepSeek2 decode step (forward_pass.rs:703-909) + LM head (lm_head.rs:98)
  * ====================================================================== */
@@ -300,6 +354,10 @@ struct zo_ds2_run {
   float *cache;          /* [L][max_tokens][kv_lora | rope] */
   float *hidden, *norm, *attn_out, *mlp_out, *logits;
   float *mla_work, *ffn_work;
+  float *mha_cache;      /* per MHA layer: K block [max_tokens][n_kv*hq] | V block [max_tokens][n_kv*v] */
+  float *mha_work;
+  uint32_t n_kv;
+  size_t mha_k_block, mha_v_block;
   uint32_t *ids;         /* [L][top_k] experts of the last forward (0 for dense layers) */
   float *wts;            /* [L][top_k] */
 };
@@ -322,8 +380,17 @@ zo_ds2_run *zo_ds2_run_create(const zo_ds2 *m, uint32_t max_tokens) {
   r->ffn_work = calloc(m->n_experts + 3 * inter + H, 4);
   r->ids = calloc((size_t)m->n_layers * (m->top_k ? m->top_k : 1), 4);
   r->wts = calloc((size_t)m->n_layers * (m->top_k ? m->top_k : 1), 4);
+  {
+    size_t n_mha = 0;
+    for (uint32_t li = 0; li < m->n_layers; ++li) n_mha += m->layers[li].mha ? 1 : 0;
+    r->n_kv = m->n_kv_heads ? m->n_kv_heads : d->n_heads;
+    r->mha_k_block = (size_t)max_tokens * r->n_kv * (d->nope_dim + d->rope_dim);
+    r->mha_v_block = (size_t)max_tokens * r->n_kv * d->v_dim;
+    r->mha_cache = calloc(n_mha ? n_mha * (r->mha_k_block + r->mha_v_block) : 1, 4);
+    r->mha_work = calloc(zo_mha_work_floats(d, r->n_kv, max_tokens), 4);
+  }
   if (!r->cache || !r->hidden || !r->norm || !r->attn_out || !r->mlp_out || !r->logits ||
-      !r->mla_work || !r->ffn_work || !r->ids || !r->wts) {
+      !r->mla_work || !r->ffn_work || !r->ids || !r->wts || !r->mha_cache || !r->mha_work) {
     zo_ds2_run_destroy(r);
     return NULL;
   }
@@ -334,17 +401,20 @@ void zo_ds2_run_destroy(zo_ds2_run *r) {
   if (!r) return;
   free(r->cache); free(r->hidden); free(r->norm); free(r->attn_out); free(r->mlp_out);
   free(r->logits); free(r->mla_work); free(r->ffn_work); free(r->ids); free(r->wts);
+  free(r->mha_cache); free(r->mha_work);
   free(r);
 }
 
 const float *zo_ds2_run_cache(const zo_ds2_run *r) { return r->cache; }
+const float *zo_ds2_run_mha_cache(const zo_ds2_run *r) { return r->mha_cache; }
 const uint32_t *zo_ds2_run_expert_ids(const zo_ds2_run *r) { return r->ids; }
 const float *zo_ds2_run_expert_weights(const zo_ds2_run *r) { return r->wts; }
 
 /* forward_pass.rs:703-909 (forward_single_token_deepseek2): embed, then per
  * layer rmsnorm -> MLA -> hidden += attn_out -> rmsnorm -> dense SwiGLU
  * (forward_pass.rs:459-508) or moe_ffn over a zeroed mlp_out -> hidden +=
- * mlp_out.  MLA layers only (the MHA variant is not part of this model). */
+ * mlp_out.  A layer flagged mha runs mha_attention_single_token on its slot
+ * of the MHA cache (the n-th MHA layer takes slot n, as mha_layer_idx). */
 int zo_ds2_run_forward(zo_ds2_run *r, uint32_t token, uint32_t pos, float *hidden_out) {
   const zo_ds2 *m = r->m;
   const zo_mla_dims *d = &m->mla;
@@ -364,13 +434,22 @@ int zo_ds2_run_forward(zo_ds2_run *r, uint32_t token, uint32_t pos, float *hidde
     }
   }
   int st;
+  size_t mha_slot = 0;
   for (uint32_t li = 0; li < m->n_layers; ++li) {
     const zo_ds2_layer *L = &m->layers[li];
     zo_rmsnorm(r->hidden, L->attn_norm, r->norm, H, d->eps);
-    float *cl = r->cache + (size_t)li * r->max_tokens * tstride;
-    if ((st = zo_mla_attention(r->norm, &L->mla, d, cl, pos, r->max_tokens, r->mla_work,
-                               r->attn_out)))
-      return st;
+    if (L->mha) {
+      float *kc = r->mha_cache + mha_slot * (r->mha_k_block + r->mha_v_block), *vc = kc + r->mha_k_block;
+      ++mha_slot;
+      if ((st = zo_mha_attention(r->norm, L->q_mha, L->k_mha, L->v_mha, L->mla.output, d, r->n_kv, kc, vc,
+                                 pos, r->max_tokens, r->mha_work, r->attn_out)))
+        return st;
+    } else {
+      float *cl = r->cache + (size_t)li * r->max_tokens * tstride;
+      if ((st = zo_mla_attention(r->norm, &L->mla, d, cl, pos, r->max_tokens, r->mla_work,
+                                 r->attn_out)))
+        return st;
+    }
     for (size_t i = 0; i < H; ++i) r->hidden[i] += r->attn_out[i];
     zo_rmsnorm(r->hidden, L->ffn_norm, r->norm, H, d->eps);
     if (!L->moe) {

@@ -294,6 +294,101 @@ def test_mla_errors():
     assert O.mla_attention(bad, lw, cfg, cache, 0)[0] == 20      # NumericalInstability
 
 
+# ------------------------------------------- MHA layers against float64
+
+
+def mha64(x, lw, cfg, k64, v64, pos):
+    """mla.rs:449-618 in float64."""
+    H, NH, NKV, NO, RD, VD = cfg.hidden, cfg.n_heads, cfg.kv_heads, cfg.nope_dim, cfg.rope_dim, cfg.v_dim
+    hq = NO + RD
+    x = x.astype(np.float64)
+    q = (deq_q4_0(lw["q_mha"], NH * hq, H) @ x).reshape(NH, hq)
+    k = (deq_q4_0(lw["k_mha"], NKV * hq, H) @ x).reshape(NKV, hq)
+    v = deq_q4_0(lw["v_mha"], NKV * VD, H) @ x
+    for h in range(NH):
+        q[h, NO:] = rope64(q[h, NO:], pos, cfg.rope_theta)
+    for h in range(NKV):
+        k[h, NO:] = rope64(k[h, NO:], pos, cfg.rope_theta)
+    k64[pos], v64[pos] = k.ravel(), v
+    out = np.zeros(NH * VD)
+    G = NH // NKV
+    for h in range(NH):
+        kv = h // G
+        K = k64[:pos + 1, kv * hq:(kv + 1) * hq]
+        Vv = v64[:pos + 1, kv * VD:(kv + 1) * VD]
+        s = K @ q[h] / np.sqrt(hq)
+        p = np.exp(s - s.max())
+        out[h * VD:(h + 1) * VD] = Vv.T @ (p / p.sum())
+    return deq_q4_0(lw["attn_output"], H, NH * VD) @ out
+
+
+@pytest.mark.parametrize("n_kv", [2, 1])
+def test_mha_against_float64(n_kv):
+    cfg = small_cfg(mha_layers=(0,), n_kv_heads=n_kv)
+    w = synth.ds2_weights(cfg, seed=16, norm_sigma=0.1)
+    lw = w["layers"][0]
+    T = 12
+    kc = np.zeros((T, cfg.kv_heads * cfg.q_head), np.float32)
+    vc = np.zeros((T, cfg.kv_heads * cfg.v_dim), np.float32)
+    k64, v64 = np.zeros(kc.shape), np.zeros(vc.shape)
+    for pos in range(T):
+        x = synth.f32(16, 300 + pos, cfg.hidden, 0.0, 1.0)
+        rc, out = O.mha_attention(x, lw, cfg, kc, vc, pos)
+        assert rc == 0
+        ref = mha64(x, lw, cfg, k64, v64, pos)
+        assert rel_l2(out, ref) < 2e-5, pos
+        assert rel_l2(kc[:pos + 1], k64[:pos + 1]) < 1e-6 and rel_l2(vc[:pos + 1], v64[:pos + 1]) < 1e-6
+
+
+def test_mha_errors():
+    cfg = small_cfg(mha_layers=(0,))
+    w = synth.ds2_weights(cfg, seed=17)
+    lw = w["layers"][0]
+    kc = np.zeros((4, cfg.kv_heads * cfg.q_head), np.float32)
+    vc = np.zeros((4, cfg.kv_heads * cfg.v_dim), np.float32)
+    x = synth.f32(17, 1, cfg.hidden, 0.0, 1.0)
+    assert O.mha_attention(x, lw, cfg, kc, vc, 4)[0] == 10      # TokenIndexOutOfRange
+    bad = x.copy()
+    bad[3] = np.inf
+    assert O.mha_attention(bad, lw, cfg, kc, vc, 0)[0] == 20    # NumericalInstability
+
+
+def test_ds2_forward_with_an_mha_layer():
+    """Layer 0 as standard attention (AttnType::Mha) inside the step: the run
+    equals the per-layer restatements composed on the residual stream."""
+    cfg = small_cfg(mha_layers=(0,), n_kv_heads=1)
+    w = synth.ds2_weights(cfg, seed=18, norm_sigma=0.1)
+    r = O.OracleDs2Run(cfg, w, 8)
+    H = cfg.hidden
+    kc = np.zeros((8, cfg.kv_heads * cfg.q_head), np.float32)
+    vc = np.zeros((8, cfg.kv_heads * cfg.v_dim), np.float32)
+    cache = np.zeros((cfg.n_layers, 8, cfg.kv_lora_rank + cfg.rope_dim), np.float32)
+    for pos, tok in enumerate([5, 9, 2]):
+        hidden = r.forward(tok, pos)
+        emb = w["token_embd"].reshape(cfg.vocab_padded, H // 32, 34)[tok]
+        h = (emb[:, 2:].view(np.int8).astype(np.float32) * emb[:, :2].copy().view(np.float16).astype(np.float32))
+        h = h.ravel().astype(np.float32)
+        for li, lw in enumerate(w["layers"]):
+            x = O.rmsnorm(h, lw["attn_norm"], cfg.rms_eps)
+            rc, a = (O.mha_attention(x, lw, cfg, kc, vc, pos) if li == 0
+                     else O.mla_attention(x, lw, cfg, cache[li], pos))
+            assert rc == 0
+            h = (h + a).astype(np.float32)
+            x = O.rmsnorm(h, lw["ffn_norm"], cfg.rms_eps)
+            if cfg.is_moe(li):
+                rc, m, _, _ = O.moe_ffn(x, lw, cfg)
+                assert rc == 0
+            else:
+                g = O.linear(x, lw["ffn_gate"], H, cfg.ffn, O.Q4_0)
+                u = O.linear(x, lw["ffn_up"], H, cfg.ffn, O.Q4_0)
+                g = (g / (np.float32(1) + np.exp(-g))).astype(np.float32)
+                m = O.linear((g * u).astype(np.float32), lw["ffn_down"], cfg.ffn, H, O.Q4_0)
+            h = (h + m).astype(np.float32)
+        assert rel_l2(hidden, h) < 1e-6
+    k_run, v_run = r.mha_cache()[0]
+    assert np.array_equal(k_run[:3], kc[:3]) and np.array_equal(v_run[:3], vc[:3])
+
+
 # ------------------------------------------- the DeepSeek2 step
 
 
