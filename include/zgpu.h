@@ -439,7 +439,15 @@ typedef struct zgpu_ds2_layer {
   const float *router_b;
   const void *gate_exps, *up_exps, *down_exps;
   const void *gate_shexp, *up_shexp, *down_shexp;
+  /* AttnType (forward_pass.rs:51-57): ZGPU_ATTN_MLA, or ZGPU_ATTN_MHA for a
+   * layer with standard attention (mla.rs:449-618): q_mha [n_heads*(nope+rope)
+   * x hidden], k_mha [n_kv*(nope+rope) x hidden], v_mha [n_kv*v x hidden] and
+   * attn_output; the MLA tensors and norms are then unused (may be NULL). */
+  uint32_t attn_type;
+  const void *q_mha, *k_mha, *v_mha;
 } zgpu_ds2_layer;
+#define ZGPU_ATTN_MLA 0u
+#define ZGPU_ATTN_MHA 1u
 
 typedef struct zgpu_ds2_desc {
   uint32_t n_layers, hidden, ffn, n_heads;
@@ -456,9 +464,27 @@ typedef struct zgpu_ds2_desc {
   const void *output;
   const float *output_norm;
   const zgpu_ds2_layer *layers;
+  uint32_t n_kv_heads;           /* kv heads of the MHA layers (0: n_heads) */
 } zgpu_ds2_desc;
 
 zgpu_status zgpu_ds2_create(zgpu_ctx *ctx, const zgpu_ds2_desc *desc, zgpu_ds2_model **out);
+
+/* MhaKvCache (kv_cache.rs:433-560) in device memory, same layout: per MHA
+ * layer a K block [max_tokens][n_kv*head_dim_qk] then a V block
+ * [max_tokens][n_kv*head_dim_v].  store_kv / get_k_slice + get_v_slice as
+ * zgpu_mha_kv_store / zgpu_mha_kv_read (host buffers). */
+typedef struct zgpu_mha_kv zgpu_mha_kv;
+zgpu_status zgpu_mha_kv_create(zgpu_ctx *ctx, uint32_t max_tokens, uint32_t n_mha_layers, uint32_t n_kv_heads,
+                               uint32_t head_dim_qk, uint32_t head_dim_v, zgpu_mha_kv **out);
+void zgpu_mha_kv_destroy(zgpu_mha_kv *kv);
+zgpu_status zgpu_mha_kv_store(zgpu_mha_kv *kv, uint32_t layer, uint32_t token, const float *k, const float *v);
+zgpu_status zgpu_mha_kv_read(zgpu_mha_kv *kv, uint32_t layer, uint32_t token_count, float *k_out, float *v_out);
+/* The MHA cache the model's MHA layers use (forward_single_token_deepseek2's
+ * mha_kv_cache argument, forward_pass.rs:730): the n-th MHA layer uses slot n.
+ * Required before a forward when the model has MHA layers (without it the
+ * forward returns ZGPU_ERR_NUMERICAL_INSTABILITY, as the reference's
+ * forward_pass.rs:791-793); NULL unbinds. */
+zgpu_status zgpu_ds2_set_mha_kv(zgpu_ds2_model *m, zgpu_mha_kv *kv);
 void zgpu_ds2_destroy(zgpu_ds2_model *m);
 /* Expert parallelism (experts sharded over 1-8 GPUs, one
  * process per GPU).  Rank `rank` of `world` runs routed experts

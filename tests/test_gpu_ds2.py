@@ -224,3 +224,84 @@ def test_ds2_full_width_layers():
     assert np.array_equal(ids[1], rid[1])
     m.close()
     ctx.close()
+
+
+# ------------------------------------------ layers with standard attention (AttnType::Mha)
+
+MHA_VARIANTS = {
+    # layer 0 as standard attention, as the builds that ship attn_q / attn_k / attn_v for it
+    "mha_layer0": synth.ds2_small_config(**BASE, mha_layers=(0,)),
+    # two MHA layers around an MLA layer, GQA 2, split k_b / v_b on the MLA layer
+    "mha_gqa2_split": synth.ds2_small_config(**BASE, mha_layers=(0, 2), n_kv_heads=2, split_kv_b=True),
+}
+
+
+@pytest.mark.parametrize("name", list(MHA_VARIANTS))
+def test_ds2_mha_layers_match_oracle(name):
+    """mha_attention_single_token (mla.rs:449-618) inside the step: greedy
+    tokens identical to the oracle's, logits and both caches within 1e-4."""
+    cfg = MHA_VARIANTS[name]
+    ctx, w, m = build(cfg, seed=34)
+    prompt = synth.ds2_prompt_ids(cfg, 7, seed=34)
+    n_gen = 8
+    kv = m.new_kv(40)
+    mkv = m.new_mha_kv(40)
+    toks, logits = m.generate_greedy(kv, prompt, n_gen, want_logits=True)
+    r = O.OracleDs2Run(cfg, w, 40)
+    rc, ref_t, margins, ref_l = r.generate(prompt, n_gen, want_logits=True)
+    assert rc == 0
+    assert np.array_equal(toks, ref_t), (toks, ref_t, margins)
+    for s in range(n_gen):
+        assert rel_l2(logits[s], ref_l[s]) < 1e-4, s
+    used = len(prompt) + n_gen - 1
+    ref_cache = r.cache()
+    for layer in range(cfg.n_layers):
+        if not cfg.is_mha(layer):
+            assert rel_l2(kv.read(layer, used), ref_cache[layer, :used]) < 1e-4, layer
+    for slot, (rk, rv) in enumerate(r.mha_cache()):
+        k, v = mkv.read(slot, used)
+        assert rel_l2(k, rk[:used]) < 1e-4 and rel_l2(v, rv[:used]) < 1e-4, slot
+    # the graph replays and the eager launches agree bit for bit
+    ctx2 = zb.Context(graph=False)
+    m2 = zb.Ds2Model(ctx2, cfg, w)
+    kv2 = m2.new_kv(40)
+    mkv2 = m2.new_mha_kv(40)
+    t2, l2 = m2.generate_greedy(kv2, prompt, n_gen, want_logits=True)
+    assert np.array_equal(t2, toks) and np.array_equal(l2.view(np.uint32), logits.view(np.uint32))
+    for c in (kv2, mkv2):
+        c.close()
+    m2.close()
+    ctx2.close()
+    for c in (kv, mkv):
+        c.close()
+    m.close()
+    ctx.close()
+
+
+def test_ds2_mha_cache_errors():
+    cfg = MHA_VARIANTS["mha_layer0"]
+    ctx, w, m = build(cfg, seed=35)
+    kv = m.new_kv(16)
+    with pytest.raises(zb.ZgpuError) as ei:                 # forward_pass.rs:791-793: no MHA cache
+        m.forward_single_token(kv, 1, 0)
+    assert ei.value.name == "NUMERICAL_INSTABILITY"
+    bad = zb.MhaKvCache(ctx, 16, 2, cfg.kv_heads, cfg.q_head, cfg.v_dim)   # two slots, one MHA layer
+    with pytest.raises(zb.ZgpuError) as ei:
+        m.set_mha_kv(bad)
+    assert ei.value.name == "KV_LAYER_OUT_OF_RANGE"
+    small = m.new_mha_kv(4)                                  # shorter than the MLA cache
+    for pos in range(4):
+        m.forward_single_token(kv, 1 + pos, pos)
+    with pytest.raises(zb.ZgpuError) as ei:
+        m.forward_single_token(kv, 7, 4)
+    assert ei.value.name == "KV_TOKEN_OUT_OF_RANGE"
+    # store / read round trip of the cache API
+    k = np.arange(small.k_width, dtype=np.float32)
+    v = -np.arange(small.v_width, dtype=np.float32)
+    small.store(0, 3, k, v)
+    rk, rv = small.read(0, 4)
+    assert np.array_equal(rk[3], k) and np.array_equal(rv[3], v)
+    for c in (kv, bad, small):
+        c.close()
+    m.close()
+    ctx.close()

@@ -449,6 +449,37 @@ class MlaKvCache:
         return out
 
 
+class MhaKvCache:
+    """MhaKvCache (kv_cache.rs:433-560) in device memory: per MHA layer a K
+    block [max_tokens, n_kv * head_dim_qk] and a V block [max_tokens, n_kv * head_dim_v]."""
+
+    def __init__(self, ctx: Context, max_tokens: int, n_mha_layers: int, n_kv_heads: int, head_dim_qk: int,
+                 head_dim_v: int):
+        self.ctx = ctx
+        self.max_tokens, self.n_layers = max_tokens, n_mha_layers
+        self.k_width, self.v_width = n_kv_heads * head_dim_qk, n_kv_heads * head_dim_v
+        h = C.c_void_p()
+        ctx._check(LIB.zgpu_mha_kv_create(ctx.h, max_tokens, n_mha_layers, n_kv_heads, head_dim_qk, head_dim_v,
+                                          C.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            LIB.zgpu_mha_kv_destroy(self.h)
+            self.h = None
+
+    def store(self, layer: int, token: int, k: np.ndarray, v: np.ndarray):
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        self.ctx._check(LIB.zgpu_mha_kv_store(self.h, layer, token, _ptr(k), _ptr(v)))
+
+    def read(self, layer: int, token_count: int):
+        k = np.empty((token_count, self.k_width), np.float32)
+        v = np.empty((token_count, self.v_width), np.float32)
+        self.ctx._check(LIB.zgpu_mha_kv_read(self.h, layer, token_count, _ptr(k), _ptr(v)))
+        return k, v
+
+
 class Ds2Model:
     """A DeepSeek2-shaped (MLA + MoE) model on the device, built from
     synth.ds2_weights() tensors (plain Q4_0 blocks; routers registered f32)."""
@@ -475,12 +506,14 @@ class Ds2Model:
             if cfg.is_moe(i):
                 L.moe = 1
                 L.router_w = ctx.register(lw["router_w"], F32, cfg.n_experts, H)
+            if cfg.is_mha(i):
+                L.attn_type = 1   # ZGPU_ATTN_MHA
         desc = ZgpuDs2Desc(
             cfg.n_layers, H, cfg.ffn, cfg.n_heads, cfg.kv_lora_rank, cfg.q_lora_rank, cfg.nope_dim,
             cfg.rope_dim, cfg.v_dim, cfg.n_experts, cfg.top_k, cfg.expert_ffn, cfg.n_shared,
             cfg.vocab_padded, cfg.vocab_real, cfg.rms_eps, cfg.rope_theta, cfg.route_mode,
             cfg.expert_weight_scale, Q4_0, eq, emb_key, oq, out_key, _ptr(weights["output_norm"]),
-            self._layers)
+            self._layers, cfg.n_kv_heads)
         h = C.c_void_p()
         if world == 1:
             ctx._check(LIB.zgpu_ds2_create(ctx.h, C.byref(desc), C.byref(h)))
@@ -509,6 +542,18 @@ class Ds2Model:
     def new_kv(self, max_tokens: int) -> MlaKvCache:
         c = self.cfg
         return MlaKvCache(self.ctx, max_tokens, c.n_layers, c.kv_lora_rank, c.rope_dim)
+
+    def new_mha_kv(self, max_tokens: int, bind: bool = True) -> MhaKvCache:
+        """A cache for the model's MHA layers (zgpu_mha_kv_create), bound to the
+        model (zgpu_ds2_set_mha_kv) unless bind is False."""
+        c = self.cfg
+        kv = MhaKvCache(self.ctx, max_tokens, len(c.mha_layers), c.kv_heads, c.q_head, c.v_dim)
+        if bind:
+            self.set_mha_kv(kv)
+        return kv
+
+    def set_mha_kv(self, kv) -> None:
+        self.ctx._check(LIB.zgpu_ds2_set_mha_kv(self.h, kv.h if kv is not None else None))
 
     def forward_single_token(self, kv: MlaKvCache, token: int, pos: int) -> np.ndarray:
         hidden = np.empty(self.cfg.hidden, np.float32)
@@ -548,5 +593,5 @@ class Ds2Model:
 
 
 __all__ = ["Context", "KvCache", "Qwen3Model", "Qwen3Config", "QWEN3_1_7B", "ZgpuError", "synth",
-           "MlaKvCache", "Ds2Model", "Ds2Config", "DS2_V2_LITE", "ROUTE_SOFTMAX", "ROUTE_SIGMOID_NORMALIZE",
+           "MlaKvCache", "MhaKvCache", "Ds2Model", "Ds2Config", "DS2_V2_LITE", "ROUTE_SOFTMAX", "ROUTE_SIGMOID_NORMALIZE",
            "F32", "Q4_0", "Q8_0", "Q4_0X4", "Q8_0X4", "Q4_K", "Q6_K"]

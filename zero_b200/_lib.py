@@ -48,6 +48,7 @@ class ZgpuDs2Layer(C.Structure):
         ("k_norm", _vp), ("moe", _u32), ("ffn_gate", _vp), ("ffn_up", _vp), ("ffn_down", _vp),
         ("router_w", _vp), ("router_b", _vp), ("gate_exps", _vp), ("up_exps", _vp), ("down_exps", _vp),
         ("gate_shexp", _vp), ("up_shexp", _vp), ("down_shexp", _vp),
+        ("attn_type", _u32), ("q_mha", _vp), ("k_mha", _vp), ("v_mha", _vp),
     ]
 
 
@@ -59,7 +60,7 @@ class ZgpuDs2Desc(C.Structure):
         ("vocab_padded", _u32), ("vocab_real", _u32), ("rms_eps", _f), ("rope_theta", _f),
         ("route_mode", _u32), ("expert_weight_scale", _f), ("attn_quant", _u32),
         ("token_embd_quant", _u32), ("token_embd", _vp), ("output_quant", _u32), ("output", _vp),
-        ("output_norm", _vp), ("layers", C.POINTER(ZgpuDs2Layer)),
+        ("output_norm", _vp), ("layers", C.POINTER(ZgpuDs2Layer)), ("n_kv_heads", _u32),
     ]
 
 
@@ -143,6 +144,11 @@ _SIGS = {
     "zgpu_prefill": (_i32, [_vp, _vp, _vp, _u32, _vp, _vp]),
     "zgpu_moe_route_f32": (_i32, [_vp, _vp, _vp, _vp, _u64, _u32, _u32, _u32, _f, _vp, _vp, _vp]),
     "zgpu_mla_kv_create": (_i32, [_vp, _u32, _u32, _u32, _u32, C.POINTER(_vp)]),
+    "zgpu_mha_kv_create": (_i32, [_vp, _u32, _u32, _u32, _u32, _u32, C.POINTER(_vp)]),
+    "zgpu_mha_kv_destroy": (None, [_vp]),
+    "zgpu_mha_kv_store": (_i32, [_vp, _u32, _u32, _vp, _vp]),
+    "zgpu_mha_kv_read": (_i32, [_vp, _u32, _u32, _vp, _vp]),
+    "zgpu_ds2_set_mha_kv": (_i32, [_vp, _vp]),
     "zgpu_mla_kv_destroy": (None, [_vp]),
     "zgpu_mla_kv_store": (_i32, [_vp, _u32, _u32, _vp, _vp]),
     "zgpu_mla_kv_read": (_i32, [_vp, _u32, _u32, _vp]),

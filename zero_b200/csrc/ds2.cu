@@ -45,6 +45,15 @@ struct zgpu_mla_kv {
   uint64_t layer_floats = 0;   // max_tokens * (kv_lora + rope)
 };
 
+// MhaKvCache (kv_cache.rs:433-560): per MHA layer a K block
+// [max_tokens][n_kv * head_dim_qk] then a V block [max_tokens][n_kv * head_dim_v].
+struct zgpu_mha_kv {
+  zgpu_ctx *ctx = nullptr;
+  float *d = nullptr;
+  uint32_t max_tokens = 0, n_layers = 0, n_kv = 0, hd_qk = 0, hd_v = 0;
+  uint64_t k_block = 0, v_block = 0;   // floats
+};
+
 namespace {
 
 constexpr uint32_t kMaxEpRanks = 8;
@@ -66,6 +75,10 @@ struct Ds2Layer {
   const DeviceTensor *down = nullptr, *sh_down = nullptr, *router = nullptr;
   float *d_router_b = nullptr;       // owned (nullable)
   unsigned long long *d_seg_gu = nullptr, *d_seg_dn = nullptr;   // owned [n_shared + top_k]
+  // standard attention (AttnType::Mha): fused q|k|v group streams, slot in the MHA cache
+  uint32_t mha = 0, mha_idx = 0;
+  uint8_t *cat_qkv = nullptr;        // owned
+  uint32_t qkv_groups = 0;
   // norms (views into the model's norm block)
   const float *attn_norm = nullptr, *ffn_norm = nullptr, *kv_a_norm = nullptr, *q_a_norm = nullptr,
               *k_norm = nullptr;
@@ -109,6 +122,11 @@ struct zgpu_ds2_model {
   unsigned long long **d_ep_dst = nullptr;  // [world] every rank's exchange buffer
   std::vector<void *> ipc_opened;
   bool ep_connected = false;
+  // MHA layers: their count, kv heads, the bound cache and the attention scratch
+  uint32_t n_mha = 0, n_kv = 0;
+  zgpu_mha_kv *mha_kv = nullptr;
+  float *d_mha_qkv = nullptr, *d_mha_part = nullptr;
+  uint32_t mha_splits = 0;
 };
 
 namespace {
@@ -146,6 +164,43 @@ cudaError_t ds2_enqueue_forward(zgpu_ds2_model *m, zgpu_mla_kv *kv, uint32_t *co
     const Ds2Layer &L = m->layers[l];
     GemvDesc g;
     GemvIo io;
+    if (L.mha) {
+      // standard attention (mla.rs:449-618): RMSNorm + fused q|k|v, RoPE and
+      // cache append, attention into the head concat
+      const uint32_t hqk = d.nope_dim + d.rope_dim;
+      g.w = L.cat_qkv;
+      g.gstride = m->gs_h;
+      g.wbytes = static_cast<uint64_t>(L.qkv_groups) * m->gs_h;
+      g.quant = d.attn_quant;
+      g.rows = NH * hqk + m->n_kv * (hqk + d.v_dim);
+      g.groups = L.qkv_groups;
+      g.in_dim = H;
+      io.x = m->d_hidden;
+      io.norm_w = L.attn_norm;
+      io.eps = d.rms_eps;
+      io.out = m->d_mha_qkv;
+      io.status = m->d_status;
+      if ((e = launch_gemv(g, PRO_RMSNORM, EPI_STORE, io, lc)) != cudaSuccess) return e;
+      MhaParams hp = {};
+      hp.qkv = m->d_mha_qkv;
+      hp.inv_freqs = m->d_inv_freqs;
+      hp.k_cache = m->mha_kv->d + static_cast<size_t>(L.mha_idx) * (m->mha_kv->k_block + m->mha_kv->v_block);
+      hp.v_cache = hp.k_cache + m->mha_kv->k_block;
+      hp.max_tokens = m->mha_kv->max_tokens;
+      hp.pos_ptr = &m->d_state->pos;
+      hp.part = m->d_mha_part;
+      hp.out = m->d_concat;
+      hp.status = m->d_status;
+      hp.n_heads = NH;
+      hp.n_kv = m->n_kv;
+      hp.nope = d.nope_dim;
+      hp.rope = d.rope_dim;
+      hp.v = d.v_dim;
+      hp.max_splits = m->mha_splits;
+      hp.scale = 1.0f / sqrtf(static_cast<float>(hqk));
+      if ((e = launch_mha_prep(hp, lc)) != cudaSuccess) return e;
+      if ((e = launch_mha_attention(hp, lc)) != cudaSuccess) return e;
+    } else {
     // RMSNorm + fused kv_a_mqa | q_a
     g.w = L.cat_a;
     g.gstride = m->gs_h;
@@ -221,6 +276,7 @@ cudaError_t ds2_enqueue_forward(zgpu_ds2_model *m, zgpu_mla_kv *kv, uint32_t *co
     io.out = m->d_concat;
     io.status = m->d_status;
     if ((e = launch_gemv(g, PRO_PLAIN, EPI_STORE, io, lc)) != cudaSuccess) return e;
+    }
     // O projection + residual
     g = GemvDesc();
     g.w = L.o->d;
@@ -480,6 +536,9 @@ zgpu_status ds2_prepare_kv(zgpu_ds2_model *m, zgpu_mla_kv *kv) {
     m->max_splits = splits;
     ds2_drop_graphs(m);
   }
+  // forward_pass.rs:790-793: an MHA layer without its cache is an error
+  if (m->n_mha && !m->mha_kv)
+    return zgpu_fail(ctx, ZGPU_ERR_NUMERICAL_INSTABILITY, "model has MHA layers: bind a cache with zgpu_ds2_set_mha_kv");
   return ZGPU_OK;
 }
 
@@ -628,6 +687,92 @@ zgpu_status zgpu_moe_route_f32(zgpu_ctx *ctx, const float *hidden, const void *r
   return zgpu_map_device_status(ctx, st);
 }
 
+// ------------------------------------------------------------ MHA cache
+
+zgpu_status zgpu_mha_kv_create(zgpu_ctx *ctx, uint32_t max_tokens, uint32_t n_mha_layers, uint32_t n_kv_heads,
+                               uint32_t head_dim_qk, uint32_t head_dim_v, zgpu_mha_kv **out) {
+  if (!ctx || !out || !max_tokens || !n_mha_layers || !n_kv_heads || !head_dim_qk || !head_dim_v)
+    return ZGPU_ERR_INVALID_ARG;
+  *out = nullptr;
+  cudaSetDevice(ctx->device);
+  zgpu_mha_kv *kv = new (std::nothrow) zgpu_mha_kv();
+  if (!kv) return ZGPU_ERR_OUT_OF_MEMORY;
+  kv->ctx = ctx;
+  kv->max_tokens = max_tokens;
+  kv->n_layers = n_mha_layers;
+  kv->n_kv = n_kv_heads;
+  kv->hd_qk = head_dim_qk;
+  kv->hd_v = head_dim_v;
+  kv->k_block = static_cast<uint64_t>(max_tokens) * n_kv_heads * head_dim_qk;
+  kv->v_block = static_cast<uint64_t>(max_tokens) * n_kv_heads * head_dim_v;
+  const size_t bytes = static_cast<size_t>(n_mha_layers) * (kv->k_block + kv->v_block) * 4;
+  if (cudaMalloc(&kv->d, bytes) != cudaSuccess) {
+    delete kv;
+    return zgpu_fail(ctx, ZGPU_ERR_OUT_OF_MEMORY, "mha cache allocation");
+  }
+  cudaMemset(kv->d, 0, bytes);
+  *out = kv;
+  return ZGPU_OK;
+}
+
+void zgpu_mha_kv_destroy(zgpu_mha_kv *kv) {
+  if (!kv) return;
+  cudaSetDevice(kv->ctx->device);
+  cudaFree(kv->d);
+  delete kv;
+}
+
+zgpu_status zgpu_mha_kv_store(zgpu_mha_kv *kv, uint32_t layer, uint32_t token, const float *k, const float *v) {
+  if (!kv || !k || !v) return ZGPU_ERR_INVALID_ARG;
+  if (layer >= kv->n_layers) return zgpu_fail(kv->ctx, ZGPU_ERR_KV_LAYER_OUT_OF_RANGE, "mha cache layer");
+  if (token >= kv->max_tokens) return zgpu_fail(kv->ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "mha cache token");
+  cudaSetDevice(kv->ctx->device);
+  const size_t ks = static_cast<size_t>(kv->n_kv) * kv->hd_qk, vs = static_cast<size_t>(kv->n_kv) * kv->hd_v;
+  float *base = kv->d + static_cast<size_t>(layer) * (kv->k_block + kv->v_block);
+  cudaError_t e = cudaMemcpy(base + token * ks, k, ks * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(base + kv->k_block + token * vs, v, vs * 4, cudaMemcpyHostToDevice);
+  return e == cudaSuccess ? ZGPU_OK : zgpu_cuda_fail(kv->ctx, e, "mha cache store");
+}
+
+zgpu_status zgpu_mha_kv_read(zgpu_mha_kv *kv, uint32_t layer, uint32_t token_count, float *k_out, float *v_out) {
+  if (!kv || !k_out || !v_out) return ZGPU_ERR_INVALID_ARG;
+  if (layer >= kv->n_layers) return zgpu_fail(kv->ctx, ZGPU_ERR_KV_LAYER_OUT_OF_RANGE, "mha cache layer");
+  if (token_count > kv->max_tokens)
+    return zgpu_fail(kv->ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "mha cache token count");
+  cudaSetDevice(kv->ctx->device);
+  cudaStreamSynchronize(kv->ctx->stream);
+  const size_t ks = static_cast<size_t>(kv->n_kv) * kv->hd_qk, vs = static_cast<size_t>(kv->n_kv) * kv->hd_v;
+  const float *base = kv->d + static_cast<size_t>(layer) * (kv->k_block + kv->v_block);
+  cudaError_t e = cudaMemcpy(k_out, base, token_count * ks * 4, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemcpy(v_out, base + kv->k_block, token_count * vs * 4, cudaMemcpyDeviceToHost);
+  return e == cudaSuccess ? ZGPU_OK : zgpu_cuda_fail(kv->ctx, e, "mha cache read");
+}
+
+zgpu_status zgpu_ds2_set_mha_kv(zgpu_ds2_model *m, zgpu_mha_kv *kv) {
+  if (!m) return ZGPU_ERR_INVALID_ARG;
+  zgpu_ctx *ctx = m->ctx;
+  cudaSetDevice(ctx->device);
+  if (kv) {
+    const zgpu_ds2_desc &d = m->desc;
+    if (kv->n_layers != m->n_mha)
+      return zgpu_fail(ctx, ZGPU_ERR_KV_LAYER_OUT_OF_RANGE, "mha cache layer count differs from the model's MHA layers");
+    if (kv->n_kv != m->n_kv || kv->hd_qk != d.nope_dim + d.rope_dim || kv->hd_v != d.v_dim)
+      return zgpu_fail(ctx, ZGPU_ERR_KV_INVALID_SLICE_LENGTH, "mha cache geometry differs from the model");
+    const uint32_t splits = mha_max_splits(kv->max_tokens);
+    if (splits > m->mha_splits) {
+      cudaFree(m->d_mha_part);
+      m->d_mha_part = nullptr;
+      m->mha_splits = 0;
+      cudaError_t e = cudaMalloc(&m->d_mha_part, static_cast<size_t>(d.n_heads) * splits * (d.v_dim + 2) * 4);
+      if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "mha attention scratch");
+      m->mha_splits = splits;
+    }
+  }
+  m->mha_kv = kv;
+  ds2_drop_graphs(m);   // the step graphs hold the cache's addresses
+  return ZGPU_OK;
+}
+
 // ------------------------------------------------------------ model
 
 void zgpu_ds2_destroy(zgpu_ds2_model *m) {
@@ -642,7 +787,10 @@ void zgpu_ds2_destroy(zgpu_ds2_model *m) {
     cudaFree(L.d_router_b);
     cudaFree(L.d_seg_gu);
     cudaFree(L.d_seg_dn);
+    cudaFree(L.cat_qkv);
   }
+  cudaFree(m->d_mha_qkv);
+  cudaFree(m->d_mha_part);
   for (float *p : {m->d_norms, m->d_inv_freqs, m->d_hidden, m->d_ca, m->d_q, m->d_qabs, m->d_qpe,
                    m->d_ctx, m->d_concat, m->d_act, m->d_expout, m->d_scores, m->d_logits, m->d_wts,
                    m->d_part})
@@ -677,6 +825,7 @@ zgpu_status ds2_create(zgpu_ctx *ctx, const zgpu_ds2_desc *d, uint32_t rank, uin
   cudaSetDevice(ctx->device);
   const uint32_t H = d->hidden, R = d->kv_lora_rank, RD = d->rope_dim, QL = d->q_lora_rank;
   const uint32_t NH = d->n_heads, NO = d->nope_dim, VD = d->v_dim, hq = NO + RD, L_ = d->n_layers;
+  const uint32_t NKV = d->n_kv_heads ? d->n_kv_heads : NH;
   auto bad = [&](const char *msg) { return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, msg); };
   if (!L_ || !NH) return bad("ds2: n_layers and n_heads must be > 0");
   if (d->attn_quant != ZGPU_Q4_0)
@@ -689,6 +838,10 @@ zgpu_status ds2_create(zgpu_ctx *ctx, const zgpu_ds2_desc *d, uint32_t rank, uin
   if (QL == 0 || QL % 32) return bad("ds2: q_lora_rank must be a multiple of 32");
   if ((NH * hq) % 8 || (R + RD + QL) % 4) return bad("ds2: projection rows must fill 4-row groups");
   if (d->vocab_real > d->vocab_padded) return bad("ds2: vocab_real > vocab_padded");
+  bool any_mha = false;
+  for (uint32_t l = 0; l < L_; ++l) any_mha |= d->layers[l].attn_type == ZGPU_ATTN_MHA;
+  if (any_mha && (NH % NKV || hq > kMhaMaxHead || VD > kMhaMaxV || (NKV * hq) % 4 || (NKV * VD) % 4))
+    return bad("ds2: MHA layers need n_heads % n_kv_heads == 0, nope + rope <= 320, v_dim <= 256");
   if (d->route_mode > 1) return bad("ds2: unknown routing mode");
   bool any_moe = false, any_dense = false;
   for (uint32_t l = 0; l < L_; ++l) (d->layers[l].moe ? any_moe : any_dense) = true;
@@ -732,19 +885,39 @@ zgpu_status ds2_create(zgpu_ctx *ctx, const zgpu_ds2_desc *d, uint32_t rank, uin
   for (uint32_t l = 0; l < L_; ++l) {
     const zgpu_ds2_layer &ly = d->layers[l];
     Ds2Layer &L = m->layers[l];
-    if (!ly.attn_norm || !ly.ffn_norm || !ly.kv_a_norm || !ly.q_a_norm)
+    if (ly.attn_type > ZGPU_ATTN_MHA) return fail(ZGPU_ERR_INVALID_ARG, "ds2_create: unknown attention type");
+    L.mha = ly.attn_type == ZGPU_ATTN_MHA;
+    if (!ly.attn_norm || !ly.ffn_norm || (!L.mha && (!ly.kv_a_norm || !ly.q_a_norm)))
       return fail(ZGPU_ERR_INVALID_ARG, "ds2_create: missing norm weights");
     float *nb = norms.data() + per_layer * l;
     std::memcpy(nb, ly.attn_norm, H * 4);
     std::memcpy(nb + H, ly.ffn_norm, H * 4);
+    L.o = need(ly.attn_output, ZGPU_Q4_0, H, static_cast<uint64_t>(NH) * VD, "attn_output");
+    if (!L.o) return fail(ZGPU_ERR_UNREGISTERED_WEIGHT, ctx->last_error);
+    if (L.mha) {
+      // standard attention (AttnType::Mha): q | k | v fused into one group stream
+      const DeviceTensor *wq = need(ly.q_mha, ZGPU_Q4_0, static_cast<uint64_t>(NH) * hq, H, "q_mha");
+      const DeviceTensor *wk = need(ly.k_mha, ZGPU_Q4_0, static_cast<uint64_t>(NKV) * hq, H, "k_mha");
+      const DeviceTensor *wv = need(ly.v_mha, ZGPU_Q4_0, static_cast<uint64_t>(NKV) * VD, H, "v_mha");
+      if (!wq || !wk || !wv) return fail(ZGPU_ERR_UNREGISTERED_WEIGHT, ctx->last_error);
+      m->gs_h = wq->gstride;
+      const uint32_t gq = static_cast<uint32_t>(wq->groups + wk->groups + wv->groups);
+      L.qkv_groups = (gq + 1) & ~1u;
+      const size_t cb = static_cast<size_t>(L.qkv_groups) * m->gs_h;
+      if ((e = cudaMalloc(&L.cat_qkv, cb)) != cudaSuccess) return fail(ZGPU_ERR_OUT_OF_MEMORY, "q|k|v allocation");
+      cudaMemset(L.cat_qkv, 0, cb);
+      cudaMemcpy(L.cat_qkv, wq->d, wq->bytes, cudaMemcpyDeviceToDevice);
+      cudaMemcpy(L.cat_qkv + wq->bytes, wk->d, wk->bytes, cudaMemcpyDeviceToDevice);
+      cudaMemcpy(L.cat_qkv + wq->bytes + wk->bytes, wv->d, wv->bytes, cudaMemcpyDeviceToDevice);
+      L.mha_idx = m->n_mha++;
+    } else {
     std::memcpy(nb + 2 * H, ly.kv_a_norm, R * 4);
     std::memcpy(nb + 2 * H + R, ly.q_a_norm, QL * 4);
     if (ly.k_norm) std::memcpy(nb + 2 * H + R + QL, ly.k_norm, RD * 4);
     const DeviceTensor *kva = need(ly.kv_a_mqa, ZGPU_Q4_0, R + RD, H, "kv_a_mqa");
     const DeviceTensor *qa = need(ly.q_a, ZGPU_Q4_0, QL, H, "q_a");
     L.q_b = need(ly.q_b, ZGPU_Q4_0, static_cast<uint64_t>(NH) * hq, QL, "q_b");
-    L.o = need(ly.attn_output, ZGPU_Q4_0, H, static_cast<uint64_t>(NH) * VD, "attn_output");
-    if (!kva || !qa || !L.q_b || !L.o) return fail(ZGPU_ERR_UNREGISTERED_WEIGHT, ctx->last_error);
+    if (!kva || !qa || !L.q_b) return fail(ZGPU_ERR_UNREGISTERED_WEIGHT, ctx->last_error);
     const DeviceTensor *vb = nullptr;
     if (ly.k_b && ly.v_b) {
       L.kb = need(ly.k_b, ZGPU_Q4_0, static_cast<uint64_t>(NH) * NO, R, "k_b");
@@ -776,6 +949,7 @@ zgpu_status ds2_create(zgpu_ctx *ctx, const zgpu_ds2_desc *d, uint32_t rank, uin
     L.v_seg_bytes = static_cast<uint64_t>(VD / 4) * vb->gstride;
     if ((e = cudaMalloc(&L.d_vseg, NH * 8)) != cudaSuccess) return fail(ZGPU_ERR_OUT_OF_MEMORY, "v table");
     cudaMemcpy(L.d_vseg, vseg.data(), NH * 8, cudaMemcpyHostToDevice);
+    }
     L.moe = ly.moe;
     if (!ly.moe) {
       const DeviceTensor *gt = need(ly.ffn_gate, ZGPU_Q4_0, d->ffn, H, "ffn_gate");
@@ -853,6 +1027,10 @@ zgpu_status ds2_create(zgpu_ctx *ctx, const zgpu_ds2_desc *d, uint32_t rank, uin
   cudaMemset(m->d_hidden, 0, H * 4);
   cudaMemset(m->d_ids, 0, L_ * topk * 4);
   cudaMemset(m->d_wts, 0, L_ * topk * 4);
+  m->n_kv = NKV;
+  // + 8: the GEMV writes the rows of the zero padding group as well
+  if (m->n_mha && cudaMalloc(&m->d_mha_qkv, (static_cast<size_t>(NH) * hq + static_cast<size_t>(NKV) * (hq + VD) + 8) * 4))
+    return fail(ZGPU_ERR_OUT_OF_MEMORY, "MHA projections");
   for (auto &ev : m->ev) cudaEventCreate(&ev);
   m->rank = rank;
   m->world = world;

@@ -49,4 +49,36 @@ cudaError_t launch_mla_prep(const MlaParams &p, const LaunchCfg &lc);
 // split-K attention over the latent cache, then the split merge into ctx
 cudaError_t launch_mla_attention(const MlaParams &p, const LaunchCfg &lc);
 
+// ------------------------------------------------------------------ MHA
+// DeepSeek2 layers with standard attention (AttnType::Mha, mla.rs:449-618),
+// kernels in mha.cu.
+constexpr uint32_t kMhaSplitTokens = 64;   // cached tokens per attention CTA
+constexpr uint32_t kMhaMaxHead = 320;      // nope + rope
+constexpr uint32_t kMhaMaxV = 256;         // v head width
+constexpr uint32_t kMhaThreads = 128;
+
+struct MhaParams {
+  float *qkv;                 // [n_heads*hq | n_kv*hq | n_kv*v] projections; mha_prep rotates q in place
+  const float *inv_freqs;     // [rope / 2]: powf(base, -2 i / rope)
+  float *k_cache, *v_cache;   // this layer's K block [max_tokens][n_kv*hq] and V block [max_tokens][n_kv*v]
+  uint32_t max_tokens;
+  const uint32_t *pos_ptr;    // device position, or null for pos_value
+  uint32_t pos_value;
+  float *part;                // [n_heads][max_splits][v + 2]
+  float *out;                 // [n_heads * v]
+  uint32_t *status;
+  uint32_t n_heads, n_kv, nope, rope, v, max_splits;
+  float scale;                // 1 / sqrt(nope + rope)
+};
+
+inline uint32_t mha_max_splits(uint32_t max_tokens) {
+  return (max_tokens + kMhaSplitTokens - 1) / kMhaSplitTokens;
+}
+// RoPE of the rope part of every q head (in place) and of the new k, and the
+// cache append of k and v at the position (store_kv, kv_cache.rs:487-531)
+cudaError_t launch_mha_prep(const MhaParams &p, const LaunchCfg &lc);
+// split attention over [0, pos] per q head, then the in-order split merge into out
+cudaError_t launch_mha_attention(const MhaParams &p, const LaunchCfg &lc);
+cudaError_t mha_setup();
+
 }  // namespace zgpu
