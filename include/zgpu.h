@@ -601,6 +601,29 @@ zgpu_status zgpu_smodel_find(const zgpu_smodel *m, const char *name, zgpu_smodel
  * models built from it are created. */
 zgpu_status zgpu_smodel_register(zgpu_ctx *ctx, const zgpu_smodel *m, uint32_t *registered);
 
+/* ---------------------------------------------------------- detokenizer */
+/* Token ids -> bytes for streaming output (kernel/src/detokenizer.rs): a
+ * vocabulary of byte strings, offsets[i] .. offsets[i + 1] being token i's
+ * bytes (vocab_size + 1 little-endian u32 entries, the layout of the
+ * reference's vocab_offsets.bin / tools/extract_vocab.py).  create copies
+ * both tables (install_runtime_vocab, detokenizer.rs:208-256; vocab_size 0
+ * is ZGPU_ERR_INVALID_ARG).  An id past the vocabulary, or an entry whose
+ * offsets run backwards or past the byte table, decodes to no bytes
+ * (decode_token, :110-205).  Host code; no device work. */
+typedef struct zgpu_detok zgpu_detok;
+zgpu_status zgpu_detok_create(const void *bytes, uint64_t n_bytes, const uint32_t *offsets, uint32_t vocab_size,
+                              zgpu_detok **out);
+void zgpu_detok_destroy(zgpu_detok *d);
+uint32_t zgpu_detok_vocab_size(const zgpu_detok *d);
+/* Token id's bytes: *bytes_out points into the detokenizer's table (valid
+ * until destroy), *len_out may be 0. */
+zgpu_status zgpu_detok_token(const zgpu_detok *d, uint32_t id, const uint8_t **bytes_out, uint64_t *len_out);
+/* The bytes of n ids, concatenated into out[cap]; *written = the bytes they
+ * take.  If that exceeds cap, nothing is written and the call returns
+ * ZGPU_ERR_INVALID_ARG with *written the size needed. */
+zgpu_status zgpu_detok_decode(const zgpu_detok *d, const uint32_t *ids, uint64_t n, uint8_t *out, uint64_t cap,
+                              uint64_t *written);
+
 #ifdef __cplusplus
 }
 #endif

@@ -146,6 +146,11 @@ _SIGS = {
     "zgpu_mla_kv_create": (_i32, [_vp, _u32, _u32, _u32, _u32, C.POINTER(_vp)]),
     "zgpu_mha_kv_create": (_i32, [_vp, _u32, _u32, _u32, _u32, _u32, C.POINTER(_vp)]),
     "zgpu_mha_kv_destroy": (None, [_vp]),
+    "zgpu_detok_create": (_i32, [_vp, _u64, _vp, _u32, C.POINTER(_vp)]),
+    "zgpu_detok_destroy": (None, [_vp]),
+    "zgpu_detok_vocab_size": (_u32, [_vp]),
+    "zgpu_detok_token": (_i32, [_vp, _u32, _vp, C.POINTER(_u64)]),
+    "zgpu_detok_decode": (_i32, [_vp, _vp, _u64, _vp, _u64, C.POINTER(_u64)]),
     "zgpu_mha_kv_store": (_i32, [_vp, _u32, _u32, _vp, _vp]),
     "zgpu_mha_kv_read": (_i32, [_vp, _u32, _u32, _vp, _vp]),
     "zgpu_ds2_set_mha_kv": (_i32, [_vp, _vp]),

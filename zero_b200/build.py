@@ -39,7 +39,7 @@ if os.environ.get("ZGPU_STEP_TRACE") == "1":
 
 CU_SOURCES = ["gemv.cu", "attention.cu", "attention_static.cu", "step.cu", "ops.cu", "moe.cu", "mla.cu", "mma_gemm.cu", "prefill.cu", "sampler.cu", "kquant.cu", "mha.cu",
               "ctx.cu", "model.cu", "ds2.cu"]
-CXX_SOURCES = ["synth.cpp", "smodel.cpp"]
+CXX_SOURCES = ["synth.cpp", "smodel.cpp", "detok.cpp"]
 
 
 def _run(cmd: list[str]) -> None:
