@@ -8,7 +8,8 @@
 // Q6_K super-blocks padded to kQ6kStride = 224 bytes at registration, so that
 // every field starts on an 8-byte boundary.
 //
-// One warp per output row, eight rows per CTA.  Per super-block, lane l owns
+// One to eight warps per output row (more for matrices with few rows),
+// eight warps per CTA.  Per super-block, lane l owns
 // eight consecutive elements that share one sub-block scale:
 //   Q4_K  sub-block j = l / 4 (32 elements), elements 32 j + 8 (l % 4) + i:
 //         the low (j even) or high (j odd) nibbles of qs[32 (j / 2) + 8 (l % 4) + i];
@@ -26,6 +27,8 @@
 // per CTA into shared memory.
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <type_traits>
 
 #include "common.cuh"
 #include "ops.h"
@@ -50,13 +53,18 @@ __device__ __forceinline__ float dot4(uint32_t q, float4 x, float bias, float s)
   return fmaf(x.w, byte_to_float(q >> 24, bias), s);
 }
 
-template <uint32_t QT>
+// WPR warps share a row (a matrix with few rows would leave most warp slots
+// empty): warp k of a row takes super-blocks k, k + WPR, ...; the partial
+// sums are added in warp order through shared memory.
+template <uint32_t QT, uint32_t WPR>
 __global__ void __launch_bounds__(32 * kRowsPerCta) gemv_kquant_kernel(const uint8_t *__restrict__ w, uint32_t rows,
                                                                      uint32_t spr, const float *__restrict__ x,
                                                                      float *__restrict__ y) {
   extern __shared__ float xs8[];   // [in_dim / 8]: sums of x over 8-element runs (Q4_K)
-  const uint32_t lane = threadIdx.x & 31;
-  const uint32_t row = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
+  __shared__ float wpart[kRowsPerCta];
+  constexpr uint32_t kRows = kRowsPerCta / WPR;
+  const uint32_t lane = threadIdx.x & 31, wk = (threadIdx.x >> 5) % WPR;
+  const uint32_t row = blockIdx.x * kRows + (threadIdx.x >> 5) / WPR;
   if (QT == ZGPU_Q4_K) {
     for (uint32_t r = threadIdx.x; r < spr * 32; r += blockDim.x) {
       const float4 a = *reinterpret_cast<const float4 *>(x + 8 * r);
@@ -65,13 +73,13 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) gemv_kquant_kernel(const uin
     }
     __syncthreads();
   }
-  if (row >= rows) return;
   float acc = 0.f;
+  if (row < rows) {
   if (QT == ZGPU_Q4_K) {
     const uint32_t j = lane >> 2, p = lane & 3, sh = (j & 1) * 4;
     const uint8_t *wr = w + static_cast<size_t>(row) * spr * 144;
 #pragma unroll 4
-    for (uint32_t b = 0; b < spr; ++b) {
+    for (uint32_t b = wk; b < spr; b += WPR) {
       const uint8_t *blk = wr + static_cast<size_t>(b) * 144;
       const uint32_t dm = *reinterpret_cast<const uint32_t *>(blk);
       const uint32_t s0 = *reinterpret_cast<const uint32_t *>(blk + 4);
@@ -103,7 +111,7 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) gemv_kquant_kernel(const uin
     const uint32_t h = lane >> 4, k = (lane >> 2) & 3, l0 = (lane & 3) * 8;
     const uint8_t *wr = w + static_cast<size_t>(row) * spr * kQ6kStride;
 #pragma unroll 4
-    for (uint32_t b = 0; b < spr; ++b) {
+    for (uint32_t b = wk; b < spr; b += WPR) {
       const uint8_t *blk = wr + static_cast<size_t>(b) * kQ6kStride;
       const uint2 ql = *reinterpret_cast<const uint2 *>(blk + 64 * h + 32 * (k & 1) + l0);
       const uint2 qh = *reinterpret_cast<const uint2 *>(blk + 128 + 32 * h + l0);
@@ -121,9 +129,20 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) gemv_kquant_kernel(const uin
       acc = fmaf(dsc, s, acc);
     }
   }
+  }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) y[row] = acc;
+  if (WPR == 1) {
+    if (lane == 0 && row < rows) y[row] = acc;
+    return;
+  }
+  if (lane == 0) wpart[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (lane == 0 && wk == 0 && row < rows) {
+    float t = wpart[threadIdx.x >> 5];
+    for (uint32_t k = 1; k < WPR; ++k) t += wpart[(threadIdx.x >> 5) + k];
+    y[row] = t;
+  }
 }
 
 }  // namespace
@@ -134,14 +153,30 @@ cudaError_t launch_gemv_kquant(const uint8_t *w, uint32_t quant, uint32_t rows, 
   if (rows == 0 || in_dim == 0 || in_dim % 256 || in_dim > kMaxKquantIn ||
       (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
     return cudaErrorInvalidValue;
-  const dim3 grid((rows + kRowsPerCta - 1) / kRowsPerCta), block(32 * kRowsPerCta);
+  if (quant != ZGPU_Q4_K && quant != ZGPU_Q6_K) return cudaErrorInvalidValue;
   const uint32_t spr = in_dim / 256;
+  // warps per row: enough warps in flight (rows x WPR >= 8192), at most one super-block each
+  uint32_t wpr = 1;
+  while (wpr < kRowsPerCta && static_cast<uint64_t>(rows) * wpr < 8192 && 2 * wpr <= spr) wpr *= 2;
+  const dim3 grid((rows + kRowsPerCta / wpr - 1) / (kRowsPerCta / wpr)), block(32 * kRowsPerCta);
+  const size_t smem = quant == ZGPU_Q4_K ? in_dim / 8 * sizeof(float) : 0;
+  auto go = [&](auto qt, auto wp) {
+    gemv_kquant_kernel<decltype(qt)::value, decltype(wp)::value><<<grid, block, smem, s>>>(w, rows, spr, x, y);
+  };
+  using Q4 = std::integral_constant<uint32_t, ZGPU_Q4_K>;
+  using Q6 = std::integral_constant<uint32_t, ZGPU_Q6_K>;
+  auto by_wpr = [&](auto qt) {
+    switch (wpr) {
+      case 1: go(qt, std::integral_constant<uint32_t, 1>()); break;
+      case 2: go(qt, std::integral_constant<uint32_t, 2>()); break;
+      case 4: go(qt, std::integral_constant<uint32_t, 4>()); break;
+      default: go(qt, std::integral_constant<uint32_t, 8>()); break;
+    }
+  };
   if (quant == ZGPU_Q4_K)
-    gemv_kquant_kernel<ZGPU_Q4_K><<<grid, block, in_dim / 8 * sizeof(float), s>>>(w, rows, spr, x, y);
-  else if (quant == ZGPU_Q6_K)
-    gemv_kquant_kernel<ZGPU_Q6_K><<<grid, block, 0, s>>>(w, rows, spr, x, y);
+    by_wpr(Q4());
   else
-    return cudaErrorInvalidValue;
+    by_wpr(Q6());
   return cudaGetLastError();
 }
 
