@@ -40,7 +40,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   q.kv_layer = sq.kv + static_cast<size_t>(layer) * 2 * sq.block;
   q.kv_block = sq.block;
   q.max_tokens = sq.max_tokens;
-  attn_decode_block<BlockBar, false, 4>(q, blockIdx.x, blockIdx.y, sq.pos, threadIdx.x, sm, BlockBar());
+  attn_decode_block<BlockBar, false, 4, kAttnWarps, AttnNoMark, true>(q, blockIdx.x, blockIdx.y, sq.pos, threadIdx.x,
+                                                                      sm, BlockBar());
 }
 
 }  // namespace

@@ -128,8 +128,11 @@ struct AttnNoMark {
   __device__ __forceinline__ void operator()(uint32_t) const {}
 };
 
+// FAST (the batched decode kernel): the run's scores of all q heads reduced
+// together (one butterfly for four values per token) and exp by __expf; the
+// result differs from the default path in the last bits of the sums.
 template <class Bar, bool TAGGED = false, int kAttnUnroll = kAttnUnrollMax, int NW = kAttnWarps,
-          class Mark = AttnNoMark>
+          class Mark = AttnNoMark, bool FAST = false>
 __device__ __forceinline__ void attn_decode_block(const AttnParams &p, uint32_t kvh, uint32_t split,
                                                   uint32_t pos, uint32_t tid, AttnSmemT<NW> &sm, Bar bar,
                                                   Mark mark = Mark()) {
@@ -220,6 +223,56 @@ __device__ __forceinline__ void attn_decode_block(const AttnParams &p, uint32_t 
         }
       }
     }
+    if constexpr (FAST) {
+      static_assert(kAttnMaxGqa == 4, "the butterfly reduces four heads");
+      // per token: lane l holds the partial dots of the four heads over its
+      // 4 dims; after exchanging pairs (xor 16), singles (xor 8) and three
+      // more rounds, lanes 8(2a + b).. hold the full dot of head 2a + b,
+      // which is then broadcast
+      float sc4[kAttnMaxGqa][kAttnUnroll];
+      const bool hi = lane & 16, bt = lane & 8;
+#pragma unroll
+      for (int u = 0; u < kAttnUnroll; ++u) {
+        float d[kAttnMaxGqa];
+#pragma unroll
+        for (int j = 0; j < kAttnMaxGqa; ++j)
+          d[j] = __fmaf_rn(q[j].w, kk[u].w, __fmaf_rn(q[j].z, kk[u].z, __fmaf_rn(q[j].y, kk[u].y, __fmul_rn(q[j].x, kk[u].x))));
+        const float r0 = __shfl_xor_sync(0xffffffffu, hi ? d[0] : d[2], 16);
+        const float r1 = __shfl_xor_sync(0xffffffffu, hi ? d[1] : d[3], 16);
+        const float a0 = (hi ? d[2] : d[0]) + r0, a1 = (hi ? d[3] : d[1]) + r1;
+        float c = (bt ? a1 : a0) + __shfl_xor_sync(0xffffffffu, bt ? a0 : a1, 8);
+        c += __shfl_xor_sync(0xffffffffu, c, 4);
+        c += __shfl_xor_sync(0xffffffffu, c, 2);
+        c += __shfl_xor_sync(0xffffffffu, c, 1);
+#pragma unroll
+        for (int j = 0; j < kAttnMaxGqa; ++j) {
+          const float dj = __shfl_sync(0xffffffffu, c, (j >> 1) * 16 + (j & 1) * 8);
+          sc4[j][u] = (tb + u < t1) ? __fmul_rn(dj, p.scale) : -INFINITY;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kAttnMaxGqa; ++j) {
+        if (j >= static_cast<int>(G)) break;
+        float mx = m[j];
+#pragma unroll
+        for (int u = 0; u < kAttnUnroll; ++u) mx = fmaxf(mx, sc4[j][u]);
+        const float corr = __expf(m[j] - mx);
+        float lj = l[j] * corr;
+        float4 oj = make_float4(o[j].x * corr, o[j].y * corr, o[j].z * corr, o[j].w * corr);
+#pragma unroll
+        for (int u = 0; u < kAttnUnroll; ++u) {
+          const float e = (tb + u < t1) ? __expf(sc4[j][u] - mx) : 0.f;
+          lj += e;
+          oj.x = __fmaf_rn(e, vv[u].x, oj.x);
+          oj.y = __fmaf_rn(e, vv[u].y, oj.y);
+          oj.z = __fmaf_rn(e, vv[u].z, oj.z);
+          oj.w = __fmaf_rn(e, vv[u].w, oj.w);
+        }
+        m[j] = mx;
+        l[j] = lj;
+        o[j] = oj;
+      }
+    } else
 #pragma unroll
     for (int j = 0; j < kAttnMaxGqa; ++j) {
       if (j >= static_cast<int>(G)) break;
