@@ -281,25 +281,32 @@ __global__ void __launch_bounds__(MmaCfg<NT>::kThreads, 1) q4q8_mma_kernel(const
       float acc[CW];
 #pragma unroll
       for (int j = 0; j < static_cast<int>(CW); ++j) acc[j] = 0.f;
-      for (uint32_t b = b0; b < b1 && ok; ++b, ++gb) {
-        const uint32_t s = gb % kStages, par = (gb / kStages) & 1;
-        if (!mbar_wait(smem_addr(&done[s]), par, p.status) || !mbar_wait(smem_addr(&full[s]), par, p.status)) {
-          ok = false;
-          break;
-        }
+      // Software-pipelined on the 32-wide tile: block b + 1's accumulator is
+      // waited for and its TMEM load issued before block b is scaled, so the
+      // load's latency overlaps the arithmetic.  Two register buffers
+      // alternate (a load's registers are not read before tcgen05.wait::ld).
+      auto tmem_ld = [&](uint32_t gbk, uint32_t (&v)[CW]) -> bool {
+        const uint32_t sk = gbk % kStages, park = (gbk / kStages) & 1;
+        if (!mbar_wait(smem_addr(&done[sk]), park, p.status) || !mbar_wait(smem_addr(&full[sk]), park, p.status))
+          return false;
         tc_fence_after();
+        if constexpr (CW == 32)
+          tmem_ld32(tmem + ((32u * q) << 16) + sk * kTileN + CW * c, v);
+        else
+          tmem_ld8(tmem + ((32u * q) << 16) + sk * kTileN + CW * c, v);
+        return true;
+      };
+      // block b (its load issued, global block count gb): prefetch b + 1, then
+      // acc += (sumi * d_w) * d_x, two columns per packed instruction.  sumi
+      // -> f32 exactly: |sumi| <= 32 * 8 * 127 < 2^22, so sumi + 1.5 * 2^23
+      // taken as float bits, minus 1.5 * 2^23, is sumi
+      auto step = [&](uint32_t b, uint32_t (&v)[CW], uint32_t (&vn)[CW], bool prefetch) -> bool {
+        tmem_ld_wait();
+        const uint32_t s = gb % kStages;
+        const bool next_ok = (prefetch && b + 1 < b1) ? tmem_ld(gb + 1, vn) : true;
         const uint8_t *st = ring + s * kStageBytes;
         const float dw = reinterpret_cast<const float *>(st + kStW)[32 * q + lane];
         const float4 *dx4 = reinterpret_cast<const float4 *>(st + kStX) + (CW / 4) * c;
-        uint32_t v[CW];
-        if constexpr (CW == 32)
-          tmem_ld32(tmem + ((32u * q) << 16) + s * kTileN + CW * c, v);
-        else
-          tmem_ld8(tmem + ((32u * q) << 16) + s * kTileN + CW * c, v);
-        tmem_ld_wait();
-        // acc += (sumi * d_w) * d_x, two columns per packed instruction.  sumi
-        // -> f32 exactly: |sumi| <= 32 * 8 * 127 < 2^22, so sumi + 1.5 * 2^23
-        // taken as float bits, minus 1.5 * 2^23, is sumi
         const float2 dw2 = make_float2(dw, dw), magic = make_float2(-12582912.0f, -12582912.0f);
 #pragma unroll
         for (int j4 = 0; j4 < static_cast<int>(CW / 4); ++j4) {
@@ -317,7 +324,25 @@ __global__ void __launch_bounds__(MmaCfg<NT>::kThreads, 1) q4q8_mma_kernel(const
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_addr(&empty[s]));
+        ++gb;
+        return next_ok;
+      };
+      uint32_t va[CW], vb[CW];
+      if constexpr (CW == 8) {
+        if (b0 < b1 && ok) ok = tmem_ld(gb, va);
+        for (uint32_t b = b0; b < b1 && ok; b += 2) {
+          ok = step(b, va, vb, true);
+          if (!ok || b + 1 >= b1) break;
+          ok = step(b + 1, vb, va, true);
+        }
+      } else {
+        // the 128-wide tile keeps one buffer (two would not fit its registers)
+        for (uint32_t b = b0; b < b1 && ok; ++b) {
+          ok = tmem_ld(gb, va);
+          if (ok) ok = step(b, va, vb, false);
+        }
       }
+      tmem_ld_wait();
       const uint32_t row = mt * kTileM + 32 * q + lane;
 #pragma unroll
       for (int j = 0; j < static_cast<int>(CW); ++j) {
