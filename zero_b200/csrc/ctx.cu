@@ -110,7 +110,6 @@ zgpu_status zgpu_clear_weights(zgpu_ctx *ctx) {
   for (auto &kv : ctx->weights) {
     cudaFree(kv.second.d);
     cudaFree(kv.second.w8);
-    cudaFree(kv.second.ws8);
   }
   ctx->weights.clear();
   return ZGPU_OK;
@@ -262,7 +261,6 @@ zgpu_status zgpu_register_weights(zgpu_ctx *ctx, const void *host_ptr, size_t le
   if (it != ctx->weights.end()) {
     cudaFree(it->second.d);
     cudaFree(it->second.w8);
-    cudaFree(it->second.ws8);
   }
   ctx->weights[key] = t;
   return ZGPU_OK;
@@ -502,13 +500,13 @@ static zgpu_status q8act_batch(zgpu_ctx *ctx, const float *d_x, const void *w_ke
   DeviceTensor *wt = const_cast<DeviceTensor *>(t);
   if (!wt->w8) {
     ZCHECK(cudaMalloc(&wt->w8, zgpu::mma_tile_bytes(out_dim, bpr)), "cudaMalloc(weight tiles)");
-    ZCHECK(cudaMalloc(&wt->ws8, zgpu::mma_scale_bytes(out_dim, bpr)), "cudaMalloc(weight tile scales)");
+    wt->ws8 = reinterpret_cast<float *>(wt->w8);   // the scales sit beside each 4 KB tile
     ZCHECK(zgpu::launch_build_w8_tiles(wt->d, wt->gstride, static_cast<uint32_t>(out_dim), bpr, t->quant, wt->w8, wt->ws8, s),
            "weight tiles");
     ++ctx->launches;
   }
-  // scratch: activation tiles | their scales
-  const size_t qbytes = zgpu::mma_tile_bytes(T, bpr), dbytes = zgpu::mma_scale_bytes(T, bpr);
+  // scratch: activation tiles with their scales
+  const size_t qbytes = zgpu::mma_tile_bytes(T, bpr), dbytes = 0;
   if (qbytes + dbytes > ctx->d_q8_cap) {
     cudaFree(ctx->d_q8);
     ctx->d_q8 = nullptr;
@@ -517,7 +515,7 @@ static zgpu_status q8act_batch(zgpu_ctx *ctx, const float *d_x, const void *w_ke
     ctx->d_q8_cap = qbytes + dbytes;
   }
   int8_t *q = reinterpret_cast<int8_t *>(ctx->d_q8);
-  float *d = reinterpret_cast<float *>(ctx->d_q8 + qbytes);
+  float *d = reinterpret_cast<float *>(ctx->d_q8);
   ZCHECK(zgpu::launch_quantize_q8_0_tiles(d_x, q, d, static_cast<uint32_t>(T), static_cast<uint32_t>(in_dim),
                                          ctx->d_status, s),
          "q8 tiles");

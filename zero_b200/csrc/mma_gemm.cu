@@ -15,8 +15,10 @@
 // quantisers, each 128 x 32 block a contiguous 4 KB in the MMA's canonical
 // layout, plus f32 scale vectors.  One CTA per SM, warp-specialised, no
 // CTA-wide barrier inside the block loop:
-//   warp 0      producer: per block, four 1-D bulk copies (A, B, d_w, d_x)
-//               into one of 4 shared-memory stages, completion on full[s];
+//   warp 0      producer: per block, one 1-D bulk copy of the weight tile
+//               with its scales and one of the token tile with its scales
+//               (two for a 32-wide token tile) into one of 4 shared-memory
+//               stages, completion on full[s];
 //   warp 1      MMA issuer: waits full[s], one tcgen05.mma into accumulator
 //               s (4 x 128 TMEM columns), tcgen05.commit to done[s];
 //   warps 2-17  epilogue: warp w reads TMEM lanes 32 (w % 4).. (weight rows)
@@ -67,9 +69,12 @@ struct MmaCfg {
   static constexpr uint32_t kEpiWarps = 16;                     // 4 lane quarters x 4 column groups
   static constexpr uint32_t kCols = NT / 4;                      // token columns per epilogue warp
   static constexpr uint32_t kThreads = 32 * (2 + kEpiWarps);
-  static constexpr uint32_t kStA = 0, kStB = 4096, kStW = 4096 + NT * 32, kStX = kStW + 512;
-  static constexpr uint32_t kStageLoad = kStX + NT * 4;        // bytes copied per stage
-  static constexpr uint32_t kStageBytes = (kStageLoad + 1023) / 1024 * 1024;
+  // A tile + its scales (one 4608-byte copy), then the NT token rows
+  // (1024-aligned) and their scales (one copy with them when NT = 128)
+  static constexpr uint32_t kStA = 0, kStW = 4096, kStB = 5120;
+  static constexpr uint32_t kStX = NT == 128 ? kStB + 4096 : kStB + NT * 32;
+  static constexpr uint32_t kStageLoad = kMmaBlockBytes + NT * 32 + NT * 4;   // bytes copied per stage
+  static constexpr uint32_t kStageBytes = (kStX + NT * 4 + 1023) / 1024 * 1024;
   // instruction descriptor of kind::i8: D s32, A and B signed int8, both
   // K-major, N = NT, M = 128, dense
   static constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((NT >> 3) << 17) | ((kTileM >> 4) << 24);
@@ -222,10 +227,10 @@ __global__ void __launch_bounds__(MmaCfg<NT>::kThreads, 1) q4q8_mma_kernel(const
         // token tile nt: rows [nt NT, nt NT + NT) of the 128-row activation
         // tiles, which in the canonical layout are NT * 32 contiguous bytes
         const uint32_t tt = nt * kTileN / kMmaTile, r0 = nt * kTileN % kMmaTile;
-        const int8_t *wa = p.wt + static_cast<size_t>(mt) * bpr * 4096u;
-        const int8_t *xa = p.xt + static_cast<size_t>(tt) * bpr * 4096u + r0 * 32u;
-        const float *ws = p.ws + static_cast<size_t>(mt) * bpr * kTileM;
-        const float *xs = p.xs + static_cast<size_t>(tt) * bpr * kMmaTile + r0;
+        // block b of a tile: kMmaBlockBytes at b * kMmaBlockBytes, its 4 KB
+        // of digits then the 128 rows' scales (ops.h)
+        const int8_t *wa = p.wt + static_cast<size_t>(mt) * bpr * kMmaBlockBytes;
+        const int8_t *xa = p.xt + static_cast<size_t>(tt) * bpr * kMmaBlockBytes;
         for (uint32_t b = b0; b < b1; ++b, ++gb) {
           const uint32_t s = gb % kStages;
           if (gb >= kStages && !mbar_wait(smem_addr(&empty[s]), ((gb / kStages) - 1) & 1, p.status)) {
@@ -234,10 +239,14 @@ __global__ void __launch_bounds__(MmaCfg<NT>::kThreads, 1) q4q8_mma_kernel(const
           }
           const uint32_t st = smem_addr(ring + s * kStageBytes), fb = smem_addr(&full[s]);
           mbar_arrive_expect_tx(fb, Cfg::kStageLoad);
-          bulk_copy_g2s(st + kStA, wa + static_cast<size_t>(b) * 4096u, 4096, fb);
-          bulk_copy_g2s(st + kStB, xa + static_cast<size_t>(b) * 4096u, kTileN * 32, fb);
-          bulk_copy_g2s(st + kStW, ws + static_cast<size_t>(b) * kTileM, 512, fb);
-          bulk_copy_g2s(st + kStX, xs + static_cast<size_t>(b) * kMmaTile, kTileN * 4, fb);
+          const int8_t *xb = xa + static_cast<size_t>(b) * kMmaBlockBytes;
+          bulk_copy_g2s(st + kStA, wa + static_cast<size_t>(b) * kMmaBlockBytes, kMmaBlockBytes, fb);
+          if (kTileN == kMmaTile) {
+            bulk_copy_g2s(st + kStB, xb, kMmaBlockBytes, fb);
+          } else {
+            bulk_copy_g2s(st + kStB, xb + r0 * 32u, kTileN * 32, fb);
+            bulk_copy_g2s(st + kStX, xb + 4096u + r0 * 4u, kTileN * 4, fb);
+          }
         }
       }
       // never leave a copy in flight when the CTA may exit

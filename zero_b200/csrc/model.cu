@@ -658,9 +658,7 @@ void zgpu_qwen3_destroy(zgpu_model *m) {
     if (e) cudaEventDestroy(e);
   for (auto &e : m->pf_ev) cudaEventDestroy(e);
   for (int8_t *p : m->pf_w8) cudaFree(p);
-  for (float *p : m->pf_ws8) cudaFree(p);
   cudaFree(m->lm_w8);
-  cudaFree(m->lm_ws8);
   cudaFree(m->d_bd);
   for (DeviceTensor *t : m->owned) {
     cudaFree(t->d);
@@ -1201,14 +1199,13 @@ zgpu_status ensure_pf_tiles(zgpu_model *m) {
       int8_t *wt = nullptr;
       float *ws = nullptr;
       cudaError_t e = cudaMalloc(&wt, mma_tile_bytes(mt.rows, mt.in_dim / 32));
-      if (e == cudaSuccess) e = cudaMalloc(&ws, mma_scale_bytes(mt.rows, mt.in_dim / 32));
+      ws = reinterpret_cast<float *>(wt);   // the scales sit beside each 4 KB tile
       m->pf_w8.push_back(wt);
       m->pf_ws8.push_back(ws);
       if (e == cudaSuccess)
         e = launch_build_w8_tiles(mt.w, mt.gstride, mt.rows, mt.in_dim / 32, ZGPU_Q4_0, wt, ws, m->ctx->stream);
       if (e != cudaSuccess) {
         for (int8_t *p : m->pf_w8) cudaFree(p);
-        for (float *p : m->pf_ws8) cudaFree(p);
         m->pf_w8.clear();
         m->pf_ws8.clear();
         return zgpu_cuda_fail(m->ctx, e, "prefill weight tiles");
@@ -1249,8 +1246,7 @@ zgpu_status prefill_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, cons
   auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
   const size_t o_tok = 0, o_hid = al(N * 4), o_qkv = o_hid + al(N * H * 4), o_qr = o_qkv + al(N * QKV * 4),
                o_at = o_qr + al(N * QD * 4), o_gu = o_at + al(N * QD * 4), o_q8 = o_gu + al(N * 2 * F * 4),
-               o_d8 = o_q8 + al(mma_tile_bytes(N, maxk / 32)),
-               total = o_d8 + al(mma_scale_bytes(N, maxk / 32));
+               o_d8 = o_q8, total = o_q8 + al(mma_tile_bytes(N, maxk / 32));   // scales inside the tiles
   if (total > m->pf_cap) {
     cudaFree(m->d_pf);
     m->d_pf = nullptr;
@@ -1421,12 +1417,11 @@ zgpu_status decode_batch_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq,
   cudaError_t e = cudaSuccess;
   if (!m->lm_w8) {
     e = cudaMalloc(&m->lm_w8, mma_tile_bytes(V, H / 32));
-    if (e == cudaSuccess) e = cudaMalloc(&m->lm_ws8, mma_scale_bytes(V, H / 32));
+    m->lm_ws8 = reinterpret_cast<float *>(m->lm_w8);   // the scales sit beside each 4 KB tile
     if (e == cudaSuccess)
       e = launch_build_w8_tiles(m->out->d, m->out->gstride, V, H / 32, m->out->quant, m->lm_w8, m->lm_ws8, s);
     if (e != cudaSuccess) {
       cudaFree(m->lm_w8);
-      cudaFree(m->lm_ws8);
       m->lm_w8 = nullptr;
       m->lm_ws8 = nullptr;
       return zgpu_cuda_fail(ctx, e, "LM head tiles");
@@ -1437,7 +1432,7 @@ zgpu_status decode_batch_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq,
   auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
   const size_t o_tok = 0, o_hid = al(N * 4), o_qkv = o_hid + al(N * H * 4), o_at = o_qkv + al(N * QKV * 4),
                o_gu = o_at + al(N * QD * 4), o_q8 = o_gu + al(N * 2 * F * 4),
-               o_d8 = o_q8 + al(mma_tile_bytes(N, maxk / 32)), total = o_d8 + al(mma_scale_bytes(N, maxk / 32));
+               o_d8 = o_q8, total = o_q8 + al(mma_tile_bytes(N, maxk / 32));   // scales inside the tiles
   if (total > m->pf_cap) {
     cudaFree(m->d_pf);
     m->d_pf = nullptr;

@@ -93,21 +93,24 @@ inline cudaLaunchConfig_t make_launch_cfg(dim3 grid, dim3 block, size_t smem, co
 // 128-row (or 128-token) tile and 32-element block, 4096 bytes of int8 in the
 // tensor core's canonical K-major layout (8-row x 16-byte core matrices, row r
 // and K half h at (r % 8) * 16 + (r / 8) * 256 + h * 128), tiles laid out
-// [tile][block]; scales f32 [tile][block][128].  Weights hold n - 8 of their
+// [tile][block], each block followed by its 128 rows' f32 scales.  Weights hold n - 8 of their
 // Q4_0 nibbles; activations the Q8_0 digits, rows past T zero.
 constexpr uint32_t kMmaTile = 128;
+// A (tile, block) is kMmaBlockBytes: the 4 KB of int8 digits, then the 128
+// rows' f32 scales, so that one copy brings a block and its scales.  The
+// scales are addressed through the same allocation: callers pass
+// reinterpret_cast<float *>(tiles) as the scale pointer.
+constexpr uint32_t kMmaBlockBytes = 4096 + 4 * kMmaTile;
 inline size_t mma_tile_bytes(uint64_t rows, uint32_t bpr) {
-  return ((rows + kMmaTile - 1) / kMmaTile) * bpr * 4096ull;
-}
-inline size_t mma_scale_bytes(uint64_t rows, uint32_t bpr) {
-  return ((rows + kMmaTile - 1) / kMmaTile) * bpr * kMmaTile * 4ull;
+  return ((rows + kMmaTile - 1) / kMmaTile) * bpr * static_cast<uint64_t>(kMmaBlockBytes);
 }
 __host__ __device__ inline size_t mma_tile_off(uint32_t r, uint32_t b, uint32_t bpr, uint32_t h) {
-  return (static_cast<size_t>(r / kMmaTile) * bpr + b) * 4096u + (r % 8) * 16u + ((r % kMmaTile) / 8) * 256u +
-         h * 128u;
+  return (static_cast<size_t>(r / kMmaTile) * bpr + b) * kMmaBlockBytes + (r % 8) * 16u +
+         ((r % kMmaTile) / 8) * 256u + h * 128u;
 }
+// f32 index of row r's scale of block b, from the tile allocation's start
 __host__ __device__ inline size_t mma_scale_off(uint32_t r, uint32_t b, uint32_t bpr) {
-  return (static_cast<size_t>(r / kMmaTile) * bpr + b) * kMmaTile + r % kMmaTile;
+  return ((static_cast<size_t>(r / kMmaTile) * bpr + b) * kMmaBlockBytes + 4096u) / 4u + r % kMmaTile;
 }
 
 struct MmaGemmParams {
