@@ -25,10 +25,11 @@
 //               x columns 32 ((w - 2) / 4).. (tokens) of accumulator s, scales
 //               and accumulates in f32 registers, then arrives on empty[s],
 //               which frees stage s and accumulator s for block b + 4.
-// For a few tokens (T <= 32, batched decode) the token tile is 32 wide:
-// 16 stages / accumulators of 32 TMEM columns each, a 1 KB activation copy
-// per block and 16 epilogue warps of 8 columns each, so that 16 blocks of
-// weights are in flight per SM instead of 4.  A weight with few 128-row tiles can also be split
+// For a few tokens (T <= 32, batched decode) the token tile is 32 wide and
+// two CTAs share an SM, each with 8 stages / accumulators of 32 TMEM columns
+// (half of TMEM), a 1 KB activation copy per block and 4 epilogue warps, so
+// that 16 blocks of weights are in flight per SM instead of 4 on two
+// independent pipelines.  A weight with few 128-row tiles can also be split
 // along K (MmaGemmParams::ksplit): each split sums its block range in order
 // into a partial, and a reduce kernel adds the partials in split order.  The
 // split count depends on the weight's shape alone, so a token's result does
@@ -62,13 +63,21 @@ constexpr uint32_t kDynSmem = 120 * 1024;        // > half of an SM: one CTA per
 // room for 16 block accumulators in flight instead of 4.  A stage holds one
 // 32-element block: the weight tile (128 rows), the first NT rows of the
 // activation tile, and both tiles' block scales.
+// The 32-wide tile runs two CTAs per SM, each on half of TMEM (8 stages, 4
+// epilogue warps of all 32 columns): two independent producer / MMA /
+// epilogue chains per SM.
 template <uint32_t NT>
 struct MmaCfg {
   static constexpr uint32_t kTileN = NT;
-  static constexpr uint32_t kStages = kTmemCols / NT;          // = TMEM accumulators
-  static constexpr uint32_t kEpiWarps = 16;                     // 4 lane quarters x 4 column groups
-  static constexpr uint32_t kCols = NT / 4;                      // token columns per epilogue warp
+  static constexpr uint32_t kCtasPerSm = NT == 128 ? 1 : 2;
+  static constexpr uint32_t kTmem = kTmemCols / kCtasPerSm;     // TMEM columns of one CTA
+  static constexpr uint32_t kStages = kTmem / NT;               // = TMEM accumulators
+  static constexpr uint32_t kEpiWarps = NT == 128 ? 16 : 4;     // 4 lane quarters x NT / kCols column groups
+  static constexpr uint32_t kCols = NT * 4 / kEpiWarps;         // token columns per epilogue warp
   static constexpr uint32_t kThreads = 32 * (2 + kEpiWarps);
+  // dynamic shared memory: more than a third of the SM for two CTAs per SM,
+  // more than half for one (a further CTA would wait on its TMEM allocation)
+  static constexpr uint32_t kDyn = NT == 128 ? kDynSmem : 80 * 1024;
   // A tile + its scales (one 4608-byte copy), then the NT token rows
   // (1024-aligned) and their scales (one copy with them when NT = 128)
   static constexpr uint32_t kStA = 0, kStW = 4096, kStB = 5120;
@@ -78,7 +87,7 @@ struct MmaCfg {
   // instruction descriptor of kind::i8: D s32, A and B signed int8, both
   // K-major, N = NT, M = 128, dense
   static constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((NT >> 3) << 17) | ((kTileM >> 4) << 24);
-  static_assert(kStages * kStageBytes <= kDynSmem, "stages fit the dynamic shared memory");
+  static_assert(kStages * kStageBytes <= kDyn, "stages fit the dynamic shared memory");
 };
 }
 
@@ -127,13 +136,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
       : "r"(taddr)
       : "memory");
 }
-// 8 consecutive 32-bit TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
-               : "r"(taddr)
-               : "memory");
-}
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 
@@ -168,7 +170,7 @@ __device__ __forceinline__ uint32_t nib_to_s8(uint32_t n4) {
 }
 
 template <uint32_t NT>
-__global__ void __launch_bounds__(MmaCfg<NT>::kThreads, 1) q4q8_mma_kernel(const MmaGemmParams p) {
+__global__ void __launch_bounds__(MmaCfg<NT>::kThreads, MmaCfg<NT>::kCtasPerSm) q4q8_mma_kernel(const MmaGemmParams p) {
   using Cfg = MmaCfg<NT>;
   constexpr uint32_t kTileN = Cfg::kTileN, kStages = Cfg::kStages, kEpiWarps = Cfg::kEpiWarps;
   constexpr uint32_t kStA = Cfg::kStA, kStB = Cfg::kStB, kStW = Cfg::kStW, kStX = Cfg::kStX;
@@ -182,7 +184,7 @@ __global__ void __launch_bounds__(MmaCfg<NT>::kThreads, 1) q4q8_mma_kernel(const
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
-                 "r"(kTmemCols)
+                 "r"(Cfg::kTmem)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -281,7 +283,7 @@ __global__ void __launch_bounds__(MmaCfg<NT>::kThreads, 1) q4q8_mma_kernel(const
     // ---------------- epilogue ----------------
     // TMEM lane quarter (a warp reads the quarter warp % 4) and group of CW token columns
     constexpr uint32_t CW = Cfg::kCols;
-    const uint32_t q = warp & 3, c = (warp - 2) >> 2;
+    const uint32_t q = warp & 3, c = kEpiWarps == 16 ? (warp - 2) >> 2 : 0;
     uint32_t gb = 0;
     bool ok = true;
     for (uint32_t tix = blockIdx.x; tix < n_tiles; tix += gridDim.x) {
@@ -290,29 +292,22 @@ __global__ void __launch_bounds__(MmaCfg<NT>::kThreads, 1) q4q8_mma_kernel(const
       float acc[CW];
 #pragma unroll
       for (int j = 0; j < static_cast<int>(CW); ++j) acc[j] = 0.f;
-      // Software-pipelined on the 32-wide tile: block b + 1's accumulator is
-      // waited for and its TMEM load issued before block b is scaled, so the
-      // load's latency overlaps the arithmetic.  Two register buffers
-      // alternate (a load's registers are not read before tcgen05.wait::ld).
+      // wait for block gbk's accumulator and start its TMEM load
       auto tmem_ld = [&](uint32_t gbk, uint32_t (&v)[CW]) -> bool {
         const uint32_t sk = gbk % kStages, park = (gbk / kStages) & 1;
         if (!mbar_wait(smem_addr(&done[sk]), park, p.status) || !mbar_wait(smem_addr(&full[sk]), park, p.status))
           return false;
         tc_fence_after();
-        if constexpr (CW == 32)
-          tmem_ld32(tmem + ((32u * q) << 16) + sk * kTileN + CW * c, v);
-        else
-          tmem_ld8(tmem + ((32u * q) << 16) + sk * kTileN + CW * c, v);
+        tmem_ld32(tmem + ((32u * q) << 16) + sk * kTileN + CW * c, v);
         return true;
       };
-      // block b (its load issued, global block count gb): prefetch b + 1, then
+      // block b (its load issued, global block count gb):
       // acc += (sumi * d_w) * d_x, two columns per packed instruction.  sumi
       // -> f32 exactly: |sumi| <= 32 * 8 * 127 < 2^22, so sumi + 1.5 * 2^23
       // taken as float bits, minus 1.5 * 2^23, is sumi
-      auto step = [&](uint32_t b, uint32_t (&v)[CW], uint32_t (&vn)[CW], bool prefetch) -> bool {
+      auto step = [&](uint32_t (&v)[CW]) {
         tmem_ld_wait();
         const uint32_t s = gb % kStages;
-        const bool next_ok = (prefetch && b + 1 < b1) ? tmem_ld(gb + 1, vn) : true;
         const uint8_t *st = ring + s * kStageBytes;
         const float dw = reinterpret_cast<const float *>(st + kStW)[32 * q + lane];
         const float4 *dx4 = reinterpret_cast<const float4 *>(st + kStX) + (CW / 4) * c;
@@ -334,22 +329,11 @@ __global__ void __launch_bounds__(MmaCfg<NT>::kThreads, 1) q4q8_mma_kernel(const
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_addr(&empty[s]));
         ++gb;
-        return next_ok;
       };
-      uint32_t va[CW], vb[CW];
-      if constexpr (CW == 8) {
-        if (b0 < b1 && ok) ok = tmem_ld(gb, va);
-        for (uint32_t b = b0; b < b1 && ok; b += 2) {
-          ok = step(b, va, vb, true);
-          if (!ok || b + 1 >= b1) break;
-          ok = step(b + 1, vb, va, true);
-        }
-      } else {
-        // the 128-wide tile keeps one buffer (two would not fit its registers)
-        for (uint32_t b = b0; b < b1 && ok; ++b) {
-          ok = tmem_ld(gb, va);
-          if (ok) ok = step(b, va, vb, false);
-        }
+      uint32_t va[CW];
+      for (uint32_t b = b0; b < b1 && ok; ++b) {
+        ok = tmem_ld(gb, va);
+        if (ok) step(va);
       }
       tmem_ld_wait();
       const uint32_t row = mt * kTileM + 32 * q + lane;
@@ -373,7 +357,7 @@ __global__ void __launch_bounds__(MmaCfg<NT>::kThreads, 1) q4q8_mma_kernel(const
   __syncthreads();
   tc_fence_after();
   if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Cfg::kTmem) : "memory");
 }
 
 // y[t][r] = (resadd ? y[t][r] : 0) + sum over splits, added in split order.
@@ -446,9 +430,9 @@ cudaError_t mma_setup() {
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(q4q8_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem);
+  e = cudaFuncSetAttribute(q4q8_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmaCfg<128>::kDyn);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(q4q8_mma_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem);
+    e = cudaFuncSetAttribute(q4q8_mma_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, MmaCfg<32>::kDyn);
   return e;
 }
 
@@ -462,11 +446,12 @@ cudaError_t launch_q4q8_mma(const MmaGemmParams &p, cudaStream_t s) {
   // per-row arithmetic is the same for both widths
   const uint32_t nt_w = p.T <= 32 ? 32u : 128u;
   const uint64_t tiles = static_cast<uint64_t>(p.rows / kTileM) * ((p.T + nt_w - 1) / nt_w) * S;
-  const unsigned grid = static_cast<unsigned>(tiles < static_cast<uint64_t>(g_sm_count) ? tiles : g_sm_count);
+  const uint64_t slots = static_cast<uint64_t>(g_sm_count) * (nt_w == 32 ? MmaCfg<32>::kCtasPerSm : 1u);
+  const unsigned grid = static_cast<unsigned>(tiles < slots ? tiles : slots);
   if (nt_w == 32)
-    q4q8_mma_kernel<32><<<grid, MmaCfg<32>::kThreads, kDynSmem, s>>>(p);
+    q4q8_mma_kernel<32><<<grid, MmaCfg<32>::kThreads, MmaCfg<32>::kDyn, s>>>(p);
   else
-    q4q8_mma_kernel<128><<<grid, MmaCfg<128>::kThreads, kDynSmem, s>>>(p);
+    q4q8_mma_kernel<128><<<grid, MmaCfg<128>::kThreads, MmaCfg<128>::kDyn, s>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || S == 1) return e;
   const uint64_t n = static_cast<uint64_t>(p.rows) * p.T;
@@ -479,7 +464,9 @@ uint32_t mma_ksplit(uint32_t rows, uint32_t bpr) {
   // The split that minimises the blocks the busiest CTA streams: waves of
   // (weight tile, split) pairs over the SMs times the blocks of one split,
   // plus a few blocks' worth of per-tile start-up; at least 4 blocks a split.
-  const uint32_t n_mt = rows / kTileM, sms = g_sm_count > 0 ? static_cast<uint32_t>(g_sm_count) : 148u;
+  // CTA slots of the 32-wide tile (the split serves few tokens): two per SM
+  const uint32_t n_mt = rows / kTileM,
+                 sms = (g_sm_count > 0 ? static_cast<uint32_t>(g_sm_count) : 148u) * MmaCfg<32>::kCtasPerSm;
   if (n_mt == 0) return 1;
   const uint32_t s_max = std::min(kMmaMaxSplit, std::max(1u, bpr / 4));
   uint32_t best = 1;
