@@ -24,6 +24,17 @@ JSON line on rank 0.
 
 With --gpus N > 1 (launched under torchrun) every rank decodes its own
 replica (weak scaling); times are the max over ranks.
+
+Other workloads (--workload), each printing the same kind of line:
+  qwen3-8b          BASELINE config 2: cache filled to 4096 tokens, greedy
+                    steps; tensor parallel over the torchrun ranks; with
+                    --batch 16, sixteen sequences per step (zgpu_decode_batch,
+                    one GPU)
+  ds2               BASELINE config 3's model (MLA + MoE), one sequence;
+                    expert parallel over the torchrun ranks
+  prefill           BASELINE config 4: a 2048-token prompt (--batch 8: eight)
+  kquant            the GGUF-compat Q4_K / Q6_K GEMVs of one token at
+                    Qwen3-1.7B shape, HBM GB/s
 """
 from __future__ import annotations
 
