@@ -1,12 +1,12 @@
 """Generate the packer golden fixtures from the reference's own tools/silicatepack.py.
 
-Run in a checkout that has the reference tree (default /root/reference, or
---reference PATH).  Writes tests/golden/packer_golden.npz, which the CPU tests
+Run where the reference tree is available (--reference PATH, the directory
+holding tools/silicatepack.py's checkout).  Writes tests/golden/packer_golden.npz, which the CPU tests
 use to pin the oracle's block encoders, fp16 conversion and X4 permutation
 (and, through the oracle, the GPU quantiser).  The fixture is committed; the
 tests never read the reference tree.
 
-    python tests/golden/gen_packer_golden.py [--reference /root/reference]
+    python tests/golden/gen_packer_golden.py --reference <reference checkout>
 """
 from __future__ import annotations
 
@@ -25,7 +25,7 @@ OUT = Path(__file__).resolve().parent / "packer_golden.npz"
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="the reference checkout (holds tools/silicatepack.py)")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference) / "tools"))
     import silicatepack as sp  # the reference's packer, imported read-only
