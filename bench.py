@@ -57,10 +57,31 @@ METRIC = "decode tok/s, Qwen3-1.7B-shape Q4_0 b=1; GEMV HBM GB/s vs ~8 TB/s peak
 PUBLISHED_TOK_S = 194.5      # README.md:29 of the reference (EPYC 9354P, AVX-512, CPU only)
 PROMPT_LEN = 16
 SEED = 0
-# DRAM bytes (read + write) per decode step of the persistent step kernel, from
-# the ncu capture summarised in profiles/step_kernel_config0.md (None until
-# captured); the roofline's traffic is this times the steps of the launch.
+# DRAM bytes (read + write) per decode step of the persistent step kernel,
+# from one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum of a
+# timed decode launch, divided by its steps), together with a digest of the
+# kernel sources it was captured on.  When those sources change the figure is
+# withheld (roofline.traffic null) until it is captured again.
 NCU_TRAFFIC_PER_STEP = 1_125_293_824
+NCU_TRAFFIC_SOURCES = ("step.cu", "step.h", "gemv_body.cuh", "attn_body.cuh", "common.cuh", "layout.h")
+NCU_TRAFFIC_DIGEST = None
+
+
+def kernel_sources_digest() -> str:
+    import hashlib
+
+    h = hashlib.sha256()
+    for name in NCU_TRAFFIC_SOURCES:
+        h.update((ROOT / "zero_b200" / "csrc" / name).read_bytes())
+    return h.hexdigest()[:16]
+
+
+def measured_traffic_per_step():
+    """ncu's DRAM bytes per decode step, or None when the step kernel's
+    sources differ from those it was captured on."""
+    if NCU_TRAFFIC_PER_STEP and NCU_TRAFFIC_DIGEST and kernel_sources_digest() == NCU_TRAFFIC_DIGEST:
+        return NCU_TRAFFIC_PER_STEP
+    return None
 
 
 
@@ -220,12 +241,42 @@ def cpu_decode_sample(cfg, weights, prompt, steps: int, threads: int):
     return steps / dt, dt
 
 
+def cpu_synth():
+    """zero_b200/synth.py loaded by file path, not through the package (whose
+    import loads libzgpu), generating through the oracle library's build of
+    the same generator: the CPU arms load no GPU code and still get the
+    seeded bytes the GPU arm uses."""
+    import importlib.util
+
+    import oracle as O
+
+    name = "zero_b200_synth_cpu"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, ROOT / "zero_b200" / "synth.py")
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    mod.use_generator(O.LIB, "zo_")
+    return mod
+
+
+def synth_module(args):
+    """The weight generator: the package's for the GPU arm, the oracle-backed
+    copy for the reference arm."""
+    if args.impl == "reference":
+        return cpu_synth()
+    from zero_b200 import synth
+
+    return synth
+
+
 def run_reference(args, rank):
     """The reference arm: the reference's CPU decode path (restated, AVX-512 order)
     on the host cores, same config and metric."""
     if rank != 0:
         return
-    from zero_b200 import synth
+    synth = cpu_synth()
 
     cfg = synth.QWEN3_1_7B
     weights = synth.qwen3_weights(cfg, seed=SEED, x4=False)
@@ -263,7 +314,7 @@ def run_ds2(args, rank, world, local):
     import torch
 
     import zero_b200 as zb
-    from zero_b200 import synth
+    synth = synth_module(args)
 
     if args.impl == "reference":
         if rank == 0:
@@ -389,7 +440,7 @@ def run_qwen3_tp(args, rank, world, local):
     stage outputs cross NVLink inside the persistent step kernel (peer stores
     of tagged words), so a step is one kernel per GPU.  Strong scaling: one
     sequence, its weights split N ways."""
-    from zero_b200 import synth
+    synth = synth_module(args)
 
     cfg = synth.QWEN3_8B
     n_cpu_prompt, n_cpu_gen = 4, 4
@@ -516,7 +567,7 @@ def run_qwen3_batch(args, rank, world, local):
     projections and LM head over Q8_0 activation rows, the decode attention
     with a sequence grid dimension).  One GPU; value = B x K tokens over the
     device time of the K steps."""
-    from zero_b200 import synth
+    synth = synth_module(args)
 
     cfg = synth.QWEN3_8B
     B = args.batch
@@ -666,7 +717,7 @@ def run_prefill(args, rank, world, local):
     """BASELINE config 4 at batch 1: a 2048-token seeded prompt through the
     token-parallel prefill (tcgen05 int8 projections, causal attention writing
     the KV cache, LM head on the last token).  A step is one whole prefill."""
-    from zero_b200 import synth
+    synth = synth_module(args)
 
     cfg = synth.QWEN3_1_7B
     n_cpu = 64
@@ -820,7 +871,7 @@ def run_kquant(args, rank, world, local):
     197 GEMVs (28 layers x 7 + the LM head) through zgpu_linear_dispatch_device,
     captured once as a CUDA graph and replayed.  The 1.15 GB of weights is
     far above the 126 MB L2, so no flush is needed between steps."""
-    from zero_b200 import synth
+    synth = synth_module(args)
 
     if world > 1:
         raise SystemExit("the kquant workload runs on one GPU")
@@ -977,7 +1028,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     import zero_b200 as zb
-    from zero_b200 import synth
+    synth = synth_module(args)
 
     cfg = synth.QWEN3_1_7B
     weights = synth.qwen3_weights(cfg, seed=SEED)
@@ -1045,6 +1096,7 @@ def main():
     kv_bytes = sum(kv_row_bytes * (PROMPT_LEN + i + 1) for i in range(args.steps))
     launch_bytes = args.steps * step_bytes + kv_bytes
     step_gbs = launch_bytes / (dec_ms / 1000.0) / 1e9
+    traffic_step = measured_traffic_per_step()
     # secondary: the standalone Q4_0 GEMV 2048 -> 6144 over the 56 gate/up
     # tensors (396 MB per sweep > L2), captured into a CUDA graph on a torch
     # stream and timed with CUDA events on that stream
@@ -1113,7 +1165,9 @@ def main():
                                    if gpu_launches == 1 else "per-op decode kernels (whole step)",
                          "achieved": round(step_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(step_gbs / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
-                         "traffic": (NCU_TRAFFIC_PER_STEP * args.steps) if NCU_TRAFFIC_PER_STEP else None,
+                         "traffic": (traffic_step * args.steps) if traffic_step else None,
+                         "traffic_source": "ncu dram bytes per step x steps" if traffic_step else
+                                           "not captured on the current step-kernel sources",
                          "algorithmic_bytes": launch_bytes,
                          "avg_launch_us": round(dec_ms * 1000 / max(gpu_launches, 1), 1),
                          "gemv_2048x6144": {"achieved": round(gemv_gbs, 1) if gemv_gbs else None,

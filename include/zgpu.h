@@ -243,7 +243,9 @@ zgpu_status zgpu_gqa_attention_decode_device(zgpu_ctx *ctx, zgpu_kv *kv, uint32_
  * 32000 tokens), and n_kv at most 256.  Larger requests return
  * ZGPU_ERR_INVALID_ARG with a message and launch nothing.  The first call on
  * a device looks up the array's device address, so make that first call
- * before any stream capture.  All calls on a device share the one array, and
+ * before any stream capture.  The address is kept until the process exits:
+ * resetting the device (cudaDeviceReset) or destroying its primary context
+ * after that first call is not supported, since the array would move.  All calls on a device share the one array, and
  * each call clears the counters on its stream.  Calls that overlap on the GPU
  * race, whether from other streams or other contexts on the same device. */
 zgpu_status zgpu_gqa_attention_decode_noalloc(zgpu_ctx *ctx, zgpu_kv *kv, uint32_t layer,

@@ -33,7 +33,8 @@ def build() -> Path:
 
 
 def _load() -> C.CDLL:
-    srcs = [HERE / "zoracle.c", HERE / "zoracle_ds2.c", HERE / "zoracle.h"]
+    srcs = [HERE / "zoracle.c", HERE / "zoracle_ds2.c", HERE / "zoracle.h", HERE / "Makefile",
+            HERE.parent / "zero_b200" / "csrc" / "synth.cpp"]
     if not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < max(p.stat().st_mtime for p in srcs):
         build()
     lib = C.CDLL(str(LIB_PATH))
@@ -79,6 +80,11 @@ def _load() -> C.CDLL:
         "zo_rope_apply_avx512": (None, [_f32p, _f32p, _f32p, sz]),
         "zo_have_avx512": (C.c_int, []),
         "zo_run_create": (C.c_void_p, [C.c_void_p, C.c_uint32, C.c_int, C.c_int, C.c_int]),
+        "zo_synth_q4_0": (None, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_void_p]),
+        "zo_synth_q8_0": (None, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_void_p]),
+        "zo_synth_f32": (None, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_float, C.c_void_p]),
+        "zo_synth_tokens": (None, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint32, C.c_void_p]),
+        "zo_pack_x4": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint64, C.c_uint32]),
         "zo_run_destroy": (None, [C.c_void_p]),
         "zo_run_forward": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, _f32p]),
         "zo_run_lm_head": (C.c_int, [C.c_void_p, _u32p, _f32p]),

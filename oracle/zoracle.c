@@ -15,6 +15,10 @@
 #include <string.h>
 #include <float.h>
 #include <pthread.h>
+#include <sched.h>
+#include <stdatomic.h>
+#include <stdio.h>
+#include <time.h>
 #include <unistd.h>
 #if defined(__x86_64__)
 #include <immintrin.h>
@@ -543,6 +547,193 @@ static void parallel_units(size_t units, int threads, void (*fn)(void *, size_t,
   for (int i = 1; i < n; ++i) pthread_join(tid[i], NULL);
 }
 
+
+/* ----------------------------------------------------------------------
+ * Persistent dispatcher for the timed CPU baseline, after the reference's
+ * SMP matmul dispatch (smp.rs:1559-1700): the worker threads are created
+ * once per run, each pinned to its own physical core, and park on a shared
+ * epoch word.  A dispatch publishes (fn, ctx, units), bumps the epoch with
+ * release semantics (the wake signal), runs participant 0's range on the
+ * calling thread and waits until every worker has arrived.  Ranges are the
+ * reference's closed-form even split in whole units (row_range_for,
+ * smp_partition.rs:143-167), so each row is computed exactly as the
+ * single-threaded kernel computes it.
+ * ---------------------------------------------------------------------- */
+#define ZO_POOL_MAX 256
+
+typedef void (*zo_part_fn)(void *ctx, size_t u0, size_t u1, int part);
+
+struct zo_pool {
+  int n;                                 /* participants, the caller is 0 */
+  pthread_t tid[ZO_POOL_MAX];
+  int cpu[ZO_POOL_MAX];                  /* pinned logical CPU (-1: not pinned) */
+  _Atomic unsigned long long epoch;
+  _Atomic int arrived;
+  _Atomic int quit;
+  zo_part_fn fn;
+  void *ctx;
+  size_t units;
+  int caller_cpu;                        /* participant 0's core (-1: not pinned) */
+};
+
+typedef struct {
+  struct zo_pool *p;
+  int part;
+} zo_worker_arg;
+
+static void zo_range_for(size_t units, int n, int i, size_t *u0, size_t *u1) {
+  size_t base = units / (size_t)n, extra = units % (size_t)n;
+  size_t s = (size_t)i * base + ((size_t)i < extra ? (size_t)i : extra);
+  *u0 = s;
+  *u1 = s + base + ((size_t)i < extra ? 1 : 0);
+}
+
+static int zo_read_int(const char *path) {
+  FILE *f = fopen(path, "r");
+  int v = -1;
+  if (f) {
+    if (fscanf(f, "%d", &v) != 1) v = -1;
+    fclose(f);
+  }
+  return v;
+}
+
+/* One logical CPU per physical core (the lowest-numbered sibling) among the
+ * CPUs this process may run on; returns how many were found. */
+static int zo_physical_cpus(int *out, int cap) {
+  cpu_set_t allowed;
+  if (sched_getaffinity(0, sizeof(allowed), &allowed) != 0) return 0;
+  int n = 0;
+  int keys[4096];
+  for (int c = 0; c < CPU_SETSIZE && n < cap; ++c) {
+    if (!CPU_ISSET(c, &allowed)) continue;
+    char path[128];
+    snprintf(path, sizeof path, "/sys/devices/system/cpu/cpu%d/topology/core_id", c);
+    int core = zo_read_int(path);
+    snprintf(path, sizeof path, "/sys/devices/system/cpu/cpu%d/topology/physical_package_id", c);
+    int pkg = zo_read_int(path);
+    int key = (core < 0 || pkg < 0) ? -1 - c : pkg * 65536 + core;
+    int seen = 0;
+    for (int k = 0; k < n; ++k) seen |= keys[k] == key;
+    if (!seen) {
+      keys[n] = key;
+      out[n++] = c;
+    }
+  }
+  return n;
+}
+
+/* The calling thread runs participant 0 on the first physical core while a
+ * forward or LM-head call is in flight, and gets its own affinity back at
+ * the end of the call (threads it creates later must not inherit the pin). */
+typedef struct {
+  cpu_set_t saved;
+  int active;
+} zo_caller_pin;
+
+static void zo_caller_pin_begin(const struct zo_pool *p, zo_caller_pin *cp);
+static void zo_caller_pin_end(zo_caller_pin *cp);
+
+static void zo_pin(int cpu) {
+  if (cpu < 0) return;
+  cpu_set_t m;
+  CPU_ZERO(&m);
+  CPU_SET(cpu, &m);
+  pthread_setaffinity_np(pthread_self(), sizeof(m), &m);
+}
+
+static void *zo_worker_main(void *a) {
+  zo_worker_arg *wa = (zo_worker_arg *)a;
+  struct zo_pool *p = wa->p;
+  const int part = wa->part;
+  free(wa);
+  zo_pin(p->cpu[part]);
+  unsigned long long seen = 0;
+  for (;;) {
+    unsigned long long e;
+    unsigned spins = 0;
+    while ((e = atomic_load_explicit(&p->epoch, memory_order_acquire)) == seen) {
+      if (atomic_load_explicit(&p->quit, memory_order_acquire)) return NULL;
+      _mm_pause();
+      if (++spins > (1u << 20)) {          /* parked for a while: stop burning the core */
+        struct timespec ts = {0, 20000};
+        nanosleep(&ts, NULL);
+        spins = 1u << 19;
+      }
+    }
+    seen = e;
+    size_t u0, u1;
+    zo_range_for(p->units, p->n, part, &u0, &u1);
+    if (u0 < u1) p->fn(p->ctx, u0, u1, part);
+    atomic_fetch_add_explicit(&p->arrived, 1, memory_order_acq_rel);
+  }
+}
+
+zo_pool *zo_pool_create(int threads) {
+  struct zo_pool *p = (struct zo_pool *)calloc(1, sizeof(struct zo_pool));
+  if (!p) return NULL;
+  int cpus[ZO_POOL_MAX];
+  int ncpu = zo_physical_cpus(cpus, ZO_POOL_MAX);
+  int n = threads > 0 ? threads : (ncpu > 0 ? ncpu : zo_ncores(0));
+  if (n > ZO_POOL_MAX) n = ZO_POOL_MAX;
+  if (n < 1) n = 1;
+  p->n = n;
+  /* workers take the physical cores after the first, which the calling
+   * thread takes during a call (zo_caller_pin_begin) */
+  for (int i = 0; i < n; ++i) p->cpu[i] = (ncpu >= n && i > 0) ? cpus[i] : -1;
+  p->caller_cpu = ncpu >= n ? cpus[0] : -1;
+  for (int i = 1; i < n; ++i) {
+    zo_worker_arg *wa = (zo_worker_arg *)malloc(sizeof(zo_worker_arg));
+    wa->p = p;
+    wa->part = i;
+    if (pthread_create(&p->tid[i], NULL, zo_worker_main, wa) != 0) {
+      free(wa);
+      p->n = i;                              /* run with the workers that started */
+      break;
+    }
+  }
+  return p;
+}
+
+static void zo_caller_pin_begin(const struct zo_pool *p, zo_caller_pin *cp) {
+  cp->active = 0;
+  if (!p || p->n <= 1 || p->caller_cpu < 0) return;
+  if (pthread_getaffinity_np(pthread_self(), sizeof(cp->saved), &cp->saved) != 0) return;
+  zo_pin(p->caller_cpu);
+  cp->active = 1;
+}
+
+static void zo_caller_pin_end(zo_caller_pin *cp) {
+  if (cp->active) pthread_setaffinity_np(pthread_self(), sizeof(cp->saved), &cp->saved);
+}
+
+void zo_pool_destroy(zo_pool *p) {
+  if (!p) return;
+  atomic_store_explicit(&p->quit, 1, memory_order_release);
+  for (int i = 1; i < p->n; ++i) pthread_join(p->tid[i], NULL);
+  free(p);
+}
+
+int zo_pool_size(const zo_pool *p) { return p ? p->n : 1; }
+
+/* One dispatch: fn over [0, units) split across the participants; returns
+ * once every participant has finished its range. */
+static void zo_pool_run(struct zo_pool *p, size_t units, zo_part_fn fn, void *ctx) {
+  if (!p || p->n <= 1) {
+    if (units) fn(ctx, 0, units, 0);
+    return;
+  }
+  p->fn = fn;
+  p->ctx = ctx;
+  p->units = units;
+  atomic_store_explicit(&p->arrived, 0, memory_order_relaxed);
+  atomic_fetch_add_explicit(&p->epoch, 1, memory_order_release);
+  size_t u0, u1;
+  zo_range_for(units, p->n, 0, &u0, &u1);
+  if (u0 < u1) fn(ctx, u0, u1, 0);
+  while (atomic_load_explicit(&p->arrived, memory_order_acquire) < p->n - 1) _mm_pause();
+}
+
 typedef struct {
   const float *x;
   const uint8_t *w;
@@ -735,16 +926,13 @@ void zo_rope_apply_avx512(float *qk, const float *c, const float *s, size_t half
  * then per q head scores q.k * (1/sqrt(hd)), softmax (attention.rs:48) and
  * sum_t p_t v_t.  k_block / v_block are this layer's K and V blocks
  * [max_tokens][n_kv*hd]; work holds (n_q + n_kv + 1)*hd + max_tokens floats. */
-int zo_gqa_attention_decode(const float *q, const float *k, const float *v, const float *q_norm,
-                            const float *k_norm, const float *inv_freqs, float *k_block,
-                            float *v_block, uint32_t pos, uint32_t max_tokens, uint32_t n_q,
-                            uint32_t n_kv, uint32_t hd, float eps, int order, float *work,
-                            float *out) {
-  if (pos >= max_tokens) return ZO_ERR_KV_TOKEN_OUT_OF_RANGE;
-  if (n_kv == 0 || n_q % n_kv || hd % 2 || hd > 512) return ZO_ERR_ARG;
-  const size_t half = hd / 2, kvd = (size_t)n_kv * hd, gqa = n_q / n_kv, total = (size_t)pos + 1;
-  const float scale = 1.0f / sqrtf((float)hd);
-  float *qo = work, *ko = qo + (size_t)n_q * hd, *head = ko + kvd, *sb = head + hd;
+/* Steps 2-3 (QK RMSNorm, RoPE at pos, store_kv) of the decode attention
+ * below; qo / ko receive the rotated q and k. */
+static void attn_prepare(const float *q, const float *k, const float *v, const float *q_norm,
+                         const float *k_norm, const float *inv_freqs, float *k_block, float *v_block,
+                         uint32_t pos, uint32_t n_q, uint32_t n_kv, uint32_t hd, float eps, int order,
+                         float *qo, float *ko) {
+  const size_t half = hd / 2, kvd = (size_t)n_kv * hd;
   float cos_lut[256], sin_lut[256];
   if (order == 1) zo_rope_sincos_lut_avx512(pos, inv_freqs, cos_lut, sin_lut, half);
   for (size_t h = 0; h < n_q; ++h) zo_rmsnorm(q + h * hd, q_norm, qo + h * hd, hd, eps);
@@ -759,27 +947,49 @@ int zo_gqa_attention_decode(const float *q, const float *k, const float *v, cons
   }
   memcpy(k_block + (size_t)pos * kvd, ko, kvd * 4);
   memcpy(v_block + (size_t)pos * kvd, v, kvd * 4);
+}
+
+/* Steps 4-5 for q head qh (attn_heads_kernel, inference_avx512.rs:1459-1512):
+ * scores into sb, softmax, then sum_t p_t v_t accumulated into out_head. */
+static int attn_head(const float *qo, const float *k_block, const float *v_block, size_t qh, size_t total,
+                     uint32_t n_q, uint32_t n_kv, uint32_t hd, int order, float *sb, float *out_head) {
+  const size_t kvd = (size_t)n_kv * hd, kh = qh / (n_q / n_kv);
+  const float scale = 1.0f / sqrtf((float)hd);
+  const float *qv = qo + qh * hd;
+  for (size_t t = 0; t < total; ++t) {
+    const float *kt = k_block + t * kvd + kh * hd;
+    if (order == 1) {
+      sb[t] = zo_dot_product_avx512(qv, kt, hd) * scale;
+    } else {
+      float dot = 0.0f;
+      for (size_t i = 0; i < hd; ++i) dot += qv[i] * kt[i];
+      sb[t] = dot * scale;
+    }
+  }
+  int st = zo_softmax(sb, total);
+  if (st) return st;
+  memset(out_head, 0, hd * 4);
+  for (size_t t = 0; t < total; ++t) {
+    const float *vt = v_block + t * kvd + kh * hd;
+    if (order == 1) zo_weighted_add_avx512(sb[t], vt, out_head, hd);
+    else for (size_t i = 0; i < hd; ++i) out_head[i] += sb[t] * vt[i];
+  }
+  return ZO_OK;
+}
+
+int zo_gqa_attention_decode(const float *q, const float *k, const float *v, const float *q_norm,
+                            const float *k_norm, const float *inv_freqs, float *k_block,
+                            float *v_block, uint32_t pos, uint32_t max_tokens, uint32_t n_q,
+                            uint32_t n_kv, uint32_t hd, float eps, int order, float *work,
+                            float *out) {
+  if (pos >= max_tokens) return ZO_ERR_KV_TOKEN_OUT_OF_RANGE;
+  if (n_kv == 0 || n_q % n_kv || hd % 2 || hd > 512) return ZO_ERR_ARG;
+  const size_t kvd = (size_t)n_kv * hd, total = (size_t)pos + 1;
+  float *qo = work, *ko = qo + (size_t)n_q * hd, *head = ko + kvd, *sb = head + hd;
+  attn_prepare(q, k, v, q_norm, k_norm, inv_freqs, k_block, v_block, pos, n_q, n_kv, hd, eps, order, qo, ko);
   for (size_t qh = 0; qh < n_q; ++qh) {
-    size_t kh = qh / gqa;
-    const float *qv = qo + qh * hd;
-    for (size_t t = 0; t < total; ++t) {
-      const float *kt = k_block + t * kvd + kh * hd;
-      if (order == 1) {
-        sb[t] = zo_dot_product_avx512(qv, kt, hd) * scale;
-      } else {
-        float dot = 0.0f;
-        for (size_t i = 0; i < hd; ++i) dot += qv[i] * kt[i];
-        sb[t] = dot * scale;
-      }
-    }
-    int st = zo_softmax(sb, total);
+    int st = attn_head(qo, k_block, v_block, qh, total, n_q, n_kv, hd, order, sb, head);
     if (st) return st;
-    memset(head, 0, hd * 4);
-    for (size_t t = 0; t < total; ++t) {
-      const float *vt = v_block + t * kvd + kh * hd;
-      if (order == 1) zo_weighted_add_avx512(sb[t], vt, head, hd);
-      else for (size_t i = 0; i < hd; ++i) head[i] += sb[t] * vt[i];
-    }
     memcpy(out + qh * hd, head, hd * 4);
   }
   return ZO_OK;
@@ -798,6 +1008,7 @@ struct zo_run {
   float *attn_work;                            /* zo_gqa_attention_decode workspace */
   uint8_t **x4;                                /* per-layer X4 copies for the AVX path */
   uint8_t *out_x4;
+  zo_pool *pool;                               /* persistent workers (AVX order, threads != 1) */
 };
 
 static uint8_t *make_x4(const uint8_t *plain, size_t rows, size_t cols, int q) {
@@ -847,12 +1058,14 @@ zo_run *zo_run_create(const zo_qwen3 *m, uint32_t max_tokens, int order, int thr
       x[6] = make_x4(L->ffn_down, H, F, ZO_Q4_0);
     }
     r->out_x4 = make_x4(m->output, m->vocab_padded, H, m->output_quant);
+    if (threads != 1) r->pool = zo_pool_create(threads);
   }
   return r;
 }
 
 void zo_run_destroy(zo_run *r) {
   if (!r) return;
+  zo_pool_destroy(r->pool);
   if (r->x4) {
     for (uint32_t i = 0; i < r->m->n_layers * 7; ++i) free(r->x4[i]);
     free(r->x4);
@@ -872,6 +1085,96 @@ const float *zo_run_kv(const zo_run *r) { return r->kv; }
  * prefill path, whose batched matmuls quantise their activations; mode 2:
  * the Q8_0 LM head too (zo_linear_q8_0_q8act), the batched decode path. */
 void zo_run_set_q8act(zo_run *r, int on) { r->q8act = on; }
+
+/* ----------------------------------------------------------------------
+ * Fused dispatches of the AVX-512 step on the persistent workers.
+ *   linear_fused_dispatch (inference_avx512.rs:890-945): several X4 tensors
+ *     that read the same input (Q|K|V, gate|up) as one virtual row space of
+ *     4-row groups, split once across the participants;
+ *   lm_head_linear_argmax_dispatch (:1093-1118): the LM-head rows and, per
+ *     participant, the first maximum of the rows it wrote, merged with the
+ *     reference's rule (lm_argmax_propose, :1027-1044: the larger value
+ *     wins, equal values go to the smaller index);
+ *   attn_heads_kernel (:1459-1512): q heads split across the participants.
+ * Every row and head is computed by the same code as the single-threaded
+ * path, so the results are identical whatever the thread count.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  const uint8_t *x4;
+  float *out;
+  size_t groups;
+} zo_seg;
+
+typedef struct {
+  const float *x;
+  size_t bpr;
+  int quant, simd, argmax;
+  int nseg;
+  zo_seg seg[4];
+  float best_v[ZO_POOL_MAX];
+  size_t best_i[ZO_POOL_MAX];
+} zo_fused_ctx;
+
+static void fused_groups(void *p, size_t g0, size_t g1, int part) {
+  zo_fused_ctx *c = (zo_fused_ctx *)p;
+  const size_t gb = (c->quant == ZO_Q4_0 ? 72 : 136) * c->bpr;
+  size_t base = 0;
+  for (int s = 0; s < c->nseg; ++s) {
+    const zo_seg *sg = &c->seg[s];
+    size_t lo = g0 > base ? g0 : base, hi = g1 < base + sg->groups ? g1 : base + sg->groups;
+    for (size_t g = lo; g < hi; ++g) {
+      const size_t lg = g - base;
+      const uint8_t *grp = sg->x4 + lg * gb;
+      float *o = sg->out + 4 * lg;
+#if defined(__x86_64__)
+      if (c->simd) {
+        if (c->quant == ZO_Q4_0) rows4_q4_avx512(c->x, c->bpr, grp, o);
+        else rows4_q8_avx512(c->x, c->bpr, grp, o);
+        continue;
+      }
+#endif
+      for (int r = 0; r < 4; ++r)
+        o[r] = c->quant == ZO_Q4_0 ? row_q4_emul(c->x, c->bpr, grp, 72, 2 * r, 8 + 16 * r)
+                                   : row_q8_emul(c->x, c->bpr, grp, 136, 2 * r, 8 + 32 * r);
+    }
+    base += sg->groups;
+  }
+  if (c->argmax) {   /* first maximum of this participant's rows of segment 0 */
+    const float *v = c->seg[0].out;
+    float mx = -INFINITY;
+    size_t idx = 4 * g0;
+    for (size_t i = 4 * g0; i < 4 * g1; ++i)
+      if (v[i] > mx) { mx = v[i]; idx = i; }
+    c->best_v[part] = mx;
+    c->best_i[part] = idx;
+  }
+}
+
+static void fused_dispatch(zo_run *r, zo_fused_ctx *c) {
+  size_t groups = 0;
+  for (int s = 0; s < c->nseg; ++s) groups += c->seg[s].groups;
+  c->simd = r->simd && zo_have_avx512();
+  if (c->argmax)
+    for (int i = 0; i < ZO_POOL_MAX; ++i) { c->best_v[i] = -INFINITY; c->best_i[i] = (size_t)-1; }
+  zo_pool_run(r->pool, groups, fused_groups, c);
+}
+
+typedef struct {
+  const float *qo, *k_block, *v_block;
+  size_t total, max_tokens;
+  uint32_t n_q, n_kv, hd;
+  float *score, *out;
+  int err[ZO_POOL_MAX];
+} zo_heads_ctx;
+
+static void heads_part(void *p, size_t h0, size_t h1, int part) {
+  zo_heads_ctx *c = (zo_heads_ctx *)p;
+  for (size_t h = h0; h < h1; ++h) {
+    int st = attn_head(c->qo, c->k_block, c->v_block, h, c->total, c->n_q, c->n_kv, c->hd, 1,
+                       c->score + h * c->max_tokens, c->out + h * c->hd);
+    if (st && !c->err[part]) c->err[part] = st;
+  }
+}
 
 static void lin(zo_run *r, const float *x, const uint8_t *plain, const uint8_t *x4, float *out,
                 size_t in, size_t outd, int quant) {
@@ -897,7 +1200,26 @@ static void lin(zo_run *r, const float *x, const uint8_t *plain, const uint8_t *
 /* forward_pass.rs:515-631 (order 0) and inference_avx512.rs:1826-1987 with
  * gqa_attention_single_token_avx512 :1527-1810 and mlp_swiglu_avx512
  * :1280-1340 (order 1). */
+static int run_forward(zo_run *r, uint32_t token, uint32_t pos, float *hidden_out);
+static int run_lm_head(zo_run *r, uint32_t *token_out, float *logits_out);
+
 int zo_run_forward(zo_run *r, uint32_t token, uint32_t pos, float *hidden_out) {
+  zo_caller_pin cp;
+  zo_caller_pin_begin(r->pool, &cp);
+  int st = run_forward(r, token, pos, hidden_out);
+  zo_caller_pin_end(&cp);
+  return st;
+}
+
+int zo_run_lm_head(zo_run *r, uint32_t *token_out, float *logits_out) {
+  zo_caller_pin cp;
+  zo_caller_pin_begin(r->pool, &cp);
+  int st = run_lm_head(r, token_out, logits_out);
+  zo_caller_pin_end(&cp);
+  return st;
+}
+
+static int run_forward(zo_run *r, uint32_t token, uint32_t pos, float *hidden_out) {
   const zo_qwen3 *m = r->m;
   size_t H = m->hidden, F = m->ffn, hd = m->head_dim;
   size_t nq = m->n_q_heads, nkv = m->n_kv_heads, qd = nq * hd, kvd = nkv * hd;
@@ -921,22 +1243,46 @@ int zo_run_forward(zo_run *r, uint32_t token, uint32_t pos, float *hidden_out) {
   for (uint32_t li = 0; li < m->n_layers; ++li) {
     const zo_qwen3_layer *L = &m->layers[li];
     uint8_t **x4 = r->order == 1 ? r->x4 + 7 * li : NULL;
+    const int fused = r->pool && x4 && !r->q8act;
     zo_rmsnorm(r->hidden, L->attn_norm, r->norm, H, m->rms_eps);
-    lin(r, r->norm, L->attn_q, x4 ? x4[0] : NULL, r->q, H, qd, ZO_Q4_0);
-    lin(r, r->norm, L->attn_k, x4 ? x4[1] : NULL, r->k, H, kvd, ZO_Q4_0);
-    lin(r, r->norm, L->attn_v, x4 ? x4[2] : NULL, r->v, H, kvd, ZO_Q4_0);
+    if (fused) {
+      zo_fused_ctx c = {.x = r->norm, .bpr = H / 32, .quant = ZO_Q4_0, .nseg = 3,
+                        .seg = {{x4[0], r->q, qd / 4}, {x4[1], r->k, kvd / 4}, {x4[2], r->v, kvd / 4}}};
+      fused_dispatch(r, &c);
+    } else {
+      lin(r, r->norm, L->attn_q, x4 ? x4[0] : NULL, r->q, H, qd, ZO_Q4_0);
+      lin(r, r->norm, L->attn_k, x4 ? x4[1] : NULL, r->k, H, kvd, ZO_Q4_0);
+      lin(r, r->norm, L->attn_v, x4 ? x4[2] : NULL, r->v, H, kvd, ZO_Q4_0);
+    }
     {
       float *kbase = r->kv + li * layer_stride;
-      int st = zo_gqa_attention_decode(r->q, r->k, r->v, L->q_norm, L->k_norm, r->inv_freqs, kbase,
-                                       kbase + block, pos, r->max_tokens, (uint32_t)nq, (uint32_t)nkv,
-                                       (uint32_t)hd, m->rms_eps, r->order, r->attn_work, r->concat);
-      if (st) return st;
+      if (fused) {
+        attn_prepare(r->q, r->k, r->v, L->q_norm, L->k_norm, r->inv_freqs, kbase, kbase + block, pos,
+                     (uint32_t)nq, (uint32_t)nkv, (uint32_t)hd, m->rms_eps, 1, r->qo, r->ko);
+        zo_heads_ctx hc = {.qo = r->qo, .k_block = kbase, .v_block = kbase + block, .total = (size_t)pos + 1,
+                           .max_tokens = r->max_tokens, .n_q = (uint32_t)nq, .n_kv = (uint32_t)nkv,
+                           .hd = (uint32_t)hd, .score = r->score, .out = r->concat};
+        zo_pool_run(r->pool, nq, heads_part, &hc);
+        for (int i = 0; i < ZO_POOL_MAX; ++i)
+          if (hc.err[i]) return hc.err[i];
+      } else {
+        int st = zo_gqa_attention_decode(r->q, r->k, r->v, L->q_norm, L->k_norm, r->inv_freqs, kbase,
+                                         kbase + block, pos, r->max_tokens, (uint32_t)nq, (uint32_t)nkv,
+                                         (uint32_t)hd, m->rms_eps, r->order, r->attn_work, r->concat);
+        if (st) return st;
+      }
     }
     lin(r, r->concat, L->attn_o, x4 ? x4[3] : NULL, r->attn_out, qd, H, ZO_Q4_0);
     for (size_t i = 0; i < H; ++i) r->hidden[i] += r->attn_out[i];
     zo_rmsnorm(r->hidden, L->ffn_norm, r->norm, H, m->rms_eps);
-    lin(r, r->norm, L->ffn_gate, x4 ? x4[4] : NULL, r->gate, H, F, ZO_Q4_0);
-    lin(r, r->norm, L->ffn_up, x4 ? x4[5] : NULL, r->up, H, F, ZO_Q4_0);
+    if (fused) {
+      zo_fused_ctx c = {.x = r->norm, .bpr = H / 32, .quant = ZO_Q4_0, .nseg = 2,
+                        .seg = {{x4[4], r->gate, F / 4}, {x4[5], r->up, F / 4}}};
+      fused_dispatch(r, &c);
+    } else {
+      lin(r, r->norm, L->ffn_gate, x4 ? x4[4] : NULL, r->gate, H, F, ZO_Q4_0);
+      lin(r, r->norm, L->ffn_up, x4 ? x4[5] : NULL, r->up, H, F, ZO_Q4_0);
+    }
     if (r->order == 1) {
       zo_silu_mul_avx512(r->gate, r->up, r->hmlp, F);
     } else {
@@ -954,16 +1300,26 @@ int zo_run_forward(zo_run *r, uint32_t token, uint32_t pos, float *hidden_out) {
 /* lm_head.rs:98-166 (order 0) / inference_avx512.rs:1200-1270 (order 1):
  * final RMSNorm, logits over the padded vocab, first-max argmax, then the
  * non-finite and padding-region checks. */
-int zo_run_lm_head(zo_run *r, uint32_t *token_out, float *logits_out) {
+static int run_lm_head(zo_run *r, uint32_t *token_out, float *logits_out) {
   const zo_qwen3 *m = r->m;
   size_t H = m->hidden, V = m->vocab_padded;
   zo_rmsnorm(r->hidden, m->output_norm, r->norm, H, m->rms_eps);
-  lin(r, r->norm, m->output, r->out_x4, r->logits, H, V, m->output_quant);
   float mx = -INFINITY;
   size_t idx = 0;
-  if (r->order == 1) {
+  if (r->pool && r->out_x4 && !r->q8act && V % 4 == 0) {
+    zo_fused_ctx c = {.x = r->norm, .bpr = H / 32, .quant = m->output_quant, .argmax = 1, .nseg = 1,
+                      .seg = {{r->out_x4, r->logits, V / 4}}};
+    fused_dispatch(r, &c);
+    mx = -INFINITY;
+    idx = (size_t)-1;
+    for (int i = 0; i < zo_pool_size(r->pool); ++i)
+      if (c.best_v[i] > mx || (c.best_v[i] == mx && c.best_i[i] < idx)) { mx = c.best_v[i]; idx = c.best_i[i]; }
+    if (idx == (size_t)-1) idx = 0;
+  } else if (r->order == 1) {
+    lin(r, r->norm, m->output, r->out_x4, r->logits, H, V, m->output_quant);
     idx = zo_argmax_avx512(r->logits, V, &mx);
   } else {
+    lin(r, r->norm, m->output, r->out_x4, r->logits, H, V, m->output_quant);
     for (size_t i = 0; i < V; ++i) if (r->logits[i] > mx) { mx = r->logits[i]; idx = i; }
   }
   if (logits_out) memcpy(logits_out, r->logits, V * 4);

@@ -163,6 +163,14 @@ typedef struct zo_qwen3 {
 /* order: 0 = scalar crate path (forward_pass.rs:515), 1 = AVX-512 kernel path
  * (inference_avx512.rs:1826).  The run keeps its own f32 KV cache with the
  * kv_cache.rs:100 layout. */
+/* Persistent dispatcher of the timed baseline: threads <= 0 -> one
+ * participant per physical core the process may use.  Worker threads are
+ * pinned one per core; the calling thread is participant 0. */
+typedef struct zo_pool zo_pool;
+zo_pool *zo_pool_create(int threads);
+void     zo_pool_destroy(zo_pool *p);
+int      zo_pool_size(const zo_pool *p);
+
 typedef struct zo_run zo_run;
 zo_run *zo_run_create(const zo_qwen3 *m, uint32_t max_tokens, int order, int threads, int simd);
 void    zo_run_destroy(zo_run *r);

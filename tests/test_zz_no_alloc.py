@@ -8,8 +8,9 @@ allocator.  Instead of context-owned scratch it uses a fixed array in the
 library's device image, shared by every call on the device.
 
 The test runs two decode steps in a row through both entry points, each on
-its own copy of the same KV cache, and holds the outputs to the relative L2
-tolerance the other attention tests use.  The context is 1024 tokens (four
+its own copy of the same KV cache.  Both run the same kernel with the same
+launch shape and a fixed reduction order, so the outputs and the appended
+cache rows must be equal bit for bit.  The context is 1024 tokens (four
 splits), so the second call finds the partials and counters that the first
 call left in the shared array.  This file sorts last so that a stop at the
 first failure has already run every other test.
@@ -28,13 +29,6 @@ pytestmark = pytest.mark.gpu
 HD = 128
 EPS = 1e-6
 THETA = 1e6
-REL_L2 = 1e-5
-
-
-def _rel_l2(a, b):
-    a = a.astype(np.float64)
-    b = b.astype(np.float64)
-    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
 def _call(fn, ctx, kv, pos, n_q, bufs, stream):
@@ -74,10 +68,11 @@ def test_noalloc_attention_matches_allocating_entry_point(ctx):
             ctx.synchronize()
             ref, new = d_ref.cpu().numpy(), d_new.cpu().numpy()
             assert np.isfinite(ref).all()
-            assert _rel_l2(new, ref) <= REL_L2, f"call at pos {pos}"
+            assert np.array_equal(new.view(np.uint32), ref.view(np.uint32)), f"call at pos {pos}"
             k_ref, v_ref = kv_ref.read(0, pos + 1)
             k_new, v_new = kv_new.read(0, pos + 1)
-            assert _rel_l2(k_new, k_ref) <= REL_L2 and _rel_l2(v_new, v_ref) <= REL_L2
+            assert np.array_equal(k_new.view(np.uint32), k_ref.view(np.uint32))
+            assert np.array_equal(v_new.view(np.uint32), v_ref.view(np.uint32))
     finally:
         kv_ref.close()
         kv_new.close()

@@ -44,7 +44,8 @@ std::mutex g_mu;
 void *g_addr[kMaxDevices] = {};
 
 // Device address of g_attn_scratch on `device`, looked up once per device
-// with that device current.
+// with that device current and kept until the process exits (a device reset
+// after the first call is not supported: the module would reload elsewhere).
 zgpu_status scratch_address(zgpu_ctx *ctx, int device, float **out) {
   if (device < 0 || device >= kMaxDevices)
     return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "attention (no-alloc): device index above 63");

@@ -8,6 +8,11 @@
 //   q8_0: per block d = fp16(scale), 32 bytes mapped to -127..127;
 //   f32:  N(mean, sigma) through Box-Muller on two uniforms.
 // The X4 writer restates tools/silicatepack.py:982-1022.
+//
+// The same source is also compiled into the CPU oracle's library with
+// ZSYNTH_ORACLE defined, which names the entry points zo_synth_* and
+// zo_pack_x4: the CPU reference arm then generates identical bytes without
+// loading this library.
 #include <cmath>
 #include <cstring>
 #include <thread>
@@ -78,9 +83,15 @@ void parallel_rows(uint64_t rows, F &&f) {
 
 }  // namespace
 
+#ifdef ZSYNTH_ORACLE
+#define ZSYNTH_NAME(n) zo_##n
+#else
+#define ZSYNTH_NAME(n) zgpu_##n
+#endif
+
 extern "C" {
 
-void zgpu_synth_q4_0(uint64_t seed, uint64_t stream, uint64_t rows, uint64_t cols, float sigma,
+void ZSYNTH_NAME(synth_q4_0)(uint64_t seed, uint64_t stream, uint64_t rows, uint64_t cols, float sigma,
                      void *out) {
   const uint64_t bpr = cols / 32;
   uint8_t *o = static_cast<uint8_t *>(out);
@@ -102,7 +113,7 @@ void zgpu_synth_q4_0(uint64_t seed, uint64_t stream, uint64_t rows, uint64_t col
   });
 }
 
-void zgpu_synth_q8_0(uint64_t seed, uint64_t stream, uint64_t rows, uint64_t cols, float scale,
+void ZSYNTH_NAME(synth_q8_0)(uint64_t seed, uint64_t stream, uint64_t rows, uint64_t cols, float scale,
                      void *out) {
   const uint64_t bpr = cols / 32;
   uint8_t *o = static_cast<uint8_t *>(out);
@@ -127,7 +138,7 @@ void zgpu_synth_q8_0(uint64_t seed, uint64_t stream, uint64_t rows, uint64_t col
   });
 }
 
-void zgpu_synth_f32(uint64_t seed, uint64_t stream, uint64_t n, float mean, float sigma,
+void ZSYNTH_NAME(synth_f32)(uint64_t seed, uint64_t stream, uint64_t n, float mean, float sigma,
                     float *out) {
   for (uint64_t i = 0; i < n; ++i) {
     out[i] = (sigma == 0.0f)
@@ -137,14 +148,14 @@ void zgpu_synth_f32(uint64_t seed, uint64_t stream, uint64_t n, float mean, floa
   }
 }
 
-void zgpu_synth_tokens(uint64_t seed, uint64_t stream, uint64_t n, uint32_t vocab, uint32_t *out) {
+void ZSYNTH_NAME(synth_tokens)(uint64_t seed, uint64_t stream, uint64_t n, uint32_t vocab, uint32_t *out) {
   for (uint64_t i = 0; i < n; ++i) {
     const uint64_t r = mix64(seed, stream, i);
     out[i] = static_cast<uint32_t>(((r >> 32) * static_cast<uint64_t>(vocab)) >> 32);
   }
 }
 
-zgpu_status zgpu_pack_x4(const void *plain, void *x4, uint64_t rows, uint64_t cols,
+zgpu_status ZSYNTH_NAME(pack_x4)(const void *plain, void *x4, uint64_t rows, uint64_t cols,
                          uint32_t quant) {
   const uint64_t bb = quant == ZGPU_Q4_0 ? 18 : quant == ZGPU_Q8_0 ? 34 : 0;
   if (!bb) return ZGPU_ERR_UNSUPPORTED_QUANT;
