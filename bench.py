@@ -17,13 +17,16 @@ JSON line on rank 0.
   roofline the dominant kernel: the persistent step kernel's decode launch
            (algorithmic bytes = steps x (1.124 GB of weights + the KV rows
            read) over its CUDA-event duration) vs the measured HBM copy
-           bandwidth; plus the standalone Q4_0 GEMV 2048 -> 6144 over the 56
-           gate/up tensors as a secondary figure.
+           bandwidth; plus, at N = 1, the BASELINE config-1 GEMV sweep (four
+           Q4_0 shapes, f32 and Q8_0 activations) as a secondary figure.
   cpu_baseline  the CPU oracle's AVX-512-order restatement of the reference
-           decode, all host cores, on a bounded sample (rank 0, N=1 only).
+           decode on a persistent pinned pool over the physical host cores,
+           on a bounded sample (rank 0, N=1 only).
 
-With --gpus N > 1 (launched under torchrun) every rank decodes its own
-replica (weak scaling); times are the max over ranks.
+With --gpus N > 1 (launched under torchrun) the one sequence is decoded
+tensor parallel over the N GPUs (strong scaling): every rank holds 1/N of the
+rows of each matmul and the stage outputs cross NVLink inside the persistent
+step kernel; times are the max over ranks.
 
 Other workloads (--workload), each printing the same kind of line:
   qwen3-8b          BASELINE config 2: cache filled to 4096 tokens, greedy
@@ -1025,7 +1028,7 @@ def main():
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     import zero_b200 as zb
     synth = synth_module(args)
@@ -1034,7 +1037,14 @@ def main():
     weights = synth.qwen3_weights(cfg, seed=SEED)
     prompt = synth.prompt_ids(cfg, PROMPT_LEN, seed=SEED)
     ctx = zb.Context(device=local)
-    model = zb.Qwen3Model(ctx, cfg, weights)
+    # N > 1: tensor parallel over the N GPUs (one sequence, its weights split
+    # N ways: strong scaling); the stage outputs cross NVLink inside the
+    # persistent step kernel
+    model = zb.Qwen3Model(ctx, cfg, weights, rank=rank, world=world)
+    if world > 1:
+        from zero_b200 import tp
+
+        tp.connect(model)
     max_tokens = 512
     n_gen_timed = args.steps + 1
     assert PROMPT_LEN + n_gen_timed - 1 <= max_tokens
@@ -1057,7 +1067,7 @@ def main():
         t = torch.tensor([dec_ms], device="cuda")
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         dec_ms = float(t.item())
-    tok_s = world * args.steps / (dec_ms / 1000.0)
+    tok_s = args.steps / (dec_ms / 1000.0)
     # kernel launches of this library inside the timed decode steps
     gpu_launches = perf["decode_launches"]
 
@@ -1080,7 +1090,7 @@ def main():
             t = torch.tensor([e2e_s], device="cuda")
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             e2e_s = float(t.item())
-        e2e_tok_s = world * args.steps / e2e_s
+        e2e_tok_s = args.steps / e2e_s
         kv2.close()
 
     # -------------------------------------- roofline of the dominant kernel
@@ -1089,51 +1099,35 @@ def main():
     # reads), duration = the CUDA-event time of that launch (decode_ms).  With
     # the per-op kernels instead, the same bytes over the same device time give
     # the whole-step figure.
+    # Tensor parallel (N > 1): per GPU, its 1/N of the weights and the K/V
+    # rows of its kv heads, over the slowest rank's launch time.
     peaks = measured_peaks()
-    step_bytes = cfg.weight_bytes_per_token()
+    step_bytes = cfg.weight_bytes_per_token() // world
     # a step at position p reads the K and V rows of tokens 0..p-1 and writes row p (f32, all layers)
-    kv_row_bytes = 2 * cfg.n_kv_heads * cfg.head_dim * 4 * cfg.n_layers
+    kv_row_bytes = 2 * (cfg.n_kv_heads // world) * cfg.head_dim * 4 * cfg.n_layers
     kv_bytes = sum(kv_row_bytes * (PROMPT_LEN + i + 1) for i in range(args.steps))
     launch_bytes = args.steps * step_bytes + kv_bytes
     step_gbs = launch_bytes / (dec_ms / 1000.0) / 1e9
-    traffic_step = measured_traffic_per_step()
-    # secondary: the standalone Q4_0 GEMV 2048 -> 6144 over the 56 gate/up
-    # tensors (396 MB per sweep > L2), captured into a CUDA graph on a torch
-    # stream and timed with CUDA events on that stream
-    gemv_bytes = cfg.ffn * cfg.hidden * 18 // 32 + cfg.hidden * 4 + cfg.ffn * 4
-    gemv_ms = None
-    if not args.no_roofline:
-        keys = []
-        for i in range(cfg.n_layers):
-            keys.append(model._layers[i].ffn_gate)
-            keys.append(model._layers[i].ffn_up)
-        x = torch.randn(cfg.hidden, device="cuda", dtype=torch.float32)
-        y = torch.empty(cfg.ffn, device="cuda", dtype=torch.float32)
-        stream = torch.cuda.Stream()
-        sh = stream.cuda_stream
+    traffic_step = measured_traffic_per_step() if world == 1 else None
+    kv.close()
+    model.close()
 
-        def sweep():
-            for k in keys:
-                ctx.linear_dispatch_device(x.data_ptr(), k, y.data_ptr(), cfg.hidden, cfg.ffn, zb.Q4_0, sh)
+    # ----------------------------- secondary: the config-1 GEMV sweep (N = 1)
+    # The four BASELINE config-1 shapes (Q4_0 weights, 2048->4096, 2048->12288,
+    # 6144->2048, 2048->151936) with f32 activations (the reference's GEMV) and
+    # with Q8_0 activations; weights rotated over > 2x L2 per sweep, launches
+    # captured in a CUDA graph and timed with CUDA events on its stream.
+    gemv_sweep = None
+    if world == 1 and not args.no_roofline:
+        from zero_b200 import microbench
 
-        with torch.cuda.stream(stream):
-            sweep()                                   # warm-up, eager
-        stream.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            sweep()
-        reps = 8
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            graph.replay()
-            e0.record(stream)
-            for _ in range(reps):
-                graph.replay()
-            e1.record(stream)
-        stream.synchronize()
-        gemv_ms = e0.elapsed_time(e1) / (reps * len(keys))
-        del graph
-    gemv_gbs = gemv_bytes / (gemv_ms * 1e-3) / 1e9 if gemv_ms else None
+        gemv_sweep = []
+        for shp in microbench.CONFIG1_SHAPES:
+            o, i = (int(v) for v in shp.split("x"))
+            for act in ("f32", "q8"):
+                r = microbench.run_shape(ctx, o, i, act, 5, None, torch)
+                r["frac"] = round(r["gbs"] / peaks["hbm_gbs"], 4)
+                gemv_sweep.append(r)
 
     # ------------------------------------------------------- CPU baseline
     cpu = None
@@ -1151,18 +1145,20 @@ def main():
             "metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(dec_ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": round(tok_s / PUBLISHED_TOK_S, 3), "dtype": "f32",
+            "scaling": "strong", "vs_baseline": round(tok_s / PUBLISHED_TOK_S, 3), "dtype": "f32",
             "data": "synthetic (seeded random-init .smodel v2 weights, BASELINE config 0)",
             "config": {"workload": "qwen3-1.7b-shape q4_0 decode b=1 (BASELINE config 0)",
                        "prompt": PROMPT_LEN, "decode_steps": args.steps, "layers": cfg.n_layers,
                        "hidden": cfg.hidden, "ffn": cfg.ffn, "vocab": cfg.vocab_padded,
                        "weight_bytes_per_step": step_bytes,
                        "l2": "inputs larger than L2 (1.12 GB of weights streamed per step)",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "parallelism": f"tp{world} (one sequence; stage outputs exchanged over NVLink "
+                                      f"inside the step kernel)" if world > 1 else "single GPU",
                        "tokens_first": [int(v) for v in toks[:4]]},
             "roofline": {"bound": "hbm",
                          "kernel": "step_kernel (persistent decode, one launch for all timed steps)"
                                    if gpu_launches == 1 else "per-op decode kernels (whole step)",
+                         "per": "GPU",
                          "achieved": round(step_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(step_gbs / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
                          "traffic": (traffic_step * args.steps) if traffic_step else None,
@@ -1170,10 +1166,7 @@ def main():
                                            "not captured on the current step-kernel sources",
                          "algorithmic_bytes": launch_bytes,
                          "avg_launch_us": round(dec_ms * 1000 / max(gpu_launches, 1), 1),
-                         "gemv_2048x6144": {"achieved": round(gemv_gbs, 1) if gemv_gbs else None,
-                                            "algorithmic_bytes": gemv_bytes,
-                                            "avg_launch_us": round(gemv_ms * 1000, 3) if gemv_ms else None,
-                                            "frac": round(gemv_gbs / peaks["hbm_gbs"], 4) if gemv_gbs else None}},
+                         "gemv_sweep_config1": gemv_sweep},
             "e2e": {"value": round(e2e_tok_s, 2) if e2e_tok_s else None, "unit": "tok/s",
                     "h2d_bytes_per_step": 84, "d2h_bytes_per_step": 12},
             "gpu_launches": int(gpu_launches),
@@ -1181,8 +1174,6 @@ def main():
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
-    kv.close()
-    model.close()
     ctx.close()
     if world > 1:
         torch.distributed.barrier()

@@ -297,13 +297,24 @@ void zgpu_qwen3_destroy(zgpu_model *m);
  * world.  After creating every rank: zgpu_qwen3_tp_export on each, exchange
  * the handles (ZGPU_IPC_HANDLE_BYTES each, rank order), then
  * zgpu_qwen3_tp_connect on each.  A rank decodes through
- * zgpu_generate_greedy only (all ranks call it with the same arguments);
- * logits_out then receives the rank's vocab_padded / world rows per step. */
+ * zgpu_generate_greedy, or token by token through zgpu_forward_single_token
+ * followed by zgpu_lm_head_argmax (all ranks make the same calls with the
+ * same arguments, in the same order); logits_out then receives the rank's
+ * vocab_padded / world rows per step, and every rank returns the same token.
+ * Sampling (zgpu_lm_head_sample) and the per-op path are one-GPU only. */
 #define ZGPU_IPC_HANDLE_BYTES 64
 zgpu_status zgpu_qwen3_create_tp(zgpu_ctx *ctx, const zgpu_qwen3_desc *desc, uint32_t rank, uint32_t world,
                                  zgpu_model **out);
 zgpu_status zgpu_qwen3_tp_export(zgpu_model *m, void *handle_out);
 zgpu_status zgpu_qwen3_tp_connect(zgpu_model *m, const void *handles);
+/* Has no counterpart in the reference: connects a tensor-parallel rank with
+ * every other rank absent.  The other ranks' copies of the activation vectors
+ * and argmax slots become local buffers that nothing reads, and the rows the
+ * absent ranks own are never written, so the first stage that needs them
+ * waits until its bounded device wait (1 s) expires; the call then returns
+ * ZGPU_ERR_DEVICE_TIMEOUT and the context stays usable.  It exists to test,
+ * on one GPU, how a rank whose peer never arrives fails. */
+zgpu_status zgpu_qwen3_tp_connect_absent(zgpu_model *m);
 /* forward_single_token (forward_pass.rs:515-631) /
  * forward_single_token_avx512 (inference_avx512.rs:1826-1987): token at
  * position `pos` through all layers, updating `kv`; the final hidden state

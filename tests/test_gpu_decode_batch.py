@@ -14,6 +14,12 @@ now and then), the KV cache within 2e-2, the same next token wherever the
 oracle's top-1/top-2 margin is clear; the oracle is fed the GPU's tokens so
 both stay on one sequence.
 
+The batch is also held, free-running, to the reference's own f32 per-token
+path (no activation quantisation, the oracle's AVX-512 order) at the north
+star's 1e-2 on logits with identical greedy tokens wherever the f32 margin is
+clear: two sequences at config-0 size and sixteen sequences at contexts past
+2048 tokens (run_f32_case).
+
 A batch is also bit-identical to the same sequences decoded one at a time:
 every matmul row, attention and argmax of a sequence is computed the same
 way whatever else is in the batch.
@@ -103,6 +109,89 @@ def test_decode_batch_matches_per_token_q8_path(cfg, lens, steps):
 def test_decode_batch_config0_full_size():
     """BASELINE config 0 weights (28 layers, hidden 2048, vocab 151936), two sequences."""
     run_case(synth.QWEN3_1_7B, [16, 23], 3, seed=0)
+
+
+def run_f32_case(cfg, lens, steps, seed, wkw):
+    """Free-running batched greedy decode against the reference's own f32
+    per-token path (ORDER_AVX512, no activation quantisation): each
+    sequence's prompt goes through zgpu_prefill, then `steps` zgpu_decode_batch
+    steps of all sequences; the oracle generates every sequence on its own
+    (forward_single_token + lm_head_argmax, its prompt, then its own greedy
+    tokens).  Per sequence and step: logits within the north-star 1e-2
+    relative L2, and the same token.  A token may differ only where the
+    oracle's top-1/top-2 margin is inside the logits error (the batch path
+    quantises its matmul inputs to Q8_0); the sequences then part and that
+    sequence's later steps are not compared.  At least 90% of the steps must
+    be compared."""
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+
+    w = synth.qwen3_weights(cfg, seed=seed, **wkw)
+    B = len(lens)
+    max_tokens = max(lens) + steps + 8
+    prompts = [synth.prompt_ids(cfg, n, seed=seed + i) for i, n in enumerate(lens)]
+    ctx = zb.Context()
+    m = zb.Qwen3Model(ctx, cfg, w)
+    kvs = [m.new_kv(max_tokens) for _ in lens]
+    first = [m.prefill(kv, p, want_logits=True) for kv, p in zip(kvs, prompts)]
+    toks = np.array([t for t, _ in first], np.uint32)
+    gpu_t = [[int(t)] for t in toks]
+    gpu_l = [[l.copy()] for _, l in first]
+    for s in range(steps):
+        pos = np.array([n + s for n in lens], np.uint32)
+        nxt, logits = m.decode_batch(kvs, toks, pos)
+        for i in range(B):
+            gpu_t[i].append(int(nxt[i]))
+            gpu_l[i].append(logits[i].copy())
+        toks = nxt
+    for kv in kvs:
+        kv.close()
+    m.close()
+    ctx.close()
+
+    def ref(i):   # ctypes releases the GIL: the sequences run side by side
+        r = O.OracleRun(cfg, w, max_tokens, order=O.ORDER_AVX512, threads=1)
+        try:
+            return r.generate(prompts[i], steps + 1, want_logits=True)
+        finally:
+            r.close()
+
+    with ThreadPoolExecutor(min(B, os.cpu_count() or 1)) as ex:
+        refs = list(ex.map(ref, range(B)))
+    compared, worst, parted = 0, 0.0, []
+    for i in range(B):
+        rc, rt, margins, rl = refs[i]
+        assert rc == 0
+        for s in range(steps + 1):
+            err = rel_l2(gpu_l[i][s], rl[s])
+            worst = max(worst, err)
+            assert err < 1e-2, (i, s, err)
+            compared += 1
+            if gpu_t[i][s] != int(rt[s]):
+                assert not margins[s] > 20 * err * float(np.abs(rl[s]).max()), (i, s, float(margins[s]), err)
+                parted.append((i, s))
+                break
+    distinct = len({t for seq in gpu_t for t in seq})
+    print(f"{cfg.name} B={B} lens {min(lens)}..{max(lens)}: worst logits vs f32 path {worst:.2e}, "
+          f"{compared} of {B * (steps + 1)} steps compared, parted at {parted}, {distinct} distinct ids")
+    assert compared >= 0.9 * B * (steps + 1), (compared, parted)
+
+
+F32_CASES = [
+    # two sequences at config-0 full size (28 layers, vocab 151936)
+    (synth.QWEN3_1_7B, [16, 23], 4, 0, dict(centered=True, norm_mean=3.0, norm_sigma=0.3)),
+    # BASELINE config 2's batch of 16, each context past 2048 tokens, on a
+    # two-layer model at config-0 widths
+    (synth.small_config(n_layers=2, hidden=2048, ffn=6144, n_q=16, n_kv=8, vocab=4096),
+     [2048 + 7 * i for i in range(16)], 4, 5, dict(centered=True, norm_mean=2.0, norm_sigma=0.3)),
+]
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("cfg,lens,steps,seed,wkw", F32_CASES,
+                         ids=[f"{c.name}-b{len(l)}-ctx{max(l)}" for c, l, *_ in F32_CASES])
+def test_decode_batch_matches_reference_f32_path(cfg, lens, steps, seed, wkw):
+    run_f32_case(cfg, lens, steps, seed, wkw)
 
 
 def test_batch_equals_sequences_alone():

@@ -26,9 +26,25 @@ VARIANTS = {
                                   expert_ffn=256, n_shared=2, vocab=1024),
     "16experts_top6_no_shared": dict(n_layers=2, hidden=1024, ffn=2048, n_heads=16, n_experts=16, top_k=6,
                                      expert_ffn=352, n_shared=0, vocab=2048),
+    # every token of every MoE layer routed to rank 0's experts (router bias
+    # -1e4 on the others): rank 0's combine never waits for slot data, so
+    # only the arrival words keep it from running two MoE layers ahead of
+    # rank 1 and overwriting slots rank 1 has not read yet
+    "8experts_top3_all_on_rank0": dict(n_layers=4, hidden=512, ffn=1024, n_heads=4, n_experts=8, top_k=3,
+                                       expert_ffn=256, n_shared=1, vocab=1024, router_bias=True),
 }
+SKEWED = {"8experts_top3_all_on_rank0"}
 CASES = [(name, 2) for name in VARIANTS] + [("16experts_top6_no_shared", 4)]
 PROMPT_LEN, N_GEN, MAX_TOKENS = 7, 10, 48
+
+
+def _weights(name, cfg):
+    w = synth.ds2_weights(cfg, seed=41, norm_sigma=0.1)
+    if name in SKEWED:
+        for lw in w["layers"]:
+            if "router_b" in lw:
+                lw["router_b"][cfg.n_experts // 2:] = -1e4
+    return w
 
 
 def _free_port() -> int:
@@ -39,16 +55,16 @@ def _free_port() -> int:
     return port
 
 
-def _rank(rank, world, port, cfg_kw, q):
+def _rank(rank, world, port, name, q):
     import torch.distributed as dist
 
     from zero_b200 import tp
 
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     try:
-        cfg = synth.ds2_small_config(**cfg_kw)
+        cfg = synth.ds2_small_config(**VARIANTS[name])
         ctx = zb.Context(device=rank)
-        w = synth.ds2_weights(cfg, seed=41, norm_sigma=0.1)
+        w = _weights(name, cfg)
         m = zb.Ds2Model(ctx, cfg, w, rank=rank, world=world)
         tp.connect(m)
         prompt = synth.ds2_prompt_ids(cfg, PROMPT_LEN, seed=41)
@@ -74,7 +90,7 @@ def test_expert_parallel_decode_equals_one_gpu(name, world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, cfg_kw, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, name, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -91,7 +107,7 @@ def test_expert_parallel_decode_equals_one_gpu(name, world):
         assert res[r][3] is None, res[r][3]
     cfg = synth.ds2_small_config(**cfg_kw)
     c1 = zb.Context(device=0)
-    m1 = zb.Ds2Model(c1, cfg, synth.ds2_weights(cfg, seed=41, norm_sigma=0.1))
+    m1 = zb.Ds2Model(c1, cfg, _weights(name, cfg))
     kv = m1.new_kv(MAX_TOKENS)
     ref_toks, ref_logits = m1.generate_greedy(kv, synth.ds2_prompt_ids(cfg, PROMPT_LEN, seed=41), N_GEN,
                                               want_logits=True)
@@ -104,3 +120,6 @@ def test_expert_parallel_decode_equals_one_gpu(name, world):
         assert np.array_equal(toks, ref_toks), (r, toks, ref_toks)
         assert np.array_equal(logits.view(np.uint32), ref_logits.view(np.uint32)), r
         assert np.array_equal(np.asarray(ids), np.asarray(ref_ids)), r
+    if name in SKEWED:   # the routing really was all on rank 0
+        moe = np.asarray(ref_ids)[cfg.n_dense:]
+        assert moe.size and (moe < cfg.n_experts // world).all(), moe

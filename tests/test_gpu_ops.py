@@ -42,8 +42,9 @@ def check_rows(y: np.ndarray, x: np.ndarray, wd: np.ndarray, bound=REL_BOUND):
     return worst
 
 
-SHAPES = [(4096, 2048), (12288, 2048), (2048, 6144), (2048, 2048), (64, 2048), (8, 32), (4, 64),
-          (400, 1024), (1028, 4096), (4, 8192)]
+# BASELINE config 1's four shapes (out x in) first, the LM-head one in Q4_0 as config 1 states it
+SHAPES = [(4096, 2048), (12288, 2048), (2048, 6144), (151936, 2048), (2048, 2048), (64, 2048), (8, 32),
+          (4, 64), (400, 1024), (1028, 4096), (4, 8192)]
 
 
 @pytest.mark.parametrize("out_dim,in_dim", SHAPES)
@@ -176,7 +177,7 @@ def test_q8_0_quantiser_bit_exact_with_packer(ctx, golden):
     assert np.array_equal(ctx.quantize_q8_0(x), O.quantize_row_q8_0(x))
 
 
-@pytest.mark.parametrize("out_dim,in_dim", [(4096, 2048), (2048, 6144), (12288, 2048), (64, 96)])
+@pytest.mark.parametrize("out_dim,in_dim", [(4096, 2048), (2048, 6144), (12288, 2048), (151936, 2048), (64, 96)])
 def test_q8_activation_gemv_matches_oracle(ctx, out_dim, in_dim):
     w = synth.q4_0(15, out_dim, out_dim, in_dim, 0.02)
     key = ctx.register(w, zb.Q4_0, out_dim, in_dim)

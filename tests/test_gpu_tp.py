@@ -23,6 +23,11 @@ pytestmark = pytest.mark.gpu
 
 CASES = [
     (dict(n_layers=2, hidden=512, ffn=1024, n_q=8, n_kv=2, vocab=1024), 2),
+    # BASELINE config 0 widths (Qwen3-1.7B: hidden 2048, FFN 6144, 16 q / 8 kv heads), the
+    # shapes bench.py --gpus N shards
+    (dict(n_layers=2, hidden=2048, ffn=6144, n_q=16, n_kv=8, vocab=2048), 2),
+    (dict(n_layers=2, hidden=2048, ffn=6144, n_q=16, n_kv=8, vocab=2048), 4),
+    (dict(n_layers=2, hidden=2048, ffn=6144, n_q=16, n_kv=8, vocab=2048), 8),
     # BASELINE config 2 widths (Qwen3-8B: hidden 4096, FFN 12288, 32 q / 8 kv heads)
     (dict(n_layers=2, hidden=4096, ffn=12288, n_q=32, n_kv=8, vocab=2048), 2),
     (dict(n_layers=2, hidden=4096, ffn=12288, n_q=32, n_kv=8, vocab=2048), 4),
@@ -57,9 +62,23 @@ def _rank(rank, world, port, cfg_kw, q):
         kv2 = m.new_kv(MAX_TOKENS)
         toks2, _ = m.generate_greedy(kv2, prompt, N_GEN)                          # one launch
         launches = m.perf()["decode_launches"]
+        # token by token through the per-token entry points, every rank in step
+        kv3 = m.new_kv(MAX_TOKENS)
+        for i, t in enumerate(prompt):
+            m.forward_single_token(kv3, int(t), i)
+        tok, lg = m.lm_head_argmax(want_logits=True)
+        toks3, logits3 = [tok], [lg]
+        for s in range(1, N_GEN):
+            m.forward_single_token(kv3, tok, PROMPT_LEN + s - 1)
+            tok, lg = m.lm_head_argmax(want_logits=True)
+            toks3.append(tok)
+            logits3.append(lg)
+        assert np.array_equal(np.array(toks3, np.uint32), toks), (toks3, toks)
+        assert np.array_equal(np.stack(logits3).view(np.uint32), logits.view(np.uint32))
         dist.barrier()
         kv.close()
         kv2.close()
+        kv3.close()
         m.close()
         ctx.close()
         q.put((rank, toks, logits, toks2, launches, None))
@@ -69,7 +88,7 @@ def _rank(rank, world, port, cfg_kw, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("cfg_kw,world", CASES, ids=[f"h{c['hidden']}-tp{w}" for c, w in CASES])
+@pytest.mark.parametrize("cfg_kw,world", CASES, ids=[f"h{c['hidden']}-q{c['n_q']}-tp{w}" for c, w in CASES])
 def test_tensor_parallel_decode_equals_one_gpu(cfg_kw, world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")

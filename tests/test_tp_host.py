@@ -1,7 +1,9 @@
-"""Host side of the tensor-parallel decode, on CPU: the shard plan tiles
-every output vector with whole 4-row groups in rank order, the
-divisibility rule refuses what the C side refuses, and the handle exchange
-over a 2-rank gloo group hands every rank all handles in rank order."""
+"""Host side of the tensor- and expert-parallel decode, on CPU: the shard
+plan tiles every output vector with whole 4-row groups in rank order, the
+divisibility rules refuse what the C side refuses, the expert plan gives
+every routed expert exactly one owner, and the handle exchange over a 2-rank
+gloo group hands every rank all handles in rank order (with the ranks
+agreeing on the expert plan)."""
 import socket
 
 import pytest
@@ -71,3 +73,57 @@ def test_handle_exchange_over_gloo():
         assert p.exitcode == 0
     for r in range(2):
         assert res[r] == [bytes([1]) * 64, bytes([2]) * 64]
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_expert_plan_gives_every_expert_one_owner(world):
+    cfg = synth.DS2_V2_LITE
+    plan = tp.expert_plan(cfg.n_experts, world)
+    owned = [e for sl in plan for e in range(sl.start, sl.stop)]
+    assert owned == list(range(cfg.n_experts))
+    for e in range(cfg.n_experts):
+        r = tp.expert_owner(e, cfg.n_experts, world)
+        assert plan[r].start <= e < plan[r].stop
+
+
+def test_expert_plan_refuses_uneven_splits():
+    with pytest.raises(ValueError):
+        tp.expert_plan(64, 3)
+    with pytest.raises(ValueError):
+        tp.expert_plan(64, 16)
+    with pytest.raises(ValueError):
+        tp.expert_plan(0, 2)
+
+
+def _ep_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        plan = tp.expert_plan(synth.DS2_V2_LITE.n_experts, world)[rank]
+        got = tp.exchange_handles(bytes([0x40 + rank]) * 64)
+        plans: list = [None] * world
+        dist.all_gather_object(plans, (plan.start, plan.stop))
+        q.put((rank, got, plans))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_parallel_exchange_over_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r, got, plans = q.get(timeout=120)
+        res[r] = (got, plans)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(2):
+        got, plans = res[r]
+        assert got == [bytes([0x40]) * 64, bytes([0x41]) * 64]
+        assert plans == [(0, 32), (32, 64)]

@@ -317,6 +317,11 @@ class Qwen3Model:
         blob = (C.c_uint8 * (IPC_HANDLE_BYTES * self.world)).from_buffer_copy(b"".join(handles))
         self.ctx._check(LIB.zgpu_qwen3_tp_connect(self.h, blob))
 
+    def tp_connect_absent(self):
+        """Connect this rank with every other rank absent (zgpu_qwen3_tp_connect_absent):
+        a test of the device-side timeout when a peer never arrives."""
+        self.ctx._check(LIB.zgpu_qwen3_tp_connect_absent(self.h))
+
     @property
     def vocab_rows(self) -> int:
         """LM-head rows (logits) of this rank."""
@@ -332,8 +337,9 @@ class Qwen3Model:
         return hidden
 
     def lm_head_argmax(self, vocab_real: int | None = None, want_logits: bool = True):
+        """(token, logits); a tensor-parallel rank's logits are its own vocabulary rows."""
         tok = C.c_uint32()
-        logits = np.empty(self.cfg.vocab_padded, np.float32) if want_logits else None
+        logits = np.empty(self.vocab_rows, np.float32) if want_logits else None
         self.ctx._check(LIB.zgpu_lm_head_argmax(
             self.h, self.cfg.vocab_real if vocab_real is None else vocab_real, C.byref(tok),
             _ptr(logits) if want_logits else None))

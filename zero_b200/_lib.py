@@ -123,6 +123,7 @@ _SIGS = {
     "zgpu_qwen3_create_tp": (_i32, [_vp, C.POINTER(ZgpuQwen3Desc), _u32, _u32, C.POINTER(_vp)]),
     "zgpu_qwen3_tp_export": (_i32, [_vp, _vp]),
     "zgpu_qwen3_tp_connect": (_i32, [_vp, _vp]),
+    "zgpu_qwen3_tp_connect_absent": (_i32, [_vp]),
     "zgpu_sample_top_k": (_i32, [_vp, _vp, _u32, _u32, _f, C.POINTER(_u64), C.POINTER(_u32)]),
     "zgpu_lm_head_sample": (_i32, [_vp, _u32, _f, C.POINTER(_u64), C.POINTER(_u32)]),
     "zgpu_smodel_open": (_i32, [C.c_char_p, C.POINTER(_vp)]),

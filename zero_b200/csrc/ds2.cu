@@ -117,7 +117,7 @@ struct zgpu_ds2_model {
   // [rank * ep_per_rank, (rank + 1) * ep_per_rank); everything else is
   // replicated.  Selected experts' outputs cross over the exchange buffers.
   uint32_t rank = 0, world = 1, ep_per_rank = 0;
-  unsigned long long *d_xslots = nullptr;   // this rank's exchange buffer [2][top_k][hidden] (tagged)
+  unsigned long long *d_xslots = nullptr;   // this rank's exchange buffer: [2][top_k][hidden] slots, arrivals
   uint32_t *d_ep_seq = nullptr;             // MoE invocations so far (the exchange version)
   unsigned long long **d_ep_dst = nullptr;  // [world] every rank's exchange buffer
   std::vector<void *> ipc_opened;
@@ -414,6 +414,7 @@ cudaError_t ds2_enqueue_forward(zgpu_ds2_model *m, zgpu_mla_kv *kv, uint32_t *co
     cp.top_k = d.top_k;
     cp.xslots = m->world > 1 ? m->d_xslots : nullptr;
     cp.ep_seq = m->d_ep_seq;
+    cp.world = m->world;
     cp.status = m->d_status;
     if ((e = launch_moe_combine(cp, lc)) != cudaSuccess) return e;
     if (m->world > 1 && (e = launch_moe_ep_advance(m->d_ep_seq, lc)) != cudaSuccess) return e;
@@ -1036,7 +1037,7 @@ zgpu_status ds2_create(zgpu_ctx *ctx, const zgpu_ds2_desc *d, uint32_t rank, uin
   m->world = world;
   m->ep_per_rank = world > 1 ? d->n_experts / world : 0;
   if (world > 1) {
-    const size_t xw = 2 * static_cast<size_t>(d->top_k) * H;
+    const size_t xw = ep_exchange_words(d->top_k, H);
     if (cudaMalloc(&m->d_xslots, xw * 8) || cudaMalloc(&m->d_ep_seq, 4))
       return fail(ZGPU_ERR_OUT_OF_MEMORY, "expert-parallel exchange buffers");
     cudaMemset(m->d_xslots, 0, xw * 8);

@@ -98,6 +98,7 @@ struct zgpu_model {
   size_t tv_off[kStepBufs] = {};
   bool tp_connected = false;
   std::vector<void *> ipc_opened;      // peers' arenas mapped into this process
+  std::vector<void *> absent_arenas;   // stand-ins for absent peers (zgpu_qwen3_tp_connect_absent)
   unsigned long long **d_peer_tv = nullptr;
   ArgSlot **d_peer_arg = nullptr;
   unsigned long long **d_attn_dst = nullptr;
@@ -556,6 +557,7 @@ cudaError_t run_step(zgpu_model *m, zgpu_kv *kv, StepMode mode, uint32_t step0, 
 void reset_step_tags(zgpu_model *m) {
   if (!m->d_tv) return;
   cudaMemsetAsync(m->d_tv, 0, m->tv_words * sizeof(unsigned long long), m->ctx->stream);
+  cudaMemsetAsync(m->d_counters, 0, m->desc.n_kv_heads * sizeof(uint32_t), m->ctx->stream);
   for (int b = 0; b < kStepBufs; ++b) m->ver[b] = 0;
 }
 
@@ -665,6 +667,7 @@ void zgpu_qwen3_destroy(zgpu_model *m) {
     delete t;
   }
   for (void *p : m->ipc_opened) cudaIpcCloseMemHandle(p);
+  for (void *p : m->absent_arenas) cudaFree(p);
   cudaFree(m->d_peer_tv);
   cudaFree(m->d_peer_arg);
   cudaFree(m->d_attn_dst);
@@ -861,6 +864,39 @@ zgpu_status zgpu_qwen3_tp_export(zgpu_model *m, void *handle_out) {
   return ZGPU_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+// The device tables of every rank's arena (base[d]: rank d's tagged vectors
+// as this rank addresses them).
+zgpu_status tp_tables(zgpu_model *m, const std::vector<unsigned long long *> &base) {
+  zgpu_ctx *ctx = m->ctx;
+  const uint32_t N = m->world;
+  std::vector<unsigned long long *> tv(static_cast<size_t>(N) * kStepBufs), dst(N);
+  std::vector<ArgSlot *> arg(N);
+  for (uint32_t d = 0; d < N; ++d) {
+    for (int b = 0; b < kStepBufs; ++b) tv[static_cast<size_t>(d) * kStepBufs + b] = base[d] + m->tv_off[b];
+    arg[d] = reinterpret_cast<ArgSlot *>(base[d] + m->arg_off);
+    dst[d] = base[d] + m->tv_off[BUF_ATTN] + static_cast<size_t>(m->rank) * m->q_loc;
+  }
+  cudaError_t e = cudaMalloc(&m->d_peer_tv, tv.size() * sizeof(void *));
+  if (e == cudaSuccess) e = cudaMalloc(&m->d_peer_arg, arg.size() * sizeof(void *));
+  if (e == cudaSuccess) e = cudaMalloc(&m->d_attn_dst, dst.size() * sizeof(void *));
+  if (e == cudaSuccess) e = cudaMemcpy(m->d_peer_tv, tv.data(), tv.size() * sizeof(void *), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(m->d_peer_arg, arg.data(), arg.size() * sizeof(void *), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(m->d_attn_dst, dst.data(), dst.size() * sizeof(void *), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "tensor parallel: peer tables");
+  m->tp_connected = true;
+  return ZGPU_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
 zgpu_status zgpu_qwen3_tp_connect(zgpu_model *m, const void *handles) {
   if (!m || !handles || m->world < 2 || !m->d_tv) return ZGPU_ERR_INVALID_ARG;
   if (m->tp_connected) return zgpu_fail(m->ctx, ZGPU_ERR_INVALID_ARG, "tensor parallel: already connected");
@@ -881,24 +917,33 @@ zgpu_status zgpu_qwen3_tp_connect(zgpu_model *m, const void *handles) {
     m->ipc_opened.push_back(p);
     base[d] = static_cast<unsigned long long *>(p);
   }
-  std::vector<unsigned long long *> tv(static_cast<size_t>(N) * kStepBufs), dst(N);
-  std::vector<ArgSlot *> arg(N);
+  return tp_tables(m, base);
+}
+
+zgpu_status zgpu_qwen3_tp_connect_absent(zgpu_model *m) {
+  if (!m || m->world < 2 || !m->d_tv) return ZGPU_ERR_INVALID_ARG;
+  if (m->tp_connected) return zgpu_fail(m->ctx, ZGPU_ERR_INVALID_ARG, "tensor parallel: already connected");
+  zgpu_ctx *ctx = m->ctx;
+  cudaSetDevice(ctx->device);
+  const uint32_t N = m->world;
+  std::vector<unsigned long long *> base(N, nullptr);
   for (uint32_t d = 0; d < N; ++d) {
-    for (int b = 0; b < kStepBufs; ++b) tv[static_cast<size_t>(d) * kStepBufs + b] = base[d] + m->tv_off[b];
-    arg[d] = reinterpret_cast<ArgSlot *>(base[d] + m->arg_off);
-    dst[d] = base[d] + m->tv_off[BUF_ATTN] + static_cast<size_t>(m->rank) * m->q_loc;
+    if (d == m->rank) {
+      base[d] = m->d_tv;
+      continue;
+    }
+    // a local arena that no kernel reads stands in for the absent rank
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, m->tv_words * sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(p, 0, m->tv_words * sizeof(unsigned long long));
+    if (e != cudaSuccess) {
+      cudaFree(p);
+      return zgpu_cuda_fail(ctx, e, "tensor parallel: stand-in arena");
+    }
+    m->absent_arenas.push_back(p);
+    base[d] = static_cast<unsigned long long *>(p);
   }
-  cudaError_t e = cudaMalloc(&m->d_peer_tv, tv.size() * sizeof(void *));
-  if (e == cudaSuccess) e = cudaMalloc(&m->d_peer_arg, arg.size() * sizeof(void *));
-  if (e == cudaSuccess) e = cudaMalloc(&m->d_attn_dst, dst.size() * sizeof(void *));
-  if (e == cudaSuccess) e = cudaMemcpy(m->d_peer_tv, tv.data(), tv.size() * sizeof(void *), cudaMemcpyHostToDevice);
-  if (e == cudaSuccess)
-    e = cudaMemcpy(m->d_peer_arg, arg.data(), arg.size() * sizeof(void *), cudaMemcpyHostToDevice);
-  if (e == cudaSuccess)
-    e = cudaMemcpy(m->d_attn_dst, dst.data(), dst.size() * sizeof(void *), cudaMemcpyHostToDevice);
-  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "tensor parallel: peer tables");
-  m->tp_connected = true;
-  return ZGPU_OK;
+  return tp_tables(m, base);
 }
 
 }  // extern "C"
@@ -933,10 +978,10 @@ extern "C" {
 zgpu_status zgpu_forward_single_token(zgpu_model *m, zgpu_kv *kv, uint32_t token, uint32_t pos,
                                       float *hidden_out) {
   if (!m || !kv) return ZGPU_ERR_INVALID_ARG;
-  if (m->world > 1)
-    return zgpu_fail(m->ctx, ZGPU_ERR_INVALID_ARG, "tensor-parallel ranks decode through zgpu_generate_greedy");
   zgpu_ctx *ctx = m->ctx;
   cudaSetDevice(ctx->device);
+  if (m->world > 1 && !m->tp_connected)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "tensor parallel: zgpu_qwen3_tp_connect first");
   zgpu_status s = prepare_kv(m, kv);
   if (s) return s;
   if (pos >= kv->max_tokens) return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "position beyond the cache");
@@ -946,6 +991,10 @@ zgpu_status zgpu_forward_single_token(zgpu_model *m, zgpu_kv *kv, uint32_t token
   if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "state buffers");
   if ((s = set_state(m, 1, pos, m->desc.vocab_real, 1))) return s;
   const bool persistent = step_usable(m, kv);
+  // a tensor-parallel rank runs the step kernel only (its stage outputs
+  // cross NVLink inside it); every rank makes the same call
+  if (m->world > 1 && !persistent)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "tensor parallel: the cache needs more attention CTAs than the step kernel has");
   const bool use_graph = !persistent && !(ctx->flags & ZGPU_FLAG_NO_GRAPH);
   if (use_graph && (s = build_graphs(m, kv))) return s;
   e = cudaMemcpyAsync(m->d_prompt, &token, 4, cudaMemcpyHostToDevice, ctx->stream);
@@ -988,10 +1037,10 @@ zgpu_status zgpu_forward_single_token(zgpu_model *m, zgpu_kv *kv, uint32_t token
 zgpu_status zgpu_lm_head_argmax(zgpu_model *m, uint32_t vocab_real, uint32_t *token_out,
                                 float *logits_out) {
   if (!m || !token_out) return ZGPU_ERR_INVALID_ARG;
-  if (m->world > 1)
-    return zgpu_fail(m->ctx, ZGPU_ERR_INVALID_ARG, "tensor-parallel ranks decode through zgpu_generate_greedy");
   zgpu_ctx *ctx = m->ctx;
   cudaSetDevice(ctx->device);
+  if (m->world > 1 && !m->tp_connected)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "tensor parallel: zgpu_qwen3_tp_connect first");
   if (vocab_real > m->desc.vocab_padded) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "vocab_real > padded");
   cudaError_t e = grow(&m->d_prompt, &m->prompt_cap, 1);
   if (e == cudaSuccess) e = grow(&m->d_tokens, &m->tokens_cap, 1);
@@ -999,6 +1048,8 @@ zgpu_status zgpu_lm_head_argmax(zgpu_model *m, uint32_t vocab_real, uint32_t *to
   zgpu_status s = set_state(m, 1, 0, vocab_real, 1);
   if (s) return s;
   const bool persistent = step_usable(m, nullptr) && m->last_fwd_persistent;
+  if (m->world > 1 && !persistent)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "tensor parallel: the LM head follows a zgpu_forward_single_token");
   const bool use_graph = !persistent && !(ctx->flags & ZGPU_FLAG_NO_GRAPH) && m->lm_graph;
   if (persistent) {
     e = run_step(m, nullptr, STEP_LM, 0, 1, 0, 0, 1);
@@ -1010,8 +1061,8 @@ zgpu_status zgpu_lm_head_argmax(zgpu_model *m, uint32_t vocab_real, uint32_t *to
     e = enqueue_lm_head(m, &ctx->launches);
   }
   if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "lm head");
-  if (logits_out) {
-    e = cudaMemcpyAsync(logits_out, m->d_logits, static_cast<size_t>(m->desc.vocab_padded) * 4,
+  if (logits_out) {   // a tensor-parallel rank holds the logits of its own vocabulary rows
+    e = cudaMemcpyAsync(logits_out, m->d_logits, static_cast<size_t>(m->lm_rows) * 4,
                         cudaMemcpyDeviceToHost, ctx->stream);
     if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "logits d2h");
   }

@@ -217,6 +217,21 @@ __global__ void moe_combine_kernel(const CombineParams p) {
   }
   const uint32_t ver = p.xslots ? __ldcg(p.ep_seq) + 1 : 0u;
   bool gave_up = false;   // after one expired wait the others are not waited for
+  if (p.xslots) {
+    // flow control: every rank has published this invocation (and so has
+    // finished its combine of the previous one)
+    const unsigned long long *arrive = p.xslots + ep_slot_words(p.top_k, p.dim);
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t r = 0; r < p.world && !gave_up; ++r) {
+      while (static_cast<uint32_t>(__ldcg(arrive + r) >> 32) != ver) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          atomicOr(p.status, ZDEV_ERR_TIMEOUT);
+          gave_up = true;
+          break;
+        }
+      }
+    }
+  }
   for (uint32_t k = 0; k < p.top_k; ++k) {
     const float w = __ldcg(p.weights + k);
     float y;
@@ -253,10 +268,15 @@ __global__ void moe_ep_publish_kernel(const EpPublishParams p) {
   pdl_launch_dependents();
   pdl_wait();
   const uint32_t k = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t ver = __ldcg(p.ep_seq) + 1;
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
+    // this rank's arrival for invocation ver, in every rank's buffer
+    const size_t a = ep_slot_words(p.top_k, p.dim) + p.ep_rank;
+    for (uint32_t d = 0; d < p.world; ++d) p.dst[d][a] = tag_word(0.0f, ver);
+  }
   if (i >= p.dim) return;
   const uint32_t e = __ldcg(p.ids + k);
   if (e / p.ep_per_rank != p.ep_rank) return;
-  const uint32_t ver = __ldcg(p.ep_seq) + 1;
   const unsigned long long w =
       tag_word(__ldcg(p.exp_out + static_cast<size_t>(p.n_shared + k) * p.dim + i), ver);
   const size_t off = (static_cast<size_t>(ver & 1u) * p.top_k + k) * p.dim + i;
@@ -308,7 +328,8 @@ cudaError_t launch_moe_combine(const CombineParams &p, const LaunchCfg &lc) {
 }
 
 cudaError_t launch_moe_ep_publish(const EpPublishParams &p, const LaunchCfg &lc) {
-  if (p.dim == 0 || p.top_k == 0 || p.world == 0 || p.ep_per_rank == 0) return cudaErrorInvalidValue;
+  if (p.dim == 0 || p.top_k == 0 || p.world == 0 || p.world > kEpMaxRanks || p.ep_per_rank == 0)
+    return cudaErrorInvalidValue;
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = make_launch_cfg(dim3((p.dim + 255) / 256, p.top_k), dim3(256), 0, lc, attr);
   if (lc.launch_counter) ++*lc.launch_counter;

@@ -5,6 +5,7 @@
 #include <stdint.h>
 
 #include "internal.h"
+#include "layout.h"
 
 namespace zgpu {
 
@@ -45,15 +46,22 @@ struct CombineParams {
   uint32_t dim, n_shared, top_k;
   // expert parallelism: the routed slots' outputs come from this rank's
   // exchange buffer (tagged words [2][top_k][dim], filled by every rank's
-  // moe_ep_publish) at version *ep_seq + 1; null: from exp_out
+  // moe_ep_publish) at version *ep_seq + 1; null: from exp_out.  The
+  // combine also waits until every rank's arrival word (ep_arrive_words
+  // after the slots, one per rank) carries that version.
   const unsigned long long *xslots;
   const uint32_t *ep_seq;
+  uint32_t world;
   uint32_t *status;
 };
 
 // Expert parallelism: the outputs of this rank's selected experts, as tagged
 // words into slot k of every rank's exchange buffer (buffer (v & 1), v =
-// *ep_seq + 1: a rank can run at most one MoE layer ahead of another).
+// *ep_seq + 1), plus this rank's arrival word for invocation v in every
+// rank's buffer.  A combine waits for all ranks' arrival words, so no rank
+// finishes invocation v + 1 before every rank has finished invocation v and
+// its reads of buffer (v & 1): publishing invocation v + 2 into that buffer
+// is then safe however the experts are routed.
 struct EpPublishParams {
   const float *exp_out;                    // [n_shared + top_k][dim]
   const uint32_t *ids;                     // [top_k] this layer's experts
@@ -61,6 +69,12 @@ struct EpPublishParams {
   const uint32_t *ep_seq;
   uint32_t dim, n_shared, top_k, world, ep_rank, ep_per_rank;
 };
+
+// Words of one rank's exchange buffer: two buffers of top_k x dim tagged
+// slot words, then one arrival word per rank.
+constexpr uint32_t kEpMaxRanks = 8;
+ZGPU_HD size_t ep_slot_words(uint32_t top_k, uint32_t dim) { return 2 * static_cast<size_t>(top_k) * dim; }
+ZGPU_HD size_t ep_exchange_words(uint32_t top_k, uint32_t dim) { return ep_slot_words(top_k, dim) + kEpMaxRanks; }
 
 cudaError_t moe_setup();
 cudaError_t launch_moe_route(const RouteParams &p, const LaunchCfg &lc);

@@ -61,6 +61,24 @@ def shard_plan(cfg, world: int) -> list[dict[str, Slice]]:
     return out
 
 
+def expert_plan(n_experts: int, world: int) -> list[Slice]:
+    """Expert parallelism (the DeepSeek2 MoE layers): rank r runs routed
+    experts [r E/N, (r+1) E/N), the split zgpu_ds2_create_ep makes; the
+    router, attention, dense layers, shared experts and LM head run on every
+    rank.  ValueError where the C side refuses the split."""
+    if not 1 <= world <= 8:
+        raise ValueError("expert parallel: 1..8 ranks")
+    if n_experts == 0 or n_experts % world:
+        raise ValueError(f"expert parallel: {n_experts} experts do not split over {world} ranks")
+    per = n_experts // world
+    return [Slice(r * per, (r + 1) * per) for r in range(world)]
+
+
+def expert_owner(expert: int, n_experts: int, world: int) -> int:
+    """The rank that runs `expert` and publishes its output row."""
+    return expert // (n_experts // world)
+
+
 def exchange_handles(handle: bytes, group=None) -> list[bytes]:
     """All ranks' handles in rank order (torch.distributed all_gather_object)."""
     import torch.distributed as dist
