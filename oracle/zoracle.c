@@ -1190,6 +1190,11 @@ static void lin(zo_run *r, const float *x, const uint8_t *plain, const uint8_t *
   }
   if (r->order == 0) {
     zo_linear_dispatch(x, plain, out, in, outd, quant);
+  } else if (r->pool && outd % 4 == 0) {
+    /* the persistent workers (linear_dispatch_avx512 through the SMP
+     * dispatcher, inference_avx512.rs:1147) */
+    zo_fused_ctx c = {.x = x, .bpr = in / 32, .quant = quant, .nseg = 1, .seg = {{x4, out, outd / 4}}};
+    fused_dispatch(r, &c);
   } else if (quant == ZO_Q4_0) {
     zo_linear_q4_0x4_avx512(x, x4, out, in, outd, r->threads, r->simd);
   } else {

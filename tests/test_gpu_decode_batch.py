@@ -177,13 +177,19 @@ def run_f32_case(cfg, lens, steps, seed, wkw):
     assert compared >= 0.9 * B * (steps + 1), (compared, parted)
 
 
+# The weights are the tame ones (gains near 1).  The Q8_0 activation
+# rounding of the batched path is a perturbation of ~0.5% per matmul; on the
+# models whose greedy sequence moves (centred nibbles, gains of 2-3) the
+# dynamics amplify it (the prefill's logits moved by 5.5e-2 on two layers and
+# by 0.54 on 28), so those models are compared with the f32 path only on
+# the f32 GPU step (test_gpu_model.py).
 F32_CASES = [
-    # two sequences at config-0 full size (28 layers, vocab 151936)
-    (synth.QWEN3_1_7B, [16, 23], 4, 0, dict(centered=True, norm_mean=3.0, norm_sigma=0.3)),
+    # two sequences at config-0 full size (28 layers, vocab 151936), BASELINE's distributions
+    (synth.QWEN3_1_7B, [16, 23], 4, 0, dict()),
     # BASELINE config 2's batch of 16, each context past 2048 tokens, on a
     # two-layer model at config-0 widths
     (synth.small_config(n_layers=2, hidden=2048, ffn=6144, n_q=16, n_kv=8, vocab=4096),
-     [2048 + 7 * i for i in range(16)], 4, 5, dict(centered=True, norm_mean=2.0, norm_sigma=0.3)),
+     [2048 + 7 * i for i in range(16)], 4, 5, dict(norm_sigma=0.1)),
 ]
 
 

@@ -220,7 +220,10 @@ def test_config0_full_size_matches_oracle(persistent, variant):
     assert np.array_equal(toks, ref_t), f"first mismatch at step {np.argmax(toks != ref_t)}"
     worst = max(rel_l2(logits[s], ref_l[s]) for s in range(n_gen))
     assert worst < 1e-2, worst
-    assert worst < 1e-4, worst          # what this path actually achieves
+    # what this path actually achieves: ~1e-5 on the baseline weights; the
+    # varied model's gains of 3 amplify every layer's last-bit differences
+    # (measured 3.5e-4 to 3.9e-4, with identical tokens)
+    assert worst < (1e-4 if variant == "baseline" else 1e-3), worst
     # the decode steps as one launch give the same tokens
     kv_b = m.new_kv(512)
     toks_b, _ = m.generate_greedy(kv_b, prompt, n_gen, want_logits=False)

@@ -340,6 +340,7 @@ static zgpu_status linear_device(zgpu_ctx *ctx, const float *d_x, const void *w_
   io.status = ctx->d_status;
   zgpu::LaunchCfg lc;
   lc.stream = stream ? stream : ctx->stream;
+  lc.pdl = true;   // the weight prefetch of back-to-back calls overlaps the previous call's tail
   lc.sm_count = ctx->sm_count;
   lc.launch_counter = &ctx->launches;
   cudaError_t e = zgpu::launch_gemv(g, zgpu::PRO_PLAIN, zgpu::EPI_STORE, io, lc);
@@ -440,6 +441,29 @@ zgpu_status zgpu_quantize_q8_0(zgpu_ctx *ctx, const float *x, void *blocks_out, 
   return check_status_word(ctx);
 }
 
+// The Q4_0 x Q8_0 GEMV on the standalone GEMV kernel's
+// streaming path with a one-digit activation image.
+static cudaError_t q8act_launch(zgpu_ctx *ctx, const DeviceTensor *t, uint64_t in_dim, uint64_t out_dim,
+                                const uint8_t *d_xq, float *d_out, cudaStream_t stream) {
+  zgpu::GemvDesc g;
+  g.w = t->d;
+  g.wbytes = t->bytes;
+  g.gstride = t->gstride;
+  g.quant = t->quant;
+  g.rows = static_cast<uint32_t>(out_dim);
+  g.groups = static_cast<uint32_t>(t->groups);
+  g.in_dim = static_cast<uint32_t>(in_dim);
+  zgpu::GemvIo io;
+  io.x = reinterpret_cast<const float *>(d_xq);
+  io.out = d_out;
+  io.status = ctx->d_status;
+  zgpu::LaunchCfg lc;
+  lc.stream = stream;
+  lc.pdl = true;
+  lc.sm_count = ctx->sm_count;
+  return zgpu::launch_gemv(g, zgpu::PRO_Q8ACT, zgpu::EPI_STORE, io, lc);
+}
+
 zgpu_status zgpu_linear_q8act_device(zgpu_ctx *ctx, const void *d_xq, const void *w_key,
                                      float *d_out, uint64_t in_dim, uint64_t out_dim, void *stream) {
   if (!ctx || !d_xq || !d_out || in_dim == 0 || in_dim % 32) return ZGPU_ERR_INVALID_ARG;
@@ -451,10 +475,7 @@ zgpu_status zgpu_linear_q8act_device(zgpu_ctx *ctx, const void *d_xq, const void
   if (t->cols != in_dim || t->rows != out_dim)
     return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "linear_q8act: shape mismatch with registration");
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
-  ZCHECK(zgpu::launch_q8act_gemv(t->d, t->gstride, static_cast<uint32_t>(out_dim),
-                                 static_cast<uint32_t>(in_dim / 32),
-                                 static_cast<const uint8_t *>(d_xq), d_out, s),
-         "q8act gemv");
+  ZCHECK(q8act_launch(ctx, t, in_dim, out_dim, static_cast<const uint8_t *>(d_xq), d_out, s), "q8act gemv");
   ++ctx->launches;
   return ZGPU_OK;
 }
@@ -473,10 +494,7 @@ zgpu_status zgpu_linear_q8act(zgpu_ctx *ctx, const void *xq_blocks, const void *
   zgpu_status s = ensure_scratch(ctx, (xbytes + 3) / 4, out_dim);
   if (s) return s;
   ZCHECK(cudaMemcpyAsync(ctx->d_x, xq_blocks, xbytes, cudaMemcpyHostToDevice, ctx->stream), "h2d");
-  ZCHECK(zgpu::launch_q8act_gemv(t->d, t->gstride, static_cast<uint32_t>(out_dim),
-                                 static_cast<uint32_t>(in_dim / 32),
-                                 reinterpret_cast<const uint8_t *>(ctx->d_x), ctx->d_y, ctx->stream),
-         "q8act gemv");
+  ZCHECK(q8act_launch(ctx, t, in_dim, out_dim, reinterpret_cast<const uint8_t *>(ctx->d_x), ctx->d_y, ctx->stream), "q8act gemv");
   ++ctx->launches;
   ZCHECK(cudaMemcpyAsync(out, ctx->d_y, out_dim * 4, cudaMemcpyDeviceToHost, ctx->stream), "d2h");
   ZCHECK(cudaStreamSynchronize(ctx->stream), "sync");

@@ -40,6 +40,11 @@
 //     applies SiLU(gate)*up / tracks the LM-head argmax.
 // Every reduction has a fixed order, so results are bitwise reproducible from
 // run to run and independent of the grid size.
+//
+// PRO_Q8ACT (BASELINE config 1's Q4_0 weight x Q8_0 activation GEMV): the
+// input is already Q8_0, so the image holds one digit per element (the int8
+// quant) with the offset -8 * sum q and the block scale d_x; a row-block is
+// one dp4a chain of eight, exact in int32, times d_w * d_x.
 #include <cfloat>
 
 #include "common.cuh"
@@ -168,9 +173,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
   // another rank's experts out); uniform over the CTA, before any barrier
   if (p.seg_w && p.seg_dynamic && __ldcg(p.seg_w + seg) == 0ull) return;
   const uint32_t tid = threadIdx.x;
-  const uint32_t nf4 = p.in_dim / 4;
+  const uint32_t nf4 = PRO == PRO_Q8ACT ? 0u : p.in_dim / 4;
   float inv = 1.0f;
   if (PRO == PRO_RMSNORM) inv = rms_inv<kWarps>(xin, p.in_dim, p.eps, red, tid, 1);
+  if (PRO == PRO_Q8ACT) {
+    // the input is already Q8_0: one thread per 34-byte block
+    const uint8_t *xq = reinterpret_cast<const uint8_t *>(xin);
+    for (uint32_t b = tid; b < p.bpr; b += kConsumers)
+      if (ZDEV_CHECK(b * 128 + 128 <= p.xbytes, p.status, 4, b, p.xbytes)) q8_block_image(xq + b * 34, b, xsm);
+  }
   // Warp-uniform trip count: the per-block statistics shuffle across the 8
   // lanes of a block, and nf4 is a multiple of 8, so a block's lanes are
   // either all in range or all out of range.
@@ -201,7 +212,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
     for (int r = 0; r < kRows; ++r) acc[r] = 0.f;
     if (!failed && b < p.bpr) {
       const uint8_t *sbase = ring + static_cast<size_t>(slot) * slot_bytes;
-      item_rows<QT, 2>(sbase, p.half_bytes, chunk_blocks(p.bpr, chunk), lane, b, xsm, acc);
+      if (PRO == PRO_Q8ACT) item_rows_q8act<2>(sbase, p.half_bytes, chunk_blocks(p.bpr, chunk), lane, b, xsm, acc);
+      else item_rows<QT, 2>(sbase, p.half_bytes, chunk_blocks(p.bpr, chunk), lane, b, xsm, acc);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_addr(&empty[slot]));
@@ -319,6 +331,7 @@ cudaError_t gemv_setup() {
   if ((e = configure_pro<ZGPU_Q4_0, PRO_PLAIN>()) != cudaSuccess) return e;
   if ((e = configure_pro<ZGPU_Q4_0, PRO_RMSNORM>()) != cudaSuccess) return e;
   if ((e = configure_pro<ZGPU_Q8_0, PRO_PLAIN>()) != cudaSuccess) return e;
+  if ((e = configure_one<ZGPU_Q4_0, PRO_Q8ACT, EPI_STORE>()) != cudaSuccess) return e;
   return configure_pro<ZGPU_Q8_0, PRO_RMSNORM>();
 }
 
@@ -328,6 +341,7 @@ cudaError_t launch_gemv(const GemvDesc &g, GemvPro pro, GemvEpi epi, const GemvI
     return cudaErrorInvalidValue;
   if (g.gstride % 16 != 0) return cudaErrorInvalidValue;
   if (epi == EPI_SWIGLU && g.quant != ZGPU_Q4_0) return cudaErrorInvalidValue;
+  if (pro == PRO_Q8ACT && (g.quant != ZGPU_Q4_0 || epi != EPI_STORE || g.seg_w)) return cudaErrorInvalidValue;
   KParams kp = {};
   kp.w = g.w;
   kp.gstride = g.gstride;
@@ -377,6 +391,7 @@ cudaError_t launch_gemv(const GemvDesc &g, GemvPro pro, GemvEpi epi, const GemvI
   const size_t smem = kp.ring_off + static_cast<size_t>(kWarps) * spw * slot + 16 * kWarps * spw;
   kp.smem_bytes = static_cast<uint32_t>(smem);
   if (g.quant == ZGPU_Q4_0) {
+    if (pro == PRO_Q8ACT) return launch_one<ZGPU_Q4_0, PRO_Q8ACT, EPI_STORE>(kp, grid, smem, lc);
     return pro == PRO_RMSNORM ? dispatch_epi<ZGPU_Q4_0, PRO_RMSNORM>(epi, kp, grid, smem, lc)
                               : dispatch_epi<ZGPU_Q4_0, PRO_PLAIN>(epi, kp, grid, smem, lc);
   }

@@ -231,4 +231,59 @@ __device__ __forceinline__ void item_rows(const uint8_t *sbase, uint32_t group_b
   }
 }
 
+// Image of a Q8_0-quantised activation block (the config-1 Q4_0 x Q8_0
+// GEMV): one digit.  Chunks 0-1 hold the block's 32 int8 quants as words
+// (word k: elements 4k..4k+3), chunk 6 holds (-8 * sum_j q_j, 0, 0, d_x as
+// f32 bits), in the same swizzled 128-byte slot as the three-digit image.
+// Called by one thread per block: the 34-byte block at xb (2-byte aligned).
+__device__ __forceinline__ void q8_block_image(const uint8_t *xb, uint32_t b, uint32_t *xsm) {
+  const uint16_t *h = reinterpret_cast<const uint16_t *>(xb);
+  const float d = h2f(__ldcg(h));
+  uint32_t w[8];
+  int sum = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    w[k] = static_cast<uint32_t>(__ldcg(h + 1 + 2 * k)) | (static_cast<uint32_t>(__ldcg(h + 2 + 2 * k)) << 16);
+    sum = dp4a_ss(0x01010101u, w[k], sum);
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) xsm[x_word(b, k >> 2, k & 3)] = w[k];
+  xsm[x_word(b, 6, 0)] = static_cast<uint32_t>(-8 * sum);
+  xsm[x_word(b, 6, 1)] = 0u;
+  xsm[x_word(b, 6, 2)] = 0u;
+  xsm[x_word(b, 6, 3)] = __float_as_uint(d);
+}
+
+// Row sums of one item against a Q8_0 activation image (q8_block_image):
+// sum_j (n_j - 8) * q_j exactly in int32 (one dp4a chain), times d_w * d_x.
+template <int G>
+__device__ __forceinline__ void item_rows_q8act(const uint8_t *sbase, uint32_t group_bytes, uint32_t nb,
+                                                uint32_t lane, uint32_t b, const uint32_t *xsm,
+                                                float (&acc)[4 * G]) {
+  const uint4 *xb = reinterpret_cast<const uint4 *>(xsm + b * 32);
+  const uint32_t sw = b & 7;
+  const uint4 v0 = xb[0 ^ sw], v1 = xb[1 ^ sw], meta = xb[6 ^ sw];
+  const uint32_t D[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+  const int off = static_cast<int>(meta.x);
+  const float dx = __uint_as_float(meta.w);
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const uint8_t *cb = sbase + g * group_bytes;
+    const uint2 sc = *reinterpret_cast<const uint2 *>(cb + 4 * nb * 16 + lane * 8);
+    const float d[4] = {h2f(sc.x & 0xFFFF), h2f(sc.x >> 16), h2f(sc.y & 0xFFFF), h2f(sc.y >> 16)};
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const uint4 q = *reinterpret_cast<const uint4 *>(cb + r * nb * 16 + lane * 16);
+      const uint32_t wq[4] = {q.x, q.y, q.z, q.w};
+      int s = off;
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        s = dp4a_us(wq[m] & 0x0F0F0F0Fu, D[m], s);
+        s = dp4a_us((wq[m] >> 4) & 0x0F0F0F0Fu, D[m + 4], s);
+      }
+      acc[4 * g + r] = __fmul_rn(d[r], dx) * static_cast<float>(s);
+    }
+  }
+}
+
 }  // namespace zgpu

@@ -51,11 +51,13 @@ struct GemvDesc {
   bool seg_dynamic = false;
 };
 
-enum GemvPro { PRO_PLAIN = 0, PRO_RMSNORM = 1 };
+// PRO_Q8ACT: the input is Q8_0 blocks (34 bytes each: fp16 d, 32 int8) and
+// the weights Q4_0 (the Q4_0 x Q8_0 GEMV of BASELINE config 1); store only.
+enum GemvPro { PRO_PLAIN = 0, PRO_RMSNORM = 1, PRO_Q8ACT = 2 };
 enum GemvEpi { EPI_STORE = 0, EPI_RESADD = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
 
 struct GemvIo {
-  const float *x = nullptr;        // input vector (the residual for PRO_RMSNORM)
+  const float *x = nullptr;        // input vector (the residual for PRO_RMSNORM; Q8_0 blocks for PRO_Q8ACT)
   const float *norm_w = nullptr;   // RMSNorm gain (PRO_RMSNORM)
   float eps = 0.f;
   float *out = nullptr;            // STORE / RESADD / SWIGLU / ARGMAX (logits)

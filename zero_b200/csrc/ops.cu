@@ -159,46 +159,6 @@ __global__ void quantize_q8_0_kernel(const float *x, uint8_t *out, uint64_t nblo
   }
 }
 
-// Q4_0 weight x Q8_0 activation GEMV (no counterpart in the reference, whose
-// decode multiplies f32 activations).  One warp per output row over the
-// layout.h device layout; per block the integer dot sum_j (n_j - 8) * q_j is formed
-// exactly with dp4a, then scaled as (sumi * d_w) * d_x and accumulated.
-__global__ void q8act_gemv_kernel(const uint8_t *w, uint64_t gstride, uint32_t rows, uint32_t bpr,
-                                  const uint8_t *xq, float *out) {
-  const uint32_t row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const uint32_t lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const uint32_t l = row & 3;
-  const uint8_t *grp = w + static_cast<uint64_t>(row >> 2) * gstride;
-  float acc = 0.f;
-  for (uint32_t b = lane; b < bpr; b += 32) {
-    const uint8_t *sc = grp + scale_entry(ZGPU_Q4_0, bpr, b) + 2 * l;
-    const float dw = h2f(static_cast<uint16_t>(sc[0] | (sc[1] << 8)));
-    const uint4 qv = *reinterpret_cast<const uint4 *>(grp + plane_entry(ZGPU_Q4_0, bpr, b, l));
-    const uint32_t q[4] = {qv.x, qv.y, qv.z, qv.w};
-    const uint8_t *xb = xq + static_cast<uint64_t>(b) * 34;
-    const float dx = h2f(static_cast<uint16_t>(xb[0] | (xb[1] << 8)));
-    uint32_t xw[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k)
-      xw[k] = static_cast<uint32_t>(xb[2 + 4 * k]) | (static_cast<uint32_t>(xb[3 + 4 * k]) << 8) |
-              (static_cast<uint32_t>(xb[4 + 4 * k]) << 16) | (static_cast<uint32_t>(xb[5 + 4 * k]) << 24);
-    int sumi = 0, sumq = 0;
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      sumi = __dp4a(static_cast<int>(q[m] & 0x0F0F0F0Fu), static_cast<int>(xw[m]), sumi);
-      sumi = __dp4a(static_cast<int>((q[m] >> 4) & 0x0F0F0F0Fu), static_cast<int>(xw[m + 4]), sumi);
-      sumq = __dp4a(0x01010101, static_cast<int>(xw[m]), sumq);
-      sumq = __dp4a(0x01010101, static_cast<int>(xw[m + 4]), sumq);
-    }
-    sumi -= 8 * sumq;
-    acc += __fmul_rn(__fmul_rn(static_cast<float>(sumi), dw), dx);
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) out[row] = acc;
-}
-
 cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem, const LaunchCfg &lc,
                             cudaLaunchAttribute *attr) {
   cudaLaunchConfig_t cfg = {};
@@ -253,14 +213,6 @@ cudaError_t launch_silu_mul(const float *g, const float *u, float *out, uint64_t
                             cudaStream_t s) {
   const uint64_t blocks = (n + 255) / 256;
   silu_mul_kernel<<<static_cast<unsigned>(blocks < 4096 ? blocks : 4096), 256, 0, s>>>(g, u, out, n);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_q8act_gemv(const uint8_t *w, uint64_t gstride, uint32_t rows, uint32_t bpr,
-                              const uint8_t *xq, float *out, cudaStream_t s) {
-  const uint64_t threads = static_cast<uint64_t>(rows) * 32;
-  q8act_gemv_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, s>>>(w, gstride, rows,
-                                                                                  bpr, xq, out);
   return cudaGetLastError();
 }
 

@@ -208,8 +208,6 @@ cudaError_t launch_rope(float *qk, const float *inv_freqs, uint32_t n_heads, uin
                         uint32_t pos, cudaStream_t s);
 cudaError_t launch_silu_mul(const float *g, const float *u, float *out, uint64_t n,
                             cudaStream_t s);
-cudaError_t launch_q8act_gemv(const uint8_t *w, uint64_t gstride, uint32_t rows, uint32_t bpr,
-                              const uint8_t *xq, float *out, cudaStream_t s);
 cudaError_t launch_quantize_q8_0(const float *x, uint8_t *out, uint64_t n, uint32_t *status,
                                  cudaStream_t s);
 
