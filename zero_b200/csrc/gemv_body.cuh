@@ -237,13 +237,19 @@ __device__ __forceinline__ void item_rows(const uint8_t *sbase, uint32_t group_b
 // f32 bits), in the same swizzled 128-byte slot as the three-digit image.
 // Called by one thread per block: the 34-byte block at xb (2-byte aligned).
 __device__ __forceinline__ void q8_block_image(const uint8_t *xb, uint32_t b, uint32_t *xsm) {
+  // all 17 halfwords are loaded before any is used, so that the loads are in
+  // flight together (the block is read once, after the launch's dependency
+  // wait: plain loads)
   const uint16_t *h = reinterpret_cast<const uint16_t *>(xb);
-  const float d = h2f(__ldcg(h));
+  uint16_t hw[17];
+#pragma unroll
+  for (int k = 0; k < 17; ++k) hw[k] = h[k];
+  const float d = h2f(hw[0]);
   uint32_t w[8];
   int sum = 0;
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    w[k] = static_cast<uint32_t>(__ldcg(h + 1 + 2 * k)) | (static_cast<uint32_t>(__ldcg(h + 2 + 2 * k)) << 16);
+    w[k] = static_cast<uint32_t>(hw[1 + 2 * k]) | (static_cast<uint32_t>(hw[2 + 2 * k]) << 16);
     sum = dp4a_ss(0x01010101u, w[k], sum);
   }
 #pragma unroll
