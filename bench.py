@@ -34,7 +34,9 @@ Other workloads (--workload), each printing the same kind of line:
                     --batch 16, sixteen sequences per step (zgpu_decode_batch,
                     one GPU)
   ds2               BASELINE config 3's model (MLA + MoE), one sequence;
-                    expert parallel over the torchrun ranks
+                    expert parallel over the torchrun ranks; with --batch 32,
+                    the config's 32 concurrent sequences per step
+                    (zgpu_ds2_decode_batch)
   prefill           BASELINE config 4: a 2048-token prompt (--batch 8: eight)
   kquant            the GGUF-compat Q4_K / Q6_K GEMVs of one token at
                     Qwen3-1.7B shape, HBM GB/s
@@ -102,7 +104,8 @@ def parse():
                          "MLA+MoE model, one sequence, as a secondary line")
     ap.add_argument("--context", type=int, default=2048, help="ds2: tokens in the cache before decode")
     ap.add_argument("--batch", type=int, default=1, help="prefill: prompts per step (BASELINE config 4: 1 or 8); "
-                    "qwen3-8b: sequences decoded together (BASELINE config 2: 1 or 16)")
+                    "qwen3-8b: sequences decoded together (BASELINE config 2: 1 or 16); "
+                    "ds2: sequences decoded together (BASELINE config 3: 32, at most 32)")
     return ap.parse_args()
 
 
@@ -446,6 +449,154 @@ def run_ds2(args, rank, world, local):
         }
         print(json.dumps(line), flush=True)
     kv.close()
+    model.close()
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+DS2_BATCH_METRIC = "decode tok/s, DeepSeek-V2-Lite-shape MLA+MoE Q4_0, 32 concurrent sequences, context 2048"
+
+
+def run_ds2_batch(args, rank, world, local):
+    """BASELINE config 3 at its serving shape: --batch sequences (32), each
+    with its own MLA cache holding --context tokens, decoded together by
+    zgpu_ds2_decode_batch; with N > 1 ranks the experts are sharded (expert
+    parallel) and every rank runs the same batch.  One cache is filled by a
+    seeded prompt and copied on the device to the others
+    (zgpu_mla_kv_copy); each sequence then continues from its own seeded
+    token.  A step is one batched greedy step of every sequence."""
+    import torch
+
+    import zero_b200 as zb
+    synth = synth_module(args)
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the ds2 secondary line has no reference arm: "
+                              "the reference re-expands the latent cache per token (hours per step at "
+                              "context 2048); see cpu_baseline on the zero_b200 line"}), flush=True)
+        return
+    cfg = synth.DS2_V2_LITE
+    n_seq = args.batch
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        from zero_b200 import tp
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    weights = synth.ds2_weights(cfg, seed=SEED)
+    prompt = synth.ds2_prompt_ids(cfg, args.context, seed=SEED)
+    ctx = zb.Context(device=local)
+    model = zb.Ds2Model(ctx, cfg, weights, rank=rank, world=world)
+    if world > 1:
+        tp.connect(model)
+    max_tokens = args.context + args.warmup + args.steps + 2
+    fill = model.new_kv(max_tokens)
+    model.generate_greedy(fill, prompt, 1)        # context tokens into the first cache
+    kvs = [fill] + [model.new_kv(max_tokens) for _ in range(n_seq - 1)]
+    for kv in kvs[1:]:
+        kv.copy_from(fill, args.context)
+    tokens = synth.ds2_prompt_ids(cfg, n_seq, seed=SEED + 1)
+    pos = np.full(n_seq, args.context, np.uint32)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    barrier()
+    for _ in range(args.warmup):
+        tokens, _ = model.decode_batch(kvs, tokens, pos, want_logits=False)
+        pos = pos + 1
+    barrier()
+    dev_ms = 0.0
+    launches = 0
+    first = []
+    with ClockSampler(physical_gpu_index(local)) as clocks:
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            tokens, _ = model.decode_batch(kvs, tokens, pos, want_logits=False)
+            pos = pos + 1
+            p = model.perf()
+            dev_ms += float(p["decode_ms"])
+            launches += int(p["decode_launches"])
+            if i == 0:
+                first = [int(v) for v in tokens[:4]]
+        barrier()
+        wall_s = time.perf_counter() - t0
+    ids, _ = model.batch_expert_ids(n_seq)
+    if world > 1:
+        t = torch.tensor([dev_ms, wall_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_ms, wall_s = float(t[0].item()), float(t[1].item())
+    tok_s = n_seq * args.steps / (dev_ms / 1000.0)
+    e2e_tok_s = n_seq * args.steps / wall_s
+    # algorithmic bytes of one batched step: every non-expert weight once,
+    # the shared experts and the distinct routed experts the batch selected
+    # (counted on the last step's ids) once each, n_seq embedding rows, and
+    # every sequence's latent cache rows
+    q4 = 18 / 32
+    H = cfg.hidden
+    expert_b = 3 * cfg.expert_ffn * H * q4
+    n_moe = cfg.n_layers - cfg.n_dense
+    distinct = [len(np.unique(ids[layer])) for layer in range(cfg.n_dense, cfg.n_layers)]
+    single_w = cfg.weight_bytes_per_token()
+    embd_row = H * (34 / 32 if cfg.embd_quant == "q8_0" else q4)
+    step_w = single_w - n_moe * cfg.top_k * expert_b + sum(distinct) * expert_b + (n_seq - 1) * embd_row
+    ctx_mean = args.context + args.warmup + (args.steps + 1) / 2
+    cache_b = n_seq * cfg.cache_bytes_per_token() * ctx_mean
+    step_bytes = step_w + cache_b
+    gbs = step_bytes * args.steps / (dev_ms / 1000.0) / 1e9
+    peaks = measured_peaks()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle as O
+
+        r = O.OracleDs2Run(cfg, weights, 8)
+        t0 = time.perf_counter()
+        rc, _, _, _ = r.generate(prompt[:4], 3)
+        dt = time.perf_counter() - t0
+        cpu = {"value": round(6 / dt, 4), "unit": "tok/s", "cores": 1, "kind": "port",
+               "sample": f"one sequence: 4-token prompt + 2 decode steps (6 forwards, context <= 6), "
+                         f"scalar restatement, 1 thread, {dt:.1f} s; rc={rc} (the reference decodes "
+                         f"concurrent sequences one forward at a time)"}
+    if rank == 0:
+        line = {
+            "metric": DS2_BATCH_METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random-init, BASELINE config 3 shapes)",
+            "config": {"workload": f"deepseek-v2-lite-shape mla+moe q4_0 decode, {n_seq} sequences "
+                                   f"(BASELINE config 3)",
+                       "context": args.context, "batch": n_seq, "decode_steps": args.steps,
+                       "layers": cfg.n_layers,
+                       "experts": f"{cfg.n_experts} routed top-{cfg.top_k} + {cfg.n_shared} shared",
+                       "distinct_experts_per_moe_layer": round(sum(distinct) / max(len(distinct), 1), 1),
+                       "q_lora_rank": cfg.q_lora_rank,
+                       "l2": "inputs larger than L2 (weights and 32 latent caches, several GB per step)",
+                       "parallelism": f"ep{world} (experts sharded; router, attention, shared experts "
+                                      f"replicated)" if world > 1 else "single GPU",
+                       "tokens_first": first},
+            "roofline": {"bound": "hbm", "kernel": "per-op decode kernels widened over the batch (CUDA graph)",
+                         "per": "GPU" if world == 1 else "step (all ranks' bytes over the slowest rank's time)",
+                         "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
+                         "traffic": None, "algorithmic_bytes_per_step": int(step_bytes),
+                         "cache_bytes_per_step": int(cache_b)},
+            "e2e": {"value": round(e2e_tok_s, 2), "unit": "tok/s",
+                    "h2d_bytes_per_step": n_seq * (4 + 4 + 8), "d2h_bytes_per_step": n_seq * 4 + 4},
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    for kv in kvs:
+        kv.close()
     model.close()
     ctx.close()
     if world > 1:
@@ -1023,7 +1174,10 @@ def main():
             import torch
 
             torch.cuda.set_device(local)
-        run_ds2(args, rank, world, local)
+        if args.batch > 1:
+            run_ds2_batch(args, rank, world, local)
+        else:
+            run_ds2(args, rank, world, local)
         return
     if args.workload == "qwen3-8b":
         if args.batch > 1:

@@ -423,6 +423,12 @@ zgpu_status zgpu_mla_kv_store(zgpu_mla_kv *kv, uint32_t layer, uint32_t token, c
  * token_count rows of kv_lora_rank + rope_dim floats copied to host. */
 zgpu_status zgpu_mla_kv_read(zgpu_mla_kv *kv, uint32_t layer, uint32_t token_count,
                              float *rows_out);
+/* Device-to-device copy of rows [0, token_count) of every layer from src to
+ * dst (same context and geometry), stream-ordered: a sequence forked from a
+ * shared prompt without a second prefill.  Not in the reference (MlaKvCache
+ * has no clone); the serving bench uses it to give 32 sequences one filled
+ * context. */
+zgpu_status zgpu_mla_kv_copy(zgpu_mla_kv *dst, const zgpu_mla_kv *src, uint32_t token_count);
 
 /* ------------------------------------------------- DeepSeek2 model */
 typedef struct zgpu_ds2_model zgpu_ds2_model;
@@ -533,6 +539,25 @@ zgpu_status zgpu_ds2_expert_ids(zgpu_ds2_model *m, uint32_t *ids_out, float *wei
 zgpu_status zgpu_ds2_generate_greedy(zgpu_ds2_model *m, zgpu_mla_kv *kv, const uint32_t *prompt,
                                      uint32_t n_prompt, uint32_t n_gen, uint32_t *tokens_out,
                                      float *logits_out);
+/* One decode step of n_seq (1..32) independent sequences, each with its own
+ * MLA cache (all of one capacity, none twice) at its own position: for every
+ * b, the result equals zgpu_ds2_forward_single_token(kvs[b], tokens[b],
+ * positions[b]) followed by zgpu_ds2_lm_head_argmax(vocab_real) bit for bit
+ * (tokens_out[b], logits row b of n_seq x vocab_padded when logits_out is
+ * not NULL; the cache rows appended).  It replaces the serving loop that
+ * calls forward_single_token_deepseek2 (forward_pass.rs:703-909) and
+ * lm_head_argmax_dynamic (lm_head.rs:98-166) once per sequence: each
+ * weight tile is fetched once per step for the whole batch.  With expert
+ * parallelism every rank makes the same call; each rank runs its own
+ * experts for every token that selected them and the outputs cross NVLink as
+ * in the one-token step.  MLA layers only (a model with MHA layers returns
+ * ZGPU_ERR_INVALID_ARG). */
+zgpu_status zgpu_ds2_decode_batch(zgpu_ds2_model *m, zgpu_mla_kv *const *kvs, uint32_t n_seq,
+                                  const uint32_t *tokens, const uint32_t *positions, uint32_t *tokens_out,
+                                  float *logits_out);
+/* Expert ids / weights of the last zgpu_ds2_decode_batch: [n_layers][n_seq][top_k]
+ * each (zeros for dense layers); either may be NULL. */
+zgpu_status zgpu_ds2_batch_expert_ids(zgpu_ds2_model *m, uint32_t n_seq, uint32_t *ids_out, float *weights_out);
 zgpu_status zgpu_ds2_perf_snapshot(const zgpu_ds2_model *m, zgpu_perf *out);
 
 /* ------------------------------------------ synthetic .smodel generation */

@@ -17,6 +17,7 @@ import torch
 import torch.multiprocessing as mp
 
 import zero_b200 as zb
+from ds2_batch_steps import prefill, prompts_for, run_batch
 from zero_b200 import synth
 
 pytestmark = pytest.mark.gpu
@@ -36,6 +37,7 @@ VARIANTS = {
 SKEWED = {"8experts_top3_all_on_rank0"}
 CASES = [(name, 2) for name in VARIANTS] + [("16experts_top6_no_shared", 4)]
 PROMPT_LEN, N_GEN, MAX_TOKENS = 7, 10, 48
+BATCH_SEQ, BATCH_STEPS = 6, 4
 
 
 def _weights(name, cfg):
@@ -55,7 +57,18 @@ def _free_port() -> int:
     return port
 
 
-def _rank(rank, world, port, name, q):
+def _batch(m, cfg):
+    """Batched steps of BATCH_SEQ sequences with prompts of different lengths."""
+    prompts = prompts_for(cfg, BATCH_SEQ, 42)
+    kvs = [m.new_kv(MAX_TOKENS) for _ in prompts]
+    prefill(m, kvs, prompts)
+    toks, logits, ids = run_batch(m, kvs, prompts, BATCH_STEPS)
+    for kv in kvs:
+        kv.close()
+    return toks, logits, ids
+
+
+def _rank(rank, world, port, name, q, batch=False):
     import torch.distributed as dist
 
     from zero_b200 import tp
@@ -67,12 +80,15 @@ def _rank(rank, world, port, name, q):
         w = _weights(name, cfg)
         m = zb.Ds2Model(ctx, cfg, w, rank=rank, world=world)
         tp.connect(m)
-        prompt = synth.ds2_prompt_ids(cfg, PROMPT_LEN, seed=41)
-        kv = m.new_kv(MAX_TOKENS)
-        toks, logits = m.generate_greedy(kv, prompt, N_GEN, want_logits=True)
-        ids, _ = m.expert_ids()
+        if batch:
+            toks, logits, ids = _batch(m, cfg)
+        else:
+            prompt = synth.ds2_prompt_ids(cfg, PROMPT_LEN, seed=41)
+            kv = m.new_kv(MAX_TOKENS)
+            toks, logits = m.generate_greedy(kv, prompt, N_GEN, want_logits=True)
+            ids, _ = m.expert_ids()
+            kv.close()
         dist.barrier()
-        kv.close()
         m.close()
         ctx.close()
         q.put((rank, toks, logits, ids, None))
@@ -82,15 +98,11 @@ def _rank(rank, world, port, name, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("name,world", CASES, ids=[f"{n}-ep{w}" for n, w in CASES])
-def test_expert_parallel_decode_equals_one_gpu(name, world):
-    if torch.cuda.device_count() < world:
-        pytest.skip(f"needs {world} GPUs")
-    cfg_kw = VARIANTS[name]
+def _spawn(name, world, batch):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, name, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, name, q, batch)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -105,7 +117,15 @@ def test_expert_parallel_decode_equals_one_gpu(name, world):
                 p.kill()
     for r in range(world):
         assert res[r][3] is None, res[r][3]
-    cfg = synth.ds2_small_config(**cfg_kw)
+    return res
+
+
+@pytest.mark.parametrize("name,world", CASES, ids=[f"{n}-ep{w}" for n, w in CASES])
+def test_expert_parallel_decode_equals_one_gpu(name, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = _spawn(name, world, False)
+    cfg = synth.ds2_small_config(**VARIANTS[name])
     c1 = zb.Context(device=0)
     m1 = zb.Ds2Model(c1, cfg, _weights(name, cfg))
     kv = m1.new_kv(MAX_TOKENS)
@@ -123,3 +143,28 @@ def test_expert_parallel_decode_equals_one_gpu(name, world):
     if name in SKEWED:   # the routing really was all on rank 0
         moe = np.asarray(ref_ids)[cfg.n_dense:]
         assert moe.size and (moe < cfg.n_experts // world).all(), moe
+
+
+BATCH_CASES = [("8experts_top3_2shared", 2), ("8experts_top3_all_on_rank0", 2), ("16experts_top6_no_shared", 4)]
+
+
+@pytest.mark.parametrize("name,world", BATCH_CASES, ids=[f"{n}-ep{w}" for n, w in BATCH_CASES])
+def test_expert_parallel_batch_equals_one_gpu(name, world):
+    """zgpu_ds2_decode_batch with the experts sharded: every rank's tokens,
+    logits and expert ids equal the one-GPU batch bit for bit (each rank runs
+    its experts for every token that selected them; the outputs of all
+    tokens cross in one publish per MoE layer)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = _spawn(name, world, True)
+    cfg = synth.ds2_small_config(**VARIANTS[name])
+    c1 = zb.Context(device=0)
+    m1 = zb.Ds2Model(c1, cfg, _weights(name, cfg))
+    ref_toks, ref_logits, ref_ids = _batch(m1, cfg)
+    m1.close()
+    c1.close()
+    for r in range(world):
+        toks, logits, ids, _ = res[r]
+        assert np.array_equal(toks, ref_toks), (r, toks, ref_toks)
+        assert np.array_equal(logits.view(np.uint32), ref_logits.view(np.uint32)), r
+        assert np.array_equal(ids[:, cfg.n_dense:], ref_ids[:, cfg.n_dense:]), r

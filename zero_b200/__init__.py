@@ -454,6 +454,10 @@ class MlaKvCache:
         self.ctx._check(LIB.zgpu_mla_kv_read(self.h, layer, token_count, _ptr(out)))
         return out
 
+    def copy_from(self, src: "MlaKvCache", token_count: int) -> None:
+        """Rows [0, token_count) of every layer of src, copied on the device (zgpu_mla_kv_copy)."""
+        self.ctx._check(LIB.zgpu_mla_kv_copy(self.h, src.h, token_count))
+
 
 class MhaKvCache:
     """MhaKvCache (kv_cache.rs:433-560) in device memory: per MHA layer a K
@@ -589,6 +593,30 @@ class Ds2Model:
         self.ctx._check(LIB.zgpu_ds2_generate_greedy(self.h, kv.h, _ptr(p), p.size, n_gen, _ptr(toks),
                                                      _ptr(logits) if want_logits else None))
         return toks, logits
+
+    def decode_batch(self, kvs, tokens, positions, want_logits: bool = True):
+        """zgpu_ds2_decode_batch: one greedy step for len(kvs) sequences,
+        sequence i feeding tokens[i] at positions[i] of its own cache; returns
+        (next tokens [n_seq], logits [n_seq, vocab_padded] or None)."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        pos = np.ascontiguousarray(positions, np.uint32)
+        n_seq = len(kvs)
+        if t.size != n_seq or pos.size != n_seq:
+            raise ValueError("one token and one position per sequence")
+        handles = (C.c_void_p * n_seq)(*[kv.h.value if isinstance(kv.h, C.c_void_p) else kv.h for kv in kvs])
+        toks = np.empty(n_seq, np.uint32)
+        logits = np.empty((n_seq, self.cfg.vocab_padded), np.float32) if want_logits else None
+        self.ctx._check(LIB.zgpu_ds2_decode_batch(self.h, handles, n_seq, _ptr(t), _ptr(pos), _ptr(toks),
+                                                  _ptr(logits) if want_logits else None))
+        return toks, logits
+
+    def batch_expert_ids(self, n_seq: int):
+        """[n_layers][n_seq][top_k] expert ids and weights of the last decode_batch."""
+        k = self.cfg.top_k
+        ids = np.empty((self.cfg.n_layers, n_seq, k), np.uint32)
+        wts = np.empty((self.cfg.n_layers, n_seq, k), np.float32)
+        self.ctx._check(LIB.zgpu_ds2_batch_expert_ids(self.h, n_seq, _ptr(ids), _ptr(wts)))
+        return ids, wts
 
     def perf(self) -> dict:
         p = ZgpuPerf()

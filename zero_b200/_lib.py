@@ -158,6 +158,7 @@ _SIGS = {
     "zgpu_mla_kv_destroy": (None, [_vp]),
     "zgpu_mla_kv_store": (_i32, [_vp, _u32, _u32, _vp, _vp]),
     "zgpu_mla_kv_read": (_i32, [_vp, _u32, _u32, _vp]),
+    "zgpu_mla_kv_copy": (_i32, [_vp, _vp, _u32]),
     "zgpu_ds2_create_ep": (_i32, [_vp, C.POINTER(ZgpuDs2Desc), _u32, _u32, C.POINTER(_vp)]),
     "zgpu_ds2_ep_export": (_i32, [_vp, _vp]),
     "zgpu_ds2_ep_connect": (_i32, [_vp, _vp]),
@@ -167,6 +168,8 @@ _SIGS = {
     "zgpu_ds2_lm_head_argmax": (_i32, [_vp, _u32, _vp, _vp]),
     "zgpu_ds2_expert_ids": (_i32, [_vp, _vp, _vp]),
     "zgpu_ds2_generate_greedy": (_i32, [_vp, _vp, _vp, _u32, _u32, _vp, _vp]),
+    "zgpu_ds2_decode_batch": (_i32, [_vp, _vp, _u32, _vp, _vp, _vp, _vp]),
+    "zgpu_ds2_batch_expert_ids": (_i32, [_vp, _u32, _vp, _vp]),
     "zgpu_ds2_perf_snapshot": (_i32, [_vp, C.POINTER(ZgpuPerf)]),
     "zgpu_synth_q4_0": (None, [_u64, _u64, _u64, _u64, _f, _vp]),
     "zgpu_synth_q8_0": (None, [_u64, _u64, _u64, _u64, _f, _vp]),

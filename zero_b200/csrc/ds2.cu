@@ -57,6 +57,9 @@ struct zgpu_mha_kv {
 namespace {
 
 constexpr uint32_t kMaxEpRanks = 8;
+// Sequences of one zgpu_ds2_decode_batch call (the expert exchange buffers
+// are sized for it when the model is created).
+constexpr uint32_t kDs2MaxBatch = 32;
 
 struct Ds2Layer {
   // attention
@@ -127,6 +130,22 @@ struct zgpu_ds2_model {
   zgpu_mha_kv *mha_kv = nullptr;
   float *d_mha_qkv = nullptr, *d_mha_part = nullptr;
   uint32_t mha_splits = 0;
+  // zgpu_ds2_decode_batch: per-sequence activations of kDs2MaxBatch
+  // sequences, allocated by the first batch call.  Sequence b's vectors sit
+  // at b times the one-sequence sizes; the router writes layer l's ids,
+  // weights and dispatch tables at l times the batch's sizes.
+  struct Batch {
+    float *hidden = nullptr, *ca = nullptr, *q = nullptr, *qabs = nullptr, *qpe = nullptr, *ctx = nullptr,
+          *concat = nullptr, *act = nullptr, *expout = nullptr, *scores = nullptr, *logits = nullptr,
+          *wts = nullptr, *part = nullptr;
+    uint32_t *ids = nullptr, *counter = nullptr, *tok = nullptr, *pos = nullptr, *out = nullptr,
+             *codes = nullptr;
+    unsigned long long *seg = nullptr;   // per layer: gate|up table then down table, kDs2MaxBatch*n_seg each
+    float **cache = nullptr;             // [kDs2MaxBatch] each sequence's zgpu_mla_kv rows
+    uint32_t ca_stride = 0, act_stride = 0, splits = 0, max_tokens = 0;
+    cudaGraphExec_t graph = nullptr;
+    uint32_t graph_n = 0, graph_kernels = 0;
+  } b;
 };
 
 namespace {
@@ -403,6 +422,7 @@ cudaError_t ds2_enqueue_forward(zgpu_ds2_model *m, zgpu_mla_kv *kv, uint32_t *co
       pp.world = m->world;
       pp.ep_rank = m->rank;
       pp.ep_per_rank = m->ep_per_rank;
+      pp.slot_cap = d.top_k * kDs2MaxBatch;
       if ((e = launch_moe_ep_publish(pp, lc)) != cudaSuccess) return e;
     }
     CombineParams cp = {};
@@ -415,6 +435,7 @@ cudaError_t ds2_enqueue_forward(zgpu_ds2_model *m, zgpu_mla_kv *kv, uint32_t *co
     cp.xslots = m->world > 1 ? m->d_xslots : nullptr;
     cp.ep_seq = m->d_ep_seq;
     cp.world = m->world;
+    cp.slot_cap = d.top_k * kDs2MaxBatch;
     cp.status = m->d_status;
     if ((e = launch_moe_combine(cp, lc)) != cudaSuccess) return e;
     if (m->world > 1 && (e = launch_moe_ep_advance(m->d_ep_seq, lc)) != cudaSuccess) return e;
@@ -448,6 +469,299 @@ cudaError_t ds2_enqueue_lm_head(zgpu_ds2_model *m, uint32_t *counter) {
   fp.tokens_out = m->d_tokens;
   fp.status = m->d_status;
   return launch_finalize(fp, lc);
+}
+
+// One decode step of ns sequences (each at its own position of its own
+// cache): the single-sequence kernel sequence with every launch widened over
+// the batch, so each sequence's arithmetic, and so its results, are those of
+// zgpu_ds2_forward_single_token + zgpu_ds2_lm_head_argmax bit for bit.  The
+// projections are same-weight segmented GEMVs (segment b = sequence b), the
+// MLA kernels and the router take the sequence as grid dimension y, and the
+// grouped expert GEMVs run ns * (n_shared + top_k) segments from the
+// router's per-token tables.  MLA layers only.
+cudaError_t ds2_enqueue_batch(zgpu_ds2_model *m, uint32_t ns, uint32_t *counter) {
+  const zgpu_ds2_desc &d = m->desc;
+  auto &B = m->b;
+  LaunchCfg lc = launch_cfg(m, counter);
+  cudaError_t e = launch_rows_embed(m->emb->d, m->emb->gstride, m->emb->quant, d.hidden,
+                                    static_cast<uint32_t>(m->emb->rows), B.tok, ns, B.hidden, m->d_status, lc.stream);
+  if (counter) ++*counter;
+  if (e != cudaSuccess) return e;
+  const uint32_t H = d.hidden, R = d.kv_lora_rank, RD = d.rope_dim, QL = d.q_lora_rank;
+  const uint32_t NH = d.n_heads, hq = d.nope_dim + d.rope_dim, VD = d.v_dim;
+  const uint32_t n_seg = d.n_shared + d.top_k;
+  for (uint32_t l = 0; l < d.n_layers; ++l) {
+    const Ds2Layer &L = m->layers[l];
+    // RMSNorm + fused kv_a_mqa | q_a, one segment per sequence
+    GemvDesc g;
+    g.w = L.cat_a;
+    g.gstride = m->gs_h;
+    g.wbytes = static_cast<uint64_t>(L.cat_a_groups) * m->gs_h;
+    g.quant = d.attn_quant;
+    g.rows = R + RD + QL;
+    g.groups = L.cat_a_groups;
+    g.in_dim = H;
+    g.seg_count = ns;
+    g.seg_x_stride = H;
+    g.seg_out_stride = B.ca_stride;
+    GemvIo io;
+    io.x = B.hidden;
+    io.norm_w = L.attn_norm;
+    io.eps = d.rms_eps;
+    io.out = B.ca;
+    io.status = m->d_status;
+    if ((e = launch_gemv(g, PRO_RMSNORM, EPI_STORE, io, lc)) != cudaSuccess) return e;
+    // RMSNorm(c_q) + q_b
+    g = GemvDesc();
+    g.w = L.q_b->d;
+    g.gstride = L.q_b->gstride;
+    g.wbytes = L.q_b->bytes;
+    g.quant = d.attn_quant;
+    g.rows = NH * hq;
+    g.groups = static_cast<uint32_t>(L.q_b->groups);
+    g.in_dim = QL;
+    g.seg_count = ns;
+    g.seg_x_stride = B.ca_stride;
+    g.seg_out_stride = NH * hq;
+    io = GemvIo();
+    io.x = B.ca + R + RD;
+    io.norm_w = L.q_a_norm;
+    io.eps = d.rms_eps;
+    io.out = B.q;
+    io.status = m->d_status;
+    if ((e = launch_gemv(g, PRO_RMSNORM, EPI_STORE, io, lc)) != cudaSuccess) return e;
+    // latent append + query absorption, attention, merge: each sequence on
+    // its own cache rows and position
+    MlaParams mp = {};
+    mp.kv_a = B.ca;
+    mp.kv_a_norm = L.kv_a_norm;
+    mp.k_norm = L.k_norm;
+    mp.q = B.q;
+    mp.kb = L.kb->d;
+    mp.kb_gstride = L.kb->gstride;
+    mp.kb_quant = L.kb->quant;
+    mp.kb_head_rows = L.kb_head_rows;
+    mp.inv_freqs = m->d_inv_freqs;
+    mp.max_tokens = B.max_tokens;
+    mp.q_abs = B.qabs;
+    mp.q_pe = B.qpe;
+    mp.ctx = B.ctx;
+    mp.part = B.part;
+    mp.status = m->d_status;
+    mp.n_heads = NH;
+    mp.kv_lora = R;
+    mp.rope = RD;
+    mp.nope = d.nope_dim;
+    mp.max_splits = B.splits;
+    mp.eps = d.rms_eps;
+    mp.scale = 1.0f / sqrtf(static_cast<float>(hq));
+    mp.n_seq = ns;
+    mp.kv_a_stride = B.ca_stride;
+    mp.q_stride = NH * hq;
+    mp.seq_cache = B.cache;
+    mp.layer_off = static_cast<uint64_t>(l) * B.max_tokens * (R + RD);
+    mp.seq_pos = B.pos;
+    if ((e = launch_mla_prep(mp, lc)) != cudaSuccess) return e;
+    if ((e = launch_mla_attention(mp, lc)) != cudaSuccess) return e;
+    // per-head V projection: segment b * NH + h reads ctx row (b, h) and
+    // head h's v rows
+    g = GemvDesc();
+    g.gstride = L.v_gstride;
+    g.wbytes = L.v_seg_bytes;
+    g.quant = d.attn_quant;
+    g.rows = VD;
+    g.groups = VD / 4;
+    g.in_dim = R;
+    g.seg_w = L.d_vseg;
+    g.seg_w_mod = NH;
+    g.seg_count = ns * NH;
+    g.seg_x_stride = R;
+    g.seg_out_stride = VD;
+    io = GemvIo();
+    io.x = B.ctx;
+    io.out = B.concat;
+    io.status = m->d_status;
+    if ((e = launch_gemv(g, PRO_PLAIN, EPI_STORE, io, lc)) != cudaSuccess) return e;
+    // O projection + residual
+    g = GemvDesc();
+    g.w = L.o->d;
+    g.gstride = L.o->gstride;
+    g.wbytes = L.o->bytes;
+    g.quant = d.attn_quant;
+    g.rows = H;
+    g.groups = H / 4;
+    g.in_dim = NH * VD;
+    g.seg_count = ns;
+    g.seg_x_stride = NH * VD;
+    g.seg_out_stride = H;
+    io = GemvIo();
+    io.x = B.concat;
+    io.out = B.hidden;
+    io.status = m->d_status;
+    if ((e = launch_gemv(g, PRO_PLAIN, EPI_RESADD, io, lc)) != cudaSuccess) return e;
+
+    if (!L.moe) {
+      g = GemvDesc();
+      g.w = L.gateup;
+      g.gstride = m->gs_h;
+      g.wbytes = static_cast<uint64_t>(2 * d.ffn / 4) * m->gs_h;
+      g.quant = ZGPU_Q4_0;
+      g.rows = d.ffn;
+      g.groups = 2 * d.ffn / 4;
+      g.in_dim = H;
+      g.seg_count = ns;
+      g.seg_x_stride = H;
+      g.seg_out_stride = B.act_stride;
+      io = GemvIo();
+      io.x = B.hidden;
+      io.norm_w = L.ffn_norm;
+      io.eps = d.rms_eps;
+      io.out = B.act;
+      io.status = m->d_status;
+      if ((e = launch_gemv(g, PRO_RMSNORM, EPI_SWIGLU, io, lc)) != cudaSuccess) return e;
+      g = GemvDesc();
+      g.w = L.down->d;
+      g.gstride = L.down->gstride;
+      g.wbytes = L.down->bytes;
+      g.quant = ZGPU_Q4_0;
+      g.rows = H;
+      g.groups = H / 4;
+      g.in_dim = d.ffn;
+      g.seg_count = ns;
+      g.seg_x_stride = B.act_stride;
+      g.seg_out_stride = H;
+      io = GemvIo();
+      io.x = B.act;
+      io.out = B.hidden;
+      io.status = m->d_status;
+      if ((e = launch_gemv(g, PRO_PLAIN, EPI_RESADD, io, lc)) != cudaSuccess) return e;
+      continue;
+    }
+    const size_t tab = static_cast<size_t>(kDs2MaxBatch) * n_seg;
+    unsigned long long *seg_gu = B.seg + 2 * tab * l, *seg_dn = seg_gu + tab;
+    RouteParams rp = {};
+    rp.x = B.hidden;
+    rp.norm_w = L.ffn_norm;
+    rp.eps = d.rms_eps;
+    rp.w = reinterpret_cast<const float *>(L.router->d);
+    rp.bias = L.d_router_b;
+    rp.dim = H;
+    rp.n_experts = d.n_experts;
+    rp.top_k = d.top_k;
+    rp.mode = d.route_mode;
+    rp.scale = d.expert_weight_scale;
+    rp.scores = B.scores;
+    rp.ids = B.ids + static_cast<size_t>(l) * kDs2MaxBatch * d.top_k;
+    rp.weights = B.wts + static_cast<size_t>(l) * kDs2MaxBatch * d.top_k;
+    rp.counter = B.counter;
+    rp.seg_gu = seg_gu;
+    rp.seg_dn = seg_dn;
+    rp.gu_base = reinterpret_cast<unsigned long long>(L.gateup);
+    rp.dn_base = reinterpret_cast<unsigned long long>(L.down->d);
+    rp.sh_gu_base = reinterpret_cast<unsigned long long>(L.sh_gateup);
+    rp.sh_dn_base = L.sh_down ? reinterpret_cast<unsigned long long>(L.sh_down->d) : 0ull;
+    rp.gu_bytes = m->gu_bytes;
+    rp.dn_bytes = m->dn_bytes;
+    rp.n_shared = d.n_shared;
+    rp.status = m->d_status;
+    rp.ep_rank = m->rank;
+    rp.ep_per_rank = m->world > 1 ? m->ep_per_rank : 0;
+    rp.n_seq = ns;
+    rp.x_stride = H;
+    if ((e = launch_moe_route(rp, lc)) != cudaSuccess) return e;
+    // grouped gate|up + SiLU*up: segment b * n_seg + s is token b's s-th
+    // expert (shared ones first), all n_seg of them on token b's input
+    g = GemvDesc();
+    g.gstride = m->gs_h;
+    g.wbytes = m->gu_bytes;
+    g.quant = ZGPU_Q4_0;
+    g.rows = d.expert_ffn;
+    g.groups = 2 * d.expert_ffn / 4;
+    g.in_dim = H;
+    g.seg_w = seg_gu;
+    g.seg_count = ns * n_seg;
+    g.seg_x_stride = H;
+    g.seg_x_group = n_seg;
+    g.seg_out_stride = d.expert_ffn;
+    g.seg_dynamic = true;
+    io = GemvIo();
+    io.x = B.hidden;
+    io.norm_w = L.ffn_norm;
+    io.eps = d.rms_eps;
+    io.out = B.act;
+    io.status = m->d_status;
+    if ((e = launch_gemv(g, PRO_RMSNORM, EPI_SWIGLU, io, lc)) != cudaSuccess) return e;
+    g = GemvDesc();
+    g.gstride = m->gs_e;
+    g.wbytes = m->dn_bytes;
+    g.quant = ZGPU_Q4_0;
+    g.rows = H;
+    g.groups = H / 4;
+    g.in_dim = d.expert_ffn;
+    g.seg_w = seg_dn;
+    g.seg_count = ns * n_seg;
+    g.seg_x_stride = d.expert_ffn;
+    g.seg_out_stride = H;
+    g.seg_dynamic = true;
+    io = GemvIo();
+    io.x = B.act;
+    io.out = B.expout;
+    io.status = m->d_status;
+    if ((e = launch_gemv(g, PRO_PLAIN, EPI_STORE, io, lc)) != cudaSuccess) return e;
+    if (m->world > 1) {
+      EpPublishParams pp = {};
+      pp.exp_out = B.expout;
+      pp.ids = rp.ids;
+      pp.dst = m->d_ep_dst;
+      pp.ep_seq = m->d_ep_seq;
+      pp.dim = H;
+      pp.n_shared = d.n_shared;
+      pp.top_k = d.top_k;
+      pp.world = m->world;
+      pp.ep_rank = m->rank;
+      pp.ep_per_rank = m->ep_per_rank;
+      pp.n_seq = ns;
+      pp.slot_cap = d.top_k * kDs2MaxBatch;
+      if ((e = launch_moe_ep_publish(pp, lc)) != cudaSuccess) return e;
+    }
+    CombineParams cp = {};
+    cp.exp_out = B.expout;
+    cp.weights = rp.weights;
+    cp.hidden = B.hidden;
+    cp.dim = H;
+    cp.n_shared = d.n_shared;
+    cp.top_k = d.top_k;
+    cp.xslots = m->world > 1 ? m->d_xslots : nullptr;
+    cp.ep_seq = m->d_ep_seq;
+    cp.world = m->world;
+    cp.n_seq = ns;
+    cp.slot_cap = d.top_k * kDs2MaxBatch;
+    cp.status = m->d_status;
+    if ((e = launch_moe_combine(cp, lc)) != cudaSuccess) return e;
+    if (m->world > 1 && (e = launch_moe_ep_advance(m->d_ep_seq, lc)) != cudaSuccess) return e;
+  }
+  // LM head: RMSNorm + GEMV per sequence, then the reference's greedy pick
+  // per logits row
+  GemvDesc g;
+  g.w = m->out->d;
+  g.wbytes = m->out->bytes;
+  g.gstride = m->out->gstride;
+  g.quant = m->out->quant;
+  g.rows = d.vocab_padded;
+  g.groups = static_cast<uint32_t>(m->out->groups);
+  g.in_dim = H;
+  g.seg_count = ns;
+  g.seg_x_stride = H;
+  g.seg_out_stride = d.vocab_padded;
+  GemvIo io;
+  io.x = B.hidden;
+  io.norm_w = m->d_out_norm;
+  io.eps = d.rms_eps;
+  io.out = B.logits;
+  io.status = m->d_status;
+  if ((e = launch_gemv(g, PRO_RMSNORM, EPI_STORE, io, lc)) != cudaSuccess) return e;
+  if (counter) ++*counter;
+  return launch_rows_argmax(B.logits, ns, d.vocab_padded, d.vocab_real, B.out, B.codes, m->d_status, lc.stream);
 }
 
 enum GraphPart { GRAPH_STEP = 0, GRAPH_FWD = 1, GRAPH_LM = 2 };
@@ -543,6 +857,70 @@ zgpu_status ds2_prepare_kv(zgpu_ds2_model *m, zgpu_mla_kv *kv) {
   return ZGPU_OK;
 }
 
+void ds2_free_batch(zgpu_ds2_model *m) {
+  auto &B = m->b;
+  if (B.graph) cudaGraphExecDestroy(B.graph);
+  for (float *p : {B.hidden, B.ca, B.q, B.qabs, B.qpe, B.ctx, B.concat, B.act, B.expout, B.scores, B.logits,
+                   B.wts, B.part})
+    cudaFree(p);
+  for (uint32_t *p : {B.ids, B.counter, B.tok, B.pos, B.out, B.codes}) cudaFree(p);
+  cudaFree(B.seg);
+  cudaFree(B.cache);
+  B = zgpu_ds2_model::Batch();
+}
+
+// The batch buffers for caches of max_tokens rows (allocated once; the
+// attention scratch again when the cache capacity changes).
+zgpu_status ds2_prepare_batch(zgpu_ds2_model *m, uint32_t max_tokens) {
+  zgpu_ctx *ctx = m->ctx;
+  const zgpu_ds2_desc &d = m->desc;
+  auto &B = m->b;
+  const size_t NB = kDs2MaxBatch;
+  const uint32_t H = d.hidden, R = d.kv_lora_rank, RD = d.rope_dim, NH = d.n_heads;
+  const uint32_t n_seg = d.n_shared + d.top_k;
+  if (!B.hidden) {
+    bool any_moe = false, any_dense = false;
+    for (const Ds2Layer &L : m->layers) (L.moe ? any_moe : any_dense) = true;
+    B.ca_stride = R + RD + d.q_lora_rank + 8;
+    B.act_stride = static_cast<uint32_t>(std::max<size_t>(any_dense ? d.ffn : 0, static_cast<size_t>(n_seg) * d.expert_ffn));
+    const size_t topk = any_moe ? d.top_k : 1;
+    const size_t tab = NB * (n_seg ? n_seg : 1);
+    const uint32_t hq = d.nope_dim + RD;
+    if (cudaMalloc(&B.hidden, NB * H * 4) || cudaMalloc(&B.ca, NB * B.ca_stride * 4) ||
+        cudaMalloc(&B.q, NB * NH * hq * 4) || cudaMalloc(&B.qabs, NB * NH * R * 4) ||
+        cudaMalloc(&B.qpe, NB * NH * (RD ? RD : 1) * 4) || cudaMalloc(&B.ctx, NB * NH * R * 4) ||
+        cudaMalloc(&B.concat, NB * NH * d.v_dim * 4) || cudaMalloc(&B.act, NB * (B.act_stride ? B.act_stride : 1) * 4) ||
+        cudaMalloc(&B.expout, NB * (n_seg ? n_seg : 1) * H * 4) ||
+        cudaMalloc(&B.scores, NB * (d.n_experts ? d.n_experts : 1) * 4) ||
+        cudaMalloc(&B.logits, NB * d.vocab_padded * 4) || cudaMalloc(&B.wts, d.n_layers * NB * topk * 4) ||
+        cudaMalloc(&B.ids, d.n_layers * NB * topk * 4) || cudaMalloc(&B.counter, NB * 4) ||
+        cudaMalloc(&B.tok, NB * 4) || cudaMalloc(&B.pos, NB * 4) || cudaMalloc(&B.out, NB * 4) ||
+        cudaMalloc(&B.codes, NB * 4) || cudaMalloc(&B.seg, d.n_layers * 2 * tab * 8) ||
+        cudaMalloc(&B.cache, NB * sizeof(float *))) {
+      ds2_free_batch(m);
+      return zgpu_fail(ctx, ZGPU_ERR_OUT_OF_MEMORY, "batch activation buffers");
+    }
+    cudaMemset(B.counter, 0, NB * 4);
+    cudaMemset(B.seg, 0, d.n_layers * 2 * tab * 8);
+    cudaMemset(B.ids, 0, d.n_layers * NB * topk * 4);
+    cudaMemset(B.wts, 0, d.n_layers * NB * topk * 4);
+  }
+  const uint32_t splits = mla_max_splits(max_tokens);
+  if (splits != B.splits || max_tokens != B.max_tokens) {
+    cudaFree(B.part);
+    B.part = nullptr;
+    B.splits = 0;
+    if (B.graph) cudaGraphExecDestroy(B.graph);
+    B.graph = nullptr;
+    const size_t n = NB * NH * splits * (R + 2);
+    cudaError_t e = cudaMalloc(&B.part, n * 4);
+    if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "batch attention scratch");
+    B.splits = splits;
+    B.max_tokens = max_tokens;
+  }
+  return ZGPU_OK;
+}
+
 // Interleave two tensors' group streams: group j of a at 2j, of b at 2j+1.
 cudaError_t interleave_groups(uint8_t **dst, const DeviceTensor *a, const DeviceTensor *b) {
   cudaError_t e = cudaMalloc(dst, a->bytes + b->bytes);
@@ -619,6 +997,23 @@ zgpu_status zgpu_mla_kv_read(zgpu_mla_kv *kv, uint32_t layer, uint32_t token_cou
                                   cudaMemcpyDeviceToHost, ctx->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "mla cache read");
+  return ZGPU_OK;
+}
+
+zgpu_status zgpu_mla_kv_copy(zgpu_mla_kv *dst, const zgpu_mla_kv *src, uint32_t token_count) {
+  if (!dst || !src || dst == src) return ZGPU_ERR_INVALID_ARG;
+  zgpu_ctx *ctx = dst->ctx;
+  if (src->ctx != ctx || src->n_layers != dst->n_layers || src->kv_lora != dst->kv_lora || src->rope != dst->rope)
+    return zgpu_fail(ctx, ZGPU_ERR_KV_INVALID_SLICE_LENGTH, "mla cache copy: geometry differs");
+  if (token_count > src->max_tokens || token_count > dst->max_tokens)
+    return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_COUNT_EXCEEDS_MAX, "token count exceeds max_tokens");
+  cudaSetDevice(ctx->device);
+  const size_t row = static_cast<size_t>(token_count) * (src->kv_lora + src->rope) * 4;
+  cudaError_t e = cudaSuccess;
+  if (row)
+    e = cudaMemcpy2DAsync(dst->d, dst->layer_floats * 4, src->d, src->layer_floats * 4, row, src->n_layers,
+                          cudaMemcpyDeviceToDevice, ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "mla cache copy");
   return ZGPU_OK;
 }
 
@@ -780,6 +1175,7 @@ void zgpu_ds2_destroy(zgpu_ds2_model *m) {
   if (!m) return;
   cudaSetDevice(m->ctx->device);
   ds2_drop_graphs(m);
+  ds2_free_batch(m);
   for (Ds2Layer &L : m->layers) {
     cudaFree(L.cat_a);
     cudaFree(L.d_vseg);
@@ -1037,7 +1433,7 @@ zgpu_status ds2_create(zgpu_ctx *ctx, const zgpu_ds2_desc *d, uint32_t rank, uin
   m->world = world;
   m->ep_per_rank = world > 1 ? d->n_experts / world : 0;
   if (world > 1) {
-    const size_t xw = ep_exchange_words(d->top_k, H);
+    const size_t xw = ep_exchange_words(d->top_k * kDs2MaxBatch, H);
     if (cudaMalloc(&m->d_xslots, xw * 8) || cudaMalloc(&m->d_ep_seq, 4))
       return fail(ZGPU_ERR_OUT_OF_MEMORY, "expert-parallel exchange buffers");
     cudaMemset(m->d_xslots, 0, xw * 8);
@@ -1241,6 +1637,116 @@ zgpu_status zgpu_ds2_generate_greedy(zgpu_ds2_model *m, zgpu_mla_kv *kv, const u
   m->perf.decode_ms = dec;
   ctx->launches += launches;
   return zgpu_map_device_status(ctx, st);
+}
+
+zgpu_status zgpu_ds2_decode_batch(zgpu_ds2_model *m, zgpu_mla_kv *const *kvs, uint32_t n_seq,
+                                  const uint32_t *tokens, const uint32_t *positions, uint32_t *tokens_out,
+                                  float *logits_out) {
+  if (!m || !kvs || !tokens || !positions || !tokens_out || n_seq == 0) return ZGPU_ERR_INVALID_ARG;
+  zgpu_ctx *ctx = m->ctx;
+  if (n_seq > kDs2MaxBatch) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "ds2 batch: at most 32 sequences");
+  if (m->world > 1 && !m->ep_connected)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "expert parallel: zgpu_ds2_ep_connect first");
+  if (m->n_mha) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "ds2 batch: MLA layers only");
+  cudaSetDevice(ctx->device);
+  const zgpu_ds2_desc &d = m->desc;
+  const uint32_t max_tokens = kvs[0] ? kvs[0]->max_tokens : 0;
+  float *caches[kDs2MaxBatch];
+  for (uint32_t b = 0; b < n_seq; ++b) {
+    zgpu_mla_kv *kv = kvs[b];
+    if (!kv) return ZGPU_ERR_INVALID_ARG;
+    if (kv->n_layers != d.n_layers)
+      return zgpu_fail(ctx, ZGPU_ERR_KV_LAYER_OUT_OF_RANGE, "mla cache layer count differs from the model");
+    if (kv->kv_lora != d.kv_lora_rank || kv->rope != d.rope_dim)
+      return zgpu_fail(ctx, ZGPU_ERR_KV_INVALID_SLICE_LENGTH, "mla cache geometry differs from the model");
+    if (kv->max_tokens != max_tokens)
+      return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "ds2 batch: every cache needs the same capacity");
+    for (uint32_t c = 0; c < b; ++c)
+      if (kvs[c] == kv) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "ds2 batch: a cache appears twice");
+    if (positions[b] >= max_tokens)
+      return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "position beyond the cache");
+    if (tokens[b] >= d.vocab_padded) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "token id beyond the vocab");
+    caches[b] = kv->d;
+  }
+  zgpu_status s = ds2_prepare_batch(m, max_tokens);
+  if (s) return s;
+  auto &B = m->b;
+  cudaStream_t st = ctx->stream;
+  cudaError_t e = cudaMemcpyAsync(B.tok, tokens, n_seq * 4, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(B.pos, positions, n_seq * 4, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(B.cache, caches, n_seq * sizeof(float *), cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "batch upload");
+  const bool use_graph = !(ctx->flags & ZGPU_FLAG_NO_GRAPH);
+  uint32_t launches = 0;
+  if (use_graph && (!B.graph || B.graph_n != n_seq)) {
+    if (B.graph) cudaGraphExecDestroy(B.graph);
+    B.graph = nullptr;
+    cudaGraph_t g = nullptr;
+    e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "begin capture");
+    uint32_t n = 0;
+    cudaError_t e1 = ds2_enqueue_batch(m, n_seq, &n);
+    e = cudaStreamEndCapture(st, &g);
+    if (e1 != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      return zgpu_cuda_fail(ctx, e1, "capture batch step");
+    }
+    if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "end capture");
+    e = cudaGraphInstantiate(&B.graph, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "graph instantiate");
+    B.graph_n = n_seq;
+    B.graph_kernels = n;
+  }
+  cudaEventRecord(m->ev[0], st);
+  if (use_graph) {
+    e = cudaGraphLaunch(B.graph, st);
+    launches = B.graph_kernels;
+  } else {
+    e = ds2_enqueue_batch(m, n_seq, &launches);
+  }
+  cudaEventRecord(m->ev[1], st);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "batch step");
+  ctx->launches += launches;
+  if (logits_out) {
+    e = cudaMemcpyAsync(logits_out, B.logits, static_cast<size_t>(n_seq) * d.vocab_padded * 4,
+                        cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "logits d2h");
+  }
+  e = cudaMemcpyAsync(tokens_out, B.out, n_seq * 4, cudaMemcpyDeviceToHost, st);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "tokens d2h");
+  uint32_t stw = 0;
+  if ((s = zgpu_read_device_status(ctx, m->d_status, &stw))) return s;
+  // the step's device time and launches (zgpu_ds2_perf_snapshot)
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, m->ev[0], m->ev[1]);
+  m->perf = zgpu_perf();
+  m->perf.steps = 1;
+  m->perf.kernel_launches = launches;
+  m->perf.decode_launches = launches;
+  m->perf.decode_ms = ms;
+  return zgpu_map_device_status(ctx, stw);
+}
+
+zgpu_status zgpu_ds2_batch_expert_ids(zgpu_ds2_model *m, uint32_t n_seq, uint32_t *ids_out, float *weights_out) {
+  if (!m || n_seq == 0 || n_seq > kDs2MaxBatch) return ZGPU_ERR_INVALID_ARG;
+  zgpu_ctx *ctx = m->ctx;
+  if (!m->b.ids) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "ds2 batch: no batch step has run");
+  cudaSetDevice(ctx->device);
+  bool any_moe = false;
+  for (const Ds2Layer &L : m->layers) any_moe |= L.moe != 0;
+  const uint32_t k = any_moe ? m->desc.top_k : 1;
+  // device rows are [layer][kDs2MaxBatch][k]: copy the first n_seq of each layer
+  cudaError_t e = cudaSuccess;
+  if (ids_out)
+    e = cudaMemcpy2DAsync(ids_out, n_seq * k * 4, m->b.ids, kDs2MaxBatch * k * 4, n_seq * k * 4,
+                          m->desc.n_layers, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess && weights_out)
+    e = cudaMemcpy2DAsync(weights_out, n_seq * k * 4, m->b.wts, kDs2MaxBatch * k * 4, n_seq * k * 4,
+                          m->desc.n_layers, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "batch expert ids");
+  return ZGPU_OK;
 }
 
 zgpu_status zgpu_ds2_perf_snapshot(const zgpu_ds2_model *m, zgpu_perf *out) {

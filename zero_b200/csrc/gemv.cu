@@ -85,9 +85,11 @@ struct KParams {
   float *out;
   unsigned long long *argmax;
   uint32_t *status;
-  // segmented launch (GemvDesc::seg_w): units / wbytes are per segment
+  // segmented launch (GemvDesc::seg_w or seg_count > 1): units / wbytes are
+  // per segment
   const unsigned long long *seg_w;
-  uint32_t ctas_per_seg, seg_x_stride, seg_out_stride, seg_dynamic;
+  uint32_t segmented, ctas_per_seg, seg_x_stride, seg_out_stride, seg_dynamic;
+  uint32_t seg_x_group, seg_w_mod;
 };
 
 template <int QT, int PRO, int EPI>
@@ -107,11 +109,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
 
   // segment of this CTA (a plain launch is one segment at p.w)
   uint32_t seg = 0, cta = blockIdx.x;
-  if (p.seg_w) {
+  if (p.segmented) {
     seg = blockIdx.x / p.ctas_per_seg;
     cta = blockIdx.x - seg * p.ctas_per_seg;
   }
-  const float *xin = p.x + static_cast<size_t>(seg) * p.seg_x_stride;
+  // the segment's weight-table entry and input vector
+  const uint32_t wseg = p.seg_w_mod ? seg % p.seg_w_mod : seg;
+  const float *xin = p.x + static_cast<size_t>(seg / p.seg_x_group) * p.seg_x_stride;
   float *yout = p.out + static_cast<size_t>(seg) * p.seg_out_stride;
   const uint32_t u0 = cta * p.units_per_cta;
   const uint32_t u1 = min(u0 + p.units_per_cta, p.units);
@@ -135,7 +139,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
       const uint8_t *w = p.w;
       if (p.seg_w) {
         if (p.seg_dynamic) pdl_wait();   // the table is the previous kernel's output
-        w = reinterpret_cast<const uint8_t *>(__ldcg(p.seg_w + seg));
+        w = reinterpret_cast<const uint8_t *>(__ldcg(p.seg_w + wseg));
         if (!w) return;   // a segment of no work (another rank's expert)
       }
       uint32_t issued = 0;
@@ -171,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_x4_kernel(const KPa
   pdl_wait();   // the activations are the previous kernel's output
   // a zero table entry: the segment does nothing (expert parallelism leaves
   // another rank's experts out); uniform over the CTA, before any barrier
-  if (p.seg_w && p.seg_dynamic && __ldcg(p.seg_w + seg) == 0ull) return;
+  if (p.seg_w && p.seg_dynamic && __ldcg(p.seg_w + wseg) == 0ull) return;
   const uint32_t tid = threadIdx.x;
   const uint32_t nf4 = PRO == PRO_Q8ACT ? 0u : p.in_dim / 4;
   float inv = 1.0f;
@@ -353,8 +357,12 @@ cudaError_t launch_gemv(const GemvDesc &g, GemvPro pro, GemvEpi epi, const GemvI
   kp.units = g.groups / 2;
   const uint32_t ctas = static_cast<uint32_t>((lc.sm_count > 0 ? lc.sm_count : 148) * kCtasPerSm);
   uint32_t grid = 0;
-  if (g.seg_w) {
-    if (g.seg_count == 0 || !g.wbytes) return cudaErrorInvalidValue;
+  kp.seg_x_group = 1;
+  if (g.seg_w || g.seg_count > 1) {
+    if (g.seg_count == 0 || !g.wbytes || g.seg_x_group == 0) return cudaErrorInvalidValue;
+    kp.segmented = 1;
+    kp.seg_x_group = g.seg_x_group;
+    kp.seg_w_mod = g.seg_w_mod;
     const uint64_t total = static_cast<uint64_t>(kp.units) * g.seg_count;
     kp.units_per_cta = static_cast<uint32_t>((total + ctas - 1) / ctas);
     kp.ctas_per_seg = (kp.units + kp.units_per_cta - 1) / kp.units_per_cta;
@@ -371,6 +379,21 @@ cudaError_t launch_gemv(const GemvDesc &g, GemvPro pro, GemvEpi epi, const GemvI
   const size_t slot = 2 * static_cast<size_t>(kp.half_bytes);
   // activation image: 128 B per block
   kp.xbytes = static_cast<uint32_t>(static_cast<size_t>(kp.bpr) * 128);
+  // A launch whose per-CTA share of units leaves no room for one ring slot
+  // per warp (a batch of many segments) takes fewer units per CTA and more
+  // CTAs than one wave.
+  const size_t unit_part = static_cast<size_t>(kp.ks) * kRows * sizeof(float);
+  const size_t room = kSmemBudget - 1024 - kp.xbytes - kWarps * slot - 127;
+  if (kSmemBudget > 1024 + kp.xbytes + kWarps * slot + 127 && kp.units_per_cta * unit_part > room) {
+    kp.units_per_cta = static_cast<uint32_t>(room / unit_part);
+    if (kp.units_per_cta == 0) return cudaErrorInvalidValue;
+    if (kp.segmented) {
+      kp.ctas_per_seg = (kp.units + kp.units_per_cta - 1) / kp.units_per_cta;
+      grid = kp.ctas_per_seg * g.seg_count;
+    } else {
+      grid = (kp.units + kp.units_per_cta - 1) / kp.units_per_cta;
+    }
+  }
   const size_t part_bytes =
       (static_cast<size_t>(kp.units_per_cta) * kp.ks * kRows * sizeof(float) + 127) & ~size_t(127);
   kp.ring_off = static_cast<uint32_t>(kp.xbytes + part_bytes);

@@ -49,6 +49,13 @@ struct GemvDesc {
   uint32_t seg_count = 0;
   uint32_t seg_x_stride = 0, seg_out_stride = 0;
   bool seg_dynamic = false;
+  // Batches: with seg_count > 1 and no table every segment streams w (the
+  // same matrix for every sequence); segment s reads its input at
+  // x + (s / seg_x_group) * seg_x_stride (several segments on one input, e.g.
+  // a token's experts), and with seg_w_mod != 0 takes table entry
+  // s % seg_w_mod (one table for every sequence).
+  uint32_t seg_x_group = 1;
+  uint32_t seg_w_mod = 0;
 };
 
 // PRO_Q8ACT: the input is Q8_0 blocks (34 bytes each: fp16 d, 32 int8) and

@@ -44,7 +44,25 @@ constexpr uint32_t kMlaAttnWarpsMax = 16;
 constexpr uint32_t kMlaMergeThreads = 128;
 
 __device__ __forceinline__ uint32_t mla_pos(const MlaParams &p) {
-  return p.pos_ptr ? *p.pos_ptr : p.pos_value;
+  return p.seq_pos ? __ldcg(p.seq_pos + blockIdx.y) : (p.pos_ptr ? *p.pos_ptr : p.pos_value);
+}
+
+// This CTA's sequence (grid dimension y) of a batch: the per-sequence
+// vectors and cache of MlaParams rebased on it.
+__device__ __forceinline__ MlaParams mla_seq(const MlaParams &p0) {
+  MlaParams p = p0;
+  const uint32_t b = blockIdx.y;
+  if (b) {
+    const uint32_t R = p.kv_lora, RD = p.rope;
+    p.kv_a += static_cast<size_t>(b) * p.kv_a_stride;
+    p.q += static_cast<size_t>(b) * p.q_stride;
+    p.q_abs += static_cast<size_t>(b) * p.n_heads * R;
+    p.q_pe += static_cast<size_t>(b) * p.n_heads * RD;
+    p.ctx += static_cast<size_t>(b) * p.n_heads * R;
+    p.part += static_cast<size_t>(b) * p.n_heads * p.max_splits * (R + 2);
+  }
+  if (p.seq_cache) p.cache = p.seq_cache[b] + p.layer_off;
+  return p;
 }
 
 // Fixed-order block sum over kMlaPrepThreads threads (thread partials, xor
@@ -68,7 +86,8 @@ __device__ __forceinline__ void rope_pair(float x0, float x1, float theta, float
   *o1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
 }
 
-__global__ void __launch_bounds__(kMlaPrepThreads) mla_prep_kernel(const MlaParams p) {
+__global__ void __launch_bounds__(kMlaPrepThreads) mla_prep_kernel(const MlaParams p0) {
+  const MlaParams p = mla_seq(p0);
   extern __shared__ __align__(16) uint8_t slab[];
   __shared__ float qn[kMlaMaxNope];
   __shared__ float red[kMlaPrepThreads / 32];
@@ -166,7 +185,8 @@ __global__ void __launch_bounds__(kMlaPrepThreads) mla_prep_kernel(const MlaPara
   }
 }
 
-__global__ void __launch_bounds__(32 * kMlaAttnWarpsMax) mla_attn_kernel(const MlaParams p) {
+__global__ void __launch_bounds__(32 * kMlaAttnWarpsMax) mla_attn_kernel(const MlaParams p0) {
+  const MlaParams p = mla_seq(p0);
   extern __shared__ __align__(128) float chunk[];   // [tokens of this split][kv_lora + rope]
   __shared__ __align__(8) uint64_t bar;
   pdl_launch_dependents();
@@ -237,7 +257,8 @@ __global__ void __launch_bounds__(32 * kMlaAttnWarpsMax) mla_attn_kernel(const M
   }
 }
 
-__global__ void __launch_bounds__(kMlaMergeThreads) mla_merge_kernel(const MlaParams p) {
+__global__ void __launch_bounds__(kMlaMergeThreads) mla_merge_kernel(const MlaParams p0) {
+  const MlaParams p = mla_seq(p0);
   pdl_launch_dependents();
   pdl_wait();
   const uint32_t pos = mla_pos(p);
@@ -281,7 +302,9 @@ cudaError_t launch_mla_prep(const MlaParams &mp, const LaunchCfg &lc) {
   if (slab > kMlaSlabMax || p.kb_gstride % 16) return cudaErrorInvalidValue;
   p.slab_bytes = static_cast<uint32_t>(slab);
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = make_launch_cfg(dim3(p.n_heads + 1), dim3(kMlaPrepThreads), slab, lc, attr);
+  const uint32_t ns = p.n_seq > 1 ? p.n_seq : 1;
+  if (ns > 1 && (!p.seq_cache || !p.seq_pos)) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = make_launch_cfg(dim3(p.n_heads + 1, ns), dim3(kMlaPrepThreads), slab, lc, attr);
   if (lc.launch_counter) ++*lc.launch_counter;
   return cudaLaunchKernelEx(&cfg, mla_prep_kernel, p);
 }
@@ -294,13 +317,16 @@ cudaError_t launch_mla_attention(const MlaParams &p, const LaunchCfg &lc) {
   const uint32_t warps = p.n_heads < kMlaAttnWarpsMax ? p.n_heads : kMlaAttnWarpsMax;
   cudaLaunchAttribute attr[1];
   const size_t chunk = static_cast<size_t>(kMlaSplitTokens) * (p.kv_lora + p.rope) * sizeof(float);
-  cudaLaunchConfig_t cfg = make_launch_cfg(dim3(mla_max_splits(p.max_tokens)), dim3(32 * warps), chunk, lc, attr);
+  const uint32_t ns = p.n_seq > 1 ? p.n_seq : 1;
+  if (ns > 1 && (!p.seq_cache || !p.seq_pos)) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg =
+      make_launch_cfg(dim3(mla_max_splits(p.max_tokens), ns), dim3(32 * warps), chunk, lc, attr);
   if (lc.launch_counter) ++*lc.launch_counter;
   cudaError_t e = cudaLaunchKernelEx(&cfg, mla_attn_kernel, p);
   if (e != cudaSuccess) return e;
   const uint32_t nq = (p.kv_lora + kMlaMergeThreads - 1) / kMlaMergeThreads;
   cudaLaunchAttribute attr2[1];
-  cudaLaunchConfig_t cfg2 = make_launch_cfg(dim3(p.n_heads * nq), dim3(kMlaMergeThreads), 0, lc, attr2);
+  cudaLaunchConfig_t cfg2 = make_launch_cfg(dim3(p.n_heads * nq, ns), dim3(kMlaMergeThreads), 0, lc, attr2);
   if (lc.launch_counter) ++*lc.launch_counter;
   return cudaLaunchKernelEx(&cfg2, mla_merge_kernel, p);
 }

@@ -36,6 +36,16 @@ struct MlaParams {
   uint32_t n_heads, kv_lora, rope, nope, max_splits;
   float eps, scale;
   uint32_t slab_bytes;        // shared bytes of one head's k_nope slab (set by the launcher)
+  // A batch of n_seq sequences (grid dimension y; 0 or 1: the one sequence
+  // above).  Sequence b reads kv_a + b * kv_a_stride and q + b * q_stride,
+  // writes q_abs / q_pe / ctx / part at b times their one-sequence sizes,
+  // and uses its own cache seq_cache[b] + layer_off (this layer of its
+  // zgpu_mla_kv, all of one capacity max_tokens) and position seq_pos[b].
+  uint32_t n_seq;
+  uint32_t kv_a_stride, q_stride;
+  float *const *seq_cache;
+  uint64_t layer_off;
+  const uint32_t *seq_pos;
 };
 
 // Splits (attention CTAs) a cache of max_tokens needs.

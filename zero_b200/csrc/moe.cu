@@ -44,7 +44,28 @@ __device__ void route_uniform(float *w, uint32_t k, float scale) {
   for (uint32_t i = 0; i < k; ++i) w[i] = (s != 1.0f) ? __fmul_rn(u, s) : u;
 }
 
-__global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const RouteParams p) {
+// This CTA's token (grid dimension y) of a batch: the per-token vectors of
+// RouteParams rebased on it.
+__device__ __forceinline__ RouteParams route_seq(const RouteParams &p0) {
+  RouteParams p = p0;
+  const uint32_t b = blockIdx.y;
+  if (b) {
+    const uint32_t nseg = p.n_shared + p.top_k;
+    p.x += static_cast<size_t>(b) * p.x_stride;
+    p.scores += static_cast<size_t>(b) * p.n_experts;
+    p.ids += static_cast<size_t>(b) * p.top_k;
+    p.weights += static_cast<size_t>(b) * p.top_k;
+    p.counter += b;
+    if (p.seg_gu) {
+      p.seg_gu += static_cast<size_t>(b) * nseg;
+      p.seg_dn += static_cast<size_t>(b) * nseg;
+    }
+  }
+  return p;
+}
+
+__global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const RouteParams p0) {
+  const RouteParams p = route_seq(p0);
   extern __shared__ __align__(16) float rsm[];
   __shared__ float red[kRouteThreads / 32];
   __shared__ uint32_t s_last;
@@ -204,9 +225,16 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const RoutePar
   }
 }
 
-__global__ void moe_combine_kernel(const CombineParams p) {
+__global__ void moe_combine_kernel(const CombineParams p0) {
   pdl_launch_dependents();
   pdl_wait();
+  // this token (grid dimension y) of a batch
+  const uint32_t tb = blockIdx.y;
+  CombineParams p = p0;
+  p.exp_out += static_cast<size_t>(tb) * (p.n_shared + p.top_k) * p.dim;
+  p.weights += static_cast<size_t>(tb) * p.top_k;
+  if (p.mlp_out) p.mlp_out += static_cast<size_t>(tb) * p.dim;
+  if (p.hidden) p.hidden += static_cast<size_t>(tb) * p.dim;
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= p.dim) return;
   float o = 0.0f;
@@ -220,7 +248,7 @@ __global__ void moe_combine_kernel(const CombineParams p) {
   if (p.xslots) {
     // flow control: every rank has published this invocation (and so has
     // finished its combine of the previous one)
-    const unsigned long long *arrive = p.xslots + ep_slot_words(p.top_k, p.dim);
+    const unsigned long long *arrive = p.xslots + ep_slot_words(p.slot_cap, p.dim);
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t r = 0; r < p.world && !gave_up; ++r) {
       while (static_cast<uint32_t>(__ldcg(arrive + r) >> 32) != ver) {
@@ -237,7 +265,8 @@ __global__ void moe_combine_kernel(const CombineParams p) {
     float y;
     if (p.xslots) {
       // the slot's output from whichever rank ran its expert (bounded wait)
-      const unsigned long long *src = p.xslots + (static_cast<size_t>(ver & 1u) * p.top_k + k) * p.dim + i;
+      const unsigned long long *src =
+          p.xslots + (static_cast<size_t>(ver & 1u) * p.slot_cap + tb * p.top_k + k) * p.dim + i;
       unsigned long long t = __ldcg(src);
       if (gave_up) {
         t = static_cast<unsigned long long>(0x7fc00000u);
@@ -263,23 +292,24 @@ __global__ void moe_combine_kernel(const CombineParams p) {
   if (p.hidden) p.hidden[i] = __fadd_rn(p.hidden[i], o);
 }
 
-// grid (ceil(dim / 256), top_k): slot k's row, when this rank ran its expert
+// grid (ceil(dim / 256), top_k, tokens): slot k's row of token z, when this
+// rank ran its expert
 __global__ void moe_ep_publish_kernel(const EpPublishParams p) {
   pdl_launch_dependents();
   pdl_wait();
-  const uint32_t k = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t k = blockIdx.y, tb = blockIdx.z, i = blockIdx.x * blockDim.x + threadIdx.x;
   const uint32_t ver = __ldcg(p.ep_seq) + 1;
-  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
+  if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0) {
     // this rank's arrival for invocation ver, in every rank's buffer
-    const size_t a = ep_slot_words(p.top_k, p.dim) + p.ep_rank;
+    const size_t a = ep_slot_words(p.slot_cap, p.dim) + p.ep_rank;
     for (uint32_t d = 0; d < p.world; ++d) p.dst[d][a] = tag_word(0.0f, ver);
   }
   if (i >= p.dim) return;
-  const uint32_t e = __ldcg(p.ids + k);
+  const uint32_t e = __ldcg(p.ids + static_cast<size_t>(tb) * p.top_k + k);
   if (e / p.ep_per_rank != p.ep_rank) return;
-  const unsigned long long w =
-      tag_word(__ldcg(p.exp_out + static_cast<size_t>(p.n_shared + k) * p.dim + i), ver);
-  const size_t off = (static_cast<size_t>(ver & 1u) * p.top_k + k) * p.dim + i;
+  const float *eo = p.exp_out + static_cast<size_t>(tb) * (p.n_shared + p.top_k) * p.dim;
+  const unsigned long long w = tag_word(__ldcg(eo + static_cast<size_t>(p.n_shared + k) * p.dim + i), ver);
+  const size_t off = (static_cast<size_t>(ver & 1u) * p.slot_cap + tb * p.top_k + k) * p.dim + i;
   for (uint32_t d = 0; d < p.world; ++d) p.dst[d][off] = w;
 }
 
@@ -315,23 +345,30 @@ cudaError_t launch_moe_route(const RouteParams &rp, const LaunchCfg &lc) {
   p.experts_per_cta = route_experts_per_cta(p.dim);
   const uint32_t grid = (p.n_experts + p.experts_per_cta - 1) / p.experts_per_cta;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = make_launch_cfg(dim3(grid), dim3(kRouteThreads), route_smem_bytes(p.dim), lc, attr);
+  const uint32_t ns = p.n_seq > 1 ? p.n_seq : 1;
+  if (ns > 1 && p.x_stride < p.dim) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg =
+      make_launch_cfg(dim3(grid, ns), dim3(kRouteThreads), route_smem_bytes(p.dim), lc, attr);
   if (lc.launch_counter) ++*lc.launch_counter;
   return cudaLaunchKernelEx(&cfg, moe_route_kernel, p);
 }
 
 cudaError_t launch_moe_combine(const CombineParams &p, const LaunchCfg &lc) {
+  const uint32_t ns = p.n_seq > 1 ? p.n_seq : 1;
+  if (p.xslots && ns * p.top_k > p.slot_cap) return cudaErrorInvalidValue;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = make_launch_cfg(dim3((p.dim + 255) / 256), dim3(256), 0, lc, attr);
+  cudaLaunchConfig_t cfg = make_launch_cfg(dim3((p.dim + 255) / 256, ns), dim3(256), 0, lc, attr);
   if (lc.launch_counter) ++*lc.launch_counter;
   return cudaLaunchKernelEx(&cfg, moe_combine_kernel, p);
 }
 
 cudaError_t launch_moe_ep_publish(const EpPublishParams &p, const LaunchCfg &lc) {
-  if (p.dim == 0 || p.top_k == 0 || p.world == 0 || p.world > kEpMaxRanks || p.ep_per_rank == 0)
+  const uint32_t ns = p.n_seq > 1 ? p.n_seq : 1;
+  if (p.dim == 0 || p.top_k == 0 || p.world == 0 || p.world > kEpMaxRanks || p.ep_per_rank == 0 ||
+      ns * p.top_k > p.slot_cap)
     return cudaErrorInvalidValue;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = make_launch_cfg(dim3((p.dim + 255) / 256, p.top_k), dim3(256), 0, lc, attr);
+  cudaLaunchConfig_t cfg = make_launch_cfg(dim3((p.dim + 255) / 256, p.top_k, ns), dim3(256), 0, lc, attr);
   if (lc.launch_counter) ++*lc.launch_counter;
   return cudaLaunchKernelEx(&cfg, moe_ep_publish_kernel, p);
 }

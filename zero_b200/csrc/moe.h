@@ -36,6 +36,10 @@ struct RouteParams {
   // (ep_rank + 1) * ep_per_rank); a selected expert of another rank gets a
   // zero table entry (its GEMV segments do nothing).  ep_per_rank == 0: all.
   uint32_t ep_rank, ep_per_rank;
+  // A batch of n_seq tokens (grid dimension y; 0 or 1: one token): token b
+  // routes x + b * x_stride and writes its scores, ids, weights, arrival
+  // counter and dispatch tables at b times their one-token sizes.
+  uint32_t n_seq, x_stride;
 };
 
 struct CombineParams {
@@ -53,6 +57,12 @@ struct CombineParams {
   const uint32_t *ep_seq;
   uint32_t world;
   uint32_t *status;
+  // A batch of n_seq tokens (grid dimension y): token b combines exp_out +
+  // b * (n_shared + top_k) * dim with weights + b * top_k into hidden /
+  // mlp_out + b * dim, and reads its routed slots at (b * top_k + k) * dim
+  // of the exchange buffer; each half of it holds slot_cap slots.
+  uint32_t n_seq;
+  uint32_t slot_cap;
 };
 
 // Expert parallelism: the outputs of this rank's selected experts, as tagged
@@ -63,18 +73,21 @@ struct CombineParams {
 // its reads of buffer (v & 1): publishing invocation v + 2 into that buffer
 // is then safe however the experts are routed.
 struct EpPublishParams {
-  const float *exp_out;                    // [n_shared + top_k][dim]
-  const uint32_t *ids;                     // [top_k] this layer's experts
+  const float *exp_out;                    // [n_shared + top_k][dim] (per token of a batch)
+  const uint32_t *ids;                     // [top_k] this layer's experts (per token)
   unsigned long long *const *dst;          // [world] every rank's exchange buffer
   const uint32_t *ep_seq;
   uint32_t dim, n_shared, top_k, world, ep_rank, ep_per_rank;
+  uint32_t n_seq;                          // tokens of a batch (grid dimension z; 0 or 1: one)
+  uint32_t slot_cap;                       // slots per half of the exchange buffer
 };
 
-// Words of one rank's exchange buffer: two buffers of top_k x dim tagged
-// slot words, then one arrival word per rank.
+// Words of one rank's exchange buffer: two buffers of slots x dim tagged
+// words (slots = top_k per token of the largest batch), then one arrival
+// word per rank.
 constexpr uint32_t kEpMaxRanks = 8;
-ZGPU_HD size_t ep_slot_words(uint32_t top_k, uint32_t dim) { return 2 * static_cast<size_t>(top_k) * dim; }
-ZGPU_HD size_t ep_exchange_words(uint32_t top_k, uint32_t dim) { return ep_slot_words(top_k, dim) + kEpMaxRanks; }
+ZGPU_HD size_t ep_slot_words(uint32_t slots, uint32_t dim) { return 2 * static_cast<size_t>(slots) * dim; }
+ZGPU_HD size_t ep_exchange_words(uint32_t slots, uint32_t dim) { return ep_slot_words(slots, dim) + kEpMaxRanks; }
 
 cudaError_t moe_setup();
 cudaError_t launch_moe_route(const RouteParams &p, const LaunchCfg &lc);
