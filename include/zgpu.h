@@ -155,6 +155,15 @@ zgpu_status zgpu_linear_q8act(zgpu_ctx *ctx, const void *xq_blocks, const void *
 zgpu_status zgpu_linear_q8act_device(zgpu_ctx *ctx, const void *d_xq_blocks, const void *w_key,
                                      float *d_out, uint64_t in_dim, uint64_t out_dim, void *stream);
 
+/* linear_dispatch (ops.rs:486) of n_vec (1..32) f32 vectors x[n_vec][in_dim]
+ * against one registered Q4_0 or Q8_0 weight on the tensor cores
+ * (tcgen05 int8 MMA over the three 8-bit digits of the GEMV's activation
+ * integers): out[v] equals zgpu_linear_dispatch(x[v]) bit for bit for every
+ * v, whatever n_vec is.  The reference multiplies one vector at a time; this
+ * is the batched-decode form of the same product.  Host buffers. */
+zgpu_status zgpu_linear_dispatch_batch(zgpu_ctx *ctx, const float *x, const void *w_key, float *out,
+                                       uint64_t n_vec, uint64_t in_dim, uint64_t out_dim, uint32_t quant);
+
 /* Batched form on the tensor cores (tcgen05 int8 MMA): T rows of f32
  * activations x[T][in_dim] are quantised per 32-block with the Q8_0 rule
  * above, then out[t][r] = sum_b (sum_j w_j*q_j * d_w) * d_x, accumulated in

@@ -146,6 +146,16 @@ class Context:
         key = w if isinstance(w, int) else _ptr(w)
         self._check(LIB.zgpu_linear_q8act_device(self.h, d_xq, key, d_out, in_dim, out_dim, stream or None))
 
+    def linear_dispatch_batch(self, x: np.ndarray, w, in_dim: int, out_dim: int, quant: int) -> np.ndarray:
+        """linear_dispatch of each row of x [n_vec, in_dim] (n_vec <= 32) on the
+        tensor cores; row v equals linear_dispatch(x[v]) bit for bit."""
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, in_dim)
+        out = np.empty((x.shape[0], out_dim), np.float32)
+        key = w if isinstance(w, int) else _ptr(w)
+        self._check(LIB.zgpu_linear_dispatch_batch(self.h, _ptr(x), key, _ptr(out), x.shape[0], in_dim, out_dim,
+                                                   quant))
+        return out
+
     def linear_q8act_batch(self, x: np.ndarray, w, in_dim: int, out_dim: int) -> np.ndarray:
         """T rows of activations (x [T, in_dim] f32) quantised to Q8_0 and
         multiplied by Q4_0 weights on the tcgen05 int8 path; returns [T, out_dim]."""

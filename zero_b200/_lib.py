@@ -105,6 +105,7 @@ _SIGS = {
     "zgpu_quantize_q8_0": (_i32, [_vp, _vp, _vp, _u64]),
     "zgpu_linear_q8act": (_i32, [_vp, _vp, _vp, _vp, _u64, _u64]),
     "zgpu_linear_q8act_device": (_i32, [_vp, _vp, _vp, _vp, _u64, _u64, _vp]),
+    "zgpu_linear_dispatch_batch": (_i32, [_vp, _vp, _vp, _vp, _u64, _u64, _u64, _u32]),
     "zgpu_linear_q8act_batch": (_i32, [_vp, _vp, _vp, _vp, _u64, _u64, _u64]),
     "zgpu_linear_q8act_batch_device": (_i32, [_vp, _vp, _vp, _vp, _u64, _u64, _u64, _vp]),
     "zgpu_rmsnorm": (_i32, [_vp, _vp, _vp, _vp, _u64, _f]),

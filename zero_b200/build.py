@@ -37,7 +37,7 @@ if os.environ.get("ZGPU_DEVICE_CHECKS") == "1":
 if os.environ.get("ZGPU_STEP_TRACE") == "1":
     CUDA_FLAGS.append("-DZGPU_STEP_TRACE")
 
-CU_SOURCES = ["gemv.cu", "attention.cu", "attention_static.cu", "step.cu", "ops.cu", "moe.cu", "mla.cu", "mma_gemm.cu", "prefill.cu", "sampler.cu", "kquant.cu", "mha.cu",
+CU_SOURCES = ["gemv.cu", "attention.cu", "attention_static.cu", "step.cu", "ops.cu", "moe.cu", "mla.cu", "mma_gemm.cu", "digit_mma.cu", "prefill.cu", "sampler.cu", "kquant.cu", "mha.cu",
               "ctx.cu", "model.cu", "ds2.cu"]
 CXX_SOURCES = ["synth.cpp", "smodel.cpp", "detok.cpp"]
 

@@ -157,6 +157,13 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Nibbles n (0..15) of four bytes -> four int8 (n - 8): flip bit 3, then
+// sign-extend it over the high nibble (0x08 * 0x1E = 0xF0, no carries).
+__device__ __forceinline__ uint32_t nib_to_s8(uint32_t n4) {
+  const uint32_t m = n4 ^ 0x08080808u;
+  return m | ((m & 0x08080808u) * 0x1Eu);
+}
+
 __device__ __forceinline__ float h2f(uint16_t bits) {
   return __half2float(__ushort_as_half(bits));
 }

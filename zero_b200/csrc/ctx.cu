@@ -6,6 +6,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "digit_mma.h"
 #include "internal.h"
 #include "layout.h"
 #include "ops.h"
@@ -94,7 +95,7 @@ zgpu_status zgpu_init(const zgpu_opts *opts, zgpu_ctx **out) {
       zgpu::gemv_setup() != cudaSuccess || zgpu::attention_setup() != cudaSuccess ||
       zgpu::ops_setup() != cudaSuccess || zgpu::step_setup() != cudaSuccess ||
       zgpu::moe_setup() != cudaSuccess || zgpu::mla_setup() != cudaSuccess ||
-      zgpu::prefill_setup() != cudaSuccess || zgpu::mma_setup() != cudaSuccess ||
+      zgpu::prefill_setup() != cudaSuccess || zgpu::mma_setup() != cudaSuccess || zgpu::dm_setup() != cudaSuccess ||
       cudaMalloc(&ctx->d_route_counter, sizeof(uint32_t)) != cudaSuccess ||
       cudaMemset(ctx->d_route_counter, 0, sizeof(uint32_t)) != cudaSuccess) {
     delete ctx;
@@ -559,6 +560,71 @@ zgpu_status zgpu_linear_q8act_batch_device(zgpu_ctx *ctx, const float *d_x, cons
   cudaSetDevice(ctx->device);
   return q8act_batch(ctx, d_x, w_key, d_out, T, in_dim, out_dim,
                      stream ? static_cast<cudaStream_t>(stream) : ctx->stream);
+}
+
+zgpu_status zgpu_linear_dispatch_batch(zgpu_ctx *ctx, const float *x, const void *w_key, float *out,
+                                       uint64_t n_vec, uint64_t in_dim, uint64_t out_dim, uint32_t quant) {
+  if (!ctx || !x || !out || n_vec == 0 || in_dim == 0 || in_dim % 32) return ZGPU_ERR_INVALID_ARG;
+  if (n_vec > zgpu::kDmMaxVec) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "linear_dispatch_batch: at most 32 vectors");
+  if (quant != ZGPU_Q4_0 && quant != ZGPU_Q8_0)
+    return zgpu_fail(ctx, ZGPU_ERR_UNSUPPORTED_QUANT, "linear_dispatch_batch: Q4_0 or Q8_0 weights");
+  const DeviceTensor *t = zgpu_lookup(ctx, w_key);
+  if (!t) return zgpu_fail(ctx, ZGPU_ERR_UNREGISTERED_WEIGHT, "linear_dispatch_batch: unregistered weight");
+  if (t->quant != quant || t->cols != in_dim || t->rows != out_dim)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "linear_dispatch_batch: shape/quant mismatch with registration");
+  cudaSetDevice(ctx->device);
+  zgpu_status s = ensure_scratch(ctx, n_vec * in_dim, n_vec * out_dim);
+  if (s) return s;
+  const uint32_t nv = static_cast<uint32_t>(n_vec), ind = static_cast<uint32_t>(in_dim),
+                 rows = static_cast<uint32_t>(out_dim);
+  const uint32_t ks = (ind / 32 + zgpu::kChunkBlocks - 1) / zgpu::kChunkBlocks;
+  const size_t img = zgpu::dm_img_bytes(ind, nv), part = static_cast<size_t>(ks) * nv * rows * 4;
+  if (img + part > ctx->d_q8_cap) {
+    cudaFree(ctx->d_q8);
+    ctx->d_q8 = nullptr;
+    ctx->d_q8_cap = 0;
+    ZCHECK(cudaMalloc(&ctx->d_q8, img + part), "cudaMalloc(digit image scratch)");
+    ctx->d_q8_cap = img + part;
+  }
+  ZCHECK(cudaMemcpyAsync(ctx->d_x, x, n_vec * in_dim * 4, cudaMemcpyHostToDevice, ctx->stream), "h2d");
+  zgpu::LaunchCfg lc;
+  lc.stream = ctx->stream;
+  lc.pdl = !(ctx->flags & ZGPU_FLAG_NO_PDL);
+  lc.sm_count = ctx->sm_count;
+  lc.launch_counter = &ctx->launches;
+  zgpu::DigitImageParams ip = {};
+  ip.x = ctx->d_x;
+  ip.x_stride = ind;
+  ip.in_dim = ind;
+  ip.n_vec = nv;
+  ip.n_img = 1;
+  ip.img = ctx->d_q8;
+  ip.status = ctx->d_status;
+  ZCHECK(zgpu::launch_digit_image(ip, lc), "digit image");
+  zgpu::DmGemmParams gp = {};
+  gp.w = t->d;
+  gp.gstride = t->gstride;
+  gp.quant = t->quant;
+  gp.rows = rows;
+  gp.in_dim = ind;
+  gp.img = ctx->d_q8;
+  gp.n_vec = nv;
+  gp.n_seg = 1;
+  gp.part = reinterpret_cast<float *>(ctx->d_q8 + img);
+  gp.status = ctx->d_status;
+  ZCHECK(zgpu::launch_dm_gemm(gp, lc), "digit mma");
+  zgpu::DmCombineParams cp = {};
+  cp.part = gp.part;
+  cp.rows = rows;
+  cp.ks = ks;
+  cp.n_vec = nv;
+  cp.n_seg = 1;
+  cp.out = ctx->d_y;
+  cp.out_vec_stride = rows;
+  cp.epi = zgpu::EPI_STORE;
+  ZCHECK(zgpu::launch_dm_combine(cp, lc), "digit combine");
+  ZCHECK(cudaMemcpyAsync(out, ctx->d_y, n_vec * out_dim * 4, cudaMemcpyDeviceToHost, ctx->stream), "d2h");
+  return check_status_word(ctx);
 }
 
 zgpu_status zgpu_linear_q8act_batch(zgpu_ctx *ctx, const float *x, const void *w_key, float *out, uint64_t T,

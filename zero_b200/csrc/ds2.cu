@@ -276,6 +276,7 @@ cudaError_t ds2_enqueue_forward(zgpu_ds2_model *m, zgpu_mla_kv *kv, uint32_t *co
     mp.max_splits = m->max_splits;
     mp.eps = d.rms_eps;
     mp.scale = 1.0f / sqrtf(static_cast<float>(hq));
+    mp.split_tokens = mla_split_tokens(1, kv->max_tokens, m->ctx->sm_count);
     if ((e = launch_mla_prep(mp, lc)) != cudaSuccess) return e;
     if ((e = launch_mla_attention(mp, lc)) != cudaSuccess) return e;
     // per-head V projection of the merged latent context
@@ -561,6 +562,7 @@ cudaError_t ds2_enqueue_batch(zgpu_ds2_model *m, uint32_t ns, uint32_t *counter)
     mp.seq_cache = B.cache;
     mp.layer_off = static_cast<uint64_t>(l) * B.max_tokens * (R + RD);
     mp.seq_pos = B.pos;
+    mp.split_tokens = mla_split_tokens(ns, B.max_tokens, m->ctx->sm_count);
     if ((e = launch_mla_prep(mp, lc)) != cudaSuccess) return e;
     if ((e = launch_mla_attention(mp, lc)) != cudaSuccess) return e;
     // per-head V projection: segment b * NH + h reads ctx row (b, h) and

@@ -132,17 +132,14 @@ __device__ __forceinline__ float rms_inv(const float *x, uint32_t n, float eps, 
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(n)), eps)));
 }
 
-// Digitise the float4 t = x[4f..4f+3] into the image (see the file header).
-// Called by all 32 lanes of a warp for 32 consecutive float4s (8 blocks):
-// the block statistics shuffle across the 8 lanes of each block, so lanes
-// with valid == false must still call it.
-template <int QT>
-__device__ __forceinline__ void digitise_f4(float4 t, uint32_t f, bool valid, uint32_t *xsm,
-                                            uint32_t bpr, uint32_t xbytes, uint32_t *status) {
-  const uint32_t b = f >> 3, k4 = f & 7;
-  // a failed check only suppresses the writes: every lane still reaches the
-  // shuffles below
-  const bool in_range = valid && ZDEV_CHECK(b < bpr && b * 128 + 128 <= xbytes, status, 3, b, xbytes);
+// The integers of one block (see the file header): n_k = rint(t_k * 2^(22-e))
+// (at most 2^23 - 1) for the float4 t = x[4f..4f+3], and the block's scale
+// 2^(e-22) (0 for an all-zero or negligible block, NaN for a non-finite
+// one).  Called by all 32 lanes of a warp for 32 consecutive float4s (8
+// blocks): the statistics shuffle across the 8 lanes of each block.  The
+// GEMV image (digitise_f4) and the batched tensor-core image (digit_mma.cu)
+// both take their digits from here.
+__device__ __forceinline__ float block_ints(float4 t, int (&n)[4]) {
   // block maximum and non-finite flag over the block's 8 lanes
   float am = fmaxf(fmaxf(fabsf(t.x), fabsf(t.y)), fmaxf(fabsf(t.z), fabsf(t.w)));
   uint32_t bad = (fabsf(t.x) <= FLT_MAX && fabsf(t.y) <= FLT_MAX && fabsf(t.z) <= FLT_MAX &&
@@ -152,7 +149,7 @@ __device__ __forceinline__ void digitise_f4(float4 t, uint32_t f, bool valid, ui
     am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
     bad |= __shfl_xor_sync(0xffffffffu, bad, off);
   }
-  int n[4] = {0, 0, 0, 0};
+  n[0] = n[1] = n[2] = n[3] = 0;
   float bscale = 0.0f;                              // all-zero (or negligible) block
   if (bad) {
     bscale = __uint_as_float(0x7fc00000u);          // NaN: the rows' sums become NaN
@@ -164,6 +161,22 @@ __device__ __forceinline__ void digitise_f4(float4 t, uint32_t f, bool valid, ui
 #pragma unroll
     for (int k = 0; k < 4; ++k) n[k] = min(__float2int_rn(v[k] * up), 0x7FFFFF);
   }
+  return bscale;
+}
+
+// Digitise the float4 t = x[4f..4f+3] into the image (see the file header).
+// Called by all 32 lanes of a warp for 32 consecutive float4s (8 blocks):
+// the block statistics shuffle across the 8 lanes of each block, so lanes
+// with valid == false must still call it.
+template <int QT>
+__device__ __forceinline__ void digitise_f4(float4 t, uint32_t f, bool valid, uint32_t *xsm,
+                                            uint32_t bpr, uint32_t xbytes, uint32_t *status) {
+  const uint32_t b = f >> 3, k4 = f & 7;
+  // a failed check only suppresses the writes: every lane still reaches the
+  // shuffles below
+  const bool in_range = valid && ZDEV_CHECK(b < bpr && b * 128 + 128 <= xbytes, status, 3, b, xbytes);
+  int n[4];
+  const float bscale = block_ints(t, n);
   const uint32_t w0 = __byte_perm(__byte_perm(n[0], n[1], 0x0040), __byte_perm(n[2], n[3], 0x0040), 0x5410);
   const uint32_t w1 = __byte_perm(__byte_perm(n[0], n[1], 0x0051), __byte_perm(n[2], n[3], 0x0051), 0x5410);
   const uint32_t w2 = __byte_perm(__byte_perm(n[0], n[1], 0x0062), __byte_perm(n[2], n[3], 0x0062), 0x5410);
@@ -226,7 +239,7 @@ __device__ __forceinline__ void item_rows(const uint8_t *sbase, uint32_t group_b
         t = q8_dot(*reinterpret_cast<const uint4 *>(cb + (2 * r) * nb * 16 + lane * 16),
                    *reinterpret_cast<const uint4 *>(cb + (2 * r + 1) * nb * 16 + lane * 16), D);
       }
-      acc[4 * g + r] = __fmul_rn(d[r], bscale) * t;
+      acc[4 * g + r] = __fmul_rn(__fmul_rn(d[r], bscale), t);
     }
   }
 }
@@ -287,7 +300,7 @@ __device__ __forceinline__ void item_rows_q8act(const uint8_t *sbase, uint32_t g
         s = dp4a_us(wq[m] & 0x0F0F0F0Fu, D[m], s);
         s = dp4a_us((wq[m] >> 4) & 0x0F0F0F0Fu, D[m + 4], s);
       }
-      acc[4 * g + r] = __fmul_rn(d[r], dx) * static_cast<float>(s);
+      acc[4 * g + r] = __fmul_rn(__fmul_rn(d[r], dx), static_cast<float>(s));
     }
   }
 }

@@ -20,9 +20,11 @@
 //              last CTA: rmsnorm(c_kv, kv_a_norm), optional k_rope RMS norm,
 //              RoPE at pos, append [c_kv | k_rope] at pos (store_compressed,
 //              kv_cache.rs:318).
-//   mla_attn   CTA s: tokens [16 s, 16 s + 16) of [0, pos]; warp per head,
-//              lane per 32nd latent column: online softmax (scale 1 /
-//              sqrt(nope + rope)), partial (m, l, sum p c) per head.
+//   mla_attn   CTA (s, sequence, head group): tokens [S s, S s + S) of
+//              [0, pos] (S = split_tokens, a multiple of 16) for up to 16
+//              heads, 4 heads per warp, lane per 32nd latent column: online
+//              softmax (scale 1 / sqrt(nope + rope)) over 8-token groups,
+//              partial (m, l, sum p c) per head.
 //   mla_merge  CTA per (head, 128 columns): merge the splits in order into
 //              ctx_h; a non-finite max or a sum <= 0 raises the
 //              NumericalInstability status (attention.rs:48-84).
@@ -30,6 +32,7 @@
 #include <cmath>
 
 #include "common.cuh"
+#include "gemv_body.cuh"
 #include "internal.h"
 #include "layout.h"
 #include "mla.h"
@@ -40,7 +43,9 @@ namespace zgpu {
 namespace {
 
 constexpr size_t kMlaSlabMax = 200 * 1024;
-constexpr uint32_t kMlaAttnWarpsMax = 16;
+constexpr uint32_t kMlaAttnWarps = 4;                       // 4 heads per warp
+constexpr uint32_t kMlaHeadsPerCta = 4 * kMlaAttnWarps;     // grid dimension z covers the rest
+constexpr uint32_t kMlaSubTokens = 16;                      // rows per staged buffer
 constexpr uint32_t kMlaMergeThreads = 128;
 
 __device__ __forceinline__ uint32_t mla_pos(const MlaParams &p) {
@@ -185,74 +190,159 @@ __global__ void __launch_bounds__(kMlaPrepThreads) mla_prep_kernel(const MlaPara
   }
 }
 
-__global__ void __launch_bounds__(32 * kMlaAttnWarpsMax) mla_attn_kernel(const MlaParams p0) {
+// Split-K attention over the latent cache.  CTA (split, sequence, head
+// group): tokens [split * split_tokens, ...) of [0, pos] for up to 16 heads;
+// warp w takes 4 heads, lane j holds latent columns j + 32 i of their
+// queries and context sums.  The split's rows stream through two 16-token
+// shared-memory buffers (bulk copies, double-buffered); scores are formed 8
+// tokens at a time: each lane accumulates partial dots of 4 heads x 8 tokens
+// and one reduce-scatter leaves lane l with head l / 8, token l % 8 (31
+// shuffles per 32 scores).  Online softmax per 8-token group, then the
+// context update from the same shared rows.  Output per head: the split's
+// (sum p c, m, l).
+__global__ void __launch_bounds__(32 * kMlaAttnWarps, 2) mla_attn_kernel(const MlaParams p0) {
   const MlaParams p = mla_seq(p0);
-  extern __shared__ __align__(128) float chunk[];   // [tokens of this split][kv_lora + rope]
-  __shared__ __align__(8) uint64_t bar;
+  extern __shared__ __align__(128) float chunk[];   // [2][kMlaSubTokens][kv_lora + rope]
+  __shared__ __align__(8) uint64_t bar[2];
   pdl_launch_dependents();
   pdl_wait();
   const uint32_t pos = mla_pos(p);
   if (pos >= p.max_tokens) return;   // reported by mla_prep
   const uint32_t R = p.kv_lora, RD = p.rope, nr = R / 32, row = R + RD;
-  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  const uint32_t split = blockIdx.x;
-  const uint32_t t0 = split * kMlaSplitTokens;
-  if (t0 > pos) return;   // beyond the context: the merge reads only splits <= pos / 16
-  const uint32_t t1 = min(t0 + kMlaSplitTokens, pos + 1);
-  const uint32_t nt = t1 - t0;
-  // the split's cache rows are contiguous: one bulk copy (row * 4 is a multiple of 16)
-  const uint32_t b = smem_addr(&bar);
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t split = blockIdx.x, st = p.split_tokens;
+  const uint32_t t0 = split * st;
+  if (t0 > pos) return;   // beyond the context: the merge reads only the splits up to pos
+  const uint32_t t1 = min(t0 + st, pos + 1);
+  const uint32_t nsub = (t1 - t0 + kMlaSubTokens - 1) / kMlaSubTokens;
+  const uint32_t bars[2] = {smem_addr(&bar[0]), smem_addr(&bar[1])};
+  // thread 0: sub-tile i (contiguous rows; row * 4 is a multiple of 16) into buffer i & 1
+  auto issue = [&](uint32_t i) {
+    const uint32_t ts = t0 + i * kMlaSubTokens, nt = min(kMlaSubTokens, t1 - ts);
+    mbar_arrive_expect_tx(bars[i & 1], nt * row * 4);
+    bulk_copy_g2s(smem_addr(chunk + (i & 1) * kMlaSubTokens * row), p.cache + static_cast<size_t>(ts) * row,
+                  nt * row * 4, bars[i & 1]);
+  };
   if (threadIdx.x == 0) {
-    mbar_init(b, 1);
+    mbar_init(bars[0], 1);
+    mbar_init(bars[1], 1);
     fence_barrier_init();
+    issue(0);
+    if (nsub > 1) issue(1);
   }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    mbar_arrive_expect_tx(b, nt * row * 4);
-    bulk_copy_g2s(smem_addr(chunk), p.cache + static_cast<size_t>(t0) * row, nt * row * 4, b);
-  }
-  const bool ok = mbar_wait(b, 0, p.status);
-  for (uint32_t h = warp; h < p.n_heads; h += nw) {
-    float qa[16], acc[16], qp[2];
+  // this warp's heads; a head beyond n_heads has zero queries and is not written
+  const uint32_t hb = blockIdx.z * kMlaHeadsPerCta + warp * 4;
+  float qa[4][16], qp[4][2], acc[4][16];
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    const bool hv = hb + h < p.n_heads;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      qa[j] = (j < static_cast<int>(nr)) ? __ldcg(p.q_abs + static_cast<size_t>(h) * R + lane + 32 * j) : 0.f;
-      acc[j] = 0.f;
+      qa[h][j] = (hv && j < static_cast<int>(nr)) ? __ldcg(p.q_abs + static_cast<size_t>(hb + h) * R + lane + 32 * j)
+                                                   : 0.f;
+      acc[h][j] = 0.f;
     }
 #pragma unroll
     for (int j = 0; j < 2; ++j)
-      qp[j] = (lane + 32 * j < RD) ? __ldcg(p.q_pe + static_cast<size_t>(h) * RD + lane + 32 * j) : 0.f;
-    float m = -INFINITY, l = 0.f;
-    for (uint32_t t = 0; ok && t < nt; ++t) {
-      const float *ct = chunk + t * row;
-      float cv[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) cv[j] = (j < static_cast<int>(nr)) ? ct[lane + 32 * j] : 0.f;
-      float d = 0.f;
-#pragma unroll
-      for (int j = 0; j < 2; ++j)
-        if (lane + 32 * j < RD) d = fmaf(qp[j], ct[R + lane + 32 * j], d);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) d = fmaf(qa[j], cv[j], d);
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
-      const float s = __fmul_rn(d, p.scale);
-      const float mn = fmaxf(m, s);
-      const float corr = (m == mn) ? 1.0f : expf(m - mn);
-      const float pe = (s == -INFINITY) ? 0.0f : expf(s - mn);
-      l = fmaf(l, corr, pe);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) acc[j] = fmaf(acc[j], corr, pe * cv[j]);
-      m = mn;
+      qp[h][j] = (hv && lane + 32 * j < RD) ? __ldcg(p.q_pe + static_cast<size_t>(hb + h) * RD + lane + 32 * j) : 0.f;
+  }
+  // lane l's score slot: head l / 8, token l % 8 of each group
+  float m_mine = -INFINITY, l_mine = 0.f;
+  __syncthreads();   // barriers initialised before anyone waits on them
+  bool ok = true;
+  for (uint32_t i = 0; i < nsub; ++i) {
+    ok = __syncthreads_and(ok && mbar_wait(bars[i & 1], (i >> 1) & 1, p.status));
+    if (!ok) {
+      // a copy that did not land: wait (bounded) for the other buffer's
+      // copy in flight, then report through a NaN sum
+      if (threadIdx.x == 0) {
+        mbar_wait(bars[i & 1], (i >> 1) & 1, p.status);
+        if (i + 1 < nsub) mbar_wait(bars[(i + 1) & 1], ((i + 1) >> 1) & 1, p.status);
+      }
+      break;
     }
-    if (!ok) l = __uint_as_float(0x7fc00000u);   // a failed copy surfaces as NumericalInstability
-    float *pp = p.part + (static_cast<size_t>(h) * p.max_splits + split) * (R + 2);
+    const float *ch = chunk + (i & 1) * kMlaSubTokens * row;
+    const uint32_t nt = min(kMlaSubTokens, t1 - (t0 + i * kMlaSubTokens));
+    for (uint32_t g = 0; g < nt; g += 8) {
+      const uint32_t ng = min(8u, nt - g);
+      float v[32];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (static_cast<uint32_t>(k) < ng) {
+          const float *ct = ch + (g + k) * row;
+          float cv[16], cr[2];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) cv[j] = (j < static_cast<int>(nr)) ? ct[lane + 32 * j] : 0.f;
+#pragma unroll
+          for (int j = 0; j < 2; ++j) cr[j] = (lane + 32 * j < RD) ? ct[R + lane + 32 * j] : 0.f;
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            float d = fmaf(qp[h][0], cr[0], 0.f);
+            d = fmaf(qp[h][1], cr[1], d);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) d = fmaf(qa[h][j], cv[j], d);
+            v[h * 8 + k] = d;
+          }
+        } else {
+#pragma unroll
+          for (int h = 0; h < 4; ++h) v[h * 8 + k] = 0.f;
+        }
+      }
+      const float dot = reduce_scatter<32>(v, lane);
+      const float s = ((lane & 7) < ng) ? __fmul_rn(dot, p.scale) : -INFINITY;
+      // this head's group max, new running max, rescale and weights
+      float gm = s;
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, off));
+      const float mn = fmaxf(m_mine, gm);
+      const float corr = (m_mine == mn) ? 1.0f : expf(m_mine - mn);
+      const float pe = (s == -INFINITY) ? 0.0f : expf(s - mn);
+      float ps = pe;
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1) ps = __fadd_rn(ps, __shfl_xor_sync(0xffffffffu, ps, off));
+      l_mine = fmaf(l_mine, corr, ps);
+      m_mine = mn;
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float c = __shfl_sync(0xffffffffu, corr, h * 8);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[h][j] = __fmul_rn(acc[h][j], c);
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (static_cast<uint32_t>(k) < ng) {
+          const float *ct = ch + (g + k) * row;
+          float pk[4];
+#pragma unroll
+          for (int h = 0; h < 4; ++h) pk[h] = __shfl_sync(0xffffffffu, pe, h * 8 + k);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            if (j < static_cast<int>(nr)) {
+              const float c = ct[lane + 32 * j];
+#pragma unroll
+              for (int h = 0; h < 4; ++h) acc[h][j] = fmaf(pk[h], c, acc[h][j]);
+            }
+          }
+        }
+      }
+    }
+    __syncthreads();   // every warp is done with buffer i & 1
+    if (threadIdx.x == 0 && i + 2 < nsub) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(i + 2);
+    }
+  }
+  if (!ok) l_mine = __uint_as_float(0x7fc00000u);   // a failed copy surfaces as NumericalInstability
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    if (hb + h >= p.n_heads) break;
+    float *pp = p.part + (static_cast<size_t>(hb + h) * p.max_splits + split) * (R + 2);
 #pragma unroll
     for (int j = 0; j < 16; ++j)
-      if (j < static_cast<int>(nr)) pp[lane + 32 * j] = acc[j];
-    if (lane == 0) {
-      pp[R] = m;
-      pp[R + 1] = l;
+      if (j < static_cast<int>(nr)) pp[lane + 32 * j] = acc[h][j];
+    if (lane == static_cast<uint32_t>(h) * 8) {
+      pp[R] = m_mine;
+      pp[R + 1] = l_mine;
     }
   }
 }
@@ -267,7 +357,7 @@ __global__ void __launch_bounds__(kMlaMergeThreads) mla_merge_kernel(const MlaPa
   const uint32_t nq = (R + kMlaMergeThreads - 1) / kMlaMergeThreads;
   const uint32_t h = blockIdx.x / nq;
   const uint32_t c = (blockIdx.x % nq) * kMlaMergeThreads + threadIdx.x;
-  const uint32_t nsplit = (pos + kMlaSplitTokens) / kMlaSplitTokens;
+  const uint32_t nsplit = pos / p.split_tokens + 1;
   const float *pb = p.part + static_cast<size_t>(h) * p.max_splits * (R + 2);
   float M = -INFINITY;
   for (uint32_t s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(pb + static_cast<size_t>(s) * (R + 2) + R));
@@ -287,8 +377,11 @@ __global__ void __launch_bounds__(kMlaMergeThreads) mla_merge_kernel(const MlaPa
 }  // namespace
 
 cudaError_t mla_setup() {
-  return cudaFuncSetAttribute(mla_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(kMlaSlabMax));
+  cudaError_t e = cudaFuncSetAttribute(mla_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(kMlaSlabMax));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(mla_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(2 * kMlaSubTokens * (kMlaMaxLatent + kMlaMaxRope) * sizeof(float)));
 }
 
 cudaError_t launch_mla_prep(const MlaParams &mp, const LaunchCfg &lc) {
@@ -309,18 +402,21 @@ cudaError_t launch_mla_prep(const MlaParams &mp, const LaunchCfg &lc) {
   return cudaLaunchKernelEx(&cfg, mla_prep_kernel, p);
 }
 
-cudaError_t launch_mla_attention(const MlaParams &p, const LaunchCfg &lc) {
+cudaError_t launch_mla_attention(const MlaParams &mp, const LaunchCfg &lc) {
+  MlaParams p = mp;
+  if (p.split_tokens == 0) p.split_tokens = kMlaSplitTokens;
   if (p.kv_lora == 0 || p.kv_lora % 32 || p.kv_lora > kMlaMaxLatent || p.rope > kMlaMaxRope ||
-      (p.kv_lora + p.rope) % 4 ||
+      (p.kv_lora + p.rope) % 4 || p.split_tokens % kMlaSplitTokens ||
       p.max_splits < mla_max_splits(p.max_tokens) || p.n_heads == 0)
     return cudaErrorInvalidValue;
-  const uint32_t warps = p.n_heads < kMlaAttnWarpsMax ? p.n_heads : kMlaAttnWarpsMax;
+  const uint32_t hg = (p.n_heads + kMlaHeadsPerCta - 1) / kMlaHeadsPerCta;
+  const uint32_t warps = hg > 1 ? kMlaAttnWarps : (p.n_heads + 3) / 4;
   cudaLaunchAttribute attr[1];
-  const size_t chunk = static_cast<size_t>(kMlaSplitTokens) * (p.kv_lora + p.rope) * sizeof(float);
+  const size_t chunk = 2 * static_cast<size_t>(kMlaSubTokens) * (p.kv_lora + p.rope) * sizeof(float);
   const uint32_t ns = p.n_seq > 1 ? p.n_seq : 1;
   if (ns > 1 && (!p.seq_cache || !p.seq_pos)) return cudaErrorInvalidValue;
-  cudaLaunchConfig_t cfg =
-      make_launch_cfg(dim3(mla_max_splits(p.max_tokens), ns), dim3(32 * warps), chunk, lc, attr);
+  const uint32_t splits = (p.max_tokens + p.split_tokens - 1) / p.split_tokens;
+  cudaLaunchConfig_t cfg = make_launch_cfg(dim3(splits, ns, hg), dim3(32 * warps), chunk, lc, attr);
   if (lc.launch_counter) ++*lc.launch_counter;
   cudaError_t e = cudaLaunchKernelEx(&cfg, mla_attn_kernel, p);
   if (e != cudaSuccess) return e;

@@ -8,7 +8,7 @@
 
 namespace zgpu {
 
-constexpr uint32_t kMlaSplitTokens = 16;   // cached tokens per attention CTA
+constexpr uint32_t kMlaSplitTokens = 16;   // cached tokens per attention CTA (the shortest split)
 constexpr uint32_t kMlaMaxLatent = 512;    // kv_lora_rank
 constexpr uint32_t kMlaMaxRope = 64;       // qk_rope_head_dim
 constexpr uint32_t kMlaMaxNope = 256;      // qk_nope_head_dim
@@ -46,11 +46,25 @@ struct MlaParams {
   float *const *seq_cache;
   uint64_t layer_off;
   const uint32_t *seq_pos;
+  // Tokens per attention split (a multiple of kMlaSplitTokens; 0: the
+  // shortest).  part holds max_splits >= mla_max_splits(max_tokens) slots
+  // per head either way.
+  uint32_t split_tokens;
 };
 
-// Splits (attention CTAs) a cache of max_tokens needs.
+// Splits (attention CTAs) a cache of max_tokens needs at the shortest split.
 inline uint32_t mla_max_splits(uint32_t max_tokens) {
   return (max_tokens + kMlaSplitTokens - 1) / kMlaSplitTokens;
+}
+// Split length for n_seq sequences on caches of max_tokens rows: the
+// shortest, doubled while the launch would still hold at least two CTAs per
+// SM (long contexts in a batch: fewer partial sums to write and merge).
+// Depends on n_seq, so a batch and a lone sequence may split (and round)
+// differently; below 2 * sm_count * 16 / n_seq tokens they agree.
+inline uint32_t mla_split_tokens(uint32_t n_seq, uint32_t max_tokens, uint32_t sm_count) {
+  uint32_t s = kMlaSplitTokens;
+  while (s < 4096 && static_cast<uint64_t>(n_seq) * ((max_tokens + 2 * s - 1) / (2 * s)) >= 2ull * sm_count) s *= 2;
+  return s;
 }
 cudaError_t mla_setup();
 // latent RMSNorm + k_rope norm/RoPE + cache append, and the per-head query

@@ -46,6 +46,7 @@
 #include <stdint.h>
 
 #include "common.cuh"
+#include "tcgen05.cuh"
 #include "internal.h"
 #include "layout.h"
 #include "ops.h"
@@ -93,50 +94,7 @@ struct MmaCfg {
 
 namespace {
 
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// UMMA shared-memory descriptor: K-major, no swizzle (layout type 0),
-// descriptor version 1, LBO / SBO in 16-byte units.
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
-  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
-  d |= 1ull << 46;   // version
-  return d;
-}
-
-
-__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint32_t mbar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)
-               : "memory");
-}
-
-// 32 consecutive 32-bit TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
-        "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-        "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-      : "r"(taddr)
-      : "memory");
-}
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 
 // Packed f32x2 add / multiply, each lane rounded to nearest.  The explicit
@@ -162,12 +120,6 @@ __device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
   return make_float2(__uint_as_float(static_cast<uint32_t>(r)), __uint_as_float(static_cast<uint32_t>(r >> 32)));
 }
 
-// Nibbles n (0..15) of four bytes -> four int8 (n - 8): flip bit 3, then
-// sign-extend it over the high nibble (0x08 * 0x1E = 0xF0, no carries).
-__device__ __forceinline__ uint32_t nib_to_s8(uint32_t n4) {
-  const uint32_t m = n4 ^ 0x08080808u;
-  return m | ((m & 0x08080808u) * 0x1Eu);
-}
 
 template <uint32_t NT>
 __global__ void __launch_bounds__(MmaCfg<NT>::kThreads, MmaCfg<NT>::kCtasPerSm) q4q8_mma_kernel(const MmaGemmParams p) {
