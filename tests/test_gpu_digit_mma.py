@@ -26,11 +26,16 @@ def inputs(n_vec, in_dim, seed):
     if n_vec > 1:
         x[1] = 0.0                                   # an all-zero vector
     if n_vec > 2:
-        x[2, :32] *= 1e-33                           # a negligible block (below 2^-100 after scaling? no: tiny)
+        x[2, :32] *= 1e-33                           # a negligible block (maximum below 2^-100)
         x[2, 32:64] = 0.0                            # a zero block
         x[2, 64:96] *= 1e30 if in_dim > 64 else 1.0  # a huge block
     if n_vec > 3:
         x[3] *= np.exp2(rng.integers(-20, 20, in_dim)).astype(np.float32)   # mixed magnitudes
+    if n_vec > 5:
+        # blocks just above the negligible limit (2^-100): block scales near
+        # 2^-120, so scale products fall into the f32 subnormal range
+        x[4] *= np.float32(2.0 ** -97)
+        x[5] *= np.float32(2.0 ** -99)
     return x
 
 

@@ -157,6 +157,46 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Packed f32x2 add / multiply, each lane rounded to nearest.  The explicit
+// .rn keeps every one a separate rounding (PTX never contracts an add or mul
+// that carries a rounding modifier into an fma), so two columns at a time
+// follow the scalar order exactly: the exact magic-number subtract, then
+// (x * d_w) * d_x.  The accumulation itself stays scalar: a packed add did
+// not reproduce the scalar sums bit for bit.
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+  uint64_t r;
+  asm("{\n\t.reg .b64 pa, pb;\n\tmov.b64 pa, {%1, %2};\n\tmov.b64 pb, {%3, %4};\n\t"
+      "add.rn.f32x2 %0, pa, pb;\n\t}"
+      : "=l"(r)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return make_float2(__uint_as_float(static_cast<uint32_t>(r)), __uint_as_float(static_cast<uint32_t>(r >> 32)));
+}
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  uint64_t r;
+  asm("{\n\t.reg .b64 pa, pb;\n\tmov.b64 pa, {%1, %2};\n\tmov.b64 pb, {%3, %4};\n\t"
+      "mul.rn.f32x2 %0, pa, pb;\n\t}"
+      : "=l"(r)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return make_float2(__uint_as_float(static_cast<uint32_t>(r)), __uint_as_float(static_cast<uint32_t>(r >> 32)));
+}
+__device__ __forceinline__ float2 sub2_rn(float2 a, float2 b) {
+  uint64_t r;
+  asm("{\n\t.reg .b64 pa, pb;\n\tmov.b64 pa, {%1, %2};\n\tmov.b64 pb, {%3, %4};\n\t"
+      "sub.rn.f32x2 %0, pa, pb;\n\t}"
+      : "=l"(r)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return make_float2(__uint_as_float(static_cast<uint32_t>(r)), __uint_as_float(static_cast<uint32_t>(r >> 32)));
+}
+// Packed fused multiply-add a * b + c, each lane rounded once.
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+  uint64_t r;
+  asm("{\n\t.reg .b64 pa, pb, pc;\n\tmov.b64 pa, {%1, %2};\n\tmov.b64 pb, {%3, %4};\n\tmov.b64 pc, {%5, %6};\n\t"
+      "fma.rn.f32x2 %0, pa, pb, pc;\n\t}"
+      : "=l"(r)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return make_float2(__uint_as_float(static_cast<uint32_t>(r)), __uint_as_float(static_cast<uint32_t>(r >> 32)));
+}
+
 // Nibbles n (0..15) of four bytes -> four int8 (n - 8): flip bit 3, then
 // sign-extend it over the high nibble (0x08 * 0x1E = 0xF0, no carries).
 __device__ __forceinline__ uint32_t nib_to_s8(uint32_t n4) {

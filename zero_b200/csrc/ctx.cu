@@ -111,6 +111,7 @@ zgpu_status zgpu_clear_weights(zgpu_ctx *ctx) {
   for (auto &kv : ctx->weights) {
     cudaFree(kv.second.d);
     cudaFree(kv.second.w8);
+    cudaFree(kv.second.dmt);
   }
   ctx->weights.clear();
   return ZGPU_OK;
@@ -262,6 +263,7 @@ zgpu_status zgpu_register_weights(zgpu_ctx *ctx, const void *host_ptr, size_t le
   if (it != ctx->weights.end()) {
     cudaFree(it->second.d);
     cudaFree(it->second.w8);
+    cudaFree(it->second.dmt);
   }
   ctx->weights[key] = t;
   return ZGPU_OK;
@@ -568,11 +570,18 @@ zgpu_status zgpu_linear_dispatch_batch(zgpu_ctx *ctx, const float *x, const void
   if (n_vec > zgpu::kDmMaxVec) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "linear_dispatch_batch: at most 32 vectors");
   if (quant != ZGPU_Q4_0 && quant != ZGPU_Q8_0)
     return zgpu_fail(ctx, ZGPU_ERR_UNSUPPORTED_QUANT, "linear_dispatch_batch: Q4_0 or Q8_0 weights");
-  const DeviceTensor *t = zgpu_lookup(ctx, w_key);
+  DeviceTensor *t = const_cast<DeviceTensor *>(zgpu_lookup(ctx, w_key));
   if (!t) return zgpu_fail(ctx, ZGPU_ERR_UNREGISTERED_WEIGHT, "linear_dispatch_batch: unregistered weight");
   if (t->quant != quant || t->cols != in_dim || t->rows != out_dim)
     return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "linear_dispatch_batch: shape/quant mismatch with registration");
   cudaSetDevice(ctx->device);
+  if (!t->dmt) {
+    ZCHECK(cudaMalloc(&t->dmt, zgpu::dm_tile_bytes(out_dim, static_cast<uint32_t>(in_dim / 32))), "cudaMalloc(tiles)");
+    ZCHECK(zgpu::launch_build_dm_tiles(t->d, t->gstride, quant, static_cast<uint32_t>(out_dim),
+                                       static_cast<uint32_t>(in_dim / 32), t->dmt, ctx->stream),
+           "weight tiles");
+    ++ctx->launches;
+  }
   zgpu_status s = ensure_scratch(ctx, n_vec * in_dim, n_vec * out_dim);
   if (s) return s;
   const uint32_t nv = static_cast<uint32_t>(n_vec), ind = static_cast<uint32_t>(in_dim),
@@ -602,9 +611,7 @@ zgpu_status zgpu_linear_dispatch_batch(zgpu_ctx *ctx, const float *x, const void
   ip.status = ctx->d_status;
   ZCHECK(zgpu::launch_digit_image(ip, lc), "digit image");
   zgpu::DmGemmParams gp = {};
-  gp.w = t->d;
-  gp.gstride = t->gstride;
-  gp.quant = t->quant;
+  gp.wt = t->dmt;
   gp.rows = rows;
   gp.in_dim = ind;
   gp.img = ctx->d_q8;

@@ -18,17 +18,21 @@
 // added in order by dm_combine.  Only integer sums are reassociated, so the
 // result is the GEMV's for any number of vectors.
 //
-// One CTA per SM, persistent over units (segment, 128-row tile, chunk of 32
-// blocks, vector group), all roles walking the same sequence of present
-// blocks (a chunk's blocks in bit-reversed order; the missing blocks of a
-// short last chunk count as +0 in the tree, as the GEMV's idle lanes):
-//   warp 0     image producer: the block's 1600-byte digit image (48 rows and
-//              16 block scales) by one bulk copy into slot s = k % 4;
-//   warp 1     MMA issuer: one tcgen05.mma into accumulator s, commit;
-//   warps 2-5  epilogue: TMEM lane quarter (warp % 4), 16 vectors per thread;
-//   warps 6-9  weight converters: thread = row; cp.async of the row's 16 (32)
-//              bytes and its scale word 7 blocks ahead, then int8 A tile,
-//              row sum and f32 scale into slot s.
+// The weights are pre-tiled once per tensor (launch_build_dm_tiles: int8
+// rows in the MMA layout with their f32 scales and row sums), so a block is
+// two bulk copies.  One CTA per SM, persistent over units (segment, 128-row
+// tile, chunk of 32 blocks, vector group), all roles walking the same
+// sequence of present blocks (a chunk's blocks in bit-reversed order; the
+// missing blocks of a short last chunk count as +0 in the tree, as the
+// GEMV's idle lanes):
+//   warp 0      producer: the weight tile block (5 KB) and the digit image
+//               block (1600 B) into stage k % 8;
+//   warp 1      MMA issuer: one tcgen05.mma (M 128, N 48, K 32) into
+//               accumulator k % 8 once the epilogue has read block k - 8
+//               out of it, commit;
+//   warps 2-17  epilogue: TMEM lane quarter (warp % 4) x 4 of the 16
+//               vectors (q, q+4, q+8, q+12: few vectors still use every
+//               warp); the block terms folded into the chunk's tree.
 // Every wait is bounded; an expired wait stops that role, which drains what
 // it has in flight, and raises ZDEV_ERR_TIMEOUT.
 #include <cuda_runtime.h>
@@ -48,22 +52,21 @@ namespace zgpu {
 
 namespace {
 
-constexpr uint32_t kDmSlots = 4;                         // A / image / scale slots = accumulators
-constexpr uint32_t kDmStg = 8;                           // weight staging depth per converter thread
+constexpr uint32_t kDmSlots = 8;                         // shared-memory stages (blocks in flight)
+constexpr uint32_t kDmAccs = 8;                          // TMEM accumulators
 constexpr uint32_t kDmAccCols = 64;                      // TMEM columns per accumulator (48 used)
-constexpr uint32_t kDmTmem = kDmSlots * kDmAccCols;      // 256
-constexpr uint32_t kDmThreads = 320;
-constexpr uint32_t kOffA = 0;                                        // kDmSlots x 4 KB int8 tiles
-constexpr uint32_t kOffB = kOffA + kDmSlots * 4096;                  // kDmSlots x image blocks
-constexpr uint32_t kOffQ = kOffB + kDmSlots * kDmImgBlock;           // kDmStg x 128 rows x 32 B
-constexpr uint32_t kOffS = kOffQ + kDmStg * 128 * 32;                // kDmStg x 128 scale words
-constexpr uint32_t kOffDw = kOffS + kDmStg * 128 * 4;                // kDmSlots x 128 f32 d_w
-constexpr uint32_t kOffRs = kOffDw + kDmSlots * 128 * 4;             // kDmSlots x 128 s32 row sums
-constexpr uint32_t kDmSmem = kOffRs + kDmSlots * 128 * 4;
+constexpr uint32_t kDmTmem = kDmAccs * kDmAccCols;       // 512: the whole TMEM, one CTA per SM
+constexpr uint32_t kDmEpiWarps = 16;                     // 4 lane quarters x 4 vector quarters
+constexpr uint32_t kDmThreads = 32 * (2 + kDmEpiWarps);  // producer, MMA, epilogue
+constexpr uint32_t kDmSlotBytes = kDmTileBlock + kDmImgBlock;   // weight block, then image block
+constexpr uint32_t kDmSmem = kDmSlots * kDmSlotBytes;
+// more than half an SM's shared memory: a second CTA on the SM would wait on
+// its TMEM allocation
+constexpr uint32_t kDmDynSmem = 120 * 1024;
 // kind::i8, D s32, A and B signed, K-major, N = 48, M = 128
 constexpr uint32_t kDmIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((kDmN >> 3) << 17) | ((128u >> 4) << 24);
-static_assert(kDmSmem + 1024 <= 227 * 1024, "shared memory");
-static_assert(kOffB % 16 == 0 && kOffQ % 16 == 0 && kDmImgBlock % 16 == 0, "bulk-copy alignment");
+static_assert(kDmSmem + 1024 <= kDmDynSmem, "shared memory");
+static_assert(kDmSlotBytes % 16 == 0 && kDmTileBlock % 16 == 0 && kDmImgBlock % 16 == 0, "bulk-copy alignment");
 
 // byte offset of (row, K half) in a K-major no-swizzle tile: 8-row core
 // matrices of 16-byte rows, K halves 128 B apart, row groups 256 B apart
@@ -81,6 +84,8 @@ __global__ void __launch_bounds__(256) digit_image_kernel(const DigitImageParams
   const uint32_t v = blockIdx.x, im = blockIdx.y;
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t nvi = p.n_vec_of ? min(__ldcg(p.n_vec_of + im), p.n_vec) : p.n_vec;
+  // a vector group no unit reads (all past the count) is not written
+  if (v >= (nvi + kDmVec - 1) / kDmVec * kDmVec) return;
   const bool live = v < nvi;
   const float *x = p.x;
   if (live)
@@ -89,7 +94,10 @@ __global__ void __launch_bounds__(256) digit_image_kernel(const DigitImageParams
   float inv = 1.0f;
   if (p.norm_w && live) inv = rms_inv<8>(x, p.in_dim, p.eps, red, tid, 1);
   const uint32_t bpr = p.in_dim / 32, nf4 = p.in_dim / 4, ng = (p.n_vec + kDmVec - 1) / kDmVec;
-  const uint32_t g = v / kDmVec, vl = v % kDmVec;
+  // vector vl of group g sits at column position pv: epilogue warp q of the
+  // 4 per lane quarter reads positions 4q..4q+3 = vectors q, q+4, q+8, q+12,
+  // so a group with few vectors still spreads them over every warp
+  const uint32_t g = v / kDmVec, vl = v % kDmVec, pv = (vl % 4) * 4 + vl / 4;
   uint8_t *img = p.img + (static_cast<uint64_t>(im) * ng + g) * bpr * kDmImgBlock;
   // warp-uniform trip count: a block's 8 lanes are all in range or all out
   for (uint32_t f0 = warp * 32; f0 < nf4; f0 += 256) {
@@ -114,16 +122,54 @@ __global__ void __launch_bounds__(256) digit_image_kernel(const DigitImageParams
       const uint32_t dw[3] = {w0 ^ 0x80808080u, w1 ^ 0x80808080u, w2};
 #pragma unroll
       for (int d = 0; d < 3; ++d)
-        *reinterpret_cast<uint32_t *>(blk + kmaj_off(d * kDmVec + vl, j >> 4) + (j & 15)) = dw[d];
-      if ((f & 7) == 0) *reinterpret_cast<float *>(blk + kDmN * 32 + vl * 4) = bs;
+        *reinterpret_cast<uint32_t *>(blk + kmaj_off(d * kDmVec + pv, j >> 4) + (j & 15)) = dw[d];
+      if ((f & 7) == 0) *reinterpret_cast<float *>(blk + kDmN * 32 + pv * 4) = bs;
     }
   }
+}
+
+// ------------------------------------------------------------ weight tiles
+// CTA (tile, block), thread = row of the tile.
+__global__ void __launch_bounds__(128) build_dm_tiles_kernel(const uint8_t *w, uint64_t gstride, uint32_t quant,
+                                                             uint32_t rows, uint32_t bpr, uint8_t *tiles) {
+  const uint32_t t = blockIdx.x, b = blockIdx.y, r = threadIdx.x, row = t * 128 + r;
+  uint8_t *blk = tiles + (static_cast<uint64_t>(t) * bpr + b) * kDmTileBlock;
+  uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
+  float dw = 0.f;
+  int rs = 0;
+  if (row < rows) {
+    const uint8_t *grp = w + static_cast<uint64_t>(row >> 2) * gstride;
+    if (quant == ZGPU_Q4_0) {
+      const uint4 qv = *reinterpret_cast<const uint4 *>(grp + plane_entry(ZGPU_Q4_0, bpr, b, row & 3));
+      lo = make_uint4(nib_to_s8(qv.x & 0x0F0F0F0Fu), nib_to_s8(qv.y & 0x0F0F0F0Fu), nib_to_s8(qv.z & 0x0F0F0F0Fu),
+                      nib_to_s8(qv.w & 0x0F0F0F0Fu));
+      hi = make_uint4(nib_to_s8((qv.x >> 4) & 0x0F0F0F0Fu), nib_to_s8((qv.y >> 4) & 0x0F0F0F0Fu),
+                      nib_to_s8((qv.z >> 4) & 0x0F0F0F0Fu), nib_to_s8((qv.w >> 4) & 0x0F0F0F0Fu));
+    } else {
+      lo = *reinterpret_cast<const uint4 *>(grp + plane_entry(ZGPU_Q8_0, bpr, b, 2 * (row & 3)));
+      hi = *reinterpret_cast<const uint4 *>(grp + plane_entry(ZGPU_Q8_0, bpr, b, 2 * (row & 3) + 1));
+    }
+    const uint32_t ones = 0x01010101u;
+    rs = dp4a_ss(lo.x, ones, dp4a_ss(lo.y, ones, dp4a_ss(lo.z, ones, dp4a_ss(lo.w, ones, 0))));
+    rs = dp4a_ss(hi.x, ones, dp4a_ss(hi.y, ones, dp4a_ss(hi.z, ones, dp4a_ss(hi.w, ones, rs))));
+    const uint8_t *sc = grp + scale_entry(quant, bpr, b) + 2 * (row & 3);
+    dw = h2f(static_cast<uint16_t>(sc[0] | (sc[1] << 8)));
+  }
+  *reinterpret_cast<uint4 *>(blk + kmaj_off(r, 0)) = lo;
+  *reinterpret_cast<uint4 *>(blk + kmaj_off(r, 1)) = hi;
+  reinterpret_cast<float *>(blk + 4096)[r] = dw;
+  reinterpret_cast<int *>(blk + 4096 + 512)[r] = rs;
 }
 
 // ------------------------------------------------------------ the MMA kernel
 struct DmGeom {
   uint32_t bpr, ks, n_mt, n_vg, n_units;
+  // per-segment vector counts and tile bases, copied to shared memory once
+  // (null: read from global memory, for launches of many segments)
+  const uint32_t *nv_s;
+  const unsigned long long *tab_s;
 };
+constexpr uint32_t kDmSegCache = 256;
 
 __device__ __forceinline__ DmGeom dm_geom(const DmGemmParams &p) {
   DmGeom g;
@@ -132,12 +178,14 @@ __device__ __forceinline__ DmGeom dm_geom(const DmGemmParams &p) {
   g.n_mt = (p.rows + 127) / 128;
   g.n_vg = (p.n_vec + kDmVec - 1) / kDmVec;
   g.n_units = p.n_seg * g.n_mt * g.ks * g.n_vg;
+  g.nv_s = nullptr;
+  g.tab_s = nullptr;
   return g;
 }
 
 struct DmUnit {
   uint32_t seg, mt, c, vg, nb, nv;   // nv: vectors of this unit's group
-  const uint8_t *w;                  // the segment's group streams
+  const uint8_t *w;                  // the segment's weight tiles
 };
 
 // Decode unit u; false when it has no work (a zero table entry, or no
@@ -148,14 +196,14 @@ __device__ __forceinline__ bool dm_unit(const DmGemmParams &p, const DmGeom &g, 
   x.mt = (u / (g.n_vg * g.ks)) % g.n_mt;
   x.seg = u / (g.n_vg * g.ks * g.n_mt);
   x.nb = chunk_blocks(g.bpr, x.c);
-  const uint32_t nvs = p.n_vec_of ? min(__ldcg(p.n_vec_of + x.seg), p.n_vec) : p.n_vec;
+  const uint32_t nvs = g.nv_s ? g.nv_s[x.seg] : p.n_vec_of ? min(__ldcg(p.n_vec_of + x.seg), p.n_vec) : p.n_vec;
   if (nvs <= x.vg * kDmVec) return false;
   x.nv = min(nvs - x.vg * kDmVec, kDmVec);
   if (p.w_tab) {
-    x.w = reinterpret_cast<const uint8_t *>(__ldcg(p.w_tab + x.seg % p.w_tab_mod));
+    x.w = reinterpret_cast<const uint8_t *>(g.tab_s ? g.tab_s[x.seg] : __ldcg(p.w_tab + x.seg % p.w_tab_mod));
     if (!x.w) return false;
   } else {
-    x.w = p.w + x.seg * p.w_seg_stride;
+    x.w = p.wt + x.seg * p.wt_seg_stride;
   }
   return true;
 }
@@ -197,10 +245,12 @@ __device__ __forceinline__ bool walk_next(const DmGemmParams &p, const DmGeom &g
 __global__ void __launch_bounds__(kDmThreads, 1) dm_gemm_kernel(const DmGemmParams p) {
   extern __shared__ __align__(1024) uint8_t dsm[];
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dsm) + 1023) & ~uintptr_t(1023));
-  __shared__ __align__(8) uint64_t afull[kDmSlots], bfull[kDmSlots], done[kDmSlots], eempty[kDmSlots], drain;
+  __shared__ __align__(8) uint64_t full[kDmSlots], eempty[kDmSlots], done[kDmAccs], drain;
   __shared__ uint32_t tmem_base;
+  __shared__ uint32_t nv_s[kDmSegCache];
+  __shared__ unsigned long long tab_s[kDmSegCache];
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const DmGeom g = dm_geom(p);
+  DmGeom g = dm_geom(p);
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
@@ -210,11 +260,10 @@ __global__ void __launch_bounds__(kDmThreads, 1) dm_gemm_kernel(const DmGemmPara
   }
   if (tid == 32) {
     for (uint32_t s = 0; s < kDmSlots; ++s) {
-      mbar_init(smem_addr(&afull[s]), 4);
-      mbar_init(smem_addr(&bfull[s]), 1);
-      mbar_init(smem_addr(&done[s]), 1);
-      mbar_init(smem_addr(&eempty[s]), 4);
+      mbar_init(smem_addr(&full[s]), 1);
+      mbar_init(smem_addr(&eempty[s]), kDmEpiWarps);
     }
+    for (uint32_t a = 0; a < kDmAccs; ++a) mbar_init(smem_addr(&done[a]), 1);
     mbar_init(smem_addr(&drain), 1);
     fence_barrier_init();
   }
@@ -224,41 +273,56 @@ __global__ void __launch_bounds__(kDmThreads, 1) dm_gemm_kernel(const DmGemmPara
   const uint32_t tmem = tmem_base;
   pdl_launch_dependents();
   pdl_wait();   // images and dispatch tables are earlier kernels' outputs
+  if (p.n_seg <= kDmSegCache) {
+    for (uint32_t sg = tid; sg < p.n_seg; sg += kDmThreads) {
+      nv_s[sg] = p.n_vec_of ? min(__ldcg(p.n_vec_of + sg), p.n_vec) : p.n_vec;
+      tab_s[sg] = p.w_tab ? __ldcg(p.w_tab + sg % p.w_tab_mod) : 0ull;
+    }
+    __syncthreads();
+    g.nv_s = nv_s;
+    g.tab_s = p.w_tab ? tab_s : nullptr;
+  }
 
   const uint64_t img_bytes = static_cast<uint64_t>(g.n_vg) * g.bpr * kDmImgBlock;
   DmWalk wk;
   walk_start(wk);
   if (warp == 0) {
-    // ---------------- image producer ----------------
+    // ---------------- producer ----------------
     if (lane == 0) {
       uint32_t k = 0;
       while (walk_next(p, g, wk)) {
         const uint32_t s = k % kDmSlots;
         if (k >= kDmSlots && !mbar_wait(smem_addr(&eempty[s]), ((k / kDmSlots) - 1) & 1, p.status)) break;
         const uint32_t b = wk.x.c * kChunkBlocks + br5(wk.i);
-        const uint8_t *src = p.img + (p.img_seg ? wk.x.seg * img_bytes : 0) +
-                             (static_cast<uint64_t>(wk.x.vg) * g.bpr + b) * kDmImgBlock;
-        const uint32_t fb = smem_addr(&bfull[s]);
-        mbar_arrive_expect_tx(fb, kDmImgBlock);
-        bulk_copy_g2s(smem_addr(sm + kOffB + s * kDmImgBlock), src, kDmImgBlock, fb);
+        const uint8_t *wsrc = wk.x.w + (static_cast<uint64_t>(wk.x.mt) * g.bpr + b) * kDmTileBlock;
+        const uint8_t *isrc = p.img + (p.img_seg ? wk.x.seg * img_bytes : 0) +
+                              (static_cast<uint64_t>(wk.x.vg) * g.bpr + b) * kDmImgBlock;
+        const uint32_t fb = smem_addr(&full[s]), dst = smem_addr(sm + s * kDmSlotBytes);
+        mbar_arrive_expect_tx(fb, kDmSlotBytes);
+        bulk_copy_g2s(dst, wsrc, kDmTileBlock, fb);
+        bulk_copy_g2s(dst + kDmTileBlock, isrc, kDmImgBlock, fb);
         ++k;
         ++wk.i;
       }
       // never leave a copy in flight when the CTA may exit
       for (uint32_t j = k > kDmSlots ? k - kDmSlots : 0; j < k; ++j)
-        mbar_wait(smem_addr(&bfull[j % kDmSlots]), (j / kDmSlots) & 1, p.status);
+        mbar_wait(smem_addr(&full[j % kDmSlots]), (j / kDmSlots) & 1, p.status);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       uint32_t k = 0;
       while (walk_next(p, g, wk)) {
-        const uint32_t s = k % kDmSlots, ph = (k / kDmSlots) & 1;
-        if (!mbar_wait(smem_addr(&afull[s]), ph, p.status) || !mbar_wait(smem_addr(&bfull[s]), ph, p.status)) break;
+        const uint32_t s = k % kDmSlots, a = k % kDmAccs;
+        if (!mbar_wait(smem_addr(&full[s]), (k / kDmSlots) & 1, p.status)) break;
+        // accumulator a is free once the epilogue has finished block k - 8
+        if (k >= kDmAccs &&
+            !mbar_wait(smem_addr(&eempty[(k - kDmAccs) % kDmSlots]), ((k - kDmAccs) / kDmSlots) & 1, p.status))
+          break;
         tc_fence_after();
-        umma_i8(tmem + s * kDmAccCols, umma_desc(smem_addr(sm + kOffA + s * 4096), 128, 256),
-                umma_desc(smem_addr(sm + kOffB + s * kDmImgBlock), 128, 256), kDmIdesc, 0u);
-        umma_commit(smem_addr(&done[s]));
+        const uint32_t st = smem_addr(sm + s * kDmSlotBytes);
+        umma_i8(tmem + a * kDmAccCols, umma_desc(st, 128, 256), umma_desc(st + kDmTileBlock, 128, 256), kDmIdesc, 0u);
+        umma_commit(smem_addr(&done[a]));
         ++k;
         ++wk.i;
       }
@@ -266,147 +330,110 @@ __global__ void __launch_bounds__(kDmThreads, 1) dm_gemm_kernel(const DmGemmPara
       umma_commit(smem_addr(&drain));
       mbar_wait(smem_addr(&drain), 0, p.status);
     }
-  } else if (warp >= 6) {
-    // ---------------- weight converters ----------------
-    const uint32_t cr = tid - 192;   // row of the tile
-    const bool q4 = p.quant == ZGPU_Q4_0;
-    DmWalk ic = wk;                  // issue cursor, kDmStg - 1 blocks ahead
-    uint32_t issued = 0;
-    auto issue_next = [&]() {
-      if (walk_next(p, g, ic)) {
-        const uint32_t row = ic.x.mt * 128 + cr, st = issued % kDmStg;
-        if (row < p.rows) {
-          const uint32_t b = ic.x.c * kChunkBlocks + br5(ic.i);
-          const uint8_t *grp = ic.x.w + static_cast<uint64_t>(row >> 2) * p.gstride;
-          const uint32_t dq = smem_addr(sm + kOffQ + st * 4096 + cr * 32);
-          if (q4) {
-            cp_async16(dq, grp + plane_entry(ZGPU_Q4_0, g.bpr, b, row & 3), 16);
-          } else {
-            cp_async16(dq, grp + plane_entry(ZGPU_Q8_0, g.bpr, b, 2 * (row & 3)), 16);
-            cp_async16(dq + 16, grp + plane_entry(ZGPU_Q8_0, g.bpr, b, 2 * (row & 3) + 1), 16);
-          }
-          cp_async4(smem_addr(sm + kOffS + st * 512 + cr * 4),
-                    grp + scale_entry(p.quant, g.bpr, b) + 4 * ((row & 3) >> 1), 4);
-        }
-        ++ic.i;
-        ++issued;
-      }
-      cp_async_commit();
-    };
-    for (uint32_t j = 0; j + 1 < kDmStg; ++j) issue_next();
-    uint32_t k = 0;
-    while (walk_next(p, g, wk)) {
-      issue_next();
-      cp_async_wait<kDmStg - 1>();
-      const uint32_t s = k % kDmSlots;
-      if (k >= kDmSlots && !mbar_wait(smem_addr(&eempty[s]), ((k / kDmSlots) - 1) & 1, p.status)) break;
-      const uint32_t row = wk.x.mt * 128 + cr, st = k % kDmStg;
-      uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
-      int rs = 0;
-      float dw = 0.f;
-      if (row < p.rows) {
-        const uint8_t *q = sm + kOffQ + st * 4096 + cr * 32;
-        if (q4) {
-          const uint4 qv = *reinterpret_cast<const uint4 *>(q);
-          lo = make_uint4(nib_to_s8(qv.x & 0x0F0F0F0Fu), nib_to_s8(qv.y & 0x0F0F0F0Fu),
-                          nib_to_s8(qv.z & 0x0F0F0F0Fu), nib_to_s8(qv.w & 0x0F0F0F0Fu));
-          hi = make_uint4(nib_to_s8((qv.x >> 4) & 0x0F0F0F0Fu), nib_to_s8((qv.y >> 4) & 0x0F0F0F0Fu),
-                          nib_to_s8((qv.z >> 4) & 0x0F0F0F0Fu), nib_to_s8((qv.w >> 4) & 0x0F0F0F0Fu));
-        } else {
-          lo = *reinterpret_cast<const uint4 *>(q);
-          hi = *reinterpret_cast<const uint4 *>(q + 16);
-        }
-        const uint32_t ones = 0x01010101u;
-        rs = dp4a_ss(lo.x, ones, dp4a_ss(lo.y, ones, dp4a_ss(lo.z, ones, dp4a_ss(lo.w, ones, 0))));
-        rs = dp4a_ss(hi.x, ones, dp4a_ss(hi.y, ones, dp4a_ss(hi.z, ones, dp4a_ss(hi.w, ones, rs))));
-        const uint32_t sw = *reinterpret_cast<const uint32_t *>(sm + kOffS + st * 512 + cr * 4);
-        dw = h2f(static_cast<uint16_t>((row & 1) ? (sw >> 16) : (sw & 0xFFFFu)));
-      }
-      uint8_t *a = sm + kOffA + s * 4096;
-      *reinterpret_cast<uint4 *>(a + kmaj_off(cr, 0)) = lo;
-      *reinterpret_cast<uint4 *>(a + kmaj_off(cr, 1)) = hi;
-      reinterpret_cast<float *>(sm + kOffDw + s * 512)[cr] = dw;
-      reinterpret_cast<int *>(sm + kOffRs + s * 512)[cr] = rs;
-      // generic-proxy writes, read by the tensor core's async proxy
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&afull[s]));
-      ++k;
-      ++wk.i;
-    }
-    cp_async_wait<0>();
   } else {
     // ---------------- epilogue ----------------
-    const uint32_t q = warp & 3, rt = 32 * q + lane;   // TMEM lane quarter, tile row
-    const uint32_t taddr = tmem + ((32u * q) << 16);
+    // thread: tile row rt (TMEM lane quarter warp % 4) x vectors vq, vq + 4,
+    // vq + 8, vq + 12 (column positions 4 vq .. 4 vq + 3)
+    const uint32_t q = warp & 3, vq = (warp - 2) >> 2, rt = 32 * q + lane;
+    const uint32_t taddr = tmem + ((32u * q) << 16) + 4 * vq;
+    const float M = 12582912.0f;   // 1.5 * 2^23: int v, |v| < 2^22, is float(bits(M) + v) - M exactly
     uint32_t k = 0;
     bool ok = true;
+    // block terms of leaf i of the chunk for the thread's 4 vectors, as two
+    // packed pairs (0 for a missing block)
+    auto leaf = [&](const DmUnit &x, uint32_t i, float2 (&val)[2]) {
+      val[0] = val[1] = make_float2(0.0f, 0.0f);
+      if (!ok || br5(i) >= x.nb) return;
+      const uint32_t s = k % kDmSlots, a = k % kDmAccs;
+      // the accumulator, and (acquired directly) the stage's scales and row sums
+      ok = mbar_wait(smem_addr(&done[a]), (k / kDmAccs) & 1, p.status) &&
+           mbar_wait(smem_addr(&full[s]), (k / kDmSlots) & 1, p.status);
+      if (!ok) return;
+      ++k;
+      if (vq >= x.nv) {   // none of this warp's vectors: only release the stage
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(&eempty[s]));
+        return;
+      }
+      tc_fence_after();
+      uint32_t a0[4], a1[4], a2[4];
+      tmem_ld4(taddr + a * kDmAccCols, a0);
+      tmem_ld4(taddr + a * kDmAccCols + kDmVec, a1);
+      tmem_ld4(taddr + a * kDmAccCols + 2 * kDmVec, a2);
+      const uint8_t *slot = sm + s * kDmSlotBytes;
+      const float dw = reinterpret_cast<const float *>(slot + 4096)[rt];
+      // s_d = a_d + 128 * row sum for the two low digits, folded into the magic constant
+      const int kk = reinterpret_cast<const int *>(slot + 4096 + 512)[rt] * 128 + 0x4B400000;
+      const float4 bs = reinterpret_cast<const float4 *>(slot + kDmTileBlock + kDmN * 32)[vq];
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&eempty[s]));
+      const float2 m2 = make_float2(M, M), c256 = make_float2(256.0f, 256.0f), c64k = make_float2(65536.0f, 65536.0f);
+      const float2 dw2 = make_float2(dw, dw);
+      const float2 bsp[2] = {make_float2(bs.x, bs.y), make_float2(bs.z, bs.w)};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (vq + 8 * h >= x.nv) break;   // pair h = vectors vq + 8h and vq + 8h + 4
+        // S0, S1, S2 exactly as floats (|S| < 2^22); X = S0 + 256 S1 rounded
+        // once, as the GEMV's int-to-float of its s0 + (s1 << 8)
+        const float2 f0 = sub2_rn(make_float2(__int_as_float(static_cast<int>(a0[2 * h]) + kk),
+                                              __int_as_float(static_cast<int>(a0[2 * h + 1]) + kk)), m2);
+        const float2 f1 = sub2_rn(make_float2(__int_as_float(static_cast<int>(a1[2 * h]) + kk),
+                                              __int_as_float(static_cast<int>(a1[2 * h + 1]) + kk)), m2);
+        const float2 f2 = sub2_rn(make_float2(__int_as_float(static_cast<int>(a2[2 * h]) + 0x4B400000),
+                                              __int_as_float(static_cast<int>(a2[2 * h + 1]) + 0x4B400000)), m2);
+        const float2 t = fma2_rn(f2, c64k, fma2_rn(f1, c256, f0));
+        val[h] = mul2_rn(mul2_rn(dw2, bsp[h]), t);
+      }
+    };
     for (uint32_t u = blockIdx.x; u < g.n_units && ok; u += gridDim.x) {
       DmUnit x;
       if (!dm_unit(p, g, u, x)) continue;
-      float L[5][kDmVec];
-      float res[kDmVec];
+      // the chunk's 32 leaves in bit-reversed block order folded as the
+      // GEMV's butterfly: 4-leaf subtrees, then a counter over 8 subtrees
+      float2 L2[2], L3[2], L4[2], res[2];
+      for (uint32_t o = 0; o < 8; ++o) {
+        float2 s01[2], v2[2], v3[2], xs[2];
+        leaf(x, 4 * o, xs);
+        leaf(x, 4 * o + 1, v2);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        float val[kDmVec];
-        if (ok && static_cast<uint32_t>(br5(i)) < x.nb) {
-          const uint32_t s = k % kDmSlots;
-          const uint32_t ph = (k / kDmSlots) & 1;
-          // the accumulator, and (acquired directly) the converters' scales
-          // and the image's block scales
-          ok = mbar_wait(smem_addr(&done[s]), ph, p.status) && mbar_wait(smem_addr(&afull[s]), ph, p.status) &&
-               mbar_wait(smem_addr(&bfull[s]), ph, p.status);
-          if (ok) {
-            tc_fence_after();
-            uint32_t d0[16], d1[16], d2[16];
-            tmem_ld16(taddr + s * kDmAccCols, d0);
-            tmem_ld16(taddr + s * kDmAccCols + 16, d1);
-            tmem_ld16(taddr + s * kDmAccCols + 32, d2);
-            tmem_ld_wait();
-            const float dw = reinterpret_cast<const float *>(sm + kOffDw + s * 512)[rt];
-            const int rs128 = reinterpret_cast<const int *>(sm + kOffRs + s * 512)[rt] * 128;
-            const float *bsc = reinterpret_cast<const float *>(sm + kOffB + s * kDmImgBlock + kDmN * 32);
+        for (int h = 0; h < 2; ++h) s01[h] = add2_rn(xs[h], v2[h]);
+        leaf(x, 4 * o + 2, v2);
+        leaf(x, 4 * o + 3, v3);
 #pragma unroll
-            for (int v = 0; v < static_cast<int>(kDmVec); ++v) {
-              const int s0 = static_cast<int>(d0[v]) + rs128, s1 = static_cast<int>(d1[v]) + rs128;
-              const float t = fmaf(static_cast<float>(static_cast<int>(d2[v])), 65536.0f,
-                                   static_cast<float>(s0 + (s1 << 8)));
-              val[v] = __fmul_rn(__fmul_rn(dw, bsc[v]), t);
+        for (int h = 0; h < 2; ++h) xs[h] = add2_rn(s01[h], add2_rn(v2[h], v3[h]));
+        if (o & 1) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) xs[h] = add2_rn(L2[h], xs[h]);
+          if (o & 2) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) xs[h] = add2_rn(L3[h], xs[h]);
+            if (o & 4) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) res[h] = add2_rn(L4[h], xs[h]);
+            } else {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) L4[h] = xs[h];
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_addr(&eempty[s]));
-            ++k;
-          }
-        }
-        if (!(ok && static_cast<uint32_t>(br5(i)) < x.nb)) {
-#pragma unroll
-          for (int v = 0; v < static_cast<int>(kDmVec); ++v) val[v] = 0.0f;
-        }
-        // leaf i of the chunk's tree: fold equal-sized subtrees (left + right)
-#pragma unroll
-        for (int lv = 0; lv < 5; ++lv) {
-          if ((i >> lv) & 1) {
-#pragma unroll
-            for (int v = 0; v < static_cast<int>(kDmVec); ++v) val[v] = __fadd_rn(L[lv][v], val[v]);
           } else {
 #pragma unroll
-            for (int v = 0; v < static_cast<int>(kDmVec); ++v) L[lv][v] = val[v];
-            break;
+            for (int h = 0; h < 2; ++h) L3[h] = xs[h];
           }
-        }
-        if (i == 31) {
+        } else {
 #pragma unroll
-          for (int v = 0; v < static_cast<int>(kDmVec); ++v) res[v] = val[v];
+          for (int h = 0; h < 2; ++h) L2[h] = xs[h];
         }
       }
+      // this thread's vectors vq, vq + 4, vq + 8, vq + 12
+      const float resv[4] = {res[0].x, res[0].y, res[1].x, res[1].y};
       const uint32_t row = x.mt * 128 + rt;
       if (row < p.rows) {
         float *dst = p.part + (static_cast<uint64_t>(x.seg) * g.ks + x.c) * p.n_vec * p.rows + row;
 #pragma unroll
-        for (int v = 0; v < static_cast<int>(kDmVec); ++v)
-          if (static_cast<uint32_t>(v) < x.nv)
-            dst[static_cast<uint64_t>(x.vg * kDmVec + v) * p.rows] = ok ? res[v] : __uint_as_float(0x7fc00000u);
+        for (int v = 0; v < 4; ++v)
+          if (vq + 4 * v < x.nv)
+            dst[static_cast<uint64_t>(x.vg * kDmVec + vq + 4 * v) * p.rows] = ok ? resv[v] : __uint_as_float(0x7fc00000u);
       }
     }
   }
@@ -450,7 +477,15 @@ __global__ void dm_combine_kernel(const DmCombineParams p) {
 
 cudaError_t dm_setup() {
   return cudaFuncSetAttribute(dm_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(kDmSmem + 1024));
+                              static_cast<int>(kDmDynSmem));
+}
+
+cudaError_t launch_build_dm_tiles(const uint8_t *w, uint64_t gstride, uint32_t quant, uint32_t rows, uint32_t bpr,
+                                  uint8_t *tiles, cudaStream_t s) {
+  if (!w || !tiles || rows == 0 || bpr == 0 || gstride % 16 || (quant != ZGPU_Q4_0 && quant != ZGPU_Q8_0))
+    return cudaErrorInvalidValue;
+  build_dm_tiles_kernel<<<dim3((rows + 127) / 128, bpr), 128, 0, s>>>(w, gstride, quant, rows, bpr, tiles);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_digit_image(const DigitImageParams &p, const LaunchCfg &lc) {
@@ -464,15 +499,27 @@ cudaError_t launch_digit_image(const DigitImageParams &p, const LaunchCfg &lc) {
 
 cudaError_t launch_dm_gemm(const DmGemmParams &p, const LaunchCfg &lc) {
   if (p.in_dim == 0 || p.in_dim % 32 || p.rows == 0 || p.n_vec == 0 || p.n_vec > kDmMaxVec || p.n_seg == 0 ||
-      p.gstride % 16 || (p.quant != ZGPU_Q4_0 && p.quant != ZGPU_Q8_0) || !p.part || !p.img ||
-      (p.w_tab && p.w_tab_mod == 0) || (!p.w_tab && !p.w))
+      !p.part || !p.img || (p.w_tab && p.w_tab_mod == 0) || (!p.w_tab && !p.wt))
     return cudaErrorInvalidValue;
   const uint64_t units = static_cast<uint64_t>(p.n_seg) * ((p.rows + 127) / 128) *
                          ((p.in_dim / 32 + kChunkBlocks - 1) / kChunkBlocks) * dm_groups(p.n_vec);
   const uint32_t sms = lc.sm_count > 0 ? static_cast<uint32_t>(lc.sm_count) : 148u;
-  const uint32_t grid = static_cast<uint32_t>(units < sms ? units : sms);
+  uint32_t grid = static_cast<uint32_t>(units < sms ? units : sms);
+  // CTA b takes units b, b + grid, ...: a grid coprime with (vector groups x
+  // chunks) gives every CTA a mix of both, whose work differs (empty vector
+  // groups, a short last chunk)
+  const uint32_t period = dm_groups(p.n_vec) * ((p.in_dim / 32 + kChunkBlocks - 1) / kChunkBlocks);
+  auto gcd = [](uint32_t a, uint32_t b) {
+    while (b) {
+      const uint32_t t = a % b;
+      a = b;
+      b = t;
+    }
+    return a;
+  };
+  while (grid > 1 && units > grid && gcd(grid, period) != 1) --grid;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = make_launch_cfg(dim3(grid), dim3(kDmThreads), kDmSmem + 1024, lc, attr);
+  cudaLaunchConfig_t cfg = make_launch_cfg(dim3(grid), dim3(kDmThreads), kDmDynSmem, lc, attr);
   if (lc.launch_counter) ++*lc.launch_counter;
   return cudaLaunchKernelEx(&cfg, dm_gemm_kernel, p);
 }

@@ -43,20 +43,31 @@ inline uint64_t dm_img_bytes(uint32_t in_dim, uint32_t n_vec) {
 }
 cudaError_t launch_digit_image(const DigitImageParams &p, const LaunchCfg &lc);
 
+// Weight tiles of the batched matvec: for each 128-row tile t and 32-element
+// block b, at (t * bpr + b) * kDmTileBlock, the 128 rows' int8 weights w_j
+// (n_j - 8 for Q4_0, q_j for Q8_0) in the MMA's K-major layout (4 KB), the
+// rows' f32 block scales, and the rows' int32 sums of w_j.  Rows past `rows`
+// in the last tile are zero.  Built once per tensor from its group streams.
+constexpr uint32_t kDmTileBlock = 4096 + 128 * 4 + 128 * 4;
+inline uint64_t dm_tile_bytes(uint64_t rows, uint32_t bpr) {
+  return (rows + 127) / 128 * static_cast<uint64_t>(bpr) * kDmTileBlock;
+}
+cudaError_t launch_build_dm_tiles(const uint8_t *w, uint64_t gstride, uint32_t quant, uint32_t rows, uint32_t bpr,
+                                  uint8_t *tiles, cudaStream_t s);
+
 // Partial sums of n_seg matvecs against digit images: segment s multiplies
-// weights w + s * w_seg_stride (or the group streams at w_tab[s % w_tab_mod])
-// by image s * img_seg (img_seg 0: one image for all), rows x in_dim, and
+// the weight tiles at wt + s * wt_seg_stride (or w_tab[s % w_tab_mod]),
+// rows x in_dim, by image s * img_seg (img_seg 0: one image for all), and
 // writes part[((s * ks + c) * n_vec + v) * rows + r]: chunk c's sum of
 // vector v for row r (ks = ceil(in_dim / 1024) chunks of 32 blocks).  A
 // zero table entry skips its segment.  n_vec_of (per segment, device):
 // fewer vectors than n_vec for that segment.
 struct DmGemmParams {
-  const uint8_t *w;
-  uint64_t w_seg_stride;
+  const uint8_t *wt;
+  uint64_t wt_seg_stride;
   const unsigned long long *w_tab;
   uint32_t w_tab_mod;
-  uint64_t gstride;
-  uint32_t quant, rows, in_dim;
+  uint32_t rows, in_dim;
   const uint8_t *img;
   uint32_t img_seg;          // 1: image s for segment s, 0: image 0 for every segment
   uint32_t n_vec, n_seg;

@@ -30,6 +30,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "digit_mma.h"
 #include "internal.h"
 #include "layout.h"
 #include "mla.h"
@@ -82,6 +83,12 @@ struct Ds2Layer {
   uint32_t mha = 0, mha_idx = 0;
   uint8_t *cat_qkv = nullptr;        // owned
   uint32_t qkv_groups = 0;
+  // tiles of the batch's tensor-core projections (digit_mma.h), built by
+  // the first zgpu_ds2_decode_batch: kv_a|q_a, q_b, O, per-head V, dense
+  // gate|up and down
+  uint8_t *t_cat = nullptr, *t_qb = nullptr, *t_o = nullptr, *t_v = nullptr, *t_gu = nullptr, *t_dn = nullptr;
+  // MoE layers: this rank's routed experts' and the shared experts' tiles
+  uint8_t *t_egu = nullptr, *t_edn = nullptr, *t_sgu = nullptr, *t_sdn = nullptr;
   // norms (views into the model's norm block)
   const float *attn_norm = nullptr, *ffn_norm = nullptr, *kv_a_norm = nullptr, *q_a_norm = nullptr,
               *k_norm = nullptr;
@@ -140,8 +147,14 @@ struct zgpu_ds2_model {
           *wts = nullptr, *part = nullptr;
     uint32_t *ids = nullptr, *counter = nullptr, *tok = nullptr, *pos = nullptr, *out = nullptr,
              *codes = nullptr;
-    unsigned long long *seg = nullptr;   // per layer: gate|up table then down table, kDs2MaxBatch*n_seg each
     float **cache = nullptr;             // [kDs2MaxBatch] each sequence's zgpu_mla_kv rows
+    uint8_t *t_out = nullptr;            // LM-head tiles
+    // the expert grouping of the current MoE layer (moe.h MoeDispatchParams)
+    uint32_t *dn_vec = nullptr, *x_rows_gu = nullptr, *x_rows_dn = nullptr;
+    float **out_gu = nullptr, **out_dn = nullptr;
+    unsigned long long *tab_gu = nullptr, *tab_dn = nullptr;
+    uint8_t *img = nullptr;              // digit images of the tensor-core projections
+    float *dpart = nullptr;              // their chunk partials
     uint32_t ca_stride = 0, act_stride = 0, splits = 0, max_tokens = 0;
     cudaGraphExec_t graph = nullptr;
     uint32_t graph_n = 0, graph_kernels = 0;
@@ -490,47 +503,104 @@ cudaError_t ds2_enqueue_batch(zgpu_ds2_model *m, uint32_t ns, uint32_t *counter)
   if (e != cudaSuccess) return e;
   const uint32_t H = d.hidden, R = d.kv_lora_rank, RD = d.rope_dim, QL = d.q_lora_rank;
   const uint32_t NH = d.n_heads, hq = d.nope_dim + d.rope_dim, VD = d.v_dim;
-  const uint32_t n_seg = d.n_shared + d.top_k;
+  // One projection of every sequence on the tensor cores (digit_mma.h):
+  // the digit image of the inputs (RMSNorm first when norm_w), the MMA
+  // partials, then the GEMV's epilogue.  n_img > 1: image / segment i uses
+  // the inputs at x + i * x_img_stride and the i-th of n_img tile sets.
+  // Each sequence's result is the single-sequence GEMV's bit for bit.
+  auto dm = [&](const float *x, uint64_t x_stride, uint64_t x_img_stride, uint32_t n_img, const float *norm_w,
+                const uint8_t *tiles, uint32_t rows, uint32_t in_dim, float *out, uint64_t out_seg_stride,
+                uint64_t out_vec_stride, GemvEpi epi) -> cudaError_t {
+    DigitImageParams ip = {};
+    ip.x = x;
+    ip.x_stride = x_stride;
+    ip.x_img_stride = x_img_stride;
+    ip.norm_w = norm_w;
+    ip.eps = d.rms_eps;
+    ip.in_dim = in_dim;
+    ip.n_vec = ns;
+    ip.n_img = n_img;
+    ip.img = B.img;
+    ip.status = m->d_status;
+    cudaError_t e2 = launch_digit_image(ip, lc);
+    if (e2 != cudaSuccess) return e2;
+    DmGemmParams gp = {};
+    gp.wt = tiles;
+    gp.wt_seg_stride = dm_tile_bytes(rows, in_dim / 32);
+    gp.rows = rows;
+    gp.in_dim = in_dim;
+    gp.img = B.img;
+    gp.img_seg = n_img > 1 ? 1 : 0;
+    gp.n_vec = ns;
+    gp.n_seg = n_img;
+    gp.part = B.dpart;
+    gp.status = m->d_status;
+    if ((e2 = launch_dm_gemm(gp, lc)) != cudaSuccess) return e2;
+    DmCombineParams cp = {};
+    cp.part = B.dpart;
+    cp.rows = rows;
+    cp.ks = (in_dim / 32 + kChunkBlocks - 1) / kChunkBlocks;
+    cp.n_vec = ns;
+    cp.n_seg = n_img;
+    cp.out = out;
+    cp.out_seg_stride = out_seg_stride;
+    cp.out_vec_stride = out_vec_stride;
+    cp.epi = epi;
+    return launch_dm_combine(cp, lc);
+  };
+  // The expert matvecs: n_segs segments of up to 32 vectors each (count
+  // B.dn_vec[s]); vector j of segment s reads row x_rows[s * 32 + j] of x,
+  // multiplies the tiles tab[s] and writes out_rows[s * 32 + j].
+  auto dm_grouped = [&](const float *x, uint64_t x_stride, const float *norm_w, const uint32_t *x_rows,
+                        const unsigned long long *tab, uint32_t n_segs, uint32_t rows, uint32_t in_dim,
+                        float *const *out_rows, GemvEpi epi) -> cudaError_t {
+    DigitImageParams ip = {};
+    ip.x = x;
+    ip.x_stride = x_stride;
+    ip.x_rows = x_rows;
+    ip.n_vec_of = B.dn_vec;
+    ip.norm_w = norm_w;
+    ip.eps = d.rms_eps;
+    ip.in_dim = in_dim;
+    ip.n_vec = kDmMaxVec;
+    ip.n_img = n_segs;
+    ip.img = B.img;
+    ip.status = m->d_status;
+    cudaError_t e2 = launch_digit_image(ip, lc);
+    if (e2 != cudaSuccess) return e2;
+    DmGemmParams gp = {};
+    gp.w_tab = tab;
+    gp.w_tab_mod = n_segs;
+    gp.rows = rows;
+    gp.in_dim = in_dim;
+    gp.img = B.img;
+    gp.img_seg = 1;
+    gp.n_vec = kDmMaxVec;
+    gp.n_seg = n_segs;
+    gp.n_vec_of = B.dn_vec;
+    gp.part = B.dpart;
+    gp.status = m->d_status;
+    if ((e2 = launch_dm_gemm(gp, lc)) != cudaSuccess) return e2;
+    DmCombineParams cp = {};
+    cp.part = B.dpart;
+    cp.rows = rows;
+    cp.ks = (in_dim / 32 + kChunkBlocks - 1) / kChunkBlocks;
+    cp.n_vec = kDmMaxVec;
+    cp.n_seg = n_segs;
+    cp.n_vec_of = B.dn_vec;
+    cp.out_rows = out_rows;
+    cp.epi = epi;
+    return launch_dm_combine(cp, lc);
+  };
   for (uint32_t l = 0; l < d.n_layers; ++l) {
     const Ds2Layer &L = m->layers[l];
-    // RMSNorm + fused kv_a_mqa | q_a, one segment per sequence
-    GemvDesc g;
-    g.w = L.cat_a;
-    g.gstride = m->gs_h;
-    g.wbytes = static_cast<uint64_t>(L.cat_a_groups) * m->gs_h;
-    g.quant = d.attn_quant;
-    g.rows = R + RD + QL;
-    g.groups = L.cat_a_groups;
-    g.in_dim = H;
-    g.seg_count = ns;
-    g.seg_x_stride = H;
-    g.seg_out_stride = B.ca_stride;
-    GemvIo io;
-    io.x = B.hidden;
-    io.norm_w = L.attn_norm;
-    io.eps = d.rms_eps;
-    io.out = B.ca;
-    io.status = m->d_status;
-    if ((e = launch_gemv(g, PRO_RMSNORM, EPI_STORE, io, lc)) != cudaSuccess) return e;
-    // RMSNorm(c_q) + q_b
-    g = GemvDesc();
-    g.w = L.q_b->d;
-    g.gstride = L.q_b->gstride;
-    g.wbytes = L.q_b->bytes;
-    g.quant = d.attn_quant;
-    g.rows = NH * hq;
-    g.groups = static_cast<uint32_t>(L.q_b->groups);
-    g.in_dim = QL;
-    g.seg_count = ns;
-    g.seg_x_stride = B.ca_stride;
-    g.seg_out_stride = NH * hq;
-    io = GemvIo();
-    io.x = B.ca + R + RD;
-    io.norm_w = L.q_a_norm;
-    io.eps = d.rms_eps;
-    io.out = B.q;
-    io.status = m->d_status;
-    if ((e = launch_gemv(g, PRO_RMSNORM, EPI_STORE, io, lc)) != cudaSuccess) return e;
+    // RMSNorm + fused kv_a_mqa | q_a; RMSNorm(c_q) + q_b
+    if ((e = dm(B.hidden, H, 0, 1, L.attn_norm, L.t_cat, R + RD + QL, H, B.ca, 0,
+                B.ca_stride, EPI_STORE)) != cudaSuccess)
+      return e;
+    if ((e = dm(B.ca + R + RD, B.ca_stride, 0, 1, L.q_a_norm, L.t_qb, NH * hq, QL, B.q, 0, NH * hq,
+                EPI_STORE)) != cudaSuccess)
+      return e;
     // latent append + query absorption, attention, merge: each sequence on
     // its own cache rows and position
     MlaParams mp = {};
@@ -565,82 +635,23 @@ cudaError_t ds2_enqueue_batch(zgpu_ds2_model *m, uint32_t ns, uint32_t *counter)
     mp.split_tokens = mla_split_tokens(ns, B.max_tokens, m->ctx->sm_count);
     if ((e = launch_mla_prep(mp, lc)) != cudaSuccess) return e;
     if ((e = launch_mla_attention(mp, lc)) != cudaSuccess) return e;
-    // per-head V projection: segment b * NH + h reads ctx row (b, h) and
-    // head h's v rows
-    g = GemvDesc();
-    g.gstride = L.v_gstride;
-    g.wbytes = L.v_seg_bytes;
-    g.quant = d.attn_quant;
-    g.rows = VD;
-    g.groups = VD / 4;
-    g.in_dim = R;
-    g.seg_w = L.d_vseg;
-    g.seg_w_mod = NH;
-    g.seg_count = ns * NH;
-    g.seg_x_stride = R;
-    g.seg_out_stride = VD;
-    io = GemvIo();
-    io.x = B.ctx;
-    io.out = B.concat;
-    io.status = m->d_status;
-    if ((e = launch_gemv(g, PRO_PLAIN, EPI_STORE, io, lc)) != cudaSuccess) return e;
+    // per-head V projection: image h holds every sequence's ctx row of
+    // head h, segment h streams head h's v rows
+    if ((e = dm(B.ctx, static_cast<uint64_t>(NH) * R, R, NH, nullptr, L.t_v, VD, R, B.concat, VD,
+                static_cast<uint64_t>(NH) * VD, EPI_STORE)) != cudaSuccess)
+      return e;
     // O projection + residual
-    g = GemvDesc();
-    g.w = L.o->d;
-    g.gstride = L.o->gstride;
-    g.wbytes = L.o->bytes;
-    g.quant = d.attn_quant;
-    g.rows = H;
-    g.groups = H / 4;
-    g.in_dim = NH * VD;
-    g.seg_count = ns;
-    g.seg_x_stride = NH * VD;
-    g.seg_out_stride = H;
-    io = GemvIo();
-    io.x = B.concat;
-    io.out = B.hidden;
-    io.status = m->d_status;
-    if ((e = launch_gemv(g, PRO_PLAIN, EPI_RESADD, io, lc)) != cudaSuccess) return e;
+    if ((e = dm(B.concat, static_cast<uint64_t>(NH) * VD, 0, 1, nullptr, L.t_o, H, NH * VD, B.hidden, 0, H,
+                EPI_RESADD)) != cudaSuccess)
+      return e;
 
     if (!L.moe) {
-      g = GemvDesc();
-      g.w = L.gateup;
-      g.gstride = m->gs_h;
-      g.wbytes = static_cast<uint64_t>(2 * d.ffn / 4) * m->gs_h;
-      g.quant = ZGPU_Q4_0;
-      g.rows = d.ffn;
-      g.groups = 2 * d.ffn / 4;
-      g.in_dim = H;
-      g.seg_count = ns;
-      g.seg_x_stride = H;
-      g.seg_out_stride = B.act_stride;
-      io = GemvIo();
-      io.x = B.hidden;
-      io.norm_w = L.ffn_norm;
-      io.eps = d.rms_eps;
-      io.out = B.act;
-      io.status = m->d_status;
-      if ((e = launch_gemv(g, PRO_RMSNORM, EPI_SWIGLU, io, lc)) != cudaSuccess) return e;
-      g = GemvDesc();
-      g.w = L.down->d;
-      g.gstride = L.down->gstride;
-      g.wbytes = L.down->bytes;
-      g.quant = ZGPU_Q4_0;
-      g.rows = H;
-      g.groups = H / 4;
-      g.in_dim = d.ffn;
-      g.seg_count = ns;
-      g.seg_x_stride = B.act_stride;
-      g.seg_out_stride = H;
-      io = GemvIo();
-      io.x = B.act;
-      io.out = B.hidden;
-      io.status = m->d_status;
-      if ((e = launch_gemv(g, PRO_PLAIN, EPI_RESADD, io, lc)) != cudaSuccess) return e;
+      if ((e = dm(B.hidden, H, 0, 1, L.ffn_norm, L.t_gu, 2 * d.ffn, H, B.act, 0, B.act_stride, EPI_SWIGLU)) != cudaSuccess)
+        return e;
+      if ((e = dm(B.act, B.act_stride, 0, 1, nullptr, L.t_dn, H, d.ffn, B.hidden, 0, H, EPI_RESADD)) != cudaSuccess)
+        return e;
       continue;
     }
-    const size_t tab = static_cast<size_t>(kDs2MaxBatch) * n_seg;
-    unsigned long long *seg_gu = B.seg + 2 * tab * l, *seg_dn = seg_gu + tab;
     RouteParams rp = {};
     rp.x = B.hidden;
     rp.norm_w = L.ffn_norm;
@@ -656,8 +667,8 @@ cudaError_t ds2_enqueue_batch(zgpu_ds2_model *m, uint32_t ns, uint32_t *counter)
     rp.ids = B.ids + static_cast<size_t>(l) * kDs2MaxBatch * d.top_k;
     rp.weights = B.wts + static_cast<size_t>(l) * kDs2MaxBatch * d.top_k;
     rp.counter = B.counter;
-    rp.seg_gu = seg_gu;
-    rp.seg_dn = seg_dn;
+    rp.seg_gu = nullptr;   // the expert grouping below replaces the per-token tables
+    rp.seg_dn = nullptr;
     rp.gu_base = reinterpret_cast<unsigned long long>(L.gateup);
     rp.dn_base = reinterpret_cast<unsigned long long>(L.down->d);
     rp.sh_gu_base = reinterpret_cast<unsigned long long>(L.sh_gateup);
@@ -671,45 +682,42 @@ cudaError_t ds2_enqueue_batch(zgpu_ds2_model *m, uint32_t ns, uint32_t *counter)
     rp.n_seq = ns;
     rp.x_stride = H;
     if ((e = launch_moe_route(rp, lc)) != cudaSuccess) return e;
-    // grouped gate|up + SiLU*up: segment b * n_seg + s is token b's s-th
-    // expert (shared ones first), all n_seg of them on token b's input
-    g = GemvDesc();
-    g.gstride = m->gs_h;
-    g.wbytes = m->gu_bytes;
-    g.quant = ZGPU_Q4_0;
-    g.rows = d.expert_ffn;
-    g.groups = 2 * d.expert_ffn / 4;
-    g.in_dim = H;
-    g.seg_w = seg_gu;
-    g.seg_count = ns * n_seg;
-    g.seg_x_stride = H;
-    g.seg_x_group = n_seg;
-    g.seg_out_stride = d.expert_ffn;
-    g.seg_dynamic = true;
-    io = GemvIo();
-    io.x = B.hidden;
-    io.norm_w = L.ffn_norm;
-    io.eps = d.rms_eps;
-    io.out = B.act;
-    io.status = m->d_status;
-    if ((e = launch_gemv(g, PRO_RMSNORM, EPI_SWIGLU, io, lc)) != cudaSuccess) return e;
-    g = GemvDesc();
-    g.gstride = m->gs_e;
-    g.wbytes = m->dn_bytes;
-    g.quant = ZGPU_Q4_0;
-    g.rows = H;
-    g.groups = H / 4;
-    g.in_dim = d.expert_ffn;
-    g.seg_w = seg_dn;
-    g.seg_count = ns * n_seg;
-    g.seg_x_stride = d.expert_ffn;
-    g.seg_out_stride = H;
-    g.seg_dynamic = true;
-    io = GemvIo();
-    io.x = B.act;
-    io.out = B.expout;
-    io.status = m->d_status;
-    if ((e = launch_gemv(g, PRO_PLAIN, EPI_STORE, io, lc)) != cudaSuccess) return e;
+    // the batch's (token, expert) pairs grouped by expert, then the grouped
+    // gate|up + SiLU*up and down matvecs on the tensor cores: segment =
+    // expert, vectors = the tokens that selected it
+    const uint32_t n_local = m->world > 1 ? m->ep_per_rank : d.n_experts, n_segs = n_local + d.n_shared;
+    MoeDispatchParams dp = {};
+    dp.ids = rp.ids;
+    dp.n_seq = ns;
+    dp.top_k = d.top_k;
+    dp.n_shared = d.n_shared;
+    dp.n_local = n_local;
+    dp.ep_rank = m->rank;
+    dp.ep_per_rank = m->world > 1 ? m->ep_per_rank : 0;
+    dp.act = B.act;
+    dp.exp_out = B.expout;
+    dp.act_row = d.expert_ffn;
+    dp.dim = H;
+    dp.tiles_gu = L.t_egu;
+    dp.tiles_dn = L.t_edn;
+    dp.sh_tiles_gu = L.t_sgu;
+    dp.sh_tiles_dn = L.t_sdn;
+    dp.tiles_gu_stride = dm_tile_bytes(2ull * d.expert_ffn, H / 32);
+    dp.tiles_dn_stride = dm_tile_bytes(H, d.expert_ffn / 32);
+    dp.n_vec = B.dn_vec;
+    dp.x_rows_gu = B.x_rows_gu;
+    dp.x_rows_dn = B.x_rows_dn;
+    dp.out_gu = B.out_gu;
+    dp.out_dn = B.out_dn;
+    dp.tab_gu = B.tab_gu;
+    dp.tab_dn = B.tab_dn;
+    if ((e = launch_moe_dispatch(dp, lc)) != cudaSuccess) return e;
+    if ((e = dm_grouped(B.hidden, H, L.ffn_norm, B.x_rows_gu, B.tab_gu, n_segs, 2 * d.expert_ffn, H, B.out_gu,
+                        EPI_SWIGLU)) != cudaSuccess)
+      return e;
+    if ((e = dm_grouped(B.act, d.expert_ffn, nullptr, B.x_rows_dn, B.tab_dn, n_segs, H, d.expert_ffn, B.out_dn,
+                        EPI_STORE)) != cudaSuccess)
+      return e;
     if (m->world > 1) {
       EpPublishParams pp = {};
       pp.exp_out = B.expout;
@@ -742,26 +750,10 @@ cudaError_t ds2_enqueue_batch(zgpu_ds2_model *m, uint32_t ns, uint32_t *counter)
     if ((e = launch_moe_combine(cp, lc)) != cudaSuccess) return e;
     if (m->world > 1 && (e = launch_moe_ep_advance(m->d_ep_seq, lc)) != cudaSuccess) return e;
   }
-  // LM head: RMSNorm + GEMV per sequence, then the reference's greedy pick
-  // per logits row
-  GemvDesc g;
-  g.w = m->out->d;
-  g.wbytes = m->out->bytes;
-  g.gstride = m->out->gstride;
-  g.quant = m->out->quant;
-  g.rows = d.vocab_padded;
-  g.groups = static_cast<uint32_t>(m->out->groups);
-  g.in_dim = H;
-  g.seg_count = ns;
-  g.seg_x_stride = H;
-  g.seg_out_stride = d.vocab_padded;
-  GemvIo io;
-  io.x = B.hidden;
-  io.norm_w = m->d_out_norm;
-  io.eps = d.rms_eps;
-  io.out = B.logits;
-  io.status = m->d_status;
-  if ((e = launch_gemv(g, PRO_RMSNORM, EPI_STORE, io, lc)) != cudaSuccess) return e;
+  // LM head: RMSNorm + matvec per sequence, then the reference's greedy
+  // pick per logits row
+  if ((e = dm(B.hidden, H, 0, 1, m->d_out_norm, B.t_out, d.vocab_padded, H, B.logits, 0, d.vocab_padded, EPI_STORE)) != cudaSuccess)
+    return e;
   if (counter) ++*counter;
   return launch_rows_argmax(B.logits, ns, d.vocab_padded, d.vocab_real, B.out, B.codes, m->d_status, lc.stream);
 }
@@ -859,6 +851,105 @@ zgpu_status ds2_prepare_kv(zgpu_ds2_model *m, zgpu_mla_kv *kv) {
   return ZGPU_OK;
 }
 
+// Scratch of the batch's tensor-core projections (digit_mma.h): the largest
+// digit image (32 vectors, per-head images for the V projection) and the
+// largest set of chunk partials.
+uint64_t ds2_dm_img_bytes(const zgpu_ds2_desc &d) {
+  const uint32_t NB = kDs2MaxBatch;
+  uint64_t b = std::max(dm_img_bytes(d.hidden, NB), static_cast<uint64_t>(d.n_heads) * dm_img_bytes(d.kv_lora_rank, NB));
+  b = std::max(b, dm_img_bytes(d.q_lora_rank, NB));
+  b = std::max(b, dm_img_bytes(d.n_heads * d.v_dim, NB));
+  if (d.ffn % 32 == 0 && d.ffn) b = std::max(b, dm_img_bytes(d.ffn, NB));
+  // expert groups: one image per expert segment
+  const uint64_t segs = static_cast<uint64_t>(d.n_experts) + d.n_shared;
+  if (d.expert_ffn % 32 == 0 && d.expert_ffn)
+    b = std::max(b, segs * std::max(dm_img_bytes(d.hidden, NB), dm_img_bytes(d.expert_ffn, NB)));
+  return b;
+}
+uint64_t ds2_dm_part_floats(const zgpu_ds2_desc &d, bool any_dense) {
+  auto ks = [](uint32_t in_dim) { return static_cast<uint64_t>((in_dim / 32 + kChunkBlocks - 1) / kChunkBlocks); };
+  const uint64_t NB = kDs2MaxBatch, H = d.hidden, R = d.kv_lora_rank;
+  const uint64_t cat_rows = (static_cast<uint64_t>(R + d.rope_dim + d.q_lora_rank) + 8) & ~7ull;
+  uint64_t f = ks(d.hidden) * NB * std::max<uint64_t>(cat_rows, d.vocab_padded);
+  if (any_dense) f = std::max(f, ks(d.hidden) * NB * 2 * d.ffn);
+  f = std::max(f, ks(d.q_lora_rank) * NB * d.n_heads * (d.nope_dim + d.rope_dim));
+  f = std::max(f, d.n_heads * ks(d.kv_lora_rank) * NB * d.v_dim);
+  f = std::max(f, ks(d.n_heads * d.v_dim) * NB * H);
+  if (any_dense) f = std::max(f, ks(d.ffn) * NB * H);
+  const uint64_t segs = static_cast<uint64_t>(d.n_experts) + d.n_shared;
+  if (d.expert_ffn % 32 == 0 && d.expert_ffn) {
+    f = std::max(f, segs * ks(d.hidden) * NB * 2 * d.expert_ffn);
+    f = std::max(f, segs * ks(d.expert_ffn) * NB * H);
+  }
+  return f;
+}
+
+// The weight tiles of every projection the batch step runs on the tensor
+// cores (MLA layers: the batch refuses MHA layers).
+bool ds2_build_tiles(zgpu_ds2_model *m) {
+  const zgpu_ds2_desc &d = m->desc;
+  cudaStream_t st = m->ctx->stream;
+  auto tiles = [&](const uint8_t *w, uint64_t gstride, uint32_t quant, uint32_t rows, uint32_t in_dim,
+                   uint8_t *dst) -> bool {
+    return launch_build_dm_tiles(w, gstride, quant, rows, in_dim / 32, dst, st) == cudaSuccess;
+  };
+  auto alloc = [&](uint8_t **p, uint64_t rows, uint32_t in_dim, uint32_t copies) -> bool {
+    return cudaMalloc(p, copies * dm_tile_bytes(rows, in_dim / 32)) == cudaSuccess;
+  };
+  const uint32_t H = d.hidden, R = d.kv_lora_rank, NH = d.n_heads, VD = d.v_dim, hq = d.nope_dim + d.rope_dim;
+  for (Ds2Layer &L : m->layers) {
+    if (L.mha) continue;
+    const uint32_t cat_rows = R + d.rope_dim + d.q_lora_rank;
+    if (!alloc(&L.t_cat, cat_rows, H, 1) || !tiles(L.cat_a, m->gs_h, d.attn_quant, cat_rows, H, L.t_cat)) return false;
+    if (!alloc(&L.t_qb, NH * hq, d.q_lora_rank, 1) ||
+        !tiles(L.q_b->d, L.q_b->gstride, d.attn_quant, NH * hq, d.q_lora_rank, L.t_qb))
+      return false;
+    if (!alloc(&L.t_o, H, NH * VD, 1) || !tiles(L.o->d, L.o->gstride, d.attn_quant, H, NH * VD, L.t_o)) return false;
+    std::vector<unsigned long long> vseg(NH);
+    if (cudaMemcpy(vseg.data(), L.d_vseg, NH * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return false;
+    if (!alloc(&L.t_v, VD, R, NH)) return false;
+    for (uint32_t h = 0; h < NH; ++h)
+      if (!tiles(reinterpret_cast<const uint8_t *>(vseg[h]), L.v_gstride, d.attn_quant, VD, R,
+                 L.t_v + h * dm_tile_bytes(VD, R / 32)))
+        return false;
+    if (!L.moe) {
+      if (!alloc(&L.t_gu, 2ull * d.ffn, H, 1) || !tiles(L.gateup, m->gs_h, ZGPU_Q4_0, 2 * d.ffn, H, L.t_gu))
+        return false;
+      if (!alloc(&L.t_dn, H, d.ffn, 1) || !tiles(L.down->d, L.down->gstride, ZGPU_Q4_0, H, d.ffn, L.t_dn))
+        return false;
+      continue;
+    }
+    // this rank's routed experts, then the shared ones (each expert's
+    // interleaved gate|up rows and its down rows as separate tile sets)
+    const uint32_t EF = d.expert_ffn, n_local = m->world > 1 ? m->ep_per_rank : d.n_experts;
+    const uint32_t e0 = m->world > 1 ? m->rank * m->ep_per_rank : 0;
+    const uint64_t sgu = dm_tile_bytes(2ull * EF, H / 32), sdn = dm_tile_bytes(H, EF / 32);
+    if (!alloc(&L.t_egu, 2ull * EF, H, n_local) || !alloc(&L.t_edn, H, EF, n_local)) return false;
+    for (uint32_t i = 0; i < n_local; ++i) {
+      if (!tiles(L.gateup + static_cast<uint64_t>(e0 + i) * m->gu_bytes, m->gs_h, ZGPU_Q4_0, 2 * EF, H,
+                 L.t_egu + i * sgu) ||
+          !tiles(L.down->d + static_cast<uint64_t>(e0 + i) * m->dn_bytes, m->gs_e, ZGPU_Q4_0, H, EF,
+                 L.t_edn + i * sdn))
+        return false;
+    }
+    if (d.n_shared) {
+      if (!alloc(&L.t_sgu, 2ull * EF, H, d.n_shared) || !alloc(&L.t_sdn, H, EF, d.n_shared)) return false;
+      for (uint32_t i = 0; i < d.n_shared; ++i) {
+        if (!tiles(L.sh_gateup + static_cast<uint64_t>(i) * m->gu_bytes, m->gs_h, ZGPU_Q4_0, 2 * EF, H,
+                   L.t_sgu + i * sgu) ||
+            !tiles(L.sh_down->d + static_cast<uint64_t>(i) * m->dn_bytes, L.sh_down->gstride, ZGPU_Q4_0, H, EF,
+                   L.t_sdn + i * sdn))
+          return false;
+      }
+    }
+  }
+  auto &B = m->b;
+  if (!alloc(&B.t_out, d.vocab_padded, H, 1) ||
+      !tiles(m->out->d, m->out->gstride, m->out->quant, d.vocab_padded, H, B.t_out))
+    return false;
+  return cudaStreamSynchronize(st) == cudaSuccess;
+}
+
 void ds2_free_batch(zgpu_ds2_model *m) {
   auto &B = m->b;
   if (B.graph) cudaGraphExecDestroy(B.graph);
@@ -866,8 +957,22 @@ void ds2_free_batch(zgpu_ds2_model *m) {
                    B.wts, B.part})
     cudaFree(p);
   for (uint32_t *p : {B.ids, B.counter, B.tok, B.pos, B.out, B.codes}) cudaFree(p);
-  cudaFree(B.seg);
   cudaFree(B.cache);
+  cudaFree(B.img);
+  cudaFree(B.dpart);
+  cudaFree(B.t_out);
+  cudaFree(B.dn_vec);
+  cudaFree(B.x_rows_gu);
+  cudaFree(B.x_rows_dn);
+  cudaFree(B.out_gu);
+  cudaFree(B.out_dn);
+  cudaFree(B.tab_gu);
+  cudaFree(B.tab_dn);
+  for (Ds2Layer &L : m->layers)
+    for (uint8_t **t : {&L.t_cat, &L.t_qb, &L.t_o, &L.t_v, &L.t_gu, &L.t_dn, &L.t_egu, &L.t_edn, &L.t_sgu, &L.t_sdn}) {
+      cudaFree(*t);
+      *t = nullptr;
+    }
   B = zgpu_ds2_model::Batch();
 }
 
@@ -886,7 +991,6 @@ zgpu_status ds2_prepare_batch(zgpu_ds2_model *m, uint32_t max_tokens) {
     B.ca_stride = R + RD + d.q_lora_rank + 8;
     B.act_stride = static_cast<uint32_t>(std::max<size_t>(any_dense ? d.ffn : 0, static_cast<size_t>(n_seg) * d.expert_ffn));
     const size_t topk = any_moe ? d.top_k : 1;
-    const size_t tab = NB * (n_seg ? n_seg : 1);
     const uint32_t hq = d.nope_dim + RD;
     if (cudaMalloc(&B.hidden, NB * H * 4) || cudaMalloc(&B.ca, NB * B.ca_stride * 4) ||
         cudaMalloc(&B.q, NB * NH * hq * 4) || cudaMalloc(&B.qabs, NB * NH * R * 4) ||
@@ -897,13 +1001,21 @@ zgpu_status ds2_prepare_batch(zgpu_ds2_model *m, uint32_t max_tokens) {
         cudaMalloc(&B.logits, NB * d.vocab_padded * 4) || cudaMalloc(&B.wts, d.n_layers * NB * topk * 4) ||
         cudaMalloc(&B.ids, d.n_layers * NB * topk * 4) || cudaMalloc(&B.counter, NB * 4) ||
         cudaMalloc(&B.tok, NB * 4) || cudaMalloc(&B.pos, NB * 4) || cudaMalloc(&B.out, NB * 4) ||
-        cudaMalloc(&B.codes, NB * 4) || cudaMalloc(&B.seg, d.n_layers * 2 * tab * 8) ||
-        cudaMalloc(&B.cache, NB * sizeof(float *))) {
+        cudaMalloc(&B.codes, NB * 4) ||
+        cudaMalloc(&B.cache, NB * sizeof(float *)) || cudaMalloc(&B.img, ds2_dm_img_bytes(d)) ||
+        cudaMalloc(&B.dpart, ds2_dm_part_floats(d, any_dense) * 4) || cudaMalloc(&B.dn_vec, kMoeMaxSegs * 4) ||
+        cudaMalloc(&B.x_rows_gu, kMoeMaxSegs * 32 * 4) || cudaMalloc(&B.x_rows_dn, kMoeMaxSegs * 32 * 4) ||
+        cudaMalloc(&B.out_gu, kMoeMaxSegs * 32 * sizeof(float *)) ||
+        cudaMalloc(&B.out_dn, kMoeMaxSegs * 32 * sizeof(float *)) || cudaMalloc(&B.tab_gu, kMoeMaxSegs * 8) ||
+        cudaMalloc(&B.tab_dn, kMoeMaxSegs * 8)) {
       ds2_free_batch(m);
       return zgpu_fail(ctx, ZGPU_ERR_OUT_OF_MEMORY, "batch activation buffers");
     }
+    if (!ds2_build_tiles(m)) {
+      ds2_free_batch(m);
+      return zgpu_fail(ctx, ZGPU_ERR_OUT_OF_MEMORY, "batch weight tiles");
+    }
     cudaMemset(B.counter, 0, NB * 4);
-    cudaMemset(B.seg, 0, d.n_layers * 2 * tab * 8);
     cudaMemset(B.ids, 0, d.n_layers * NB * topk * 4);
     cudaMemset(B.wts, 0, d.n_layers * NB * topk * 4);
   }

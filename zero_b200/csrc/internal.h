@@ -28,6 +28,8 @@ struct DeviceTensor {
   // batched-matmul operand tiles (ops.h), built on first batched use (Q4_0)
   int8_t *w8 = nullptr;
   float *ws8 = nullptr;
+  // tiles of the digit-image matvec (digit_mma.h), built on first use
+  uint8_t *dmt = nullptr;
 };
 
 // Geometry of one GEMV launch over a device tensor in the layout.h format.

@@ -97,30 +97,6 @@ namespace {
 
 
 
-// Packed f32x2 add / multiply, each lane rounded to nearest.  The explicit
-// .rn keeps every one a separate rounding (PTX never contracts an add or mul
-// that carries a rounding modifier into an fma), so two columns at a time
-// follow the scalar order exactly: the exact magic-number subtract, then
-// (x * d_w) * d_x.  The accumulation itself stays scalar: a packed add did
-// not reproduce the scalar sums bit for bit.
-__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
-  uint64_t r;
-  asm("{\n\t.reg .b64 pa, pb;\n\tmov.b64 pa, {%1, %2};\n\tmov.b64 pb, {%3, %4};\n\t"
-      "add.rn.f32x2 %0, pa, pb;\n\t}"
-      : "=l"(r)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return make_float2(__uint_as_float(static_cast<uint32_t>(r)), __uint_as_float(static_cast<uint32_t>(r >> 32)));
-}
-__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
-  uint64_t r;
-  asm("{\n\t.reg .b64 pa, pb;\n\tmov.b64 pa, {%1, %2};\n\tmov.b64 pb, {%3, %4};\n\t"
-      "mul.rn.f32x2 %0, pa, pb;\n\t}"
-      : "=l"(r)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return make_float2(__uint_as_float(static_cast<uint32_t>(r)), __uint_as_float(static_cast<uint32_t>(r >> 32)));
-}
-
-
 template <uint32_t NT>
 __global__ void __launch_bounds__(MmaCfg<NT>::kThreads, MmaCfg<NT>::kCtasPerSm) q4q8_mma_kernel(const MmaGemmParams p) {
   using Cfg = MmaCfg<NT>;

@@ -331,6 +331,43 @@ size_t route_smem_bytes(uint32_t dim) {
   return (dim + e * (dim + kRouteRowPad)) * sizeof(float);
 }
 
+__global__ void __launch_bounds__(256) moe_dispatch_kernel(const MoeDispatchParams p) {
+  __shared__ uint32_t cnt[kMoeMaxSegs];
+  pdl_launch_dependents();
+  pdl_wait();   // the router's selections
+  const uint32_t n_segs = p.n_local + p.n_shared, n_slot = p.n_shared + p.top_k;
+  for (uint32_t s = threadIdx.x; s < n_segs; s += blockDim.x) cnt[s] = s < p.n_local ? 0u : p.n_seq;
+  __syncthreads();
+  auto put = [&](uint32_t s, uint32_t j, uint32_t b, uint32_t slot) {
+    const uint32_t pr = b * n_slot + slot, i = s * 32 + j;
+    p.x_rows_gu[i] = b;
+    p.x_rows_dn[i] = pr;
+    p.out_gu[i] = p.act + static_cast<uint64_t>(pr) * p.act_row;
+    p.out_dn[i] = p.exp_out + static_cast<uint64_t>(pr) * p.dim;
+  };
+  for (uint32_t t = threadIdx.x; t < p.n_seq * p.top_k; t += blockDim.x) {
+    const uint32_t b = t / p.top_k, k = t % p.top_k, e = __ldcg(p.ids + t);
+    uint32_t s = e;
+    if (p.ep_per_rank) {
+      if (e / p.ep_per_rank != p.ep_rank) continue;   // another rank's expert
+      s = e - p.ep_rank * p.ep_per_rank;
+    }
+    if (s >= p.n_local) continue;
+    put(s, atomicAdd(&cnt[s], 1u), b, p.n_shared + k);
+  }
+  for (uint32_t t = threadIdx.x; t < p.n_seq * p.n_shared; t += blockDim.x)
+    put(p.n_local + t % p.n_shared, t / p.n_shared, t / p.n_shared, t % p.n_shared);
+  __syncthreads();
+  for (uint32_t s = threadIdx.x; s < n_segs; s += blockDim.x) {
+    const uint32_t n = cnt[s];
+    p.n_vec[s] = n;
+    const bool sh = s >= p.n_local;
+    const uint64_t o = sh ? s - p.n_local : s;
+    p.tab_gu[s] = n ? reinterpret_cast<unsigned long long>((sh ? p.sh_tiles_gu : p.tiles_gu) + o * p.tiles_gu_stride) : 0ull;
+    p.tab_dn[s] = n ? reinterpret_cast<unsigned long long>((sh ? p.sh_tiles_dn : p.tiles_dn) + o * p.tiles_dn_stride) : 0ull;
+  }
+}
+
 cudaError_t moe_setup() {
   const size_t max_smem = route_smem_bytes(kMoeMaxDim);
   return cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -351,6 +388,16 @@ cudaError_t launch_moe_route(const RouteParams &rp, const LaunchCfg &lc) {
       make_launch_cfg(dim3(grid, ns), dim3(kRouteThreads), route_smem_bytes(p.dim), lc, attr);
   if (lc.launch_counter) ++*lc.launch_counter;
   return cudaLaunchKernelEx(&cfg, moe_route_kernel, p);
+}
+
+cudaError_t launch_moe_dispatch(const MoeDispatchParams &p, const LaunchCfg &lc) {
+  if (p.n_seq == 0 || p.n_seq > 32 || p.top_k == 0 || p.n_local + p.n_shared == 0 ||
+      p.n_local + p.n_shared > kMoeMaxSegs)
+    return cudaErrorInvalidValue;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = make_launch_cfg(dim3(1), dim3(256), 0, lc, attr);
+  if (lc.launch_counter) ++*lc.launch_counter;
+  return cudaLaunchKernelEx(&cfg, moe_dispatch_kernel, p);
 }
 
 cudaError_t launch_moe_combine(const CombineParams &p, const LaunchCfg &lc) {

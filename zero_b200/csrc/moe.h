@@ -89,8 +89,35 @@ constexpr uint32_t kEpMaxRanks = 8;
 ZGPU_HD size_t ep_slot_words(uint32_t slots, uint32_t dim) { return 2 * static_cast<size_t>(slots) * dim; }
 ZGPU_HD size_t ep_exchange_words(uint32_t slots, uint32_t dim) { return ep_slot_words(slots, dim) + kEpMaxRanks; }
 
+// Grouping of a batch's (token, expert) pairs by expert for the tensor-core
+// expert matvecs (digit_mma.h).  Segment s < n_local is this rank's routed
+// expert ep_rank * ep_per_rank + s (all experts without expert
+// parallelism), segment n_local + i the shared expert i.  Per segment:
+// n_vec[s] tokens (at most 32, each token selects an expert once); for its
+// j-th token b and that token's slot (shared experts first, then the k-th
+// selection) the pair row p = b * (n_shared + top_k) + slot:
+//   x_rows_gu[s * 32 + j] = b,           out_gu[s * 32 + j] = act + p * act_row
+//   x_rows_dn[s * 32 + j] = p,           out_dn[s * 32 + j] = exp_out + p * dim
+// and the tile tables tab_gu[s] / tab_dn[s] = the segment's weight tiles,
+// 0 when no token selected it.  Which column a token takes inside its
+// segment does not change any result.
+struct MoeDispatchParams {
+  const uint32_t *ids;               // [n_seq][top_k] this layer's selections
+  uint32_t n_seq, top_k, n_shared, n_local, ep_rank, ep_per_rank;   // ep_per_rank 0: no expert parallelism
+  float *act, *exp_out;
+  uint32_t act_row, dim;
+  const uint8_t *tiles_gu, *tiles_dn;          // routed experts' tiles, tiles_*_stride bytes apart
+  const uint8_t *sh_tiles_gu, *sh_tiles_dn;    // shared experts' tiles
+  uint64_t tiles_gu_stride, tiles_dn_stride;
+  uint32_t *n_vec, *x_rows_gu, *x_rows_dn;
+  float **out_gu, **out_dn;
+  unsigned long long *tab_gu, *tab_dn;
+};
+constexpr uint32_t kMoeMaxSegs = 256;
+
 cudaError_t moe_setup();
 cudaError_t launch_moe_route(const RouteParams &p, const LaunchCfg &lc);
+cudaError_t launch_moe_dispatch(const MoeDispatchParams &p, const LaunchCfg &lc);
 cudaError_t launch_moe_combine(const CombineParams &p, const LaunchCfg &lc);
 cudaError_t launch_moe_ep_publish(const EpPublishParams &p, const LaunchCfg &lc);
 // ++*ep_seq (one thread), after the layer's combine
