@@ -155,7 +155,7 @@ zgpu_status zgpu_linear_q8act(zgpu_ctx *ctx, const void *xq_blocks, const void *
 zgpu_status zgpu_linear_q8act_device(zgpu_ctx *ctx, const void *d_xq_blocks, const void *w_key,
                                      float *d_out, uint64_t in_dim, uint64_t out_dim, void *stream);
 
-/* linear_dispatch (ops.rs:486) of n_vec (1..32) f32 vectors x[n_vec][in_dim]
+/* linear_dispatch (ops.rs:486) of n_vec (1..256) f32 vectors x[n_vec][in_dim]
  * against one registered Q4_0 or Q8_0 weight on the tensor cores
  * (tcgen05 int8 MMA over the three 8-bit digits of the GEMV's activation
  * integers): out[v] equals zgpu_linear_dispatch(x[v]) bit for bit for every

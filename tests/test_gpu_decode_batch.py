@@ -2,27 +2,25 @@
 own cache at its own position, one step at a time.
 
 Per sequence, the step is forward_single_token + the LM head pick
-(forward_pass.rs:515-631, lm_head.rs:98-166).  The batch computes the
-projections and the LM head on the tcgen05 int8 path over Q8_0-quantised
-activation rows, so the reference for it is the oracle's per-token path with
-the same rounding (q8act mode 2: every matmul input, the LM head's included,
-quantised to Q8_0 first).  The prompt goes through zgpu_prefill, whose LM
-head is f32 (q8act mode 1).  Bars, as for the prefill: logits within 1e-2
-relative L2 of that path at every step (RMSNorm and attention reduce in
-another order; a last-bit difference flips the Q8_0 rounding of an element
-now and then), the KV cache within 2e-2, the same next token wherever the
-oracle's top-1/top-2 margin is clear; the oracle is fed the GPU's tokens so
-both stay on one sequence.
-
-The batch is also held, free-running, to the reference's own f32 per-token
-path (no activation quantisation, the oracle's AVX-512 order) at the north
-star's 1e-2 on logits with identical greedy tokens wherever the f32 margin is
-clear: two sequences at config-0 size and sixteen sequences at contexts past
-2048 tokens (run_f32_case).
-
-A batch is also bit-identical to the same sequences decoded one at a time:
-every matmul row, attention and argmax of a sequence is computed the same
-way whatever else is in the batch.
+(forward_pass.rs:515-631, lm_head.rs:98-166).  The batch runs every
+projection and the LM head on the tensor cores with the single-token GEMV's
+arithmetic (digit_mma.cu: int8 MMA over the three 8-bit digits of the
+GEMV's activation integers, the GEMV's block and chunk order), so its f32
+path is the reference's own, not a quantised one.  Bars:
+- against the same sequences decoded one at a time on the per-op
+  single-token path (zgpu_forward_single_token + zgpu_lm_head_argmax with
+  ZGPU_FLAG_NO_PERSISTENT): the projections are that path's GEMVs bit for
+  bit, the batched attention's exp (__expf) moves the last bits, so logits
+  agree to 2e-5; bit-identical to the same sequences batched alone;
+- against the oracle's f32 per-token path (the reference's AVX-512 order):
+  logits within 1e-2 relative L2 at every step (the prompt goes through
+  zgpu_prefill, whose Q8_0 activations leave the caches within 2e-2 of
+  the oracle's, and the oracle's prompt runs with the same rounding), the KV
+  cache within 2e-2, the same next token wherever the oracle's top-1/top-2
+  margin is clear;
+- free-running against the oracle's f32 path with no activation rounding
+  anywhere at config-0 size and sixteen sequences at contexts past 2048
+  tokens (run_f32_case).
 """
 import numpy as np
 import pytest
@@ -70,7 +68,7 @@ def run_case(cfg, lens, steps, seed=43):
             r.forward(int(t), i)
         rc, rtok, _ = r.lm_head()
         assert rc == 0
-        r.set_q8act(2)
+        r.set_q8act(0)   # the decode steps: f32 activations, as the batch
         refs.append(r)
     worst, kv_worst = 0.0, 0.0
     for s in range(steps):
@@ -102,7 +100,7 @@ def run_case(cfg, lens, steps, seed=43):
 
 
 @pytest.mark.parametrize("cfg,lens,steps", CASES, ids=[f"{c.name}-b{len(l)}" for c, l, _ in CASES])
-def test_decode_batch_matches_per_token_q8_path(cfg, lens, steps):
+def test_decode_batch_matches_per_token_path(cfg, lens, steps):
     run_case(cfg, lens, steps)
 
 
@@ -119,10 +117,10 @@ def run_f32_case(cfg, lens, steps, seed, wkw):
     (forward_single_token + lm_head_argmax, its prompt, then its own greedy
     tokens).  Per sequence and step: logits within the north-star 1e-2
     relative L2, and the same token.  A token may differ only where the
-    oracle's top-1/top-2 margin is inside the logits error (the batch path
-    quantises its matmul inputs to Q8_0); the sequences then part and that
-    sequence's later steps are not compared.  At least 90% of the steps must
-    be compared."""
+    oracle's top-1/top-2 margin is inside the logits error (the prompt's
+    prefill quantises its matmul inputs to Q8_0); the sequences then part and
+    that sequence's later steps are not compared.  At least 90% of the steps
+    must be compared."""
     import os
     from concurrent.futures import ThreadPoolExecutor
 
@@ -226,6 +224,53 @@ def test_batch_equals_sequences_alone():
             ka, va = a[i].read(layer, n + 4)
             kb, vb = b[i].read(layer, n + 4)
             assert np.array_equal(ka, kb) and np.array_equal(va, vb)
+    for kv in a + b:
+        kv.close()
+    m.close()
+    ctx.close()
+
+
+@pytest.mark.parametrize("cfg", [synth.small_config(n_layers=2, hidden=512, ffn=1024, n_q=8, n_kv=2, vocab=1024),
+                                 synth.small_config(n_layers=2, hidden=4096, ffn=12288, n_q=32, n_kv=8, vocab=2048)],
+                         ids=["small", "config2-widths"])
+def test_batch_equals_single_token_path(cfg):
+    """Each sequence of a batch step against the per-op single-token step
+    (forward_single_token + lm_head_argmax, ZGPU_FLAG_NO_PERSISTENT): the
+    projections are the single-token GEMV's bit for bit; the batched
+    attention reduces the q heads' scores together and takes exp by __expf,
+    which moves the last bits, so logits agree to 2e-5 relative L2 and the
+    tokens wherever the top-1/top-2 margin is clear."""
+    ctx = zb.Context(persistent=False)
+    w = synth.qwen3_weights(cfg, seed=6, norm_sigma=0.1)
+    m = zb.Qwen3Model(ctx, cfg, w)
+    lens = [3, 40, 17, 1, 9]
+    prompts = [synth.prompt_ids(cfg, n, seed=80 + i) for i, n in enumerate(lens)]
+    a = [m.new_kv(64) for _ in lens]
+    b = [m.new_kv(64) for _ in lens]
+    ta = np.zeros(len(lens), np.uint32)
+    for i, p in enumerate(prompts):   # identical prompt caches through the single-token path
+        for kvs in (a, b):
+            for pos, t in enumerate(p[:-1]):
+                m.forward_single_token(kvs[i], int(t), pos)
+        ta[i] = p[-1]
+    tb = ta.copy()
+    for s in range(4):
+        pos = np.array([n - 1 + s for n in lens], np.uint32)
+        na, la = m.decode_batch(a, ta, pos)
+        for i in range(len(lens)):
+            m.forward_single_token(b[i], int(tb[i]), int(pos[i]))
+            nb, lb = m.lm_head_argmax()
+            err = rel_l2(la[i], lb)
+            assert err < 2e-5, (s, i, err)
+            if top2_gap(lb) > 20 * err * float(np.abs(lb).max()):
+                assert nb == na[i], (s, i)
+            tb[i] = na[i]   # both continue on the batch's token
+        ta = na
+    for i, n in enumerate(lens):
+        for layer in range(cfg.n_layers):
+            ka, va = a[i].read(layer, n + 3)
+            kb, vb = b[i].read(layer, n + 3)
+            assert rel_l2(ka, kb) < 2e-5 and rel_l2(va, vb) < 2e-5
     for kv in a + b:
         kv.close()
     m.close()

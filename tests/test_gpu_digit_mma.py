@@ -55,6 +55,19 @@ def test_batch_equals_single_gemv(ctx, quant, out_dim, in_dim):
         assert same.all(), (n_vec, np.argwhere(~same)[:5], y[~same][:5], single[:n_vec][~same][:5])
 
 
+def test_batch_many_vector_groups(ctx):
+    """100 and 256 vectors (7 and 16 vector groups of one launch)."""
+    out_dim, in_dim = 1024, 4096
+    w = synth.q4_0(25, 3, out_dim, in_dim, 0.02)
+    key = ctx.register(w, zb.Q4_0, out_dim, in_dim)
+    x = inputs(256, in_dim, 9)
+    for n_vec in (100, 256):
+        y = ctx.linear_dispatch_batch(x[:n_vec], key, in_dim, out_dim, zb.Q4_0)
+        for v in (0, 5, 16, 47, n_vec - 1):
+            assert np.array_equal(y[v].view(np.uint32),
+                                  ctx.linear_dispatch(x[v], key, in_dim, out_dim, zb.Q4_0).view(np.uint32)), (n_vec, v)
+
+
 def test_batch_lm_head_shape(ctx):
     """The ds2 LM head shape (Q8_0, 102400 x 2048) with 32 vectors."""
     out_dim, in_dim = 102400, 2048
@@ -70,7 +83,7 @@ def test_batch_rejects_bad_args(ctx):
     w = synth.q4_0(24, 1, 64, 64, 0.02)
     key = ctx.register(w, zb.Q4_0, 64, 64)
     with pytest.raises(zb.ZgpuError) as ei:
-        ctx.linear_dispatch_batch(np.zeros((33, 64), np.float32), key, 64, 64, zb.Q4_0)
+        ctx.linear_dispatch_batch(np.zeros((257, 64), np.float32), key, 64, 64, zb.Q4_0)
     assert ei.value.name == "INVALID_ARG"
     with pytest.raises(zb.ZgpuError) as ei:
         ctx.linear_dispatch_batch(np.zeros((2, 64), np.float32), key, 64, 64, zb.Q4_K)

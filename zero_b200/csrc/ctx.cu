@@ -567,7 +567,8 @@ zgpu_status zgpu_linear_q8act_batch_device(zgpu_ctx *ctx, const float *d_x, cons
 zgpu_status zgpu_linear_dispatch_batch(zgpu_ctx *ctx, const float *x, const void *w_key, float *out,
                                        uint64_t n_vec, uint64_t in_dim, uint64_t out_dim, uint32_t quant) {
   if (!ctx || !x || !out || n_vec == 0 || in_dim == 0 || in_dim % 32) return ZGPU_ERR_INVALID_ARG;
-  if (n_vec > zgpu::kDmMaxVec) return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "linear_dispatch_batch: at most 32 vectors");
+  if (n_vec > zgpu::kDmMaxVecPlain)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "linear_dispatch_batch: at most 256 vectors");
   if (quant != ZGPU_Q4_0 && quant != ZGPU_Q8_0)
     return zgpu_fail(ctx, ZGPU_ERR_UNSUPPORTED_QUANT, "linear_dispatch_batch: Q4_0 or Q8_0 weights");
   DeviceTensor *t = const_cast<DeviceTensor *>(zgpu_lookup(ctx, w_key));

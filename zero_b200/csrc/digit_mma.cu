@@ -489,7 +489,8 @@ cudaError_t launch_build_dm_tiles(const uint8_t *w, uint64_t gstride, uint32_t q
 }
 
 cudaError_t launch_digit_image(const DigitImageParams &p, const LaunchCfg &lc) {
-  if (p.in_dim == 0 || p.in_dim % 32 || p.n_vec == 0 || p.n_vec > kDmMaxVec || p.n_img == 0 || !p.img)
+  if (p.in_dim == 0 || p.in_dim % 32 || p.n_vec == 0 || p.n_img == 0 || !p.img ||
+      p.n_vec > (p.x_rows || p.n_vec_of ? kDmMaxVec : kDmMaxVecPlain))
     return cudaErrorInvalidValue;
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = make_launch_cfg(dim3(dm_groups(p.n_vec) * kDmVec, p.n_img), dim3(256), 0, lc, attr);
@@ -498,8 +499,9 @@ cudaError_t launch_digit_image(const DigitImageParams &p, const LaunchCfg &lc) {
 }
 
 cudaError_t launch_dm_gemm(const DmGemmParams &p, const LaunchCfg &lc) {
-  if (p.in_dim == 0 || p.in_dim % 32 || p.rows == 0 || p.n_vec == 0 || p.n_vec > kDmMaxVec || p.n_seg == 0 ||
-      !p.part || !p.img || (p.w_tab && p.w_tab_mod == 0) || (!p.w_tab && !p.wt))
+  if (p.in_dim == 0 || p.in_dim % 32 || p.rows == 0 || p.n_vec == 0 || p.n_seg == 0 ||
+      p.n_vec > (p.n_vec_of ? kDmMaxVec : kDmMaxVecPlain) || !p.part || !p.img || (p.w_tab && p.w_tab_mod == 0) ||
+      (!p.w_tab && !p.wt))
     return cudaErrorInvalidValue;
   const uint64_t units = static_cast<uint64_t>(p.n_seg) * ((p.rows + 127) / 128) *
                          ((p.in_dim / 32 + kChunkBlocks - 1) / kChunkBlocks) * dm_groups(p.n_vec);
@@ -525,7 +527,8 @@ cudaError_t launch_dm_gemm(const DmGemmParams &p, const LaunchCfg &lc) {
 }
 
 cudaError_t launch_dm_combine(const DmCombineParams &p, const LaunchCfg &lc) {
-  if (p.rows == 0 || p.ks == 0 || p.n_vec == 0 || p.n_vec > kDmMaxVec || p.n_seg == 0 ||
+  if (p.rows == 0 || p.ks == 0 || p.n_vec == 0 || p.n_vec > (p.out_rows || p.n_vec_of ? kDmMaxVec : kDmMaxVecPlain) ||
+      p.n_seg == 0 ||
       (p.epi != EPI_STORE && p.epi != EPI_RESADD && p.epi != EPI_SWIGLU) ||
       (p.epi == EPI_SWIGLU && p.rows % 8) || (!p.out && !p.out_rows))
     return cudaErrorInvalidValue;

@@ -13,7 +13,8 @@ namespace zgpu {
 constexpr uint32_t kDmVec = 16;                              // vectors per MMA (a vector group)
 constexpr uint32_t kDmN = 3 * kDmVec;                        // MMA columns: 3 digits x 16 vectors
 constexpr uint32_t kDmImgBlock = kDmN * 32 + kDmVec * 4;     // image bytes per (vector group, block)
-constexpr uint32_t kDmMaxVec = 32;
+constexpr uint32_t kDmMaxVec = 32;        // vectors of one segment of a grouped (tabled) launch
+constexpr uint32_t kDmMaxVecPlain = 256;  // vectors of a launch without vector tables
 
 // Digit image of up to 32 vectors of in_dim floats: for each vector group g
 // (16 vectors) and 32-element block b, at img + (g * bpr + b) * kDmImgBlock,

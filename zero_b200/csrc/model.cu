@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "digit_mma.h"
 #include "internal.h"
 #include "layout.h"
 #include "ops.h"
@@ -82,11 +83,12 @@ struct zgpu_model {
   // per layer QKV, O, gate/up, down
   std::vector<int8_t *> pf_w8;
   std::vector<float *> pf_ws8;
-  // batched decode (zgpu_decode_batch): the LM head's operand tiles, and a
-  // block holding the sequence table, attention partials and arrival
-  // counters, logits, tokens and per-row codes
-  int8_t *lm_w8 = nullptr;
-  float *lm_ws8 = nullptr;
+  // batched decode (zgpu_decode_batch): a block holding the sequence table,
+  // attention partials and arrival counters, logits, tokens, per-row codes,
+  // the digit images and the matvec partials
+  // the tensor-core matvec's weight tiles (digit_mma.h), built on the first
+  // batched decode: per layer QKV, O, gate/up, down, then the LM head
+  std::vector<uint8_t *> dm_tiles;
   uint8_t *d_bd = nullptr;
   size_t bd_cap = 0;
   // tensor parallelism (world > 1): this rank's slice of every stage
@@ -660,7 +662,7 @@ void zgpu_qwen3_destroy(zgpu_model *m) {
     if (e) cudaEventDestroy(e);
   for (auto &e : m->pf_ev) cudaEventDestroy(e);
   for (int8_t *p : m->pf_w8) cudaFree(p);
-  cudaFree(m->lm_w8);
+  for (uint8_t *p : m->dm_tiles) cudaFree(p);
   cudaFree(m->d_bd);
   for (DeviceTensor *t : m->owned) {
     cudaFree(t->d);
@@ -1429,6 +1431,41 @@ zgpu_status prefill_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, cons
 // and the LM head run on the tensor cores over Q8_0-quantised activation rows
 // (the prefill arithmetic, with the LM head's Q8_0 weights as int8 tiles);
 // the attention is the decode kernel with a sequence grid dimension.
+// The tensor-core matvec's weight tiles of every projection and the LM
+// head, built once per model by the first batched decode.
+zgpu_status ensure_dm_tiles(zgpu_model *m) {
+  if (!m->dm_tiles.empty()) return ZGPU_OK;
+  const zgpu_qwen3_desc &d = m->desc;
+  const uint32_t H = d.hidden, F = d.ffn, QD = m->q_dim, QKV = QD + 2 * m->kv_dim;
+  struct Mat {
+    const uint8_t *w;
+    uint64_t gstride;
+    uint32_t quant, rows, in_dim;
+  };
+  std::vector<Mat> mats;
+  for (uint32_t l = 0; l < d.n_layers; ++l) {
+    mats.push_back({m->qkv[l], m->gs_h, ZGPU_Q4_0, QKV, H});
+    mats.push_back({m->o[l]->d, m->o[l]->gstride, ZGPU_Q4_0, H, QD});
+    mats.push_back({m->gateup[l], m->gs_h, ZGPU_Q4_0, 2 * F, H});
+    mats.push_back({m->down[l]->d, m->down[l]->gstride, ZGPU_Q4_0, H, F});
+  }
+  mats.push_back({m->out->d, m->out->gstride, m->out->quant, d.vocab_padded, H});
+  for (const Mat &mt : mats) {
+    uint8_t *t = nullptr;
+    cudaError_t e = cudaMalloc(&t, dm_tile_bytes(mt.rows, mt.in_dim / 32));
+    if (e == cudaSuccess) {
+      m->dm_tiles.push_back(t);
+      e = launch_build_dm_tiles(mt.w, mt.gstride, mt.quant, mt.rows, mt.in_dim / 32, t, m->ctx->stream);
+    }
+    if (e != cudaSuccess) {
+      for (uint8_t *p : m->dm_tiles) cudaFree(p);
+      m->dm_tiles.clear();
+      return zgpu_cuda_fail(m->ctx, e, "batched decode weight tiles");
+    }
+  }
+  return ZGPU_OK;
+}
+
 zgpu_status decode_batch_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq, const uint32_t *tokens,
                              const uint32_t *positions, uint32_t *tokens_out, float *logits_out) {
   if (!m || !kvs || !tokens || !positions || !tokens_out || n_seq == 0) return ZGPU_ERR_INVALID_ARG;
@@ -1440,9 +1477,8 @@ zgpu_status decode_batch_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq,
   const zgpu_qwen3_desc &d = m->desc;
   const uint32_t H = d.hidden, F = d.ffn, QD = m->q_dim, KVD = m->kv_dim, QKV = QD + 2 * KVD;
   const uint32_t V = d.vocab_padded, hd = d.head_dim;
-  if (H % 128 || QKV % 128 || (2 * F) % 128 || QD % 32 || F % 32 || V % 128)
-    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG,
-                     "decode batch: projection and vocabulary rows must be multiples of 128");
+  if (H % 32 || QD % 32 || F % 32 || F % 4)
+    return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "decode batch: hidden, q and ffn widths must be multiples of 32");
   if (hd != 128)   // the decode attention kernel's head size
     return zgpu_fail(ctx, ZGPU_ERR_INVALID_ARG, "decode batch: head_dim must be 128");
   uint32_t splits = 0;
@@ -1463,27 +1499,15 @@ zgpu_status decode_batch_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq,
     splits = std::max(splits, attention_max_splits(kv->max_tokens));
   }
   zgpu_status st;
-  if ((st = ensure_pf_tiles(m))) return st;
+  if ((st = ensure_dm_tiles(m))) return st;
   cudaStream_t s = ctx->stream;
   cudaError_t e = cudaSuccess;
-  if (!m->lm_w8) {
-    e = cudaMalloc(&m->lm_w8, mma_tile_bytes(V, H / 32));
-    m->lm_ws8 = reinterpret_cast<float *>(m->lm_w8);   // the scales sit beside each 4 KB tile
-    if (e == cudaSuccess)
-      e = launch_build_w8_tiles(m->out->d, m->out->gstride, V, H / 32, m->out->quant, m->lm_w8, m->lm_ws8, s);
-    if (e != cudaSuccess) {
-      cudaFree(m->lm_w8);
-      m->lm_w8 = nullptr;
-      m->lm_ws8 = nullptr;
-      return zgpu_cuda_fail(ctx, e, "LM head tiles");
-    }
-  }
-  // projection scratch (the prefill layout, n_seq rows)
+  // scratch (n_seq rows each): tokens | residual | q|k|v | attention output |
+  // SwiGLU output
   const size_t N = n_seq, maxk = std::max(std::max(H, QD), F);
   auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
   const size_t o_tok = 0, o_hid = al(N * 4), o_qkv = o_hid + al(N * H * 4), o_at = o_qkv + al(N * QKV * 4),
-               o_gu = o_at + al(N * QD * 4), o_q8 = o_gu + al(N * 2 * F * 4),
-               o_d8 = o_q8, total = o_q8 + al(mma_tile_bytes(N, maxk / 32));   // scales inside the tiles
+               o_gu = o_at + al(N * QD * 4), total = o_gu + al(N * F * 4);
   if (total > m->pf_cap) {
     cudaFree(m->d_pf);
     m->d_pf = nullptr;
@@ -1491,18 +1515,19 @@ zgpu_status decode_batch_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq,
     if ((e = cudaMalloc(&m->d_pf, total)) != cudaSuccess) return zgpu_cuda_fail(ctx, e, "decode batch scratch");
     m->pf_cap = total;
   }
-  // GEMM K-split partials: the largest split x rows of the step's matmuls
-  size_t split_rows = 0;
+  // the matvec partials: the largest chunks x rows of the step's products
+  auto ks_of = [](uint32_t in_dim) { return static_cast<size_t>((in_dim / 32 + kChunkBlocks - 1) / kChunkBlocks); };
+  size_t part_f = 0;
   {
     const uint32_t shapes[5][2] = {{QKV, H}, {H, QD}, {2 * F, H}, {H, F}, {V, H}};
-    for (const auto &sh : shapes)
-      split_rows = std::max(split_rows, static_cast<size_t>(mma_ksplit(sh[0], sh[1] / 32)) * sh[0]);
+    for (const auto &sh : shapes) part_f = std::max(part_f, ks_of(sh[1]) * sh[0]);
   }
-  // batch block: seq table | partials | counters | logits | tokens | codes | GEMM partials
+  // batch block: seq table | partials | counters | logits | tokens | codes | digit image | matvec partials
   const size_t b_seq = 0, b_part = al(N * sizeof(AttnBatchSeq)),
                b_cnt = b_part + al(N * d.n_q_heads * splits * (hd + 2) * 4),
                b_log = b_cnt + al(N * d.n_kv_heads * 4), b_tok = b_log + al(N * V * 4), b_code = b_tok + al(N * 4),
-               b_gpart = b_code + al(N * 4), b_total = b_gpart + al(split_rows * N * 4);
+               b_img = b_code + al(N * 4), b_dpart = b_img + al(dm_img_bytes(maxk, n_seq)),
+               b_total = b_dpart + al(part_f * N * 4);
   if (b_total > m->bd_cap) {
     cudaFree(m->d_bd);
     m->d_bd = nullptr;
@@ -1517,16 +1542,16 @@ zgpu_status decode_batch_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq,
   uint8_t *B = m->d_pf, *BB = m->d_bd;
   uint32_t *d_tok = reinterpret_cast<uint32_t *>(B + o_tok);
   float *hid = reinterpret_cast<float *>(B + o_hid), *qkv = reinterpret_cast<float *>(B + o_qkv),
-        *at = reinterpret_cast<float *>(B + o_at), *gu = reinterpret_cast<float *>(B + o_gu);
-  int8_t *q8 = reinterpret_cast<int8_t *>(B + o_q8);
-  float *d8 = reinterpret_cast<float *>(B + o_d8);
+        *at = reinterpret_cast<float *>(B + o_at), *act = reinterpret_cast<float *>(B + o_gu);
   AttnBatchSeq *d_seqs = reinterpret_cast<AttnBatchSeq *>(BB + b_seq);
   float *logits = reinterpret_cast<float *>(BB + b_log);
   uint32_t *d_out_tok = reinterpret_cast<uint32_t *>(BB + b_tok),
            *d_codes = reinterpret_cast<uint32_t *>(BB + b_code);
+  uint8_t *img = BB + b_img;
+  float *dpart = reinterpret_cast<float *>(BB + b_dpart);
   const uint32_t T = n_seq;
   uint32_t launches = 0;
-  // an event pair around every GEMM and attention launch: per-class device time
+  // an event pair around every projection and attention launch: per-class device time
   const size_t n_ev = static_cast<size_t>(d.n_layers) * 10 + 2;
   while (m->pf_ev.size() < n_ev) {
     cudaEvent_t ev;
@@ -1536,27 +1561,52 @@ zgpu_status decode_batch_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq,
   size_t ev_i = 0;
   std::vector<uint8_t> ev_attn;   // per event pair: 1 for an attention launch
   auto mark = [&]() { cudaEventRecord(m->pf_ev[ev_i++], s); };
-  auto gemm = [&](const int8_t *wt, const float *ws, uint32_t rows, uint32_t in_dim, float *y, bool resadd) {
-    MmaGemmParams p = {};
-    p.wt = wt;
-    p.ws = ws;
-    p.rows = rows;
-    p.bpr = in_dim / 32;
-    p.T = T;
-    p.ldy = rows;
-    p.xt = q8;
-    p.xs = d8;
-    p.y = y;
-    p.status = m->d_status;
-    p.resadd = resadd ? 1u : 0u;
-    p.ksplit = mma_ksplit(rows, in_dim / 32);
-    p.part = reinterpret_cast<float *>(BB + b_gpart);
-    launches += p.ksplit > 1 ? 2 : 1;
+  LaunchCfg lc;
+  lc.stream = s;
+  lc.pdl = !(ctx->flags & ZGPU_FLAG_NO_PDL);
+  lc.sm_count = ctx->sm_count;
+  lc.launch_counter = &launches;
+  // One projection of every sequence on the tensor cores (digit_mma.h):
+  // digit image (RMSNorm first when norm_w), MMA partials, the GEMV's
+  // epilogue.  Each sequence's row equals the one-token GEMV's bit for bit.
+  auto proj = [&](const float *x, uint32_t in_dim, const float *norm_w, const uint8_t *tiles, uint32_t rows, float *y,
+                  uint32_t ldy, GemvEpi epi) -> cudaError_t {
     mark();
     ev_attn.push_back(0);
-    const cudaError_t ge = launch_q4q8_mma(p, s);
+    DigitImageParams ip = {};
+    ip.x = x;
+    ip.x_stride = in_dim;
+    ip.norm_w = norm_w;
+    ip.eps = d.rms_eps;
+    ip.in_dim = in_dim;
+    ip.n_vec = T;
+    ip.n_img = 1;
+    ip.img = img;
+    ip.status = m->d_status;
+    cudaError_t pe = launch_digit_image(ip, lc);
+    if (pe != cudaSuccess) return pe;
+    DmGemmParams gp = {};
+    gp.wt = tiles;
+    gp.rows = rows;
+    gp.in_dim = in_dim;
+    gp.img = img;
+    gp.n_vec = T;
+    gp.n_seg = 1;
+    gp.part = dpart;
+    gp.status = m->d_status;
+    if ((pe = launch_dm_gemm(gp, lc)) != cudaSuccess) return pe;
+    DmCombineParams cp = {};
+    cp.part = dpart;
+    cp.rows = rows;
+    cp.ks = static_cast<uint32_t>(ks_of(in_dim));
+    cp.n_vec = T;
+    cp.n_seg = 1;
+    cp.out = y;
+    cp.out_vec_stride = ldy;
+    cp.epi = epi;
+    pe = launch_dm_combine(cp, lc);
     mark();
-    return ge;
+    return pe;
   };
   e = cudaMemcpyAsync(d_tok, tokens, N * 4, cudaMemcpyHostToDevice, s);
   if (e == cudaSuccess)
@@ -1567,11 +1617,8 @@ zgpu_status decode_batch_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq,
                           T, hid, m->d_status, s);
     ++launches;
   }
-  LaunchCfg lc;
-  lc.stream = s;
-  lc.pdl = false;
-  lc.sm_count = ctx->sm_count;
-  lc.launch_counter = &launches;
+  LaunchCfg alc = lc;
+  alc.pdl = false;
   AttnParams ap = {};
   ap.qkv = qkv;
   ap.inv_freqs = m->d_inv_freqs;
@@ -1585,30 +1632,20 @@ zgpu_status decode_batch_run(zgpu_model *m, zgpu_kv *const *kvs, uint32_t n_seq,
   ap.eps = d.rms_eps;
   ap.scale = 1.0f / sqrtf(static_cast<float>(hd));
   for (uint32_t l = 0; l < d.n_layers && e == cudaSuccess; ++l) {
-    const int8_t *const *w8 = m->pf_w8.data() + 4 * l;
-    const float *const *ws8 = m->pf_ws8.data() + 4 * l;
-    if ((e = launch_rows_rmsnorm_quant(hid, norm_attn(m, l), d.rms_eps, T, H, q8, d8, m->d_status, s))) break;
-    if ((e = gemm(w8[0], ws8[0], QKV, H, qkv, false))) break;
+    uint8_t *const *tl = m->dm_tiles.data() + 4 * l;
+    if ((e = proj(hid, H, norm_attn(m, l), tl[0], QKV, qkv, QKV, EPI_STORE))) break;
     ap.q_norm = norm_q(m, l);
     ap.k_norm = norm_k(m, l);
     mark();
     ev_attn.push_back(1);
-    e = launch_attention_batch(ap, d_seqs, l, T, QKV, QD, lc);
+    e = launch_attention_batch(ap, d_seqs, l, T, QKV, QD, alc);
     mark();
     if (e) break;
-    if ((e = launch_quantize_q8_0_tiles(at, q8, d8, T, QD, m->d_status, s))) break;
-    if ((e = gemm(w8[1], ws8[1], H, QD, hid, true))) break;
-    if ((e = launch_rows_rmsnorm_quant(hid, norm_ffn(m, l), d.rms_eps, T, H, q8, d8, m->d_status, s))) break;
-    if ((e = gemm(w8[2], ws8[2], 2 * F, H, gu, false))) break;
-    if ((e = launch_swiglu_quant_tiles(gu, q8, d8, T, F, m->d_status, s))) break;
-    if ((e = gemm(w8[3], ws8[3], H, F, hid, true))) break;
-    launches += 4;   // two row norms, the attention output and SwiGLU quantisers
+    if ((e = proj(at, QD, nullptr, tl[1], H, hid, H, EPI_RESADD))) break;
+    if ((e = proj(hid, H, norm_ffn(m, l), tl[2], 2 * F, act, F, EPI_SWIGLU))) break;
+    if ((e = proj(act, F, nullptr, tl[3], H, hid, H, EPI_RESADD))) break;
   }
-  if (e == cudaSuccess) {
-    e = launch_rows_rmsnorm_quant(hid, norm_out(m), d.rms_eps, T, H, q8, d8, m->d_status, s);
-    ++launches;
-  }
-  if (e == cudaSuccess) e = gemm(m->lm_w8, m->lm_ws8, V, H, logits, false);
+  if (e == cudaSuccess) e = proj(hid, H, norm_out(m), m->dm_tiles.back(), V, logits, V, EPI_STORE);
   if (e == cudaSuccess) {
     e = launch_rows_argmax(logits, T, V, d.vocab_real, d_out_tok, d_codes, m->d_status, s);
     ++launches;
