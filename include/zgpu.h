@@ -551,9 +551,11 @@ zgpu_status zgpu_ds2_generate_greedy(zgpu_ds2_model *m, zgpu_mla_kv *kv, const u
 /* One decode step of n_seq (1..32) independent sequences, each with its own
  * MLA cache (all of one capacity, none twice) at its own position: for every
  * b, the result equals zgpu_ds2_forward_single_token(kvs[b], tokens[b],
- * positions[b]) followed by zgpu_ds2_lm_head_argmax(vocab_real) bit for bit
- * (tokens_out[b], logits row b of n_seq x vocab_padded when logits_out is
- * not NULL; the cache rows appended).  It replaces the serving loop that
+ * positions[b]) followed by zgpu_ds2_lm_head_argmax(vocab_real) (tokens_out[b],
+ * logits row b of n_seq x vocab_padded when logits_out is not NULL; the
+ * cache rows appended) -- bit for bit while both split the attention into
+ * 16-token pieces (a cache capacity below 2 * SMs * 16 / n_seq rows), to f32
+ * rounding beyond that, where the batch takes longer splits.  It replaces the serving loop that
  * calls forward_single_token_deepseek2 (forward_pass.rs:703-909) and
  * lm_head_argmax_dynamic (lm_head.rs:98-166) once per sequence: each
  * weight tile is fetched once per step for the whole batch.  With expert
