@@ -16,6 +16,15 @@ linear_dispatch); --act q8 runs the Q4_0 x Q8_0-activation GEMV.
 on the tcgen05 int8 path instead: T activation rows per launch (quantisation
 included), reported as int8 TOPS (2 * rows * in * T per launch) next to the
 weight and activation bytes.
+
+--vectors V runs the exact batched matvec (zgpu_linear_dispatch_batch: V f32
+rows per call, host buffers) on each shape, for profiling its kernels.
+
+--ds2-batch N decodes N sequences of the
+DeepSeek-V2-Lite-shaped model (--layers L of its 27) together with
+zgpu_ds2_decode_batch: every sequence's latent cache holds --context seeded
+rows (stored once, copied on the device), then --reps steps, each printed
+with its device time and the distinct experts of its MoE layers.
 """
 from __future__ import annotations
 
@@ -118,6 +127,49 @@ def run_batch(ctx, out_dim: int, in_dim: int, T: int, reps: int, torch):
             "bytes": out_dim * in_dim * 18 // 32 + T * in_dim * 4 + T * out_dim * 4}
 
 
+def run_vectors(ctx, out_dim: int, in_dim: int, V: int, reps: int):
+    w = synth.q4_0(100, out_dim + 7 * in_dim, out_dim, in_dim, 0.02)
+    key = ctx.register(w, zb.Q4_0, out_dim, in_dim)
+    x = np.random.default_rng(0).standard_normal((V, in_dim)).astype(np.float32)
+    for _ in range(reps):
+        ctx.linear_dispatch_batch(x, key, in_dim, out_dim, zb.Q4_0)
+    ctx.clear_weights()
+    return {"kernel": "dm_gemm (tcgen05 kind::i8 over activation digits)", "shape": f"{in_dim}->{out_dim}",
+            "vectors": V, "reps": reps}
+
+
+def run_ds2_batch(n_seq: int, context: int, layers: int, reps: int):
+    cfg = synth.DS2_V2_LITE
+    if layers != cfg.n_layers:
+        cfg = synth.Ds2Config(**{**cfg.__dict__, "n_layers": layers})
+    ctx = zb.Context()
+    m = zb.Ds2Model(ctx, cfg, synth.ds2_weights(cfg, seed=0))
+    max_tokens = context + reps + 4
+    first = m.new_kv(max_tokens)
+    rows = synth.f32(1, 2, context * (cfg.kv_lora_rank + cfg.rope_dim), 0.0, 0.5).reshape(context, -1)
+    for layer in range(cfg.n_layers):
+        for t in range(context):
+            first.store_compressed(layer, t, rows[t, :cfg.kv_lora_rank], rows[t, cfg.kv_lora_rank:])
+    kvs = [first] + [m.new_kv(max_tokens) for _ in range(n_seq - 1)]
+    for kv in kvs[1:]:
+        kv.copy_from(first, context)
+    tokens = synth.ds2_prompt_ids(cfg, n_seq, seed=1)
+    pos = np.full(n_seq, context, np.uint32)
+    for s in range(reps):
+        tokens, _ = m.decode_batch(kvs, tokens, pos, want_logits=False)
+        pos = pos + 1
+        ms = m.perf()["decode_ms"]
+        ids, _ = m.batch_expert_ids(n_seq)
+        distinct = float(np.mean([len(np.unique(ids[layer])) for layer in range(cfg.n_dense, cfg.n_layers)]))
+        print(json.dumps({"workload": "ds2 batch", "sequences": n_seq, "context": context, "layers": cfg.n_layers,
+                          "step": s, "ms": round(ms, 3), "tok_s": round(n_seq / (ms * 1e-3), 1),
+                          "distinct_experts": round(distinct, 1)}), flush=True)
+    for kv in kvs:
+        kv.close()
+    m.close()
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--shape", action="append", help="OUTxIN, repeatable (default: config 1 sweep)")
@@ -125,13 +177,22 @@ def main():
     ap.add_argument("--reps", type=int, default=10)
     ap.add_argument("--copies", type=int, default=None, help="weight copies (default: > 2x L2)")
     ap.add_argument("--tokens", type=int, default=0, help="time the batched tcgen05 matmul over T tokens")
+    ap.add_argument("--vectors", type=int, default=0, help="run the exact batched matvec on V rows")
+    ap.add_argument("--ds2-batch", type=int, default=0, help="decode N DeepSeek2 sequences together")
+    ap.add_argument("--context", type=int, default=2048, help="--ds2-batch: cached rows per sequence")
+    ap.add_argument("--layers", type=int, default=27, help="--ds2-batch: layers of the model")
     args = ap.parse_args()
+    if args.ds2_batch:
+        run_ds2_batch(args.ds2_batch, args.context, args.layers, args.reps)
+        return
     import torch
 
     ctx = zb.Context()
     for s in args.shape or CONFIG1_SHAPES:
         o, i = (int(v) for v in s.lower().split("x"))
-        if args.tokens:
+        if args.vectors:
+            print(json.dumps(run_vectors(ctx, o, i, args.vectors, args.reps)), flush=True)
+        elif args.tokens:
             print(json.dumps(run_batch(ctx, o, i, args.tokens, args.reps, torch)), flush=True)
         else:
             print(json.dumps(run_shape(ctx, o, i, args.act, args.reps, args.copies, torch)), flush=True)
