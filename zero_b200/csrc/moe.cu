@@ -247,11 +247,13 @@ __global__ void moe_combine_kernel(const CombineParams p0) {
   bool gave_up = false;   // after one expired wait the others are not waited for
   if (p.xslots) {
     // flow control: every rank has published this invocation (and so has
-    // finished its combine of the previous one)
+    // finished its combine of the previous one).  A rank may already have
+    // published the next invocation (its arrival word then reads ver + 1),
+    // so the test is "at least ver".
     const unsigned long long *arrive = p.xslots + ep_slot_words(p.slot_cap, p.dim);
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t r = 0; r < p.world && !gave_up; ++r) {
-      while (static_cast<uint32_t>(__ldcg(arrive + r) >> 32) != ver) {
+      while (static_cast<uint32_t>(__ldcg(arrive + r) >> 32) < ver) {
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
           atomicOr(p.status, ZDEV_ERR_TIMEOUT);
           gave_up = true;
