@@ -30,9 +30,9 @@
 //   warp 1      MMA issuer: one tcgen05.mma (M 128, N 48, K 32) into
 //               accumulator k % 8 once the epilogue has read block k - 8
 //               out of it, commit;
-//   warps 2-17  epilogue: TMEM lane quarter (warp % 4) x 4 of the 16
-//               vectors (q, q+4, q+8, q+12: few vectors still use every
-//               warp); the block terms folded into the chunk's tree.
+//   warps 2-9   epilogue: TMEM lane quarter (warp % 4) x 8 of the 16
+//               vectors (vq, vq + 2, ..., vq + 14: few vectors still use
+//               every warp); the block terms folded into the chunk's tree.
 // Every wait is bounded; an expired wait stops that role, which drains what
 // it has in flight, and raises ZDEV_ERR_TIMEOUT.
 #include <cuda_runtime.h>
@@ -56,7 +56,15 @@ constexpr uint32_t kDmSlots = 8;                         // shared-memory stages
 constexpr uint32_t kDmAccs = 8;                          // TMEM accumulators
 constexpr uint32_t kDmAccCols = 64;                      // TMEM columns per accumulator (48 used)
 constexpr uint32_t kDmTmem = kDmAccs * kDmAccCols;       // 512: the whole TMEM, one CTA per SM
-constexpr uint32_t kDmEpiWarps = 16;                     // 4 lane quarters x 4 vector quarters
+constexpr uint32_t kDmEpiWarps = 8;                      // 4 lane quarters x kDmVq vector sets
+constexpr uint32_t kDmVq = kDmEpiWarps / 4;              // epilogue warps per TMEM lane quarter
+constexpr uint32_t kDmVpw = kDmVec / kDmVq;              // vectors per epilogue thread
+constexpr uint32_t kDmPairs = kDmVpw / 2;                // of them, packed f32x2 pairs
+static_assert(kDmEpiWarps % 4 == 0 && kDmVec % (2 * kDmVq) == 0, "epilogue shape");
+// Column position of vector v of a group: epilogue warp vq of a lane quarter
+// reads positions kDmVpw * vq .. + kDmVpw - 1 = vectors vq, vq + kDmVq, ...,
+// so a group with few vectors still spreads them over every warp.
+__host__ __device__ __forceinline__ uint32_t dm_pos(uint32_t v) { return (v % kDmVq) * kDmVpw + v / kDmVq; }
 constexpr uint32_t kDmThreads = 32 * (2 + kDmEpiWarps);  // producer, MMA, epilogue
 constexpr uint32_t kDmSlotBytes = kDmTileBlock + kDmImgBlock;   // weight block, then image block
 constexpr uint32_t kDmSmem = kDmSlots * kDmSlotBytes;
@@ -94,10 +102,8 @@ __global__ void __launch_bounds__(256) digit_image_kernel(const DigitImageParams
   float inv = 1.0f;
   if (p.norm_w && live) inv = rms_inv<8>(x, p.in_dim, p.eps, red, tid, 1);
   const uint32_t bpr = p.in_dim / 32, nf4 = p.in_dim / 4, ng = (p.n_vec + kDmVec - 1) / kDmVec;
-  // vector vl of group g sits at column position pv: epilogue warp q of the
-  // 4 per lane quarter reads positions 4q..4q+3 = vectors q, q+4, q+8, q+12,
-  // so a group with few vectors still spreads them over every warp
-  const uint32_t g = v / kDmVec, vl = v % kDmVec, pv = (vl % 4) * 4 + vl / 4;
+  // vector vl of group g sits at column position pv (dm_pos)
+  const uint32_t g = v / kDmVec, vl = v % kDmVec, pv = dm_pos(vl);
   uint8_t *img = p.img + (static_cast<uint64_t>(im) * ng + g) * bpr * kDmImgBlock;
   // warp-uniform trip count: a block's 8 lanes are all in range or all out
   for (uint32_t f0 = warp * 32; f0 < nf4; f0 += 256) {
@@ -332,17 +338,18 @@ __global__ void __launch_bounds__(kDmThreads, 1) dm_gemm_kernel(const DmGemmPara
     }
   } else {
     // ---------------- epilogue ----------------
-    // thread: tile row rt (TMEM lane quarter warp % 4) x vectors vq, vq + 4,
-    // vq + 8, vq + 12 (column positions 4 vq .. 4 vq + 3)
+    // thread: tile row rt (TMEM lane quarter warp % 4) x vectors vq, vq + kDmVq,
+    // ... (column positions kDmVpw * vq .. + kDmVpw - 1, dm_pos)
     const uint32_t q = warp & 3, vq = (warp - 2) >> 2, rt = 32 * q + lane;
-    const uint32_t taddr = tmem + ((32u * q) << 16) + 4 * vq;
+    const uint32_t taddr = tmem + ((32u * q) << 16) + kDmVpw * vq;
     const float M = 12582912.0f;   // 1.5 * 2^23: int v, |v| < 2^22, is float(bits(M) + v) - M exactly
     uint32_t k = 0;
     bool ok = true;
-    // block terms of leaf i of the chunk for the thread's 4 vectors, as two
-    // packed pairs (0 for a missing block)
-    auto leaf = [&](const DmUnit &x, uint32_t i, float2 (&val)[2]) {
-      val[0] = val[1] = make_float2(0.0f, 0.0f);
+    // block terms of leaf i of the chunk for the thread's vectors, as packed
+    // pairs (0 for a missing block)
+    auto leaf = [&](const DmUnit &x, uint32_t i, float2 (&val)[kDmPairs]) {
+#pragma unroll
+      for (int h = 0; h < static_cast<int>(kDmPairs); ++h) val[h] = make_float2(0.0f, 0.0f);
       if (!ok || br5(i) >= x.nb) return;
       const uint32_t s = k % kDmSlots, a = k % kDmAccs;
       // the accumulator, and (acquired directly) the stage's scales and row sums
@@ -356,25 +363,34 @@ __global__ void __launch_bounds__(kDmThreads, 1) dm_gemm_kernel(const DmGemmPara
         return;
       }
       tc_fence_after();
-      uint32_t a0[4], a1[4], a2[4];
-      tmem_ld4(taddr + a * kDmAccCols, a0);
-      tmem_ld4(taddr + a * kDmAccCols + kDmVec, a1);
-      tmem_ld4(taddr + a * kDmAccCols + 2 * kDmVec, a2);
+      uint32_t a0[kDmVpw], a1[kDmVpw], a2[kDmVpw];
+      tmem_ld_cols(taddr + a * kDmAccCols, a0);
+      tmem_ld_cols(taddr + a * kDmAccCols + kDmVec, a1);
+      tmem_ld_cols(taddr + a * kDmAccCols + 2 * kDmVec, a2);
       const uint8_t *slot = sm + s * kDmSlotBytes;
       const float dw = reinterpret_cast<const float *>(slot + 4096)[rt];
       // s_d = a_d + 128 * row sum for the two low digits, folded into the magic constant
       const int kk = reinterpret_cast<const int *>(slot + 4096 + 512)[rt] * 128 + 0x4B400000;
-      const float4 bs = reinterpret_cast<const float4 *>(slot + kDmTileBlock + kDmN * 32)[vq];
+      float bsv[kDmVpw];
+      const float4 *bs4 = reinterpret_cast<const float4 *>(slot + kDmTileBlock + kDmN * 32) + vq * (kDmVpw / 4);
+#pragma unroll
+      for (int c = 0; c < static_cast<int>(kDmVpw / 4); ++c) {
+        const float4 b4 = bs4[c];
+        bsv[4 * c] = b4.x;
+        bsv[4 * c + 1] = b4.y;
+        bsv[4 * c + 2] = b4.z;
+        bsv[4 * c + 3] = b4.w;
+      }
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_addr(&eempty[s]));
       const float2 m2 = make_float2(M, M), c256 = make_float2(256.0f, 256.0f), c64k = make_float2(65536.0f, 65536.0f);
       const float2 dw2 = make_float2(dw, dw);
-      const float2 bsp[2] = {make_float2(bs.x, bs.y), make_float2(bs.z, bs.w)};
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        if (vq + 8 * h >= x.nv) break;   // pair h = vectors vq + 8h and vq + 8h + 4
+      for (int h = 0; h < static_cast<int>(kDmPairs); ++h) {
+        // pair h = vectors vq + kDmVq * 2h and vq + kDmVq * (2h + 1)
+        if (vq + kDmVq * 2 * h >= x.nv) break;
         // S0, S1, S2 exactly as floats (|S| < 2^22); X = S0 + 256 S1 rounded
         // once, as the GEMV's int-to-float of its s0 + (s1 << 8)
         const float2 f0 = sub2_rn(make_float2(__int_as_float(static_cast<int>(a0[2 * h]) + kk),
@@ -384,7 +400,7 @@ __global__ void __launch_bounds__(kDmThreads, 1) dm_gemm_kernel(const DmGemmPara
         const float2 f2 = sub2_rn(make_float2(__int_as_float(static_cast<int>(a2[2 * h]) + 0x4B400000),
                                               __int_as_float(static_cast<int>(a2[2 * h + 1]) + 0x4B400000)), m2);
         const float2 t = fma2_rn(f2, c64k, fma2_rn(f1, c256, f0));
-        val[h] = mul2_rn(mul2_rn(dw2, bsp[h]), t);
+        val[h] = mul2_rn(mul2_rn(dw2, make_float2(bsv[2 * h], bsv[2 * h + 1])), t);
       }
     };
     for (uint32_t u = blockIdx.x; u < g.n_units && ok; u += gridDim.x) {
@@ -392,48 +408,48 @@ __global__ void __launch_bounds__(kDmThreads, 1) dm_gemm_kernel(const DmGemmPara
       if (!dm_unit(p, g, u, x)) continue;
       // the chunk's 32 leaves in bit-reversed block order folded as the
       // GEMV's butterfly: 4-leaf subtrees, then a counter over 8 subtrees
-      float2 L2[2], L3[2], L4[2], res[2];
+      float2 L2[kDmPairs], L3[kDmPairs], L4[kDmPairs], res[kDmPairs];
       for (uint32_t o = 0; o < 8; ++o) {
-        float2 s01[2], v2[2], v3[2], xs[2];
+        float2 s01[kDmPairs], v2[kDmPairs], v3[kDmPairs], xs[kDmPairs];
         leaf(x, 4 * o, xs);
         leaf(x, 4 * o + 1, v2);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) s01[h] = add2_rn(xs[h], v2[h]);
+        for (int h = 0; h < static_cast<int>(kDmPairs); ++h) s01[h] = add2_rn(xs[h], v2[h]);
         leaf(x, 4 * o + 2, v2);
         leaf(x, 4 * o + 3, v3);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) xs[h] = add2_rn(s01[h], add2_rn(v2[h], v3[h]));
+        for (int h = 0; h < static_cast<int>(kDmPairs); ++h) xs[h] = add2_rn(s01[h], add2_rn(v2[h], v3[h]));
         if (o & 1) {
 #pragma unroll
-          for (int h = 0; h < 2; ++h) xs[h] = add2_rn(L2[h], xs[h]);
+          for (int h = 0; h < static_cast<int>(kDmPairs); ++h) xs[h] = add2_rn(L2[h], xs[h]);
           if (o & 2) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) xs[h] = add2_rn(L3[h], xs[h]);
+            for (int h = 0; h < static_cast<int>(kDmPairs); ++h) xs[h] = add2_rn(L3[h], xs[h]);
             if (o & 4) {
 #pragma unroll
-              for (int h = 0; h < 2; ++h) res[h] = add2_rn(L4[h], xs[h]);
+              for (int h = 0; h < static_cast<int>(kDmPairs); ++h) res[h] = add2_rn(L4[h], xs[h]);
             } else {
 #pragma unroll
-              for (int h = 0; h < 2; ++h) L4[h] = xs[h];
+              for (int h = 0; h < static_cast<int>(kDmPairs); ++h) L4[h] = xs[h];
             }
           } else {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) L3[h] = xs[h];
+            for (int h = 0; h < static_cast<int>(kDmPairs); ++h) L3[h] = xs[h];
           }
         } else {
 #pragma unroll
-          for (int h = 0; h < 2; ++h) L2[h] = xs[h];
+          for (int h = 0; h < static_cast<int>(kDmPairs); ++h) L2[h] = xs[h];
         }
       }
-      // this thread's vectors vq, vq + 4, vq + 8, vq + 12
-      const float resv[4] = {res[0].x, res[0].y, res[1].x, res[1].y};
       const uint32_t row = x.mt * 128 + rt;
       if (row < p.rows) {
         float *dst = p.part + (static_cast<uint64_t>(x.seg) * g.ks + x.c) * p.n_vec * p.rows + row;
 #pragma unroll
-        for (int v = 0; v < 4; ++v)
-          if (vq + 4 * v < x.nv)
-            dst[static_cast<uint64_t>(x.vg * kDmVec + vq + 4 * v) * p.rows] = ok ? resv[v] : __uint_as_float(0x7fc00000u);
+        for (int j = 0; j < static_cast<int>(kDmVpw); ++j) {
+          const uint32_t v = vq + kDmVq * j;   // this thread's j-th vector
+          const float r = (j & 1) ? res[j / 2].y : res[j / 2].x;
+          if (v < x.nv) dst[static_cast<uint64_t>(x.vg * kDmVec + v) * p.rows] = ok ? r : __uint_as_float(0x7fc00000u);
+        }
       }
     }
   }
