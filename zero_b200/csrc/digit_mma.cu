@@ -464,9 +464,16 @@ __global__ void __launch_bounds__(kDmThreads, 1) dm_gemm_kernel(const DmGemmPara
 __global__ void dm_combine_kernel(const DmCombineParams p) {
   pdl_launch_dependents();
   pdl_wait();
-  const uint32_t seg = blockIdx.z, v = blockIdx.y;
-  const uint32_t nvs = p.n_vec_of ? min(__ldcg(p.n_vec_of + seg), p.n_vec) : p.n_vec;
-  if (v >= nvs) return;
+  uint32_t seg = blockIdx.z, v = blockIdx.y;
+  if (p.pairs) {
+    if (blockIdx.y >= __ldcg(p.n_pairs)) return;
+    const uint32_t sv = __ldcg(p.pairs + blockIdx.y);
+    seg = sv >> 8;
+    v = sv & 0xFFu;
+  } else {
+    const uint32_t nvs = p.n_vec_of ? min(__ldcg(p.n_vec_of + seg), p.n_vec) : p.n_vec;
+    if (v >= nvs) return;
+  }
   const uint32_t j = blockIdx.x * blockDim.x + threadIdx.x;
   const uint32_t out_rows = p.epi == EPI_SWIGLU ? p.rows / 2 : p.rows;
   if (j >= out_rows) return;
@@ -548,9 +555,11 @@ cudaError_t launch_dm_combine(const DmCombineParams &p, const LaunchCfg &lc) {
       (p.epi != EPI_STORE && p.epi != EPI_RESADD && p.epi != EPI_SWIGLU) ||
       (p.epi == EPI_SWIGLU && p.rows % 8) || (!p.out && !p.out_rows))
     return cudaErrorInvalidValue;
+  if (p.pairs && (!p.n_pairs || p.max_pairs == 0 || p.max_pairs > 65535)) return cudaErrorInvalidValue;
   const uint32_t out_rows = p.epi == EPI_SWIGLU ? p.rows / 2 : p.rows;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = make_launch_cfg(dim3((out_rows + 255) / 256, p.n_vec, p.n_seg), dim3(256), 0, lc, attr);
+  const dim3 grid = p.pairs ? dim3((out_rows + 255) / 256, p.max_pairs, 1) : dim3((out_rows + 255) / 256, p.n_vec, p.n_seg);
+  cudaLaunchConfig_t cfg = make_launch_cfg(grid, dim3(256), 0, lc, attr);
   if (lc.launch_counter) ++*lc.launch_counter;
   return cudaLaunchKernelEx(&cfg, dm_combine_kernel, p);
 }

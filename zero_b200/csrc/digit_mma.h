@@ -91,6 +91,11 @@ struct DmCombineParams {
   uint64_t out_seg_stride, out_vec_stride;
   float *const *out_rows;
   uint32_t epi;
+  // optional: the launch covers only the (segment, vector) pairs pairs[i] =
+  // segment << 8 | vector for i < *n_pairs (at most max_pairs), instead of
+  // every segment x n_vec (a grouped launch whose segments hold few vectors)
+  const uint32_t *pairs, *n_pairs;
+  uint32_t max_pairs;
 };
 cudaError_t launch_dm_combine(const DmCombineParams &p, const LaunchCfg &lc);
 cudaError_t dm_setup();

@@ -150,7 +150,7 @@ struct zgpu_ds2_model {
     float **cache = nullptr;             // [kDs2MaxBatch] each sequence's zgpu_mla_kv rows
     uint8_t *t_out = nullptr;            // LM-head tiles
     // the expert grouping of the current MoE layer (moe.h MoeDispatchParams)
-    uint32_t *dn_vec = nullptr, *x_rows_gu = nullptr, *x_rows_dn = nullptr;
+    uint32_t *dn_vec = nullptr, *x_rows_gu = nullptr, *x_rows_dn = nullptr, *pairs = nullptr;
     float **out_gu = nullptr, **out_dn = nullptr;
     unsigned long long *tab_gu = nullptr, *tab_dn = nullptr;
     uint8_t *img = nullptr;              // digit images of the tensor-core projections
@@ -590,6 +590,10 @@ cudaError_t ds2_enqueue_batch(zgpu_ds2_model *m, uint32_t ns, uint32_t *counter)
     cp.n_vec_of = B.dn_vec;
     cp.out_rows = out_rows;
     cp.epi = epi;
+    // only the (expert, token) pairs in use: at most n_seq x (n_shared + top_k)
+    cp.pairs = B.pairs;
+    cp.n_pairs = B.dn_vec + kMoeMaxSegs;
+    cp.max_pairs = ns * (d.n_shared + d.top_k);
     return launch_dm_combine(cp, lc);
   };
   for (uint32_t l = 0; l < d.n_layers; ++l) {
@@ -711,6 +715,8 @@ cudaError_t ds2_enqueue_batch(zgpu_ds2_model *m, uint32_t ns, uint32_t *counter)
     dp.out_dn = B.out_dn;
     dp.tab_gu = B.tab_gu;
     dp.tab_dn = B.tab_dn;
+    dp.pairs = B.pairs;
+    dp.n_pairs = B.dn_vec + kMoeMaxSegs;
     if ((e = launch_moe_dispatch(dp, lc)) != cudaSuccess) return e;
     if ((e = dm_grouped(B.hidden, H, L.ffn_norm, B.x_rows_gu, B.tab_gu, n_segs, 2 * d.expert_ffn, H, B.out_gu,
                         EPI_SWIGLU)) != cudaSuccess)
@@ -962,6 +968,7 @@ void ds2_free_batch(zgpu_ds2_model *m) {
   cudaFree(B.dpart);
   cudaFree(B.t_out);
   cudaFree(B.dn_vec);
+  cudaFree(B.pairs);
   cudaFree(B.x_rows_gu);
   cudaFree(B.x_rows_dn);
   cudaFree(B.out_gu);
@@ -1003,7 +1010,8 @@ zgpu_status ds2_prepare_batch(zgpu_ds2_model *m, uint32_t max_tokens) {
         cudaMalloc(&B.tok, NB * 4) || cudaMalloc(&B.pos, NB * 4) || cudaMalloc(&B.out, NB * 4) ||
         cudaMalloc(&B.codes, NB * 4) ||
         cudaMalloc(&B.cache, NB * sizeof(float *)) || cudaMalloc(&B.img, ds2_dm_img_bytes(d)) ||
-        cudaMalloc(&B.dpart, ds2_dm_part_floats(d, any_dense) * 4) || cudaMalloc(&B.dn_vec, kMoeMaxSegs * 4) ||
+        cudaMalloc(&B.dpart, ds2_dm_part_floats(d, any_dense) * 4) || cudaMalloc(&B.dn_vec, kMoeMaxSegs * 4 + 4) ||
+        cudaMalloc(&B.pairs, kMoeMaxSegs * 32 * 4) ||
         cudaMalloc(&B.x_rows_gu, kMoeMaxSegs * 32 * 4) || cudaMalloc(&B.x_rows_dn, kMoeMaxSegs * 32 * 4) ||
         cudaMalloc(&B.out_gu, kMoeMaxSegs * 32 * sizeof(float *)) ||
         cudaMalloc(&B.out_dn, kMoeMaxSegs * 32 * sizeof(float *)) || cudaMalloc(&B.tab_gu, kMoeMaxSegs * 8) ||

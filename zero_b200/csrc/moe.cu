@@ -360,6 +360,20 @@ __global__ void __launch_bounds__(256) moe_dispatch_kernel(const MoeDispatchPara
   for (uint32_t t = threadIdx.x; t < p.n_seq * p.n_shared; t += blockDim.x)
     put(p.n_local + t % p.n_shared, t / p.n_shared, t / p.n_shared, t % p.n_shared);
   __syncthreads();
+  // the pair list: segment s's pairs after those of segments < s (a serial
+  // prefix over at most kMoeMaxSegs counts, by thread 0)
+  __shared__ uint32_t base[kMoeMaxSegs];
+  if (threadIdx.x == 0) {
+    uint32_t acc = 0;
+    for (uint32_t s = 0; s < n_segs; ++s) {
+      base[s] = acc;
+      acc += cnt[s];
+    }
+    *p.n_pairs = acc;
+  }
+  __syncthreads();
+  for (uint32_t s = threadIdx.x; s < n_segs; s += blockDim.x)
+    for (uint32_t j = 0; j < cnt[s]; ++j) p.pairs[base[s] + j] = s << 8 | j;
   for (uint32_t s = threadIdx.x; s < n_segs; s += blockDim.x) {
     const uint32_t n = cnt[s];
     p.n_vec[s] = n;

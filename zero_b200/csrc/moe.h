@@ -112,6 +112,8 @@ struct MoeDispatchParams {
   uint32_t *n_vec, *x_rows_gu, *x_rows_dn;
   float **out_gu, **out_dn;
   unsigned long long *tab_gu, *tab_dn;
+  // every (segment, token slot) pair in use, segment << 8 | slot, and their count
+  uint32_t *pairs, *n_pairs;
 };
 constexpr uint32_t kMoeMaxSegs = 256;
 
