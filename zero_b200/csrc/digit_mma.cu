@@ -89,11 +89,20 @@ __global__ void __launch_bounds__(256) digit_image_kernel(const DigitImageParams
   __shared__ float red[8];
   pdl_launch_dependents();
   pdl_wait();
-  const uint32_t v = blockIdx.x, im = blockIdx.y;
+  uint32_t v = blockIdx.x, im = blockIdx.y;
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t nvi = p.n_vec_of ? min(__ldcg(p.n_vec_of + im), p.n_vec) : p.n_vec;
-  // a vector group no unit reads (all past the count) is not written
-  if (v >= (nvi + kDmVec - 1) / kDmVec * kDmVec) return;
+  uint32_t nvi;
+  if (p.pairs) {
+    if (blockIdx.x >= __ldcg(p.n_pairs)) return;
+    const uint32_t iv = __ldcg(p.pairs + blockIdx.x);
+    im = iv >> 8;
+    v = iv & 0xFFu;
+    nvi = v + 1;   // this vector is live
+  } else {
+    nvi = p.n_vec_of ? min(__ldcg(p.n_vec_of + im), p.n_vec) : p.n_vec;
+    // a vector group no unit reads (all past the count) is not written
+    if (v >= (nvi + kDmVec - 1) / kDmVec * kDmVec) return;
+  }
   const bool live = v < nvi;
   const float *x = p.x;
   if (live)
@@ -515,8 +524,10 @@ cudaError_t launch_digit_image(const DigitImageParams &p, const LaunchCfg &lc) {
   if (p.in_dim == 0 || p.in_dim % 32 || p.n_vec == 0 || p.n_img == 0 || !p.img ||
       p.n_vec > (p.x_rows || p.n_vec_of ? kDmMaxVec : kDmMaxVecPlain))
     return cudaErrorInvalidValue;
+  if (p.pairs && (!p.n_pairs || p.max_pairs == 0)) return cudaErrorInvalidValue;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = make_launch_cfg(dim3(dm_groups(p.n_vec) * kDmVec, p.n_img), dim3(256), 0, lc, attr);
+  const dim3 grid = p.pairs ? dim3(p.max_pairs) : dim3(dm_groups(p.n_vec) * kDmVec, p.n_img);
+  cudaLaunchConfig_t cfg = make_launch_cfg(grid, dim3(256), 0, lc, attr);
   if (lc.launch_counter) ++*lc.launch_counter;
   return cudaLaunchKernelEx(&cfg, digit_image_kernel, p);
 }

@@ -37,6 +37,11 @@ struct DigitImageParams {
   uint32_t in_dim, n_vec, n_img;
   uint8_t *img;
   uint32_t *status;
+  // optional: only the (image, vector) pairs pairs[i] = image << 8 | vector
+  // for i < *n_pairs (at most max_pairs); the columns of absent vectors are
+  // then left as they are (the matvec never reads their sums)
+  const uint32_t *pairs, *n_pairs;
+  uint32_t max_pairs;
 };
 inline uint32_t dm_groups(uint32_t n_vec) { return (n_vec + kDmVec - 1) / kDmVec; }
 inline uint64_t dm_img_bytes(uint32_t in_dim, uint32_t n_vec) {

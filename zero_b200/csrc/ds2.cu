@@ -566,6 +566,9 @@ cudaError_t ds2_enqueue_batch(zgpu_ds2_model *m, uint32_t ns, uint32_t *counter)
     ip.n_img = n_segs;
     ip.img = B.img;
     ip.status = m->d_status;
+    ip.pairs = B.pairs;
+    ip.n_pairs = B.dn_vec + kMoeMaxSegs;
+    ip.max_pairs = ns * (d.n_shared + d.top_k);
     cudaError_t e2 = launch_digit_image(ip, lc);
     if (e2 != cudaSuccess) return e2;
     DmGemmParams gp = {};
