@@ -388,6 +388,161 @@ __global__ void __launch_bounds__(32 * kMlaAttnWarps, 2) mla_attn_kernel(const M
   }
 }
 
+// The DeepSeek2 geometry (kv_lora 512, rope 64) on packed f32x2 arithmetic:
+// the structure of mla_attn_kernel, with lane l holding latent columns
+// 128 i + 4 l .. + 3 as two column pairs each, so that a score's dot product
+// runs as two interleaved chains (even and odd columns, added at the end) of
+// fma.rn.f32x2 and the context update as one fma.rn.f32x2 per column pair;
+// each lane rounds as the scalar instruction.
+__global__ void __launch_bounds__(32 * kMlaAttnWarps, 2) mla_attn512_kernel(const MlaParams p0) {
+  const MlaParams p = mla_seq(p0);
+  extern __shared__ __align__(128) float chunk[];   // [2][kMlaSubTokens][576]
+  __shared__ __align__(8) uint64_t bar[2];
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t pos = mla_pos(p);
+  if (pos >= p.max_tokens) return;   // reported by mla_prep
+  constexpr uint32_t R = 512, RD = 64, row = R + RD;
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t split = blockIdx.x, st = p.split_tokens;
+  const uint32_t t0 = split * st;
+  if (t0 > pos) return;   // beyond the context: the merge reads only the splits up to pos
+  const uint32_t t1 = min(t0 + st, pos + 1);
+  const uint32_t nsub = (t1 - t0 + kMlaSubTokens - 1) / kMlaSubTokens;
+  const uint32_t bars[2] = {smem_addr(&bar[0]), smem_addr(&bar[1])};
+  auto issue = [&](uint32_t i) {
+    const uint32_t ts = t0 + i * kMlaSubTokens, nt = min(kMlaSubTokens, t1 - ts);
+    mbar_arrive_expect_tx(bars[i & 1], nt * row * 4);
+    bulk_copy_g2s(smem_addr(chunk + (i & 1) * kMlaSubTokens * row), p.cache + static_cast<size_t>(ts) * row,
+                  nt * row * 4, bars[i & 1]);
+  };
+  if (threadIdx.x == 0) {
+    mbar_init(bars[0], 1);
+    mbar_init(bars[1], 1);
+    fence_barrier_init();
+    issue(0);
+    if (nsub > 1) issue(1);
+  }
+  const uint32_t hb = blockIdx.z * kMlaHeadsPerCta + warp * 4;
+  // column pair i of this lane: columns 128 (i / 2) + 4 lane + 2 (i % 2) + {0, 1}
+  float2 qa[4][8], acc[4][8], qp[4];
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    const bool hv = hb + h < p.n_heads;
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const float4 q4 = hv ? __ldcg(reinterpret_cast<const float4 *>(p.q_abs + static_cast<size_t>(hb + h) * R) +
+                                    32 * jj + lane)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      qa[h][2 * jj] = make_float2(q4.x, q4.y);
+      qa[h][2 * jj + 1] = make_float2(q4.z, q4.w);
+      acc[h][2 * jj] = acc[h][2 * jj + 1] = make_float2(0.f, 0.f);
+    }
+    qp[h] = hv ? __ldcg(reinterpret_cast<const float2 *>(p.q_pe + static_cast<size_t>(hb + h) * RD) + lane)
+               : make_float2(0.f, 0.f);
+  }
+  auto load_row = [&](const float *ct, float2 (&cv)[8], float2 &cr) {
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const float4 c4 = reinterpret_cast<const float4 *>(ct)[32 * jj + lane];
+      cv[2 * jj] = make_float2(c4.x, c4.y);
+      cv[2 * jj + 1] = make_float2(c4.z, c4.w);
+    }
+    cr = reinterpret_cast<const float2 *>(ct + R)[lane];
+  };
+  float m_mine = -INFINITY, l_mine = 0.f;
+  __syncthreads();   // barriers initialised before anyone waits on them
+  bool ok = true;
+  for (uint32_t i = 0; i < nsub; ++i) {
+    ok = __syncthreads_and(ok && mbar_wait(bars[i & 1], (i >> 1) & 1, p.status));
+    if (!ok) {
+      if (threadIdx.x == 0) {
+        mbar_wait(bars[i & 1], (i >> 1) & 1, p.status);
+        if (i + 1 < nsub) mbar_wait(bars[(i + 1) & 1], ((i + 1) >> 1) & 1, p.status);
+      }
+      break;
+    }
+    const float *ch = chunk + (i & 1) * kMlaSubTokens * row;
+    const uint32_t nt = min(kMlaSubTokens, t1 - (t0 + i * kMlaSubTokens));
+    for (uint32_t g = 0; g < nt; g += 8) {
+      const uint32_t ng = min(8u, nt - g);
+      float v[32];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (static_cast<uint32_t>(k) < ng) {
+          float2 cv[8], cr;
+          load_row(ch + (g + k) * row, cv, cr);
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            float2 d = mul2_rn(qp[h], cr);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) d = fma2_rn(qa[h][c], cv[c], d);
+            v[h * 8 + k] = __fadd_rn(d.x, d.y);
+          }
+        } else {
+#pragma unroll
+          for (int h = 0; h < 4; ++h) v[h * 8 + k] = 0.f;
+        }
+      }
+      const float dot = reduce_scatter<32>(v, lane);
+      const float s = ((lane & 7) < ng) ? __fmul_rn(dot, p.scale) : -INFINITY;
+      float gm = s;
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, off));
+      const float mn = fmaxf(m_mine, gm);
+      const float corr = (m_mine == mn) ? 1.0f : expf(m_mine - mn);
+      const float pe = (s == -INFINITY) ? 0.0f : expf(s - mn);
+      float ps = pe;
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1) ps = __fadd_rn(ps, __shfl_xor_sync(0xffffffffu, ps, off));
+      l_mine = fmaf(l_mine, corr, ps);
+      m_mine = mn;
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float c = __shfl_sync(0xffffffffu, corr, h * 8);
+        const float2 c2 = make_float2(c, c);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[h][j] = mul2_rn(acc[h][j], c2);
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (static_cast<uint32_t>(k) < ng) {
+          float2 cv[8], cr;
+          load_row(ch + (g + k) * row, cv, cr);
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const float pk = __shfl_sync(0xffffffffu, pe, h * 8 + k);
+            const float2 pk2 = make_float2(pk, pk);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[h][j] = fma2_rn(pk2, cv[j], acc[h][j]);
+          }
+        }
+      }
+    }
+    __syncthreads();   // every warp is done with buffer i & 1
+    if (threadIdx.x == 0 && i + 2 < nsub) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(i + 2);
+    }
+  }
+  if (!ok) l_mine = __uint_as_float(0x7fc00000u);   // a failed copy surfaces as NumericalInstability
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    if (hb + h >= p.n_heads) break;
+    float *pp = p.part + (static_cast<size_t>(hb + h) * p.max_splits + split) * (R + 2);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t c0 = 128u * (j / 2) + 4u * lane + 2u * (j % 2);
+      pp[c0] = acc[h][j].x;
+      pp[c0 + 1] = acc[h][j].y;
+    }
+    if (lane == static_cast<uint32_t>(h) * 8) {
+      pp[R] = m_mine;
+      pp[R + 1] = l_mine;
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kMlaMergeThreads) mla_merge_kernel(const MlaParams p0) {
   const MlaParams p = mla_seq(p0);
   pdl_launch_dependents();
@@ -422,7 +577,7 @@ cudaError_t mla_setup() {
                                        static_cast<int>(kMlaSlabMax));
   if (e != cudaSuccess) return e;
   const int smem = static_cast<int>(2 * kMlaSubTokens * (kMlaMaxLatent + kMlaMaxRope) * sizeof(float));
-  e = cudaFuncSetAttribute(mla_attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  e = cudaFuncSetAttribute(mla_attn512_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(mla_attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
 }
@@ -461,7 +616,7 @@ cudaError_t launch_mla_attention(const MlaParams &mp, const LaunchCfg &lc) {
   const uint32_t splits = (p.max_tokens + p.split_tokens - 1) / p.split_tokens;
   cudaLaunchConfig_t cfg = make_launch_cfg(dim3(splits, ns, hg), dim3(32 * warps), chunk, lc, attr);
   if (lc.launch_counter) ++*lc.launch_counter;
-  cudaError_t e = (p.kv_lora == 512 && p.rope == 64) ? cudaLaunchKernelEx(&cfg, mla_attn_kernel<true>, p)
+  cudaError_t e = (p.kv_lora == 512 && p.rope == 64) ? cudaLaunchKernelEx(&cfg, mla_attn512_kernel, p)
                                                       : cudaLaunchKernelEx(&cfg, mla_attn_kernel<false>, p);
   if (e != cudaSuccess) return e;
   const uint32_t nq = (p.kv_lora + kMlaMergeThreads - 1) / kMlaMergeThreads;
