@@ -200,11 +200,8 @@ __global__ void __launch_bounds__(kMlaPrepThreads) mla_prep_kernel(const MlaPara
 // shuffles per 32 scores).  Online softmax per 8-token group, then the
 // context update from the same shared rows.  Output per head: the split's
 // (sum p c, m, l).
-// V512: the DeepSeek2 geometry (kv_lora 512, rope 64), where lane l holds
-// latent columns 128 i + 4 l .. 128 i + 4 l + 3 and rope columns 2 l, 2 l + 1,
-// so each cached row is read with four 16-byte and one 8-byte shared load
-// per lane instead of eighteen 4-byte ones.
-template <bool V512>
+// Any supported geometry; kv_lora 512 / rope 64 (DeepSeek2's) runs
+// mla_attn512_kernel below.
 __global__ void __launch_bounds__(32 * kMlaAttnWarps, 2) mla_attn_kernel(const MlaParams p0) {
   const MlaParams p = mla_seq(p0);
   extern __shared__ __align__(128) float chunk[];   // [2][kMlaSubTokens][kv_lora + rope]
@@ -242,55 +239,22 @@ __global__ void __launch_bounds__(32 * kMlaAttnWarps, 2) mla_attn_kernel(const M
   for (int h = 0; h < 4; ++h) {
     const bool hv = hb + h < p.n_heads;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) acc[h][j] = 0.f;
-    if (V512) {
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        const float4 q4 = hv ? __ldcg(reinterpret_cast<const float4 *>(p.q_abs + static_cast<size_t>(hb + h) * 512) +
-                                      32 * jj + lane)
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
-        qa[h][4 * jj] = q4.x;
-        qa[h][4 * jj + 1] = q4.y;
-        qa[h][4 * jj + 2] = q4.z;
-        qa[h][4 * jj + 3] = q4.w;
-      }
-      const float2 r2 = hv ? __ldcg(reinterpret_cast<const float2 *>(p.q_pe + static_cast<size_t>(hb + h) * 64) + lane)
-                           : make_float2(0.f, 0.f);
-      qp[h][0] = r2.x;
-      qp[h][1] = r2.y;
-    } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        qa[h][j] = (hv && j < static_cast<int>(nr)) ? __ldcg(p.q_abs + static_cast<size_t>(hb + h) * R + lane + 32 * j)
-                                                     : 0.f;
-#pragma unroll
-      for (int j = 0; j < 2; ++j)
-        qp[h][j] = (hv && lane + 32 * j < RD) ? __ldcg(p.q_pe + static_cast<size_t>(hb + h) * RD + lane + 32 * j) : 0.f;
+    for (int j = 0; j < 16; ++j) {
+      acc[h][j] = 0.f;
+      qa[h][j] = (hv && j < static_cast<int>(nr)) ? __ldcg(p.q_abs + static_cast<size_t>(hb + h) * R + lane + 32 * j)
+                                                   : 0.f;
     }
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+      qp[h][j] = (hv && lane + 32 * j < RD) ? __ldcg(p.q_pe + static_cast<size_t>(hb + h) * RD + lane + 32 * j) : 0.f;
   }
   // one cached row's latent values (cv) and rope values (cr) for this lane
   auto load_row = [&](const float *ct, float (&cv)[16], float (&cr)[2]) {
-    if (V512) {
 #pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        const float4 c4 = reinterpret_cast<const float4 *>(ct)[32 * jj + lane];
-        cv[4 * jj] = c4.x;
-        cv[4 * jj + 1] = c4.y;
-        cv[4 * jj + 2] = c4.z;
-        cv[4 * jj + 3] = c4.w;
-      }
-      const float2 r2 = reinterpret_cast<const float2 *>(ct + 512)[lane];
-      cr[0] = r2.x;
-      cr[1] = r2.y;
-    } else {
+    for (int j = 0; j < 16; ++j) cv[j] = (j < static_cast<int>(nr)) ? ct[lane + 32 * j] : 0.f;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) cv[j] = (j < static_cast<int>(nr)) ? ct[lane + 32 * j] : 0.f;
-#pragma unroll
-      for (int j = 0; j < 2; ++j) cr[j] = (lane + 32 * j < RD) ? ct[R + lane + 32 * j] : 0.f;
-    }
+    for (int j = 0; j < 2; ++j) cr[j] = (lane + 32 * j < RD) ? ct[R + lane + 32 * j] : 0.f;
   };
-  // the latent column of this lane's value j
-  auto col = [&](int j) -> uint32_t { return V512 ? 128u * (j / 4) + 4u * lane + (j % 4) : lane + 32u * j; };
   // lane l's score slot: head l / 8, token l % 8 of each group
   float m_mine = -INFINITY, l_mine = 0.f;
   __syncthreads();   // barriers initialised before anyone waits on them
@@ -359,7 +323,7 @@ __global__ void __launch_bounds__(32 * kMlaAttnWarps, 2) mla_attn_kernel(const M
           load_row(ch + (g + k) * row, cv, cr);
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            if (V512 || j < static_cast<int>(nr)) {
+            if (j < static_cast<int>(nr)) {
 #pragma unroll
               for (int h = 0; h < 4; ++h) acc[h][j] = fmaf(pk[h], cv[j], acc[h][j]);
             }
@@ -380,7 +344,7 @@ __global__ void __launch_bounds__(32 * kMlaAttnWarps, 2) mla_attn_kernel(const M
     float *pp = p.part + (static_cast<size_t>(hb + h) * p.max_splits + split) * (R + 2);
 #pragma unroll
     for (int j = 0; j < 16; ++j)
-      if (V512 || j < static_cast<int>(nr)) pp[col(j)] = acc[h][j];
+      if (j < static_cast<int>(nr)) pp[lane + 32 * j] = acc[h][j];
     if (lane == static_cast<uint32_t>(h) * 8) {
       pp[R] = m_mine;
       pp[R + 1] = l_mine;
@@ -579,7 +543,7 @@ cudaError_t mla_setup() {
   const int smem = static_cast<int>(2 * kMlaSubTokens * (kMlaMaxLatent + kMlaMaxRope) * sizeof(float));
   e = cudaFuncSetAttribute(mla_attn512_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(mla_attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  return cudaFuncSetAttribute(mla_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
 }
 
 cudaError_t launch_mla_prep(const MlaParams &mp, const LaunchCfg &lc) {
@@ -617,7 +581,7 @@ cudaError_t launch_mla_attention(const MlaParams &mp, const LaunchCfg &lc) {
   cudaLaunchConfig_t cfg = make_launch_cfg(dim3(splits, ns, hg), dim3(32 * warps), chunk, lc, attr);
   if (lc.launch_counter) ++*lc.launch_counter;
   cudaError_t e = (p.kv_lora == 512 && p.rope == 64) ? cudaLaunchKernelEx(&cfg, mla_attn512_kernel, p)
-                                                      : cudaLaunchKernelEx(&cfg, mla_attn_kernel<false>, p);
+                                                      : cudaLaunchKernelEx(&cfg, mla_attn_kernel, p);
   if (e != cudaSuccess) return e;
   const uint32_t nq = (p.kv_lora + kMlaMergeThreads - 1) / kMlaMergeThreads;
   cudaLaunchAttribute attr2[1];
