@@ -94,6 +94,9 @@ struct zgpu_ctx {
   uint32_t flags = 0;
   cudaStream_t stream = nullptr;
   std::string last_error;
+  // the first expired device wait of the last status read (words 4..7 of
+  // the status block: site, three values; site 0 when none was recorded)
+  uint32_t last_wait[4] = {0, 0, 0, 0};
   std::map<uintptr_t, zgpu::DeviceTensor> weights;
   // scratch for the host-buffer entry points (grown on demand)
   float *d_x = nullptr, *d_y = nullptr;

@@ -22,6 +22,7 @@
 #include "digit_mma.h"
 #include "internal.h"
 #include "layout.h"
+#include "moe.h"
 #include "ops.h"
 #include "step.h"
 
@@ -114,6 +115,7 @@ zgpu_status zgpu_read_device_status(zgpu_ctx *ctx, uint32_t *d_status, uint32_t 
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) return zgpu_cuda_fail(ctx, e, "step status");
   *st_out = sw[0];
+  for (int i = 0; i < 4; ++i) ctx->last_wait[i] = (sw[0] & ZDEV_ERR_TIMEOUT) ? sw[4 + i] : 0u;
   if (sw[0]) cudaMemsetAsync(d_status, 0, sizeof(sw), ctx->stream);
   if (sw[1])
     return zgpu_fail(ctx, ZGPU_ERR_CUDA, "device bounds check " + std::to_string(sw[1]) + " failed (" +
@@ -123,7 +125,16 @@ zgpu_status zgpu_read_device_status(zgpu_ctx *ctx, uint32_t *d_status, uint32_t 
 
 zgpu_status zgpu_map_device_status(zgpu_ctx *ctx, uint32_t st) {
   if (!st) return ZGPU_OK;
-  if (st & ZDEV_ERR_TIMEOUT) return zgpu_fail(ctx, ZGPU_ERR_DEVICE_TIMEOUT, "device wait timed out");
+  if (st & ZDEV_ERR_TIMEOUT) {
+    std::string what = "device wait timed out";
+    const uint32_t *w = ctx->last_wait;
+    if (w[0] == ZDEV_WAIT_EP_ARRIVAL || w[0] == ZDEV_WAIT_EP_SLOT)
+      what += std::string(w[0] == ZDEV_WAIT_EP_ARRIVAL ? " (expert-parallel arrival word of rank "
+                                                        : " (expert-parallel slot ") +
+              std::to_string(w[3]) + ": waited for version " + std::to_string(w[1]) + ", read " +
+              std::to_string(w[2]) + ")";
+    return zgpu_fail(ctx, ZGPU_ERR_DEVICE_TIMEOUT, what);
+  }
   if (st & ZDEV_ERR_BOUNDS)
     return zgpu_fail(ctx, ZGPU_ERR_KV_TOKEN_OUT_OF_RANGE, "token or position outside the cache");
   if (st & ZDEV_ERR_NUMERICAL)

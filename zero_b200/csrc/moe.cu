@@ -225,6 +225,17 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const RoutePar
   }
 }
 
+// An expired combine wait: the timeout bit, and (first one only) the wait
+// in words 4..7 of the status block.
+__device__ void wait_expired(uint32_t *status, uint32_t site, uint32_t ver, uint32_t tag, uint32_t which) {
+  if (atomicCAS(&status[4], 0u, site) == 0u) {
+    status[5] = ver;
+    status[6] = tag;
+    status[7] = which;
+  }
+  atomicOr(status, ZDEV_ERR_TIMEOUT);
+}
+
 __global__ void moe_combine_kernel(const CombineParams p0) {
   pdl_launch_dependents();
   pdl_wait();
@@ -253,9 +264,10 @@ __global__ void moe_combine_kernel(const CombineParams p0) {
     const unsigned long long *arrive = p.xslots + ep_slot_words(p.slot_cap, p.dim);
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t r = 0; r < p.world && !gave_up; ++r) {
-      while (static_cast<uint32_t>(__ldcg(arrive + r) >> 32) < ver) {
+      uint32_t tag;
+      while ((tag = static_cast<uint32_t>(__ldcg(arrive + r) >> 32)) < ver) {
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
-          atomicOr(p.status, ZDEV_ERR_TIMEOUT);
+          wait_expired(p.status, ZDEV_WAIT_EP_ARRIVAL, ver, tag, r);
           gave_up = true;
           break;
         }
@@ -276,7 +288,7 @@ __global__ void moe_combine_kernel(const CombineParams p0) {
         const uint64_t t0 = globaltimer_ns();
         while (static_cast<uint32_t>(t >> 32) != ver) {
           if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            atomicOr(p.status, ZDEV_ERR_TIMEOUT);
+            wait_expired(p.status, ZDEV_WAIT_EP_SLOT, ver, static_cast<uint32_t>(t >> 32), tb * p.top_k + k);
             t = static_cast<unsigned long long>(0x7fc00000u);
             gave_up = true;
             break;

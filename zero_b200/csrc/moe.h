@@ -42,6 +42,12 @@ struct RouteParams {
   uint32_t n_seq, x_stride;
 };
 
+// A combine wait that gives up records itself in words 4..7 of the status
+// block (the first one only): the site, the version it waited for, the tag
+// it last read, and which word (the rank for an arrival word, b * top_k + k
+// for a slot).
+enum : uint32_t { ZDEV_WAIT_EP_ARRIVAL = 2, ZDEV_WAIT_EP_SLOT = 3 };
+
 struct CombineParams {
   const float *exp_out;      // [n_shared + top_k][dim]
   const float *weights;      // [top_k]
