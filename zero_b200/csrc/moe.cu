@@ -225,6 +225,21 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const RoutePar
   }
 }
 
+// Words another GPU writes and this one polls (or the reverse) are accessed
+// with relaxed system-scope operations.  A weak load (ld.global.cg) carries
+// no guarantee that it ever observes a store from another GPU: it may keep
+// returning a copy of the word cached on this GPU while the peer's store has
+// reached the word's home.  The tags make every word self-validating, so no
+// acquire / release ordering is needed beyond that.
+__device__ __forceinline__ unsigned long long ld_peer_u64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_peer_u64(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 // An expired combine wait: the timeout bit, and (first one only) the wait
 // in words 4..7 of the status block.
 __device__ void wait_expired(uint32_t *status, uint32_t site, uint32_t ver, uint32_t tag, uint32_t which) {
@@ -265,7 +280,7 @@ __global__ void moe_combine_kernel(const CombineParams p0) {
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t r = 0; r < p.world && !gave_up; ++r) {
       uint32_t tag;
-      while ((tag = static_cast<uint32_t>(__ldcg(arrive + r) >> 32)) < ver) {
+      while ((tag = static_cast<uint32_t>(ld_peer_u64(arrive + r) >> 32)) < ver) {
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
           wait_expired(p.status, ZDEV_WAIT_EP_ARRIVAL, ver, tag, r);
           gave_up = true;
@@ -281,7 +296,7 @@ __global__ void moe_combine_kernel(const CombineParams p0) {
       // the slot's output from whichever rank ran its expert (bounded wait)
       const unsigned long long *src =
           p.xslots + (static_cast<size_t>(ver & 1u) * p.slot_cap + tb * p.top_k + k) * p.dim + i;
-      unsigned long long t = __ldcg(src);
+      unsigned long long t = ld_peer_u64(src);
       if (gave_up) {
         t = static_cast<unsigned long long>(0x7fc00000u);
       } else if (static_cast<uint32_t>(t >> 32) != ver) {
@@ -293,7 +308,7 @@ __global__ void moe_combine_kernel(const CombineParams p0) {
             gave_up = true;
             break;
           }
-          t = __ldcg(src);
+          t = ld_peer_u64(src);
         }
       }
       y = __uint_as_float(static_cast<uint32_t>(t));
@@ -316,7 +331,7 @@ __global__ void moe_ep_publish_kernel(const EpPublishParams p) {
   if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0) {
     // this rank's arrival for invocation ver, in every rank's buffer
     const size_t a = ep_slot_words(p.slot_cap, p.dim) + p.ep_rank;
-    for (uint32_t d = 0; d < p.world; ++d) p.dst[d][a] = tag_word(0.0f, ver);
+    for (uint32_t d = 0; d < p.world; ++d) st_peer_u64(p.dst[d] + a, tag_word(0.0f, ver));
   }
   if (i >= p.dim) return;
   const uint32_t e = __ldcg(p.ids + static_cast<size_t>(tb) * p.top_k + k);
@@ -324,7 +339,7 @@ __global__ void moe_ep_publish_kernel(const EpPublishParams p) {
   const float *eo = p.exp_out + static_cast<size_t>(tb) * (p.n_shared + p.top_k) * p.dim;
   const unsigned long long w = tag_word(__ldcg(eo + static_cast<size_t>(p.n_shared + k) * p.dim + i), ver);
   const size_t off = (static_cast<size_t>(ver & 1u) * p.slot_cap + tb * p.top_k + k) * p.dim + i;
-  for (uint32_t d = 0; d < p.world; ++d) p.dst[d][off] = w;
+  for (uint32_t d = 0; d < p.world; ++d) st_peer_u64(p.dst[d] + off, w);
 }
 
 __global__ void moe_ep_advance_kernel(uint32_t *ep_seq) {
