@@ -526,7 +526,12 @@ void zgpu_ds2_destroy(zgpu_ds2_model *m);
  * divide by world.  Bring-up as zgpu_qwen3_create_tp: create every rank,
  * zgpu_ds2_ep_export on each, exchange the ZGPU_IPC_HANDLE_BYTES handles in
  * rank order, zgpu_ds2_ep_connect on each; then every rank makes the same
- * calls (forward, LM head, generate) with the same arguments. */
+ * calls (forward, LM head, generate) with the same arguments.  A combine
+ * wait that runs out (1 s) fails the call with ZGPU_ERR_DEVICE_TIMEOUT,
+ * naming the wait in zgpu_last_error, and aborts the model's exchange:
+ * every later call fails at once the same way; create the ranks again to
+ * recover.  Status of this build: its two-GPU tests end with such timeouts
+ * (an open defect), so bit identity with one GPU is not established. */
 zgpu_status zgpu_ds2_create_ep(zgpu_ctx *ctx, const zgpu_ds2_desc *desc, uint32_t rank, uint32_t world,
                                zgpu_ds2_model **out);
 zgpu_status zgpu_ds2_ep_export(zgpu_ds2_model *m, void *handle_out);

@@ -127,7 +127,7 @@ struct zgpu_ds2_model {
   // [rank * ep_per_rank, (rank + 1) * ep_per_rank); everything else is
   // replicated.  Selected experts' outputs cross over the exchange buffers.
   uint32_t rank = 0, world = 1, ep_per_rank = 0;
-  unsigned long long *d_xslots = nullptr;   // this rank's exchange buffer: [2][top_k][hidden] slots, arrivals
+  unsigned long long *d_xslots = nullptr;   // this rank's exchange buffer: slots, arrival words, abort word
   uint32_t *d_ep_seq = nullptr;             // MoE invocations so far (the exchange version)
   unsigned long long **d_ep_dst = nullptr;  // [world] every rank's exchange buffer
   std::vector<void *> ipc_opened;

@@ -128,7 +128,9 @@ zgpu_status zgpu_map_device_status(zgpu_ctx *ctx, uint32_t st) {
   if (st & ZDEV_ERR_TIMEOUT) {
     std::string what = "device wait timed out";
     const uint32_t *w = ctx->last_wait;
-    if (w[0] == ZDEV_WAIT_EP_ARRIVAL || w[0] == ZDEV_WAIT_EP_SLOT)
+    if (w[0] == ZDEV_WAIT_EP_ABORTED)
+      what += " (the expert-parallel exchange was aborted by an earlier expired wait; create the model again)";
+    else if (w[0] == ZDEV_WAIT_EP_ARRIVAL || w[0] == ZDEV_WAIT_EP_SLOT)
       what += std::string(w[0] == ZDEV_WAIT_EP_ARRIVAL ? " (expert-parallel arrival word of rank "
                                                         : " (expert-parallel slot ") +
               std::to_string(w[3]) + ": waited for version " + std::to_string(w[1]) + ", read " +

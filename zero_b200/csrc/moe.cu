@@ -271,18 +271,24 @@ __global__ void moe_combine_kernel(const CombineParams p0) {
   }
   const uint32_t ver = p.xslots ? __ldcg(p.ep_seq) + 1 : 0u;
   bool gave_up = false;   // after one expired wait the others are not waited for
+  unsigned long long *abort_w = p.xslots ? p.xslots + ep_abort_word(p.slot_cap, p.dim) : nullptr;
   if (p.xslots) {
     // flow control: every rank has published this invocation (and so has
     // finished its combine of the previous one).  A rank may already have
     // published the next invocation (its arrival word then reads ver + 1),
     // so the test is "at least ver".
     const unsigned long long *arrive = p.xslots + ep_slot_words(p.slot_cap, p.dim);
+    if (ld_peer_u64(abort_w) != 0ull) {
+      wait_expired(p.status, ZDEV_WAIT_EP_ABORTED, ver, 0u, 0u);
+      gave_up = true;
+    }
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t r = 0; r < p.world && !gave_up; ++r) {
       uint32_t tag;
       while ((tag = static_cast<uint32_t>(ld_peer_u64(arrive + r) >> 32)) < ver) {
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
           wait_expired(p.status, ZDEV_WAIT_EP_ARRIVAL, ver, tag, r);
+          st_peer_u64(abort_w, 1ull);
           gave_up = true;
           break;
         }
@@ -304,6 +310,7 @@ __global__ void moe_combine_kernel(const CombineParams p0) {
         while (static_cast<uint32_t>(t >> 32) != ver) {
           if (globaltimer_ns() - t0 > kWaitLimitNs) {
             wait_expired(p.status, ZDEV_WAIT_EP_SLOT, ver, static_cast<uint32_t>(t >> 32), tb * p.top_k + k);
+            st_peer_u64(abort_w, 1ull);
             t = static_cast<unsigned long long>(0x7fc00000u);
             gave_up = true;
             break;

@@ -46,7 +46,9 @@ struct RouteParams {
 // block (the first one only): the site, the version it waited for, the tag
 // it last read, and which word (the rank for an arrival word, b * top_k + k
 // for a slot).
-enum : uint32_t { ZDEV_WAIT_EP_ARRIVAL = 2, ZDEV_WAIT_EP_SLOT = 3 };
+// Site ZDEV_WAIT_EP_ABORTED: the exchange was already aborted (abort word
+// set) and the combine did not wait.
+enum : uint32_t { ZDEV_WAIT_EP_ARRIVAL = 2, ZDEV_WAIT_EP_SLOT = 3, ZDEV_WAIT_EP_ABORTED = 4 };
 
 struct CombineParams {
   const float *exp_out;      // [n_shared + top_k][dim]
@@ -59,7 +61,7 @@ struct CombineParams {
   // moe_ep_publish) at version *ep_seq + 1; null: from exp_out.  The
   // combine also waits until every rank's arrival word (ep_arrive_words
   // after the slots, one per rank) carries that version.
-  const unsigned long long *xslots;
+  unsigned long long *xslots;
   const uint32_t *ep_seq;
   uint32_t world;
   uint32_t *status;
@@ -93,7 +95,12 @@ struct EpPublishParams {
 // word per rank.
 constexpr uint32_t kEpMaxRanks = 8;
 ZGPU_HD size_t ep_slot_words(uint32_t slots, uint32_t dim) { return 2 * static_cast<size_t>(slots) * dim; }
-ZGPU_HD size_t ep_exchange_words(uint32_t slots, uint32_t dim) { return ep_slot_words(slots, dim) + kEpMaxRanks; }
+// After the arrival words, this rank's abort word: nonzero once one of its
+// combine waits expired.  Every later combine then gives up at once (the
+// ranks are out of step, so every wait would run to its limit); the
+// exchange stays aborted for the model's lifetime.
+ZGPU_HD size_t ep_abort_word(uint32_t slots, uint32_t dim) { return ep_slot_words(slots, dim) + kEpMaxRanks; }
+ZGPU_HD size_t ep_exchange_words(uint32_t slots, uint32_t dim) { return ep_abort_word(slots, dim) + 1; }
 
 // Grouping of a batch's (token, expert) pairs by expert for the tensor-core
 // expert matvecs (digit_mma.h).  Segment s < n_local is this rank's routed
