@@ -525,9 +525,11 @@ void zgpu_ds2_destroy(zgpu_ds2_model *m);
  * expert ids equal the one-GPU model bit for bit.  Requires n_experts to
  * divide by world.  Bring-up as zgpu_qwen3_create_tp: create every rank,
  * zgpu_ds2_ep_export on each, exchange the ZGPU_IPC_HANDLE_BYTES handles in
- * rank order, zgpu_ds2_ep_connect on each; then every rank makes the same
- * calls (forward, LM head, generate) with the same arguments.  A combine
- * wait that runs out (1 s) fails the call with ZGPU_ERR_DEVICE_TIMEOUT,
+ * rank order, zgpu_ds2_ep_connect on each, then a host barrier over the
+ * ranks (no rank's first exchange may start while a peer is still mapping
+ * handles); then every rank makes the same calls (forward, LM head,
+ * generate) with the same arguments.  A combine wait for another rank that
+ * runs out (5 s) fails the call with ZGPU_ERR_DEVICE_TIMEOUT,
  * naming the wait in zgpu_last_error, and aborts the model's exchange:
  * every later call fails at once the same way; create the ranks again to
  * recover.  Status of this build: its two-GPU tests end with such timeouts

@@ -240,6 +240,14 @@ __device__ __forceinline__ void st_peer_u64(unsigned long long *p, unsigned long
   asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
+// Limit of a combine's waits for other ranks (arrival words, slots).  Each
+// rank's kernels are launched by its own host thread, so a peer can start an
+// invocation seconds late for legitimate reasons (graph builds, allocations,
+// a process still mapping its peers); 5 s covers that and still bounds a
+// dead peer.  The first expiry aborts the exchange, so a failing model pays
+// this once.
+constexpr uint64_t kEpWaitLimitNs = 5000000000ull;
+
 // An expired combine wait: the timeout bit, and (first one only) the wait
 // in words 4..7 of the status block.
 __device__ void wait_expired(uint32_t *status, uint32_t site, uint32_t ver, uint32_t tag, uint32_t which) {
@@ -286,7 +294,7 @@ __global__ void moe_combine_kernel(const CombineParams p0) {
     for (uint32_t r = 0; r < p.world && !gave_up; ++r) {
       uint32_t tag;
       while ((tag = static_cast<uint32_t>(ld_peer_u64(arrive + r) >> 32)) < ver) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (globaltimer_ns() - t0 > kEpWaitLimitNs) {
           wait_expired(p.status, ZDEV_WAIT_EP_ARRIVAL, ver, tag, r);
           st_peer_u64(abort_w, 1ull);
           gave_up = true;
@@ -308,7 +316,7 @@ __global__ void moe_combine_kernel(const CombineParams p0) {
       } else if (static_cast<uint32_t>(t >> 32) != ver) {
         const uint64_t t0 = globaltimer_ns();
         while (static_cast<uint32_t>(t >> 32) != ver) {
-          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          if (globaltimer_ns() - t0 > kEpWaitLimitNs) {
             wait_expired(p.status, ZDEV_WAIT_EP_SLOT, ver, static_cast<uint32_t>(t >> 32), tb * p.top_k + k);
             st_peer_u64(abort_w, 1ull);
             t = static_cast<unsigned long long>(0x7fc00000u);

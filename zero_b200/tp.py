@@ -90,5 +90,11 @@ def exchange_handles(handle: bytes, group=None) -> list[bytes]:
 
 
 def connect(model, group=None) -> None:
-    """Export this rank's handle, gather everyone's, map the peers."""
+    """Export this rank's handle, gather everyone's, map the peers, then wait
+    until every rank has mapped them.  The device-side waits for a peer are
+    bounded, so no rank may start its first exchange while another is still
+    opening handles (the first peer mapping of a process can take long)."""
+    import torch.distributed as dist
+
     model.tp_connect(exchange_handles(model.tp_export(), group))
+    dist.barrier(group=group)
