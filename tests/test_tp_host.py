@@ -5,6 +5,7 @@ every routed expert exactly one owner, and the handle exchange over a 2-rank
 gloo group hands every rank all handles in rank order (with the ranks
 agreeing on the expert plan)."""
 import socket
+import time
 
 import pytest
 import torch.multiprocessing as mp
@@ -127,3 +128,54 @@ def test_expert_parallel_exchange_over_gloo():
         got, plans = res[r]
         assert got == [bytes([0x40]) * 64, bytes([0x41]) * 64]
         assert plans == [(0, 32), (32, 64)]
+
+
+class _FakePeerModel:
+    """tp_export / tp_connect of a model; rank 1 maps its peers slowly."""
+
+    def __init__(self, rank):
+        self.rank = rank
+        self.mapped_at = None
+
+    def tp_export(self):
+        return bytes([0x60 + self.rank]) * 64
+
+    def tp_connect(self, handles):
+        if self.rank == 1:
+            time.sleep(1.5)
+        self.handles = handles
+        self.mapped_at = time.time()
+
+
+def _connect_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        m = _FakePeerModel(rank)
+        tp.connect(m)
+        q.put((rank, m.handles, m.mapped_at, time.time()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_connect_returns_only_after_every_rank_mapped_its_peers():
+    """No rank may start its first exchange (bounded device waits) while a
+    peer is still mapping handles: connect ends with a barrier."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_connect_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r, handles, mapped_at, returned_at = q.get(timeout=120)
+        res[r] = (handles, mapped_at, returned_at)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(2):
+        assert res[r][0] == [bytes([0x60]) * 64, bytes([0x61]) * 64]
+    # rank 0 mapped at once but returned only after the slow rank 1 had mapped
+    assert res[0][2] >= res[1][1]
