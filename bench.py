@@ -357,7 +357,7 @@ def run_ds2(args, rank, world, local):
 
         from zero_b200 import tp
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     weights = synth.ds2_weights(cfg, seed=SEED)
     prompt = synth.ds2_prompt_ids(cfg, args.context, seed=SEED)
@@ -487,7 +487,7 @@ def run_ds2_batch(args, rank, world, local):
 
         from zero_b200 import tp
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     weights = synth.ds2_weights(cfg, seed=SEED)
     prompt = synth.ds2_prompt_ids(cfg, args.context, seed=SEED)
@@ -648,7 +648,7 @@ def run_qwen3_tp(args, rank, world, local):
 
     torch.cuda.set_device(local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     weights = synth.qwen3_weights(cfg, seed=SEED)
     prompt = synth.prompt_ids(cfg, TP_CONTEXT, seed=SEED)
@@ -1359,4 +1359,19 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        # A rank that fails (a device-wait timeout, an exception) ends at once
+        # with a non-zero status, so the launcher stops the other ranks;
+        # unwinding normally could block in process-group teardown while its
+        # peers wait at their next collective.
+        try:
+            main()
+        except BaseException:
+            import traceback
+
+            traceback.print_exc()
+            sys.stderr.flush()
+            sys.stdout.flush()
+            os._exit(1)
+    else:
+        main()
