@@ -29,6 +29,16 @@ def test_libzgpu_exports_every_declared_symbol():
     assert set(_lib.EXPORTED) <= declared
 
 
+def test_integration_notes_bind_every_declared_symbol():
+    """INTEGRATION.md's Rust extern blocks declare every entry point of
+    zgpu.h (the binding a maintainer adds to the crate)."""
+    declared = _declared(ROOT / "include" / "zgpu.h", "zgpu_")
+    notes = (ROOT / "INTEGRATION.md").read_text()
+    bound = set(re.findall(r"pub fn (zgpu_\w+)\s*\(", notes))
+    missing = sorted(declared - bound)
+    assert not missing, f"no Rust binding in INTEGRATION.md for: {missing}"
+
+
 def test_liboracle_exports_every_declared_symbol():
     import oracle
 
