@@ -332,23 +332,76 @@ def run_reference(args, rank):
 DS2_METRIC = "decode tok/s, DeepSeek-V2-Lite-shape MLA+MoE Q4_0, one sequence"
 
 
+def ds2_cpu_sample(cfg, weights, context: int, steps: int):
+    """The reference's own DeepSeek2 step on the host cores: the oracle's
+    restatement of its AVX-512 kernel path (inference_avx512.rs:2141-2825:
+    every cached latent re-expanded through kv_b twice per layer, matmuls on
+    a persistent pinned pool, one participant per physical core), one
+    sequence at `context` cached tokens.  The cache rows are seeded (the cost
+    depends on the context, not on the values).  Returns (tok/s, seconds,
+    threads) over `steps` forward + LM-head steps; the reference decodes
+    concurrent sequences one forward at a time, so this is also its batch
+    throughput."""
+    import oracle as O
+
+    r = O.OracleDs2Run(cfg, weights, context + steps + 1, order=O.ORDER_AVX512, threads=0)
+    rng = np.random.default_rng(SEED)
+    width = cfg.kv_lora_rank + cfg.rope_dim
+    for layer in range(cfg.n_layers):
+        r.set_cache_rows(layer, 0, rng.standard_normal((context, width), dtype=np.float32))
+    tok = 1
+    t0 = time.perf_counter()
+    for s in range(steps):
+        r.forward(tok, context + s)
+        rc, nxt, _ = r.lm_head()
+        tok = nxt if rc == 0 else 1
+    dt = time.perf_counter() - t0
+    threads = r.threads
+    r.close()
+    return steps / dt, dt, threads
+
+
+def ds2_reference_line(args, rank, metric, config):
+    """The reference arm of the DeepSeek2 lines: ds2_cpu_sample at the line's
+    context, min(K, 2) timed steps after one untimed (each takes seconds)."""
+    if rank != 0:
+        return
+    synth = cpu_synth()
+    cfg = synth.DS2_V2_LITE
+    weights = synth.ds2_weights(cfg, seed=SEED)
+    ds2_cpu_sample(cfg, weights, args.context, 1)
+    steps = max(1, min(args.steps, 2))
+    tok_s, dt, threads = ds2_cpu_sample(cfg, weights, args.context, steps)
+    sample = (f"{steps} decode step(s) of one sequence at context {args.context} (cache rows seeded), "
+              f"the reference's AVX-512 kernel order restated, {threads} threads, {dt:.1f} s")
+    print(json.dumps({
+        "impl": "reference", "metric": metric, "value": round(tok_s, 4), "unit": "tok/s", "n_gpus": 0,
+        "steps": steps, "warmup": 1, "ms_per_step": round(1000 * dt / steps, 1), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, same weights)",
+        "config": config,
+        "cpu_baseline": {"value": round(tok_s, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(tok_s, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def run_ds2(args, rank, world, local):
     """BASELINE config 3's model (27 layers, MLA kv_lora 512, 64 experts top-6 +
     2 shared, vocab 102400) decoding one sequence: the cache is filled to
     --context tokens by a seeded prompt, then K greedy steps are timed.  The
-    config's batch of 32 sequences and its expert parallelism are not in this
-    line (one sequence, one GPU)."""
+    config's batch of 32 sequences is --batch 32; under torchrun the experts
+    are sharded over the ranks (expert parallelism)."""
+    if args.impl == "reference":
+        ds2_reference_line(args, rank, DS2_METRIC,
+                           {"workload": "deepseek-v2-lite-shape mla+moe q4_0 decode, 1 sequence "
+                                        "(BASELINE config 3 model)", "context": args.context,
+                            "parallelism": "cpu threads"})
+        return
     import torch
 
     import zero_b200 as zb
     synth = synth_module(args)
 
-    if args.impl == "reference":
-        if rank == 0:
-            print(json.dumps({"impl": "reference", "unavailable": "the ds2 secondary line has no reference arm: "
-                              "the reference re-expands the latent cache per token (hours per step at "
-                              "context 2048); see cpu_baseline on the zero_b200 line"}), flush=True)
-        return
     cfg = synth.DS2_V2_LITE
     if world > 1:
         import datetime
@@ -406,20 +459,14 @@ def run_ds2(args, rank, world, local):
     cache_b = sum(cfg.cache_bytes_per_token() * (args.context + i + 1) for i in range(args.steps))
     launch_bytes = args.steps * step_w + cache_b
     gbs = launch_bytes / (dec_ms / 1000.0) / 1e9
-    # CPU baseline: the oracle's scalar restatement of the reference step
-    # (forward_pass.rs:703-909 re-expands every cached latent through kv_b),
-    # on a bounded sample: 2 steps after a 4-token prompt on the same weights
+    # CPU baseline: the reference's AVX-512 step restated, one step at the
+    # line's context (ds2_cpu_sample)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        import oracle as O
-
-        r = O.OracleDs2Run(cfg, weights, 8)
-        t0 = time.perf_counter()
-        rc, _, _, _ = r.generate(prompt[:4], 3)
-        dt = time.perf_counter() - t0
-        cpu = {"value": round(6 / dt, 4), "unit": "tok/s", "cores": 1, "kind": "port",
-               "sample": f"4-token prompt + 2 decode steps (6 forwards, context <= 6), scalar "
-                         f"restatement, 1 thread, {dt:.1f} s; rc={rc}"}
+        c_tok_s, dt, threads = ds2_cpu_sample(cfg, weights, args.context, 1)
+        cpu = {"value": round(c_tok_s, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": f"one decode step of one sequence at context {args.context} (cache rows seeded), "
+                         f"the reference's AVX-512 kernel order restated, {threads} threads, {dt:.1f} s"}
     if rank == 0:
         line = {
             "metric": DS2_METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world,
@@ -467,17 +514,18 @@ def run_ds2_batch(args, rank, world, local):
     seeded prompt and copied on the device to the others
     (zgpu_mla_kv_copy); each sequence then continues from its own seeded
     token.  A step is one batched greedy step of every sequence."""
+    if args.impl == "reference":
+        ds2_reference_line(args, rank, DS2_BATCH_METRIC,
+                           {"workload": f"deepseek-v2-lite-shape mla+moe q4_0 decode, {args.batch} sequences "
+                                        f"(BASELINE config 3)", "context": args.context, "batch": args.batch,
+                            "parallelism": "cpu threads (the reference decodes the sequences one forward "
+                                           "at a time)"})
+        return
     import torch
 
     import zero_b200 as zb
     synth = synth_module(args)
 
-    if args.impl == "reference":
-        if rank == 0:
-            print(json.dumps({"impl": "reference", "unavailable": "the ds2 secondary line has no reference arm: "
-                              "the reference re-expands the latent cache per token (hours per step at "
-                              "context 2048); see cpu_baseline on the zero_b200 line"}), flush=True)
-        return
     cfg = synth.DS2_V2_LITE
     n_seq = args.batch
     if world > 1:
@@ -555,16 +603,11 @@ def run_ds2_batch(args, rank, world, local):
     peaks = measured_peaks()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        import oracle as O
-
-        r = O.OracleDs2Run(cfg, weights, 8)
-        t0 = time.perf_counter()
-        rc, _, _, _ = r.generate(prompt[:4], 3)
-        dt = time.perf_counter() - t0
-        cpu = {"value": round(6 / dt, 4), "unit": "tok/s", "cores": 1, "kind": "port",
-               "sample": f"one sequence: 4-token prompt + 2 decode steps (6 forwards, context <= 6), "
-                         f"scalar restatement, 1 thread, {dt:.1f} s; rc={rc} (the reference decodes "
-                         f"concurrent sequences one forward at a time)"}
+        c_tok_s, dt, threads = ds2_cpu_sample(cfg, weights, args.context, 1)
+        cpu = {"value": round(c_tok_s, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": f"one decode step of one sequence at context {args.context} (cache rows seeded), "
+                         f"the reference's AVX-512 kernel order restated, {threads} threads, {dt:.1f} s "
+                         f"(the reference decodes concurrent sequences one forward at a time)"}
     if rank == 0:
         line = {
             "metric": DS2_BATCH_METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world,

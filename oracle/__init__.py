@@ -99,6 +99,10 @@ def _load() -> C.CDLL:
         "zo_mla_attention": (C.c_int, [_f32p, C.c_void_p, C.c_void_p, _f32p, C.c_uint32, C.c_uint32, _f32p,
                                        _f32p]),
         "zo_ds2_run_create": (C.c_void_p, [C.c_void_p, C.c_uint32]),
+        "zo_ds2_run_create_order": (C.c_void_p, [C.c_void_p, C.c_uint32, C.c_int, C.c_int, C.c_int]),
+        "zo_ds2_run_threads": (C.c_int, [C.c_void_p]),
+        "zo_ds2_run_set_cache_rows": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, _f32p]),
+        "zo_linear_plain_pool": (C.c_int, [C.c_void_p, _f32p, _u8p, _f32p, sz, sz, C.c_int, C.c_int]),
         "zo_ds2_run_destroy": (None, [C.c_void_p]),
         "zo_ds2_run_forward": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, _f32p]),
         "zo_ds2_run_lm_head": (C.c_int, [C.c_void_p, _u32p, _f32p]),
@@ -572,10 +576,15 @@ def mha_attention(x, lw: dict, cfg, k_cache: np.ndarray, v_cache: np.ndarray, po
 
 
 class OracleDs2Run:
-    """A DeepSeek2-shaped decode run on the CPU oracle (scalar crate order,
-    forward_pass.rs:703-909), over synth.ds2_weights() tensors."""
+    """A DeepSeek2-shaped decode run on the CPU oracle, over synth.ds2_weights()
+    tensors.  order: ORDER_SCALAR (the crate's scalar path,
+    forward_pass.rs:703-909; the parity oracle) or ORDER_AVX512 (its AVX-512
+    kernel path, inference_avx512.rs:2141-2825, the one the reference times),
+    the latter over a persistent pool of `threads` participants (<= 0: one per
+    physical core); simd 0 runs the lane emulation (same bits)."""
 
-    def __init__(self, cfg, weights, max_tokens: int):
+    def __init__(self, cfg, weights, max_tokens: int, order: int = ORDER_SCALAR, threads: int = 1,
+                 simd: int = 1):
         self._keep = weights
         self.cfg = cfg
         self.max_tokens = max_tokens
@@ -599,9 +608,21 @@ class OracleDs2Run:
                        Q8_0 if cfg.embd_quant == "q8_0" else Q4_0, weights["token_embd"].ctypes.data,
                        Q8_0 if cfg.output_quant == "q8_0" else Q4_0, weights["output"].ctypes.data,
                        weights["output_norm"].ctypes.data, self._layers, cfg.kv_heads)
-        self._r = LIB.zo_ds2_run_create(C.byref(self._m), max_tokens)
+        self._r = LIB.zo_ds2_run_create_order(C.byref(self._m), max_tokens, order, threads, simd)
         if not self._r:
             raise MemoryError("oracle ds2 run allocation failed")
+        self.order = order
+
+    @property
+    def threads(self) -> int:
+        return LIB.zo_ds2_run_threads(self._r)
+
+    def set_cache_rows(self, layer: int, t0: int, rows: np.ndarray):
+        """Cached latent rows [t0, t0 + len(rows)) of one layer := rows [n, kv_lora + rope]."""
+        rows = np.ascontiguousarray(rows, np.float32)
+        rc = LIB.zo_ds2_run_set_cache_rows(self._r, layer, t0, rows.shape[0], _f(rows))
+        if rc:
+            raise ValueError(f"oracle ds2 cache rows refused: {rc}")
 
     def close(self):
         if self._r:

@@ -497,6 +497,42 @@ __attribute__((target("avx512f,fma"))) static void rows4_q8_avx512(
   }
   for (int r = 0; r < 4; ++r) out4[r] = hsum512(_mm512_add_ps(lo[r], hi[r]));
 }
+
+/* The plain-layout single-row bodies (linear.rs:710-859 / :1271-1402) as
+ * real AVX-512: one row of 18- (Q4_0) or 34-byte (Q8_0) blocks, the same
+ * lane sequence as row_q4_emul / row_q8_emul. */
+__attribute__((target("avx512f,fma"))) static float row_q4_plain_avx512(const float *x, size_t bpr,
+                                                                        const uint8_t *row) {
+  const __m512i m = _mm512_set1_epi32(0x0F);
+  const __m512 b8 = _mm512_set1_ps(8.0f);
+  __m512 lo = _mm512_setzero_ps(), hi = _mm512_setzero_ps();
+  for (size_t b = 0; b < bpr; ++b) {
+    const uint8_t *blk = row + b * 18;
+    __m512 xl = _mm512_loadu_ps(x + b * 32), xh = _mm512_loadu_ps(x + b * 32 + 16);
+    __m512 d = _mm512_set1_ps(zo_fp16_to_f32(rd16(blk)));
+    __m512i by = _mm512_cvtepu8_epi32(_mm_loadu_si128((const __m128i *)(blk + 2)));
+    __m512 l = _mm512_cvtepi32_ps(_mm512_and_epi32(by, m));
+    __m512 h = _mm512_cvtepi32_ps(_mm512_and_epi32(_mm512_srli_epi32(by, 4), m));
+    lo = _mm512_fmadd_ps(xl, _mm512_mul_ps(d, _mm512_sub_ps(l, b8)), lo);
+    hi = _mm512_fmadd_ps(xh, _mm512_mul_ps(d, _mm512_sub_ps(h, b8)), hi);
+  }
+  return hsum512(_mm512_add_ps(lo, hi));
+}
+
+__attribute__((target("avx512f,fma"))) static float row_q8_plain_avx512(const float *x, size_t bpr,
+                                                                        const uint8_t *row) {
+  __m512 lo = _mm512_setzero_ps(), hi = _mm512_setzero_ps();
+  for (size_t b = 0; b < bpr; ++b) {
+    const uint8_t *blk = row + b * 34;
+    __m512 xl = _mm512_loadu_ps(x + b * 32), xh = _mm512_loadu_ps(x + b * 32 + 16);
+    __m512 d = _mm512_set1_ps(zo_fp16_to_f32(rd16(blk)));
+    __m512 l = _mm512_cvtepi32_ps(_mm512_cvtepi8_epi32(_mm_loadu_si128((const __m128i *)(blk + 2))));
+    __m512 h = _mm512_cvtepi32_ps(_mm512_cvtepi8_epi32(_mm_loadu_si128((const __m128i *)(blk + 18))));
+    lo = _mm512_fmadd_ps(xl, _mm512_mul_ps(d, l), lo);
+    hi = _mm512_fmadd_ps(xh, _mm512_mul_ps(d, h), hi);
+  }
+  return hsum512(_mm512_add_ps(lo, hi));
+}
 #endif
 
 int zo_have_avx512(void) {
@@ -732,6 +768,45 @@ static void zo_pool_run(struct zo_pool *p, size_t units, zo_part_fn fn, void *ct
   zo_range_for(units, p->n, 0, &u0, &u1);
   if (u0 < u1) fn(ctx, u0, u1, 0);
   while (atomic_load_explicit(&p->arrived, memory_order_acquire) < p->n - 1) _mm_pause();
+}
+
+typedef struct {
+  const float *x;
+  const uint8_t *w;
+  float *out;
+  size_t bpr;
+  int quant, simd;
+} zo_plain_ctx;
+
+static void plain_rows_part(void *p, size_t i0, size_t i1, int part) {
+  (void)part;
+  const zo_plain_ctx *c = (const zo_plain_ctx *)p;
+  const size_t rb = c->bpr * (c->quant == ZO_Q4_0 ? 18 : 34);
+  for (size_t i = i0; i < i1; ++i) {
+    const uint8_t *row = c->w + i * rb;
+#if defined(__x86_64__)
+    if (c->simd) {
+      c->out[i] = c->quant == ZO_Q4_0 ? row_q4_plain_avx512(c->x, c->bpr, row)
+                                      : row_q8_plain_avx512(c->x, c->bpr, row);
+      continue;
+    }
+#endif
+    c->out[i] = c->quant == ZO_Q4_0 ? row_q4_emul(c->x, c->bpr, row, 18, 0, 2)
+                                    : row_q8_emul(c->x, c->bpr, row, 34, 0, 2);
+  }
+}
+
+/* linear_dispatch_avx512 (inference_avx512.rs:1147) on plain Q4_0 / Q8_0
+ * rows (the DeepSeek2 tensors): rows split over the pool's participants
+ * (a null pool: the calling thread alone); each row's arithmetic is the
+ * single-row AVX-512 body, so the split does not change any bit. */
+int zo_linear_plain_pool(zo_pool *p, const float *x, const uint8_t *w, float *out, size_t in_dim,
+                         size_t out_dim, int quant, int simd) {
+  if (quant != ZO_Q4_0 && quant != ZO_Q8_0) return ZO_ERR_UNSUPPORTED_QUANT;
+  if (in_dim % 32) return ZO_ERR_ARG;
+  zo_plain_ctx c = {x, w, out, in_dim / 32, quant, simd && zo_have_avx512()};
+  zo_pool_run(p, out_dim, plain_rows_part, &c);
+  return ZO_OK;
 }
 
 typedef struct {

@@ -170,6 +170,10 @@ typedef struct zo_pool zo_pool;
 zo_pool *zo_pool_create(int threads);
 void     zo_pool_destroy(zo_pool *p);
 int      zo_pool_size(const zo_pool *p);
+/* linear_dispatch_avx512 on plain Q4_0 / Q8_0 rows over the pool (NULL: the
+ * calling thread); simd 0 runs the lane emulation (same bits). */
+int      zo_linear_plain_pool(zo_pool *p, const float *x, const uint8_t *w, float *out,
+                              size_t in_dim, size_t out_dim, int quant, int simd);
 
 typedef struct zo_run zo_run;
 zo_run *zo_run_create(const zo_qwen3 *m, uint32_t max_tokens, int order, int threads, int simd);
@@ -271,7 +275,18 @@ int zo_mha_attention(const float *x, const uint8_t *wq, const uint8_t *wk, const
                      float *v_cache, uint32_t pos, uint32_t max_tokens, float *work, float *out);
 
 typedef struct zo_ds2_run zo_ds2_run;
+/* The scalar crate order. */
 zo_ds2_run *zo_ds2_run_create(const zo_ds2 *m, uint32_t max_tokens);
+/* order 0: the scalar crate order; 1: the crate's AVX-512 kernel order
+ * (inference_avx512.rs:2141-2825) over a persistent pool of `threads`
+ * participants (<= 0: one per physical core); simd 0 runs its lane
+ * emulation (same bits). */
+zo_ds2_run *zo_ds2_run_create_order(const zo_ds2 *m, uint32_t max_tokens, int order, int threads,
+                                    int simd);
+int     zo_ds2_run_threads(const zo_ds2_run *r);
+/* cached latent rows [t0, t0 + n) of one layer := rows ([n][kv_lora | rope]) */
+int     zo_ds2_run_set_cache_rows(zo_ds2_run *r, uint32_t layer, uint32_t t0, uint32_t n,
+                                  const float *rows);
 void    zo_ds2_run_destroy(zo_ds2_run *r);
 /* forward_pass.rs:703-909 */
 int     zo_ds2_run_forward(zo_ds2_run *r, uint32_t token, uint32_t pos, float *hidden_out);

@@ -6,7 +6,9 @@
  * multiply and add separately rounded (compiled with -ffp-contract=off),
  * sequential loops exactly as the Rust source writes them, libm
  * expf/sinf/cosf/powf/sqrtf through glibc.  Each function cites the
- * reference lines it restates.
+ * reference lines it restates.  A run can instead take the crate's AVX-512
+ * kernel order (inference_avx512.rs:2141-2825), the path the reference
+ * times: see ds2_ops below.
  */
 #define _GNU_SOURCE
 #include "zoracle.h"
@@ -14,6 +16,29 @@
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
+
+/* The two arithmetic orders of the DeepSeek2 step.  NULL / avx == 0: the
+ * scalar crate path (mla.rs, moe.rs, forward_pass.rs:703-909).  avx == 1:
+ * forward_single_token_deepseek2_avx512 (inference_avx512.rs:2611-2825),
+ * which differs in exactly these places: every matmul is
+ * linear_dispatch_avx512 (16-lane accumulators, rows split over the SMP
+ * pool), mla_attention_avx512 (:2301-2577) scores each cached token as
+ * dot_product_f32_avx512(q_nope, k_nope) + dot_product_f32_avx512(q_rope,
+ * k_rope) and accumulates the context with weighted_add_f32_avx512,
+ * moe_ffn_avx512 (:2195-2290) adds each routed expert with
+ * weighted_add_f32_avx512, and the SwiGLU activations (expert_swiglu_avx512
+ * :2141-2186, the dense FFN) run silu_mul_avx512.  RMSNorm, RoPE, softmax,
+ * routing and the MHA layers stay scalar there too. */
+typedef struct {
+  int avx, simd;
+  zo_pool *pool;
+} ds2_ops;
+
+static int ops_lin(const ds2_ops *o, const float *x, const uint8_t *w, float *out, size_t in_dim,
+                   size_t out_dim, int quant) {
+  if (o && o->avx) return zo_linear_plain_pool(o->pool, x, w, out, in_dim, out_dim, quant, o->simd);
+  return zo_linear_dispatch(x, w, out, in_dim, out_dim, quant);
+}
 
 /* moe.rs:65-85 (normalised_expert_weight_scale / apply_expert_weight_scale):
  * a non-finite or non-positive scale means 1.0; a scale of exactly 1.0 is
@@ -116,18 +141,28 @@ int zo_moe_route_f32(const float *hidden, size_t dim, const float *router_w,
 /* moe.rs:345-397 (expert_swiglu): gate and up projections, silu(g) =
  * g / (1 + expf(-g)), h = silu * up, then the down projection.
  * work: 3 * inter floats. */
+static int expert_swiglu_ops(const ds2_ops *o, const float *x, const uint8_t *gate_w,
+                             const uint8_t *up_w, const uint8_t *down_w, size_t dim, size_t inter,
+                             int quant, float *work, float *out) {
+  float *g = work, *u = work + inter, *h = work + 2 * inter;
+  int st;
+  if ((st = ops_lin(o, x, gate_w, g, dim, inter, quant))) return st;
+  if ((st = ops_lin(o, x, up_w, u, dim, inter, quant))) return st;
+  if (o && o->avx) {
+    zo_silu_mul_avx512(g, u, h, inter);
+  } else {
+    for (size_t i = 0; i < inter; ++i) {
+      float silu = g[i] / (1.0f + expf(-g[i]));
+      h[i] = silu * u[i];
+    }
+  }
+  return ops_lin(o, h, down_w, out, inter, dim, quant);
+}
+
 int zo_expert_swiglu(const float *x, const uint8_t *gate_w, const uint8_t *up_w,
                      const uint8_t *down_w, size_t dim, size_t inter, int quant, float *work,
                      float *out) {
-  float *g = work, *u = work + inter, *h = work + 2 * inter;
-  int st;
-  if ((st = zo_linear_dispatch(x, gate_w, g, dim, inter, quant))) return st;
-  if ((st = zo_linear_dispatch(x, up_w, u, dim, inter, quant))) return st;
-  for (size_t i = 0; i < inter; ++i) {
-    float silu = g[i] / (1.0f + expf(-g[i]));
-    h[i] = silu * u[i];
-  }
-  return zo_linear_dispatch(h, down_w, out, inter, dim, quant);
+  return expert_swiglu_ops(NULL, x, gate_w, up_w, down_w, dim, inter, quant, work, out);
 }
 
 static size_t quant_row_bytes(size_t cols, int quant) {
@@ -147,12 +182,12 @@ static size_t quant_row_bytes(size_t cols, int quant) {
  * n_shared SwiGLUs of width inter, so this is DeepSeek-V2-Lite's "2 shared
  * experts".  n_shared == 0 starts from out = 0.
  * work: n_experts + 3 * inter + dim floats. */
-int zo_moe_ffn(const float *x, const float *router_w, const float *router_bias,
-               const uint8_t *gate_exps, const uint8_t *up_exps, const uint8_t *down_exps,
-               const uint8_t *gate_sh, const uint8_t *up_sh, const uint8_t *down_sh,
-               size_t n_shared, size_t n_experts, size_t top_k, size_t dim, size_t inter,
-               int quant, int mode, float expert_weight_scale, float *work, uint32_t *ids_out,
-               float *weights_out, float *out) {
+static int moe_ffn_ops(const ds2_ops *o, const float *x, const float *router_w,
+                       const float *router_bias, const uint8_t *gate_exps, const uint8_t *up_exps,
+                       const uint8_t *down_exps, const uint8_t *gate_sh, const uint8_t *up_sh,
+                       const uint8_t *down_sh, size_t n_shared, size_t n_experts, size_t top_k,
+                       size_t dim, size_t inter, int quant, int mode, float expert_weight_scale,
+                       float *work, uint32_t *ids_out, float *weights_out, float *out) {
   if (top_k == 0 || top_k > n_experts) return ZO_ERR_ARG;
   if (quant != ZO_Q4_0 && quant != ZO_Q8_0) return ZO_ERR_UNSUPPORTED_QUANT;
   float *scores = work, *sw = work + n_experts, *eo = sw + 3 * inter;
@@ -164,8 +199,8 @@ int zo_moe_ffn(const float *x, const float *router_w, const float *router_bias,
   if (n_shared == 0) memset(out, 0, dim * sizeof(float));
   for (size_t s = 0; s < n_shared; ++s) {
     float *dst = s == 0 ? out : eo;
-    if ((st = zo_expert_swiglu(x, gate_sh + s * gu_bytes, up_sh + s * gu_bytes,
-                               down_sh + s * dn_bytes, dim, inter, quant, sw, dst)))
+    if ((st = expert_swiglu_ops(o, x, gate_sh + s * gu_bytes, up_sh + s * gu_bytes,
+                                down_sh + s * dn_bytes, dim, inter, quant, sw, dst)))
       return st;
     if (s > 0)
       for (size_t i = 0; i < dim; ++i) out[i] += eo[i];
@@ -173,12 +208,26 @@ int zo_moe_ffn(const float *x, const float *router_w, const float *router_bias,
   for (size_t k = 0; k < top_k; ++k) {
     size_t e = ids_out[k];
     float w = weights_out[k];
-    if ((st = zo_expert_swiglu(x, gate_exps + e * gu_bytes, up_exps + e * gu_bytes,
-                               down_exps + e * dn_bytes, dim, inter, quant, sw, eo)))
+    if ((st = expert_swiglu_ops(o, x, gate_exps + e * gu_bytes, up_exps + e * gu_bytes,
+                                down_exps + e * dn_bytes, dim, inter, quant, sw, eo)))
       return st;
-    for (size_t i = 0; i < dim; ++i) out[i] += w * eo[i];
+    if (o && o->avx)
+      zo_weighted_add_avx512(w, eo, out, dim);
+    else
+      for (size_t i = 0; i < dim; ++i) out[i] += w * eo[i];
   }
   return ZO_OK;
+}
+
+int zo_moe_ffn(const float *x, const float *router_w, const float *router_bias,
+               const uint8_t *gate_exps, const uint8_t *up_exps, const uint8_t *down_exps,
+               const uint8_t *gate_sh, const uint8_t *up_sh, const uint8_t *down_sh,
+               size_t n_shared, size_t n_experts, size_t top_k, size_t dim, size_t inter,
+               int quant, int mode, float expert_weight_scale, float *work, uint32_t *ids_out,
+               float *weights_out, float *out) {
+  return moe_ffn_ops(NULL, x, router_w, router_bias, gate_exps, up_exps, down_exps, gate_sh, up_sh,
+                     down_sh, n_shared, n_experts, top_k, dim, inter, quant, mode,
+                     expert_weight_scale, work, ids_out, weights_out, out);
 }
 
 /* mla.rs:169-171 / :199-213: NeoX half-split rotation of one rope slice,
@@ -219,9 +268,9 @@ size_t zo_mla_work_floats(const zo_mla_dims *d, uint32_t max_tokens) {
  * With w->k_b and w->v_b both set, the split projections are used instead
  * of kv_b (mla.rs:251-275).  cache_layer is this layer's slice of the
  * cache; work: zo_mla_work_floats floats. */
-int zo_mla_attention(const float *x, const zo_mla_weights *w, const zo_mla_dims *d,
-                     float *cache_layer, uint32_t pos, uint32_t max_tokens, float *work,
-                     float *out) {
+static int mla_attention_ops(const ds2_ops *o, const float *x, const zo_mla_weights *w,
+                             const zo_mla_dims *d, float *cache_layer, uint32_t pos,
+                             uint32_t max_tokens, float *work, float *out) {
   const size_t H = d->hidden, R = d->kv_lora_rank, RD = d->rope_dim, NH = d->n_heads;
   const size_t NO = d->nope_dim, VD = d->v_dim, QL = d->q_lora_rank;
   const size_t kv_a_out = R + RD, nv = NO + VD, tk = NO + RD;
@@ -233,7 +282,7 @@ int zo_mla_attention(const float *x, const zo_mla_weights *w, const zo_mla_dims 
         *c_qn = c_q + QL, *q = c_qn + QL, *score = q + qb_out, *concat = score + NH * max_tokens;
   const size_t tstride = R + RD, total = (size_t)pos + 1;
   int st;
-  if ((st = zo_linear_dispatch(x, w->kv_a_mqa, kv_a, H, kv_a_out, quant))) return st;
+  if ((st = ops_lin(o, x, w->kv_a_mqa, kv_a, H, kv_a_out, quant))) return st;
   zo_rmsnorm(kv_a, w->kv_a_norm, c_kv, R, d->eps);
   {
     float *kr = kv_a + R;
@@ -248,25 +297,30 @@ int zo_mla_attention(const float *x, const zo_mla_weights *w, const zo_mla_dims 
   }
   memcpy(cache_layer + (size_t)pos * tstride, c_kv, R * sizeof(float));
   memcpy(cache_layer + (size_t)pos * tstride + R, kv_a + R, RD * sizeof(float));
-  if ((st = zo_linear_dispatch(x, w->q_a, c_q, H, QL, quant))) return st;
+  if ((st = ops_lin(o, x, w->q_a, c_q, H, QL, quant))) return st;
   zo_rmsnorm(c_q, w->q_a_norm, c_qn, QL, d->eps);
-  if ((st = zo_linear_dispatch(c_qn, w->q_b, q, QL, qb_out, quant))) return st;
+  if ((st = ops_lin(o, c_qn, w->q_b, q, QL, qb_out, quant))) return st;
   for (size_t h = 0; h < NH; ++h) mla_rope(q + h * tk + NO, RD, pos, d->rope_base);
   const float scale = 1.0f / sqrtf((float)tk);
   for (size_t t = 0; t < total; ++t) {
     const float *ct = cache_layer + t * tstride, *krt = ct + R;
     if (split) {
-      if ((st = zo_linear_dispatch(ct, w->k_b, kvd, R, kn_out, quant))) return st;
-      if ((st = zo_linear_dispatch(ct, w->v_b, kvd + kn_out, R, v_out, quant))) return st;
-    } else if ((st = zo_linear_dispatch(ct, w->kv_b, kvd, R, kvb_out, quant))) {
+      if ((st = ops_lin(o, ct, w->k_b, kvd, R, kn_out, quant))) return st;
+      if ((st = ops_lin(o, ct, w->v_b, kvd + kn_out, R, v_out, quant))) return st;
+    } else if ((st = ops_lin(o, ct, w->kv_b, kvd, R, kvb_out, quant))) {
       return st;
     }
     for (size_t h = 0; h < NH; ++h) {
       const float *qn = q + h * tk, *qr = qn + NO;
       const float *kn = split ? kvd + h * NO : kvd + h * nv;
-      float dot = 0.0f;
-      for (size_t i = 0; i < NO; ++i) dot += qn[i] * kn[i];
-      for (size_t i = 0; i < RD; ++i) dot += qr[i] * krt[i];
+      float dot;
+      if (o && o->avx) {
+        dot = zo_dot_product_avx512(qn, kn, NO) + zo_dot_product_avx512(qr, krt, RD);
+      } else {
+        dot = 0.0f;
+        for (size_t i = 0; i < NO; ++i) dot += qn[i] * kn[i];
+        for (size_t i = 0; i < RD; ++i) dot += qr[i] * krt[i];
+      }
       score[h * max_tokens + t] = dot * scale;
     }
   }
@@ -276,18 +330,27 @@ int zo_mla_attention(const float *x, const zo_mla_weights *w, const zo_mla_dims 
   for (size_t t = 0; t < total; ++t) {
     const float *ct = cache_layer + t * tstride;
     if (split) {
-      if ((st = zo_linear_dispatch(ct, w->k_b, kvd, R, kn_out, quant))) return st;
-      if ((st = zo_linear_dispatch(ct, w->v_b, kvd + kn_out, R, v_out, quant))) return st;
-    } else if ((st = zo_linear_dispatch(ct, w->kv_b, kvd, R, kvb_out, quant))) {
+      if ((st = ops_lin(o, ct, w->k_b, kvd, R, kn_out, quant))) return st;
+      if ((st = ops_lin(o, ct, w->v_b, kvd + kn_out, R, v_out, quant))) return st;
+    } else if ((st = ops_lin(o, ct, w->kv_b, kvd, R, kvb_out, quant))) {
       return st;
     }
     for (size_t h = 0; h < NH; ++h) {
       const float *vh = split ? kvd + kn_out + h * VD : kvd + h * nv + NO;
       float p = score[h * max_tokens + t];
-      for (size_t i = 0; i < VD; ++i) concat[h * VD + i] += p * vh[i];
+      if (o && o->avx)
+        zo_weighted_add_avx512(p, vh, concat + h * VD, VD);
+      else
+        for (size_t i = 0; i < VD; ++i) concat[h * VD + i] += p * vh[i];
     }
   }
-  return zo_linear_dispatch(concat, w->output, out, v_out, H, quant);
+  return ops_lin(o, concat, w->output, out, v_out, H, quant);
+}
+
+int zo_mla_attention(const float *x, const zo_mla_weights *w, const zo_mla_dims *d,
+                     float *cache_layer, uint32_t pos, uint32_t max_tokens, float *work,
+                     float *out) {
+  return mla_attention_ops(NULL, x, w, d, cache_layer, pos, max_tokens, work, out);
 }
 
 size_t zo_mha_work_floats(const zo_mla_dims *d, uint32_t n_kv, uint32_t max_tokens) {
@@ -360,13 +423,24 @@ struct zo_ds2_run {
   size_t mha_k_block, mha_v_block;
   uint32_t *ids;         /* [L][top_k] experts of the last forward (0 for dense layers) */
   float *wts;            /* [L][top_k] */
+  ds2_ops ops;           /* arithmetic order (and the AVX-512 order's pool) */
 };
 
-zo_ds2_run *zo_ds2_run_create(const zo_ds2 *m, uint32_t max_tokens) {
+zo_ds2_run *zo_ds2_run_create_order(const zo_ds2 *m, uint32_t max_tokens, int order, int threads,
+                                    int simd) {
   zo_ds2_run *r = (zo_ds2_run *)calloc(1, sizeof(zo_ds2_run));
   if (!r) return NULL;
   r->m = m;
   r->max_tokens = max_tokens;
+  r->ops.avx = order == 1;
+  r->ops.simd = simd;
+  if (r->ops.avx) {
+    r->ops.pool = zo_pool_create(threads);
+    if (!r->ops.pool) {
+      free(r);
+      return NULL;
+    }
+  }
   const zo_mla_dims *d = &m->mla;
   size_t H = d->hidden;
   size_t inter = m->ffn > m->expert_ffn ? m->ffn : m->expert_ffn;
@@ -397,12 +471,30 @@ zo_ds2_run *zo_ds2_run_create(const zo_ds2 *m, uint32_t max_tokens) {
   return r;
 }
 
+zo_ds2_run *zo_ds2_run_create(const zo_ds2 *m, uint32_t max_tokens) {
+  return zo_ds2_run_create_order(m, max_tokens, 0, 1, 0);
+}
+
 void zo_ds2_run_destroy(zo_ds2_run *r) {
   if (!r) return;
   free(r->cache); free(r->hidden); free(r->norm); free(r->attn_out); free(r->mlp_out);
   free(r->logits); free(r->mla_work); free(r->ffn_work); free(r->ids); free(r->wts);
   free(r->mha_cache); free(r->mha_work);
+  zo_pool_destroy(r->ops.pool);
   free(r);
+}
+
+int zo_ds2_run_threads(const zo_ds2_run *r) { return r->ops.avx ? zo_pool_size(r->ops.pool) : 1; }
+
+/* Overwrite cached latent rows [t0, t0 + n) of one MLA layer with `rows`
+ * ([n][kv_lora | rope]): a cache at a given context without decoding every
+ * token first (what a step costs depends on the context, not the values). */
+int zo_ds2_run_set_cache_rows(zo_ds2_run *r, uint32_t layer, uint32_t t0, uint32_t n, const float *rows) {
+  const zo_mla_dims *d = &r->m->mla;
+  const size_t ts = d->kv_lora_rank + d->rope_dim;
+  if (layer >= r->m->n_layers || (uint64_t)t0 + n > r->max_tokens) return ZO_ERR_ARG;
+  memcpy(r->cache + ((size_t)layer * r->max_tokens + t0) * ts, rows, (size_t)n * ts * sizeof(float));
+  return ZO_OK;
 }
 
 const float *zo_ds2_run_cache(const zo_ds2_run *r) { return r->cache; }
@@ -446,8 +538,8 @@ int zo_ds2_run_forward(zo_ds2_run *r, uint32_t token, uint32_t pos, float *hidde
         return st;
     } else {
       float *cl = r->cache + (size_t)li * r->max_tokens * tstride;
-      if ((st = zo_mla_attention(r->norm, &L->mla, d, cl, pos, r->max_tokens, r->mla_work,
-                                 r->attn_out)))
+      if ((st = mla_attention_ops(&r->ops, r->norm, &L->mla, d, cl, pos, r->max_tokens, r->mla_work,
+                                  r->attn_out)))
         return st;
     }
     for (size_t i = 0; i < H; ++i) r->hidden[i] += r->attn_out[i];
@@ -456,22 +548,26 @@ int zo_ds2_run_forward(zo_ds2_run *r, uint32_t token, uint32_t pos, float *hidde
       float *g = r->ffn_work, *u = g + F, *h = u + F;
       /* mlp_swiglu_dispatch needs 3 * ffn floats: ffn_work holds
        * n_experts + 3 * max(ffn, expert_ffn) + H */
-      if ((st = zo_linear_dispatch(r->norm, L->ffn_gate, g, H, F, d->quant))) return st;
-      if ((st = zo_linear_dispatch(r->norm, L->ffn_up, u, H, F, d->quant))) return st;
-      for (size_t i = 0; i < F; ++i) g[i] = g[i] / (1.0f + expf(-g[i]));
-      for (size_t i = 0; i < F; ++i) h[i] = g[i] * u[i];
-      if ((st = zo_linear_dispatch(h, L->ffn_down, r->mlp_out, F, H, d->quant))) return st;
+      if ((st = ops_lin(&r->ops, r->norm, L->ffn_gate, g, H, F, d->quant))) return st;
+      if ((st = ops_lin(&r->ops, r->norm, L->ffn_up, u, H, F, d->quant))) return st;
+      if (r->ops.avx) {
+        zo_silu_mul_avx512(g, u, h, F);
+      } else {
+        for (size_t i = 0; i < F; ++i) g[i] = g[i] / (1.0f + expf(-g[i]));
+        for (size_t i = 0; i < F; ++i) h[i] = g[i] * u[i];
+      }
+      if ((st = ops_lin(&r->ops, h, L->ffn_down, r->mlp_out, F, H, d->quant))) return st;
       for (size_t k = 0; k < m->top_k; ++k) {
         r->ids[(size_t)li * m->top_k + k] = 0;
         r->wts[(size_t)li * m->top_k + k] = 0.0f;
       }
     } else {
       memset(r->mlp_out, 0, H * sizeof(float));
-      if ((st = zo_moe_ffn(r->norm, L->router_w, L->router_b, L->gate_exps, L->up_exps,
-                           L->down_exps, L->gate_shexp, L->up_shexp, L->down_shexp, m->n_shared,
-                           m->n_experts, m->top_k, H, m->expert_ffn, d->quant, m->route_mode,
-                           m->expert_weight_scale, r->ffn_work, r->ids + (size_t)li * m->top_k,
-                           r->wts + (size_t)li * m->top_k, r->mlp_out)))
+      if ((st = moe_ffn_ops(&r->ops, r->norm, L->router_w, L->router_b, L->gate_exps, L->up_exps,
+                            L->down_exps, L->gate_shexp, L->up_shexp, L->down_shexp, m->n_shared,
+                            m->n_experts, m->top_k, H, m->expert_ffn, d->quant, m->route_mode,
+                            m->expert_weight_scale, r->ffn_work, r->ids + (size_t)li * m->top_k,
+                            r->wts + (size_t)li * m->top_k, r->mlp_out)))
         return st;
     }
     for (size_t i = 0; i < H; ++i) r->hidden[i] += r->mlp_out[i];
@@ -485,7 +581,7 @@ int zo_ds2_run_lm_head(zo_ds2_run *r, uint32_t *token_out, float *logits_out) {
   const zo_ds2 *m = r->m;
   size_t H = m->mla.hidden, V = m->vocab_padded;
   zo_rmsnorm(r->hidden, m->output_norm, r->norm, H, m->mla.eps);
-  int st = zo_linear_dispatch(r->norm, m->output, r->logits, H, V, m->output_quant);
+  int st = ops_lin(&r->ops, r->norm, m->output, r->logits, H, V, m->output_quant);
   if (st) return st;
   float mx = -INFINITY;
   size_t idx = 0;

@@ -433,3 +433,64 @@ def test_ds2_generate_is_deterministic():
     a = O.OracleDs2Run(cfg, w, 16).generate(prompt, 6)
     b = O.OracleDs2Run(cfg, w, 16).generate(prompt, 6)
     assert a[0] == 0 and np.array_equal(a[1], b[1]) and np.array_equal(a[2], b[2])
+
+
+# ---- the AVX-512 kernel order (inference_avx512.rs:2141-2825): the path the
+# reference times, used for the config-3 CPU baseline
+
+@pytest.mark.parametrize("variant", [dict(), dict(split_kv_b=True), dict(n_shared=0)])
+def test_ds2_avx512_order_tracks_the_scalar_order(variant):
+    """The AVX-512 order (16-lane matmul and dot accumulators, fused
+    weighted adds, the polynomial SiLU) differs from the scalar crate order
+    only in the last bits: same greedy tokens and expert ids, logits within
+    1e-5."""
+    kw = dict(n_layers=2, hidden=256, ffn=512, n_heads=2, n_experts=8, top_k=3, expert_ffn=128, n_shared=2,
+              vocab=256)
+    kw.update(variant)
+    cfg = synth.ds2_small_config(**kw)
+    w = synth.ds2_weights(cfg, seed=11, norm_sigma=0.1)
+    prompt = synth.ds2_prompt_ids(cfg, 5, seed=11)
+    a = O.OracleDs2Run(cfg, w, 16)
+    b = O.OracleDs2Run(cfg, w, 16, order=O.ORDER_AVX512, threads=2)
+    ra, rb = a.generate(prompt, 6, want_logits=True), b.generate(prompt, 6, want_logits=True)
+    assert ra[0] == 0 and rb[0] == 0
+    assert np.array_equal(ra[1], rb[1])
+    assert np.array_equal(a.expert_ids()[0], b.expert_ids()[0])
+    for s in range(6):
+        assert rel_l2(rb[3][s], ra[3][s]) < 1e-5, s
+
+
+def test_ds2_avx512_order_bits_do_not_depend_on_threads_or_simd():
+    """Rows are independent, so the pool's split leaves every bit as it is,
+    and the intrinsics reproduce the lane emulation exactly."""
+    cfg = small_cfg()
+    w = synth.ds2_weights(cfg, seed=12, norm_sigma=0.1)
+    prompt = synth.ds2_prompt_ids(cfg, 4, seed=12)
+    runs = [O.OracleDs2Run(cfg, w, 16, order=O.ORDER_AVX512, threads=t, simd=s) for t, s in ((1, 0), (1, 1), (3, 1))]
+    outs = [r.generate(prompt, 5, want_logits=True) for r in runs]
+    for o in outs[1:]:
+        assert np.array_equal(o[1], outs[0][1])
+        assert np.array_equal(o[3].view(np.uint32), outs[0][3].view(np.uint32))
+    assert runs[2].threads == 3
+
+
+def test_ds2_cache_rows_set_a_context_without_decoding_it():
+    """A cache filled row by row from the decode equals one written by
+    set_cache_rows from those rows: the next step's logits are identical."""
+    cfg = small_cfg()
+    w = synth.ds2_weights(cfg, seed=13, norm_sigma=0.1)
+    prompt = synth.ds2_prompt_ids(cfg, 6, seed=13)
+    a = O.OracleDs2Run(cfg, w, 16)
+    for pos, t in enumerate(prompt):
+        a.forward(int(t), pos)
+    rows = a.cache()
+    b = O.OracleDs2Run(cfg, w, 16)
+    for layer in range(cfg.n_layers):
+        b.set_cache_rows(layer, 0, rows[layer, :len(prompt)])
+    a.forward(7, len(prompt))
+    b.forward(7, len(prompt))
+    assert np.array_equal(a.lm_head()[2].view(np.uint32), b.lm_head()[2].view(np.uint32))
+    with pytest.raises(ValueError):
+        b.set_cache_rows(cfg.n_layers, 0, rows[0, :1])
+    with pytest.raises(ValueError):
+        b.set_cache_rows(0, 15, rows[0, :2])
