@@ -305,7 +305,9 @@ void zgpu_qwen3_destroy(zgpu_model *m);
  * Requires n_kv_heads, hidden / 8, ffn / 8 and the LM-head units to divide by
  * world.  After creating every rank: zgpu_qwen3_tp_export on each, exchange
  * the handles (ZGPU_IPC_HANDLE_BYTES each, rank order), then
- * zgpu_qwen3_tp_connect on each.  A rank decodes through
+ * zgpu_qwen3_tp_connect on each, then a host barrier over the ranks (the
+ * kernel's waits for a peer are bounded: no rank may start decoding while
+ * another is still mapping handles).  A rank decodes through
  * zgpu_generate_greedy, or token by token through zgpu_forward_single_token
  * followed by zgpu_lm_head_argmax (all ranks make the same calls with the
  * same arguments, in the same order); logits_out then receives the rank's
