@@ -781,10 +781,12 @@ BATCH_METRIC = "decode tok/s (all sequences), Qwen3-8B-shape Q4_0, batch B, cont
 def run_qwen3_batch(args, rank, world, local):
     """BASELINE config 2 at batch B (16): B sequences, each cache filled to
     4096 seeded tokens (zgpu_prefill_batch, four sequences at a time), then K
-    greedy steps of all B sequences at once (zgpu_decode_batch: tcgen05 int8
-    projections and LM head over Q8_0 activation rows, the decode attention
-    with a sequence grid dimension).  One GPU; value = B x K tokens over the
-    device time of the K steps."""
+    greedy steps of all B sequences at once (zgpu_decode_batch: projections
+    and LM head on the exact tensor-core matvec, which multiplies the f32
+    activations' integer digits by int8 weight tiles and reproduces the
+    single-token GEMV bit for bit; the decode attention with a sequence grid
+    dimension).  One GPU; value = B x K tokens over the device time of the K
+    steps."""
     synth = synth_module(args)
 
     cfg = synth.QWEN3_8B
@@ -859,7 +861,10 @@ def run_qwen3_batch(args, rank, world, local):
     attn_gbs = attn_launch_bytes / (attn_us / 1e6) / 1e9
     tile_bytes = (cfg.n_layers * ((cfg.q_dim + 2 * cfg.kv_dim) * cfg.hidden + cfg.hidden * cfg.q_dim
                                   + 2 * cfg.ffn * cfg.hidden + cfg.hidden * cfg.ffn)
-                  + cfg.vocab_padded * cfg.hidden) * 9 // 8        # int8 tiles + one f32 scale per 32
+                  + cfg.vocab_padded * cfg.hidden) * 5 // 4
+    # the matvec's weight tiles: per 128 rows x 32 columns, 4 KB of int8, the
+    # rows' f32 block scales and int32 row sums (5 KB); every Qwen3-8B row
+    # count is a multiple of 128
     gemm_gbs = tile_bytes / (statistics.mean(gemm_ms) / 1000.0) / 1e9
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
@@ -875,7 +880,8 @@ def run_qwen3_batch(args, rank, world, local):
     print(json.dumps({
         "metric": BATCH_METRIC, "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": 1, "steps": K,
         "warmup": args.warmup, "ms_per_step": round(statistics.mean(dev_ms), 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> int32 (Q8_0 x Q4_0 / Q8_0), f32 elsewhere",
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 (projections: exact int8 digit x int8 weight -> int32 products on tcgen05)",
         "data": "synthetic (seeded random-init .smodel v2 weights, BASELINE config 2 shapes)",
         "config": {"workload": f"qwen3-8b-shape q4_0 decode b={B} (BASELINE config 2)", "batch": B,
                    "context": TP_CONTEXT, "decode_steps": K, "layers": cfg.n_layers,
@@ -883,7 +889,8 @@ def run_qwen3_batch(args, rank, world, local):
                    "gemm_ms_per_step": round(statistics.mean(gemm_ms), 4),
                    "attention_ms_per_step": round(statistics.mean(attn_ms), 4),
                    "gemm_tile_gbs": round(gemm_gbs, 1),
-                   "l2": "inputs larger than L2 (9.9 GB of weight tiles and 19 GB of KV rows per step)",
+                   "l2": f"inputs larger than L2 ({tile_bytes / 1e9:.1f} GB of weight tiles and "
+                         f"{B * TP_CONTEXT * cfg.n_layers * 2 * cfg.kv_dim * 4 / 1e9:.0f} GB of KV rows per step)",
                    "tokens_first_seq0": first},
         "roofline": {"bound": "hbm", "kernel": "attn_decode_batch_kernel (one layer, all sequences)",
                      "achieved": round(attn_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
